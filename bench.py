@@ -1,0 +1,392 @@
+"""Training-throughput benchmark: the f32 decoder-LM training step on B200.
+
+Workload: the medium decoder LM (12 layers, d_model 1024, 16 heads, FFN 4096,
+vocab 32768, seq 1024) at a fixed global batch of 64 sequences (65,536
+tokens per step), 3xTF32 contractions with f32 master weights and AdamW;
+synthetic uniform tokens from a seed, N(0, 0.02) weights.  One step is
+forward + backward (+ NCCL gradient allreduce across ranks) + AdamW.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torchrun (one process per GPU): each rank takes 64/N
+sequences (strong scaling), gradients are summed with NCCL.  Rank 0 prints one
+JSON line.  `value` times device-resident token batches with CUDA events on
+the model's stream (max over ranks); `e2e` times the public host API
+(et_b200_lm_step_v1: host ids/targets copied in, loss copied out) the same
+way.  `--impl reference` times the reference's own CPU implementation of the
+same step on this host's cores by sampled per-operation timing.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "train tokens/s (fwd+bwd+opt, f32) at 1/2/4/8 B200"
+UNIT = "tokens/s"
+WORKLOAD = "medium decoder LM L12 d1024 H16 F4096 V32768 T1024, global batch 64"
+GLOBAL_BATCH = 64
+SHAPE = dict(layers=12, d_model=1024, heads=16, ffn=4096, vocabulary=32768, seq_len=1024)
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "fallback": True}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{gpu}_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        try:
+            rows = [r.split(",") for r in self.path.read_text().strip().splitlines()]
+        except Exception:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ----------------------------------------------------------------- B200 arm
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import eshkol_transformer_b200 as etb
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://",
+                                timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    if GLOBAL_BATCH % world:
+        raise SystemExit("global batch 64 must divide across ranks")
+    batch = GLOBAL_BATCH // world
+    shape = etb.ModelShape(batch=batch, **SHAPE)
+    tokens_rank = batch * shape.seq_len
+    global_tokens = GLOBAL_BATCH * shape.seq_len
+    model = etb.LanguageModel(shape, precision=etb.PRECISION_TF32X3, global_tokens=global_tokens)
+    model.init(20261201)
+    if world > 1:
+        uid = [etb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        model.enable_data_parallel(uid[0], rank, world)
+    stream = torch.cuda.ExternalStream(model.stream())
+    # distinct token batches per step, resident in HBM before timing
+    nbuf = 4
+    batches = [etb.synthetic_batch(1000 + 97 * i + rank, batch, shape.seq_len, shape.vocabulary)
+               for i in range(nbuf)]
+    dev = [(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()) for a, b in batches]
+    loss = torch.zeros(1, device="cuda")
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        model.step_device(dev[i % nbuf][0].data_ptr(), dev[i % nbuf][1].data_ptr(), loss.data_ptr())
+    barrier()
+    model.profile(True)
+    launches0 = etb.launch_count()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record(stream)
+        for i in range(args.steps):
+            ids, tg = dev[i % nbuf]
+            model.step_device(ids.data_ptr(), tg.data_ptr(), loss.data_ptr())
+        stop.record(stream)
+        barrier()
+    launches = etb.launch_count() - launches0
+    ms = start.elapsed_time(stop)
+    prof = model.profile_read()
+    model.profile(False)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = t.item()
+    value = global_tokens * args.steps / (ms_max / 1e3)
+
+    # e2e through the public host API: host ids/targets in, loss out
+    host = [(np.ascontiguousarray(a), np.ascontiguousarray(b)) for a, b in batches]
+    barrier()
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    e2e_stop = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 5))
+    e2e_start.record(stream)
+    t0 = time.perf_counter()
+    losses = []
+    for i in range(e2e_steps):
+        a, b = host[i % nbuf]
+        losses.append(model.step(a, b))
+    e2e_stop.record(stream)
+    barrier()
+    wall = time.perf_counter() - t0
+    e2e_ms = max(e2e_start.elapsed_time(e2e_stop), wall * 1e3)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    e2e_value = global_tokens * e2e_steps / (e2e_ms / 1e3)
+
+    peaks = measured_peaks()
+    gemm = prof["gemm"]
+    gemm_tflops = gemm["flop"] / (gemm["ms"] / 1e3) / 1e12 if gemm["ms"] else 0.0
+    peak_t = peaks.get("bf16_tflops_sustained", 1400.0)
+    per_launch_flop = gemm["flop"] / max(gemm["launches"], 1)
+    attn_b = prof["attention_backward"]
+    attn_tflops = attn_b["flop"] / (attn_b["ms"] / 1e3) / 1e12 if attn_b["ms"] else 0.0
+    total_prof_ms = sum(v["ms"] for v in prof.values())
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic uniform tokens (seeded), N(0,0.02) random-init weights",
+        "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH,
+                   "seq_len": shape.seq_len, "tokens_per_step": global_tokens,
+                   "contractions": "3xTF32 tcgen05", "parallelism": f"dp{world}",
+                   "l2": "activations (GBs per step) exceed the 126 MB L2; no flush needed"},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "linear GEMM (tcgen05 kind::tf32, 3 passes)",
+                     "achieved": round(gemm_tflops, 2), "peak": peak_t, "unit": "TFLOP/s",
+                     "frac": round(gemm_tflops / peak_t, 4) if peak_t else None,
+                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
+                     if not peaks.get("fallback") else "fallback",
+                     "tf32_dense_peak": peak_t / 2,
+                     "frac_of_tf32_peak_algorithmic": round(gemm_tflops / (peak_t / 2), 4),
+                     "tensor_mma_per_algorithmic_flop": 3,
+                     "flop_per_launch": per_launch_flop,
+                     "avg_launch_ms": gemm["ms"] / max(gemm["launches"], 1),
+                     "traffic": None},
+        "attention_backward": {"achieved_tflops": round(attn_tflops, 2),
+                               "ms_per_step": round(attn_b["ms"] / args.steps, 3)},
+        "profile_ms_per_step": {k: round(v["ms"] / args.steps, 3) for k, v in prof.items()},
+        "profile_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in prof.items()}
+        if total_prof_ms else {},
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT,
+                "h2d_bytes_per_step": 2 * 8 * tokens_rank, "d2h_bytes_per_step": 4,
+                "steps": e2e_steps, "final_loss": losses[-1]},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(kind="port", budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------- CPU arm
+
+def cpu_baseline(kind: str = "port", budget_s: float = 20.0) -> dict:
+    """Sampled per-operation timing of the CPU implementation of one training
+    step of the workload, scaled to tokens/s by the step's operation counts.
+
+    kind "port": the oracle restatement (OpenMP over the host cores);
+    kind "reference": the reference's own C providers (oracle/_ref, serial),
+    with AdamW from the port (the O2 optimizer needs the reference's tensor
+    carriers and is 28 B/parameter of streaming work either way).
+    """
+    import ctypes as C
+
+    from oracle import oracle as orc
+
+    ref = orc.ref() if kind == "reference" else None
+    if kind == "reference" and ref is None:
+        kind = "port"
+    threads = os.cpu_count() or 1 if kind == "port" else 1
+    L, d, H, F, V, T = (SHAPE[k] for k in ("layers", "d_model", "heads", "ffn", "vocabulary",
+                                         "seq_len"))
+    Dh = d // H
+    S = 16 if kind == "reference" else 64  # token sample for the contractions
+    rows = S
+    t = {}
+
+    def timed(name, fn, repeat=1):
+        t0 = time.perf_counter()
+        for _ in range(repeat):
+            fn()
+        t[name] = (time.perf_counter() - t0) / repeat
+
+    x = orc.fill_normal(1, 1, rows * F)
+    dy = orc.fill_normal(1, 2, rows * F)
+
+    def linear_pair(din, dout):
+        xi = x[:rows * din].reshape(1, rows, din)
+        w = orc.fill_normal(1, 3, dout * din, 0, 0.02).reshape(dout, din)
+        b = np.zeros(dout, np.float32)
+        g = dy[:rows * dout].reshape(1, rows, dout)
+        if ref is not None:
+            y = np.empty((1, rows, dout), np.float32)
+            dx = np.empty_like(xi)
+            dw = np.empty_like(w)
+            db = np.empty(dout, np.float32)
+            p = lambda a: a.ctypes.data_as(C.c_void_p)
+            return lambda: (ref.ref_n2_linear_forward(C.c_size_t(1), C.c_size_t(rows),
+                                                      C.c_size_t(din), C.c_size_t(dout), p(xi),
+                                                      p(w), p(b), p(y)),
+                            ref.ref_n2_linear_backward(C.c_size_t(1), C.c_size_t(rows),
+                                                       C.c_size_t(din), C.c_size_t(dout), p(xi),
+                                                       p(w), p(g), 1, p(dx), p(dw), p(db)))
+        return lambda: (orc.linear_forward(xi, w, b), orc.linear_backward(xi, w, g))
+
+    timed("qkv", linear_pair(d, 3 * d))
+    timed("out", linear_pair(d, d))
+    timed("up", linear_pair(d, F))
+    timed("down", linear_pair(F, d))
+    # tied head at a smaller sample (largest contraction), scaled to S
+    Sh = max(4, S // 4)
+    xh = x[:Sh * d].reshape(1, Sh, d)
+    wh = orc.fill_normal(1, 4, V * d, 0, 0.02).reshape(V, d)
+    gh = orc.fill_normal(1, 5, Sh * V).reshape(1, Sh, V)
+    t0 = time.perf_counter()
+    orc.linear_forward(xh, wh)
+    orc.linear_backward(xh, wh, gh, with_bias=False)
+    head = (time.perf_counter() - t0) * S / Sh
+    # attention at the full sequence length for one (sequence, head), scaled
+    shp = (1, 1, 1, T, T, Dh) if kind == "port" else (1, 1, 1, 256, 256, Dh)
+    Ta = shp[3]
+    q = orc.fill_normal(2, 1, Ta * Dh).reshape(1, 1, Ta, Dh)
+    pos = np.arange(Ta, dtype=np.int64).reshape(1, Ta)
+    mask = np.ones((1, Ta, Ta), np.uint8)
+    t0 = time.perf_counter()
+    orc.attention_forward(shp, q, q, q, pos, pos, mask)
+    orc.attention_backward(shp, q, q, q, pos, pos, mask, q)
+    att_one = (time.perf_counter() - t0) * (T / Ta) ** 2  # O(T^2) per (sequence, head)
+    att_per_token = att_one * H / T
+    # LN / GELU / CE / AdamW per element, sampled
+    xl = orc.fill_normal(3, 1, rows * d).reshape(1, rows, d)
+    gam = np.ones(d, np.float32)
+    t0 = time.perf_counter()
+    orc.layer_norm_forward(xl, gam, gam, 1e-5)
+    orc.layer_norm_backward(xl, gam, 1e-5, xl)
+    ln = time.perf_counter() - t0
+    u = x[:rows * F]
+    t0 = time.perf_counter()
+    orc.gelu_forward(u)
+    orc.gelu_backward(u, u)
+    gelu = time.perf_counter() - t0
+    lg = orc.fill_normal(3, 2, rows * V).reshape(1, rows, V)
+    tg = orc.fill_tokens(3, 3, rows, V).reshape(1, rows)
+    t0 = time.perf_counter()
+    orc.ce_forward(lg, tg)
+    orc.ce_backward(lg, tg, np.ones((1, rows), np.float32))
+    ce = time.perf_counter() - t0
+    n_params = 12 * (4 * d * d + 2 * d * F) + V * d
+    pa = orc.fill_normal(4, 1, 1 << 20)
+    m = np.zeros_like(pa)
+    v = np.zeros_like(pa)
+    t0 = time.perf_counter()
+    orc.adamw_step(pa, pa, m, v, orc.adamw_options(1e-3, 0.9, 0.999, 1e-8, 0.01), 1)
+    adam = (time.perf_counter() - t0) * n_params / (1 << 20)
+    per_token = ((t["qkv"] + t["out"] + t["up"] + t["down"] + 2 * ln + gelu) * L + head + ln
+                 + ce) / S + att_per_token * L + adam / (GLOBAL_BATCH * T)
+    return {"value": round(1.0 / per_token, 3), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": (f"per-op timing on {S} tokens of the {WORKLOAD} step (tied head on {Sh} "
+                       f"tokens, attention on one (sequence, head) at T={Ta} scaled by (T/{Ta})^2, "
+                       f"AdamW on 2^20 parameters) scaled by the step's operation counts")}
+
+
+def run_reference(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    t0 = time.perf_counter()
+    samples = []
+    for _ in range(max(1, args.steps)):
+        samples.append(cpu_baseline(kind="reference", budget_s=args.cpu_budget))
+    value = statistics.median(s["value"] for s in samples)
+    base = samples[0]
+    ms_per_step = GLOBAL_BATCH * SHAPE["seq_len"] / value * 1e3
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH,
+                   "seq_len": SHAPE["seq_len"], "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": base["cores"],
+                         "kind": base["kind"], "sample": base["sample"]},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(time.perf_counter() - t0, 1)}), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

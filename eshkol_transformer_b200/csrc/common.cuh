@@ -1,0 +1,99 @@
+// Shared host/device helpers for libet_b200 (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+
+#include "eshkol_b200/et_b200.h"
+
+namespace etb {
+
+// Kernels launched by this library since load; sampled by callers to count
+// the launches inside a timed region.
+extern std::atomic<uint64_t> g_launches;
+inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+inline int32_t set_error(et_kernel_error *e, uint32_t category, uint32_t code,
+                         const char *operation, const char *message) {
+  if (e != nullptr) {
+    memset(e, 0, sizeof(*e));
+    e->category = category;
+    e->code = code;
+    snprintf(e->operation, sizeof(e->operation), "%s", operation ? operation : "et-b200");
+    snprintf(e->message, sizeof(e->message), "%s", message ? message : "error");
+  }
+  return (int32_t)category;
+}
+
+inline int32_t cuda_error(et_kernel_error *e, cudaError_t status, const char *operation) {
+  char text[160];
+  snprintf(text, sizeof(text), "CUDA: %s", cudaGetErrorString(status));
+  return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, operation, text);
+}
+
+inline unsigned ceil_div(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
+
+// Number of SMs of the current device (cached per device id).
+int sm_count();
+
+// Device word (one per GPU) that bounded device-side waits set when they
+// give up; host entry points read and clear it.
+int* device_error_word();
+
+// ---- correctly rounded f32 arithmetic without contraction (device) -----
+__device__ __forceinline__ float rn_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float rn_sub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float rn_mul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float rn_div(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float rn_sqrt(float a) { return __fsqrt_rn(a); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide reduction helpers (blockDim.x multiple of 32, <= 1024).
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int warps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < warps ? scratch[lane] : scratch[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) scratch[0] = v;
+  }
+  __syncthreads();
+  T r = scratch[0];
+  __syncthreads();
+  return r;
+}
+
+struct AddOp {
+  template <typename T> __device__ __forceinline__ T operator()(T a, T b) const { return a + b; }
+};
+struct MaxOp {
+  __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); }
+};
+
+}  // namespace etb

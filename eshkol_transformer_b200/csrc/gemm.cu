@@ -1,0 +1,569 @@
+// N2/N3K linear contractions: C[m,n] = sum_k A(m,k) B(n,k) (+ bias) (+ C).
+//
+// The three linear products of native/n2_primitives_provider.c:347-419 map
+// onto this one operation with different operand majorness:
+//   forward  y  = x W^T : A = x  (K-major), B = W  (K-major)
+//   backward dX = dY W  : A = dY (K-major), B = W  (N-major)
+//   backward dW = dY^T x: A = dY (M-major), B = x  (N-major)
+//
+// Tensor-core path (sm_100a): a persistent, warp-specialised kernel.
+//   warp 0   one lane issues TMA tile loads (128-byte swizzle, no multicast)
+//            into a STAGES-deep shared-memory ring;
+//   warp 1   allocates the TMEM accumulators and one lane issues
+//            tcgen05.mma.kind::tf32 (M=128, N=BN, K=8 per instruction);
+//            tcgen05.commit releases ring slots and hands finished
+//            accumulators to the epilogue;
+//   warps 2-5 read the accumulator with tcgen05.ld (one TMEM lane per row),
+//            add the bias and store f32 results.
+// Two TMEM accumulators (2 x BN columns) let the epilogue of one tile overlap
+// the main loop of the next.  The 3xTF32 mode feeds tf32-exact operands
+// (hi = x with its low 13 mantissa bits cleared) plus their residuals lo and
+// accumulates A B + A B_lo + A_lo B, which keeps f32-grade accuracy.
+// Every mbarrier wait is bounded (about two seconds of clock) and reports
+// through the device error word instead of hanging.
+//
+// FFMA path: a plain 128x128 register-tiled kernel, used for the f32 mode and
+// for shapes the tensor-core path does not take (unaligned strides, K = 0).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "ops.cuh"
+
+namespace etb {
+
+
+
+namespace {
+
+// ============================================================== FFMA path
+
+constexpr int SB_M = 128, SB_N = 128, SB_K = 8;
+
+__global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs g) {
+  __shared__ __align__(16) float As[SB_K][SB_M];
+  __shared__ __align__(16) float Bs[SB_K][SB_N];
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  const int m0 = blockIdx.y * SB_M, n0 = blockIdx.x * SB_N;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+  for (int k0 = 0; k0 < g.K; k0 += SB_K) {
+    for (int i = tid; i < SB_M * SB_K; i += 256) {
+      int mm, kk;
+      if (g.a_kmajor) { mm = i / SB_K; kk = i % SB_K; } else { kk = i / SB_M; mm = i % SB_M; }
+      const int m = m0 + mm, k = k0 + kk;
+      float v = 0.0f;
+      if (m < g.M && k < g.K)
+        v = g.a_kmajor ? g.A[(int64_t)m * g.lda + k] : g.A[(int64_t)k * g.lda + m];
+      As[kk][mm] = v;
+    }
+    for (int i = tid; i < SB_N * SB_K; i += 256) {
+      int nn, kk;
+      if (g.b_kmajor) { nn = i / SB_K; kk = i % SB_K; } else { kk = i / SB_N; nn = i % SB_N; }
+      const int n = n0 + nn, k = k0 + kk;
+      float v = 0.0f;
+      if (n < g.N && k < g.K)
+        v = g.b_kmajor ? g.B[(int64_t)n * g.ldb + k] : g.B[(int64_t)k * g.ldb + n];
+      Bs[kk][nn] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < SB_K; kk++) {
+      float a[8], b[8];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][ty * 8 + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4 + 64]);
+      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+      a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+      b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int m = m0 + ty * 8 + i;
+    if (m >= g.M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int n = n0 + tx * 4 + (j & 3) + (j >> 2) * 64;
+      if (n >= g.N) continue;
+      float v = acc[i][j];
+      if (g.bias) v += g.bias[n];
+      float* c = g.C + (int64_t)m * g.ldc + n;
+      if (g.accumulate) v += *c;
+      *c = v;
+    }
+  }
+}
+
+// ============================================================== tcgen05 path
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 32;  // one 128-byte swizzle row of f32
+constexpr int TC_THREADS = 192;
+constexpr long long kWaitCycles = 1ll << 32;
+
+struct TcArgs {
+  int M, N, K;
+  float* C;
+  int64_t ldc;
+  const float* bias;
+  int accumulate;
+  int a_mn, b_mn;
+  int tiles_m, tiles_n;
+  int* error;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the error word set) when the phase does not
+// complete within kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* error) {
+  if (mbar_try(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (clock64() - start > kWaitCycles) {
+      atomicExch(error, 0x6e6d);  // 'mm': GEMM pipeline wait timed out
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3fffu);
+  d |= (uint64_t)((lbo >> 4) & 0x3fffu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3fffu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Descriptor of the j-th K=8 slice of a staged operand tile.
+//   K-major : rows of 128 B (32 k), 8-row atoms 1024 B apart, slice j at +32j B
+//   MN-major: per 32-wide MN chunk 32 k-rows of 128 B (4096 B), chunks 4096 B
+//             apart (LBO), 8-k-row groups 1024 B apart (SBO), slice j at +1024j B
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int j) {
+  return mn_major ? sdesc(base + 1024u * j, 4096u, 1024u) : sdesc(base + 32u * j, 16u, 1024u);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Grouped rasterisation: 16 M-tiles per group so the CTAs in flight share
+// their A row blocks and B column blocks through L2.
+__device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  constexpr int G = 16;
+  const int per_group = G * tiles_n;
+  const int group = tile / per_group;
+  const int first = group * G;
+  const int gm = min(tiles_m - first, G);
+  const int in = tile % per_group;
+  tm = first + in % gm;
+  tn = in / gm;
+}
+
+template <int BN, int STAGES, bool THREE>
+struct TcLayout {
+  static constexpr int A_BYTES = TC_BM * TC_BK * 4;
+  static constexpr int B_BYTES = BN * TC_BK * 4;
+  static constexpr int OPS = THREE ? 2 : 1;
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * OPS;
+  static constexpr int RING_BYTES = STAGE_BYTES * STAGES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = RING_BYTES + BAR_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+template <int BN, int STAGES, bool THREE>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
+               const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb_lo,
+               TcArgs args) {
+  using L = TcLayout<BN, STAGES, THREE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::RING_BYTES);
+  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; then the TMEM slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(L::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int nkb = (args.K + TC_BK - 1) / TC_BK;
+  const int tiles = args.tiles_m * args.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t armed = 0;  // bitmask of stages with an armed phase in flight
+      uint32_t armed_phase[STAGES];
+      for (int s = 0; s < STAGES; s++) armed_phase[s] = 0;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        int tm, tn;
+        raster(tile, args.tiles_m, args.tiles_n, tm, tn);
+        const int m0 = tm * TC_BM, n0 = tn * BN;
+        for (int kb = 0; kb < nkb; kb++) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, args.error)) { ok = false; break; }
+          const uint32_t full = full0 + 8 * stage;
+          mbar_expect_tx(full, L::STAGE_BYTES);
+          armed |= 1u << stage;
+          armed_phase[stage] = phase;
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+          const int k0 = kb * TC_BK;
+#pragma unroll
+          for (int op = 0; op < L::OPS; op++) {
+            const CUtensorMap* mA = op == 0 ? &ta : &ta_lo;
+            const CUtensorMap* mB = op == 0 ? &tb : &tb_lo;
+            const uint32_t da = sa + op * (L::A_BYTES + L::B_BYTES);
+            const uint32_t db = sb + op * (L::A_BYTES + L::B_BYTES);
+            if (args.a_mn) {
+              for (int c = 0; c < TC_BM / 32; c++) tma_load_2d(da + 4096u * c, mA, full, m0 + 32 * c, k0);
+            } else {
+              tma_load_2d(da, mA, full, k0, m0);
+            }
+            if (args.b_mn) {
+              for (int c = 0; c < BN / 32; c++) tma_load_2d(db + 4096u * c, mB, full, n0 + 32 * c, k0);
+            } else {
+              tma_load_2d(db, mB, full, k0, n0);
+            }
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        // drain: let every armed copy land before the CTA can exit
+        for (int s = 0; s < STAGES; s++)
+          if (armed & (1u << s)) mbar_wait(full0 + 8 * s, armed_phase[s], args.error);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)args.a_mn << 15) |
+                             ((uint32_t)args.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(TC_BM >> 4) << 24);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, args.error)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nkb; kb++) {
+          if (!mbar_wait(full0 + 8 * stage, phase, args.error)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int j = 0; j < TC_BK / 8; j++) {
+            const uint64_t a = operand_desc(sa, args.a_mn, j);
+            const uint64_t b = operand_desc(sb, args.b_mn, j);
+            umma_tf32(d_tmem, a, b, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+            if (THREE) {
+              const uint32_t lo = L::A_BYTES + L::B_BYTES;
+              const uint64_t alo = operand_desc(sa + lo, args.a_mn, j);
+              const uint64_t blo = operand_desc(sb + lo, args.b_mn, j);
+              umma_tf32(d_tmem, a, blo, idesc, 1u);
+              umma_tf32(d_tmem, alo, b, idesc, 1u);
+            }
+          }
+          umma_commit(empty0 + 8 * stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(tfull0 + 8 * acc);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 own TMEM lanes 32*(warp%4)..
+    const int lane_base = 32 * (warp & 3);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      // one lane observes the phase; the warp stays converged for tcgen05.ld
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(tfull0 + 8 * acc, acc_phase, args.error) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      __syncwarp();
+      tc_fence_after();
+      int tm, tn;
+      raster(tile, args.tiles_m, args.tiles_n, tm, tn);
+      const int m = tm * TC_BM + lane_base + lane;
+      const int n_tile = tn * BN;
+      float* crow = args.C + (int64_t)m * args.ldc;
+      const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c), v);
+        if (m < args.M) {
+          const int n0 = n_tile + c;
+          if (vec && n0 + 32 <= args.N) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 r = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+              if (args.bias) {
+                r.x += args.bias[n0 + i];
+                r.y += args.bias[n0 + i + 1];
+                r.z += args.bias[n0 + i + 2];
+                r.w += args.bias[n0 + i + 3];
+              }
+              float4* dst = reinterpret_cast<float4*>(crow + n0 + i);
+              if (args.accumulate) {
+                const float4 o = *dst;
+                r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
+              }
+              *dst = r;
+            }
+          } else {
+            for (int i = 0; i < 32; i++) {
+              const int n = n0 + i;
+              if (n >= args.N) break;
+              float r = v[i];
+              if (args.bias) r += args.bias[n];
+              if (args.accumulate) r += crow[n];
+              crow[n] = r;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D f32 tensor map over a row-major [outer, inner] array with row stride
+// `ld` elements; box {32, box_outer}, 128-byte swizzle, zero OOB fill.
+bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, int64_t ld,
+              uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  const cuuint32_t box[2] = {32, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Operand map: K-major [rows, K] with box {32 k, tile rows}; MN-major [K, rows]
+// with box {32 mn, 32 k} (one load per 32-wide chunk).
+bool operand_map(CUtensorMap* map, const float* p, bool kmajor, int rows, int K, int64_t ld,
+                 int tile_rows) {
+  if (kmajor) return make_map(map, p, (uint64_t)K, (uint64_t)rows, ld, (uint32_t)tile_rows);
+  return make_map(map, p, (uint64_t)rows, (uint64_t)K, ld, 32u);
+}
+
+template <int BN, int STAGES, bool THREE>
+void launch_tc(const GemmArgs& g, cudaStream_t stream) {
+  using L = TcLayout<BN, STAGES, THREE>;
+  CUtensorMap ta, tb, ta_lo, tb_lo;
+  bool ok = operand_map(&ta, g.A, g.a_kmajor, g.M, g.K, g.lda, TC_BM) &&
+            operand_map(&tb, g.B, g.b_kmajor, g.N, g.K, g.ldb, BN);
+  if (THREE) {
+    ok = ok && operand_map(&ta_lo, g.A_lo, g.a_kmajor, g.M, g.K, g.lda, TC_BM) &&
+         operand_map(&tb_lo, g.B_lo, g.b_kmajor, g.N, g.K, g.ldb, BN);
+  } else {
+    ta_lo = ta;
+    tb_lo = tb;
+  }
+  if (!ok) {
+    gemm_simt(g, stream);
+    return;
+  }
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, THREE>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+    configured = true;
+  }
+  TcArgs a;
+  a.M = g.M; a.N = g.N; a.K = g.K;
+  a.C = g.C; a.ldc = g.ldc; a.bias = g.bias; a.accumulate = g.accumulate ? 1 : 0;
+  a.a_mn = g.a_kmajor ? 0 : 1;
+  a.b_mn = g.b_kmajor ? 0 : 1;
+  a.tiles_m = (g.M + TC_BM - 1) / TC_BM;
+  a.tiles_n = (g.N + BN - 1) / BN;
+  a.error = device_error_word();
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  gemm_tc_kernel<BN, STAGES, THREE><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(ta, ta_lo, tb,
+                                                                                 tb_lo, a);
+  count_launch();
+}
+
+}  // namespace
+
+void gemm_simt(const GemmArgs& g, cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0) return;
+  dim3 grid((g.N + SB_N - 1) / SB_N, (g.M + SB_M - 1) / SB_M);
+  gemm_simt_kernel<<<grid, 256, 0, stream>>>(g);
+  count_launch();
+}
+
+bool gemm_tc_supported(const GemmArgs& g) {
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return false;
+  if ((g.lda & 3) || (g.ldb & 3)) return false;
+  if (!aligned(g.A) || !aligned(g.B)) return false;
+  if (g.A_lo && !aligned(g.A_lo)) return false;
+  if (g.B_lo && !aligned(g.B_lo)) return false;
+  // TMA global extents and strides must fit the descriptor limits
+  if (g.lda > ((int64_t)1 << 36) || g.ldb > ((int64_t)1 << 36)) return false;
+  return encode_fn() != nullptr;
+}
+
+void gemm_tc(const GemmArgs& g, bool three_pass, cudaStream_t stream) {
+  if (three_pass) launch_tc<128, 3, true>(g, stream);
+  else launch_tc<256, 4, false>(g, stream);
+}
+
+void gemm(const GemmArgs& g, int precision, cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0) return;
+  const bool three = precision == ET_B200_PRECISION_TF32X3;
+  if (precision == ET_B200_PRECISION_F32 || !gemm_tc_supported(g) ||
+      (three && (g.A_lo == nullptr || g.B_lo == nullptr))) {
+    gemm_simt(g, stream);
+    return;
+  }
+  gemm_tc(g, three, stream);
+}
+
+}  // namespace etb

@@ -1,0 +1,161 @@
+// Internal launch API shared by the libet_b200 translation units.  Every
+// function enqueues on `stream`, counts its launches and never synchronises.
+#pragma once
+
+#include "common.cuh"
+
+namespace etb {
+
+// ---------------------------------------------------------------- L2 CE
+// Fused indexed cross-entropy: per row r of logits [rows, V], the loss
+// log(sum exp(x - m)) + (m - x[t]) and, when dlogits != nullptr, the gradient
+// u_r (softmax(x) - onehot(t)) with u_r = upstream[r] (or upstream_scale when
+// upstream is null).  dlogits may alias logits.  status[0] is set to 1 when a
+// target is outside [0, V).
+void ce_fused(const float* logits, float* dlogits, const int64_t* targets,
+              const float* upstream, float upstream_scale, float* loss,
+              size_t rows, size_t V, int* status, cudaStream_t stream);
+// Mean of loss[rows] as one f32 (fixed-order tree in f64).
+void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream);
+
+// ---------------------------------------------------------------- O2 AdamW
+struct AdamwTensor {
+  float* value;
+  const float* grad;
+  float* exp_avg;
+  float* exp_avg_sq;
+  uint64_t count;
+  // per-tensor scalars computed on the host with the reference's rounding
+  float beta1, beta2, one_minus_beta1, one_minus_beta2, bias1, bias2, lr,
+      decay, epsilon;
+};
+// One fused pass over every tensor of the table (device array `tensors`,
+// `prefix[i]` = first global element of tensor i, total = prefix[count]).
+// weight/clip divide and scale gradients as o2_optimizer.c:1738 does.
+// status[1] is set when any staged value is nonfinite.
+void adamw_multi(const AdamwTensor* tensors, const uint64_t* prefix,
+                 int tensor_count, uint64_t total, float weight, float clip,
+                 int* status, cudaStream_t stream);
+// Sum of squares of grad/weight over the table, in f64, plus status[0] = 1 on
+// any nonfinite gradient.  out_sumsq receives one double.
+void grad_sumsq(const AdamwTensor* tensors, const uint64_t* prefix,
+                int tensor_count, uint64_t total, float weight,
+                double* partials, int partial_count, double* out_sumsq,
+                int* status, cudaStream_t stream);
+
+// ---------------------------------------------------------------- N2 family
+void layer_norm_forward(const float* x, const float* gamma, const float* beta,
+                        float epsilon, float* y, float* mean, float* rstd,
+                        size_t rows, size_t d, cudaStream_t stream);
+// dx = (accumulate ? dx : 0) + LN'(dy); dgamma/dbeta over all rows via a
+// fixed-order two-stage column reduction in `workspace` (>= ln_workspace()).
+size_t ln_workspace_floats(size_t rows, size_t d);
+void layer_norm_backward(const float* x, const float* gamma, const float* mean,
+                         const float* rstd, const float* dy, float* dx,
+                         int accumulate, float* dgamma, float* dbeta,
+                         float* workspace, size_t rows, size_t d,
+                         cudaStream_t stream);
+void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream);
+void gelu_backward(const float* x, const float* dy, float* dx, size_t count,
+                   cudaStream_t stream);
+void relu_forward(const float* x, float* y, size_t count, cudaStream_t stream);
+void relu_backward(const float* x, const float* dy, float* dx, size_t count,
+                   cudaStream_t stream);
+void add_tensors(const float* a, const float* b, float* out, size_t count,
+                 cudaStream_t stream);
+void copy_tensor(const float* a, float* out, size_t count, cudaStream_t stream);
+// Row gather y[r] = W[ids[r]]; status[0] = 1 on an id outside [0, V).
+void embedding_forward(const int64_t* ids, const float* w, float* y,
+                       size_t rows, size_t V, size_t d, int* status,
+                       cudaStream_t stream);
+// dW[v] = (base ? base[v] : 0) + (sum over rows r with ids[r] == v, in
+// ascending r, starting from +0).  Bit-identical to the reference's order.
+// `scratch` holds >= embedding_scratch_bytes(rows, V) bytes.
+size_t embedding_scratch_bytes(size_t rows, size_t V);
+void embedding_backward(const int64_t* ids, const float* dy, const float* base,
+                        float* dw, size_t rows, size_t V, size_t d,
+                        void* scratch, cudaStream_t stream);
+// out[n] = sum over rows of dy[r, n] (fixed-order two-stage).
+size_t colsum_workspace_floats(size_t rows, size_t n);
+void column_sum(const float* dy, float* out, size_t rows, size_t n,
+                float* workspace, cudaStream_t stream);
+// 3xTF32 operand split: hi = x with its low 13 mantissa bits cleared (exactly
+// representable in TF32) and lo = x - hi (exact).  hi may alias x.
+void split_tf32(const float* x, float* hi, float* lo, size_t count, cudaStream_t stream);
+// Standalone RoPE over [N,H,T,Dh] with a host-built cos/sin table
+// [N*T, Dh/2] each (bit-identical rotation).
+void rope_apply(const float* x, float* y, const float* cos_table,
+                const float* sin_table, size_t N, size_t H, size_t T,
+                size_t Dh, int backward, cudaStream_t stream);
+// status flags: sets *flag = 1 if any of count values is nonfinite.
+void check_finite(const float* x, size_t count, int* flag, cudaStream_t stream);
+
+// ---------------------------------------------------------------- A2
+// Strided attention operands: element (b, h, t, j) of a tensor lives at
+// base + b*sb + h*sh + t*st + j.
+struct AttnTensor {
+  const float* ptr;
+  int64_t sb, sh, st;
+};
+struct AttnOut {
+  float* ptr;
+  int64_t sb, sh, st;
+};
+struct AttnParams {
+  int B, Hq, Hkv, Tq, Tk, Dh;
+  float scale;
+  AttnTensor q, k, v;
+  // positions i64 [B,Tq] / [B,Tk]; keep mask u8 [B,Tq,Tk] (null = all kept)
+  const int64_t* qpos;
+  const int64_t* kpos;
+  const uint8_t* mask;
+  // optional RoPE applied to q/k on load (tables [B*T, Dh/2]; null = none)
+  const float* q_cos;
+  const float* q_sin;
+  const float* k_cos;
+  const float* k_sin;
+  // 1 when a table has B*T rows (row b*T + t), 0 when it has T rows shared
+  // by every sequence (row t).
+  int q_rope_batched, k_rope_batched;
+};
+// Forward: o and per-row statistics m (row max of scaled scores) and l (sum
+// of exp(s - m)); rows with no admitted key produce o = 0, m = 0, l = 0.
+void attention_forward(const AttnParams& p, AttnOut o, float* row_max,
+                       float* row_sum, cudaStream_t stream);
+// Backward: dq/dk/dv (RoPE backward applied to dq/dk when tables are set).
+// delta[B*Hq*Tq] is scratch for rowsum(dO * O); when o_lo is given (same
+// strides as o) the forward output is o + o_lo (a 3xTF32 hi/lo pair).
+void attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
+                        const float* row_max, const float* row_sum,
+                        float* delta, AttnOut dq, AttnOut dk, AttnOut dv,
+                        cudaStream_t stream);
+
+// ---------------------------------------------------------------- GEMM
+// C[m, n] = sum_k A(m, k) B(n, k) (+ bias[n]) (+ C when accumulate).
+// A(m,k) = a_kmajor ? A[m*lda + k] : A[k*lda + m]
+// B(n,k) = b_kmajor ? B[n*ldb + k] : B[k*ldb + n]
+// For the TF32 modes a_lo/b_lo hold x - tf32(x) of the same layout (3xTF32
+// uses A*B + A*B_lo + A_lo*B); they are ignored in the other modes.
+struct GemmArgs {
+  int M, N, K;
+  const float* A;
+  const float* A_lo;
+  int64_t lda;
+  bool a_kmajor;
+  const float* B;
+  const float* B_lo;
+  int64_t ldb;
+  bool b_kmajor;
+  float* C;
+  int64_t ldc;
+  const float* bias;
+  bool accumulate;
+};
+void gemm(const GemmArgs& g, int precision, cudaStream_t stream);
+// True when the tensor-core path accepts this problem (alignment / shape);
+// otherwise gemm() uses the FFMA path.
+bool gemm_tc_supported(const GemmArgs& g);
+void gemm_simt(const GemmArgs& g, cudaStream_t stream);
+void gemm_tc(const GemmArgs& g, bool three_pass, cudaStream_t stream);
+
+}  // namespace etb

@@ -1,0 +1,444 @@
+// N2-family bandwidth kernels: LayerNorm, GELU/ReLU, residual, embedding,
+// column sums (bias gradients), the TF32 residual split and standalone RoPE.
+//
+// Rounding points follow native/n2_primitives_provider.c:313-622 where the
+// operation is elementwise (GELU, residual, RoPE rotation, embedding sums),
+// so those outputs differ from the reference only through the device libm
+// (erff/expf) and not through contraction.  Row and column reductions use a
+// fixed-order tree, so every result is deterministic run to run.
+#include <cub/cub.cuh>
+
+#include "ops.cuh"
+
+namespace etb {
+
+namespace {
+
+// ---- LayerNorm --------------------------------------------------------------
+
+constexpr int kLnWarps = 4;
+
+// One warp per row; the row is re-read from L1 for each of the three sweeps
+// (mean, centred variance, output) so HBM sees one read and one write.
+__global__ void __launch_bounds__(kLnWarps * 32)
+ln_forward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                  const float* __restrict__ beta, float epsilon, float* __restrict__ y,
+                  float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                  int64_t rows, int64_t d) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + row * d;
+  const float dim = (float)d;
+  float s = 0.0f;
+  for (int64_t j = lane; j < d; j += 32) s += xr[j];
+  s = warp_sum(s);
+  const float mean = rn_div(s, dim);
+  float v = 0.0f;
+  for (int64_t j = lane; j < d; j += 32) {
+    const float delta = rn_sub(xr[j], mean);
+    v += rn_mul(delta, delta);
+  }
+  v = warp_sum(v);
+  const float variance = rn_div(v, dim);
+  const float rstd = rn_div(1.0f, rn_sqrt(rn_add(variance, epsilon)));
+  float* yr = y + row * d;
+  for (int64_t j = lane; j < d; j += 32) {
+    const float normalized = rn_mul(rn_sub(xr[j], mean), rstd);
+    yr[j] = rn_add(rn_mul(normalized, gamma[j]), beta[j]);
+  }
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = rstd;
+  }
+}
+
+int ln_backward_blocks(size_t rows) {
+  const size_t want = (rows + kLnWarps - 1) / kLnWarps;
+  const size_t cap = (size_t)sm_count() * 4;
+  return (int)(want < cap ? want : cap);
+}
+
+// dx per row (n2_primitives_provider.c:490-512):
+//   h = dy * gamma, n = (x - mean) rstd,
+//   dx = (rstd / d) * ((d h - sum h) - n * sum(h n))
+// and per-block column partials of dy * n (dgamma) and dy (dbeta), reduced
+// over the block's warps in a fixed order.
+__global__ void __launch_bounds__(kLnWarps * 32)
+ln_backward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                   const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                   const float* __restrict__ dy, float* __restrict__ dx, int accumulate,
+                   float* __restrict__ partial, int64_t rows, int64_t d) {
+  extern __shared__ float sm[];  // [kLnWarps][2][d]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* pg = sm + (size_t)warp * 2 * d;
+  float* pb = pg + d;
+  for (int64_t j = lane; j < d; j += 32) { pg[j] = 0.0f; pb[j] = 0.0f; }
+  const float dim = (float)d;
+  const float inv_dim = rn_div(1.0f, dim);
+  for (int64_t row = (int64_t)blockIdx.x * kLnWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kLnWarps) {
+    const float* xr = x + row * d;
+    const float* gr = dy + row * d;
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float sh = 0.0f, shn = 0.0f;
+    for (int64_t j = lane; j < d; j += 32) {
+      const float n = rn_mul(rn_sub(xr[j], mean), rstd);
+      const float h = rn_mul(gr[j], gamma[j]);
+      sh += h;
+      shn += rn_mul(h, n);
+      pg[j] += rn_mul(gr[j], n);
+      pb[j] += gr[j];
+    }
+    sh = warp_sum(sh);
+    shn = warp_sum(shn);
+    const float factor = rn_mul(rstd, inv_dim);
+    float* dr = dx + row * d;
+    for (int64_t j = lane; j < d; j += 32) {
+      const float n = rn_mul(rn_sub(xr[j], mean), rstd);
+      const float h = rn_mul(gr[j], gamma[j]);
+      const float val = rn_mul(factor, rn_sub(rn_sub(rn_mul(dim, h), sh), rn_mul(n, shn)));
+      dr[j] = accumulate ? rn_add(dr[j], val) : val;
+    }
+  }
+  __syncthreads();
+  float* out = partial + (size_t)blockIdx.x * 2 * d;
+  for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
+    float g = 0.0f, b = 0.0f;
+    for (int w = 0; w < kLnWarps; w++) {
+      g += sm[(size_t)w * 2 * d + j];
+      b += sm[(size_t)w * 2 * d + d + j];
+    }
+    out[j] = g;
+    out[d + j] = b;
+  }
+}
+
+// Sums `count` partial rows of width `width` (row stride `stride`) in order.
+__global__ void reduce_partials_kernel(const float* __restrict__ partial, int count,
+                                       int64_t width, int64_t stride, float* __restrict__ out) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= width) return;
+  float s = 0.0f;
+  for (int b = 0; b < count; b++) s += partial[(size_t)b * stride + j];
+  out[j] = s;
+}
+
+// ---- activations -------------------------------------------------------------
+
+// Exact-erf GELU with the reference's binary32 constants
+// (n2_primitives_provider.c:545-583).
+__global__ void gelu_forward_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  const float inv_sqrt_2 = 0x1.6a09e6p-1f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const float e = erff(rn_mul(v, inv_sqrt_2));
+    y[i] = rn_mul(rn_mul(0.5f, v), rn_add(1.0f, e));
+  }
+}
+
+__global__ void gelu_backward_kernel(const float* __restrict__ x, const float* __restrict__ dy,
+                                     float* __restrict__ dx, int64_t n) {
+  const float inv_sqrt_2 = 0x1.6a09e6p-1f, inv_sqrt_2pi = 0x1.988454p-2f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const float cdf = rn_mul(0.5f, rn_add(1.0f, erff(rn_mul(v, inv_sqrt_2))));
+    const float density = rn_mul(expf(-rn_mul(0.5f, rn_mul(v, v))), inv_sqrt_2pi);
+    const float slope = rn_add(cdf, rn_mul(v, density));
+    dx[i] = rn_mul(dy[i], slope);
+  }
+}
+
+__global__ void relu_kernel(const float* __restrict__ x, const float* __restrict__ dy,
+                            float* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    out[i] = v > 0.0f ? (dy ? dy[i] : v) : 0.0f;
+  }
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                           float* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = rn_add(a[i], b[i]);
+}
+
+__global__ void copy_kernel(const float* __restrict__ a, float* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = a[i];
+}
+
+__global__ void split_tf32_kernel(const float* x, float* hi_out, float* __restrict__ lo,
+                                  int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+    lo[i] = v - hi;  // exact: the dropped low mantissa bits
+    hi_out[i] = hi;
+  }
+}
+
+__global__ void finite_kernel(const float* __restrict__ x, int64_t n, int* flag) {
+  bool bad = false;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    bad |= !isfinite(x[i]);
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicExch(flag, 1);
+}
+
+// ---- embedding --------------------------------------------------------------
+
+__global__ void embedding_forward_kernel(const int64_t* __restrict__ ids, const float* __restrict__ w,
+                                         float* __restrict__ y, int64_t rows, int64_t V, int64_t d,
+                                         int* status) {
+  const int64_t row = blockIdx.x;
+  const int64_t id = ids[row];
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) atomicExch(status, 1);
+    return;
+  }
+  const float* src = w + id * d;
+  float* dst = y + row * d;
+  for (int64_t j = threadIdx.x; j < d; j += blockDim.x) dst[j] = src[j];
+}
+
+__global__ void ids_to_keys_kernel(const int64_t* __restrict__ ids, uint32_t* __restrict__ keys,
+                                   uint32_t* __restrict__ vals, int64_t rows) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < rows) {
+    keys[i] = (uint32_t)ids[i];
+    vals[i] = (uint32_t)i;
+  }
+}
+
+// One block per vocabulary row: locate its run in the sorted keys, then sum
+// the matching token rows in ascending row order starting from +0 and add it
+// to the base (the tied head gradient), exactly as the reference orders it.
+__global__ void embedding_backward_kernel(const uint32_t* __restrict__ keys,
+                                          const uint32_t* __restrict__ rows_sorted,
+                                          const float* __restrict__ dy,
+                                          const float* __restrict__ base, float* __restrict__ dw,
+                                          int64_t rows, int64_t d) {
+  const uint32_t v = blockIdx.x;
+  __shared__ int64_t range[2];
+  if (threadIdx.x == 0) {
+    int64_t lo = 0, hi = rows;
+    while (lo < hi) {  // first key >= v
+      const int64_t mid = (lo + hi) >> 1;
+      if (keys[mid] < v) lo = mid + 1; else hi = mid;
+    }
+    int64_t lo2 = lo, hi2 = rows;
+    while (lo2 < hi2) {  // first key > v
+      const int64_t mid = (lo2 + hi2) >> 1;
+      if (keys[mid] <= v) lo2 = mid + 1; else hi2 = mid;
+    }
+    range[0] = lo;
+    range[1] = lo2;
+  }
+  __syncthreads();
+  const int64_t a = range[0], b = range[1];
+  for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
+    float acc = 0.0f;
+    for (int64_t p = a; p < b; p++) acc = rn_add(acc, dy[(int64_t)rows_sorted[p] * d + j]);
+    dw[(int64_t)v * d + j] = base ? rn_add(base[(int64_t)v * d + j], acc) : acc;
+  }
+}
+
+// ---- column sums ------------------------------------------------------------
+
+constexpr int kColRowsChunk = 256;
+
+__global__ void colsum_partial_kernel(const float* __restrict__ dy, float* __restrict__ partial,
+                                      int64_t rows, int64_t n) {
+  __shared__ float sm[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t col = (int64_t)blockIdx.x * 32 + lane;
+  const int64_t r0 = (int64_t)blockIdx.y * kColRowsChunk;
+  const int64_t r1 = min(rows, r0 + kColRowsChunk);
+  float acc = 0.0f;
+  if (col < n)
+    for (int64_t r = r0 + warp; r < r1; r += 8) acc += dy[r * n + col];
+  sm[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && col < n) {
+    float s = 0.0f;
+    for (int w = 0; w < 8; w++) s += sm[w][lane];
+    partial[(int64_t)blockIdx.y * n + col] = s;
+  }
+}
+
+// ---- RoPE -------------------------------------------------------------------
+
+// Pair rotation with the reference's rounding points
+// (a2_attention_provider.c:792-804): forward (a - b, c + d), backward
+// (a + b, -c + d), a = x0 cos, b = x1 sin, c = x0 sin, d = x1 cos.
+__global__ void rope_kernel(const float* __restrict__ x, float* __restrict__ y,
+                            const float* __restrict__ ct, const float* __restrict__ st,
+                            int64_t N, int64_t H, int64_t T, int64_t half, int backward) {
+  const int64_t total = N * H * T * half;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pair = i % half;
+    const int64_t t = (i / half) % T;
+    const int64_t n = i / (half * T * H);
+    const float c = ct[(n * T + t) * half + pair];
+    const float s = st[(n * T + t) * half + pair];
+    const float x0 = x[2 * i], x1 = x[2 * i + 1];
+    const float a = rn_mul(x0, c), b = rn_mul(x1, s), cc = rn_mul(x0, s), dd = rn_mul(x1, c);
+    y[2 * i] = backward ? rn_add(a, b) : rn_sub(a, b);
+    y[2 * i + 1] = backward ? rn_add(-cc, dd) : rn_add(cc, dd);
+  }
+}
+
+unsigned grid_for(int64_t n, int threads) {
+  const int64_t want = (n + threads - 1) / threads;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  return (unsigned)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+}  // namespace
+
+void layer_norm_forward(const float* x, const float* gamma, const float* beta, float epsilon,
+                        float* y, float* mean, float* rstd, size_t rows, size_t d,
+                        cudaStream_t stream) {
+  if (rows == 0) return;
+  ln_forward_kernel<<<ceil_div(rows, kLnWarps), kLnWarps * 32, 0, stream>>>(
+      x, gamma, beta, epsilon, y, mean, rstd, (int64_t)rows, (int64_t)d);
+  count_launch();
+}
+
+size_t ln_workspace_floats(size_t rows, size_t d) {
+  return (size_t)ln_backward_blocks(rows) * 2 * d;
+}
+
+void layer_norm_backward(const float* x, const float* gamma, const float* mean, const float* rstd,
+                         const float* dy, float* dx, int accumulate, float* dgamma, float* dbeta,
+                         float* workspace, size_t rows, size_t d, cudaStream_t stream) {
+  if (rows == 0) return;
+  const int blocks = ln_backward_blocks(rows);
+  const size_t smem = (size_t)kLnWarps * 2 * d * sizeof(float);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(ln_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ln_backward_kernel<<<blocks, kLnWarps * 32, smem, stream>>>(
+      x, gamma, mean, rstd, dy, dx, accumulate, workspace, (int64_t)rows, (int64_t)d);
+  reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace, blocks, (int64_t)d,
+                                                               (int64_t)(2 * d), dgamma);
+  reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + d, blocks, (int64_t)d,
+                                                               (int64_t)(2 * d), dbeta);
+  count_launch(3);
+}
+
+void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream) {
+  gelu_forward_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, y, (int64_t)count);
+  count_launch();
+}
+void gelu_backward(const float* x, const float* dy, float* dx, size_t count, cudaStream_t stream) {
+  gelu_backward_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, dy, dx, (int64_t)count);
+  count_launch();
+}
+void relu_forward(const float* x, float* y, size_t count, cudaStream_t stream) {
+  relu_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, nullptr, y, (int64_t)count);
+  count_launch();
+}
+void relu_backward(const float* x, const float* dy, float* dx, size_t count, cudaStream_t stream) {
+  relu_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, dy, dx, (int64_t)count);
+  count_launch();
+}
+void add_tensors(const float* a, const float* b, float* out, size_t count, cudaStream_t stream) {
+  add_kernel<<<grid_for(count, 256), 256, 0, stream>>>(a, b, out, (int64_t)count);
+  count_launch();
+}
+void copy_tensor(const float* a, float* out, size_t count, cudaStream_t stream) {
+  copy_kernel<<<grid_for(count, 256), 256, 0, stream>>>(a, out, (int64_t)count);
+  count_launch();
+}
+void split_tf32(const float* x, float* hi, float* lo, size_t count, cudaStream_t stream) {
+  if (count == 0) return;
+  split_tf32_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, hi, lo, (int64_t)count);
+  count_launch();
+}
+void check_finite(const float* x, size_t count, int* flag, cudaStream_t stream) {
+  if (count == 0) return;
+  finite_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, (int64_t)count, flag);
+  count_launch();
+}
+
+void embedding_forward(const int64_t* ids, const float* w, float* y, size_t rows, size_t V,
+                       size_t d, int* status, cudaStream_t stream) {
+  if (rows == 0) return;
+  embedding_forward_kernel<<<(unsigned)rows, 128, 0, stream>>>(ids, w, y, (int64_t)rows,
+                                                               (int64_t)V, (int64_t)d, status);
+  count_launch();
+}
+
+static size_t cub_sort_bytes(size_t rows) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                  (const uint32_t*)nullptr, (uint32_t*)nullptr, (int)rows);
+  return (bytes + 255) & ~(size_t)255;
+}
+
+size_t embedding_scratch_bytes(size_t rows, size_t V) {
+  (void)V;
+  const size_t arr = ((rows * sizeof(uint32_t)) + 255) & ~(size_t)255;
+  return 4 * arr + cub_sort_bytes(rows);
+}
+
+void embedding_backward(const int64_t* ids, const float* dy, const float* base, float* dw,
+                        size_t rows, size_t V, size_t d, void* scratch, cudaStream_t stream) {
+  const size_t arr = ((rows * sizeof(uint32_t)) + 255) & ~(size_t)255;
+  uint8_t* p = (uint8_t*)scratch;
+  uint32_t* keys_in = (uint32_t*)p;
+  uint32_t* keys_out = (uint32_t*)(p + arr);
+  uint32_t* vals_in = (uint32_t*)(p + 2 * arr);
+  uint32_t* vals_out = (uint32_t*)(p + 3 * arr);
+  void* temp = p + 4 * arr;
+  size_t temp_bytes = cub_sort_bytes(rows);
+  int end_bit = 1;
+  while (end_bit < 32 && (1ull << end_bit) < V) end_bit++;
+  if (rows > 0) {
+    ids_to_keys_kernel<<<ceil_div(rows, 256), 256, 0, stream>>>(ids, keys_in, vals_in, (int64_t)rows);
+    cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, vals_out,
+                                    (int)rows, 0, end_bit, stream);
+    count_launch(2);
+  }
+  embedding_backward_kernel<<<(unsigned)V, 128, 0, stream>>>(keys_out, vals_out, dy, base, dw,
+                                                             (int64_t)rows, (int64_t)d);
+  count_launch();
+}
+
+size_t colsum_workspace_floats(size_t rows, size_t n) {
+  return ((rows + kColRowsChunk - 1) / kColRowsChunk) * n;
+}
+
+void column_sum(const float* dy, float* out, size_t rows, size_t n, float* workspace,
+                cudaStream_t stream) {
+  const unsigned chunks = ceil_div(rows, kColRowsChunk);
+  if (chunks == 0) {
+    cudaMemsetAsync(out, 0, n * sizeof(float), stream);
+    return;
+  }
+  dim3 grid(ceil_div(n, 32), chunks);
+  colsum_partial_kernel<<<grid, 256, 0, stream>>>(dy, workspace, (int64_t)rows, (int64_t)n);
+  reduce_partials_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(workspace, (int)chunks, (int64_t)n,
+                                                               (int64_t)n, out);
+  count_launch(2);
+}
+
+void rope_apply(const float* x, float* y, const float* cos_table, const float* sin_table, size_t N,
+                size_t H, size_t T, size_t Dh, int backward, cudaStream_t stream) {
+  const int64_t total = (int64_t)(N * H * T * (Dh / 2));
+  if (total == 0) return;
+  rope_kernel<<<grid_for(total, 256), 256, 0, stream>>>(x, y, cos_table, sin_table, (int64_t)N,
+                                                        (int64_t)H, (int64_t)T, (int64_t)(Dh / 2),
+                                                        backward);
+  count_launch();
+}
+
+}  // namespace etb

@@ -1,0 +1,871 @@
+// Decoder-only LM training step on one B200 (and across ranks with NCCL).
+//
+// The composition follows the reference's fixed M3 schedule
+// (native/m3_schedule.esk:3-52; roles in src/eshkol_transformer/m3t_transport.c:
+// 516-563) with RoPE on Q/K instead of learned positions and biased linears:
+//   forward   x0 = E[ids]; per layer h = LN1(x); qkv = h Wqkv^T + b;
+//             o = attention(RoPE(q), RoPE(k), v); x' = x + o Wo^T + b;
+//             h2 = LN2(x'); x'' = x' + GELU(h2 W1^T + b1) W2^T + b2;
+//             logits = LN_f(x_L) E^T; loss = CE(logits, targets)
+//   backward  the reverse schedule, with the tied embedding gradient summed
+//             head first (m3t_transport.c:562);
+//   update    AdamW over every tensor (o2_optimizer.c:1738-1756).
+// The CE backward carries the 1/N token weight (N = global tokens) that the
+// reference applies as the O2 normalisation weight; for N = 2^k that move is
+// exact.  Activations live in HBM for the whole step (f32), laid out token-
+// major [rows, features]; attention reads Q/K/V straight out of the fused
+// [rows, 3d] QKV buffer and writes its output merged into [rows, d].  In the
+// 3xTF32 mode every GEMM operand is kept as a (hi, lo) pair: producers' outputs
+// are split once, weights after every update.
+//
+// Data parallelism: each rank runs its own batch; after a layer's backward its
+// contiguous gradient slice is summed across ranks by ncclAllReduce on a side
+// stream while the next layer's backward runs; AdamW waits for the last bucket.
+#include <math.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "nccl_loader.cuh"
+#include "ops.cuh"
+
+using namespace etb;
+
+namespace {
+
+enum { kPerLayer = 12 };
+enum {
+  T_LN1G = 0, T_LN1B, T_WQKV, T_BQKV, T_WO, T_BO, T_LN2G, T_LN2B, T_W1, T_B1, T_W2, T_B2
+};
+
+// Profile classes reported by et_b200_lm_profile_read_v1.
+enum {
+  P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_CE, P_ADAMW, P_NORM, P_ELEMENTWISE, P_EMBED,
+  P_SPLIT, P_ALLREDUCE_WAIT, P_COUNT
+};
+
+struct LayerActs {
+  float *x = nullptr, *h1 = nullptr, *h1lo = nullptr, *mu1 = nullptr, *rs1 = nullptr;
+  float *qkv = nullptr, *ao = nullptr, *aolo = nullptr, *am = nullptr, *al = nullptr;
+  float *xmid = nullptr, *h2 = nullptr, *h2lo = nullptr, *mu2 = nullptr, *rs2 = nullptr;
+  float *u = nullptr, *g = nullptr, *glo = nullptr;
+};
+
+struct ProfileMark {
+  int cls;
+  double flop, bytes;
+  cudaEvent_t start, stop;
+};
+
+}  // namespace
+
+struct et_b200_lm {
+  et_b200_lm_config_v1 cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr, comm = nullptr;
+  int64_t L = 0, d = 0, H = 0, Dh = 0, F = 0, V = 0, T = 0, B = 0, R = 0;
+  float ce_scale = 0, eps = 0, attn_scale = 0;
+  int precision = 0;
+  bool three = false;
+  // parameters (flat, tensor order as documented in et_b200.h)
+  size_t P = 0;
+  std::vector<size_t> off, sz;
+  float *params = nullptr, *grads = nullptr, *m1 = nullptr, *m2 = nullptr;
+  float *whi = nullptr, *wlo = nullptr;
+  AdamwTensor* d_adam = nullptr;
+  uint64_t* d_prefix = nullptr;
+  uint64_t updates = 0;
+  // activations
+  std::vector<LayerActs> layers;
+  float *x_final = nullptr, *xf = nullptr, *xflo = nullptr, *muf = nullptr, *rsf = nullptr;
+  float *logits = nullptr, *logits_lo = nullptr, *loss_rows = nullptr, *loss_mean = nullptr;
+  // backward scratch
+  float *dx = nullptr, *dxhi = nullptr, *dxlo = nullptr, *dtmp = nullptr, *dqkv = nullptr,
+        *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *dg = nullptr, *delta = nullptr;
+  float *ln_ws = nullptr, *col_ws = nullptr;
+  void* emb_scratch = nullptr;
+  int64_t *ids = nullptr, *targets = nullptr, *pos = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  int* status = nullptr;  // [0] index range, [1] optimizer nonfinite
+  std::vector<void*> allocations;
+  // data parallel
+  ncclComm_t nccl_comm = nullptr;
+  int rank = 0, world = 1;
+  bool dp = false;
+  std::vector<cudaEvent_t> layer_done;
+  cudaEvent_t tail_done = nullptr, comm_done = nullptr;
+  // profiling
+  bool profile = false;
+  std::vector<ProfileMark> marks;
+  size_t mark_used = 0;
+  double prof[P_COUNT][4] = {};  // launches, ms, flop, bytes
+
+  float* W(int t) { return (three ? whi : params) + off[t]; }
+  float* Wlo(int t) { return three ? wlo + off[t] : nullptr; }
+  float* Pp(int t) { return params + off[t]; }
+  float* G(int t) { return grads + off[t]; }
+  int lt(int l, int j) const { return 1 + l * kPerLayer + j; }
+  int lnf_g() const { return 1 + (int)L * kPerLayer; }
+  int lnf_b() const { return 2 + (int)L * kPerLayer; }
+};
+
+namespace {
+
+// RAII profiling bracket: records an event pair around a launch group when
+// profiling is on.
+struct Mark {
+  et_b200_lm* lm;
+  ProfileMark* m = nullptr;
+  Mark(et_b200_lm* l, int cls, double flop, double bytes) : lm(l) {
+    if (!lm->profile) return;
+    if (lm->mark_used == lm->marks.size()) {
+      ProfileMark pm{};
+      cudaEventCreate(&pm.start);
+      cudaEventCreate(&pm.stop);
+      lm->marks.push_back(pm);
+    }
+    m = &lm->marks[lm->mark_used++];
+    m->cls = cls;
+    m->flop = flop;
+    m->bytes = bytes;
+    cudaEventRecord(m->start, lm->stream);
+  }
+  ~Mark() {
+    if (m) cudaEventRecord(m->stop, lm->stream);
+  }
+};
+
+template <typename T>
+T* dalloc(et_b200_lm* lm, size_t count, cudaError_t* err) {
+  void* p = nullptr;
+  if (count == 0) count = 1;
+  cudaError_t st = cudaMalloc(&p, count * sizeof(T));
+  if (st != cudaSuccess) {
+    *err = st;
+    return nullptr;
+  }
+  lm->allocations.push_back(p);
+  return static_cast<T*>(p);
+}
+
+void tensor_sizes(const et_b200_lm_config_v1& c, std::vector<size_t>& sz) {
+  const size_t d = c.d_model, F = c.ffn, V = c.vocabulary;
+  sz.clear();
+  sz.push_back(V * d);
+  for (int64_t l = 0; l < c.layers; l++) {
+    sz.push_back(d); sz.push_back(d);
+    sz.push_back(3 * d * d); sz.push_back(3 * d);
+    sz.push_back(d * d); sz.push_back(d);
+    sz.push_back(d); sz.push_back(d);
+    sz.push_back(F * d); sz.push_back(F);
+    sz.push_back(d * F); sz.push_back(d);
+  }
+  sz.push_back(d);
+  sz.push_back(d);
+}
+
+float fbits(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
+
+// Square-and-multiply power with one f32 rounding per product
+// (o2_optimizer.c:419-435).
+float pow_steps(float base, uint64_t e) {
+  volatile float result = 1.0f;
+  volatile float b = base;
+  while (e != 0u) {
+    if (e & 1u) result = result * b;
+    e >>= 1u;
+    if (e != 0u) b = b * b;
+  }
+  return result;
+}
+
+void split(et_b200_lm* lm, float* x, float* lo, size_t n) {
+  Mark mk(lm, P_SPLIT, 0, 12.0 * n);
+  split_tf32(x, x, lo, n, lm->stream);
+}
+
+// ---- linear wrappers ---------------------------------------------------------
+
+void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t rows, int64_t din,
+                    int64_t dout, int wt, const float* bias, float* y) {
+  GemmArgs g{};
+  g.M = (int)rows; g.N = (int)dout; g.K = (int)din;
+  g.A = x; g.A_lo = xlo; g.lda = din; g.a_kmajor = true;
+  g.B = lm->W(wt); g.B_lo = lm->Wlo(wt); g.ldb = din; g.b_kmajor = true;
+  g.C = y; g.ldc = dout; g.bias = bias; g.accumulate = false;
+  Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
+  gemm(g, lm->precision, lm->stream);
+}
+
+void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int64_t rows,
+                        int64_t din, int64_t dout, int wt, float* dxo) {
+  GemmArgs g{};
+  g.M = (int)rows; g.N = (int)din; g.K = (int)dout;
+  g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = true;
+  g.B = lm->W(wt); g.B_lo = lm->Wlo(wt); g.ldb = din; g.b_kmajor = false;
+  g.C = dxo; g.ldc = din; g.bias = nullptr; g.accumulate = false;
+  Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
+  gemm(g, lm->precision, lm->stream);
+}
+
+void linear_backward_dw(et_b200_lm* lm, const float* dy, const float* dylo, const float* x,
+                        const float* xlo, int64_t rows, int64_t din, int64_t dout, float* dw) {
+  GemmArgs g{};
+  g.M = (int)dout; g.N = (int)din; g.K = (int)rows;
+  g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = false;
+  g.B = x; g.B_lo = xlo; g.ldb = din; g.b_kmajor = false;
+  g.C = dw; g.ldc = din; g.bias = nullptr; g.accumulate = false;
+  Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
+  gemm(g, lm->precision, lm->stream);
+}
+
+void bias_grad(et_b200_lm* lm, const float* dy, int64_t rows, int64_t n, float* db) {
+  Mark mk(lm, P_ELEMENTWISE, 0, 4.0 * rows * n);
+  column_sum(dy, db, rows, n, lm->col_ws, lm->stream);
+}
+
+AttnParams attn_params(et_b200_lm* lm, const float* qkv) {
+  AttnParams p{};
+  p.B = (int)lm->B; p.Hq = (int)lm->H; p.Hkv = (int)lm->H;
+  p.Tq = (int)lm->T; p.Tk = (int)lm->T; p.Dh = (int)lm->Dh;
+  p.scale = lm->attn_scale;
+  const int64_t w = 3 * lm->d;
+  p.q = AttnTensor{qkv, lm->T * w, lm->Dh, w};
+  p.k = AttnTensor{qkv + lm->d, lm->T * w, lm->Dh, w};
+  p.v = AttnTensor{qkv + 2 * lm->d, lm->T * w, lm->Dh, w};
+  p.qpos = lm->pos; p.kpos = lm->pos; p.mask = nullptr;
+  p.q_cos = lm->rope_cos; p.q_sin = lm->rope_sin;
+  p.k_cos = lm->rope_cos; p.k_sin = lm->rope_sin;
+  p.q_rope_batched = 0; p.k_rope_batched = 0;
+  return p;
+}
+
+double attn_flop(et_b200_lm* lm, double gemms) {
+  // causal: half of the dense B*H*T^2*Dh work per 2-FLOP GEMM
+  return gemms * 2.0 * lm->B * lm->H * (double)lm->T * lm->T * lm->Dh * 0.5;
+}
+
+// ---- forward -------------------------------------------------------------------
+
+void forward(et_b200_lm* lm) {
+  const int64_t R = lm->R, d = lm->d, F = lm->F, V = lm->V;
+  cudaStream_t s = lm->stream;
+  {
+    Mark mk(lm, P_EMBED, 0, 8.0 * R * d);
+    embedding_forward(lm->ids, lm->Pp(0), lm->layers[0].x, R, V, d, lm->status, s);
+  }
+  for (int l = 0; l < lm->L; l++) {
+    LayerActs& a = lm->layers[l];
+    float* xnext = (l + 1 < lm->L) ? lm->layers[l + 1].x : lm->x_final;
+    {
+      Mark mk(lm, P_NORM, 0, 8.0 * R * d);
+      layer_norm_forward(a.x, lm->Pp(lm->lt(l, T_LN1G)), lm->Pp(lm->lt(l, T_LN1B)), lm->eps, a.h1,
+                         a.mu1, a.rs1, R, d, s);
+    }
+    if (lm->three) split(lm, a.h1, a.h1lo, R * d);
+    linear_forward(lm, a.h1, a.h1lo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->Pp(lm->lt(l, T_BQKV)),
+                   a.qkv);
+    {
+      AttnParams p = attn_params(lm, a.qkv);
+      Mark mk(lm, P_ATTN_FWD, attn_flop(lm, 2), 0);
+      attention_forward(p, AttnOut{a.ao, lm->T * d, lm->Dh, d}, a.am, a.al, s);
+    }
+    if (lm->three) split(lm, a.ao, a.aolo, R * d);
+    linear_forward(lm, a.ao, a.aolo, R, d, d, lm->lt(l, T_WO), lm->Pp(lm->lt(l, T_BO)), lm->dtmp);
+    {
+      Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * d);
+      add_tensors(a.x, lm->dtmp, a.xmid, R * d, s);
+    }
+    {
+      Mark mk(lm, P_NORM, 0, 8.0 * R * d);
+      layer_norm_forward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), lm->Pp(lm->lt(l, T_LN2B)), lm->eps,
+                         a.h2, a.mu2, a.rs2, R, d, s);
+    }
+    if (lm->three) split(lm, a.h2, a.h2lo, R * d);
+    linear_forward(lm, a.h2, a.h2lo, R, d, F, lm->lt(l, T_W1), lm->Pp(lm->lt(l, T_B1)), a.u);
+    {
+      Mark mk(lm, P_ELEMENTWISE, 0, 8.0 * R * F);
+      gelu_forward(a.u, a.g, R * F, s);
+    }
+    if (lm->three) split(lm, a.g, a.glo, R * F);
+    linear_forward(lm, a.g, a.glo, R, F, d, lm->lt(l, T_W2), lm->Pp(lm->lt(l, T_B2)), lm->dtmp);
+    {
+      Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * d);
+      add_tensors(a.xmid, lm->dtmp, xnext, R * d, s);
+    }
+  }
+  {
+    Mark mk(lm, P_NORM, 0, 8.0 * R * d);
+    layer_norm_forward(lm->x_final, lm->Pp(lm->lnf_g()), lm->Pp(lm->lnf_b()), lm->eps, lm->xf,
+                       lm->muf, lm->rsf, R, d, s);
+  }
+  if (lm->three) split(lm, lm->xf, lm->xflo, R * d);
+  linear_forward(lm, lm->xf, lm->xflo, R, d, V, 0, nullptr, lm->logits);
+  {
+    Mark mk(lm, P_CE, 0, 8.0 * R * V + 12.0 * R);
+    ce_fused(lm->logits, lm->logits, lm->targets, nullptr, lm->ce_scale, lm->loss_rows, R, V,
+             lm->status, s);
+    mean_loss(lm->loss_rows, R, lm->loss_mean, s);
+  }
+}
+
+// ---- backward --------------------------------------------------------------------
+
+void allreduce_range(et_b200_lm* lm, int t_begin, int t_end, cudaEvent_t ready) {
+  if (!lm->dp) return;
+  cudaEventRecord(ready, lm->stream);
+  cudaStreamWaitEvent(lm->comm, ready, 0);
+  const size_t begin = lm->off[t_begin];
+  const size_t end = lm->off[t_end - 1] + lm->sz[t_end - 1];
+  nccl().AllReduce(lm->grads + begin, lm->grads + begin, end - begin, ncclFloat32, ncclSum,
+                   lm->nccl_comm, lm->comm);
+}
+
+void backward(et_b200_lm* lm) {
+  const int64_t R = lm->R, d = lm->d, F = lm->F, V = lm->V;
+  cudaStream_t s = lm->stream;
+  const bool three = lm->three;
+  // head (tied): dlogits already in place of the logits
+  float* dlog = lm->logits;
+  if (three) split(lm, dlog, lm->logits_lo, R * V);
+  linear_backward_dx(lm, dlog, lm->logits_lo, R, d, V, 0, lm->dtmp);
+  linear_backward_dw(lm, dlog, lm->logits_lo, lm->xf, lm->xflo, R, d, V, lm->G(0));
+  {
+    Mark mk(lm, P_NORM, 0, 16.0 * R * d);
+    layer_norm_backward(lm->x_final, lm->Pp(lm->lnf_g()), lm->muf, lm->rsf, lm->dtmp, lm->dx, 0,
+                        lm->G(lm->lnf_g()), lm->G(lm->lnf_b()), lm->ln_ws, R, d, s);
+  }
+  for (int l = (int)lm->L - 1; l >= 0; l--) {
+    LayerActs& a = lm->layers[l];
+    // FFN down: dY = dx (flows to the skip and the branch)
+    bias_grad(lm, lm->dx, R, d, lm->G(lm->lt(l, T_B2)));
+    const float* dyh = lm->dx;
+    const float* dyl = nullptr;
+    if (three) {
+      Mark mk(lm, P_SPLIT, 0, 12.0 * R * d);
+      split_tf32(lm->dx, lm->dxhi, lm->dxlo, R * d, s);
+      dyh = lm->dxhi;
+      dyl = lm->dxlo;
+    }
+    linear_backward_dx(lm, dyh, dyl, R, F, d, lm->lt(l, T_W2), lm->dg);
+    linear_backward_dw(lm, dyh, dyl, a.g, a.glo, R, F, d, lm->G(lm->lt(l, T_W2)));
+    {
+      Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * F);
+      gelu_backward(a.u, lm->dg, lm->du, R * F, s);
+    }
+    bias_grad(lm, lm->du, R, F, lm->G(lm->lt(l, T_B1)));
+    if (three) split(lm, lm->du, lm->dulo, R * F);
+    linear_backward_dx(lm, lm->du, lm->dulo, R, d, F, lm->lt(l, T_W1), lm->dtmp);
+    linear_backward_dw(lm, lm->du, lm->dulo, a.h2, a.h2lo, R, d, F, lm->G(lm->lt(l, T_W1)));
+    {
+      Mark mk(lm, P_NORM, 0, 20.0 * R * d);
+      layer_norm_backward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), a.mu2, a.rs2, lm->dtmp, lm->dx, 1,
+                          lm->G(lm->lt(l, T_LN2G)), lm->G(lm->lt(l, T_LN2B)), lm->ln_ws, R, d, s);
+    }
+    // attention output projection: dY = dx
+    bias_grad(lm, lm->dx, R, d, lm->G(lm->lt(l, T_BO)));
+    dyh = lm->dx;
+    dyl = nullptr;
+    if (three) {
+      Mark mk(lm, P_SPLIT, 0, 12.0 * R * d);
+      split_tf32(lm->dx, lm->dxhi, lm->dxlo, R * d, s);
+      dyh = lm->dxhi;
+      dyl = lm->dxlo;
+    }
+    linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp);
+    linear_backward_dw(lm, dyh, dyl, a.ao, a.aolo, R, d, d, lm->G(lm->lt(l, T_WO)));
+    {
+      AttnParams p = attn_params(lm, a.qkv);
+      Mark mk(lm, P_ATTN_BWD, attn_flop(lm, 4), 0);
+      const int64_t w = 3 * d;
+      attention_backward(p, AttnTensor{a.ao, lm->T * d, lm->Dh, d}, a.aolo,
+                         AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d}, a.am, a.al, lm->delta,
+                         AttnOut{lm->dqkv, lm->T * w, lm->Dh, w},
+                         AttnOut{lm->dqkv + d, lm->T * w, lm->Dh, w},
+                         AttnOut{lm->dqkv + 2 * d, lm->T * w, lm->Dh, w}, s);
+    }
+    bias_grad(lm, lm->dqkv, R, 3 * d, lm->G(lm->lt(l, T_BQKV)));
+    if (three) split(lm, lm->dqkv, lm->dqkvlo, R * 3 * d);
+    linear_backward_dx(lm, lm->dqkv, lm->dqkvlo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->dtmp);
+    linear_backward_dw(lm, lm->dqkv, lm->dqkvlo, a.h1, a.h1lo, R, d, 3 * d,
+                       lm->G(lm->lt(l, T_WQKV)));
+    {
+      Mark mk(lm, P_NORM, 0, 20.0 * R * d);
+      layer_norm_backward(a.x, lm->Pp(lm->lt(l, T_LN1G)), a.mu1, a.rs1, lm->dtmp, lm->dx, 1,
+                          lm->G(lm->lt(l, T_LN1G)), lm->G(lm->lt(l, T_LN1B)), lm->ln_ws, R, d, s);
+    }
+    allreduce_range(lm, lm->lt(l, 0), lm->lt(l, 0) + kPerLayer, lm->layer_done[l]);
+  }
+  {
+    Mark mk(lm, P_EMBED, 0, 12.0 * V * d + 8.0 * R * d);
+    embedding_backward(lm->ids, lm->dx, lm->G(0), lm->G(0), R, V, d, lm->emb_scratch, s);
+  }
+  if (lm->dp) {
+    allreduce_range(lm, 0, 1, lm->tail_done);
+    const int lg = lm->lnf_g();
+    nccl().AllReduce(lm->G(lg), lm->G(lg), lm->sz[lg] + lm->sz[lg + 1], ncclFloat32, ncclSum,
+                     lm->nccl_comm, lm->comm);
+    cudaEventRecord(lm->comm_done, lm->comm);
+    Mark mk(lm, P_ALLREDUCE_WAIT, 0, 0);
+    cudaStreamWaitEvent(s, lm->comm_done, 0);
+  }
+}
+
+void refresh_weight_split(et_b200_lm* lm) {
+  if (!lm->three) return;
+  Mark mk(lm, P_SPLIT, 0, 12.0 * lm->P);
+  split_tf32(lm->params, lm->whi, lm->wlo, lm->P, lm->stream);
+}
+
+void optimizer_step(et_b200_lm* lm) {
+  const et_b200_lm_config_v1& c = lm->cfg;
+  const uint64_t t = lm->updates + 1;
+  AdamwTensor h{};
+  h.value = lm->params;
+  h.grad = lm->grads;
+  h.exp_avg = lm->m1;
+  h.exp_avg_sq = lm->m2;
+  h.count = lm->P;
+  volatile float b1 = fbits(c.beta1_bits), b2 = fbits(c.beta2_bits);
+  volatile float one = 1.0f;
+  h.beta1 = b1;
+  h.beta2 = b2;
+  h.one_minus_beta1 = one - b1;
+  h.one_minus_beta2 = one - b2;
+  h.bias1 = one - pow_steps(b1, t);
+  h.bias2 = one - pow_steps(b2, t);
+  volatile float lr = fbits(c.learning_rate_bits) * 1.0f;  // constant schedule factor 1
+  volatile float lrwd = lr * fbits(c.weight_decay_bits);
+  h.lr = lr;
+  h.decay = one - lrwd;
+  h.epsilon = fbits(c.epsilon_bits);
+  cudaMemcpyAsync(lm->d_adam, &h, sizeof(h), cudaMemcpyHostToDevice, lm->stream);
+  {
+    Mark mk(lm, P_ADAMW, 0, 28.0 * lm->P);
+    adamw_multi(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, lm->status, lm->stream);
+  }
+  lm->updates = t;
+  refresh_weight_split(lm);
+}
+
+int32_t check_ready(et_b200_lm* lm, et_kernel_error* e, const char* op) {
+  if (lm == nullptr) return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, op, "model is null");
+  cudaSetDevice(lm->device);
+  return 0;
+}
+
+int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, const char* op) {
+  float loss = 0.0f;
+  int flags[2] = {0, 0};
+  int word = 0;
+  cudaMemcpyAsync(&loss, lm->loss_mean, sizeof(float), cudaMemcpyDeviceToHost, lm->stream);
+  cudaMemcpyAsync(flags, lm->status, sizeof(flags), cudaMemcpyDeviceToHost, lm->stream);
+  cudaMemcpyAsync(&word, device_error_word(), sizeof(int), cudaMemcpyDeviceToHost, lm->stream);
+  cudaError_t st = cudaStreamSynchronize(lm->stream);
+  if (st != cudaSuccess) return cuda_error(e, st, op);
+  if (host_loss) *host_loss = loss;
+  if (word != 0) {
+    cudaMemset(device_error_word(), 0, sizeof(int));
+    return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "a device pipeline wait timed out");
+  }
+  if (flags[0] || flags[1]) {
+    cudaMemsetAsync(lm->status, 0, 2 * sizeof(int), lm->stream);
+    cudaStreamSynchronize(lm->stream);
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     flags[0] ? "token id or target outside the vocabulary"
+                              : "AdamW produced a nonfinite value");
+  }
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+void collect_profile(et_b200_lm* lm) {
+  if (!lm->profile) return;
+  for (size_t i = 0; i < lm->mark_used; i++) {
+    ProfileMark& m = lm->marks[i];
+    float ms = 0.0f;
+    if (cudaEventSynchronize(m.stop) == cudaSuccess &&
+        cudaEventElapsedTime(&ms, m.start, m.stop) == cudaSuccess) {
+      lm->prof[m.cls][0] += 1;
+      lm->prof[m.cls][1] += ms;
+      lm->prof[m.cls][2] += m.flop;
+      lm->prof[m.cls][3] += m.bytes;
+    }
+  }
+  lm->mark_used = 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
+                             et_kernel_error* e) {
+  const char* op = "lm-create";
+  if (c == nullptr || out == nullptr)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, op, "config and output are required");
+  *out = nullptr;
+  if (c->struct_size < sizeof(et_b200_lm_config_v1))
+    return set_error(e, ET_KERNEL_ERROR_VERSION_MISMATCH, ET_KERNEL_CODE_INVALID_STRUCT_SIZE, op, "config is truncated");
+  if (c->layers < 1 || c->d_model < 2 || c->heads < 1 || c->d_model % c->heads != 0 ||
+      (c->d_model / c->heads) % 2 != 0 || c->d_model / c->heads > 128 || c->ffn < 1 ||
+      c->vocabulary < 1 || c->seq_len < 1 || c->batch < 1 || c->precision > 2)
+    return set_error(e, ET_KERNEL_ERROR_SHAPE_MISMATCH, ET_KERNEL_CODE_INVALID_SHAPE, op,
+                     "unsupported model shape (head dim must be even and <= 128)");
+  int32_t rc = et_b200_device_check_v1(e);
+  if (rc != 0) return rc;
+  et_b200_lm* lm = new et_b200_lm();
+  lm->cfg = *c;
+  cudaGetDevice(&lm->device);
+  lm->L = c->layers; lm->d = c->d_model; lm->H = c->heads; lm->Dh = c->d_model / c->heads;
+  lm->F = c->ffn; lm->V = c->vocabulary; lm->T = c->seq_len; lm->B = c->batch;
+  lm->R = lm->B * lm->T;
+  const double global = c->global_tokens > 0 ? (double)c->global_tokens : (double)lm->R;
+  lm->ce_scale = (float)(1.0 / global);
+  lm->eps = fbits(c->ln_epsilon_bits);
+  {
+    volatile float root = sqrtf((float)lm->Dh);
+    lm->attn_scale = 1.0f / root;
+  }
+  lm->precision = (int)c->precision;
+  lm->three = c->precision == ET_B200_PRECISION_TF32X3;
+  tensor_sizes(*c, lm->sz);
+  lm->off.resize(lm->sz.size());
+  size_t total = 0;
+  for (size_t i = 0; i < lm->sz.size(); i++) {
+    lm->off[i] = total;
+    total += (lm->sz[i] + 3) & ~(size_t)3;  // keep every tensor 16-byte aligned
+  }
+  lm->P = total;
+  cudaError_t err = cudaSuccess;
+  const int64_t R = lm->R, d = lm->d, F = lm->F, V = lm->V, L = lm->L;
+  cudaStreamCreateWithFlags(&lm->stream, cudaStreamNonBlocking);
+  cudaStreamCreateWithFlags(&lm->comm, cudaStreamNonBlocking);
+  lm->params = dalloc<float>(lm, lm->P, &err);
+  lm->grads = dalloc<float>(lm, lm->P, &err);
+  lm->m1 = dalloc<float>(lm, lm->P, &err);
+  lm->m2 = dalloc<float>(lm, lm->P, &err);
+  if (lm->three) {
+    lm->whi = dalloc<float>(lm, lm->P, &err);
+    lm->wlo = dalloc<float>(lm, lm->P, &err);
+  }
+  lm->d_adam = dalloc<AdamwTensor>(lm, 1, &err);
+  lm->d_prefix = dalloc<uint64_t>(lm, 2, &err);
+  lm->layers.resize(L);
+  for (int64_t l = 0; l < L; l++) {
+    LayerActs& a = lm->layers[l];
+    a.x = dalloc<float>(lm, R * d, &err);
+    a.h1 = dalloc<float>(lm, R * d, &err);
+    a.mu1 = dalloc<float>(lm, R, &err);
+    a.rs1 = dalloc<float>(lm, R, &err);
+    a.qkv = dalloc<float>(lm, R * 3 * d, &err);
+    a.ao = dalloc<float>(lm, R * d, &err);
+    a.am = dalloc<float>(lm, R * lm->H, &err);
+    a.al = dalloc<float>(lm, R * lm->H, &err);
+    a.xmid = dalloc<float>(lm, R * d, &err);
+    a.h2 = dalloc<float>(lm, R * d, &err);
+    a.mu2 = dalloc<float>(lm, R, &err);
+    a.rs2 = dalloc<float>(lm, R, &err);
+    a.u = dalloc<float>(lm, R * F, &err);
+    a.g = dalloc<float>(lm, R * F, &err);
+    if (lm->three) {
+      a.h1lo = dalloc<float>(lm, R * d, &err);
+      a.aolo = dalloc<float>(lm, R * d, &err);
+      a.h2lo = dalloc<float>(lm, R * d, &err);
+      a.glo = dalloc<float>(lm, R * F, &err);
+    }
+  }
+  lm->x_final = dalloc<float>(lm, R * d, &err);
+  lm->xf = dalloc<float>(lm, R * d, &err);
+  lm->muf = dalloc<float>(lm, R, &err);
+  lm->rsf = dalloc<float>(lm, R, &err);
+  lm->logits = dalloc<float>(lm, (size_t)R * V, &err);
+  lm->loss_rows = dalloc<float>(lm, R, &err);
+  lm->loss_mean = dalloc<float>(lm, 1, &err);
+  lm->dx = dalloc<float>(lm, R * d, &err);
+  lm->dtmp = dalloc<float>(lm, R * d, &err);
+  lm->dqkv = dalloc<float>(lm, R * 3 * d, &err);
+  lm->du = dalloc<float>(lm, R * F, &err);
+  lm->dg = dalloc<float>(lm, R * F, &err);
+  lm->delta = dalloc<float>(lm, R * lm->H, &err);
+  if (lm->three) {
+    lm->xflo = dalloc<float>(lm, R * d, &err);
+    lm->logits_lo = dalloc<float>(lm, (size_t)R * V, &err);
+    lm->dxhi = dalloc<float>(lm, R * d, &err);
+    lm->dxlo = dalloc<float>(lm, R * d, &err);
+    lm->dqkvlo = dalloc<float>(lm, R * 3 * d, &err);
+    lm->dulo = dalloc<float>(lm, R * F, &err);
+  }
+  const size_t widest = (size_t)std::max<int64_t>(3 * d, F);
+  lm->ln_ws = dalloc<float>(lm, ln_workspace_floats(R, d), &err);
+  lm->col_ws = dalloc<float>(lm, colsum_workspace_floats(R, widest), &err);
+  lm->emb_scratch = dalloc<uint8_t>(lm, embedding_scratch_bytes(R, V), &err);
+  lm->ids = dalloc<int64_t>(lm, R, &err);
+  lm->targets = dalloc<int64_t>(lm, R, &err);
+  lm->pos = dalloc<int64_t>(lm, R, &err);
+  lm->rope_cos = dalloc<float>(lm, lm->T * lm->Dh / 2, &err);
+  lm->rope_sin = dalloc<float>(lm, lm->T * lm->Dh / 2, &err);
+  lm->status = dalloc<int>(lm, 4, &err);
+  if (err != cudaSuccess) {
+    et_b200_lm_destroy_v1(&lm);
+    return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_ALLOCATION_FAILED, op,
+                     "device memory for the model and activations is insufficient");
+  }
+  // positions 0..T-1 per sequence; RoPE tables from libm on the host
+  std::vector<int64_t> pos(R);
+  for (int64_t b = 0; b < lm->B; b++)
+    for (int64_t t = 0; t < lm->T; t++) pos[b * lm->T + t] = t;
+  const int64_t half = lm->Dh / 2;
+  std::vector<float> inv(half), ct(lm->T * half), st(lm->T * half);
+  for (int64_t i = 0; i < half; i++)
+    inv[i] = (float)(1.0 / pow(c->rope_base, (double)(2 * i) / (double)lm->Dh));
+  for (int64_t t = 0; t < lm->T; t++)
+    for (int64_t i = 0; i < half; i++) {
+      volatile float angle = (float)t * inv[i];
+      ct[t * half + i] = cosf(angle);
+      st[t * half + i] = sinf(angle);
+    }
+  const uint64_t prefix[2] = {0, lm->P};
+  cudaMemcpy(lm->pos, pos.data(), R * sizeof(int64_t), cudaMemcpyHostToDevice);
+  cudaMemcpy(lm->rope_cos, ct.data(), ct.size() * sizeof(float), cudaMemcpyHostToDevice);
+  cudaMemcpy(lm->rope_sin, st.data(), st.size() * sizeof(float), cudaMemcpyHostToDevice);
+  cudaMemcpy(lm->d_prefix, prefix, sizeof(prefix), cudaMemcpyHostToDevice);
+  cudaMemset(lm->params, 0, lm->P * sizeof(float));
+  cudaMemset(lm->grads, 0, lm->P * sizeof(float));
+  cudaMemset(lm->m1, 0, lm->P * sizeof(float));
+  cudaMemset(lm->m2, 0, lm->P * sizeof(float));
+  cudaMemset(lm->status, 0, 4 * sizeof(int));
+  lm->layer_done.resize(L);
+  for (auto& ev : lm->layer_done) cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&lm->tail_done, cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&lm->comm_done, cudaEventDisableTiming);
+  err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) {
+    et_b200_lm_destroy_v1(&lm);
+    return cuda_error(e, err, op);
+  }
+  *out = lm;
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+void et_b200_lm_destroy_v1(et_b200_lm** slot) {
+  if (slot == nullptr || *slot == nullptr) return;
+  et_b200_lm* lm = *slot;
+  cudaSetDevice(lm->device);
+  if (lm->stream) cudaStreamSynchronize(lm->stream);
+  if (lm->comm) cudaStreamSynchronize(lm->comm);
+  if (lm->nccl_comm && nccl().ok) nccl().CommDestroy(lm->nccl_comm);
+  for (void* p : lm->allocations) cudaFree(p);
+  for (auto& ev : lm->layer_done) cudaEventDestroy(ev);
+  if (lm->tail_done) cudaEventDestroy(lm->tail_done);
+  if (lm->comm_done) cudaEventDestroy(lm->comm_done);
+  for (auto& m : lm->marks) {
+    cudaEventDestroy(m.start);
+    cudaEventDestroy(m.stop);
+  }
+  if (lm->stream) cudaStreamDestroy(lm->stream);
+  if (lm->comm) cudaStreamDestroy(lm->comm);
+  delete lm;
+  *slot = nullptr;
+}
+
+size_t et_b200_lm_tensor_count_v1(const et_b200_lm* lm) { return lm ? lm->sz.size() : 0; }
+
+size_t et_b200_lm_parameter_count_v1(const et_b200_lm* lm) {
+  if (!lm) return 0;
+  size_t n = 0;
+  for (size_t s : lm->sz) n += s;
+  return n;
+}
+
+int32_t et_b200_lm_tensor_sizes_v1(const et_b200_lm* lm, size_t* sizes) {
+  if (!lm || !sizes) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  for (size_t i = 0; i < lm->sz.size(); i++) sizes[i] = lm->sz[i];
+  return 0;
+}
+
+// Host copies use the packed order (tensor after tensor, no alignment gaps).
+static int32_t transfer(et_b200_lm* lm, int32_t which, float* host, const float* src_host,
+                        size_t count, et_kernel_error* e, bool to_device) {
+  const char* op = to_device ? "lm-write" : "lm-read";
+  if (check_ready(lm, e, op)) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  float* base = which == 0 ? lm->params : which == 1 ? lm->grads : which == 2 ? lm->m1 :
+                which == 3 ? lm->m2 : nullptr;
+  if (base == nullptr)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_INVALID_ENUM, op, "unknown buffer selector");
+  if (count != et_b200_lm_parameter_count_v1(lm))
+    return set_error(e, ET_KERNEL_ERROR_SHAPE_MISMATCH, ET_KERNEL_CODE_BUFFER_TOO_SMALL, op, "count must equal the parameter count");
+  cudaStreamSynchronize(lm->stream);
+  size_t packed = 0;
+  for (size_t t = 0; t < lm->sz.size(); t++) {
+    cudaError_t st = to_device
+        ? cudaMemcpy(base + lm->off[t], src_host + packed, lm->sz[t] * 4, cudaMemcpyHostToDevice)
+        : cudaMemcpy(host + packed, base + lm->off[t], lm->sz[t] * 4, cudaMemcpyDeviceToHost);
+    if (st != cudaSuccess) return cuda_error(e, st, op);
+    packed += lm->sz[t];
+  }
+  if (to_device && which == 0) refresh_weight_split(lm);
+  cudaError_t st = cudaStreamSynchronize(lm->stream);
+  if (st != cudaSuccess) return cuda_error(e, st, op);
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+int32_t et_b200_lm_read_v1(et_b200_lm* lm, int32_t which, float* host, size_t count,
+                           et_kernel_error* e) {
+  return transfer(lm, which, host, nullptr, count, e, false);
+}
+
+int32_t et_b200_lm_write_v1(et_b200_lm* lm, int32_t which, const float* host, size_t count,
+                            et_kernel_error* e) {
+  return transfer(lm, which, nullptr, host, count, e, true);
+}
+
+int32_t et_b200_lm_init_v1(et_b200_lm* lm, uint64_t seed, et_kernel_error* e) {
+  if (check_ready(lm, e, "lm-init")) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  const size_t n = et_b200_lm_parameter_count_v1(lm);
+  std::vector<float> host(n);
+  size_t packed = 0;
+  const size_t count = lm->sz.size();
+  for (size_t t = 0; t < count; t++) {
+    int kind;  // 0 weight N(0, 0.02), 1 gamma, 2 zero
+    if (t == 0) kind = 0;
+    else if (t >= count - 2) kind = (t == count - 2) ? 1 : 2;
+    else {
+      const size_t j = (t - 1) % kPerLayer;
+      kind = (j == T_LN1G || j == T_LN2G) ? 1
+             : (j == T_WQKV || j == T_WO || j == T_W1 || j == T_W2) ? 0 : 2;
+    }
+    if (kind == 0) et_b200_fill_normal_v1(seed, t, lm->sz[t], 0.0, 0.02, host.data() + packed);
+    else
+      for (size_t i = 0; i < lm->sz[t]; i++) host[packed + i] = kind == 1 ? 1.0f : 0.0f;
+    packed += lm->sz[t];
+  }
+  lm->updates = 0;
+  cudaMemset(lm->m1, 0, lm->P * sizeof(float));
+  cudaMemset(lm->m2, 0, lm->P * sizeof(float));
+  return et_b200_lm_write_v1(lm, 0, host.data(), n, e);
+}
+
+static int32_t stage_tokens(et_b200_lm* lm, const int64_t* ids, const int64_t* targets,
+                            cudaMemcpyKind kind) {
+  cudaMemcpyAsync(lm->ids, ids, lm->R * sizeof(int64_t), kind, lm->stream);
+  cudaMemcpyAsync(lm->targets, targets, lm->R * sizeof(int64_t), kind, lm->stream);
+  return 0;
+}
+
+int32_t et_b200_lm_step_device_v1(et_b200_lm* lm, const int64_t* device_ids,
+                                  const int64_t* device_targets, float* device_loss,
+                                  et_kernel_error* e) {
+  if (check_ready(lm, e, "lm-step")) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  if (device_ids == nullptr || device_targets == nullptr)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, "lm-step", "ids and targets are required");
+  if (device_ids != lm->ids) stage_tokens(lm, device_ids, device_targets, cudaMemcpyDeviceToDevice);
+  forward(lm);
+  backward(lm);
+  optimizer_step(lm);
+  if (device_loss)
+    cudaMemcpyAsync(device_loss, lm->loss_mean, sizeof(float), cudaMemcpyDeviceToDevice, lm->stream);
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return cuda_error(e, st, "lm-step");
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+int32_t et_b200_lm_step_v1(et_b200_lm* lm, const int64_t* host_ids, const int64_t* host_targets,
+                           float* host_loss, et_kernel_error* e) {
+  if (check_ready(lm, e, "lm-step")) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  if (host_ids == nullptr || host_targets == nullptr)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, "lm-step", "ids and targets are required");
+  stage_tokens(lm, host_ids, host_targets, cudaMemcpyHostToDevice);
+  forward(lm);
+  backward(lm);
+  optimizer_step(lm);
+  const int32_t rc = finish_host_step(lm, host_loss, e, "lm-step");
+  collect_profile(lm);
+  return rc;
+}
+
+int32_t et_b200_lm_forward_backward_v1(et_b200_lm* lm, const int64_t* host_ids,
+                                       const int64_t* host_targets, float* host_loss,
+                                       et_kernel_error* e) {
+  if (check_ready(lm, e, "lm-forward-backward")) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  if (host_ids == nullptr || host_targets == nullptr)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, "lm-forward-backward", "ids and targets are required");
+  stage_tokens(lm, host_ids, host_targets, cudaMemcpyHostToDevice);
+  forward(lm);
+  backward(lm);
+  const int32_t rc = finish_host_step(lm, host_loss, e, "lm-forward-backward");
+  collect_profile(lm);
+  return rc;
+}
+
+void* et_b200_lm_stream_v1(et_b200_lm* lm) { return lm ? (void*)lm->stream : nullptr; }
+
+int32_t et_b200_nccl_unique_id_v1(uint8_t unique_id[128], et_kernel_error* e) {
+  if (!nccl().ok)
+    return set_error(e, ET_KERNEL_ERROR_UNSUPPORTED, ET_KERNEL_CODE_SYMBOL_MISSING, "nccl-id", "libnccl.so.2 is not available");
+  ncclUniqueId id;
+  if (nccl().GetUniqueId(&id) != ncclSuccess)
+    return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, "nccl-id", "ncclGetUniqueId failed");
+  static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+  memcpy(unique_id, &id, 128);
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+int32_t et_b200_lm_enable_data_parallel_v1(et_b200_lm* lm, const uint8_t unique_id[128],
+                                           int32_t rank, int32_t world, et_kernel_error* e) {
+  const char* op = "lm-data-parallel";
+  if (check_ready(lm, e, op)) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  if (world < 1 || rank < 0 || rank >= world)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_INVALID_SHAPE, op, "rank must lie in [0, world)");
+  if (world == 1) {
+    lm->dp = false;
+    return 0;
+  }
+  if (!nccl().ok)
+    return set_error(e, ET_KERNEL_ERROR_UNSUPPORTED, ET_KERNEL_CODE_SYMBOL_MISSING, op, "libnccl.so.2 is not available");
+  ncclUniqueId id;
+  memcpy(&id, unique_id, 128);
+  ncclResult_t r = nccl().CommInitRank(&lm->nccl_comm, world, id, rank);
+  if (r != ncclSuccess) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "ncclCommInitRank failed: %s",
+             nccl().GetErrorString ? nccl().GetErrorString(r) : "?");
+    return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op, msg);
+  }
+  lm->rank = rank;
+  lm->world = world;
+  lm->dp = true;
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+// Profiling: when enabled, every launch group of a step is bracketed by CUDA
+// events on the model's stream.  et_b200_lm_profile_read_v1 returns, per
+// class, {launch groups, milliseconds, algorithmic FLOP, algorithmic bytes}.
+int32_t et_b200_lm_profile_v1(et_b200_lm* lm, int32_t enable) {
+  if (!lm) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  lm->profile = enable != 0;
+  memset(lm->prof, 0, sizeof(lm->prof));
+  lm->mark_used = 0;
+  return 0;
+}
+
+int32_t et_b200_lm_profile_collect_v1(et_b200_lm* lm) {
+  if (!lm) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  collect_profile(lm);
+  return 0;
+}
+
+int32_t et_b200_lm_profile_read_v1(et_b200_lm* lm, double* out, size_t count) {
+  if (!lm || !out || count < (size_t)P_COUNT * 4) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  memcpy(out, lm->prof, sizeof(lm->prof));
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,221 @@
+/*
+ * libet_b200 -- B200 (sm_100a) implementation of eshkol-transformer's f32
+ * training-step hot path behind its K1 kernel ABI.
+ *
+ * Every entry point is plain C: pointers, sizes and the K1 v1 structs.  Each
+ * declaration names the reference interface it replaces (path:line within the
+ * eshkol-transformer project).  Device pointers are CUDA global memory on the
+ * current device; "host" pointers are ordinary (preferably pinned) memory.
+ * Functions returning int32_t return 0 on success or a K1 error category
+ * (ET_KERNEL_ERROR_*) and fill the optional et_kernel_error record.
+ */
+#ifndef ESHKOL_B200_ET_B200_H
+#define ESHKOL_B200_ET_B200_H
+
+#include "eshkol_b200/kernel_abi_v1.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ET_B200_ABI_MAJOR 1u
+#define ET_B200_ABI_MINOR 0u
+
+/* ------------------------------------------------------------ library */
+
+int32_t et_b200_abi_major_v1(void);
+int32_t et_b200_abi_minor_v1(void);
+/* Kernels this library has launched since load (all devices, all threads).
+ * A caller samples it around a region to count the region's launches. */
+uint64_t et_b200_launch_count_v1(void);
+/* 0 when the current CUDA device is an sm_100 part this build runs on. */
+int32_t et_b200_device_check_v1(et_kernel_error *error);
+
+/* ------------------------------------------------------------ K1 providers
+ *
+ * Drop-in replacements for the reference's carrier-neutral providers.  They
+ * accept dense zero-offset views on device "cuda" (device pointers, results
+ * complete when invoke returns) and on device "cpu" (host pointers, staged
+ * through the GPU).  Capabilities are verified for every shape the kernels
+ * support rather than the reference's exact tiny rows.  validate_call keeps
+ * the reference's checks (finite inputs, canonical positions and masks, ids
+ * in range) and its error categories; invoke_call never fails.
+ */
+/* replaces include/eshkol_transformer/a2_attention_abi.h:32
+ * (kernel.causal-attention forward/backward, kernel.rope forward/backward) */
+const et_kernel_provider_v1 *et_a2_kernel_provider_v1(void);
+/* replaces include/eshkol_transformer/n2_primitives_abi.h:18
+ * (kernel.matmul linear.*, kernel.norm, kernel.activation gelu/relu,
+ *  kernel.residual, kernel.embedding-forward/backward) */
+const et_kernel_provider_v1 *et_n2_kernel_provider_v1(void);
+/* replaces include/eshkol_transformer/n3k_primitives_abi.h:12
+ * (n3k.linear forward/backward-no-bias) */
+const et_kernel_provider_v1 *et_n3k_kernel_provider_v1(void);
+/* replaces include/eshkol_transformer/indexed_cross_entropy.h:22-29 */
+int32_t et_l2_indexed_cross_entropy_abi_major_v1(void);
+int32_t et_l2_indexed_cross_entropy_abi_minor_v1(void);
+const et_kernel_provider_v1 *et_l2_indexed_cross_entropy_provider_v1(void);
+/* Contraction mode (ET_B200_PRECISION_*) the kernel.matmul and n3k.linear
+ * providers use; process-wide, default ET_B200_PRECISION_TF32X3.  No
+ * reference counterpart: the reference's only mode is serial FP32. */
+int32_t et_b200_k1_precision_v1(uint32_t precision);
+
+/* ------------------------------------------------------------ synthetic data
+ * Seeded inputs shared with the tests: value i of (seed, stream) is a pure
+ * function of (seed, stream, i).  Host-only; no device is needed. */
+void et_b200_fill_normal_v1(uint64_t seed, uint64_t stream, size_t count,
+                            double mean, double stddev, float *out);
+void et_b200_fill_tokens_v1(uint64_t seed, uint64_t stream, size_t count,
+                            uint64_t vocabulary, int64_t *out);
+
+/* ------------------------------------------------------------ O2 AdamW
+ * Device counterpart of the O2 optimizer (native/o2_optimizer_internal.h:
+ * 137-160 builder/step API; element maths o2_optimizer.c:1738-1756).  The
+ * optimizer owns zero-initialised device moments; parameters and gradients are
+ * caller-owned device tensors.  Each step divides gradients by the
+ * normalisation weight, applies the global-L2 clip factor and the schedule
+ * factor, and updates all tensors in one fused multi-tensor pass whose
+ * per-element arithmetic is bit-identical to the reference. */
+enum { ET_B200_O2_CLIP_NONE = 0, ET_B200_O2_CLIP_GLOBAL_L2 = 1 };
+enum { ET_B200_O2_SCHEDULE_CONSTANT = 0, ET_B200_O2_SCHEDULE_LINEAR = 1 };
+
+typedef struct et_b200_o2_parameter_v1 {
+  size_t struct_size;
+  float *value;    /* device, count f32 */
+  float *gradient; /* device, count f32 (weighted numerators) */
+  size_t count;
+  uint32_t learning_rate_bits;
+  uint32_t beta1_bits;
+  uint32_t beta2_bits;
+  uint32_t epsilon_bits;
+  uint32_t weight_decay_bits;
+  uint32_t reserved;
+} et_b200_o2_parameter_v1;
+
+typedef struct et_b200_o2_optimizer et_b200_o2_optimizer;
+
+/* replaces et_o2_optimizer_builder_create_v1/_set_v1/_finish_v1
+ * (native/o2_optimizer_internal.h:137-150) */
+int32_t et_b200_o2_optimizer_create_v1(
+    size_t parameter_count, const et_b200_o2_parameter_v1 *parameters,
+    uint32_t clip_kind, uint32_t clip_max_bits, uint32_t schedule_kind,
+    uint64_t warmup_updates, uint64_t total_updates,
+    uint32_t minimum_ratio_bits, et_b200_o2_optimizer **optimizer,
+    et_kernel_error *error);
+/* replaces et_o2_optimizer_step_v1 (native/o2_optimizer.c:1784-1944).
+ * normalization_weight_bits is the f32 bit pattern of the accumulated
+ * contribution weight.  norm_bits (optional) receives the global norm. */
+int32_t et_b200_o2_optimizer_step_v1(et_b200_o2_optimizer *optimizer,
+                                     uint32_t normalization_weight_bits,
+                                     uint32_t *norm_bits,
+                                     et_kernel_error *error);
+int32_t et_b200_o2_optimizer_completed_updates_v1(
+    const et_b200_o2_optimizer *optimizer, uint64_t *updates);
+/* Device pointers of parameter `index`'s moments (for checkpoint/inspection). */
+int32_t et_b200_o2_optimizer_moments_v1(et_b200_o2_optimizer *optimizer,
+                                        size_t index, float **exp_avg,
+                                        float **exp_avg_sq);
+void et_b200_o2_optimizer_destroy_v1(et_b200_o2_optimizer **optimizer);
+/* The schedule factor of update `update` as f32 bits: 1 for the constant
+ * schedule; the exactly rounded linear warmup/decay ratio otherwise
+ * (replaces et_o2_schedule_factor, native/o2_optimizer.c:1345-1374). */
+uint32_t et_b200_o2_schedule_factor_v1(uint32_t kind, uint64_t warmup,
+                                       uint64_t total,
+                                       uint32_t minimum_ratio_bits,
+                                       uint64_t update);
+
+/* ------------------------------------------------------------ LM training
+ * A decoder-only LM training step composed from the same primitives in the
+ * reference's schedule order (native/m3_schedule.esk:3-52): token embedding,
+ * L pre-LN blocks (fused QKV linear, RoPE on Q/K, causal attention, output
+ * linear, residual, LN, FFN up, exact-erf GELU, FFN down, residual), final
+ * LN, head tied to the embedding, indexed cross-entropy with the 1/N token
+ * weight fused into its backward, AdamW.  This is the training loop's fast
+ * path: it runs the kernels directly instead of one K1 dispatch per role.
+ */
+enum {
+  ET_B200_PRECISION_TF32X3 = 0, /* 3xTF32 tcgen05 contractions (f32-grade) */
+  ET_B200_PRECISION_TF32 = 1,   /* single TF32 tcgen05 contractions        */
+  ET_B200_PRECISION_F32 = 2     /* FP32 FFMA contractions (no tensor core)  */
+};
+
+typedef struct et_b200_lm_config_v1 {
+  size_t struct_size;
+  int64_t layers;
+  int64_t d_model;
+  int64_t heads;
+  int64_t ffn;
+  int64_t vocabulary;
+  int64_t seq_len;
+  int64_t batch;            /* sequences per step on this rank */
+  int64_t global_tokens;    /* CE weight N across all ranks; 0 = batch*seq */
+  uint32_t ln_epsilon_bits; /* 0x3727c5ac = 1e-5 */
+  uint32_t precision;       /* ET_B200_PRECISION_* */
+  double rope_base;         /* 10000 */
+  uint32_t learning_rate_bits, beta1_bits, beta2_bits, epsilon_bits,
+      weight_decay_bits;
+  uint32_t reserved;
+} et_b200_lm_config_v1;
+
+typedef struct et_b200_lm et_b200_lm;
+
+int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1 *config,
+                             et_b200_lm **lm, et_kernel_error *error);
+void et_b200_lm_destroy_v1(et_b200_lm **lm);
+/* Parameter tensors, in order, and their element counts. */
+size_t et_b200_lm_tensor_count_v1(const et_b200_lm *lm);
+size_t et_b200_lm_parameter_count_v1(const et_b200_lm *lm);
+int32_t et_b200_lm_tensor_sizes_v1(const et_b200_lm *lm, size_t *sizes);
+/* Seeded initialisation: weights N(0, 0.02), LN gammas 1, biases 0. */
+int32_t et_b200_lm_init_v1(et_b200_lm *lm, uint64_t seed,
+                           et_kernel_error *error);
+/* which: 0 parameters, 1 gradients, 2 exp_avg, 3 exp_avg_sq (host copies). */
+int32_t et_b200_lm_read_v1(et_b200_lm *lm, int32_t which, float *host,
+                           size_t count, et_kernel_error *error);
+int32_t et_b200_lm_write_v1(et_b200_lm *lm, int32_t which, const float *host,
+                            size_t count, et_kernel_error *error);
+/* One training step from HOST token ids/targets [batch, seq_len]: copies
+ * them in, runs forward, backward (with the data-parallel gradient allreduce
+ * when enabled), the AdamW update, and copies the mean loss out. */
+int32_t et_b200_lm_step_v1(et_b200_lm *lm, const int64_t *host_ids,
+                           const int64_t *host_targets, float *host_loss,
+                           et_kernel_error *error);
+/* The same step on DEVICE-resident ids/targets; the mean loss stays on the
+ * device (device_loss may be NULL).  Enqueued on the model's stream; returns
+ * without synchronising. */
+int32_t et_b200_lm_step_device_v1(et_b200_lm *lm, const int64_t *device_ids,
+                                  const int64_t *device_targets,
+                                  float *device_loss, et_kernel_error *error);
+/* Forward + backward only (no optimizer update): gradients left in place. */
+int32_t et_b200_lm_forward_backward_v1(et_b200_lm *lm,
+                                       const int64_t *host_ids,
+                                       const int64_t *host_targets,
+                                       float *host_loss,
+                                       et_kernel_error *error);
+/* The cudaStream_t the model enqueues on. */
+void *et_b200_lm_stream_v1(et_b200_lm *lm);
+/* Data parallelism: NCCL communicator over `world` ranks.  unique_id is the
+ * 128-byte ncclUniqueId rank 0 obtained from et_b200_nccl_unique_id_v1 and
+ * shared with every rank.  Gradients are then summed across ranks in buckets
+ * on a side stream as backward produces them. */
+int32_t et_b200_nccl_unique_id_v1(uint8_t unique_id[128],
+                                  et_kernel_error *error);
+int32_t et_b200_lm_enable_data_parallel_v1(et_b200_lm *lm,
+                                           const uint8_t unique_id[128],
+                                           int32_t rank, int32_t world,
+                                           et_kernel_error *error);
+/* Per-kernel-class timing with CUDA events on the model's stream.  Classes,
+ * in order: 0 GEMM, 1 attention forward, 2 attention backward, 3 cross-
+ * entropy, 4 AdamW, 5 LayerNorm, 6 other elementwise, 7 embedding, 8 TF32
+ * split, 9 allreduce wait.  read fills count >= 40 doubles: per class
+ * {launch groups, milliseconds, algorithmic FLOP, algorithmic bytes}
+ * accumulated since profiling was enabled; collect folds the events of
+ * device-side steps into those totals (host steps do it themselves). */
+int32_t et_b200_lm_profile_v1(et_b200_lm *lm, int32_t enable);
+int32_t et_b200_lm_profile_collect_v1(et_b200_lm *lm);
+int32_t et_b200_lm_profile_read_v1(et_b200_lm *lm, double *out, size_t count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,1036 @@
+/*
+ * CPU oracle for the f32 training-step hot path -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A restatement of eshkol-transformer's serial CPU arithmetic, keeping each
+ * reference summation order and rounding point (see oracle.h).  Loops are
+ * re-nested for cache locality and parallelised with OpenMP only across
+ * independent output elements, so every output keeps the reference's
+ * per-element operation sequence and is bit-identical to it.
+ *
+ * Build: gcc -std=c11 -O2 -ffp-contract=off -fno-fast-math -fopenmp
+ *        -shared -fPIC oracle.c -o liboracle.so -lm
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#pragma STDC FP_CONTRACT OFF
+
+/* ------------------------------------------------------------------ RNG */
+
+uint64_t orc_splitmix64(uint64_t x) {
+  x += UINT64_C(0x9e3779b97f4a7c15);
+  x = (x ^ (x >> 30)) * UINT64_C(0xbf58476d1ce4e5b9);
+  x = (x ^ (x >> 27)) * UINT64_C(0x94d049bb133111eb);
+  return x ^ (x >> 31);
+}
+
+static uint64_t stream_key(uint64_t seed, uint64_t stream) {
+  return orc_splitmix64(seed) ^
+         orc_splitmix64(stream * UINT64_C(0x632be59bd9b4e019) + 1u);
+}
+
+static uint64_t stream_word(uint64_t key, uint64_t counter) {
+  return orc_splitmix64(key + counter * UINT64_C(0x9e3779b97f4a7c15));
+}
+
+void orc_fill_normal(uint64_t seed, uint64_t stream, size_t count, double mean,
+                     double stddev, float *out) {
+  const uint64_t key = stream_key(seed, stream);
+  const double two_pi = 6.283185307179586476925286766559;
+  for (size_t i = 0; i < count; i++) {
+    const uint64_t a = stream_word(key, 2u * (uint64_t)i);
+    const uint64_t b = stream_word(key, 2u * (uint64_t)i + 1u);
+    const double u1 = (double)((a >> 11) + 1u) * 0x1p-53; /* (0, 1] */
+    const double u2 = (double)(b >> 11) * 0x1p-53;        /* [0, 1) */
+    const double z = sqrt(-2.0 * log(u1)) * cos(two_pi * u2);
+    out[i] = (float)(mean + stddev * z);
+  }
+}
+
+void orc_fill_tokens(uint64_t seed, uint64_t stream, size_t count,
+                     uint64_t vocabulary, int64_t *out) {
+  const uint64_t key = stream_key(seed, stream);
+  const uint64_t limit = (UINT64_MAX / vocabulary) * vocabulary;
+  for (size_t i = 0; i < count; i++) {
+    uint64_t attempt = 0;
+    for (;;) {
+      const uint64_t x =
+          stream_word(key, (uint64_t)i | (attempt << 40));
+      if (x < limit) {
+        out[i] = (int64_t)(x % vocabulary);
+        break;
+      }
+      attempt++;
+    }
+  }
+}
+
+/* ------------------------------------------------------------ attention */
+
+typedef struct att_shape {
+  size_t n, hq, hkv, tq, tk, dh;
+} att_shape;
+
+static att_shape att_from(const int64_t s[6]) {
+  att_shape r = {(size_t)s[0], (size_t)s[1], (size_t)s[2],
+                 (size_t)s[3], (size_t)s[4], (size_t)s[5]};
+  return r;
+}
+
+/* 1/sqrtf(Dh), rounded in two steps (a2_attention_provider.c:221-224). */
+static float att_scale(size_t dh) {
+  const float root = sqrtf((float)dh);
+  return 1.0f / root;
+}
+
+/* Scores of one query row against every admitted key, the row maximum and
+ * the exp-sum denominator (a2_attention_provider.c:249-318).  Returns the
+ * number of admitted keys; admitted[tk] marks them. */
+static size_t att_row(const att_shape *s, const float *q, const float *k,
+                      const int64_t *qpos, const int64_t *kpos,
+                      const uint8_t *mask, float scale, size_t n, size_t hq,
+                      size_t tq, float *scores, uint8_t *admitted,
+                      float *maximum, float *denominator) {
+  const size_t hkv = hq / (s->hq / s->hkv);
+  const float *qrow = q + (((n * s->hq + hq) * s->tq + tq) * s->dh);
+  size_t count = 0;
+  float row_max = 0.0f;
+  for (size_t tk = 0; tk < s->tk; tk++) {
+    const int ok = mask[(n * s->tq + tq) * s->tk + tk] != 0u &&
+                   kpos[n * s->tk + tk] <= qpos[n * s->tq + tq];
+    admitted[tk] = (uint8_t)ok;
+    if (!ok) continue;
+    const float *krow = k + (((n * s->hkv + hkv) * s->tk + tk) * s->dh);
+    float sum = 0.0f;
+    for (size_t d = 0; d < s->dh; d++) {
+      const float product = qrow[d] * krow[d];
+      sum = sum + product;
+    }
+    sum = sum * scale;
+    scores[tk] = sum;
+    if (count == 0 || sum > row_max) row_max = sum;
+    count++;
+  }
+  if (count == 0) {
+    *maximum = 0.0f;
+    *denominator = 1.0f;
+    return 0;
+  }
+  float total = 0.0f;
+  for (size_t tk = 0; tk < s->tk; tk++) {
+    if (!admitted[tk]) continue;
+    total = total + expf(scores[tk] - row_max);
+  }
+  *maximum = row_max;
+  *denominator = total;
+  return count;
+}
+
+void orc_attention_forward(const int64_t shape[6], const float *q,
+                           const float *k, const float *v,
+                           const int64_t *qpos, const int64_t *kpos,
+                           const uint8_t *mask, float *output) {
+  const att_shape s = att_from(shape);
+  const float scale = att_scale(s.dh);
+  memset(output, 0, s.n * s.hq * s.tq * s.dh * sizeof(float));
+#pragma omp parallel
+  {
+    float *scores = (float *)malloc(s.tk * sizeof(float));
+    uint8_t *adm = (uint8_t *)malloc(s.tk);
+#pragma omp for collapse(2) schedule(dynamic)
+    for (size_t n = 0; n < s.n; n++) {
+      for (size_t hq = 0; hq < s.hq; hq++) {
+        const size_t hkv = hq / (s.hq / s.hkv);
+        for (size_t tq = 0; tq < s.tq; tq++) {
+          float maximum, denominator;
+          if (att_row(&s, q, k, qpos, kpos, mask, scale, n, hq, tq, scores,
+                      adm, &maximum, &denominator) == 0)
+            continue;
+          float *orow = output + (((n * s.hq + hq) * s.tq + tq) * s.dh);
+          for (size_t tk = 0; tk < s.tk; tk++) {
+            if (!adm[tk]) continue;
+            const float p = expf(scores[tk] - maximum) / denominator;
+            const float *vrow = v + (((n * s.hkv + hkv) * s.tk + tk) * s.dh);
+            for (size_t d = 0; d < s.dh; d++) orow[d] = orow[d] + p * vrow[d];
+          }
+        }
+      }
+    }
+    free(scores);
+    free(adm);
+  }
+}
+
+/* Backward in the reference's loop order n, hq, tq, tk
+ * (a2_attention_provider.c:718-790): dK/dV of one KV head accumulate over its
+ * query-head group and query rows in that order, so work is split across
+ * (n, hkv) only. */
+void orc_attention_backward(const int64_t shape[6], const float *q,
+                            const float *k, const float *v,
+                            const int64_t *qpos, const int64_t *kpos,
+                            const uint8_t *mask, const float *upstream,
+                            float *dq, float *dk, float *dv) {
+  const att_shape s = att_from(shape);
+  const float scale = att_scale(s.dh);
+  const size_t group = s.hq / s.hkv;
+  memset(dq, 0, s.n * s.hq * s.tq * s.dh * sizeof(float));
+  memset(dk, 0, s.n * s.hkv * s.tk * s.dh * sizeof(float));
+  memset(dv, 0, s.n * s.hkv * s.tk * s.dh * sizeof(float));
+#pragma omp parallel
+  {
+    float *scores = (float *)malloc(s.tk * sizeof(float));
+    float *dps = (float *)malloc(s.tk * sizeof(float));
+    uint8_t *adm = (uint8_t *)malloc(s.tk);
+#pragma omp for collapse(2) schedule(dynamic)
+    for (size_t n = 0; n < s.n; n++) {
+      for (size_t hkv = 0; hkv < s.hkv; hkv++) {
+        for (size_t hq = hkv * group; hq < (hkv + 1) * group; hq++) {
+          for (size_t tq = 0; tq < s.tq; tq++) {
+            float maximum, denominator;
+            if (att_row(&s, q, k, qpos, kpos, mask, scale, n, hq, tq, scores,
+                        adm, &maximum, &denominator) == 0)
+              continue;
+            const size_t qo = ((n * s.hq + hq) * s.tq + tq) * s.dh;
+            const float *urow = upstream + qo;
+            const float *qrow = q + qo;
+            float *dqrow = dq + qo;
+            float mean = 0.0f;
+            for (size_t tk = 0; tk < s.tk; tk++) {
+              if (!adm[tk]) continue;
+              const float p = expf(scores[tk] - maximum) / denominator;
+              const float *vrow = v + (((n * s.hkv + hkv) * s.tk + tk) * s.dh);
+              float dp = 0.0f;
+              for (size_t d = 0; d < s.dh; d++) {
+                const float product = urow[d] * vrow[d];
+                dp = dp + product;
+              }
+              dps[tk] = dp;
+              mean = mean + p * dp;
+            }
+            for (size_t tk = 0; tk < s.tk; tk++) {
+              if (!adm[tk]) continue;
+              const float p = expf(scores[tk] - maximum) / denominator;
+              const size_t ko = ((n * s.hkv + hkv) * s.tk + tk) * s.dh;
+              const float ds = p * (dps[tk] - mean);
+              const float dss = ds * scale;
+              for (size_t d = 0; d < s.dh; d++) {
+                dqrow[d] = dqrow[d] + dss * k[ko + d];
+                dk[ko + d] = dk[ko + d] + dss * qrow[d];
+                dv[ko + d] = dv[ko + d] + p * urow[d];
+              }
+            }
+          }
+        }
+      }
+    }
+    free(scores);
+    free(dps);
+    free(adm);
+  }
+}
+
+/* RoPE pair rotation (a2_attention_provider.c:792-804, 908-935):
+ * forward (a - b, c + d), backward (a + b, -c + d) with a = x0 cos,
+ * b = x1 sin, c = x0 sin, d = x1 cos and cos/sin of (float)pos * inv_freq. */
+void orc_rope(const int64_t shape[4], const float *x, const int64_t *positions,
+              const float *inv_freq, int backward, float *y) {
+  const size_t N = (size_t)shape[0], H = (size_t)shape[1],
+               T = (size_t)shape[2], D = (size_t)shape[3];
+#pragma omp parallel for collapse(2)
+  for (size_t n = 0; n < N; n++) {
+    for (size_t h = 0; h < H; h++) {
+      for (size_t t = 0; t < T; t++) {
+        const int64_t position = positions[n * T + t];
+        for (size_t pair = 0; pair < D / 2; pair++) {
+          const size_t base = ((n * H + h) * T + t) * D + pair * 2;
+          const float angle = (float)position * inv_freq[pair];
+          const float cosine = cosf(angle);
+          const float sine = sinf(angle);
+          const float a = x[base] * cosine;
+          const float b = x[base + 1] * sine;
+          const float c = x[base] * sine;
+          const float d = x[base + 1] * cosine;
+          y[base] = backward ? a + b : a - b;
+          y[base + 1] = backward ? -c + d : c + d;
+        }
+      }
+    }
+  }
+}
+
+/* ------------------------------------------------------------ linear */
+
+/* y[r,o] = ((0 + x[r,0] W[o,0]) + ...) + b[o]  (n2_primitives_provider.c:347-370) */
+void orc_linear_forward(size_t rows, size_t din, size_t dout, const float *x,
+                        const float *w, const float *bias, float *y) {
+#pragma omp parallel for schedule(static)
+  for (size_t r = 0; r < rows; r++) {
+    for (size_t o = 0; o < dout; o++) {
+      float sum = 0.0f;
+      for (size_t i = 0; i < din; i++) {
+        const float product = x[r * din + i] * w[o * din + i];
+        sum = sum + product;
+      }
+      if (bias != NULL) sum = sum + bias[o];
+      y[r * dout + o] = sum;
+    }
+  }
+}
+
+/* dX[r,i] = sum over o ascending of dY[r,o] W[o,i]; dW[o,i] and dB[o] sum
+ * over rows ascending (n2_primitives_provider.c:372-419).  dW is computed one
+ * output row o at a time so the row loop stays innermost-but-one while each
+ * element still accumulates rows in ascending order. */
+void orc_linear_backward(size_t rows, size_t din, size_t dout, const float *x,
+                         const float *w, const float *dy, float *dx, float *dw,
+                         float *dbias) {
+  if (dx != NULL) {
+#pragma omp parallel
+    {
+      float *acc = (float *)malloc(din * sizeof(float));
+#pragma omp for schedule(static)
+      for (size_t r = 0; r < rows; r++) {
+        for (size_t i = 0; i < din; i++) acc[i] = 0.0f;
+        for (size_t o = 0; o < dout; o++) {
+          const float g = dy[r * dout + o];
+          const float *wrow = w + o * din;
+          for (size_t i = 0; i < din; i++) {
+            const float product = g * wrow[i];
+            acc[i] = acc[i] + product;
+          }
+        }
+        memcpy(dx + r * din, acc, din * sizeof(float));
+      }
+      free(acc);
+    }
+  }
+  if (dw != NULL) {
+#pragma omp parallel
+    {
+      float *acc = (float *)malloc(din * sizeof(float));
+#pragma omp for schedule(static)
+      for (size_t o = 0; o < dout; o++) {
+        for (size_t i = 0; i < din; i++) acc[i] = 0.0f;
+        for (size_t r = 0; r < rows; r++) {
+          const float g = dy[r * dout + o];
+          const float *xrow = x + r * din;
+          for (size_t i = 0; i < din; i++) {
+            const float product = g * xrow[i];
+            acc[i] = acc[i] + product;
+          }
+        }
+        memcpy(dw + o * din, acc, din * sizeof(float));
+      }
+      free(acc);
+    }
+  }
+  if (dbias != NULL) {
+    for (size_t o = 0; o < dout; o++) {
+      float sum = 0.0f;
+      for (size_t r = 0; r < rows; r++) sum = sum + dy[r * dout + o];
+      dbias[o] = sum;
+    }
+  }
+}
+
+/* ------------------------------------------------------------ LayerNorm */
+
+/* Two-pass mean / biased variance, rstd = 1 / sqrtf(var + eps)
+ * (n2_primitives_provider.c:421-454). */
+static void ln_stats(const float *row, size_t d, float epsilon, float *mean,
+                     float *rstd) {
+  const float dimension = (float)d;
+  float sum = 0.0f;
+  for (size_t j = 0; j < d; j++) sum = sum + row[j];
+  const float m = sum / dimension;
+  float var_sum = 0.0f;
+  for (size_t j = 0; j < d; j++) {
+    const float delta = row[j] - m;
+    const float square = delta * delta;
+    var_sum = var_sum + square;
+  }
+  const float variance = var_sum / dimension;
+  const float adjusted = variance + epsilon;
+  const float root = sqrtf(adjusted);
+  *mean = m;
+  *rstd = 1.0f / root;
+}
+
+void orc_layer_norm_forward(size_t rows, size_t d, const float *x,
+                            const float *gamma, const float *beta,
+                            float epsilon, float *y) {
+#pragma omp parallel for schedule(static)
+  for (size_t r = 0; r < rows; r++) {
+    float mean, rstd;
+    const float *row = x + r * d;
+    ln_stats(row, d, epsilon, &mean, &rstd);
+    for (size_t j = 0; j < d; j++) {
+      const float delta = row[j] - mean;
+      const float normalized = delta * rstd;
+      const float scaled = normalized * gamma[j];
+      y[r * d + j] = scaled + beta[j];
+    }
+  }
+}
+
+/* (n2_primitives_provider.c:456-543) */
+void orc_layer_norm_backward(size_t rows, size_t d, const float *x,
+                             const float *gamma, float epsilon,
+                             const float *dy, float *dx, float *dgamma,
+                             float *dbeta) {
+  const float dimension = (float)d;
+  const float reciprocal_dimension = 1.0f / dimension;
+  float *means = (float *)malloc(rows * sizeof(float));
+  float *rstds = (float *)malloc(rows * sizeof(float));
+#pragma omp parallel for schedule(static)
+  for (size_t r = 0; r < rows; r++) {
+    float mean, rstd;
+    const float *row = x + r * d;
+    const float *up = dy + r * d;
+    ln_stats(row, d, epsilon, &mean, &rstd);
+    means[r] = mean;
+    rstds[r] = rstd;
+    float sum_h = 0.0f, sum_hn = 0.0f;
+    for (size_t j = 0; j < d; j++) {
+      const float delta = row[j] - mean;
+      const float normalized = delta * rstd;
+      const float h = up[j] * gamma[j];
+      const float product = h * normalized;
+      sum_h = sum_h + h;
+      sum_hn = sum_hn + product;
+    }
+    const float factor = rstd * reciprocal_dimension;
+    if (dx != NULL) {
+      for (size_t j = 0; j < d; j++) {
+        const float delta = row[j] - mean;
+        const float normalized = delta * rstd;
+        const float h = up[j] * gamma[j];
+        const float first = dimension * h;
+        const float second = first - sum_h;
+        const float third = normalized * sum_hn;
+        const float fourth = second - third;
+        dx[r * d + j] = factor * fourth;
+      }
+    }
+  }
+  if (dgamma != NULL || dbeta != NULL) {
+#pragma omp parallel for schedule(static)
+    for (size_t j = 0; j < d; j++) {
+      float sg = 0.0f, sb = 0.0f;
+      for (size_t r = 0; r < rows; r++) {
+        const float delta = x[r * d + j] - means[r];
+        const float normalized = delta * rstds[r];
+        const float product = dy[r * d + j] * normalized;
+        sg = sg + product;
+        sb = sb + dy[r * d + j];
+      }
+      if (dgamma != NULL) dgamma[j] = sg;
+      if (dbeta != NULL) dbeta[j] = sb;
+    }
+  }
+  free(means);
+  free(rstds);
+}
+
+/* ------------------------------------------------------------ GELU */
+
+/* Exact-erf GELU and its derivative with the reference's binary32 constants
+ * (n2_primitives_provider.c:545-583). */
+void orc_gelu_forward(size_t count, const float *x, float *y) {
+  const float half = 0x1p-1f, one = 0x1p+0f, inv_sqrt_2 = 0x1.6a09e6p-1f;
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < count; i++) {
+    const float scaled = x[i] * inv_sqrt_2;
+    const float erf_value = erff(scaled);
+    const float sum = one + erf_value;
+    const float half_x = half * x[i];
+    y[i] = half_x * sum;
+  }
+}
+
+void orc_gelu_backward(size_t count, const float *x, const float *dy,
+                       float *dx) {
+  const float half = 0x1p-1f, one = 0x1p+0f, inv_sqrt_2 = 0x1.6a09e6p-1f,
+              inv_sqrt_2pi = 0x1.988454p-2f;
+#pragma omp parallel for schedule(static)
+  for (size_t i = 0; i < count; i++) {
+    const float scaled = x[i] * inv_sqrt_2;
+    const float erf_value = erff(scaled);
+    const float sum = one + erf_value;
+    const float cdf = half * sum;
+    const float square = x[i] * x[i];
+    const float exponent = -(half * square);
+    const float density = expf(exponent) * inv_sqrt_2pi;
+    const float xd = x[i] * density;
+    const float slope = cdf + xd;
+    dx[i] = dy[i] * slope;
+  }
+}
+
+/* ------------------------------------------------------------ embedding */
+
+void orc_embedding_forward(size_t rows, size_t vocabulary, size_t d,
+                           const int64_t *ids, const float *w, float *y) {
+  (void)vocabulary;
+  for (size_t r = 0; r < rows; r++)
+    memcpy(y + r * d, w + (size_t)ids[r] * d, d * sizeof(float));
+}
+
+/* dW[v,:] = sum over token rows with id v in ascending (n,t) order, starting
+ * from +0 (n2_primitives_provider.c:328-345). */
+void orc_embedding_backward(size_t rows, size_t vocabulary, size_t d,
+                            const int64_t *ids, const float *dy, float *dw) {
+  memset(dw, 0, vocabulary * d * sizeof(float));
+  for (size_t r = 0; r < rows; r++) {
+    float *dst = dw + (size_t)ids[r] * d;
+    for (size_t j = 0; j < d; j++) dst[j] = dst[j] + dy[r * d + j];
+  }
+}
+
+/* ------------------------------------------------------------ L2 CE */
+
+static float ce_row_max(const float *row, size_t V) {
+  float m = row[0];
+  for (size_t j = 1; j < V; j++)
+    if (row[j] > m) m = row[j];
+  return m;
+}
+
+static float ce_row_sum(const float *row, size_t V, float m) {
+  float s = 0.0f;
+  for (size_t j = 0; j < V; j++) s += expf(row[j] - m);
+  return s;
+}
+
+void orc_ce_forward(size_t rows, size_t V, const float *logits,
+                    const int64_t *targets, float *loss) {
+#pragma omp parallel for schedule(static)
+  for (size_t r = 0; r < rows; r++) {
+    const float *row = logits + r * V;
+    const float m = ce_row_max(row, V);
+    const float s = ce_row_sum(row, V, m);
+    loss[r] = logf(s) + (m - row[(size_t)targets[r]]);
+  }
+}
+
+void orc_ce_backward(size_t rows, size_t V, const float *logits,
+                     const int64_t *targets, const float *upstream,
+                     float *grad) {
+#pragma omp parallel for schedule(static)
+  for (size_t r = 0; r < rows; r++) {
+    const float *row = logits + r * V;
+    const float m = ce_row_max(row, V);
+    const float s = ce_row_sum(row, V, m);
+    const float u = upstream[r];
+    const size_t target = (size_t)targets[r];
+    for (size_t j = 0; j < V; j++) {
+      const float p = expf(row[j] - m) / s;
+      grad[r * V + j] = u * (p - (j == target ? 1.0f : 0.0f));
+    }
+  }
+}
+
+float orc_mean_loss(size_t rows, const float *loss) {
+  float w = 0.0f, n = 0.0f;
+  for (size_t r = 0; r < rows; r++) {
+    w = w + 1.0f;
+    const float p = 1.0f * loss[r];
+    n = n + p;
+  }
+  return n / w;
+}
+
+/* ------------------------------------------------------------ O2 AdamW */
+
+static float fbits(uint32_t b) {
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+static uint32_t bitsf(float f) {
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  return b;
+}
+
+/* Square-and-multiply power with one rounding per product
+ * (o2_optimizer.c:419-435). */
+uint32_t orc_pow_bits(uint32_t base_bits, uint64_t exponent) {
+  float result = 1.0f, base = fbits(base_bits);
+  while (exponent != 0u) {
+    if (exponent & 1u) result = result * base;
+    exponent >>= 1u;
+    if (exponent != 0u) base = base * base;
+  }
+  return bitsf(result);
+}
+
+/* Per element (o2_optimizer.c:1738-1756):
+ *   g  = (grad / W) * clip
+ *   m' = b1 m + (1 - b1) g ;  v' = b2 v + (1 - b2) g^2
+ *   p' = p (1 - lr wd) - (lr m'/(1-b1^t)) / (sqrt(v'/(1-b2^t)) + eps) */
+int orc_adamw_step(size_t count, float *parameter, const float *gradient,
+                   float *exp_avg, float *exp_avg_sq,
+                   const orc_adamw_options *o, uint64_t update,
+                   uint32_t weight_bits, uint32_t schedule_factor_bits,
+                   uint32_t clip_factor_bits) {
+  const float b1 = fbits(o->beta1_bits), b2 = fbits(o->beta2_bits);
+  const float eps = fbits(o->epsilon_bits), wd = fbits(o->weight_decay_bits);
+  const float bias1 = 1.0f - fbits(orc_pow_bits(o->beta1_bits, update));
+  const float bias2 = 1.0f - fbits(orc_pow_bits(o->beta2_bits, update));
+  const float lr = fbits(o->learning_rate_bits) * fbits(schedule_factor_bits);
+  const float weight = fbits(weight_bits), clip = fbits(clip_factor_bits);
+  const float one_b1 = 1.0f - b1, one_b2 = 1.0f - b2;
+  const float decay = 1.0f - lr * wd;
+  float *np = (float *)malloc(count * sizeof(float));
+  float *nm = (float *)malloc(count * sizeof(float));
+  float *nv = (float *)malloc(count * sizeof(float));
+  int bad = 0;
+  for (size_t i = 0; i < count; i++) {
+    const float g = (gradient[i] / weight) * clip;
+    const float m = b1 * exp_avg[i] + one_b1 * g;
+    const float gg = g * g;
+    const float v = b2 * exp_avg_sq[i] + one_b2 * gg;
+    const float mh = m / bias1;
+    const float vh = v / bias2;
+    const float den = sqrtf(vh) + eps;
+    const float p = parameter[i] * decay - (lr * mh) / den;
+    if (!isfinite(g) || !isfinite(m) || !isfinite(v) || !isfinite(p)) bad = 1;
+    np[i] = p;
+    nm[i] = m;
+    nv[i] = v;
+  }
+  if (!bad) {
+    memcpy(parameter, np, count * sizeof(float));
+    memcpy(exp_avg, nm, count * sizeof(float));
+    memcpy(exp_avg_sq, nv, count * sizeof(float));
+  }
+  free(np);
+  free(nm);
+  free(nv);
+  return bad;
+}
+
+/* Running scaled sum of squares (o2_optimizer.c:1548-1618): scale is the
+ * largest |g/W| so far, sumsq the sum of (|g/W| / scale)^2. */
+uint32_t orc_global_norm(size_t tensor_count, const float *const *gradients,
+                         const size_t *counts, uint32_t weight_bits) {
+  const float weight = fbits(weight_bits);
+  float scale = 0.0f, sumsq = 1.0f;
+  for (size_t t = 0; t < tensor_count; t++) {
+    for (size_t i = 0; i < counts[t]; i++) {
+      const float a = fabsf(gradients[t][i] / weight);
+      if (a == 0.0f) continue;
+      if (scale == 0.0f || scale < a) {
+        const float ratio = scale == 0.0f ? 0.0f : scale / a;
+        sumsq = 1.0f + sumsq * (ratio * ratio);
+        scale = a;
+      } else {
+        const float ratio = a / scale;
+        sumsq = sumsq + ratio * ratio;
+      }
+    }
+  }
+  if (scale == 0.0f) return 0u;
+  return bitsf(scale * sqrtf(sumsq));
+}
+
+/* Exact rational -> binary32 (round half to even) over little-endian 32-bit
+ * limbs; used for the linear schedule factor
+ * ((D - e) 2^p + e r) / (D 2^p) of o2_optimizer.c:589-611. */
+#define BIG_LIMBS 10
+typedef struct big {
+  uint32_t w[BIG_LIMBS];
+} big;
+
+static void big_set64(big *a, uint64_t v) {
+  memset(a, 0, sizeof(*a));
+  a->w[0] = (uint32_t)v;
+  a->w[1] = (uint32_t)(v >> 32);
+}
+static int big_cmp(const big *a, const big *b) {
+  for (int i = BIG_LIMBS - 1; i >= 0; i--)
+    if (a->w[i] != b->w[i]) return a->w[i] < b->w[i] ? -1 : 1;
+  return 0;
+}
+static void big_shl(big *a, unsigned s) {
+  big r;
+  memset(&r, 0, sizeof(r));
+  const unsigned limb = s / 32, bit = s % 32;
+  for (int i = BIG_LIMBS - 1; i >= (int)limb; i--) {
+    uint64_t v = (uint64_t)a->w[i - limb] << bit;
+    r.w[i] |= (uint32_t)v;
+    if (i + 1 < BIG_LIMBS) r.w[i + 1] |= (uint32_t)(v >> 32);
+  }
+  *a = r;
+}
+static void big_add(big *a, const big *b) {
+  uint64_t c = 0;
+  for (int i = 0; i < BIG_LIMBS; i++) {
+    c += (uint64_t)a->w[i] + b->w[i];
+    a->w[i] = (uint32_t)c;
+    c >>= 32;
+  }
+}
+static void big_sub(big *a, const big *b) {
+  int64_t c = 0;
+  for (int i = 0; i < BIG_LIMBS; i++) {
+    int64_t v = (int64_t)a->w[i] - b->w[i] + c;
+    a->w[i] = (uint32_t)v;
+    c = v < 0 ? -1 : 0;
+  }
+}
+static void big_mul_small(big *a, uint32_t m) {
+  uint64_t c = 0;
+  for (int i = 0; i < BIG_LIMBS; i++) {
+    c += (uint64_t)a->w[i] * m;
+    a->w[i] = (uint32_t)c;
+    c >>= 32;
+  }
+}
+static int big_zero(const big *a) {
+  for (int i = 0; i < BIG_LIMBS; i++)
+    if (a->w[i]) return 0;
+  return 1;
+}
+
+/* num/den with 0 <= num/den <= 1: find e with 2^(e) <= num/den < 2^(e+1),
+ * then extract 24 significant bits (or fewer below the normal range) by
+ * restoring division, and round half to even on the remainder. */
+static uint32_t big_round_f32(big num, big den) {
+  if (big_zero(&num)) return 0u;
+  int e = 0; /* exponent: value in [2^e, 2^(e+1)) */
+  big t = num;
+  while (big_cmp(&t, &den) < 0) {
+    big_shl(&t, 1);
+    e--;
+  }
+  /* significand bits: normal numbers keep 24, subnormals fewer */
+  int keep = 24;
+  if (e < -126) keep = 24 - (-126 - e);
+  if (keep <= 0) keep = 0;
+  /* q = floor(num * 2^(keep - 1 - e) / den) */
+  big scaled = num;
+  big_shl(&scaled, (unsigned)(keep - 1 - e));
+  uint32_t q = 0;
+  big rem;
+  memset(&rem, 0, sizeof(rem));
+  for (int bit = BIG_LIMBS * 32 - 1; bit >= 0; bit--) {
+    big_shl(&rem, 1);
+    rem.w[0] |= (scaled.w[bit / 32] >> (bit % 32)) & 1u;
+    q <<= 1;
+    if (big_cmp(&rem, &den) >= 0) {
+      big_sub(&rem, &den);
+      q |= 1u;
+    }
+  }
+  big twice = rem;
+  big_shl(&twice, 1);
+  const int c = big_cmp(&twice, &den);
+  if (c > 0 || (c == 0 && (q & 1u))) q++;
+  if (e < -126) return q; /* subnormal encoding (q may carry into normal) */
+  if (q == (1u << 24)) {
+    q >>= 1;
+    e++;
+  }
+  return ((uint32_t)(e + 127) << 23) | (q - (1u << 23));
+}
+
+uint32_t orc_schedule_factor(uint32_t kind, uint64_t warmup, uint64_t total,
+                             uint32_t minimum_ratio_bits, uint64_t update) {
+  if (kind == 0u) return 0x3f800000u;
+  if (update > total) return minimum_ratio_bits;
+  big num, den;
+  if (warmup > 0u && update <= warmup) {
+    big_set64(&num, update);
+    big_set64(&den, warmup);
+    return big_round_f32(num, den);
+  }
+  const uint64_t elapsed = update - warmup, duration = total - warmup;
+  const uint32_t exponent = (minimum_ratio_bits >> 23) & 0xffu;
+  const uint32_t fraction = minimum_ratio_bits & 0x7fffffu;
+  const unsigned p = exponent == 0u ? 149u : 150u - exponent;
+  const uint32_t r = exponent == 0u ? fraction : (0x800000u | fraction);
+  big term;
+  big_set64(&term, elapsed);
+  big_mul_small(&term, r);
+  big_set64(&num, duration - elapsed);
+  big_shl(&num, p);
+  big_add(&num, &term);
+  big_set64(&den, duration);
+  big_shl(&den, p);
+  return big_round_f32(num, den);
+}
+
+/* ------------------------------------------------------------ LM model */
+
+/* Parameter tensors in order: token embedding [V,d]; per layer: ln1 gamma,
+ * ln1 beta, Wqkv [3d,d], bqkv, Wo [d,d], bo, ln2 gamma, ln2 beta, W1 [F,d],
+ * b1, W2 [d,F], b2; then final LN gamma, beta.  The head is tied to the
+ * token embedding (logits = LN_f(x) E^T). */
+enum { LM_PER_LAYER = 12 };
+
+size_t orc_lm_tensor_count(const orc_lm_config *c) {
+  return 1u + (size_t)c->layers * LM_PER_LAYER + 2u;
+}
+
+size_t orc_lm_tensor_sizes(const orc_lm_config *c, size_t *sizes) {
+  const size_t d = (size_t)c->d_model, F = (size_t)c->ffn,
+               V = (size_t)c->vocabulary;
+  size_t k = 0, total = 0;
+  sizes[k++] = V * d;
+  for (int64_t l = 0; l < c->layers; l++) {
+    sizes[k++] = d;
+    sizes[k++] = d;
+    sizes[k++] = 3 * d * d;
+    sizes[k++] = 3 * d;
+    sizes[k++] = d * d;
+    sizes[k++] = d;
+    sizes[k++] = d;
+    sizes[k++] = d;
+    sizes[k++] = F * d;
+    sizes[k++] = F;
+    sizes[k++] = d * F;
+    sizes[k++] = d;
+  }
+  sizes[k++] = d;
+  sizes[k++] = d;
+  for (size_t i = 0; i < k; i++) total += sizes[i];
+  return total;
+}
+
+/* Weights N(0, 0.02) with stream = tensor index; LN gammas 1; biases and
+ * betas 0. */
+void orc_lm_init(const orc_lm_config *c, uint64_t seed, float *params) {
+  const size_t count = orc_lm_tensor_count(c);
+  size_t *sizes = (size_t *)malloc(count * sizeof(size_t));
+  orc_lm_tensor_sizes(c, sizes);
+  size_t off = 0;
+  for (size_t t = 0; t < count; t++) {
+    int kind; /* 0 weight, 1 gamma, 2 zero */
+    if (t == 0) kind = 0;
+    else if (t >= count - 2) kind = t == count - 2 ? 1 : 2;
+    else {
+      const size_t j = (t - 1) % LM_PER_LAYER;
+      kind = (j == 0 || j == 6) ? 1
+             : (j == 2 || j == 4 || j == 8 || j == 10) ? 0 : 2;
+    }
+    if (kind == 0) orc_fill_normal(seed, t, sizes[t], 0.0, 0.02, params + off);
+    else
+      for (size_t i = 0; i < sizes[t]; i++)
+        params[off + i] = kind == 1 ? 1.0f : 0.0f;
+    off += sizes[t];
+  }
+  free(sizes);
+}
+
+void orc_rope_inv_freq(int64_t head_dim, double base, float *inv_freq) {
+  for (int64_t i = 0; i < head_dim / 2; i++)
+    inv_freq[i] = (float)(1.0 / pow(base, (double)(2 * i) / (double)head_dim));
+}
+
+/* [rows, 3d] qkv columns (which*d + h*Dh + j) <-> [B,H,T,Dh] head layout. */
+static void split_heads(const float *qkv, size_t B, size_t T, size_t H,
+                        size_t Dh, size_t which, float *out) {
+  const size_t d = H * Dh;
+  for (size_t b = 0; b < B; b++)
+    for (size_t h = 0; h < H; h++)
+      for (size_t t = 0; t < T; t++)
+        memcpy(out + ((b * H + h) * T + t) * Dh,
+               qkv + (b * T + t) * 3 * d + which * d + h * Dh,
+               Dh * sizeof(float));
+}
+static void merge_heads(const float *in, size_t B, size_t T, size_t H,
+                        size_t Dh, size_t width, size_t offset, float *out) {
+  for (size_t b = 0; b < B; b++)
+    for (size_t h = 0; h < H; h++)
+      for (size_t t = 0; t < T; t++)
+        memcpy(out + (b * T + t) * width + offset + h * Dh,
+               in + ((b * H + h) * T + t) * Dh, Dh * sizeof(float));
+}
+
+static void add_into(size_t count, float *dst, const float *src) {
+  for (size_t i = 0; i < count; i++) dst[i] = dst[i] + src[i];
+}
+
+float orc_lm_forward_backward(const orc_lm_config *c, const float *params,
+                              const int64_t *ids, const int64_t *targets,
+                              double token_scale, float *grads) {
+  const size_t L = (size_t)c->layers, d = (size_t)c->d_model,
+               H = (size_t)c->heads, F = (size_t)c->ffn,
+               V = (size_t)c->vocabulary, T = (size_t)c->seq_len,
+               B = (size_t)c->batch, Dh = d / H, R = B * T;
+  const size_t count = orc_lm_tensor_count(c);
+  size_t *sizes = (size_t *)malloc(count * sizeof(size_t));
+  size_t *offs = (size_t *)malloc(count * sizeof(size_t));
+  orc_lm_tensor_sizes(c, sizes);
+  size_t off = 0;
+  for (size_t t = 0; t < count; t++) {
+    offs[t] = off;
+    off += sizes[t];
+  }
+#define P(t) (params + offs[t])
+#define G(t) (grads + offs[t])
+#define LT(l, j) (1 + (l) * LM_PER_LAYER + (j))
+  const float eps = c->ln_epsilon;
+  const int64_t att_shape[6] = {(int64_t)B, (int64_t)H, (int64_t)H,
+                                (int64_t)T, (int64_t)T, (int64_t)Dh};
+  const int64_t rope_shape[4] = {(int64_t)B, (int64_t)H, (int64_t)T,
+                                 (int64_t)Dh};
+  float *inv_freq = (float *)malloc(Dh / 2 * sizeof(float));
+  orc_rope_inv_freq((int64_t)Dh, c->rope_base, inv_freq);
+  int64_t *pos = (int64_t *)malloc(B * T * sizeof(int64_t));
+  uint8_t *keep = (uint8_t *)malloc(B * T * T);
+  for (size_t b = 0; b < B; b++)
+    for (size_t t = 0; t < T; t++) pos[b * T + t] = (int64_t)t;
+  memset(keep, 1, B * T * T);
+
+  /* saved activations per layer */
+  float **xin = (float **)calloc(L + 1, sizeof(float *));
+  float **h1 = (float **)calloc(L, sizeof(float *));
+  float **qh = (float **)calloc(L, sizeof(float *)); /* post-RoPE, heads */
+  float **kh = (float **)calloc(L, sizeof(float *));
+  float **vh = (float **)calloc(L, sizeof(float *));
+  float **om = (float **)calloc(L, sizeof(float *)); /* merged attn out */
+  float **xmid = (float **)calloc(L, sizeof(float *));
+  float **h2 = (float **)calloc(L, sizeof(float *));
+  float **u = (float **)calloc(L, sizeof(float *));
+  float **g = (float **)calloc(L, sizeof(float *));
+  float *qkv = (float *)malloc(R * 3 * d * sizeof(float));
+  float *tmpa = (float *)malloc(R * d * sizeof(float));
+  float *tmpb = (float *)malloc(R * d * sizeof(float));
+  float *heads = (float *)malloc(R * d * sizeof(float));
+
+  xin[0] = (float *)malloc(R * d * sizeof(float));
+  orc_embedding_forward(R, V, d, ids, P(0), xin[0]);
+  for (size_t l = 0; l < L; l++) {
+    h1[l] = (float *)malloc(R * d * sizeof(float));
+    orc_layer_norm_forward(R, d, xin[l], P(LT(l, 0)), P(LT(l, 1)), eps, h1[l]);
+    orc_linear_forward(R, d, 3 * d, h1[l], P(LT(l, 2)), P(LT(l, 3)), qkv);
+    qh[l] = (float *)malloc(R * d * sizeof(float));
+    kh[l] = (float *)malloc(R * d * sizeof(float));
+    vh[l] = (float *)malloc(R * d * sizeof(float));
+    split_heads(qkv, B, T, H, Dh, 0, heads);
+    orc_rope(rope_shape, heads, pos, inv_freq, 0, qh[l]);
+    split_heads(qkv, B, T, H, Dh, 1, heads);
+    orc_rope(rope_shape, heads, pos, inv_freq, 0, kh[l]);
+    split_heads(qkv, B, T, H, Dh, 2, vh[l]);
+    orc_attention_forward(att_shape, qh[l], kh[l], vh[l], pos, pos, keep,
+                          heads);
+    om[l] = (float *)malloc(R * d * sizeof(float));
+    merge_heads(heads, B, T, H, Dh, d, 0, om[l]);
+    orc_linear_forward(R, d, d, om[l], P(LT(l, 4)), P(LT(l, 5)), tmpa);
+    xmid[l] = (float *)malloc(R * d * sizeof(float));
+    for (size_t i = 0; i < R * d; i++) xmid[l][i] = xin[l][i] + tmpa[i];
+    h2[l] = (float *)malloc(R * d * sizeof(float));
+    orc_layer_norm_forward(R, d, xmid[l], P(LT(l, 6)), P(LT(l, 7)), eps,
+                           h2[l]);
+    u[l] = (float *)malloc(R * F * sizeof(float));
+    orc_linear_forward(R, d, F, h2[l], P(LT(l, 8)), P(LT(l, 9)), u[l]);
+    g[l] = (float *)malloc(R * F * sizeof(float));
+    orc_gelu_forward(R * F, u[l], g[l]);
+    orc_linear_forward(R, F, d, g[l], P(LT(l, 10)), P(LT(l, 11)), tmpa);
+    xin[l + 1] = (float *)malloc(R * d * sizeof(float));
+    for (size_t i = 0; i < R * d; i++) xin[l + 1][i] = xmid[l][i] + tmpa[i];
+  }
+  float *xf = (float *)malloc(R * d * sizeof(float));
+  orc_layer_norm_forward(R, d, xin[L], P(count - 2), P(count - 1), eps, xf);
+  float *logits = (float *)malloc(R * V * sizeof(float));
+  orc_linear_forward(R, d, V, xf, P(0), NULL, logits);
+  float *loss = (float *)malloc(R * sizeof(float));
+  orc_ce_forward(R, V, logits, targets, loss);
+  const float mean = orc_mean_loss(R, loss);
+
+  /* backward: CE upstream is 1/N (the reference's numerator seed 1 with the
+   * O2 division by the token weight N moved here; exact for N = 2^k). */
+  float *upstream = loss; /* reuse */
+  const float scale = (float)(1.0 / (token_scale > 0 ? token_scale : (double)R));
+  for (size_t r = 0; r < R; r++) upstream[r] = scale;
+  float *dlogits = logits; /* in place is fine: each row reads before write */
+  {
+    float *tmp = (float *)malloc(R * V * sizeof(float));
+    orc_ce_backward(R, V, logits, targets, upstream, tmp);
+    memcpy(dlogits, tmp, R * V * sizeof(float));
+    free(tmp);
+  }
+  float *dhead = (float *)malloc(V * d * sizeof(float));
+  float *dx = (float *)malloc(R * d * sizeof(float));
+  float *dxf = (float *)malloc(R * d * sizeof(float));
+  orc_linear_backward(R, d, V, xf, P(0), dlogits, dxf, dhead, NULL);
+  orc_layer_norm_backward(R, d, xin[L], P(count - 2), eps, dxf, dx,
+                          G(count - 2), G(count - 1));
+  float *du = (float *)malloc(R * F * sizeof(float));
+  float *dg = (float *)malloc(R * F * sizeof(float));
+  float *dqkv = (float *)malloc(R * 3 * d * sizeof(float));
+  float *dq = (float *)malloc(R * d * sizeof(float));
+  float *dk = (float *)malloc(R * d * sizeof(float));
+  float *dv = (float *)malloc(R * d * sizeof(float));
+  float *dbr = (float *)malloc(R * d * sizeof(float));
+  for (size_t li = L; li-- > 0;) {
+    const size_t l = li;
+    /* FFN branch: dx is the upstream of both the skip and the branch */
+    orc_linear_backward(R, F, d, g[l], P(LT(l, 10)), dx, dg, G(LT(l, 10)),
+                        G(LT(l, 11)));
+    orc_gelu_backward(R * F, u[l], dg, du);
+    orc_linear_backward(R, d, F, h2[l], P(LT(l, 8)), du, tmpa, G(LT(l, 8)),
+                        G(LT(l, 9)));
+    orc_layer_norm_backward(R, d, xmid[l], P(LT(l, 6)), eps, tmpa, dbr,
+                            G(LT(l, 6)), G(LT(l, 7)));
+    add_into(R * d, dx, dbr); /* skip + branch */
+    /* attention branch */
+    orc_linear_backward(R, d, d, om[l], P(LT(l, 4)), dx, tmpa, G(LT(l, 4)),
+                        G(LT(l, 5)));
+    {
+      /* merged [R,d] -> heads */
+      for (size_t b = 0; b < B; b++)
+        for (size_t h = 0; h < H; h++)
+          for (size_t t = 0; t < T; t++)
+            memcpy(heads + ((b * H + h) * T + t) * Dh,
+                   tmpa + (b * T + t) * d + h * Dh, Dh * sizeof(float));
+    }
+    orc_attention_backward(att_shape, qh[l], kh[l], vh[l], pos, pos, keep,
+                           heads, dq, dk, dv);
+    orc_rope(rope_shape, dq, pos, inv_freq, 1, tmpb);
+    merge_heads(tmpb, B, T, H, Dh, 3 * d, 0, dqkv);
+    orc_rope(rope_shape, dk, pos, inv_freq, 1, tmpb);
+    merge_heads(tmpb, B, T, H, Dh, 3 * d, d, dqkv);
+    merge_heads(dv, B, T, H, Dh, 3 * d, 2 * d, dqkv);
+    orc_linear_backward(R, d, 3 * d, h1[l], P(LT(l, 2)), dqkv, tmpa,
+                        G(LT(l, 2)), G(LT(l, 3)));
+    orc_layer_norm_backward(R, d, xin[l], P(LT(l, 0)), eps, tmpa, dbr,
+                            G(LT(l, 0)), G(LT(l, 1)));
+    add_into(R * d, dx, dbr);
+  }
+  /* tied embedding: head gradient first, then the token-embedding scatter */
+  orc_embedding_backward(R, V, d, ids, dx, G(0));
+  for (size_t i = 0; i < V * d; i++) G(0)[i] = dhead[i] + G(0)[i];
+
+  for (size_t l = 0; l < L; l++) {
+    free(h1[l]); free(qh[l]); free(kh[l]); free(vh[l]); free(om[l]);
+    free(xmid[l]); free(h2[l]); free(u[l]); free(g[l]);
+  }
+  for (size_t l = 0; l <= L; l++) free(xin[l]);
+  free(xin); free(h1); free(qh); free(kh); free(vh); free(om); free(xmid);
+  free(h2); free(u); free(g); free(qkv); free(tmpa); free(tmpb); free(heads);
+  free(xf); free(logits); free(loss); free(dhead); free(dx); free(dxf);
+  free(du); free(dg); free(dqkv); free(dq); free(dk); free(dv); free(dbr);
+  free(inv_freq); free(pos); free(keep); free(sizes); free(offs);
+#undef P
+#undef G
+#undef LT
+  return mean;
+}
+
+int orc_lm_adamw(const orc_lm_config *c, float *params, const float *grads,
+                 float *exp_avg, float *exp_avg_sq,
+                 const orc_adamw_options *options, uint64_t update) {
+  const size_t count = orc_lm_tensor_count(c);
+  size_t *sizes = (size_t *)malloc(count * sizeof(size_t));
+  const size_t total = orc_lm_tensor_sizes(c, sizes);
+  free(sizes);
+  return orc_adamw_step(total, params, grads, exp_avg, exp_avg_sq, options,
+                        update, 0x3f800000u, 0x3f800000u, 0x3f800000u);
+}

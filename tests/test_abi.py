@@ -1,0 +1,122 @@
+"""The C-ABI surface, checked without a GPU: the library loads, exports every
+entry point include/ declares, keeps the K1 v1 struct layouts, and its host-
+side pieces (seeded inputs, schedule rounding, provider descriptors) agree
+with the oracle."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import eshkol_transformer_b200 as etb
+from eshkol_transformer_b200 import k1
+from helpers import bits_equal
+from oracle import oracle as orc
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_functions():
+    names = set()
+    for header in (ROOT / "include").rglob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        for m in re.finditer(r"\b(et_[a-z0-9_]+)\s*\(", text):
+            if not m.group(1).endswith("_t"):
+                names.add(m.group(1))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_k1_layouts_match_reference_sizes():
+    for name, size in k1.LAYOUT_SIZES.items():
+        assert C.sizeof(getattr(k1, name)) == size, name
+    assert k1.TensorView.shape.offset == 64
+    assert k1.Call.outputs.offset == 80
+    assert k1.Provider.invoke_call.offset == 88
+    assert k1.Capability.shape_ranges.offset == 112
+
+
+def test_header_compiles_standalone_c_and_cpp(tmp_path):
+    import subprocess
+    src = tmp_path / "t.c"
+    src.write_text('#include "eshkol_b200/et_b200.h"\nint main(void){return 0;}\n')
+    for compiler, name in (("gcc", "t.c"), ("g++", "t.cpp")):
+        f = tmp_path / name
+        f.write_text(src.read_text())
+        subprocess.run([compiler, "-std=c11" if compiler == "gcc" else "-std=c++17", "-Wall",
+                        "-Werror", f"-I{ROOT / 'include'}", "-fsyntax-only", str(f)], check=True)
+
+
+@pytest.mark.parametrize("seed,stream,count", [(1, 0, 1000), (20261201, 7, 4096), (99, 12345, 33)])
+def test_synthetic_inputs_identical_to_oracle(seed, stream, count):
+    assert bits_equal(etb.fill_normal(seed, stream, count, 0.0, 0.02),
+                      orc.fill_normal(seed, stream, count, 0.0, 0.02))
+    assert np.array_equal(etb.fill_tokens(seed, stream, count, 32768),
+                          orc.fill_tokens(seed, stream, count, 32768))
+    assert np.array_equal(etb.fill_tokens(seed, stream, count, 1000),
+                          orc.fill_tokens(seed, stream, count, 1000))
+
+
+def test_schedule_factor_identical_to_oracle(lib):
+    for warm, total, minimum in ((2, 6, 0.1), (0, 4, 0.25), (10, 1000, 0.0), (3, 7, 1e-40),
+                                 (1, 3, 0.3333)):
+        mb = orc.bits(minimum)
+        for u in range(1, total + 3):
+            assert lib.et_b200_o2_schedule_factor_v1(1, warm, total, mb, u) == \
+                orc.schedule_factor(1, warm, total, mb, u), (warm, total, minimum, u)
+    assert lib.et_b200_o2_schedule_factor_v1(0, 0, 0, 0, 5) == 0x3F800000
+
+
+@pytest.mark.parametrize("accessor,caps", [
+    ("et_a2_kernel_provider_v1", {"kernel.causal-attention", "kernel.rope"}),
+    ("et_n2_kernel_provider_v1", {"kernel.matmul", "kernel.norm", "kernel.activation",
+                                  "kernel.residual", "kernel.embedding-forward",
+                                  "kernel.embedding-backward"}),
+    ("et_n3k_kernel_provider_v1", {"n3k.linear"}),
+    ("et_l2_indexed_cross_entropy_provider_v1", {"kernel.indexed-cross-entropy"}),
+])
+def test_provider_descriptors(lib, accessor, caps):
+    p = k1.provider(lib, accessor)
+    assert p.struct_size == 96 and p.abi_major == 1
+    got = k1.capabilities(p)
+    assert set(got) == caps
+    for cap in got.values():
+        assert cap["status"] == k1.CAPABILITY_VERIFIED and cap["deterministic"]
+        assert set(cap["devices"]) == {"cpu", "cuda"} and cap["dtypes"] == ["f32"]
+        assert cap["operations"] == sorted(cap["operations"])
+
+
+def test_reference_k1_runtime_discovers_b200_providers(lib):
+    """The reference's own K1 runtime (native/kernel_abi.c, compiled by
+    oracle/Makefile.ref) accepts each provider descriptor unchanged."""
+    ref = orc.ref()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    RESOLVER = C.CFUNCTYPE(C.c_void_p, C.c_void_p, C.c_char_p)
+    for accessor in ("et_a2_kernel_provider_v1", "et_n2_kernel_provider_v1",
+                     "et_n3k_kernel_provider_v1", "et_l2_indexed_cross_entropy_provider_v1"):
+        fn = getattr(lib, accessor)
+        fn.restype = C.c_void_p
+        target = fn()
+        resolver = RESOLVER(lambda ctx, sym, t=target: t)
+        runtime = C.c_void_p()
+        err = k1.KernelError()
+        ref.et_kernel_runtime_discover.argtypes = [RESOLVER, C.c_void_p, C.POINTER(C.c_void_p),
+                                                   C.POINTER(k1.KernelError)]
+        rc = ref.et_kernel_runtime_discover(resolver, None, C.byref(runtime), C.byref(err))
+        assert rc == 0, str(err)
+        ref.et_kernel_runtime_destroy.argtypes = [C.c_void_p]
+        ref.et_kernel_runtime_destroy(runtime)
+
+
+def test_k1_precision_setter(lib):
+    assert lib.et_b200_k1_precision_v1(etb.PRECISION_F32) == 0
+    assert lib.et_b200_k1_precision_v1(9) != 0
+    assert lib.et_b200_k1_precision_v1(etb.PRECISION_TF32X3) == 0

@@ -1,0 +1,157 @@
+"""The fused training step and the device AdamW against the oracle.
+
+* O2 AdamW on device: parameters and moments bit-identical to the
+  reference's per-element arithmetic (oracle pinned by the adamw fixtures).
+* The tiny decoder LM (2 layers, d 128, 4 heads, FFN 512, vocab 1024, seq 64,
+  batch 8): seeded initial weights bit-identical; per-tensor gradients within
+  a stated normwise tolerance; updated weights; the loss over several steps.
+"""
+import numpy as np
+import pytest
+import torch
+
+import eshkol_transformer_b200 as etb
+from helpers import assert_close, assert_close_norm, bits_equal
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("clip,schedule", [(0.0, 0), (0.5, 0), (0.0, 1), (1e9, 1)])
+def test_o2_device_adamw_bit_identical(lib, cuda, clip, schedule):
+    sizes = [1000, 37, 4096, 1]
+    opts = [(1e-3, 0.9, 0.999, 1e-8, 0.01), (5e-3, 0.8, 0.95, 1e-6, 0.0),
+            (2e-2, 0.9, 0.999, 1e-8, 0.1), (1e-3, 0.5, 0.9, 1e-5, 0.2)]
+    params = [orc.fill_normal(3, i, n) for i, n in enumerate(sizes)]
+    p_dev = [torch.from_numpy(p.copy()).cuda() for p in params]
+    g_dev = [torch.zeros(n, device="cuda") for n in sizes]
+    entries = [(p_dev[i].data_ptr(), g_dev[i].data_ptr(), n, *opts[i]) for i, n in enumerate(sizes)]
+    warm, total, minimum = (2, 6, 0.1) if schedule else (0, 0, 0.0)
+    opt = etb.Optimizer(entries, clip_kind=1 if clip else 0, clip_max=clip,
+                        schedule_kind=schedule, warmup=warm, total=total, minimum_ratio=minimum)
+    ref_p = [p.copy() for p in params]
+    ref_m = [np.zeros(n, np.float32) for n in sizes]
+    ref_v = [np.zeros(n, np.float32) for n in sizes]
+    weight = 3.0
+    for step in range(1, 5):
+        grads = [orc.fill_normal(100 + step, i, n, 0.0, 2.0) for i, n in enumerate(sizes)]
+        for gd, g in zip(g_dev, grads):
+            gd.copy_(torch.from_numpy(g))
+        norm = opt.step(weight)
+        ref_norm = orc.global_norm(grads, weight)
+        assert abs(norm - ref_norm) <= 1e-6 * ref_norm  # summation order differs
+        clip_f = np.float32(1.0)
+        if clip and ref_norm > clip:
+            clip_f = np.float32(np.float32(clip) / np.float32(norm))
+        sched = orc.schedule_factor(schedule, warm, total, orc.bits(minimum) if schedule else 0,
+                                    step)
+        for i in range(len(sizes)):
+            assert orc.adamw_step(ref_p[i], grads[i], ref_m[i], ref_v[i],
+                                  orc.adamw_options(*opts[i]), step, weight, sched,
+                                  float(clip_f)) == 0
+        torch.cuda.synchronize()
+        for i in range(len(sizes)):
+            m_ptr, v_ptr = opt.moments(i)
+            m = device_view(m_ptr, sizes[i]).cpu().numpy()
+            v = device_view(v_ptr, sizes[i]).cpu().numpy()
+            assert bits_equal(p_dev[i].cpu().numpy(), ref_p[i]), (step, i, "parameter")
+            assert bits_equal(m, ref_m[i]), (step, i, "exp_avg")
+            assert bits_equal(v, ref_v[i]), (step, i, "exp_avg_sq")
+    opt.close()
+
+
+class _DeviceArray:
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3}
+
+
+def device_view(ptr: int, n: int) -> torch.Tensor:
+    """Zero-copy torch view of an f32 device buffer the library owns."""
+    return torch.as_tensor(_DeviceArray(ptr, n), device="cuda")
+
+
+TINY = etb.TINY
+
+
+def _oracle_model():
+    s = TINY
+    return orc.LanguageModel(s.layers, s.d_model, s.heads, s.ffn, s.vocabulary, s.seq_len, s.batch)
+
+
+# Per-tensor gradient tolerance (max |err| <= tol * max |ref|) of one step of
+# the tiny LM against the serial-f32 oracle: the GEMMs, attention, LN and CE
+# reductions all sum in a different order from the reference.
+GRAD_TOL = {etb.PRECISION_TF32X3: 5e-5, etb.PRECISION_F32: 5e-5, etb.PRECISION_TF32: 5e-3}
+
+
+@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F32, etb.PRECISION_TF32])
+def test_tiny_lm_gradients_vs_oracle(lib, cuda, precision):
+    s = TINY
+    om = _oracle_model()
+    params = om.init(1234)
+    ids, targets = orc.synthetic_batch(77, s.batch, s.seq_len, s.vocabulary)
+    loss_ref, grads_ref = om.forward_backward(params, ids, targets)
+    model = etb.LanguageModel(s, precision=precision)
+    model.init(1234)
+    assert bits_equal(model.read(0), params)  # seeded init is bit-identical
+    loss = model.forward_backward(ids, targets)
+    grads = model.read(1)
+    assert abs(loss - loss_ref) <= 2e-5 * abs(loss_ref), (loss, loss_ref)
+    worst = []
+    for t, (g, r) in enumerate(zip(om.split(grads), om.split(grads_ref))):
+        err = np.abs(g.astype(np.float64) - r).max() / max(np.abs(r).max(), 1e-30)
+        worst.append(err)
+        assert err <= GRAD_TOL[precision], (t, err)
+    print("worst per-tensor normwise gradient error", max(worst))
+    model.close()
+
+
+def test_tiny_lm_training_trajectory_vs_oracle(lib, cuda):
+    """Five AdamW steps: loss trajectory and final weights.  Loss within 2e-5
+    relative (the reference's TR3 loss tolerance); weights within 2e-6 abs."""
+    s = TINY
+    om = _oracle_model()
+    params = om.init(99)
+    m = np.zeros_like(params)
+    v = np.zeros_like(params)
+    opts = orc.adamw_options(1e-3, 0.9, 0.999, 1e-8, 0.01)
+    model = etb.LanguageModel(s, precision=etb.PRECISION_TF32X3)
+    model.init(99)
+    for step in range(1, 6):
+        ids, targets = orc.synthetic_batch(1000 + step, s.batch, s.seq_len, s.vocabulary)
+        loss_ref, grads_ref = om.forward_backward(params, ids, targets)
+        assert om.adamw(params, grads_ref, m, v, opts, step) == 0
+        loss = model.step(ids, targets)
+        assert abs(loss - loss_ref) <= 2e-5 * abs(loss_ref), (step, loss, loss_ref)
+    assert_close(model.read(0), params, 2e-6, 0.0, "weights after 5 steps")
+    model.close()
+
+
+def test_step_rejects_out_of_range_ids(lib, cuda):
+    s = TINY
+    model = etb.LanguageModel(s)
+    model.init(5)
+    ids, targets = orc.synthetic_batch(5, s.batch, s.seq_len, s.vocabulary)
+    targets[0, 3] = s.vocabulary
+    with pytest.raises(etb.B200Error):
+        model.forward_backward(ids, targets)
+    ids2, targets2 = orc.synthetic_batch(6, s.batch, s.seq_len, s.vocabulary)
+    assert np.isfinite(model.forward_backward(ids2, targets2))  # recovers
+    model.close()
+
+
+def test_launch_counter_and_device_step(lib, cuda):
+    s = TINY
+    model = etb.LanguageModel(s)
+    model.init(3)
+    ids, targets = orc.synthetic_batch(3, s.batch, s.seq_len, s.vocabulary)
+    d_ids = torch.from_numpy(ids).cuda()
+    d_tg = torch.from_numpy(targets).cuda()
+    loss = torch.zeros(1, device="cuda")
+    before = etb.launch_count()
+    model.step_device(d_ids.data_ptr(), d_tg.data_ptr(), loss.data_ptr())
+    torch.cuda.synchronize()
+    assert etb.launch_count() - before > 20
+    assert np.isfinite(loss.item())
+    model.close()
