@@ -381,7 +381,16 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="small case of the same kernels for ncu captures (2 layers, global "
+                         "batch 4 = 4096 tokens; a few GB on the device); not a bench value")
     args = ap.parse_args()
+    if args.profile_case:
+        global GLOBAL_BATCH, WORKLOAD
+        SHAPE["layers"] = 2
+        GLOBAL_BATCH = 4
+        WORKLOAD = "ncu profiling case: medium-LM widths, 2 layers, global batch 4"
+        args.no_cpu_baseline = True
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -67,7 +67,8 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Block-wide reduction helpers (blockDim.x multiple of 32, <= 1024).
+// Block-wide reduction helpers (blockDim.x multiple of 32, <= 1024); lanes
+// past the warp count contribute Op's identity.
 template <typename T, typename Op>
 __device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -78,7 +79,7 @@ __device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
   if (lane == 0) scratch[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    v = lane < warps ? scratch[lane] : scratch[0];
+    v = lane < warps ? scratch[lane] : Op::template identity<T>();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
     if (lane == 0) scratch[0] = v;
@@ -91,9 +92,11 @@ __device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
 
 struct AddOp {
   template <typename T> __device__ __forceinline__ T operator()(T a, T b) const { return a + b; }
+  template <typename T> __device__ __forceinline__ static T identity() { return T(0); }
 };
 struct MaxOp {
   __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); }
+  template <typename T> __device__ __forceinline__ static T identity() { return -INFINITY; }
 };
 
 }  // namespace etb

@@ -17,7 +17,7 @@
 //            add the bias and store f32 results.
 // Two TMEM accumulators (2 x BN columns) let the epilogue of one tile overlap
 // the main loop of the next.  The 3xTF32 mode feeds tf32-exact operands
-// (hi = x with its low 13 mantissa bits cleared) plus their residuals lo and
+// (hi = x rounded to TF32, low 13 mantissa bits zero) plus residuals lo and
 // accumulates A B + A B_lo + A_lo B, which keeps f32-grade accuracy.
 // Every mbarrier wait is bounded (about two seconds of clock) and reports
 // through the device error word instead of hanging.
@@ -57,8 +57,11 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs g) {
       if (g.a_kmajor) { mm = i / SB_K; kk = i % SB_K; } else { kk = i / SB_M; mm = i % SB_M; }
       const int m = m0 + mm, k = k0 + kk;
       float v = 0.0f;
-      if (m < g.M && k < g.K)
-        v = g.a_kmajor ? g.A[(int64_t)m * g.lda + k] : g.A[(int64_t)k * g.lda + m];
+      if (m < g.M && k < g.K) {
+        const int64_t at = g.a_kmajor ? (int64_t)m * g.lda + k : (int64_t)k * g.lda + m;
+        v = g.A[at];
+        if (g.A_lo) v += g.A_lo[at];  // hi + lo restores the f32 operand exactly
+      }
       As[kk][mm] = v;
     }
     for (int i = tid; i < SB_N * SB_K; i += 256) {
@@ -66,8 +69,11 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs g) {
       if (g.b_kmajor) { nn = i / SB_K; kk = i % SB_K; } else { kk = i / SB_N; nn = i % SB_N; }
       const int n = n0 + nn, k = k0 + kk;
       float v = 0.0f;
-      if (n < g.N && k < g.K)
-        v = g.b_kmajor ? g.B[(int64_t)n * g.ldb + k] : g.B[(int64_t)k * g.ldb + n];
+      if (n < g.N && k < g.K) {
+        const int64_t at = g.b_kmajor ? (int64_t)n * g.ldb + k : (int64_t)k * g.ldb + n;
+        v = g.B[at];
+        if (g.B_lo) v += g.B_lo[at];
+      }
       Bs[kk][nn] = v;
     }
     __syncthreads();
@@ -172,22 +178,28 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
-__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor (sm_100 version field = 1).  layout 2 is
+// the 128-byte swizzle with 16-byte atoms; layout 1 the 128-byte swizzle with
+// 32-byte atoms, the only MN-major layout tcgen05 accepts for 32-bit operands.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                          uint32_t layout) {
   uint64_t d = (uint64_t)((addr >> 4) & 0x3fffu);
   d |= (uint64_t)((lbo >> 4) & 0x3fffu) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3fffu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;
   return d;
 }
 
 // Descriptor of the j-th K=8 slice of a staged operand tile.
-//   K-major : rows of 128 B (32 k), 8-row atoms 1024 B apart, slice j at +32j B
-//   MN-major: per 32-wide MN chunk 32 k-rows of 128 B (4096 B), chunks 4096 B
-//             apart (LBO), 8-k-row groups 1024 B apart (SBO), slice j at +1024j B
+//   K-major : rows of 128 B (32 k), 8-row swizzle atoms 1024 B apart (SBO),
+//             slice j at +32j B within the atom row.
+//   MN-major: per 32-wide MN chunk, 32 k-rows of 128 B (4096 B); chunks 4096 B
+//             apart (LBO); 4-row swizzle groups 512 B apart (SBO); slice j
+//             (8 k-rows) at +1024j B.
 __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int j) {
-  return mn_major ? sdesc(base + 1024u * j, 4096u, 1024u) : sdesc(base + 32u * j, 16u, 1024u);
+  return mn_major ? sdesc(base + 1024u * j, 4096u, 512u, 1u)
+                  : sdesc(base + 32u * j, 16u, 1024u, 2u);
 }
 
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
@@ -469,9 +481,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D f32 tensor map over a row-major [outer, inner] array with row stride
-// `ld` elements; box {32, box_outer}, 128-byte swizzle, zero OOB fill.
+// `ld` elements; box {32, box_outer}, zero OOB fill.  The swizzle must match
+// the descriptor layout the MMA reads the tile with.
 bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, int64_t ld,
-              uint32_t box_outer) {
+              uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {inner, outer};
@@ -479,16 +492,20 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t oute
   const cuuint32_t box[2] = {32, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Operand map: K-major [rows, K] with box {32 k, tile rows}; MN-major [K, rows]
-// with box {32 mn, 32 k} (one load per 32-wide chunk).
+// Operand map: K-major [rows, K] with box {32 k, tile rows} and the 16-byte-
+// atom 128-byte swizzle; MN-major [K, rows] with box {32 mn, 32 k} (one load
+// per 32-wide chunk) and the 32-byte-atom 128-byte swizzle.
 bool operand_map(CUtensorMap* map, const float* p, bool kmajor, int rows, int K, int64_t ld,
                  int tile_rows) {
-  if (kmajor) return make_map(map, p, (uint64_t)K, (uint64_t)rows, ld, (uint32_t)tile_rows);
-  return make_map(map, p, (uint64_t)rows, (uint64_t)K, ld, 32u);
+  if (kmajor)
+    return make_map(map, p, (uint64_t)K, (uint64_t)rows, ld, (uint32_t)tile_rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_map(map, p, (uint64_t)rows, (uint64_t)K, ld, 32u,
+                  CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
 template <int BN, int STAGES, bool THREE>

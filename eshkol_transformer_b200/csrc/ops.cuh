@@ -79,8 +79,9 @@ void embedding_backward(const int64_t* ids, const float* dy, const float* base,
 size_t colsum_workspace_floats(size_t rows, size_t n);
 void column_sum(const float* dy, float* out, size_t rows, size_t n,
                 float* workspace, cudaStream_t stream);
-// 3xTF32 operand split: hi = x with its low 13 mantissa bits cleared (exactly
-// representable in TF32) and lo = x - hi (exact).  hi may alias x.
+// 3xTF32 operand split: hi = x rounded to the nearest TF32 value (exactly
+// representable, low 13 mantissa bits zero) and lo = x - hi (exact, at most
+// 2^-11 |x|).  hi may alias x.
 void split_tf32(const float* x, float* hi, float* lo, size_t count, cudaStream_t stream);
 // Standalone RoPE over [N,H,T,Dh] with a host-built cos/sin table
 // [N*T, Dh/2] each (bit-identical rotation).

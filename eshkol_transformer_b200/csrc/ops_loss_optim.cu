@@ -41,6 +41,9 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
   const int64_t target = targets[row];
   const bool target_ok = target >= 0 && target < V;
   if (!target_ok && threadIdx.x == 0) atomicExch(status, 1);
+  // The target logit is read before the block reductions: once they finish,
+  // other threads overwrite the row with gradients when dlogits == logits.
+  const float x_target = (threadIdx.x == 0 && target_ok) ? x[target] : 0.0f;
 
   float m = -INFINITY, s = 0.0f;
   const bool vec = ((V & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
@@ -62,10 +65,7 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
   const float mine = (s == 0.0f) ? 0.0f : s * expf(m - row_max);
   const float row_sum = block_reduce(mine, red_s, AddOp());
 
-  if (threadIdx.x == 0 && loss != nullptr) {
-    const float xt = target_ok ? x[target] : 0.0f;
-    loss[row] = logf(row_sum) + (row_max - xt);
-  }
+  if (threadIdx.x == 0 && loss != nullptr) loss[row] = logf(row_sum) + (row_max - x_target);
   if (dlogits == nullptr) return;
   const float u = upstream != nullptr ? upstream[row] : upstream_scale;
   float* g = dlogits + row * V;

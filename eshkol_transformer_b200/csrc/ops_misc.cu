@@ -178,8 +178,16 @@ __global__ void split_tf32_kernel(const float* x, float* hi_out, float* __restri
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float v = x[i];
-    const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
-    lo[i] = v - hi;  // exact: the dropped low mantissa bits
+    // hi: v rounded to the nearest TF32 value (10 explicit mantissa bits,
+    // ties away from zero), so |lo| <= 2^-11 |v|; the add cannot carry past
+    // the exponent except into the next binade, which is still exact.
+    uint32_t b = __float_as_uint(v);
+    if ((b & 0x7f800000u) != 0x7f800000u) {
+      const uint32_t r = (b + 0x1000u) & 0xffffe000u;
+      b = ((r & 0x7f800000u) == 0x7f800000u) ? (b & 0xffffe000u) : r;  // no overflow to inf
+    }
+    const float hi = __uint_as_float(b);
+    lo[i] = v - hi;  // exact: |v - hi| fits in the low mantissa bits
     hi_out[i] = hi;
   }
 }
