@@ -116,6 +116,34 @@ int32_t et_b200_o2_optimizer_moments_v1(et_b200_o2_optimizer *optimizer,
                                         size_t index, float **exp_avg,
                                         float **exp_avg_sq);
 void et_b200_o2_optimizer_destroy_v1(et_b200_o2_optimizer **optimizer);
+/* AdamW step for callers that cannot allocate device memory: hosts that give
+ * all of HBM to their own allocator at start-up, and loops that keep the
+ * device footprint fixed because cudaMalloc/cudaFree can synchronise the
+ * device mid-step.  No counterpart in the reference (its O2 optimizer is a
+ * CPU object).  The caller owns the parameter, gradient and both moments
+ * (device f32, `count` elements, moments zero before update 1); the call
+ * divides the gradient by the normalisation weight, computes the global L2
+ * norm, clips to clip_max_bits when that is nonzero, and applies the O2
+ * update `update` (1-based, constant schedule) with the same per-element
+ * rounding as et_b200_o2_optimizer_step_v1.  Its only scratch is a 64 KiB
+ * file-scope device array that every GPU loading the library holds until
+ * exit; count above ET_B200_ADAMW_NOALLOC_MAX_ELEMENTS is rejected.  Calls
+ * share that array and its contents persist between calls: the call clears
+ * what must start at zero itself, and calls that overlap on the GPU (on
+ * different streams or host threads) race on it.  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) and
+ * should come before any stream capture.  Enqueued on `stream` (a
+ * cudaStream_t, NULL = legacy default stream) and synchronised before
+ * returning; norm_bits (optional) receives the norm.  A nonfinite gradient
+ * leaves every tensor unchanged and returns INVALID_ARGUMENT. */
+#define ET_B200_ADAMW_NOALLOC_MAX_ELEMENTS ((uint64_t)8192u * 65536u)
+int32_t et_b200_adamw_step_noalloc_v1(
+    float *value, const float *gradient, float *exp_avg, float *exp_avg_sq,
+    uint64_t count, uint32_t learning_rate_bits, uint32_t beta1_bits,
+    uint32_t beta2_bits, uint32_t epsilon_bits, uint32_t weight_decay_bits,
+    uint64_t update, uint32_t normalization_weight_bits,
+    uint32_t clip_max_bits, void *stream, uint32_t *norm_bits,
+    et_kernel_error *error);
 /* The schedule factor of update `update` as f32 bits: 1 for the constant
  * schedule; the exactly rounded linear warmup/decay ratio otherwise
  * (replaces et_o2_schedule_factor, native/o2_optimizer.c:1345-1374). */
