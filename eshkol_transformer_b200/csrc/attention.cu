@@ -489,6 +489,7 @@ void launch_bwd(const AttnParams& p, AttnTensor dout, const float* m, const floa
 void attention_forward(const AttnParams& p, AttnOut o, float* row_max, float* row_sum,
                        cudaStream_t stream) {
   if (p.B == 0 || p.Hq == 0 || p.Tq == 0) return;
+  if (attention_forward_tc(p, o, row_max, row_sum, stream)) return;
   const int qb = p.q_rope_batched, kb = p.k_rope_batched;
   if (p.Dh <= 32) launch_fwd<32>(p, o, row_max, row_sum, qb, kb, stream);
   else if (p.Dh <= 64) launch_fwd<64>(p, o, row_max, row_sum, qb, kb, stream);

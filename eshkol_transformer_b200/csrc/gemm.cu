@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "ops.cuh"
+#include "tcgen05.cuh"
 
 namespace etb {
 
@@ -117,7 +118,6 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs g) {
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 32;  // one 128-byte swizzle row of f32
 constexpr int TC_THREADS = 192;
-constexpr long long kWaitCycles = 1ll << 32;
 
 struct TcArgs {
   int M, N, K;
@@ -129,114 +129,6 @@ struct TcArgs {
   int tiles_m, tiles_n;
   int* error;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: false (and the error word set) when the phase does not
-// complete within kWaitCycles.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* error) {
-  if (mbar_try(bar, parity)) return true;
-  const long long start = clock64();
-  while (!mbar_try(bar, parity)) {
-    if (clock64() - start > kWaitCycles) {
-      atomicExch(error, 0x6e6d);  // 'mm': GEMM pipeline wait timed out
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor (sm_100 version field = 1).  layout 2 is
-// the 128-byte swizzle with 16-byte atoms; layout 1 the 128-byte swizzle with
-// 32-byte atoms, the only MN-major layout tcgen05 accepts for 32-bit operands.
-__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo,
-                                          uint32_t layout) {
-  uint64_t d = (uint64_t)((addr >> 4) & 0x3fffu);
-  d |= (uint64_t)((lbo >> 4) & 0x3fffu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3fffu) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)layout << 61;
-  return d;
-}
-
-// Descriptor of the j-th K=8 slice of a staged operand tile.
-//   K-major : rows of 128 B (32 k), 8-row swizzle atoms 1024 B apart (SBO),
-//             slice j at +32j B within the atom row.
-//   MN-major: per 32-wide MN chunk, 32 k-rows of 128 B (4096 B); chunks 4096 B
-//             apart (LBO); 4-row swizzle groups 512 B apart (SBO); slice j
-//             (8 k-rows) at +1024j B.
-__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int j) {
-  return mn_major ? sdesc(base + 1024u * j, 4096u, 512u, 1u)
-                  : sdesc(base + 32u * j, 16u, 1024u, 2u);
-}
-
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
 
 // Grouped rasterisation: 16 M-tiles per group so the CTAs in flight share
 // their A row blocks and B column blocks through L2.
@@ -465,36 +357,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
 }
 
 // ---- host side ---------------------------------------------------------------
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// 2-D f32 tensor map over a row-major [outer, inner] array with row stride
-// `ld` elements; box {32, box_outer}, zero OOB fill.  The swizzle must match
-// the descriptor layout the MMA reads the tile with.
-bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, int64_t ld,
-              uint32_t box_outer, CUtensorMapSwizzle swizzle) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  const cuuint32_t box[2] = {32, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 // Operand map: K-major [rows, K] with box {32 k, tile rows} and the 16-byte-
 // atom 128-byte swizzle; MN-major [K, rows] with box {32 mn, 32 k} (one load

@@ -118,11 +118,19 @@ struct AttnParams {
   // 1 when a table has B*T rows (row b*T + t), 0 when it has T rows shared
   // by every sequence (row t).
   int q_rope_batched, k_rope_batched;
+  // optional device workspace of attention_workspace_floats(p) floats, 16-byte
+  // aligned; the tensor-core forward needs it (null = SIMT forward).
+  float* ws;
 };
+size_t attention_workspace_floats(const AttnParams& p);
 // Forward: o and per-row statistics m (row max of scaled scores) and l (sum
 // of exp(s - m)); rows with no admitted key produce o = 0, m = 0, l = 0.
 void attention_forward(const AttnParams& p, AttnOut o, float* row_max,
                        float* row_sum, cudaStream_t stream);
+// The tcgen05 forward (attention_tc.cu); false when the shape or layout is
+// outside it (Dh not 32/64/128, strides TMA cannot describe), nothing launched.
+bool attention_forward_tc(const AttnParams& p, AttnOut o, float* row_max,
+                          float* row_sum, cudaStream_t stream);
 // Backward: dq/dk/dv (RoPE backward applied to dq/dk when tables are set).
 // delta[B*Hq*Tq] is scratch for rowsum(dO * O); when o_lo is given (same
 // strides as o) the forward output is o + o_lo (a 3xTF32 hi/lo pair).

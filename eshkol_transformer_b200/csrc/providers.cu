@@ -367,6 +367,7 @@ void run_attention(Call& cl, const AttShape& s, bool backward, bool scratch,
   const int64_t* kp = (const int64_t*)dev_in(cl, 4);
   const uint8_t* mask = (const uint8_t*)dev_in(cl, 5);
   AttnParams p = attention_params(s, q, k, v, qp, kp, mask);
+  p.ws = (float*)P.alloc(attention_workspace_floats(p) * 4);
   const size_t rows = s.n * s.hq * s.tq;
   float* m = (float*)P.alloc(rows * 4);
   float* l = (float*)P.alloc(rows * 4);

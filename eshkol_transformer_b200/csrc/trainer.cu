@@ -83,7 +83,7 @@ struct et_b200_lm {
   // backward scratch
   float *dx = nullptr, *dxhi = nullptr, *dxlo = nullptr, *dtmp = nullptr, *dqkv = nullptr,
         *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *dg = nullptr, *delta = nullptr;
-  float *ln_ws = nullptr, *col_ws = nullptr;
+  float *ln_ws = nullptr, *col_ws = nullptr, *attn_ws = nullptr;
   void* emb_scratch = nullptr;
   int64_t *ids = nullptr, *targets = nullptr, *pos = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
@@ -238,6 +238,7 @@ AttnParams attn_params(et_b200_lm* lm, const float* qkv) {
   p.q_cos = lm->rope_cos; p.q_sin = lm->rope_sin;
   p.k_cos = lm->rope_cos; p.k_sin = lm->rope_sin;
   p.q_rope_batched = 0; p.k_rope_batched = 0;
+  p.ws = lm->attn_ws;
   return p;
 }
 
@@ -602,6 +603,12 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->ln_ws = dalloc<float>(lm, ln_workspace_floats(R, d), &err);
   lm->col_ws = dalloc<float>(lm, colsum_workspace_floats(R, widest), &err);
   lm->emb_scratch = dalloc<uint8_t>(lm, embedding_scratch_bytes(R, V), &err);
+  {
+    AttnParams shape{};
+    shape.B = (int)lm->B; shape.Hq = (int)lm->H; shape.Hkv = (int)lm->H;
+    shape.Tq = (int)lm->T; shape.Tk = (int)lm->T; shape.Dh = (int)lm->Dh;
+    lm->attn_ws = dalloc<float>(lm, attention_workspace_floats(shape), &err);
+  }
   lm->ids = dalloc<int64_t>(lm, R, &err);
   lm->targets = dalloc<int64_t>(lm, R, &err);
   lm->pos = dalloc<int64_t>(lm, R, &err);

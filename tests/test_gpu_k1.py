@@ -122,6 +122,9 @@ def _attention_inputs(shape, seed, masked=False):
     ((2, 4, 2, 100, 100, 64), True),    # GQA, ragged tiles, keep mask, empty row
     ((1, 2, 2, 37, 70, 128), False),    # Tq < Tk (cached-decode layout), Dh 128
     ((1, 3, 3, 65, 65, 8), True),
+    ((1, 2, 2, 512, 512, 64), False),   # several query tiles, fully visible key blocks
+    ((1, 4, 2, 300, 800, 32), False),   # Tq < Tk over several tiles, GQA
+    ((1, 2, 2, 256, 256, 128), False),  # Dh 128 over several tiles
 ])
 def test_attention_vs_oracle(lib, cuda, shape, masked):
     N, Hq, Hkv, Tq, Tk, Dh = shape
