@@ -501,6 +501,7 @@ void attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, At
                         const float* row_sum, float* delta, AttnOut dq, AttnOut dk, AttnOut dv,
                         cudaStream_t stream) {
   if (p.B == 0 || p.Hq == 0) return;
+  if (attention_backward_tc(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream)) return;
   const int64_t rows = (int64_t)p.B * p.Hq * p.Tq;
   if (rows > 0) {
     attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p, o, o_lo, dout, delta);

@@ -26,8 +26,7 @@
 // Key blocks entirely visible to every row of the tile skip the per-element
 // admission test.  All mbarrier waits are bounded; a timeout is taken
 // block-uniformly so the CTA always releases its TMEM.
-#include "ops.cuh"
-#include "tcgen05.cuh"
+#include "attention_tc.cuh"
 
 namespace etb {
 
@@ -36,8 +35,6 @@ namespace {
 constexpr int QM = 128;  // query rows per CTA
 constexpr int KN = 64;   // keys per block
 constexpr int THREADS = 256;
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
 
 // Dh <= 64: S is double buffered in TMEM, so Q K^T of the next key block runs
 // on the tensor cores while this block's softmax runs on the SM; Dh 128 has no
@@ -60,30 +57,6 @@ struct TcFwdArgs {
   const float *qh, *ql;  // head-major [B, Hq, Tq, Dh]
   int* error;
 };
-
-// Nearest TF32 value of a probability in [0, 1].
-__device__ __forceinline__ float tf32_round(float v) {
-  return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xffffe000u);
-}
-// Nearest TF32 value of a finite operand; magnitudes that would round up to
-// infinity are truncated instead, so hi stays finite and lo = x - hi exact.
-__device__ __forceinline__ float tf32_hi(float v) {
-  const uint32_t u = __float_as_uint(v);
-  uint32_t r = (u + 0x1000u) & 0xffffe000u;
-  if ((r & 0x7f800000u) == 0x7f800000u) r = u & 0xffffe000u;
-  return __uint_as_float(r);
-}
-
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t idesc_tf32(int n, int b_mn) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(QM >> 4) << 24);
-}
 
 // ---- operand preparation -------------------------------------------------------
 
@@ -204,8 +177,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap kh_map, const __grid_cons
       tma_load_2d(base + 3 * L::KTILE + c * KN * 128, &vl_map, full, 32 * c, r);
     }
   };
-  const uint32_t idesc_s = idesc_tf32(KN, 0);
-  const uint32_t idesc_o = idesc_tf32(DH, 1);
+  const uint32_t idesc_s = idesc_tf32_m128(KN, 0);
+  const uint32_t idesc_o = idesc_tf32_m128(DH, 1);
   auto s_slot = [&](int kb) { return L::S0 + (uint32_t)(L::PIPE ? (kb & 1) * KN : 0); };
   auto issue_s = [&](int kb) -> bool {  // thread 0: S(kb) = Q K(kb)^T
     const int k = next_full++;
@@ -216,9 +189,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap kh_map, const __grid_cons
     const uint32_t d = tmem + s_slot(kb);
 #pragma unroll
     for (int j = 0; j < DH / 8; j++) {
-      const uint32_t koff = (uint32_t)(j >> 2) * KN * 128u + (uint32_t)(j & 3) * 32u;
-      const uint64_t dh = sdesc(khs + koff, 16u, 1024u, 2u);
-      const uint64_t dl = sdesc(kls + koff, 16u, 1024u, 2u);
+      const uint64_t dh = kmajor_desc(khs, KN, j);
+      const uint64_t dl = kmajor_desc(kls, KN, j);
       umma_tf32_ts(d, tmem + L::QH + 8 * j, dh, idesc_s, j > 0 ? 1u : 0u);
       umma_tf32_ts(d, tmem + L::QH + 8 * j, dl, idesc_s, 1u);
       umma_tf32_ts(d, tmem + L::QL + 8 * j, dh, idesc_s, 1u);
@@ -233,8 +205,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap kh_map, const __grid_cons
     const uint32_t ph = tmem + s_slot(kb);
 #pragma unroll
     for (int j = 0; j < KN / 8; j++) {
-      const uint64_t dh = sdesc(vhs + 1024u * j, (uint32_t)KN * 128u, 512u, 1u);
-      const uint64_t dl = sdesc(vls + 1024u * j, (uint32_t)KN * 128u, 512u, 1u);
+      const uint64_t dh = mnmajor_desc(vhs, KN, j);
+      const uint64_t dl = mnmajor_desc(vls, KN, j);
       const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
       umma_tf32_ts(tmem + L::O, ph + 8 * j, dh, idesc_o, acc);
       umma_tf32_ts(tmem + L::O, ph + 8 * j, dl, idesc_o, 1u);
@@ -434,37 +406,19 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap kh_map, const __grid_cons
 }
 
 template <int DH>
-bool launch_fwd_tc(const AttnParams& p, AttnOut o, float* m, float* l, float* ws,
-                   cudaStream_t stream) {
+bool launch_fwd_tc(const AttnParams& p, AttnOut o, float* m, float* l, cudaStream_t stream) {
   using L = FwdLayout<DH>;
-  const int64_t nq = (int64_t)p.B * p.Hq * p.Tq * DH, nk = (int64_t)p.B * p.Hkv * p.Tk * DH;
-  float* qh = ws;
-  float* ql = qh + nq;
-  float* kh = ql + nq;
-  float* kl = kh + nk;
-  float* vh = kl + nk;
-  float* vl = vh + nk;
+  const AttnWs w = attn_ws(p);
   const int64_t krows = (int64_t)p.B * p.Hkv * p.Tk;
   if (krows >= ((int64_t)1 << 31)) return false;
   CUtensorMap mkh, mkl, mvh, mvl;
-  if (!make_map(&mkh, kh, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mkl, kl, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mvh, vh, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
-      !make_map(&mvl, vl, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+  if (!make_map(&mkh, w.kh, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mkl, w.kl, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mvh, w.vh, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+      !make_map(&mvl, w.vl, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return false;
-  const int threads = 256;
-  auto prep = [&](const AttnTensor& t, int H, int T, const float* ct, const float* st, int bat,
-                  float* hi, float* lo) {
-    const int64_t pairs = (int64_t)p.B * H * T * (DH / 2);
-    const int64_t want = (pairs + threads - 1) / threads;
-    const int grid = (int)(want < (int64_t)sm_count() * 32 ? want : (int64_t)sm_count() * 32);
-    attn_prepare_kernel<<<grid, threads, 0, stream>>>(t, p.B, H, T, DH, ct, st, bat, hi, lo);
-  };
-  prep(p.q, p.Hq, p.Tq, p.q_cos, p.q_sin, p.q_rope_batched, qh, ql);
-  prep(p.k, p.Hkv, p.Tk, p.k_cos, p.k_sin, p.k_rope_batched, kh, kl);
-  prep(p.v, p.Hkv, p.Tk, nullptr, nullptr, 0, vh, vl);
-  count_launch(3);
-  TcFwdArgs a{qh, ql, device_error_word()};
+  attention_prepare_qkv(p, w, stream);
+  TcFwdArgs a{w.qh, w.ql, device_error_word()};
   cudaFuncSetAttribute(attn_fwd_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        L::SMEM);
   dim3 grid((p.Tq + QM - 1) / QM, p.Hq, p.B);
@@ -475,9 +429,26 @@ bool launch_fwd_tc(const AttnParams& p, AttnOut o, float* m, float* l, float* ws
 
 }  // namespace
 
+void attention_prepare_qkv(const AttnParams& p, const AttnWs& w, cudaStream_t stream) {
+  const int threads = 256;
+  auto prep = [&](const AttnTensor& t, int H, int T, const float* ct, const float* st, int bat,
+                  float* hi, float* lo) {
+    const int64_t pairs = (int64_t)p.B * H * T * (p.Dh / 2);
+    const int64_t want = (pairs + threads - 1) / threads;
+    const int grid = (int)(want < (int64_t)sm_count() * 32 ? want : (int64_t)sm_count() * 32);
+    if (grid > 0)
+      attn_prepare_kernel<<<grid, threads, 0, stream>>>(t, p.B, H, T, p.Dh, ct, st, bat, hi, lo);
+  };
+  prep(p.q, p.Hq, p.Tq, p.q_cos, p.q_sin, p.q_rope_batched, w.qh, w.ql);
+  prep(p.k, p.Hkv, p.Tk, p.k_cos, p.k_sin, p.k_rope_batched, w.kh, w.kl);
+  prep(p.v, p.Hkv, p.Tk, nullptr, nullptr, 0, w.vh, w.vl);
+  count_launch(3);
+}
+
 size_t attention_workspace_floats(const AttnParams& p) {
   const size_t nq = (size_t)p.B * p.Hq * p.Tq * p.Dh, nk = (size_t)p.B * p.Hkv * p.Tk * p.Dh;
-  return 2 * nq + 4 * nk + 64;
+  const size_t rows = (size_t)p.B * p.Hq * p.Tq;
+  return 4 * nq + 4 * nk + rows + 64;
 }
 
 bool attention_forward_tc(const AttnParams& p, AttnOut o, float* row_max, float* row_sum,
@@ -485,9 +456,9 @@ bool attention_forward_tc(const AttnParams& p, AttnOut o, float* row_max, float*
   if (p.ws == nullptr || encode_fn() == nullptr) return false;
   if (reinterpret_cast<uintptr_t>(p.ws) & 15) return false;
   switch (p.Dh) {
-    case 32: return launch_fwd_tc<32>(p, o, row_max, row_sum, p.ws, stream);
-    case 64: return launch_fwd_tc<64>(p, o, row_max, row_sum, p.ws, stream);
-    case 128: return launch_fwd_tc<128>(p, o, row_max, row_sum, p.ws, stream);
+    case 32: return launch_fwd_tc<32>(p, o, row_max, row_sum, stream);
+    case 64: return launch_fwd_tc<64>(p, o, row_max, row_sum, stream);
+    case 128: return launch_fwd_tc<128>(p, o, row_max, row_sum, stream);
     default: return false;
   }
 }

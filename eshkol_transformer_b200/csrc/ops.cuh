@@ -138,6 +138,11 @@ void attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, At
                         const float* row_max, const float* row_sum,
                         float* delta, AttnOut dq, AttnOut dk, AttnOut dv,
                         cudaStream_t stream);
+// The tcgen05 backward (attention_bwd_tc.cu); false when the shape is outside
+// it (Dh not 32/64, no workspace), nothing launched.
+bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
+                           const float* row_max, const float* row_sum, float* delta, AttnOut dq,
+                           AttnOut dk, AttnOut dv, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMM
 // C[m, n] = sum_k A(m, k) B(n, k) (+ bias[n]) (+ C when accumulate).
