@@ -17,20 +17,21 @@
 //     query r; Q and dO hi/lo in TMEM.  For each 64-key block:
 //       S = Q K^T, dP = dO V^T (B = K, V K-major); dS -> TMEM hi/lo;
 //       dQ += dS K (B = K MN-major)
+//   Each kernel issues its MMAs from two threads in two warps, one chain per
+//   accumulator pair (a single issuing thread tops out near one N = 64 MMA
+//   per 46 cycles, two keep the tensor core busy); while one chain waits for
+//   the probabilities of a block the other chain's MMAs run.
 //
 // A prepass writes the RoPE'd, TF32-split head-major Q/K/V (shared with the
 // forward) and a second one dO hi/lo, delta and the base-2 log-sum-exp of
-// every query row, so P = 2^(s scale log2(e) - lse2).  8 warps: warp w serves
-// lanes 32*(w%4).. and columns 32*(w/4).. of each 64-wide block.  All
-// mbarrier waits are bounded; a timeout is taken block-uniformly, in-flight
-// copies and MMAs are waited for (bounded) and TMEM is always released.
+// every query row, so P = 2^(s scale log2(e) - lse2).  All mbarrier waits
+// are bounded; a timeout raises a CTA-wide abort flag, in-flight copies and
+// MMAs are waited for (bounded) and TMEM is always released.
 #include "attention_tc.cuh"
 
 namespace etb {
 
 namespace {
-
-constexpr int THREADS = 256;
 
 // ---- prepass -----------------------------------------------------------------------
 
@@ -80,26 +81,15 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
 }
 
-// Loads 32 floats of a row (zeros when the row is invalid) into TMEM.
-__device__ __forceinline__ void row_to_tmem(uint32_t taddr, const float* src, bool valid) {
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    const float4 x = valid ? *reinterpret_cast<const float4*>(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
-  }
-  tmem_st32(taddr, v);
-}
-
-// Scales 2m columns of an accumulator row, applies the RoPE backward
-// rotation to each (even, odd) pair when a table is given, and stores them.
+// Scales n columns [first, first + n) of an accumulator row and applies the
+// RoPE backward rotation to each (even, odd) pair when a table is given
+// (table entry trow + (col0 + i - first) / 2), in place.
 template <int N>
-__device__ __forceinline__ void store_grad_row(const float (&acc)[32], int first, float* dst,
-                                               float scale, const float* ct, const float* st,
-                                               int64_t trow, int col0) {
+__device__ __forceinline__ void grad_row(float (&v)[32], int first, float scale, const float* ct,
+                                         const float* st, int64_t trow, int col0) {
 #pragma unroll
   for (int i = first; i < first + N; i += 2) {
-    float x0 = rn_mul(acc[i], scale), x1 = rn_mul(acc[i + 1], scale);
+    float x0 = rn_mul(v[i], scale), x1 = rn_mul(v[i + 1], scale);
     if (ct != nullptr) {
       const int64_t ti = trow + (col0 + i - first) / 2;
       const float c = ct[ti], s = st[ti];
@@ -107,34 +97,63 @@ __device__ __forceinline__ void store_grad_row(const float (&acc)[32], int first
       x0 = rn_add(a, bb);
       x1 = rn_add(-cc, dd);
     }
-    dst[i - first] = x0;
-    dst[i - first + 1] = x1;
+    v[i] = x0;
+    v[i + 1] = x1;
   }
 }
 
+// Number of entries of the ascending array a[0..n) that are below x.
+__device__ __forceinline__ int count_below(const int64_t* a, int n, int64_t x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a[mid] < x) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+// ---- warp roles ----------------------------------------------------------------------------
+//
+// Warps 0-7 compute probabilities (TMEM lane quarter w%4, column half w/4 of
+// every block); warps 8 and 9 each issue one chain of tcgen05 MMAs from one
+// thread (a single issuing thread cannot keep the tensor core busy with
+// N = 64 tiles, two can); warp 10 loads operand tiles by TMA and stages
+// per-block row data.  Hand-offs are mbarriers, and every wait is at most one
+// phase behind its barrier.
+
+constexpr int THREADS = 352;
+constexpr int SOFT = 256;  // probability threads (warps 0-7)
+constexpr int MMA_A = 8, MMA_B = 9, LOADER = 10;
+
 // ---- dK / dV ---------------------------------------------------------------------------
 
-constexpr int BK = 128;  // keys per CTA
-constexpr int BQ = 64;   // queries per step
+constexpr int BK = 128;  // keys per CTA (TMEM lanes)
+constexpr int BQ = 64;   // queries per block
 
 template <int DH>
 struct KvLayout {
-  static constexpr int QT = BQ * DH * 4;      // [BQ, DH] tile: DH/32 chunks of BQ rows x 128 B
-  static constexpr int KT = BK * DH * 4;      // [BK, DH] tile
-  static constexpr int KL = 0, VL = KT;       // K lo, V lo (smem A operands)
-  static constexpr int KSET = 2 * KT;         // Q hi, Q lo, dO hi, dO lo (K-major)
-  static constexpr int MSET = KSET + 4 * QT;  // Q hi, Q lo, dO hi, dO lo (MN-major)
-  static constexpr int SMEM_BUF = MSET + 4 * QT;
-  static constexpr int SMEM = SMEM_BUF + 1024 + 256 + BQ * 16;
+  static constexpr int QT = BQ * DH * 4;  // [BQ, DH] tile: DH/32 chunks of BQ rows x 128 B
+  static constexpr int KT = BK * DH * 4;  // [BK, DH] tile
+  // K lo, V lo (shared-memory A operands), then hi+lo pairs of Q and dO,
+  // K-major (B of S^T, dP^T) and MN-major (B of dK, dV)
+  static constexpr int KL = 0, VL = KT, QK = 2 * KT, GK = QK + 2 * QT, GM = GK + 2 * QT,
+                       QM = GM + 2 * QT;
+  static constexpr int BARS = QM + 2 * QT;
+  static constexpr int SMEM = BARS + 256 + 1024;
+  // TMEM: K hi, V hi (A operands), dK, dV accumulators, S^T, dP^T, P^T lo,
+  // dS^T lo (P^T hi over S^T, dS^T hi over dP^T)
   static constexpr uint32_t KH = 0, VH = DH, DK = 2 * DH, DV = 3 * DH, ST = 4 * DH,
                             DPT = ST + BQ, PL = ST + 2 * BQ, DSL = ST + 3 * BQ;
   static constexpr uint32_t COLS = 512;
   static_assert(DSL + BQ <= COLS, "TMEM columns");
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
 template <int DH>
 __global__ void __launch_bounds__(THREADS, 1)
-attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kl_map,
+attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
+                      const __grid_constant__ CUtensorMap vh_map,
+                      const __grid_constant__ CUtensorMap kl_map,
                       const __grid_constant__ CUtensorMap vl_map,
                       const __grid_constant__ CUtensorMap qkh_map,
                       const __grid_constant__ CUtensorMap qkl_map,
@@ -148,22 +167,32 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kl_map,
   using L = KvLayout<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::SMEM_BUF);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
-  float* lse_s = reinterpret_cast<float*>(smem + L::SMEM_BUF + 256);  // [BQ]
-  float* dlt_s = lse_s + BQ;                                            // [BQ]
-  int64_t* qp_s = reinterpret_cast<int64_t*>(dlt_s + BQ);               // [BQ]
+  __shared__ __align__(16) float lse_s[2 * BQ], dlt_s[2 * BQ];  // per-block statistics ring
+  __shared__ __align__(16) int64_t qp_s[2 * BQ];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
+  enum {
+    LO_FULL, QK_FULL, QK_EMPTY, GK_FULL, GK_EMPTY, GM_FULL, GM_EMPTY, QM_FULL, QM_EMPTY,
+    SA_DONE, SB_DONE, P_READY, VA_DONE, KB_DONE, D_READY0, D_READY1, ST_FULL0, ST_FULL1, NBARS
+  };
+  const uint32_t bar0 = smem_u32(bars);
+  auto B_ = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, khalf = warp >> 2;
+  const int quarter = warp & 3, khalf = (warp >> 2) & 1;
   const int row = quarter * 32 + lane;
   const int k0 = blockIdx.x * BK, hkv = blockIdx.y, b = blockIdx.z;
   const int G = p.Hq / p.Hkv;
   const int tk = k0 + row;
   const bool valid_k = tk < p.Tk;
-  const uint32_t lobar = smem_u32(bars), kfull = lobar + 8, mfull = lobar + 16, sbar = lobar + 24,
-                 pvbar = lobar + 32;
   if (tid == 0) {
-    for (int i = 0; i < 5; i++) mbar_init(lobar + 8 * i, 1);
+    for (int i = 0; i < NBARS; i++) {
+      const uint32_t n = (i == P_READY || i == D_READY0 || i == D_READY1) ? SOFT
+                         : (i == ST_FULL0 || i == ST_FULL1)               ? 32
+                                                                          : 1;
+      mbar_init(B_(i), n);
+    }
+    *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
   }
@@ -173,6 +202,7 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kl_map,
   // position reaches the first key's, for every query head of the group
   const int64_t* kp = p.kpos + (int64_t)b * p.Tk;
   const int64_t* qp = p.qpos + (int64_t)b * p.Tq;
+  const uint32_t base = smem_u32(smem);
   int q_begin = 0;
   {
     const int64_t first = kp[k0];
@@ -186,193 +216,295 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kl_map,
   const int jb = q_begin / BQ, nqb = (p.Tq + BQ - 1) / BQ;
   const int per_head = q_begin < p.Tq ? nqb - jb : 0;
   const int n_it = G * per_head;
-  const int64_t kpos_row = valid_k ? kp[tk] : INT64_MAX;
-  const bool keys_full = k0 + BK <= p.Tk;
-  const int64_t kpos_last = kp[min(k0 + BK, p.Tk) - 1];
   auto q0_of = [&](int it) { return (jb + it % per_head) * BQ; };
   auto hq_of = [&](int it) { return hkv * G + it / per_head; };
+  if (tid == 0 && n_it > 0) {
+    // the key tile: K, V lo stay in shared memory as A operands; K, V hi pass
+    // through the (still unused) Q/dO buffers on their way to TMEM
+    mbar_expect_tx(B_(LO_FULL), 4 * L::KT);
+    const int r = (int)(((int64_t)b * p.Hkv + hkv) * p.Tk + k0);
+#pragma unroll
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t o = (uint32_t)c * BK * 128u;
+      tma_load_2d(base + L::KL + o, &kl_map, B_(LO_FULL), 32 * c, r);
+      tma_load_2d(base + L::VL + o, &vl_map, B_(LO_FULL), 32 * c, r);
+      tma_load_2d(base + L::QK + o, &kh_map, B_(LO_FULL), 32 * c, r);
+      tma_load_2d(base + L::GK + o, &vh_map, B_(LO_FULL), 32 * c, r);
+    }
+  }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-
-  // producer state (thread 0)
-  bool t0ok = true;
-  int k_loads = 0, k_waits = 0, m_loads = 0, m_waits = 0, s_issued = 0, pv_issued = 0;
-  bool lo_loaded = false, lo_waited = false;
-  const uint32_t base = smem_u32(smem);
-  auto load_set = [&](int it, bool kset) {
-    const uint32_t bar = kset ? kfull : mfull;
-    mbar_expect_tx(bar, 4 * L::QT);
-    const int r = (int)(((int64_t)b * p.Hq + hq_of(it)) * p.Tq + q0_of(it));
-    const uint32_t dst = base + (kset ? L::KSET : L::MSET);
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      const uint32_t o = (uint32_t)c * BQ * 128u;
-      tma_load_2d(dst + o, kset ? &qkh_map : &qmh_map, bar, 32 * c, r);
-      tma_load_2d(dst + L::QT + o, kset ? &qkl_map : &qml_map, bar, 32 * c, r);
-      tma_load_2d(dst + 2 * L::QT + o, kset ? &gkh_map : &gmh_map, bar, 32 * c, r);
-      tma_load_2d(dst + 3 * L::QT + o, kset ? &gkl_map : &gml_map, bar, 32 * c, r);
-    }
-    if (kset) k_loads++; else m_loads++;
-  };
-  if (tid == 0 && n_it > 0) {
-    mbar_expect_tx(lobar, 2 * L::KT);
-    const int r = (int)(((int64_t)b * p.Hkv + hkv) * p.Tk + k0);
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      tma_load_2d(base + L::KL + c * BK * 128, &kl_map, lobar, 32 * c, r);
-      tma_load_2d(base + L::VL + c * BK * 128, &vl_map, lobar, 32 * c, r);
-    }
-    lo_loaded = true;
-    load_set(0, true);
-    load_set(0, false);
-  }
-
   // K hi (warps 0-3) and V hi (warps 4-7) rows -> TMEM
-  {
-    const float* src = (khalf == 0 ? a.kh : a.vh) + (((int64_t)b * p.Hkv + hkv) * p.Tk + tk) * DH;
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++)
-      row_to_tmem(trow + (khalf == 0 ? L::KH : L::VH) + 32 * c, src + 32 * c, valid_k);
-    tmem_wait_st();
+  if (warp < 8 && n_it > 0) {
+    const bool ok = mbar_wait(B_(LO_FULL), 0u, a.error);
+    if (!ok) *abort = 1;
+    if (__all_sync(0xffffffffu, ok)) {
+      const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+      tile_row_to_tmem<DH>(base + (khalf == 0 ? L::QK : L::GK), row, trow,
+                           khalf == 0 ? L::KH : L::VH);
+      tmem_wait_st();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  tc_fence_after();
 
-  const float c2 = p.scale * kLog2e;
-  constexpr uint32_t idesc_s = idesc_tf32_m128(BQ, 0);
-  constexpr uint32_t idesc_o = idesc_tf32_m128(DH, 1);
-  bool ok = true;
-  for (int it = 0; ok && it < n_it; it++) {
-    const int q0 = q0_of(it), hq = hq_of(it);
-    if (tid == 0 && t0ok) {
-      if (!lo_waited) {
-        t0ok = mbar_wait(lobar, 0u, a.error);
-        lo_waited = true;
-      }
-      if (t0ok) t0ok = mbar_wait(kfull, (uint32_t)(k_waits & 1), a.error);
-      k_waits++;
-      if (t0ok) {
-        tc_fence_after();
-        const uint32_t qkh = base + L::KSET, qkl = qkh + L::QT, gkh = qkh + 2 * L::QT,
-                       gkl = qkh + 3 * L::QT, klo = base + L::KL, vlo = base + L::VL;
+  if (warp == LOADER) {
+    // ---- producer: operand pairs by TMA, per-block statistics by the lanes
+    bool ok = true;
+    auto load_pair = [&](int full, const CUtensorMap* hm, const CUtensorMap* lm, int off, int r) {
+      mbar_expect_tx(B_(full), 2 * L::QT);
 #pragma unroll
-        for (int j = 0; j < DH / 8; j++) {
-          const uint32_t acc = j > 0 ? 1u : 0u;
-          umma_tf32_ts(tmem + L::ST, tmem + L::KH + 8 * j, kmajor_desc(qkh, BQ, j), idesc_s, acc);
-          umma_tf32_ts(tmem + L::ST, tmem + L::KH + 8 * j, kmajor_desc(qkl, BQ, j), idesc_s, 1u);
-          umma_tf32(tmem + L::ST, kmajor_desc(klo, BK, j), kmajor_desc(qkh, BQ, j), idesc_s, 1u);
-          umma_tf32_ts(tmem + L::DPT, tmem + L::VH + 8 * j, kmajor_desc(gkh, BQ, j), idesc_s, acc);
-          umma_tf32_ts(tmem + L::DPT, tmem + L::VH + 8 * j, kmajor_desc(gkl, BQ, j), idesc_s, 1u);
-          umma_tf32(tmem + L::DPT, kmajor_desc(vlo, BK, j), kmajor_desc(gkh, BQ, j), idesc_s, 1u);
+      for (int c = 0; c < DH / 32; c++) {
+        const uint32_t o = (uint32_t)c * BQ * 128u;
+        tma_load_2d(base + off + o, hm, B_(full), 32 * c, r);
+        tma_load_2d(base + off + L::QT + o, lm, B_(full), 32 * c, r);
+      }
+    };
+    int nqk = 0, ngk = 0, ngm = 0, nqm = 0;  // pairs issued per buffer (lane 0)
+    for (int j = 0; ok && j < n_it; j++) {
+      const int q0 = q0_of(j), hq = hq_of(j);
+      const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
+      const uint32_t prev = (uint32_t)((j - 1) & 1);
+      if (lane == 0) {
+        if (j > 0) ok = role_wait(B_(QK_EMPTY), prev, a.error, abort);
+        if (ok) { load_pair(QK_FULL, &qkh_map, &qkl_map, L::QK, r); nqk++; }
+        if (ok && j > 0) ok = role_wait(B_(GK_EMPTY), prev, a.error, abort);
+        if (ok) { load_pair(GK_FULL, &gkh_map, &gkl_map, L::GK, r); ngk++; }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      // statistics of block j into ring slot j&1, free once block j-2's
+      // gradients are done
+      if (ok && j >= 2) ok = role_wait(B_(D_READY0 + (j & 1)), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+#pragma unroll
+        for (int h = 0; h < BQ / 32; h++) {
+          const int q = q0 + 32 * h + lane, si = (j & 1) * BQ + 32 * h + lane;
+          const int64_t rr = ((int64_t)b * p.Hq + hq) * p.Tq + q;
+          lse_s[si] = q < p.Tq ? a.lse2[rr] : INFINITY;
+          dlt_s[si] = q < p.Tq ? a.delta[rr] : 0.0f;
+          qp_s[si] = q < p.Tq ? qp[q] : INT64_MAX;  // keeps the block's positions ascending
         }
-        umma_commit(sbar);
+        mbar_arrive(B_(ST_FULL0 + (j & 1)));
+      }
+      if (ok && lane == 0) {
+        if (j > 0) ok = role_wait(B_(GM_EMPTY), prev, a.error, abort);
+        if (ok) { load_pair(GM_FULL, &gmh_map, &gml_map, L::GM, r); ngm++; }
+        if (ok && j > 0) ok = role_wait(B_(QM_EMPTY), prev, a.error, abort);
+        if (ok) { load_pair(QM_FULL, &qmh_map, &qml_map, L::QM, r); nqm++; }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (lane == 0 && n_it > 0) {
+      // every copy has landed before the CTA releases its memory (on the
+      // normal path these phases completed long ago)
+      mbar_wait(B_(LO_FULL), 0u, a.error);
+      if (nqk > 0) mbar_wait(B_(QK_FULL), (uint32_t)((nqk - 1) & 1), a.error);
+      if (ngk > 0) mbar_wait(B_(GK_FULL), (uint32_t)((ngk - 1) & 1), a.error);
+      if (ngm > 0) mbar_wait(B_(GM_FULL), (uint32_t)((ngm - 1) & 1), a.error);
+      if (nqm > 0) mbar_wait(B_(QM_FULL), (uint32_t)((nqm - 1) & 1), a.error);
+    }
+  } else if (warp == MMA_A || warp == MMA_B) {
+    // ---- MMA chains.  A: S^T = K Q^T, dV += P^T dO.  B: dP^T = V dO^T, dK += dS^T Q.
+    const bool is_a = warp == MMA_A;
+    if (lane == 0 && n_it > 0) {
+      constexpr uint32_t idesc_s = idesc_tf32_m128(BQ, 0);
+      constexpr uint32_t idesc_o = idesc_tf32_m128(DH, 1);
+      const uint32_t xh = is_a ? L::KH : L::VH;                 // TMEM A operand (hi)
+      const uint64_t xlo = kmajor_desc(base + (is_a ? L::KL : L::VL), BK, 0);
+      const uint64_t bk_h = kmajor_desc(base + (is_a ? L::QK : L::GK), BQ, 0);
+      const uint64_t bk_l = kmajor_desc(base + (is_a ? L::QK : L::GK) + L::QT, BQ, 0);
+      const uint64_t bm_h = mnmajor_desc(base + (is_a ? L::GM : L::QM), BQ, 0);
+      const uint64_t bm_l = mnmajor_desc(base + (is_a ? L::GM : L::QM) + L::QT, BQ, 0);
+      const uint32_t sd = tmem + (is_a ? L::ST : L::DPT);       // score accumulator; hi operand after
+      const uint32_t lo_op = tmem + (is_a ? L::PL : L::DSL);    // lo operand
+      const uint32_t acc_d = tmem + (is_a ? L::DV : L::DK);
+      const int kfull = is_a ? QK_FULL : GK_FULL, kempty = is_a ? QK_EMPTY : GK_EMPTY;
+      const int mfull = is_a ? GM_FULL : QM_FULL, mempty = is_a ? GM_EMPTY : QM_EMPTY;
+      const int sdone = is_a ? SA_DONE : SB_DONE, gdone = is_a ? VA_DONE : KB_DONE;
+      int s_issued = 0, g_issued = 0;
+      bool ok = role_wait(B_(LO_FULL), 0u, a.error, abort);
+      for (int j = 0; ok && j < n_it; j++) {
+        const uint32_t par = (uint32_t)(j & 1);
+        ok = role_wait(B_(kfull), par, a.error, abort);
+        // the score columns are free once the previous block's gradient MMAs read them
+        if (ok && j > 0) ok = role_wait(B_(gdone), (uint32_t)((j - 1) & 1), a.error, abort);
+        // dP^T waits for S^T: S^T then has the tensor core to itself, and
+        // dP^T runs while the SM turns S^T into P^T.  S^T of the next block
+        // waits for dP^T of this one, which keeps both chains within one
+        // phase of these two barriers.
+        if (ok && !is_a) ok = role_wait(B_(SA_DONE), par, a.error, abort);
+        if (ok && is_a && j > 0) ok = role_wait(B_(SB_DONE), (uint32_t)((j - 1) & 1), a.error, abort);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < DH / 8; k++) {
+          const uint32_t acc = k > 0 ? 1u : 0u;
+          umma_tf32_ts(sd, tmem + xh + 8 * k, kslice<BQ>(bk_h, k), idesc_s, acc);
+          umma_tf32_ts(sd, tmem + xh + 8 * k, kslice<BQ>(bk_l, k), idesc_s, 1u);
+          umma_tf32(sd, kslice<BK>(xlo, k), kslice<BQ>(bk_h, k), idesc_s, 1u);
+        }
+        umma_commit(B_(sdone));
+        umma_commit(B_(kempty));
         s_issued++;
-      }
-    }
-    // statistics of this query block (their previous readers passed the
-    // barrier that ended the last iteration)
-    if (tid < BQ) {
-      const int q = q0 + tid;
-      const int64_t r = ((int64_t)b * p.Hq + hq) * p.Tq + q;
-      lse_s[tid] = q < p.Tq ? a.lse2[r] : INFINITY;
-      dlt_s[tid] = q < p.Tq ? a.delta[r] : 0.0f;
-      qp_s[tid] = q < p.Tq ? qp[q] : INT64_MIN;
-    }
-    const bool full_block =
-        p.mask == nullptr && keys_full && q0 + BQ <= p.Tq && qp[q0] >= kpos_last;
-    bool good = mbar_wait(sbar, (uint32_t)(it & 1), a.error);
-    good = __all_sync(0xffffffffu, good) && (tid != 0 || t0ok);
-    if (__syncthreads_or(!good)) { ok = false; break; }
-    tc_fence_after();
-    if (tid == 0 && it + 1 < n_it) load_set(it + 1, true);  // S^T and dP^T consumed the K-major set
-    float st[32], dpt[32];
-    tmem_ld32(trow + L::ST + 32 * khalf, st);
-    tmem_ld32(trow + L::DPT + 32 * khalf, dpt);
-    float ph[32], pl[32], dh[32], dl[32];
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      const int c = 32 * khalf + i;
-      bool adm = full_block;
-      if (!full_block) {
-        adm = kpos_row <= qp_s[c];
-        if (adm && p.mask != nullptr)
-          adm = p.mask[((int64_t)b * p.Tq + q0 + c) * p.Tk + tk] != 0;
-      }
-      const float pv = adm ? ex2(st[i] * c2 - lse_s[c]) : 0.0f;
-      const float ds = pv * (dpt[i] - dlt_s[c]);
-      ph[i] = tf32_round(pv);
-      pl[i] = pv - ph[i];
-      dh[i] = tf32_hi(ds);
-      dl[i] = ds - dh[i];
-    }
-    tmem_st32(trow + L::ST + 32 * khalf, ph);
-    tmem_st32(trow + L::PL + 32 * khalf, pl);
-    tmem_st32(trow + L::DPT + 32 * khalf, dh);
-    tmem_st32(trow + L::DSL + 32 * khalf, dl);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && t0ok) {
-      t0ok = mbar_wait(mfull, (uint32_t)(m_waits & 1), a.error);
-      m_waits++;
-      if (t0ok) {
+        ok = role_wait(B_(is_a ? P_READY : D_READY0 + (j & 1)), is_a ? par : (uint32_t)((j >> 1) & 1),
+                       a.error, abort);
+        if (ok) ok = role_wait(B_(mfull), par, a.error, abort);
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t qmh = base + L::MSET, qml = qmh + L::QT, gmh = qmh + 2 * L::QT,
-                       gml = qmh + 3 * L::QT;
 #pragma unroll
-        for (int j = 0; j < BQ / 8; j++) {
-          const uint32_t acc = (it > 0 || j > 0) ? 1u : 0u;
-          umma_tf32_ts(tmem + L::DV, tmem + L::ST + 8 * j, mnmajor_desc(gmh, BQ, j), idesc_o, acc);
-          umma_tf32_ts(tmem + L::DV, tmem + L::ST + 8 * j, mnmajor_desc(gml, BQ, j), idesc_o, 1u);
-          umma_tf32_ts(tmem + L::DV, tmem + L::PL + 8 * j, mnmajor_desc(gmh, BQ, j), idesc_o, 1u);
-          umma_tf32_ts(tmem + L::DK, tmem + L::DPT + 8 * j, mnmajor_desc(qmh, BQ, j), idesc_o, acc);
-          umma_tf32_ts(tmem + L::DK, tmem + L::DPT + 8 * j, mnmajor_desc(qml, BQ, j), idesc_o, 1u);
-          umma_tf32_ts(tmem + L::DK, tmem + L::DSL + 8 * j, mnmajor_desc(qmh, BQ, j), idesc_o, 1u);
+        for (int k = 0; k < BQ / 8; k++) {
+          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          umma_tf32_ts(acc_d, sd + 8 * k, mslice(bm_h, k), idesc_o, acc);
+          umma_tf32_ts(acc_d, sd + 8 * k, mslice(bm_l, k), idesc_o, 1u);
+          umma_tf32_ts(acc_d, lo_op + 8 * k, mslice(bm_h, k), idesc_o, 1u);
         }
-        umma_commit(pvbar);
-        pv_issued++;
-        // S^T / dP^T of the next block overwrite what these MMAs read
-        t0ok = mbar_wait(pvbar, (uint32_t)(it & 1), a.error);
-        if (t0ok && it + 1 < n_it) load_set(it + 1, false);
+        umma_commit(B_(gdone));
+        umma_commit(B_(mempty));
+        g_issued++;
+      }
+      // committed MMAs finish before TMEM and shared memory are released
+      if (s_issued > 0) {
+        mbar_wait(B_(sdone), (uint32_t)((s_issued - 1) & 1), a.error);
+        mbar_wait(B_(kempty), (uint32_t)((s_issued - 1) & 1), a.error);
+      }
+      if (g_issued > 0) {
+        mbar_wait(B_(gdone), (uint32_t)((g_issued - 1) & 1), a.error);
+        mbar_wait(B_(mempty), (uint32_t)((g_issued - 1) & 1), a.error);
       }
     }
-  }
-  if (ok && n_it > 0) {
-    bool good = mbar_wait(pvbar, (uint32_t)((n_it - 1) & 1), a.error);
-    good = good && (tid != 0 || t0ok);
-    if (__syncthreads_or(!good)) ok = false;
-    tc_fence_after();
-  }
-
-  if (ok) {
-    // warps 0-3: dK (scale, RoPE backward); warps 4-7: dV
-    const AttnOut& out = khalf == 0 ? dk : dv;
-    float* orow = out.ptr + b * out.sb + hkv * out.sh + (int64_t)tk * out.st;
-    const float* ct = khalf == 0 ? p.k_cos : nullptr;
-    const float* sn = khalf == 0 ? p.k_sin : nullptr;
-    const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + tk : tk) * (DH / 2);
+  } else {
+    // ---- P^T = 2^(S^T scale log2(e) - lse2), then dS^T = P^T (dP^T - delta)
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int64_t kpos_row = valid_k ? kp[tk] : INT64_MAX;
+    const bool keys_full = k0 + BK <= p.Tk;
+    const int64_t kpos_last = kp[min(k0 + BK, p.Tk) - 1];
+    const float c2 = p.scale * kLog2e;
+    const int cb = 32 * khalf;  // this thread's first column of the block
+    bool ok = true;
+    for (int j = 0; ok && j < n_it; j++) {
+      const int s = j & 1;
+      const uint32_t par = (uint32_t)(j & 1), spar = (uint32_t)((j >> 1) & 1);
+      const int q0 = q0_of(j);
+      uint8_t keep[32];
+      if (p.mask != nullptr) {  // issued ahead of the waits; clamped indices stay in bounds
+        const int tkc = min(tk, p.Tk - 1);
 #pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      float v[32];
-      if (n_it > 0) {
-        tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = 0.0f;
+        for (int i = 0; i < 32; i++) {
+          const int q = min(q0 + cb + i, p.Tq - 1);
+          keep[i] = p.mask[((int64_t)b * p.Tq + q) * p.Tk + tkc];
+        }
       }
-      if (valid_k)
-        store_grad_row<32>(v, 0, orow + 32 * c, khalf == 0 ? p.scale : 1.0f, ct, sn, trw, 32 * c);
+      ok = role_wait(B_(ST_FULL0 + s), spar, a.error, abort);
+      if (ok) ok = role_wait(B_(SA_DONE), par, a.error, abort);
+      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld/st are warp-collective
+      if (!ok) break;
+      tc_fence_after();
+      const bool full_block =
+          p.mask == nullptr && keys_full && q0 + BQ <= p.Tq && qp_s[s * BQ] >= kpos_last;
+      float pv[32];
+      {
+        float sv[32], hi[32], lo[32];
+        tmem_ld32(trow + L::ST + cb, sv);
+        const float4* l4 = reinterpret_cast<const float4*>(lse_s + s * BQ + cb);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float4 v = l4[i];
+          hi[4 * i] = v.x; hi[4 * i + 1] = v.y; hi[4 * i + 2] = v.z; hi[4 * i + 3] = v.w;
+        }
+        if (full_block) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) pv[i] = ex2(fmaf(sv[i], c2, -hi[i]));
+        } else {
+          // queries of the block see this key from the first whose position
+          // reaches it, up to the last query of the sequence
+          const int first = count_below(qp_s + s * BQ, BQ, kpos_row) - cb;
+          const int last = p.Tq - q0 - cb;
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            bool adm = i >= first && i < last;
+            if (p.mask != nullptr) adm = adm && keep[i] != 0;
+            pv[i] = adm ? ex2(fmaf(sv[i], c2, -hi[i])) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          hi[i] = tf32_round(pv[i]);
+          lo[i] = pv[i] - hi[i];
+        }
+        tmem_st32(trow + L::ST + cb, hi);
+        tmem_st32(trow + L::PL + cb, lo);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(B_(P_READY));
+      }
+      ok = role_wait(B_(SB_DONE), par, a.error, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      {
+        float dp[32], hi[32], lo[32];
+        tmem_ld32(trow + L::DPT + cb, dp);
+        const float4* d4 = reinterpret_cast<const float4*>(dlt_s + s * BQ + cb);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float4 v = d4[i];
+          lo[4 * i] = v.x; lo[4 * i + 1] = v.y; lo[4 * i + 2] = v.z; lo[4 * i + 3] = v.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const float ds = pv[i] * (dp[i] - lo[i]);
+          hi[i] = tf32_hi(ds);
+          lo[i] = ds - hi[i];
+        }
+        tmem_st32(trow + L::DPT + cb, hi);
+        tmem_st32(trow + L::DSL + cb, lo);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(B_(D_READY0 + s));
+      }
     }
-  } else if (tid == 0) {
-    if (lo_loaded && !lo_waited) mbar_wait(lobar, 0u, a.error);
-    for (int k = k_waits; k < k_loads; k++) mbar_wait(kfull, (uint32_t)(k & 1), a.error);
-    for (int k = m_waits; k < m_loads; k++) mbar_wait(mfull, (uint32_t)(k & 1), a.error);
-    if (s_issued > 0) mbar_wait(sbar, (uint32_t)((s_issued - 1) & 1), a.error);
-    if (pv_issued > 0) mbar_wait(pvbar, (uint32_t)((pv_issued - 1) & 1), a.error);
+    if (ok && n_it > 0) {
+      const uint32_t last = (uint32_t)((n_it - 1) & 1);
+      ok = role_wait(B_(VA_DONE), last, a.error, abort);
+      if (ok) ok = role_wait(B_(KB_DONE), last, a.error, abort);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    // warps 0-3: dK (scale, RoPE backward), warps 4-7: dV, staged in the
+    // free operand buffers and written out with coalesced stores
+    const uint32_t stage = base + L::QK + (uint32_t)(khalf * 128 * (DH + 4) * 4);
+    if (ok) {
+      tc_fence_after();
+      const float* ct = khalf == 0 ? p.k_cos : nullptr;
+      const float* sn = khalf == 0 ? p.k_sin : nullptr;
+      const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + tk : tk) * (DH / 2);
+#pragma unroll
+      for (int c = 0; c < DH / 32; c++) {
+        float v[32];
+        if (n_it > 0) {
+          tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = 0.0f;
+        }
+        grad_row<32>(v, 0, khalf == 0 ? p.scale : 1.0f, ct, sn, trw, 32 * c);
+        stage_row32(stage, DH, row, 32 * c, v, 0, 32);
+      }
+    }
+    named_sync(1, SOFT);
+    if (ok) {
+      const int rows = min(BK, p.Tk - k0);
+      for (int t = 0; t < 2; t++) {
+        const AttnOut& out = t == 0 ? dk : dv;
+        store_staged_rows(base + L::QK + (uint32_t)(t * 128 * (DH + 4) * 4), DH, rows,
+                          out.ptr + b * out.sb + hkv * out.sh + (int64_t)k0 * out.st, out.st, tid,
+                          SOFT);
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -384,25 +516,33 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kl_map,
 
 // ---- dQ ----------------------------------------------------------------------------------
 
-constexpr int QM = 128;  // queries per CTA
-constexpr int KN = 64;   // keys per step
+constexpr int QM = 128;  // queries per CTA (TMEM lanes)
+constexpr int KN = 64;   // keys per block
 
 template <int DH>
 struct QLayout {
-  static constexpr int KT = KN * DH * 4;  // one [KN, DH] tile
-  static constexpr int STAGE = 6 * KT;    // K hi/lo, V hi/lo (K-major), K hi/lo (MN-major)
-  static constexpr int NBUF = 2;
-  static constexpr int SMEM_BUF = NBUF * STAGE;
-  static constexpr int SMEM = SMEM_BUF + 1024 + 256 + KN * 8;
+  static constexpr int KT = KN * DH * 4;  // [KN, DH] tile: DH/32 chunks of KN rows x 128 B
+  static constexpr int STAGE = 6 * KT;    // K hi/lo, V hi/lo (K-major); K hi/lo (MN-major)
+  static constexpr int NS = 2;
+  static constexpr int KPOS = NS * STAGE;  // [2][KN] key positions
+  static constexpr int BARS = KPOS + 2 * KN * 8;
+  static constexpr int SMEM = BARS + 256 + 1024;
+  // TMEM: Q hi, Q lo, dO hi, dO lo (A operands); S, dP (dS hi over S, dS lo
+  // over dP); dQ in two accumulators (hi and lo chains), summed at the end
   static constexpr uint32_t QH = 0, QL = DH, GH = 2 * DH, GL = 3 * DH, S = 4 * DH, DP = S + KN,
-                            DQ = DP + KN;
-  static constexpr uint32_t COLS = DQ + DH <= 256 ? 256 : 512;
-  static_assert(DQ + DH <= 512, "TMEM columns");
+                            DQA = DP + KN, DQB = DQA + DH;
+  static constexpr uint32_t COLS = DQB + DH <= 256 ? 256 : 512;
+  static_assert(DQB + DH <= 512, "TMEM columns");
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
 template <int DH>
 __global__ void __launch_bounds__(THREADS, 1)
-attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap kkh_map,
+attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
+                     const __grid_constant__ CUtensorMap ql_map,
+                     const __grid_constant__ CUtensorMap gh_map,
+                     const __grid_constant__ CUtensorMap gl_map,
+                     const __grid_constant__ CUtensorMap kkh_map,
                      const __grid_constant__ CUtensorMap kkl_map,
                      const __grid_constant__ CUtensorMap vkh_map,
                      const __grid_constant__ CUtensorMap vkl_map,
@@ -412,19 +552,31 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap kkh_map,
   using L = QLayout<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::SMEM_BUF);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + L::NBUF + 2);
-  int64_t* kpos_s = reinterpret_cast<int64_t*>(smem + L::SMEM_BUF + 256);  // [KN]
+  int64_t* kpos_s = reinterpret_cast<int64_t*>(smem + L::KPOS);  // [2][KN]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
+  enum {
+    FULL0, FULL1, EMPTYA0, EMPTYA1, EMPTYB0, EMPTYB1, SA_DONE, SB_DONE, DS_READY0, DS_READY1,
+    QA_DONE, QB_DONE, KP_FULL0, KP_FULL1, ROWS_FULL, NBARS
+  };
+  const uint32_t bar0 = smem_u32(bars);
+  auto B_ = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, khalf = warp >> 2;
+  const int quarter = warp & 3, khalf = (warp >> 2) & 1;
   const int row = quarter * 32 + lane;
   const int q0 = blockIdx.x * QM, hq = blockIdx.y, b = blockIdx.z;
   const int hkv = hq / (p.Hq / p.Hkv);
   const int tq = q0 + row;
   const bool valid_q = tq < p.Tq;
-  const uint32_t full0 = smem_u32(bars), sbar = full0 + 8 * L::NBUF, pvbar = sbar + 8;
   if (tid == 0) {
-    for (int i = 0; i < L::NBUF + 2; i++) mbar_init(full0 + 8 * i, 1);
+    for (int i = 0; i < NBARS; i++) {
+      const uint32_t n = (i == DS_READY0 || i == DS_READY1) ? SOFT
+                         : (i == KP_FULL0 || i == KP_FULL1) ? 32
+                                                            : 1;
+      mbar_init(B_(i), n);
+    }
+    *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
   }
@@ -449,175 +601,236 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap kkh_map,
     }
     full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? lo2 / KN : 0;
   }
-  auto load_kpos = [&](int kb) {
-    if (kb < nkb && kb >= full_kb && tid < KN) {
-      const int t = kb * KN + tid;
-      kpos_s[tid] = t < p.Tk ? p.kpos[(int64_t)b * p.Tk + t] : INT64_MAX;
+  const uint32_t base = smem_u32(smem);
+  constexpr uint32_t RT = QM * DH * 4;  // one [128, DH] row tile
+  if (tid == 0) {
+    // Q and dO hi/lo rows pass through the (still unused) K/V stages on their way to TMEM
+    mbar_expect_tx(B_(ROWS_FULL), 4 * RT);
+    const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
+#pragma unroll
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t o = (uint32_t)c * QM * 128u;
+      tma_load_2d(base + o, &qh_map, B_(ROWS_FULL), 32 * c, r);
+      tma_load_2d(base + RT + o, &ql_map, B_(ROWS_FULL), 32 * c, r);
+      tma_load_2d(base + 2 * RT + o, &gh_map, B_(ROWS_FULL), 32 * c, r);
+      tma_load_2d(base + 3 * RT + o, &gl_map, B_(ROWS_FULL), 32 * c, r);
     }
-  };
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-
-  bool t0ok = true;
-  int next_load = 0, waits = 0, s_issued = 0, pv_issued = 0;
-  const uint32_t base = smem_u32(smem);
-  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
-  auto stage_addr = [&](int kb) { return base + (uint32_t)((kb % L::NBUF) * L::STAGE); };
-  auto issue_load = [&]() {
-    const int kb = next_load++;
-    const uint32_t bar = full0 + 8 * (kb % L::NBUF);
-    mbar_expect_tx(bar, L::STAGE);
-    const int r = (int)(kv_row0 + (int64_t)kb * KN);
-    const uint32_t dst = stage_addr(kb);
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      const uint32_t o = (uint32_t)c * KN * 128u;
-      tma_load_2d(dst + o, &kkh_map, bar, 32 * c, r);
-      tma_load_2d(dst + L::KT + o, &kkl_map, bar, 32 * c, r);
-      tma_load_2d(dst + 2 * L::KT + o, &vkh_map, bar, 32 * c, r);
-      tma_load_2d(dst + 3 * L::KT + o, &vkl_map, bar, 32 * c, r);
-      tma_load_2d(dst + 4 * L::KT + o, &kmh_map, bar, 32 * c, r);
-      tma_load_2d(dst + 5 * L::KT + o, &kml_map, bar, 32 * c, r);
+  // Q hi/lo and dO hi/lo rows -> TMEM (warps 0-3 hi, 4-7 lo)
+  if (warp < 8) {
+    const bool ok = mbar_wait(B_(ROWS_FULL), 0u, a.error);
+    if (!ok) *abort = 1;
+    if (__all_sync(0xffffffffu, ok)) {
+      const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+      tile_row_to_tmem<DH>(base + (uint32_t)khalf * RT, row, trow, khalf == 0 ? L::QH : L::QL);
+      tile_row_to_tmem<DH>(base + (uint32_t)(2 + khalf) * RT, row, trow,
+                           khalf == 0 ? L::GH : L::GL);
+      tmem_wait_st();
     }
-  };
-  if (tid == 0)
-    while (next_load < L::NBUF && next_load < nkb) issue_load();
-
-  // Q hi/lo and dO hi/lo rows -> TMEM
-  {
-    const int64_t off = (((int64_t)b * p.Hq + hq) * p.Tq + tq) * DH;
-    const float* s1 = (khalf == 0 ? a.qh : a.ql) + off;
-    const float* s2 = (khalf == 0 ? a.doh : a.dol) + off;
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      row_to_tmem(trow + (khalf == 0 ? L::QH : L::QL) + 32 * c, s1 + 32 * c, valid_q);
-      row_to_tmem(trow + (khalf == 0 ? L::GH : L::GL) + 32 * c, s2 + 32 * c, valid_q);
-    }
-    tmem_wait_st();
   }
-  const int64_t ri = ((int64_t)b * p.Hq + hq) * p.Tq + tq;
-  const float lse_row = valid_q ? a.lse2[ri] : INFINITY;
-  const float dlt_row = valid_q ? a.delta[ri] : 0.0f;
-  const int64_t qpos_row = valid_q ? p.qpos[(int64_t)b * p.Tq + tq] : -1;
   tc_fence_before();
   __syncthreads();
+  tc_fence_after();
 
-  const float c2 = p.scale * kLog2e;
-  constexpr uint32_t idesc_s = idesc_tf32_m128(KN, 0);
-  constexpr uint32_t idesc_q = idesc_tf32_m128(DH, 1);
-  bool ok = true;
-  for (int kb = 0; ok && kb < nkb; kb++) {
-    const bool full_block = kb < full_kb;
-    if (tid == 0 && t0ok) {
-      const int k = waits++;
-      t0ok = mbar_wait(full0 + 8 * (k % L::NBUF), (uint32_t)((k / L::NBUF) & 1), a.error);
-      if (t0ok) {
-        tc_fence_after();
-        const uint32_t kkh = stage_addr(kb), kkl = kkh + L::KT, vkh = kkh + 2 * L::KT,
-                       vkl = kkh + 3 * L::KT;
-#pragma unroll
-        for (int j = 0; j < DH / 8; j++) {
-          const uint32_t acc = j > 0 ? 1u : 0u;
-          umma_tf32_ts(tmem + L::S, tmem + L::QH + 8 * j, kmajor_desc(kkh, KN, j), idesc_s, acc);
-          umma_tf32_ts(tmem + L::S, tmem + L::QH + 8 * j, kmajor_desc(kkl, KN, j), idesc_s, 1u);
-          umma_tf32_ts(tmem + L::S, tmem + L::QL + 8 * j, kmajor_desc(kkh, KN, j), idesc_s, 1u);
-          umma_tf32_ts(tmem + L::DP, tmem + L::GH + 8 * j, kmajor_desc(vkh, KN, j), idesc_s, acc);
-          umma_tf32_ts(tmem + L::DP, tmem + L::GH + 8 * j, kmajor_desc(vkl, KN, j), idesc_s, 1u);
-          umma_tf32_ts(tmem + L::DP, tmem + L::GL + 8 * j, kmajor_desc(vkh, KN, j), idesc_s, 1u);
+  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
+  if (warp == LOADER) {
+    // ---- producer: K/V stages by TMA, key positions by the lanes
+    int loads = 0;
+    bool ok = true;
+    for (int j = 0; ok && j < nkb; j++) {
+      const int s = j & 1;
+      if (lane == 0) {
+        if (j >= 2) {
+          const uint32_t par = (uint32_t)(((j >> 1) - 1) & 1);
+          ok = role_wait(B_(EMPTYA0 + s), par, a.error, abort);
+          if (ok) ok = role_wait(B_(EMPTYB0 + s), par, a.error, abort);
         }
-        umma_commit(sbar);
+        if (ok) {
+          const uint32_t bar = B_(FULL0 + s), dst = base + s * L::STAGE;
+          const int r = (int)(kv_row0 + (int64_t)j * KN);
+          mbar_expect_tx(bar, L::STAGE);
+#pragma unroll
+          for (int c = 0; c < DH / 32; c++) {
+            const uint32_t o = (uint32_t)c * KN * 128u;
+            tma_load_2d(dst + o, &kkh_map, bar, 32 * c, r);
+            tma_load_2d(dst + L::KT + o, &kkl_map, bar, 32 * c, r);
+            tma_load_2d(dst + 2 * L::KT + o, &vkh_map, bar, 32 * c, r);
+            tma_load_2d(dst + 3 * L::KT + o, &vkl_map, bar, 32 * c, r);
+            tma_load_2d(dst + 4 * L::KT + o, &kmh_map, bar, 32 * c, r);
+            tma_load_2d(dst + 5 * L::KT + o, &kml_map, bar, 32 * c, r);
+          }
+          loads++;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok && j >= 2) ok = role_wait(B_(DS_READY0 + s), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+#pragma unroll
+        for (int h = 0; h < KN / 32; h++) {
+          const int t = j * KN + 32 * h + lane;
+          kpos_s[s * KN + 32 * h + lane] = t < p.Tk ? p.kpos[(int64_t)b * p.Tk + t] : INT64_MAX;
+        }
+        mbar_arrive(B_(KP_FULL0 + s));
+      }
+    }
+    if (lane == 0) {  // every copy has landed before the CTA releases its memory
+      for (int j = loads - 2 < 0 ? 0 : loads - 2; j < loads; j++)
+        mbar_wait(B_(FULL0 + (j & 1)), (uint32_t)((j >> 1) & 1), a.error);
+    }
+  } else if (warp == MMA_A || warp == MMA_B) {
+    // ---- MMA chains.  A: S = Q K^T, dQa += dS_hi K.  B: dP = dO V^T, dQb += dS_lo K_hi.
+    const bool is_a = warp == MMA_A;
+    if (lane == 0 && nkb > 0) {
+      constexpr uint32_t idesc_s = idesc_tf32_m128(KN, 0);
+      constexpr uint32_t idesc_q = idesc_tf32_m128(DH, 1);
+      const uint32_t xh = tmem + (is_a ? L::QH : L::GH), xl = tmem + (is_a ? L::QL : L::GL);
+      const uint32_t sd = tmem + (is_a ? L::S : L::DP);
+      const uint32_t dqd = tmem + (is_a ? L::DQA : L::DQB);
+      const int sdone = is_a ? SA_DONE : SB_DONE, qdone = is_a ? QA_DONE : QB_DONE;
+      const int empty0 = is_a ? EMPTYA0 : EMPTYB0;
+      int s_issued = 0, q_issued = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < nkb; j++) {
+        const int s = j & 1;
+        ok = role_wait(B_(FULL0 + s), (uint32_t)((j >> 1) & 1), a.error, abort);
+        if (ok && j > 0) ok = role_wait(B_(qdone), (uint32_t)((j - 1) & 1), a.error, abort);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t stg = base + s * L::STAGE;
+        const uint64_t bh = kmajor_desc(stg + (is_a ? 0 : 2 * L::KT), KN, 0);
+        const uint64_t bl = kmajor_desc(stg + (is_a ? L::KT : 3 * L::KT), KN, 0);
+#pragma unroll
+        for (int k = 0; k < DH / 8; k++) {
+          const uint32_t acc = k > 0 ? 1u : 0u;
+          umma_tf32_ts(sd, xh + 8 * k, kslice<KN>(bh, k), idesc_s, acc);
+          umma_tf32_ts(sd, xh + 8 * k, kslice<KN>(bl, k), idesc_s, 1u);
+          umma_tf32_ts(sd, xl + 8 * k, kslice<KN>(bh, k), idesc_s, 1u);
+        }
+        umma_commit(B_(sdone));
         s_issued++;
-      }
-    }
-    load_kpos(kb);  // the previous block's readers passed the last barrier
-    bool good = mbar_wait(sbar, (uint32_t)(kb & 1), a.error);
-    good = __all_sync(0xffffffffu, good) && (tid != 0 || t0ok);
-    if (__syncthreads_or(!good)) { ok = false; break; }
-    tc_fence_after();
-    float s[32], dp[32];
-    tmem_ld32(trow + L::S + 32 * khalf, s);
-    tmem_ld32(trow + L::DP + 32 * khalf, dp);
-    float dh[32], dl[32];
+        ok = role_wait(B_(DS_READY0 + s), (uint32_t)((j >> 1) & 1), a.error, abort);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t kmh = mnmajor_desc(stg + 4 * L::KT, KN, 0);
+        const uint64_t kml = mnmajor_desc(stg + 5 * L::KT, KN, 0);
 #pragma unroll
-    for (int i = 0; i < 32; i++) {
-      const int k = 32 * khalf + i;
-      bool adm = full_block;
-      if (!full_block) {
-        adm = valid_q && kpos_s[k] <= qpos_row;
-        if (adm && p.mask != nullptr)
-          adm = p.mask[((int64_t)b * p.Tq + tq) * p.Tk + kb * KN + k] != 0;
+        for (int k = 0; k < KN / 8; k++) {
+          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          umma_tf32_ts(dqd, sd + 8 * k, mslice(kmh, k), idesc_q, acc);
+          if (is_a) umma_tf32_ts(dqd, sd + 8 * k, mslice(kml, k), idesc_q, 1u);
+        }
+        umma_commit(B_(qdone));
+        umma_commit(B_(empty0 + s));
+        q_issued++;
       }
-      const float pv = adm ? ex2(s[i] * c2 - lse_row) : 0.0f;
-      const float ds = pv * (dp[i] - dlt_row);
-      dh[i] = tf32_hi(ds);
-      dl[i] = ds - dh[i];
+      // committed MMAs finish before TMEM and shared memory are released
+      if (s_issued > 0) mbar_wait(B_(sdone), (uint32_t)((s_issued - 1) & 1), a.error);
+      if (q_issued > 0) {
+        mbar_wait(B_(qdone), (uint32_t)((q_issued - 1) & 1), a.error);
+        mbar_wait(B_(empty0 + ((q_issued - 1) & 1)), (uint32_t)(((q_issued - 1) >> 1) & 1), a.error);
+      }
     }
-    tmem_st32(trow + L::S + 32 * khalf, dh);
-    tmem_st32(trow + L::DP + 32 * khalf, dl);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && t0ok) {
+  } else {
+    // ---- dS = P (dP - delta), P = 2^(S scale log2(e) - lse2)
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int64_t ri = ((int64_t)b * p.Hq + hq) * p.Tq + tq;
+    const float lse_row = valid_q ? a.lse2[ri] : INFINITY;
+    const float dlt_row = valid_q ? a.delta[ri] : 0.0f;
+    const int64_t qpos_row = valid_q ? p.qpos[(int64_t)b * p.Tq + tq] : INT64_MIN;
+    const float c2 = p.scale * kLog2e;
+    const int cb = 32 * khalf;
+    bool ok = true;
+    for (int j = 0; ok && j < nkb; j++) {
+      const int s = j & 1;
+      const uint32_t par = (uint32_t)(j & 1), spar = (uint32_t)((j >> 1) & 1);
+      const bool full_block = j < full_kb;
+      uint8_t keep[32];
+      if (!full_block && p.mask != nullptr) {  // clamped indices stay in bounds
+        const int64_t mrow = ((int64_t)b * p.Tq + min(tq, p.Tq - 1)) * p.Tk;
+#pragma unroll
+        for (int i = 0; i < 32; i++) keep[i] = p.mask[mrow + min(j * KN + cb + i, p.Tk - 1)];
+      }
+      ok = role_wait(B_(KP_FULL0 + s), spar, a.error, abort);
+      if (ok) ok = role_wait(B_(SA_DONE), par, a.error, abort);
+      if (ok) ok = role_wait(B_(SB_DONE), par, a.error, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
       tc_fence_after();
-      const uint32_t kmh = stage_addr(kb) + 4 * L::KT, kml = kmh + L::KT;
+      // keys of the block this query sees: those whose position does not exceed its own
+      const int seen = full_block ? KN : count_below(kpos_s + s * KN, KN, qpos_row + 1) - cb;
+      float sv[32], dp[32];
+      tmem_ld32(trow + L::S + cb, sv);
+      tmem_ld32(trow + L::DP + cb, dp);
 #pragma unroll
-      for (int j = 0; j < KN / 8; j++) {
-        const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-        umma_tf32_ts(tmem + L::DQ, tmem + L::S + 8 * j, mnmajor_desc(kmh, KN, j), idesc_q, acc);
-        umma_tf32_ts(tmem + L::DQ, tmem + L::S + 8 * j, mnmajor_desc(kml, KN, j), idesc_q, 1u);
-        umma_tf32_ts(tmem + L::DQ, tmem + L::DP + 8 * j, mnmajor_desc(kmh, KN, j), idesc_q, 1u);
+      for (int i = 0; i < 32; i++) {
+        bool adm = full_block;
+        if (!full_block) {
+          adm = i < seen;
+          if (p.mask != nullptr) adm = adm && keep[i] != 0;
+        }
+        const float pv = adm ? ex2(fmaf(sv[i], c2, -lse_row)) : 0.0f;
+        const float ds = pv * (dp[i] - dlt_row);
+        sv[i] = tf32_hi(ds);
+        dp[i] = ds - sv[i];
       }
-      umma_commit(pvbar);
-      pv_issued++;
-      // the next S / dP overwrite what these MMAs read; the stage is free after
-      t0ok = mbar_wait(pvbar, (uint32_t)(kb & 1), a.error);
-      if (t0ok && next_load < nkb) issue_load();
+      tmem_st32(trow + L::S + cb, sv);
+      tmem_st32(trow + L::DP + cb, dp);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B_(DS_READY0 + s));
     }
-  }
-  if (ok && nkb > 0) {
-    bool good = mbar_wait(pvbar, (uint32_t)((nkb - 1) & 1), a.error);
-    good = good && (tid != 0 || t0ok);
-    if (__syncthreads_or(!good)) ok = false;
-    tc_fence_after();
-  }
-
-  if (ok) {
-    float* orow = dq.ptr + b * dq.sb + hq * dq.sh + (int64_t)tq * dq.st;
-    const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + tq : tq) * (DH / 2);
-    if constexpr (DH >= 64) {
-#pragma unroll
-      for (int c = 0; c < DH / 64; c++) {
-        const int col = khalf * (DH / 2) + 32 * c;
-        float v[32];
+    if (ok && nkb > 0) {
+      const uint32_t last = (uint32_t)((nkb - 1) & 1);
+      ok = role_wait(B_(QA_DONE), last, a.error, abort);
+      if (ok) ok = role_wait(B_(QB_DONE), last, a.error, abort);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+      const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + tq : tq) * (DH / 2);
+      auto load_dq = [&](int col, float (&v)[32]) {
         if (nkb > 0) {
-          tmem_ld32(trow + L::DQ + col, v);
+          float w[32];
+          tmem_ld32(trow + L::DQA + col, v);
+          tmem_ld32(trow + L::DQB + col, w);
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = v[i] + w[i];
         } else {
 #pragma unroll
           for (int i = 0; i < 32; i++) v[i] = 0.0f;
         }
-        if (valid_q) store_grad_row<32>(v, 0, orow + col, p.scale, p.q_cos, p.q_sin, trw, col);
-      }
-    } else {
-      float v[32];
-      if (nkb > 0) {
-        tmem_ld32(trow + L::DQ, v);
-      } else {
+      };
+      // dQ rows staged in the free K/V stages, written out with coalesced stores
+      if constexpr (DH >= 64) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = 0.0f;
-      }
-      if (valid_q) {
-        if (khalf == 0) store_grad_row<16>(v, 0, orow, p.scale, p.q_cos, p.q_sin, trw, 0);
-        else store_grad_row<16>(v, 16, orow + 16, p.scale, p.q_cos, p.q_sin, trw, 16);
+        for (int c = 0; c < DH / 64; c++) {
+          const int col = khalf * (DH / 2) + 32 * c;
+          float v[32];
+          load_dq(col, v);
+          grad_row<32>(v, 0, p.scale, p.q_cos, p.q_sin, trw, col);
+          stage_row32(base, DH, row, col, v, 0, 32);
+        }
+      } else {
+        float v[32];
+        load_dq(0, v);
+        if (khalf == 0) {
+          grad_row<16>(v, 0, p.scale, p.q_cos, p.q_sin, trw, 0);
+          stage_row32(base, DH, row, 0, v, 0, 16);
+        } else {
+          grad_row<16>(v, 16, p.scale, p.q_cos, p.q_sin, trw, 16);
+          stage_row32(base, DH, row, 16, v, 16, 16);
+        }
       }
     }
-  } else if (tid == 0) {
-    for (int k = waits; k < next_load; k++)
-      mbar_wait(full0 + 8 * (k % L::NBUF), (uint32_t)((k / L::NBUF) & 1), a.error);
-    if (s_issued > 0) mbar_wait(sbar, (uint32_t)((s_issued - 1) & 1), a.error);
-    if (pv_issued > 0) mbar_wait(pvbar, (uint32_t)((pv_issued - 1) & 1), a.error);
+    named_sync(1, SOFT);
+    if (ok)
+      store_staged_rows(base, DH, min(QM, p.Tq - q0),
+                        dq.ptr + b * dq.sb + hq * dq.sh + (int64_t)q0 * dq.st, dq.st, tid, SOFT);
   }
   tc_fence_before();
   __syncthreads();
@@ -636,9 +849,12 @@ bool launch_bwd_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTen
   if (qrows >= ((int64_t)1 << 31) || krows >= ((int64_t)1 << 31)) return false;
   constexpr auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   constexpr auto SW32 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-  CUtensorMap kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml;
-  CUtensorMap kkh, kkl, vkh, vkl, kmh, kml;
-  bool built = make_map(&kl, w.kl, DH, krows, DH, BK, SW) && make_map(&vl, w.vl, DH, krows, DH, BK, SW) &&
+  CUtensorMap kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml;
+  CUtensorMap qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml;
+  bool built = make_map(&kh, w.kh, DH, krows, DH, BK, SW) && make_map(&vh, w.vh, DH, krows, DH, BK, SW) &&
+               make_map(&kl, w.kl, DH, krows, DH, BK, SW) && make_map(&vl, w.vl, DH, krows, DH, BK, SW) &&
+               make_map(&qh128, w.qh, DH, qrows, DH, QM, SW) && make_map(&ql128, w.ql, DH, qrows, DH, QM, SW) &&
+               make_map(&gh128, w.doh, DH, qrows, DH, QM, SW) && make_map(&gl128, w.dol, DH, qrows, DH, QM, SW) &&
                make_map(&qkh, w.qh, DH, qrows, DH, BQ, SW) && make_map(&qkl, w.ql, DH, qrows, DH, BQ, SW) &&
                make_map(&gkh, w.doh, DH, qrows, DH, BQ, SW) && make_map(&gkl, w.dol, DH, qrows, DH, BQ, SW) &&
                make_map(&qmh, w.qh, DH, qrows, DH, BQ, SW32) && make_map(&qml, w.ql, DH, qrows, DH, BQ, SW32) &&
@@ -656,12 +872,12 @@ bool launch_bwd_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTen
                        KvLayout<DH>::SMEM);
   cudaFuncSetAttribute(attn_bwd_q_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        QLayout<DH>::SMEM);
-  dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);
+  dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);  // THREADS: 8 probability warps, MMA, loads
   attn_bwd_kv_tc_kernel<DH><<<g1, THREADS, KvLayout<DH>::SMEM, stream>>>(
-      kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
+      kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
   dim3 g2((p.Tq + QM - 1) / QM, p.Hq, p.B);
-  attn_bwd_q_tc_kernel<DH><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(kkh, kkl, vkh, vkl, kmh,
-                                                                        kml, p, dq, a);
+  attn_bwd_q_tc_kernel<DH><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(
+      qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml, p, dq, a);
   count_launch(2);
   return true;
 }

@@ -74,5 +74,97 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int rows, int j) 
 __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int krows, int j) {
   return sdesc(base + 1024u * (uint32_t)j, (uint32_t)krows * 128u, 512u, 1u);
 }
+// The same descriptors from a slice-0 descriptor plus a constant: the start
+// address field holds address >> 4 and shared-memory addresses stay below
+// 2^18, so adding (offset >> 4) never carries out of the field.
+template <int ROWS>
+__device__ __forceinline__ uint64_t kslice(uint64_t d0, int j) {
+  return d0 + (uint64_t)((((uint32_t)(j >> 2) * ROWS * 128u) + (uint32_t)(j & 3) * 32u) >> 4);
+}
+__device__ __forceinline__ uint64_t mslice(uint64_t d0, int j) { return d0 + (uint64_t)(64 * j); }
+
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// Row `row` of a 128-row K-major tile staged by TMA with the 128-byte swizzle
+// (32-column chunks of 128 rows x 128 B) -> 32 TMEM columns per chunk of this
+// thread's lane, starting at column `col` of `trow`.
+template <int COLS>
+__device__ __forceinline__ void tile_row_to_tmem(uint32_t tile, int row, uint32_t trow,
+                                                 uint32_t col) {
+#pragma unroll
+  for (int c = 0; c < COLS / 32; c++) {
+    float v[32];
+    const uint32_t rp = tile + (uint32_t)c * 128u * 128u + (uint32_t)row * 128u;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const float4 x = lds128(rp + (((uint32_t)u ^ (uint32_t)(row & 7)) << 4));
+      v[4 * u] = x.x; v[4 * u + 1] = x.y; v[4 * u + 2] = x.z; v[4 * u + 3] = x.w;
+    }
+    tmem_st32(trow + col + 32 * c, v);
+  }
+}
+
+// Output rows are staged in shared memory as [128][cols + 4] floats (the pad
+// spreads a row-per-lane float4 store over all banks) and copied out with
+// coalesced float4 stores: `nthreads` threads starting at thread `t`.
+__device__ __forceinline__ void stage_row32(uint32_t stage, int cols, int row, int col,
+                                            const float (&v)[32], int first, int n) {
+  const uint32_t rp = stage + ((uint32_t)row * (uint32_t)(cols + 4) + (uint32_t)col) * 4u;
+#pragma unroll
+  for (int i = 0; i < n; i += 4)
+    sts128(rp + 4u * (uint32_t)i, make_float4(v[first + i], v[first + i + 1], v[first + i + 2],
+                                              v[first + i + 3]));
+}
+__device__ __forceinline__ void store_staged_rows(uint32_t stage, int cols, int rows_valid,
+                                                  float* base, int64_t row_stride, int t,
+                                                  int nthreads) {
+  const int per_row = cols / 4;
+  const bool vec = ((reinterpret_cast<uintptr_t>(base) | (uintptr_t)(row_stride * 4)) & 15) == 0;
+  for (int idx = t; idx < rows_valid * per_row; idx += nthreads) {
+    const int r = idx / per_row, c4 = idx - r * per_row;
+    const float4 v = lds128(stage + ((uint32_t)r * (uint32_t)(cols + 4) + 4u * (uint32_t)c4) * 4u);
+    float* dst = base + (int64_t)r * row_stride + 4 * c4;
+    if (vec) {
+      *reinterpret_cast<float4*>(dst) = v;
+    } else {
+      dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+    }
+  }
+}
+
+// Named barrier over the first `threads` threads (warps 0..threads/32-1).
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Bounded wait that also gives up when another role of the CTA has aborted
+// (*abort set); on a timeout it records the error and raises *abort.
+__device__ __forceinline__ bool role_wait(uint32_t bar, uint32_t parity, int* error,
+                                          volatile int* abort) {
+  if (mbar_try(bar, parity)) return true;
+  const long long start = clock64();
+  for (int n = 0;; n++) {
+    if (mbar_try(bar, parity)) return true;
+    if ((n & 63) == 63) {
+      if (*abort) return false;
+      if (clock64() - start > kWaitCycles) {
+        atomicExch(error, 0x6e6d);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
 
 }  // namespace etb
