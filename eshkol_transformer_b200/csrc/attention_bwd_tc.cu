@@ -203,16 +203,7 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   const int64_t* kp = p.kpos + (int64_t)b * p.Tk;
   const int64_t* qp = p.qpos + (int64_t)b * p.Tq;
   const uint32_t base = smem_u32(smem);
-  int q_begin = 0;
-  {
-    const int64_t first = kp[k0];
-    int lo = 0, hi = p.Tq;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (qp[mid] < first) lo = mid + 1; else hi = mid;
-    }
-    q_begin = lo;
-  }
+  const int q_begin = warp_count(qp, p.Tq, kp[k0], false);  // first query that can see a key
   const int jb = q_begin / BQ, nqb = (p.Tq + BQ - 1) / BQ;
   const int per_head = q_begin < p.Tq ? nqb - jb : 0;
   const int n_it = G * per_head;
@@ -588,18 +579,10 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
     const int64_t qmax = p.qpos[(int64_t)b * p.Tq + qlast];
     const int64_t qmin = p.qpos[(int64_t)b * p.Tq + q0];
     const int64_t* kp = p.kpos + (int64_t)b * p.Tk;
-    int lo = 0, hi = p.Tk;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (kp[mid] <= qmax) lo = mid + 1; else hi = mid;
-    }
-    nkb = (lo + KN - 1) / KN;
-    int lo2 = 0, hi2 = lo;
-    while (lo2 < hi2) {
-      const int mid = (lo2 + hi2) >> 1;
-      if (kp[mid] <= qmin) lo2 = mid + 1; else hi2 = mid;
-    }
-    full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? lo2 / KN : 0;
+    const int seen = warp_count(kp, p.Tk, qmax, true);      // keys some row of the tile sees
+    const int seen_all = warp_count(kp, seen, qmin, true);  // keys every row sees
+    nkb = (seen + KN - 1) / KN;
+    full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? seen_all / KN : 0;
   }
   const uint32_t base = smem_u32(smem);
   constexpr uint32_t RT = QM * DH * 4;  // one [128, DH] row tile

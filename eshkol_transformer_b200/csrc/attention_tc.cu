@@ -11,21 +11,23 @@
 // [B, H, T, Dh], so every tile below is a plain TMA box.
 //
 // Main kernel: one CTA owns 128 query rows of one (batch, head); TMEM lane r
-// is query row r.  8 warps: warp w handles rows 32*(w%4).. and key columns
-// 32*(w/4).. of each 64-key block, so two threads share a row and exchange
-// their row max / exp-sum through shared memory.
-//   Q hi/lo  global -> registers -> TMEM (A operand of every S MMA)
+// is query row r.  Warps 0-7 run the softmax (warp w: rows 32*(w%4).., key
+// columns 32*(w/4).. of each 64-key block; the two threads of a row exchange
+// their block maxima through shared memory); warp 8 issues S = Q K^T, warp 9
+// issues O += P V (one thread each), warp 10 loads K/V tiles by TMA.
+//   Q hi/lo  TMA -> shared -> TMEM (A operand of every S MMA)
 //   K, V     TMA (128-byte swizzle; K 16-byte atoms, V 32-byte atoms),
 //            hi and lo tiles, 3 stages (1 for Dh 128)
-//   S        = Q K^T, tcgen05.mma kind::tf32 with A from TMEM, 3 passes;
-//            for Dh <= 64 two S slots, so S of block j+1 is computed while
-//            the SM runs the softmax of block j
-//   softmax  base-2 online softmax in registers; P hi/lo -> TMEM (P_hi over S);
-//            the O rows are rescaled in TMEM only when their max grows
+//   S        kind::tf32 MMAs with A from TMEM, 3 passes; two S slots for
+//            Dh <= 64, so S of block j+1 runs during the softmax of block j
+//   softmax  base-2 online softmax; P hi/lo -> TMEM (P hi over S)
 //   O       += P V, A = P from TMEM, B = V (MN-major), 3 passes
-// Key blocks entirely visible to every row of the tile skip the per-element
-// admission test.  All mbarrier waits are bounded; a timeout is taken
-// block-uniformly so the CTA always releases its TMEM.
+// The softmax keeps a stale row maximum until a block's maximum exceeds it
+// by more than 2^8: P = 2^(s - m_used) then stays below 256 and O, l share
+// the same scale, so the O rows in TMEM are rescaled (after the previous
+// P V completes) only on those rare jumps.  All mbarrier waits are bounded;
+// a timeout raises a CTA-wide abort flag, in-flight copies and MMAs are
+// waited for (bounded) and TMEM is always released.
 #include "attention_tc.cuh"
 
 namespace etb {
@@ -34,27 +36,32 @@ namespace {
 
 constexpr int QM = 128;  // query rows per CTA
 constexpr int KN = 64;   // keys per block
-constexpr int THREADS = 256;
+constexpr int THREADS = 352;
+constexpr int SOFT = 256;  // softmax threads (warps 0-7)
+constexpr int MMA_S = 8, MMA_O = 9, LOADER = 10;
+constexpr float kRescale = 8.0f;  // log2 of the largest P the stale maximum allows
 
-// Dh <= 64: S is double buffered in TMEM, so Q K^T of the next key block runs
-// on the tensor cores while this block's softmax runs on the SM; Dh 128 has no
-// TMEM room for that and runs the stages back to back.
 template <int DH>
 struct FwdLayout {
-  static constexpr bool PIPE = DH <= 64;
-  static constexpr int NBUF = PIPE ? 3 : 1;
-  static constexpr int KTILE = KN * DH * 4;  // DH/32 chunks of KN rows x 128 B
-  static constexpr int BUF = 4 * KTILE;      // K hi, K lo, V hi, V lo
-  static constexpr int SMEM_BUF = NBUF * BUF;
-  static constexpr int SMEM = SMEM_BUF + 1024 + 256 + 2 * 2 * QM * 4 + KN * 8;
-  static constexpr uint32_t QH = 0, QL = DH, S0 = 2 * DH, NS = PIPE ? 2 : 1,
-                            PL = S0 + NS * KN, O = PL + KN;
+  static constexpr int NSLOT = DH <= 64 ? 2 : 1;   // S / P lo slots in TMEM
+  static constexpr int NSTAGE = DH <= 64 ? 3 : 1;  // K/V stages in shared memory
+  static constexpr int KT = KN * DH * 4;           // one [KN, DH] tile
+  static constexpr int STAGE = 4 * KT;             // K hi, K lo (K-major), V hi, V lo (MN-major)
+  static constexpr int RT = QM * DH * 4;           // one [128, DH] row tile
+  // the stages also carry the Q row tiles (before the loop) and the staged
+  // output rows (after it)
+  static constexpr int SMEM_BUF = NSTAGE * STAGE >= 2 * RT ? NSTAGE * STAGE : 2 * RT;
+  static_assert(QM * (DH + 4) * 4 <= SMEM_BUF, "output stage");
+  static constexpr int BARS = SMEM_BUF;
+  static constexpr int SMEM = BARS + 256 + 1024;
+  static constexpr uint32_t QH = 0, QL = DH, S0 = 2 * DH, PL0 = S0 + NSLOT * KN,
+                            O = PL0 + NSLOT * KN;
   static constexpr uint32_t COLS = (O + DH) <= 256 ? 256 : 512;
   static_assert(O + DH <= 512, "TMEM columns");
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
 struct TcFwdArgs {
-  const float *qh, *ql;  // head-major [B, Hq, Tq, Dh]
   int* error;
 };
 
@@ -90,40 +97,65 @@ __global__ void attn_prepare_kernel(AttnTensor src, int B, int H, int T, int Dh,
   }
 }
 
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
+}
+
+// Number of entries of the ascending array a[0..n) that are below x.
+__device__ __forceinline__ int count_below(const int64_t* a, int n, int64_t x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a[mid] < x) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
 // ---- forward kernel --------------------------------------------------------------
 
 template <int DH>
 __global__ void __launch_bounds__(THREADS, 1)
-attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap kh_map, const __grid_constant__ CUtensorMap kl_map,
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_constant__ CUtensorMap ql_map,
+                   const __grid_constant__ CUtensorMap kh_map, const __grid_constant__ CUtensorMap kl_map,
                    const __grid_constant__ CUtensorMap vh_map, const __grid_constant__ CUtensorMap vl_map,
                    AttnParams p, AttnOut o, float* __restrict__ row_max,
                    float* __restrict__ row_sum, TcFwdArgs a) {
   using L = FwdLayout<DH>;
+  constexpr int NSL = L::NSLOT, NST = L::NSTAGE;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~(uintptr_t)1023);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::SMEM_BUF);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + L::NBUF + 2);
-  float* xmax = reinterpret_cast<float*>(smem + L::SMEM_BUF + 256);  // [2][QM]
-  float* xsum = xmax + 2 * QM;                                          // [2][QM]
-  int64_t* kpos_s = reinterpret_cast<int64_t*>(xsum + 2 * QM);          // [KN]
+  uint8_t* smem = align1024(smem_raw);
+  __shared__ int64_t kpos_s[2 * KN];     // key positions of the block, ring of 2
+  __shared__ float xmax[2 * 2 * QM];     // [block parity][half][row] maxima / exp-sums
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
+  // barrier slots: full[NST] | empty[NST] | s_full[NSL] | pv_done[NSL] | p_ready[2] |
+  // kp_full[2] | rows | pair[4] (the two softmax warps of a lane quarter)
+  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t FULL = bar0, EMPTY = FULL + 8 * NST, SFULL = EMPTY + 8 * NST,
+                 PVD = SFULL + 8 * NSL, PREADY = PVD + 8 * NSL, KPFULL = PREADY + 16,
+                 ROWS = KPFULL + 16, PAIR = ROWS + 8;
+  constexpr int NBARS = 2 * NST + 2 * NSL + 9;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, khalf = warp >> 2;
+  const int quarter = warp & 3, khalf = (warp >> 2) & 1;
   const int row = quarter * 32 + lane;  // query row in the tile == TMEM lane
   const int q0 = blockIdx.x * QM, hq = blockIdx.y, b = blockIdx.z;
   const int hkv = hq / (p.Hq / p.Hkv);
-  const uint32_t full0 = smem_u32(bars), sbar = smem_u32(bars + L::NBUF),
-                 pvbar = smem_u32(bars + L::NBUF + 1);
+  const int tq = q0 + row;
+  const bool valid_q = tq < p.Tq;
   if (tid == 0) {
-    for (int i = 0; i < L::NBUF; i++) mbar_init(full0 + 8 * i, 1);
-    mbar_init(sbar, 1);
-    mbar_init(pvbar, 1);
+    for (int i = 0; i < NBARS; i++) {
+      const uint32_t bar = bar0 + 8 * i;
+      const bool soft = bar == PREADY || bar == PREADY + 8;
+      const bool kp = bar == KPFULL || bar == KPFULL + 8;
+      const bool pair = bar >= PAIR;
+      mbar_init(bar, soft ? SOFT : kp ? 32 : pair ? 64 : 1);
+    }
+    *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), L::COLS);
-  const int tq = q0 + row;
-  const bool valid_q = tq < p.Tq;
 
   // key blocks that can hold an admitted key, and the number of leading
   // blocks visible to every row of the tile (positions strictly increase)
@@ -133,269 +165,274 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap kh_map, const __grid_cons
     const int64_t qmax = p.qpos[(int64_t)b * p.Tq + qlast];
     const int64_t qmin = p.qpos[(int64_t)b * p.Tq + q0];
     const int64_t* kp = p.kpos + (int64_t)b * p.Tk;
-    int lo = 0, hi = p.Tk;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (kp[mid] <= qmax) lo = mid + 1; else hi = mid;
-    }
-    nkb = (lo + KN - 1) / KN;
-    int lo2 = 0, hi2 = lo;
-    while (lo2 < hi2) {
-      const int mid = (lo2 + hi2) >> 1;
-      if (kp[mid] <= qmin) lo2 = mid + 1; else hi2 = mid;
-    }
-    full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? lo2 / KN : 0;
+    const int seen = warp_count(kp, p.Tk, qmax, true);      // keys some row of the tile sees
+    const int seen_all = warp_count(kp, seen, qmin, true);  // keys every row sees
+    nkb = (seen + KN - 1) / KN;
+    full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? seen_all / KN : 0;
   }
-  auto load_kpos = [&](int kb) {
-    if (kb < nkb && kb >= full_kb && tid < KN) {
-      const int tk = kb * KN + tid;
-      kpos_s[tid] = tk < p.Tk ? p.kpos[(int64_t)b * p.Tk + tk] : INT64_MAX;
+  const uint32_t base = smem_u32(smem);
+  if (tid == 0) {
+    // Q hi/lo rows pass through the (still unused) K/V stages on their way to TMEM
+    mbar_expect_tx(ROWS, 2 * L::RT);
+    const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
+#pragma unroll
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t off = (uint32_t)c * QM * 128u;
+      tma_load_2d(base + off, &qh_map, ROWS, 32 * c, r);
+      tma_load_2d(base + L::RT + off, &ql_map, ROWS, 32 * c, r);
     }
-  };
-  load_kpos(0);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
   const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-
-  // producer / MMA state, meaningful in thread 0 only
-  int next_load = 0, next_full = 0, s_issued = 0, pv_issued = 0;
-  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
-  auto buf_addr = [&](int kb) { return smem_u32(smem) + (uint32_t)((kb % L::NBUF) * L::BUF); };
-  auto issue_load = [&]() {  // next_load into its buffer
-    const int kb = next_load++;
-    const uint32_t full = full0 + 8 * (kb % L::NBUF);
-    mbar_expect_tx(full, 4 * L::KTILE);
-    const int r = (int)(kv_row0 + (int64_t)kb * KN);
-    const uint32_t base = buf_addr(kb);
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      tma_load_2d(base + c * KN * 128, &kh_map, full, 32 * c, r);
-      tma_load_2d(base + L::KTILE + c * KN * 128, &kl_map, full, 32 * c, r);
-      tma_load_2d(base + 2 * L::KTILE + c * KN * 128, &vh_map, full, 32 * c, r);
-      tma_load_2d(base + 3 * L::KTILE + c * KN * 128, &vl_map, full, 32 * c, r);
+  if (warp < 8) {
+    const bool ok = mbar_wait(ROWS, 0u, a.error);
+    if (!ok) *abort = 1;
+    if (__all_sync(0xffffffffu, ok)) {
+      tile_row_to_tmem<DH>(base + (uint32_t)khalf * L::RT, row, trow, khalf == 0 ? L::QH : L::QL);
+      tmem_wait_st();
     }
-  };
-  const uint32_t idesc_s = idesc_tf32_m128(KN, 0);
-  const uint32_t idesc_o = idesc_tf32_m128(DH, 1);
-  auto s_slot = [&](int kb) { return L::S0 + (uint32_t)(L::PIPE ? (kb & 1) * KN : 0); };
-  auto issue_s = [&](int kb) -> bool {  // thread 0: S(kb) = Q K(kb)^T
-    const int k = next_full++;
-    if (!mbar_wait(full0 + 8 * (k % L::NBUF), (uint32_t)((k / L::NBUF) & 1), a.error))
-      return false;
-    tc_fence_after();
-    const uint32_t khs = buf_addr(kb), kls = khs + L::KTILE;
-    const uint32_t d = tmem + s_slot(kb);
-#pragma unroll
-    for (int j = 0; j < DH / 8; j++) {
-      const uint64_t dh = kmajor_desc(khs, KN, j);
-      const uint64_t dl = kmajor_desc(kls, KN, j);
-      umma_tf32_ts(d, tmem + L::QH + 8 * j, dh, idesc_s, j > 0 ? 1u : 0u);
-      umma_tf32_ts(d, tmem + L::QH + 8 * j, dl, idesc_s, 1u);
-      umma_tf32_ts(d, tmem + L::QL + 8 * j, dh, idesc_s, 1u);
-    }
-    umma_commit(sbar);
-    s_issued++;
-    return true;
-  };
-  auto issue_pv = [&](int kb) {  // thread 0: O += P(kb) V(kb)
-    tc_fence_after();
-    const uint32_t vhs = buf_addr(kb) + 2 * L::KTILE, vls = vhs + L::KTILE;
-    const uint32_t ph = tmem + s_slot(kb);
-#pragma unroll
-    for (int j = 0; j < KN / 8; j++) {
-      const uint64_t dh = mnmajor_desc(vhs, KN, j);
-      const uint64_t dl = mnmajor_desc(vls, KN, j);
-      const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-      umma_tf32_ts(tmem + L::O, ph + 8 * j, dh, idesc_o, acc);
-      umma_tf32_ts(tmem + L::O, ph + 8 * j, dl, idesc_o, 1u);
-      umma_tf32_ts(tmem + L::O, tmem + L::PL + 8 * j, dh, idesc_o, 1u);
-    }
-    umma_commit(pvbar);
-    pv_issued++;
-  };
-
-  bool ok = true;
-  if (tid == 0) {
-    while (next_load < L::NBUF && next_load < nkb) issue_load();
-  }
-
-  // ---- Q hi/lo rows -> TMEM (warps 0-3 hi, 4-7 lo)
-  {
-    const float* src = khalf == 0 ? a.qh : a.ql;
-    const float* qrow = src + (((int64_t)b * p.Hq + hq) * p.Tq + tq) * DH;
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        float4 x = valid_q ? *reinterpret_cast<const float4*>(qrow + c * 32 + i)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
-      }
-      tmem_st32(trow + (khalf == 0 ? L::QH : L::QL) + c * 32, v);
-    }
-    tmem_wait_st();
   }
   tc_fence_before();
   __syncthreads();
-  if (L::PIPE && tid == 0 && nkb > 0) ok = issue_s(0);
-  if (__syncthreads_or(!ok)) ok = false;
+  tc_fence_after();
 
-  const float c2 = p.scale * kLog2e;  // base-2 score scale
-  float m = -INFINITY, l = 0.0f;      // base-2 running max, exp-sum
-  const int64_t qpos_row = valid_q ? p.qpos[(int64_t)b * p.Tq + tq] : -1;
-  for (int kb = 0; ok && kb < nkb; kb++) {
-    const bool full_block = kb < full_kb;
-    bool good = true;
-    if (!L::PIPE && tid == 0) good = issue_s(kb);
-    // S(kb) ready
-    if (good) good = mbar_wait(sbar, (uint32_t)(kb & 1), a.error);
-    good = __all_sync(0xffffffffu, good);  // tcgen05.ld/st are warp-collective
-    float s[32];
-    if (good) {
-      tc_fence_after();
-      tmem_ld32(trow + s_slot(kb) + 32 * khalf, s);
-    }
-    float bmax = -INFINITY;
-    if (full_block) {
+  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
+  if (warp == LOADER) {
+    // ---- K/V stages by TMA, key positions by the lanes
+    int loads = 0;
+    bool ok = true;
+    for (int j = 0; ok && j < nkb; j++) {
+      const int st = j % NST;
+      if (lane == 0) {
+        if (j >= NST) ok = role_wait(EMPTY + 8 * st, (uint32_t)((j / NST - 1) & 1), a.error, abort);
+        if (ok) {
+          const uint32_t bar = FULL + 8 * st, dst = base + st * L::STAGE;
+          const int r = (int)(kv_row0 + (int64_t)j * KN);
+          mbar_expect_tx(bar, L::STAGE);
 #pragma unroll
-      for (int i = 0; i < 32; i++) {
-        s[i] *= c2;
-        bmax = fmaxf(bmax, s[i]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; i++) {
-        const int k = 32 * khalf + i;
-        bool adm = valid_q && kpos_s[k] <= qpos_row;
-        if (adm && p.mask != nullptr)
-          adm = p.mask[((int64_t)b * p.Tq + tq) * p.Tk + kb * KN + k] != 0;
-        s[i] = adm ? s[i] * c2 : -INFINITY;
-        bmax = fmaxf(bmax, s[i]);
-      }
-    }
-    xmax[khalf * QM + row] = bmax;
-    if (__syncthreads_or(!good)) { ok = false; break; }
-    bmax = fmaxf(bmax, xmax[(1 - khalf) * QM + row]);
-    if (L::PIPE) {
-      // PV(kb-1) done: its K/V buffer, P columns and O are free
-      if (kb > 0) good = mbar_wait(pvbar, (uint32_t)((kb - 1) & 1), a.error);
-      if (tid == 0 && good) {
-        if (kb > 0 && next_load < nkb) issue_load();  // into the buffer of block kb-1
-        if (kb + 1 < nkb) good = issue_s(kb + 1);
-      }
-      good = __all_sync(0xffffffffu, good);
-      tc_fence_after();
-    }
-    const float m_new = fmaxf(m, bmax);
-    float corr = 1.0f;
-    if (m_new != -INFINITY) corr = (m == -INFINITY) ? 0.0f : ex2(m - m_new);
-    float psum = 0.0f;
-    float ph[32], pl[32];
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      const float pv = (s[i] == -INFINITY) ? 0.0f : ex2(s[i] - m_new);
-      psum += pv;
-      ph[i] = tf32_round(pv);
-      pl[i] = pv - ph[i];
-    }
-    xsum[khalf * QM + row] = psum;
-    // rescale this thread's half of the O row (warp-uniform branch)
-    if (good && kb > 0 && __any_sync(0xffffffffu, corr != 1.0f)) {
-      if constexpr (DH >= 64) {
-#pragma unroll
-        for (int c = 0; c < DH / 64; c++) {
-          float ov[32];
-          const uint32_t col = L::O + (uint32_t)(khalf * (DH / 2) + c * 32);
-          tmem_ld32(trow + col, ov);
-#pragma unroll
-          for (int i = 0; i < 32; i++) ov[i] *= corr;
-          tmem_st32(trow + col, ov);
-        }
-      } else if (khalf == 0) {  // Dh 32: warps 0-3 rescale the whole row
-        float ov[32];
-        tmem_ld32(trow + L::O, ov);
-#pragma unroll
-        for (int i = 0; i < 32; i++) ov[i] *= corr;
-        tmem_st32(trow + L::O, ov);
-      }
-    }
-    if (good) {
-      tmem_st32(trow + s_slot(kb) + 32 * khalf, ph);
-      tmem_st32(trow + L::PL + 32 * khalf, pl);
-      tmem_wait_st();
-    }
-    load_kpos(kb + 1);
-    tc_fence_before();
-    if (__syncthreads_or(!good)) { ok = false; break; }
-    l = l * corr + (xsum[row] + xsum[QM + row]);
-    m = m_new;
-    if (tid == 0) issue_pv(kb);
-    if (!L::PIPE) {
-      good = mbar_wait(pvbar, (uint32_t)(kb & 1), a.error);
-      if (tid == 0 && good && next_load < nkb) issue_load();
-      if (__syncthreads_or(!good)) { ok = false; break; }
-      tc_fence_after();
-    }
-  }
-  if (L::PIPE && ok && nkb > 0) {
-    if (__syncthreads_or(!mbar_wait(pvbar, (uint32_t)((nkb - 1) & 1), a.error))) ok = false;
-    tc_fence_after();
-  }
-
-  // ---- epilogue: O / l (each thread writes its half of the row), statistics
-  if (ok) {
-    const bool empty = l == 0.0f;
-    float* orow = o.ptr + b * o.sb + hq * o.sh + (int64_t)tq * o.st;
-    if (valid_q && khalf == 0) {
-      const int64_t ri = ((int64_t)b * p.Hq + hq) * p.Tq + tq;
-      row_max[ri] = empty ? 0.0f : m * kLn2;
-      row_sum[ri] = empty ? 0.0f : l;
-    }
-    if (nkb > 0) {
-      if constexpr (DH >= 64) {
-#pragma unroll
-        for (int c = 0; c < DH / 64; c++) {
-          float ov[32];
-          tmem_ld32(trow + L::O + khalf * (DH / 2) + c * 32, ov);
-          if (valid_q) {
-            float* dst = orow + khalf * (DH / 2) + c * 32;
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              float4 w;
-              w.x = empty ? 0.0f : rn_div(ov[i], l);
-              w.y = empty ? 0.0f : rn_div(ov[i + 1], l);
-              w.z = empty ? 0.0f : rn_div(ov[i + 2], l);
-              w.w = empty ? 0.0f : rn_div(ov[i + 3], l);
-              if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                *reinterpret_cast<float4*>(dst + i) = w;
-              } else {
-                dst[i] = w.x; dst[i + 1] = w.y; dst[i + 2] = w.z; dst[i + 3] = w.w;
-              }
-            }
+          for (int c = 0; c < DH / 32; c++) {
+            const uint32_t off = (uint32_t)c * KN * 128u;
+            tma_load_2d(dst + off, &kh_map, bar, 32 * c, r);
+            tma_load_2d(dst + L::KT + off, &kl_map, bar, 32 * c, r);
+            tma_load_2d(dst + 2 * L::KT + off, &vh_map, bar, 32 * c, r);
+            tma_load_2d(dst + 3 * L::KT + off, &vl_map, bar, 32 * c, r);
           }
+          loads++;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok && j >= 2) ok = role_wait(PREADY + 8 * (j & 1), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+#pragma unroll
+        for (int h = 0; h < KN / 32; h++) {
+          const int t = j * KN + 32 * h + lane;
+          kpos_s[(j & 1) * KN + 32 * h + lane] = t < p.Tk ? p.kpos[(int64_t)b * p.Tk + t] : INT64_MAX;
+        }
+        mbar_arrive(KPFULL + 8 * (j & 1));
+      }
+    }
+    if (lane == 0) {  // every copy has landed before the CTA releases its memory
+      for (int j = loads - NST < 0 ? 0 : loads - NST; j < loads; j++)
+        mbar_wait(FULL + 8 * (j % NST), (uint32_t)((j / NST) & 1), a.error);
+    }
+  } else if (warp == MMA_S) {
+    // ---- S = Q K^T (3 passes) into slot j % NSLOT
+    if (lane == 0 && nkb > 0) {
+      constexpr uint32_t idesc = idesc_tf32_m128(KN, 0);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < nkb; j++) {
+        const int sl = j % NSL, st = j % NST;
+        ok = role_wait(FULL + 8 * st, (uint32_t)((j / NST) & 1), a.error, abort);
+        // the slot holds P of block j - NSLOT until its P V completes
+        if (ok && j >= NSL) ok = role_wait(PVD + 8 * sl, (uint32_t)((j / NSL - 1) & 1), a.error, abort);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t stg = base + st * L::STAGE;
+        const uint64_t kh = kmajor_desc(stg, KN, 0), kl = kmajor_desc(stg + L::KT, KN, 0);
+        const uint32_t d = tmem + L::S0 + sl * KN;
+#pragma unroll
+        for (int k = 0; k < DH / 8; k++) {
+          const uint32_t acc = k > 0 ? 1u : 0u;
+          umma_tf32_ts(d, tmem + L::QH + 8 * k, kslice<KN>(kh, k), idesc, acc);
+          umma_tf32_ts(d, tmem + L::QH + 8 * k, kslice<KN>(kl, k), idesc, 1u);
+          umma_tf32_ts(d, tmem + L::QL + 8 * k, kslice<KN>(kh, k), idesc, 1u);
+        }
+        umma_commit(SFULL + 8 * sl);
+        issued++;
+      }
+      if (issued > 0)  // committed MMAs finish before TMEM is released
+        mbar_wait(SFULL + 8 * ((issued - 1) % NSL), (uint32_t)(((issued - 1) / NSL) & 1), a.error);
+    }
+  } else if (warp == MMA_O) {
+    // ---- O += P V (3 passes)
+    if (lane == 0 && nkb > 0) {
+      constexpr uint32_t idesc = idesc_tf32_m128(DH, 1);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < nkb; j++) {
+        const int sl = j % NSL, st = j % NST;
+        ok = role_wait(PREADY + 8 * (j & 1), (uint32_t)((j >> 1) & 1), a.error, abort);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t stg = base + st * L::STAGE;
+        const uint64_t vh = mnmajor_desc(stg + 2 * L::KT, KN, 0),
+                       vl = mnmajor_desc(stg + 3 * L::KT, KN, 0);
+        const uint32_t ph = tmem + L::S0 + sl * KN, pl = tmem + L::PL0 + sl * KN;
+#pragma unroll
+        for (int k = 0; k < KN / 8; k++) {
+          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          umma_tf32_ts(tmem + L::O, ph + 8 * k, mslice(vh, k), idesc, acc);
+          umma_tf32_ts(tmem + L::O, ph + 8 * k, mslice(vl, k), idesc, 1u);
+          umma_tf32_ts(tmem + L::O, pl + 8 * k, mslice(vh, k), idesc, 1u);
+        }
+        umma_commit(PVD + 8 * sl);
+        umma_commit(EMPTY + 8 * st);
+        issued++;
+      }
+      if (issued > 0) {  // committed MMAs finish before TMEM and shared memory are released
+        const int jl = issued - 1;
+        mbar_wait(PVD + 8 * (jl % NSL), (uint32_t)((jl / NSL) & 1), a.error);
+        mbar_wait(EMPTY + 8 * (jl % NST), (uint32_t)((jl / NST) & 1), a.error);
+      }
+    }
+  } else {
+    // ---- softmax: this thread's 32 keys of each block, row shared with warp w^4
+    const float c2 = p.scale * kLog2e;  // base-2 score scale
+    const int cb = 32 * khalf;
+    const int64_t qpos_row = valid_q ? p.qpos[(int64_t)b * p.Tq + tq] : INT64_MIN;
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; ok && j < nkb; j++) {
+      const int sl = j % NSL;
+      const bool full_block = j < full_kb;
+      uint8_t keep[32];
+      if (!full_block && p.mask != nullptr) {  // clamped indices stay in bounds
+        const int64_t mrow = ((int64_t)b * p.Tq + min(tq, p.Tq - 1)) * p.Tk;
+#pragma unroll
+        for (int i = 0; i < 32; i++) keep[i] = p.mask[mrow + min(j * KN + cb + i, p.Tk - 1)];
+      }
+      ok = role_wait(KPFULL + 8 * (j & 1), (uint32_t)((j >> 1) & 1), a.error, abort);
+      if (ok) ok = role_wait(SFULL + 8 * sl, (uint32_t)((j / NSL) & 1), a.error, abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      float s[32];
+      tmem_ld32(trow + L::S0 + sl * KN + cb, s);
+      float bmax = -INFINITY;
+      if (full_block) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          s[i] *= c2;
+          bmax = fmaxf(bmax, s[i]);
+        }
+      } else {
+        // keys of the block this row sees: those whose position does not exceed its own
+        const int seen = count_below(kpos_s + (j & 1) * KN, KN, qpos_row + 1) - cb;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          bool adm = i < seen;
+          if (p.mask != nullptr) adm = adm && keep[i] != 0;
+          s[i] = adm ? s[i] * c2 : -INFINITY;
+          bmax = fmaxf(bmax, s[i]);
+        }
+      }
+      // warps w and w+4 hold the two halves of these rows: exchange maxima
+      // (a slot per block parity; a slot is rewritten only after the partner
+      // has passed the next exchange, so after it read this one)
+      float* xm = xmax + (j & 1) * 2 * QM;
+      xm[khalf * QM + row] = bmax;
+      mbar_arrive(PAIR + 8 * quarter);
+      ok = __all_sync(0xffffffffu, role_wait(PAIR + 8 * quarter, (uint32_t)(j & 1), a.error, abort));
+      if (!ok) break;
+      bmax = fmaxf(bmax, xm[(1 - khalf) * QM + row]);
+      // a stale maximum stands until this block exceeds it by more than 2^kRescale
+      float factor = 1.0f;
+      const bool jump = bmax > m_used + kRescale;  // false for -inf blocks
+      if (jump) {
+        factor = m_used == -INFINITY ? 0.0f : ex2(m_used - bmax);
+        l *= factor;
+        m_used = bmax;
+      }
+      if (__any_sync(0xffffffffu, jump && factor != 0.0f)) {
+        // O already holds earlier blocks: wait for the last P V, rescale this half
+        bool w = true;
+        if (j > 0)
+          w = role_wait(PVD + 8 * ((j - 1) % NSL), (uint32_t)(((j - 1) / NSL) & 1), a.error, abort);
+        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < (DH >= 64 ? DH / 64 : 1); c++) {
+          const uint32_t col = L::O + (DH >= 64 ? (uint32_t)(khalf * (DH / 2) + 32 * c) : 0u);
+          if (DH >= 64 || khalf == 0) {
+            float ov[32];
+            tmem_ld32(trow + col, ov);
+#pragma unroll
+            for (int i = 0; i < 32; i++) ov[i] *= factor;
+            tmem_st32(trow + col, ov);
+          }
+        }
+      }
+      float ph[32], pl[32];
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        const float pv = (s[i] == -INFINITY) ? 0.0f : ex2(s[i] - m_used);
+        l += pv;
+        ph[i] = tf32_round(pv);
+        pl[i] = pv - ph[i];
+      }
+      tmem_st32(trow + L::S0 + sl * KN + cb, ph);
+      tmem_st32(trow + L::PL0 + sl * KN + cb, pl);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(PREADY + 8 * (j & 1));
+    }
+    if (ok && nkb > 0)
+      ok = role_wait(PVD + 8 * ((nkb - 1) % NSL), (uint32_t)(((nkb - 1) / NSL) & 1), a.error, abort);
+    ok = __all_sync(0xffffffffu, ok);
+    // full exp-sum of the row from the two halves (one more exchange)
+    float* xl = xmax + (nkb & 1) * 2 * QM;
+    xl[khalf * QM + row] = l;
+    mbar_arrive(PAIR + 8 * quarter);
+    if (ok) ok = __all_sync(0xffffffffu, role_wait(PAIR + 8 * quarter, (uint32_t)(nkb & 1), a.error, abort));
+    const float lsum = l + xl[(1 - khalf) * QM + row];
+    const bool empty = lsum == 0.0f;
+    if (ok && valid_q && khalf == 0) {
+      const int64_t ri = ((int64_t)b * p.Hq + hq) * p.Tq + tq;
+      row_max[ri] = empty ? 0.0f : m_used * kLn2;
+      row_sum[ri] = empty ? 0.0f : lsum;
+    }
+    // O / l staged in the free stages, written out with coalesced stores
+    const uint32_t stage = base;
+    if (ok) {
+      tc_fence_after();
+      if constexpr (DH >= 64) {
+#pragma unroll
+        for (int c = 0; c < DH / 64; c++) {
+          const int col = khalf * (DH / 2) + 32 * c;
+          float ov[32];
+          if (nkb > 0) tmem_ld32(trow + L::O + col, ov);
+#pragma unroll
+          for (int i = 0; i < 32; i++) ov[i] = (empty || nkb == 0) ? 0.0f : rn_div(ov[i], lsum);
+          stage_row32(stage, DH, row, col, ov, 0, 32);
         }
       } else {
         float ov[32];
-        tmem_ld32(trow + L::O, ov);
-        if (valid_q) {
+        if (nkb > 0) tmem_ld32(trow + L::O, ov);
 #pragma unroll
-          for (int i = 0; i < 32; i++)
-            if ((i >> 4) == khalf) orow[i] = empty ? 0.0f : rn_div(ov[i], l);
-        }
+        for (int i = 0; i < 32; i++) ov[i] = (empty || nkb == 0) ? 0.0f : rn_div(ov[i], lsum);
+        if (khalf == 0) stage_row32(stage, DH, row, 0, ov, 0, 16);
+        else stage_row32(stage, DH, row, 16, ov, 16, 16);
       }
-    } else if (valid_q) {
-      for (int i = khalf * (DH / 2); i < (khalf + 1) * (DH / 2); i++) orow[i] = 0.0f;
     }
-  } else if (tid == 0) {
-    // a wait ran out: let every copy and MMA still in flight land (bounded)
-    // before the shared memory and TMEM are released
-    for (int k = next_full; k < next_load; k++)
-      mbar_wait(full0 + 8 * (k % L::NBUF), (uint32_t)((k / L::NBUF) & 1), a.error);
-    if (s_issued > 0) mbar_wait(sbar, (uint32_t)((s_issued - 1) & 1), a.error);
-    if (pv_issued > 0) mbar_wait(pvbar, (uint32_t)((pv_issued - 1) & 1), a.error);
+    named_sync(1, SOFT);
+    if (ok)
+      store_staged_rows(stage, DH, min(QM, p.Tq - q0),
+                        o.ptr + b * o.sb + hq * o.sh + (int64_t)q0 * o.st, o.st, tid, SOFT);
   }
   tc_fence_before();
   __syncthreads();
@@ -409,20 +446,22 @@ template <int DH>
 bool launch_fwd_tc(const AttnParams& p, AttnOut o, float* m, float* l, cudaStream_t stream) {
   using L = FwdLayout<DH>;
   const AttnWs w = attn_ws(p);
-  const int64_t krows = (int64_t)p.B * p.Hkv * p.Tk;
-  if (krows >= ((int64_t)1 << 31)) return false;
-  CUtensorMap mkh, mkl, mvh, mvl;
-  if (!make_map(&mkh, w.kh, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mkl, w.kl, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mvh, w.vh, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
-      !make_map(&mvl, w.vl, DH, krows, DH, KN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+  const int64_t qrows = (int64_t)p.B * p.Hq * p.Tq, krows = (int64_t)p.B * p.Hkv * p.Tk;
+  if (qrows >= ((int64_t)1 << 31) || krows >= ((int64_t)1 << 31)) return false;
+  constexpr auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  constexpr auto SW32 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+  if (!make_map(&mqh, w.qh, DH, qrows, DH, QM, SW) || !make_map(&mql, w.ql, DH, qrows, DH, QM, SW) ||
+      !make_map(&mkh, w.kh, DH, krows, DH, KN, SW) || !make_map(&mkl, w.kl, DH, krows, DH, KN, SW) ||
+      !make_map(&mvh, w.vh, DH, krows, DH, KN, SW32) || !make_map(&mvl, w.vl, DH, krows, DH, KN, SW32))
     return false;
   attention_prepare_qkv(p, w, stream);
-  TcFwdArgs a{w.qh, w.ql, device_error_word()};
+  TcFwdArgs a{device_error_word()};
   cudaFuncSetAttribute(attn_fwd_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        L::SMEM);
   dim3 grid((p.Tq + QM - 1) / QM, p.Hq, p.B);
-  attn_fwd_tc_kernel<DH><<<grid, THREADS, L::SMEM, stream>>>(mkh, mkl, mvh, mvl, p, o, m, l, a);
+  attn_fwd_tc_kernel<DH><<<grid, THREADS, L::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, p, o,
+                                                              m, l, a);
   count_launch();
   return true;
 }

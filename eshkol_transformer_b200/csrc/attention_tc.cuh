@@ -143,6 +143,31 @@ __device__ __forceinline__ void store_staged_rows(uint32_t stage, int cols, int 
   }
 }
 
+// Number of entries of the ascending array a[0..n) that are <= x (le) or < x
+// (!le), found by a 32-ary search of the calling warp (every lane gets the
+// result): each round loads 32 entries at once and narrows the bracket 32-fold,
+// two dependent load rounds for n <= 1024.
+__device__ __forceinline__ int warp_count(const int64_t* a, int n, int64_t x, bool le) {
+  const int lane = threadIdx.x & 31;
+  int lo = 0, hi = n;  // the count lies in [lo, hi]
+  while (hi - lo > 32) {
+    const int step = (hi - lo + 31) / 32;
+    const int idx = lo + lane * step;
+    const bool in = idx < hi;
+    const int64_t v = in ? a[idx] : 0;
+    const unsigned below = __ballot_sync(0xffffffffu, in && (le ? v <= x : v < x));
+    const int c = __popc(below);  // a prefix of the lanes, as a is ascending
+    if (c == 0) return lo;        // a[lo] already fails
+    const int last = lo + (c - 1) * step;
+    lo = last + 1;
+    hi = min(hi, last + step);
+  }
+  const int idx = lo + lane;
+  const bool in = idx < hi;
+  const int64_t v = in ? a[idx] : 0;
+  return lo + __popc(__ballot_sync(0xffffffffu, in && (le ? v <= x : v < x)));
+}
+
 // Named barrier over the first `threads` threads (warps 0..threads/32-1).
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

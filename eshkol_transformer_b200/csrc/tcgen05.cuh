@@ -76,17 +76,6 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t 
   return d;
 }
 
-// Descriptor of the j-th K=8 slice of a staged operand tile.
-//   K-major : rows of 128 B (32 k), 8-row swizzle atoms 1024 B apart (SBO),
-//             slice j at +32j B within the atom row.
-//   MN-major: per 32-wide MN chunk, 32 k-rows of 128 B (4096 B); chunks 4096 B
-//             apart (LBO); 4-row swizzle groups 512 B apart (SBO); slice j
-//             (8 k-rows) at +1024j B.
-__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int j) {
-  return mn_major ? sdesc(base + 1024u * j, 4096u, 512u, 1u)
-                  : sdesc(base + 32u * j, 16u, 1024u, 2u);
-}
-
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                           uint32_t accumulate) {
   asm volatile(
@@ -223,19 +212,25 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D f32 tensor map over a row-major [outer, inner] array with row stride
-// `ld` elements; box {32, box_outer}, zero OOB fill.  The swizzle must match
-// the descriptor layout the MMA reads the tile with.
-inline bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, int64_t ld,
-              uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+// `ld` elements; box {box_inner, box_outer}, zero OOB fill.  The swizzle must
+// match the descriptor layout the MMA reads the tile with.
+inline bool make_map_box(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+                         int64_t ld, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  const cuuint32_t box[2] = {32, box_outer};
+  const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// Box {32, box_outer}: one 128-byte row of f32 per box row.
+inline bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, int64_t ld,
+                     uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  return make_map_box(map, base, inner, outer, ld, 32u, box_outer, swizzle);
 }
 
 }  // namespace etb
