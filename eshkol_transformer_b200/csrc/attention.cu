@@ -486,22 +486,24 @@ void launch_bwd(const AttnParams& p, AttnTensor dout, const float* m, const floa
 
 }  // namespace
 
-void attention_forward(const AttnParams& p, AttnOut o, float* row_max, float* row_sum,
+bool attention_forward(const AttnParams& p, AttnOut o, float* row_max, float* row_sum,
                        cudaStream_t stream) {
-  if (p.B == 0 || p.Hq == 0 || p.Tq == 0) return;
-  if (attention_forward_tc(p, o, row_max, row_sum, stream)) return;
+  if (p.B == 0 || p.Hq == 0 || p.Tq == 0) return false;
+  if (attention_forward_tc(p, o, row_max, row_sum, stream)) return true;
   const int qb = p.q_rope_batched, kb = p.k_rope_batched;
   if (p.Dh <= 32) launch_fwd<32>(p, o, row_max, row_sum, qb, kb, stream);
   else if (p.Dh <= 64) launch_fwd<64>(p, o, row_max, row_sum, qb, kb, stream);
   else launch_fwd<128>(p, o, row_max, row_sum, qb, kb, stream);
+  return false;
 }
 
-void attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
+bool attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
                         const float* row_max,
                         const float* row_sum, float* delta, AttnOut dq, AttnOut dk, AttnOut dv,
                         cudaStream_t stream) {
-  if (p.B == 0 || p.Hq == 0) return;
-  if (attention_backward_tc(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream)) return;
+  if (p.B == 0 || p.Hq == 0) return false;
+  if (attention_backward_tc(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream))
+    return true;
   const int64_t rows = (int64_t)p.B * p.Hq * p.Tq;
   if (rows > 0) {
     attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p, o, o_lo, dout, delta);
@@ -511,6 +513,7 @@ void attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, At
   if (p.Dh <= 32) launch_bwd<32>(p, dout, row_max, row_sum, delta, dq, dk, dv, qb, kb, stream);
   else if (p.Dh <= 64) launch_bwd<64>(p, dout, row_max, row_sum, delta, dq, dk, dv, qb, kb, stream);
   else launch_bwd<128>(p, dout, row_max, row_sum, delta, dq, dk, dv, qb, kb, stream);
+  return false;
 }
 
 }  // namespace etb

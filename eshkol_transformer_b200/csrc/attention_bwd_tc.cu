@@ -466,35 +466,42 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
     }
     ok = __all_sync(0xffffffffu, ok);
     // warps 0-3: dK (scale, RoPE backward), warps 4-7: dV, staged in the
-    // free operand buffers and written out with coalesced stores
-    const uint32_t stage = base + L::QK + (uint32_t)(khalf * 128 * (DH + 4) * 4);
-    if (ok) {
-      tc_fence_after();
-      const float* ct = khalf == 0 ? p.k_cos : nullptr;
-      const float* sn = khalf == 0 ? p.k_sin : nullptr;
-      const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + tk : tk) * (DH / 2);
+    // free operand buffers and written out with coalesced stores; with .lo
+    // outputs the TF32 hi parts go first, then the residuals
+    const uint32_t stage = base + (uint32_t)(khalf * 128 * (DH + 4) * 4);
+    const int parts = (dk.lo != nullptr && dv.lo != nullptr) ? 2 : 1;
+    for (int part = 0; part < parts; part++) {
+      if (ok) {
+        tc_fence_after();
+        const float* ct = khalf == 0 ? p.k_cos : nullptr;
+        const float* sn = khalf == 0 ? p.k_sin : nullptr;
+        const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + tk : tk) * (DH / 2);
 #pragma unroll
-      for (int c = 0; c < DH / 32; c++) {
-        float v[32];
-        if (n_it > 0) {
-          tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
-        } else {
+        for (int c = 0; c < DH / 32; c++) {
+          float v[32];
+          if (n_it > 0) {
+            tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = 0.0f;
+            for (int i = 0; i < 32; i++) v[i] = 0.0f;
+          }
+          grad_row<32>(v, 0, khalf == 0 ? p.scale : 1.0f, ct, sn, trw, 32 * c);
+          if (parts == 2) split_part(v, part);
+          stage_row32(stage, DH, row, 32 * c, v, 0, 32);
         }
-        grad_row<32>(v, 0, khalf == 0 ? p.scale : 1.0f, ct, sn, trw, 32 * c);
-        stage_row32(stage, DH, row, 32 * c, v, 0, 32);
       }
-    }
-    named_sync(1, SOFT);
-    if (ok) {
-      const int rows = min(BK, p.Tk - k0);
-      for (int t = 0; t < 2; t++) {
-        const AttnOut& out = t == 0 ? dk : dv;
-        store_staged_rows(base + L::QK + (uint32_t)(t * 128 * (DH + 4) * 4), DH, rows,
-                          out.ptr + b * out.sb + hkv * out.sh + (int64_t)k0 * out.st, out.st, tid,
-                          SOFT);
+      named_sync(1, SOFT);
+      if (ok) {
+        const int rows = min(BK, p.Tk - k0);
+        for (int t = 0; t < 2; t++) {
+          const AttnOut& out = t == 0 ? dk : dv;
+          float* dst = part == 0 ? out.ptr : out.lo;
+          store_staged_rows(base + (uint32_t)(t * 128 * (DH + 4) * 4), DH, rows,
+                            dst + b * out.sb + hkv * out.sh + (int64_t)k0 * out.st, out.st, tid,
+                            SOFT);
+        }
       }
+      named_sync(1, SOFT);
     }
   }
   tc_fence_before();
@@ -773,47 +780,57 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
       if (ok) ok = role_wait(B_(QB_DONE), last, a.error, abort);
     }
     ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      tc_fence_after();
-      const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + tq : tq) * (DH / 2);
-      auto load_dq = [&](int col, float (&v)[32]) {
-        if (nkb > 0) {
-          float w[32];
-          tmem_ld32(trow + L::DQA + col, v);
-          tmem_ld32(trow + L::DQB + col, w);
+    const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + tq : tq) * (DH / 2);
+    auto load_dq = [&](int col, float (&v)[32]) {
+      if (nkb > 0) {
+        float w[32];
+        tmem_ld32(trow + L::DQA + col, v);
+        tmem_ld32(trow + L::DQB + col, w);
 #pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = v[i] + w[i];
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = 0.0f;
-        }
-      };
-      // dQ rows staged in the free K/V stages, written out with coalesced stores
-      if constexpr (DH >= 64) {
-#pragma unroll
-        for (int c = 0; c < DH / 64; c++) {
-          const int col = khalf * (DH / 2) + 32 * c;
-          float v[32];
-          load_dq(col, v);
-          grad_row<32>(v, 0, p.scale, p.q_cos, p.q_sin, trw, col);
-          stage_row32(base, DH, row, col, v, 0, 32);
-        }
+        for (int i = 0; i < 32; i++) v[i] = v[i] + w[i];
       } else {
-        float v[32];
-        load_dq(0, v);
-        if (khalf == 0) {
-          grad_row<16>(v, 0, p.scale, p.q_cos, p.q_sin, trw, 0);
-          stage_row32(base, DH, row, 0, v, 0, 16);
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = 0.0f;
+      }
+    };
+    // dQ rows staged in the free K/V stages, written out with coalesced
+    // stores; with dq.lo the TF32 hi part first, then the residual
+    const int parts = dq.lo != nullptr ? 2 : 1;
+    for (int part = 0; part < parts; part++) {
+      if (ok) {
+        tc_fence_after();
+        if constexpr (DH >= 64) {
+#pragma unroll
+          for (int c = 0; c < DH / 64; c++) {
+            const int col = khalf * (DH / 2) + 32 * c;
+            float v[32];
+            load_dq(col, v);
+            grad_row<32>(v, 0, p.scale, p.q_cos, p.q_sin, trw, col);
+            if (parts == 2) split_part(v, part);
+            stage_row32(base, DH, row, col, v, 0, 32);
+          }
         } else {
-          grad_row<16>(v, 16, p.scale, p.q_cos, p.q_sin, trw, 16);
-          stage_row32(base, DH, row, 16, v, 16, 16);
+          float v[32];
+          load_dq(0, v);
+          if (khalf == 0) {
+            grad_row<16>(v, 0, p.scale, p.q_cos, p.q_sin, trw, 0);
+            if (parts == 2) split_part(v, part);
+            stage_row32(base, DH, row, 0, v, 0, 16);
+          } else {
+            grad_row<16>(v, 16, p.scale, p.q_cos, p.q_sin, trw, 16);
+            if (parts == 2) split_part(v, part);
+            stage_row32(base, DH, row, 16, v, 16, 16);
+          }
         }
       }
+      named_sync(1, SOFT);
+      if (ok) {
+        float* dst = part == 0 ? dq.ptr : dq.lo;
+        store_staged_rows(base, DH, min(QM, p.Tq - q0),
+                          dst + b * dq.sb + hq * dq.sh + (int64_t)q0 * dq.st, dq.st, tid, SOFT);
+      }
+      named_sync(1, SOFT);
     }
-    named_sync(1, SOFT);
-    if (ok)
-      store_staged_rows(base, DH, min(QM, p.Tq - q0),
-                        dq.ptr + b * dq.sb + hq * dq.sh + (int64_t)q0 * dq.st, dq.st, tid, SOFT);
   }
   tc_fence_before();
   __syncthreads();
@@ -846,7 +863,7 @@ bool launch_bwd_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTen
                make_map(&vkh, w.vh, DH, krows, DH, KN, SW) && make_map(&vkl, w.vl, DH, krows, DH, KN, SW) &&
                make_map(&kmh, w.kh, DH, krows, DH, KN, SW32) && make_map(&kml, w.kl, DH, krows, DH, KN, SW32);
   if (!built) return false;
-  attention_prepare_qkv(p, w, stream);
+  if (!p.ws_ready) attention_prepare_qkv(p, w, stream);
   attn_bwd_prepare_kernel<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(
       p, o, o_lo, dout, row_max, row_sum, delta, w.lse2, w.doh, w.dol);
   count_launch();
@@ -871,7 +888,7 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
                            const float* row_max, const float* row_sum, float* delta, AttnOut dq,
                            AttnOut dk, AttnOut dv, cudaStream_t stream) {
   if (p.ws == nullptr || encode_fn() == nullptr || p.Tq == 0 || p.Tk == 0) return false;
-  if (reinterpret_cast<uintptr_t>(p.ws) & 15) return false;
+  if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
   switch (p.Dh) {
     case 32:
       return launch_bwd_tc<32>(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream);

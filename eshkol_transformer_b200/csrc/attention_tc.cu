@@ -406,33 +406,42 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
       row_max[ri] = empty ? 0.0f : m_used * kLn2;
       row_sum[ri] = empty ? 0.0f : lsum;
     }
-    // O / l staged in the free stages, written out with coalesced stores
+    // O / l staged in the free stages, written out with coalesced stores; with
+    // o.lo the TF32 hi part goes to o and the residual to o.lo (two rounds)
     const uint32_t stage = base;
-    if (ok) {
-      tc_fence_after();
-      if constexpr (DH >= 64) {
+    const int parts = o.lo != nullptr ? 2 : 1;
+    for (int part = 0; part < parts; part++) {
+      if (ok) {
+        tc_fence_after();
+        if constexpr (DH >= 64) {
 #pragma unroll
-        for (int c = 0; c < DH / 64; c++) {
-          const int col = khalf * (DH / 2) + 32 * c;
+          for (int c = 0; c < DH / 64; c++) {
+            const int col = khalf * (DH / 2) + 32 * c;
+            float ov[32];
+            if (nkb > 0) tmem_ld32(trow + L::O + col, ov);
+#pragma unroll
+            for (int i = 0; i < 32; i++) ov[i] = (empty || nkb == 0) ? 0.0f : rn_div(ov[i], lsum);
+            if (parts == 2) split_part(ov, part);
+            stage_row32(stage, DH, row, col, ov, 0, 32);
+          }
+        } else {
           float ov[32];
-          if (nkb > 0) tmem_ld32(trow + L::O + col, ov);
+          if (nkb > 0) tmem_ld32(trow + L::O, ov);
 #pragma unroll
           for (int i = 0; i < 32; i++) ov[i] = (empty || nkb == 0) ? 0.0f : rn_div(ov[i], lsum);
-          stage_row32(stage, DH, row, col, ov, 0, 32);
+          if (parts == 2) split_part(ov, part);
+          if (khalf == 0) stage_row32(stage, DH, row, 0, ov, 0, 16);
+          else stage_row32(stage, DH, row, 16, ov, 16, 16);
         }
-      } else {
-        float ov[32];
-        if (nkb > 0) tmem_ld32(trow + L::O, ov);
-#pragma unroll
-        for (int i = 0; i < 32; i++) ov[i] = (empty || nkb == 0) ? 0.0f : rn_div(ov[i], lsum);
-        if (khalf == 0) stage_row32(stage, DH, row, 0, ov, 0, 16);
-        else stage_row32(stage, DH, row, 16, ov, 16, 16);
       }
+      named_sync(1, SOFT);
+      if (ok) {
+        float* dst = part == 0 ? o.ptr : o.lo;
+        store_staged_rows(stage, DH, min(QM, p.Tq - q0),
+                          dst + b * o.sb + hq * o.sh + (int64_t)q0 * o.st, o.st, tid, SOFT);
+      }
+      named_sync(1, SOFT);  // the stage is rewritten by the next round
     }
-    named_sync(1, SOFT);
-    if (ok)
-      store_staged_rows(stage, DH, min(QM, p.Tq - q0),
-                        o.ptr + b * o.sb + hq * o.sh + (int64_t)q0 * o.st, o.st, tid, SOFT);
   }
   tc_fence_before();
   __syncthreads();
@@ -484,10 +493,16 @@ void attention_prepare_qkv(const AttnParams& p, const AttnWs& w, cudaStream_t st
   count_launch(3);
 }
 
-size_t attention_workspace_floats(const AttnParams& p) {
+size_t attention_qkv_workspace_floats(const AttnParams& p) {
   const size_t nq = (size_t)p.B * p.Hq * p.Tq * p.Dh, nk = (size_t)p.B * p.Hkv * p.Tk * p.Dh;
-  const size_t rows = (size_t)p.B * p.Hq * p.Tq;
-  return 4 * nq + 4 * nk + rows + 64;
+  return 2 * nq + 4 * nk;
+}
+size_t attention_grad_workspace_floats(const AttnParams& p) {
+  const size_t nq = (size_t)p.B * p.Hq * p.Tq * p.Dh, rows = (size_t)p.B * p.Hq * p.Tq;
+  return 2 * nq + rows + 64;
+}
+size_t attention_workspace_floats(const AttnParams& p) {
+  return attention_qkv_workspace_floats(p) + attention_grad_workspace_floats(p);
 }
 
 bool attention_forward_tc(const AttnParams& p, AttnOut o, float* row_max, float* row_sum,

@@ -28,7 +28,7 @@ inline AttnWs attn_ws(const AttnParams& p) {
   w.kl = w.kh + nk;
   w.vh = w.kl + nk;
   w.vl = w.vh + nk;
-  w.doh = w.vl + nk;
+  w.doh = p.ws_grad != nullptr ? p.ws_grad : w.vl + nk;
   w.dol = w.doh + nq;
   w.lse2 = w.dol + nq;
   return w;
@@ -166,6 +166,18 @@ __device__ __forceinline__ int warp_count(const int64_t* a, int n, int64_t x, bo
   const bool in = idx < hi;
   const int64_t v = in ? a[idx] : 0;
   return lo + __popc(__ballot_sync(0xffffffffu, in && (le ? v <= x : v < x)));
+}
+
+// Part `part` of a 3xTF32 operand pair: the TF32 hi value (part 0) or the
+// residual (part 1) of every element, in place.
+template <int N>
+__device__ __forceinline__ void split_part(float (&v)[N], int part) {
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    float h, l;
+    tf32_split(v[i], h, l);
+    v[i] = part == 0 ? h : l;
+  }
 }
 
 // Named barrier over the first `threads` threads (warps 0..threads/32-1).

@@ -51,6 +51,19 @@ __device__ __forceinline__ float rn_mul(float a, float b) { return __fmul_rn(a, 
 __device__ __forceinline__ float rn_div(float a, float b) { return __fdiv_rn(a, b); }
 __device__ __forceinline__ float rn_sqrt(float a) { return __fsqrt_rn(a); }
 
+// v = hi + lo exactly, hi = v rounded to the nearest TF32 value (10 explicit
+// mantissa bits; magnitudes that would round up to infinity are truncated
+// instead), the operand pair of the 3xTF32 tensor-core GEMMs.
+__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
+  uint32_t b = __float_as_uint(v);
+  if ((b & 0x7f800000u) != 0x7f800000u) {
+    const uint32_t r = (b + 0x1000u) & 0xffffe000u;
+    b = ((r & 0x7f800000u) == 0x7f800000u) ? (b & 0xffffe000u) : r;
+  }
+  hi = __uint_as_float(b);
+  lo = v - hi;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

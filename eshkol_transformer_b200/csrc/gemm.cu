@@ -144,6 +144,11 @@ struct TcArgs {
   int accumulate;
   int a_mn, b_mn;
   int tiles_m, tiles_n;
+  // split-K: work unit u covers tile u % tiles over K blocks
+  // [s * kb_per_split, min(nkb, (s + 1) * kb_per_split)), s = u / tiles, and
+  // writes its raw sum to partial + s * M * N (row stride N)
+  int splits, kb_per_split;
+  float* partial;
   int* error;
 };
 
@@ -214,6 +219,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
 
   const int nkb = (args.K + BK - 1) / BK;
   const int tiles = args.tiles_m * args.tiles_n;
+  const int units = tiles * args.splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -224,11 +230,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       uint32_t armed = 0;  // bitmask of stages with an armed phase in flight
       uint32_t armed_phase[STAGES];
       for (int s = 0; s < STAGES; s++) armed_phase[s] = 0;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x) {
+        const int tile = unit % tiles, split = unit / tiles;
         int tm, tn;
         raster(tile, args.tiles_m, args.tiles_n, tm, tn);
         const int m0 = tm * TC_BM, n0 = tn * BN;
-        for (int kb = 0; kb < nkb; kb++) {
+        const int kb_end = min(nkb, (split + 1) * args.kb_per_split);
+        for (int kb = split * args.kb_per_split; kb < kb_end; kb++) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, args.error)) { ok = false; break; }
           const uint32_t full = full0 + 8 * stage;
           mbar_expect_tx(full, L::STAGE_BYTES);
@@ -274,11 +282,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x) {
+        const int split = unit / tiles;
         if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, args.error)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < nkb; kb++) {
+        const int kb_begin = split * args.kb_per_split;
+        const int kb_end = min(nkb, kb_begin + args.kb_per_split);
+        for (int kb = kb_begin; kb < kb_end; kb++) {
           if (!mbar_wait(full0 + 8 * stage, phase, args.error)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
@@ -287,7 +298,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
           for (int j = 0; j < BK / 8; j++) {
             const uint64_t a = tile_desc<BK>(sa, args.a_mn, j);
             const uint64_t b = tile_desc<BK>(sb, args.b_mn, j);
-            umma_tf32(d_tmem, a, b, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+            umma_tf32(d_tmem, a, b, idesc, (kb > kb_begin || j > 0) ? 1u : 0u);
             if (THREE) {
               const uint32_t lo = L::A_BYTES + L::B_BYTES;
               const uint64_t alo = tile_desc<BK>(sa + lo, args.a_mn, j);
@@ -309,7 +320,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     const int lane_base = 32 * (warp & 3);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+      const int tile = unit % tiles, split = unit / tiles;
       // one lane observes the phase; the warp stays converged for tcgen05.ld
       int ok = 1;
       if (lane == 0) ok = mbar_wait(tfull0 + 8 * acc, acc_phase, args.error) ? 1 : 0;
@@ -321,8 +333,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       raster(tile, args.tiles_m, args.tiles_n, tm, tn);
       const int m = tm * TC_BM + lane_base + lane;
       const int n_tile = tn * BN;
-      float* crow = args.C + (int64_t)m * args.ldc;
-      const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0);
+      // split-K units write their raw sum to their partial buffer
+      const bool part = args.splits > 1;
+      float* cbase = part ? args.partial + (int64_t)split * args.M * args.N : args.C;
+      const int64_t ldc = part ? (int64_t)args.N : args.ldc;
+      const float* bias = part ? nullptr : args.bias;
+      const int accumulate = part ? 0 : args.accumulate;
+      float* crow = cbase + (int64_t)m * ldc;
+      const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
@@ -333,14 +351,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
               float4 r = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-              if (args.bias) {
-                r.x += args.bias[n0 + i];
-                r.y += args.bias[n0 + i + 1];
-                r.z += args.bias[n0 + i + 2];
-                r.w += args.bias[n0 + i + 3];
+              if (bias) {
+                r.x += bias[n0 + i];
+                r.y += bias[n0 + i + 1];
+                r.z += bias[n0 + i + 2];
+                r.w += bias[n0 + i + 3];
               }
               float4* dst = reinterpret_cast<float4*>(crow + n0 + i);
-              if (args.accumulate) {
+              if (accumulate) {
                 const float4 o = *dst;
                 r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
               }
@@ -351,8 +369,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
               const int n = n0 + i;
               if (n >= args.N) break;
               float r = v[i];
-              if (args.bias) r += args.bias[n];
-              if (args.accumulate) r += crow[n];
+              if (bias) r += bias[n];
+              if (accumulate) r += crow[n];
               crow[n] = r;
             }
           }
@@ -390,6 +408,42 @@ bool operand_map(CUtensorMap* map, const float* p, bool kmajor, int rows, int K,
                       CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
+// C = (accumulate ? C : 0) + bias + sum over s of partial[s] (s ascending).
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
+                                     float* __restrict__ C, int64_t ldc,
+                                     const float* __restrict__ bias, int accumulate) {
+  const int64_t total = (int64_t)M * N;
+  const int64_t plane = total;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / N), n = (int)(i - (int64_t)m * N);
+    float acc = partial[i];
+    for (int s = 1; s < splits; s++) acc += partial[(int64_t)s * plane + i];
+    float* c = C + (int64_t)m * ldc + n;
+    if (bias) acc += bias[n];
+    if (accumulate) acc += *c;
+    *c = acc;
+  }
+}
+
+// Splits that best fill whole waves of the GPU for `tiles` output tiles and
+// nkb K blocks (each split keeps at least 32 K blocks); 1 when the tiles fill
+// the GPU well already.
+int choose_splits(int tiles, int nkb, int sms) {
+  auto fill = [&](int s) {
+    const int u = tiles * s;
+    return (double)u / (double)(((u + sms - 1) / sms) * sms);
+  };
+  int best = 1;
+  double best_fill = fill(1);
+  if (tiles >= 4 * sms || best_fill >= 0.9) return 1;
+  for (int s = 2; s <= 16 && nkb / s >= 32; s++) {
+    const double f = fill(s);
+    if (f > best_fill + 0.02) { best = s; best_fill = f; }
+  }
+  return best;
+}
+
 template <int BN, int STAGES, bool THREE, int BK>
 void launch_tc(const GemmArgs& g, cudaStream_t stream) {
   using L = TcLayout<BN, STAGES, THREE, BK>;
@@ -418,10 +472,30 @@ void launch_tc(const GemmArgs& g, cudaStream_t stream) {
   a.tiles_n = (g.N + BN - 1) / BN;
   a.error = device_error_word();
   const int tiles = a.tiles_m * a.tiles_n;
-  const int grid = tiles < sm_count() ? tiles : sm_count();
+  const int nkb = (g.K + BK - 1) / BK;
+  a.splits = 1;
+  a.kb_per_split = nkb;
+  a.partial = nullptr;
+  const int s = choose_splits(tiles, nkb, sm_count());
+  if (s > 1 && g.workspace != nullptr &&
+      g.workspace_floats >= (size_t)s * (size_t)g.M * (size_t)g.N) {
+    a.kb_per_split = (nkb + s - 1) / s;
+    a.splits = (nkb + a.kb_per_split - 1) / a.kb_per_split;
+    a.partial = g.workspace;
+  }
+  const int units = tiles * a.splits;
+  const int grid = units < sm_count() ? units : sm_count();
   gemm_tc_kernel<BN, STAGES, THREE, BK><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(
       ta, ta_lo, tb, tb_lo, a);
   count_launch();
+  if (a.splits > 1) {
+    const int64_t total = (int64_t)g.M * g.N;
+    const int64_t want = (total + 255) / 256;
+    const int blocks = (int)(want < (int64_t)sm_count() * 16 ? want : (int64_t)sm_count() * 16);
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(a.partial, a.splits, g.M, g.N, g.C, g.ldc,
+                                                      g.bias, g.accumulate ? 1 : 0);
+    count_launch();
+  }
 }
 
 }  // namespace
@@ -432,6 +506,8 @@ void gemm_simt(const GemmArgs& g, cudaStream_t stream) {
   gemm_simt_kernel<<<grid, 256, 0, stream>>>(g);
   count_launch();
 }
+
+size_t gemm_splitk_floats(int M, int N) { return (size_t)16 * (size_t)M * (size_t)N; }
 
 bool gemm_tc_supported(const GemmArgs& g) {
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };

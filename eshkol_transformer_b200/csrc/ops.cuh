@@ -12,9 +12,12 @@ namespace etb {
 // u_r (softmax(x) - onehot(t)) with u_r = upstream[r] (or upstream_scale when
 // upstream is null).  dlogits may alias logits.  status[0] is set to 1 when a
 // target is outside [0, V).
+// With dlogits_lo, dlogits receives the TF32 hi part and dlogits_lo the
+// residual (the 3xTF32 operand pair) instead of the f32 gradient.
 void ce_fused(const float* logits, float* dlogits, const int64_t* targets,
               const float* upstream, float upstream_scale, float* loss,
-              size_t rows, size_t V, int* status, cudaStream_t stream);
+              size_t rows, size_t V, int* status, cudaStream_t stream,
+              float* dlogits_lo = nullptr);
 // Mean of loss[rows] as one f32 (fixed-order tree in f64).
 void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream);
 
@@ -44,20 +47,24 @@ void grad_sumsq(const AdamwTensor* tensors, const uint64_t* prefix,
                 int* status, cudaStream_t stream);
 
 // ---------------------------------------------------------------- N2 family
+// With y_lo, y receives the TF32 hi part of the output and y_lo the residual.
 void layer_norm_forward(const float* x, const float* gamma, const float* beta,
                         float epsilon, float* y, float* mean, float* rstd,
-                        size_t rows, size_t d, cudaStream_t stream);
+                        size_t rows, size_t d, cudaStream_t stream, float* y_lo = nullptr);
 // dx = (accumulate ? dx : 0) + LN'(dy); dgamma/dbeta over all rows via a
 // fixed-order two-stage column reduction in `workspace` (>= ln_workspace()).
 size_t ln_workspace_floats(size_t rows, size_t d);
+// With dx_hi/dx_lo, the final dx is also written as a 3xTF32 operand pair.
 void layer_norm_backward(const float* x, const float* gamma, const float* mean,
                          const float* rstd, const float* dy, float* dx,
                          int accumulate, float* dgamma, float* dbeta,
                          float* workspace, size_t rows, size_t d,
-                         cudaStream_t stream);
-void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream);
+                         cudaStream_t stream, float* dx_hi = nullptr, float* dx_lo = nullptr);
+// With a lo output, the result is written as TF32 hi (y / dx) plus residual.
+void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream,
+                  float* y_lo = nullptr);
 void gelu_backward(const float* x, const float* dy, float* dx, size_t count,
-                   cudaStream_t stream);
+                   cudaStream_t stream, float* dx_lo = nullptr);
 void relu_forward(const float* x, float* y, size_t count, cudaStream_t stream);
 void relu_backward(const float* x, const float* dy, float* dx, size_t count,
                    cudaStream_t stream);
@@ -77,8 +84,9 @@ void embedding_backward(const int64_t* ids, const float* dy, const float* base,
                         void* scratch, cudaStream_t stream);
 // out[n] = sum over rows of dy[r, n] (fixed-order two-stage).
 size_t colsum_workspace_floats(size_t rows, size_t n);
+// dy_lo (optional) is added to dy element by element first (hi + lo is exact).
 void column_sum(const float* dy, float* out, size_t rows, size_t n,
-                float* workspace, cudaStream_t stream);
+                float* workspace, cudaStream_t stream, const float* dy_lo = nullptr);
 // 3xTF32 operand split: hi = x rounded to the nearest TF32 value (exactly
 // representable, low 13 mantissa bits zero) and lo = x - hi (exact, at most
 // 2^-11 |x|).  hi may alias x.
@@ -101,6 +109,9 @@ struct AttnTensor {
 struct AttnOut {
   float* ptr;
   int64_t sb, sh, st;
+  // optional: when set (same strides as ptr), ptr receives the TF32 hi part
+  // and lo the residual (a 3xTF32 operand pair); tensor-core kernels only
+  float* lo;
 };
 struct AttnParams {
   int B, Hq, Hkv, Tq, Tk, Dh;
@@ -119,13 +130,23 @@ struct AttnParams {
   // by every sequence (row t).
   int q_rope_batched, k_rope_batched;
   // optional device workspace of attention_workspace_floats(p) floats, 16-byte
-  // aligned; the tensor-core forward needs it (null = SIMT forward).
+  // aligned; the tensor-core kernels need it (null = SIMT kernels).  With
+  // ws_grad set, the backward's dO / statistics part lives there instead
+  // (attention_grad_workspace_floats) and ws needs only the Q/K/V part
+  // (attention_qkv_workspace_floats).  ws_ready: ws already holds this
+  // call's prepared Q/K/V (written by its forward), so the backward skips
+  // that pass.
   float* ws;
+  float* ws_grad;
+  int ws_ready;
 };
 size_t attention_workspace_floats(const AttnParams& p);
+size_t attention_qkv_workspace_floats(const AttnParams& p);
+size_t attention_grad_workspace_floats(const AttnParams& p);
 // Forward: o and per-row statistics m (row max of scaled scores) and l (sum
 // of exp(s - m)); rows with no admitted key produce o = 0, m = 0, l = 0.
-void attention_forward(const AttnParams& p, AttnOut o, float* row_max,
+// Returns true when the tensor-core path ran (and so prepared p.ws).
+bool attention_forward(const AttnParams& p, AttnOut o, float* row_max,
                        float* row_sum, cudaStream_t stream);
 // The tcgen05 forward (attention_tc.cu); false when the shape or layout is
 // outside it (Dh not 32/64/128, strides TMA cannot describe), nothing launched.
@@ -134,7 +155,8 @@ bool attention_forward_tc(const AttnParams& p, AttnOut o, float* row_max,
 // Backward: dq/dk/dv (RoPE backward applied to dq/dk when tables are set).
 // delta[B*Hq*Tq] is scratch for rowsum(dO * O); when o_lo is given (same
 // strides as o) the forward output is o + o_lo (a 3xTF32 hi/lo pair).
-void attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
+// Returns true when the tensor-core path ran (the only one writing lo outputs).
+bool attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
                         const float* row_max, const float* row_sum,
                         float* delta, AttnOut dq, AttnOut dk, AttnOut dv,
                         cudaStream_t stream);
@@ -164,7 +186,14 @@ struct GemmArgs {
   int64_t ldc;
   const float* bias;
   bool accumulate;
+  // optional scratch for split-K: when the output has too few tiles to fill
+  // the GPU and K is long, the K range is split across CTAs into partial
+  // [M, N] sums here, then reduced in a fixed order (gemm_splitk_floats).
+  float* workspace;
+  size_t workspace_floats;
 };
+// Scratch floats split-K may use for an M x N output.
+size_t gemm_splitk_floats(int M, int N);
 void gemm(const GemmArgs& g, int precision, cudaStream_t stream);
 // True when the tensor-core path accepts this problem (alignment / shape);
 // otherwise gemm() uses the FFMA path.

@@ -33,7 +33,7 @@ __global__ void __launch_bounds__(kCeThreads)
 ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
                 const int64_t* __restrict__ targets,
                 const float* __restrict__ upstream, float upstream_scale,
-                float* __restrict__ loss, int64_t V, int* status) {
+                float* __restrict__ loss, int64_t V, int* status, float* __restrict__ dlo) {
   __shared__ float red_m[32];
   __shared__ float red_s[32];
   const int64_t row = blockIdx.x;
@@ -81,12 +81,22 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
       r.y = u * (rn_div(expf(v.y - row_max), row_sum) - (j + 1 == target ? 1.0f : 0.0f));
       r.z = u * (rn_div(expf(v.z - row_max), row_sum) - (j + 2 == target ? 1.0f : 0.0f));
       r.w = u * (rn_div(expf(v.w - row_max), row_sum) - (j + 3 == target ? 1.0f : 0.0f));
+      if (dlo != nullptr) {
+        float4 l;
+        tf32_split(r.x, r.x, l.x);
+        tf32_split(r.y, r.y, l.y);
+        tf32_split(r.z, r.z, l.z);
+        tf32_split(r.w, r.w, l.w);
+        reinterpret_cast<float4*>(dlo + row * V)[i] = l;
+      }
       g4[i] = r;
     }
   } else {
     for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
       const float v = x[j];
-      g[j] = u * (rn_div(expf(v - row_max), row_sum) - (j == target ? 1.0f : 0.0f));
+      float r = u * (rn_div(expf(v - row_max), row_sum) - (j == target ? 1.0f : 0.0f));
+      if (dlo != nullptr) tf32_split(r, r, dlo[row * V + j]);
+      g[j] = r;
     }
   }
 }
@@ -189,10 +199,11 @@ __global__ void sum_partials_kernel(const double* partials, int count, double* o
 
 void ce_fused(const float* logits, float* dlogits, const int64_t* targets,
               const float* upstream, float upstream_scale, float* loss,
-              size_t rows, size_t V, int* status, cudaStream_t stream) {
+              size_t rows, size_t V, int* status, cudaStream_t stream, float* dlogits_lo) {
   if (rows == 0) return;
   ce_fused_kernel<<<(unsigned)rows, kCeThreads, 0, stream>>>(
-      logits, dlogits, targets, upstream, upstream_scale, loss, (int64_t)V, status);
+      logits, dlogits, targets, upstream, upstream_scale, loss, (int64_t)V, status,
+      dlogits ? dlogits_lo : nullptr);
   count_launch();
 }
 

@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(kLnWarps * 32)
 ln_forward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                   const float* __restrict__ beta, float epsilon, float* __restrict__ y,
                   float* __restrict__ mean_out, float* __restrict__ rstd_out,
-                  int64_t rows, int64_t d) {
+                  int64_t rows, int64_t d, float* __restrict__ y_lo) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -45,7 +45,9 @@ ln_forward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
   float* yr = y + row * d;
   for (int64_t j = lane; j < d; j += 32) {
     const float normalized = rn_mul(rn_sub(xr[j], mean), rstd);
-    yr[j] = rn_add(rn_mul(normalized, gamma[j]), beta[j]);
+    float val = rn_add(rn_mul(normalized, gamma[j]), beta[j]);
+    if (y_lo != nullptr) tf32_split(val, val, y_lo[row * d + j]);
+    yr[j] = val;
   }
   if (lane == 0) {
     if (mean_out) mean_out[row] = mean;
@@ -68,7 +70,8 @@ __global__ void __launch_bounds__(kLnWarps * 32)
 ln_backward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                    const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                    const float* __restrict__ dy, float* __restrict__ dx, int accumulate,
-                   float* __restrict__ partial, int64_t rows, int64_t d) {
+                   float* __restrict__ partial, int64_t rows, int64_t d,
+                   float* __restrict__ dx_hi, float* __restrict__ dx_lo) {
   extern __shared__ float sm[];  // [kLnWarps][2][d]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* pg = sm + (size_t)warp * 2 * d;
@@ -98,7 +101,9 @@ ln_backward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
       const float n = rn_mul(rn_sub(xr[j], mean), rstd);
       const float h = rn_mul(gr[j], gamma[j]);
       const float val = rn_mul(factor, rn_sub(rn_sub(rn_mul(dim, h), sh), rn_mul(n, shn)));
-      dr[j] = accumulate ? rn_add(dr[j], val) : val;
+      const float out = accumulate ? rn_add(dr[j], val) : val;
+      dr[j] = out;
+      if (dx_lo != nullptr) tf32_split(out, dx_hi[row * d + j], dx_lo[row * d + j]);
     }
   }
   __syncthreads();
@@ -128,18 +133,21 @@ __global__ void reduce_partials_kernel(const float* __restrict__ partial, int co
 
 // Exact-erf GELU with the reference's binary32 constants
 // (n2_primitives_provider.c:545-583).
-__global__ void gelu_forward_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+__global__ void gelu_forward_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n,
+                                    float* __restrict__ y_lo) {
   const float inv_sqrt_2 = 0x1.6a09e6p-1f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float v = x[i];
     const float e = erff(rn_mul(v, inv_sqrt_2));
-    y[i] = rn_mul(rn_mul(0.5f, v), rn_add(1.0f, e));
+    float r = rn_mul(rn_mul(0.5f, v), rn_add(1.0f, e));
+    if (y_lo != nullptr) tf32_split(r, r, y_lo[i]);
+    y[i] = r;
   }
 }
 
 __global__ void gelu_backward_kernel(const float* __restrict__ x, const float* __restrict__ dy,
-                                     float* __restrict__ dx, int64_t n) {
+                                     float* __restrict__ dx, int64_t n, float* __restrict__ dx_lo) {
   const float inv_sqrt_2 = 0x1.6a09e6p-1f, inv_sqrt_2pi = 0x1.988454p-2f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -147,7 +155,9 @@ __global__ void gelu_backward_kernel(const float* __restrict__ x, const float* _
     const float cdf = rn_mul(0.5f, rn_add(1.0f, erff(rn_mul(v, inv_sqrt_2))));
     const float density = rn_mul(expf(-rn_mul(0.5f, rn_mul(v, v))), inv_sqrt_2pi);
     const float slope = rn_add(cdf, rn_mul(v, density));
-    dx[i] = rn_mul(dy[i], slope);
+    float r = rn_mul(dy[i], slope);
+    if (dx_lo != nullptr) tf32_split(r, r, dx_lo[i]);
+    dx[i] = r;
   }
 }
 
@@ -262,8 +272,8 @@ __global__ void embedding_backward_kernel(const uint32_t* __restrict__ keys,
 
 constexpr int kColRowsChunk = 256;
 
-__global__ void colsum_partial_kernel(const float* __restrict__ dy, float* __restrict__ partial,
-                                      int64_t rows, int64_t n) {
+__global__ void colsum_partial_kernel(const float* __restrict__ dy, const float* __restrict__ dy_lo,
+                                      float* __restrict__ partial, int64_t rows, int64_t n) {
   __shared__ float sm[8][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t col = (int64_t)blockIdx.x * 32 + lane;
@@ -271,7 +281,8 @@ __global__ void colsum_partial_kernel(const float* __restrict__ dy, float* __res
   const int64_t r1 = min(rows, r0 + kColRowsChunk);
   float acc = 0.0f;
   if (col < n)
-    for (int64_t r = r0 + warp; r < r1; r += 8) acc += dy[r * n + col];
+    for (int64_t r = r0 + warp; r < r1; r += 8)
+      acc += dy_lo != nullptr ? dy[r * n + col] + dy_lo[r * n + col] : dy[r * n + col];
   sm[warp][lane] = acc;
   __syncthreads();
   if (warp == 0 && col < n) {
@@ -314,10 +325,10 @@ unsigned grid_for(int64_t n, int threads) {
 
 void layer_norm_forward(const float* x, const float* gamma, const float* beta, float epsilon,
                         float* y, float* mean, float* rstd, size_t rows, size_t d,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, float* y_lo) {
   if (rows == 0) return;
   ln_forward_kernel<<<ceil_div(rows, kLnWarps), kLnWarps * 32, 0, stream>>>(
-      x, gamma, beta, epsilon, y, mean, rstd, (int64_t)rows, (int64_t)d);
+      x, gamma, beta, epsilon, y, mean, rstd, (int64_t)rows, (int64_t)d, y_lo);
   count_launch();
 }
 
@@ -327,14 +338,16 @@ size_t ln_workspace_floats(size_t rows, size_t d) {
 
 void layer_norm_backward(const float* x, const float* gamma, const float* mean, const float* rstd,
                          const float* dy, float* dx, int accumulate, float* dgamma, float* dbeta,
-                         float* workspace, size_t rows, size_t d, cudaStream_t stream) {
+                         float* workspace, size_t rows, size_t d, cudaStream_t stream,
+                         float* dx_hi, float* dx_lo) {
   if (rows == 0) return;
   const int blocks = ln_backward_blocks(rows);
   const size_t smem = (size_t)kLnWarps * 2 * d * sizeof(float);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(ln_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   ln_backward_kernel<<<blocks, kLnWarps * 32, smem, stream>>>(
-      x, gamma, mean, rstd, dy, dx, accumulate, workspace, (int64_t)rows, (int64_t)d);
+      x, gamma, mean, rstd, dy, dx, accumulate, workspace, (int64_t)rows, (int64_t)d,
+      dx_lo ? dx_hi : nullptr, dx_lo);
   reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace, blocks, (int64_t)d,
                                                                (int64_t)(2 * d), dgamma);
   reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + d, blocks, (int64_t)d,
@@ -342,12 +355,13 @@ void layer_norm_backward(const float* x, const float* gamma, const float* mean, 
   count_launch(3);
 }
 
-void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream) {
-  gelu_forward_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, y, (int64_t)count);
+void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream, float* y_lo) {
+  gelu_forward_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, y, (int64_t)count, y_lo);
   count_launch();
 }
-void gelu_backward(const float* x, const float* dy, float* dx, size_t count, cudaStream_t stream) {
-  gelu_backward_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, dy, dx, (int64_t)count);
+void gelu_backward(const float* x, const float* dy, float* dx, size_t count, cudaStream_t stream,
+                   float* dx_lo) {
+  gelu_backward_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, dy, dx, (int64_t)count, dx_lo);
   count_launch();
 }
 void relu_forward(const float* x, float* y, size_t count, cudaStream_t stream) {
@@ -426,14 +440,14 @@ size_t colsum_workspace_floats(size_t rows, size_t n) {
 }
 
 void column_sum(const float* dy, float* out, size_t rows, size_t n, float* workspace,
-                cudaStream_t stream) {
+                cudaStream_t stream, const float* dy_lo) {
   const unsigned chunks = ceil_div(rows, kColRowsChunk);
   if (chunks == 0) {
     cudaMemsetAsync(out, 0, n * sizeof(float), stream);
     return;
   }
   dim3 grid(ceil_div(n, 32), chunks);
-  colsum_partial_kernel<<<grid, 256, 0, stream>>>(dy, workspace, (int64_t)rows, (int64_t)n);
+  colsum_partial_kernel<<<grid, 256, 0, stream>>>(dy, dy_lo, workspace, (int64_t)rows, (int64_t)n);
   reduce_partials_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(workspace, (int)chunks, (int64_t)n,
                                                                (int64_t)n, out);
   count_launch(2);

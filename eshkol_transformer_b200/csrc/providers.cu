@@ -381,12 +381,13 @@ void run_attention(Call& cl, const AttShape& s, bool backward, bool scratch,
   }
   const float* dout = (const float*)dev_in(cl, 6);
   float* o = (float*)P.alloc(rows * s.dh * 4);
-  attention_forward(p, AttnOut{o, qsb, qsh, (int64_t)s.dh}, m, l, P.stream);
+  const bool prepared = attention_forward(p, AttnOut{o, qsb, qsh, (int64_t)s.dh}, m, l, P.stream);
   float* dq = (float*)dev_out(cl, 0, scratch);
   float* dk = (float*)dev_out(cl, 1, scratch);
   float* dv = (float*)dev_out(cl, 2, scratch);
   outs = {dq, dk, dv};
   float* delta = (float*)P.alloc(rows * 4);
+  p.ws_ready = prepared ? 1 : 0;  // the forward above prepared Q/K/V in p.ws
   attention_backward(p, AttnTensor{o, qsb, qsh, (int64_t)s.dh}, nullptr,
                      AttnTensor{dout, qsb, qsh, (int64_t)s.dh}, m, l, delta,
                      AttnOut{dq, qsb, qsh, (int64_t)s.dh}, AttnOut{dk, kvsb, kvsh, (int64_t)s.dh},

@@ -83,7 +83,13 @@ struct et_b200_lm {
   // backward scratch
   float *dx = nullptr, *dxhi = nullptr, *dxlo = nullptr, *dtmp = nullptr, *dqkv = nullptr,
         *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *dg = nullptr, *delta = nullptr;
-  float *ln_ws = nullptr, *col_ws = nullptr, *attn_ws = nullptr;
+  float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr;
+  // attention: per-layer prepared Q/K/V (written by the forward, reused by
+  // the backward) and one shared backward scratch
+  std::vector<float*> attn_qkv_ws;
+  std::vector<char> attn_prepared;
+  float* attn_grad_ws = nullptr;
+  size_t splitk_floats = 0;
   void* emb_scratch = nullptr;
   int64_t *ids = nullptr, *targets = nullptr, *pos = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
@@ -216,16 +222,19 @@ void linear_backward_dw(et_b200_lm* lm, const float* dy, const float* dylo, cons
   g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = false;
   g.B = x; g.B_lo = xlo; g.ldb = din; g.b_kmajor = false;
   g.C = dw; g.ldc = din; g.bias = nullptr; g.accumulate = false;
+  g.workspace = lm->splitk_ws; g.workspace_floats = lm->splitk_floats;
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->precision, lm->stream);
 }
 
-void bias_grad(et_b200_lm* lm, const float* dy, int64_t rows, int64_t n, float* db) {
-  Mark mk(lm, P_ELEMENTWISE, 0, 4.0 * rows * n);
-  column_sum(dy, db, rows, n, lm->col_ws, lm->stream);
+// db = column sums of dy (+ dy_lo when dy holds only the TF32 hi part).
+void bias_grad(et_b200_lm* lm, const float* dy, int64_t rows, int64_t n, float* db,
+               const float* dy_lo = nullptr) {
+  Mark mk(lm, P_ELEMENTWISE, 0, (dy_lo ? 8.0 : 4.0) * rows * n);
+  column_sum(dy, db, rows, n, lm->col_ws, lm->stream, dy_lo);
 }
 
-AttnParams attn_params(et_b200_lm* lm, const float* qkv) {
+AttnParams attn_params(et_b200_lm* lm, const float* qkv, int layer) {
   AttnParams p{};
   p.B = (int)lm->B; p.Hq = (int)lm->H; p.Hkv = (int)lm->H;
   p.Tq = (int)lm->T; p.Tk = (int)lm->T; p.Dh = (int)lm->Dh;
@@ -238,7 +247,9 @@ AttnParams attn_params(et_b200_lm* lm, const float* qkv) {
   p.q_cos = lm->rope_cos; p.q_sin = lm->rope_sin;
   p.k_cos = lm->rope_cos; p.k_sin = lm->rope_sin;
   p.q_rope_batched = 0; p.k_rope_batched = 0;
-  p.ws = lm->attn_ws;
+  p.ws = lm->attn_qkv_ws[layer];
+  p.ws_grad = lm->attn_grad_ws;
+  p.ws_ready = 0;
   return p;
 }
 
@@ -261,18 +272,19 @@ void forward(et_b200_lm* lm) {
     float* xnext = (l + 1 < lm->L) ? lm->layers[l + 1].x : lm->x_final;
     {
       Mark mk(lm, P_NORM, 0, 8.0 * R * d);
+      // with 3xTF32 the producers write each GEMM operand as a hi/lo pair
       layer_norm_forward(a.x, lm->Pp(lm->lt(l, T_LN1G)), lm->Pp(lm->lt(l, T_LN1B)), lm->eps, a.h1,
-                         a.mu1, a.rs1, R, d, s);
+                         a.mu1, a.rs1, R, d, s, a.h1lo);
     }
-    if (lm->three) split(lm, a.h1, a.h1lo, R * d);
     linear_forward(lm, a.h1, a.h1lo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->Pp(lm->lt(l, T_BQKV)),
                    a.qkv);
     {
-      AttnParams p = attn_params(lm, a.qkv);
+      AttnParams p = attn_params(lm, a.qkv, l);
       Mark mk(lm, P_ATTN_FWD, attn_flop(lm, 2), 0);
-      attention_forward(p, AttnOut{a.ao, lm->T * d, lm->Dh, d}, a.am, a.al, s);
+      lm->attn_prepared[l] =
+          attention_forward(p, AttnOut{a.ao, lm->T * d, lm->Dh, d, a.aolo}, a.am, a.al, s);
     }
-    if (lm->three) split(lm, a.ao, a.aolo, R * d);
+    if (lm->three && !lm->attn_prepared[l]) split(lm, a.ao, a.aolo, R * d);
     linear_forward(lm, a.ao, a.aolo, R, d, d, lm->lt(l, T_WO), lm->Pp(lm->lt(l, T_BO)), lm->dtmp);
     {
       Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * d);
@@ -281,15 +293,13 @@ void forward(et_b200_lm* lm) {
     {
       Mark mk(lm, P_NORM, 0, 8.0 * R * d);
       layer_norm_forward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), lm->Pp(lm->lt(l, T_LN2B)), lm->eps,
-                         a.h2, a.mu2, a.rs2, R, d, s);
+                         a.h2, a.mu2, a.rs2, R, d, s, a.h2lo);
     }
-    if (lm->three) split(lm, a.h2, a.h2lo, R * d);
     linear_forward(lm, a.h2, a.h2lo, R, d, F, lm->lt(l, T_W1), lm->Pp(lm->lt(l, T_B1)), a.u);
     {
       Mark mk(lm, P_ELEMENTWISE, 0, 8.0 * R * F);
-      gelu_forward(a.u, a.g, R * F, s);
+      gelu_forward(a.u, a.g, R * F, s, a.glo);
     }
-    if (lm->three) split(lm, a.g, a.glo, R * F);
     linear_forward(lm, a.g, a.glo, R, F, d, lm->lt(l, T_W2), lm->Pp(lm->lt(l, T_B2)), lm->dtmp);
     {
       Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * d);
@@ -299,14 +309,13 @@ void forward(et_b200_lm* lm) {
   {
     Mark mk(lm, P_NORM, 0, 8.0 * R * d);
     layer_norm_forward(lm->x_final, lm->Pp(lm->lnf_g()), lm->Pp(lm->lnf_b()), lm->eps, lm->xf,
-                       lm->muf, lm->rsf, R, d, s);
+                       lm->muf, lm->rsf, R, d, s, lm->xflo);
   }
-  if (lm->three) split(lm, lm->xf, lm->xflo, R * d);
   linear_forward(lm, lm->xf, lm->xflo, R, d, V, 0, nullptr, lm->logits);
   {
     Mark mk(lm, P_CE, 0, 8.0 * R * V + 12.0 * R);
     ce_fused(lm->logits, lm->logits, lm->targets, nullptr, lm->ce_scale, lm->loss_rows, R, V,
-             lm->status, s);
+             lm->status, s, lm->logits_lo);
     mean_loss(lm->loss_rows, R, lm->loss_mean, s);
   }
 }
@@ -329,72 +338,66 @@ void backward(et_b200_lm* lm) {
   const bool three = lm->three;
   // head (tied): dlogits already in place of the logits
   float* dlog = lm->logits;
-  if (three) split(lm, dlog, lm->logits_lo, R * V);
   linear_backward_dx(lm, dlog, lm->logits_lo, R, d, V, 0, lm->dtmp);
   linear_backward_dw(lm, dlog, lm->logits_lo, lm->xf, lm->xflo, R, d, V, lm->G(0));
   {
     Mark mk(lm, P_NORM, 0, 16.0 * R * d);
     layer_norm_backward(lm->x_final, lm->Pp(lm->lnf_g()), lm->muf, lm->rsf, lm->dtmp, lm->dx, 0,
-                        lm->G(lm->lnf_g()), lm->G(lm->lnf_b()), lm->ln_ws, R, d, s);
+                        lm->G(lm->lnf_g()), lm->G(lm->lnf_b()), lm->ln_ws, R, d, s, lm->dxhi,
+                        lm->dxlo);
   }
   for (int l = (int)lm->L - 1; l >= 0; l--) {
     LayerActs& a = lm->layers[l];
+    bool dqkv_split = false;
     // FFN down: dY = dx (flows to the skip and the branch)
     bias_grad(lm, lm->dx, R, d, lm->G(lm->lt(l, T_B2)));
-    const float* dyh = lm->dx;
-    const float* dyl = nullptr;
-    if (three) {
-      Mark mk(lm, P_SPLIT, 0, 12.0 * R * d);
-      split_tf32(lm->dx, lm->dxhi, lm->dxlo, R * d, s);
-      dyh = lm->dxhi;
-      dyl = lm->dxlo;
-    }
+    // dx arrives with its hi/lo pair from the LayerNorm backward above
+    const float* dyh = three ? lm->dxhi : lm->dx;
+    const float* dyl = three ? lm->dxlo : nullptr;
     linear_backward_dx(lm, dyh, dyl, R, F, d, lm->lt(l, T_W2), lm->dg);
     linear_backward_dw(lm, dyh, dyl, a.g, a.glo, R, F, d, lm->G(lm->lt(l, T_W2)));
     {
       Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * F);
-      gelu_backward(a.u, lm->dg, lm->du, R * F, s);
+      gelu_backward(a.u, lm->dg, lm->du, R * F, s, lm->dulo);
     }
-    bias_grad(lm, lm->du, R, F, lm->G(lm->lt(l, T_B1)));
-    if (three) split(lm, lm->du, lm->dulo, R * F);
+    bias_grad(lm, lm->du, R, F, lm->G(lm->lt(l, T_B1)), lm->dulo);
     linear_backward_dx(lm, lm->du, lm->dulo, R, d, F, lm->lt(l, T_W1), lm->dtmp);
     linear_backward_dw(lm, lm->du, lm->dulo, a.h2, a.h2lo, R, d, F, lm->G(lm->lt(l, T_W1)));
     {
       Mark mk(lm, P_NORM, 0, 20.0 * R * d);
       layer_norm_backward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), a.mu2, a.rs2, lm->dtmp, lm->dx, 1,
-                          lm->G(lm->lt(l, T_LN2G)), lm->G(lm->lt(l, T_LN2B)), lm->ln_ws, R, d, s);
+                          lm->G(lm->lt(l, T_LN2G)), lm->G(lm->lt(l, T_LN2B)), lm->ln_ws, R, d, s,
+                          lm->dxhi, lm->dxlo);
     }
     // attention output projection: dY = dx
     bias_grad(lm, lm->dx, R, d, lm->G(lm->lt(l, T_BO)));
-    dyh = lm->dx;
-    dyl = nullptr;
-    if (three) {
-      Mark mk(lm, P_SPLIT, 0, 12.0 * R * d);
-      split_tf32(lm->dx, lm->dxhi, lm->dxlo, R * d, s);
-      dyh = lm->dxhi;
-      dyl = lm->dxlo;
-    }
+    dyh = three ? lm->dxhi : lm->dx;
+    dyl = three ? lm->dxlo : nullptr;
     linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp);
     linear_backward_dw(lm, dyh, dyl, a.ao, a.aolo, R, d, d, lm->G(lm->lt(l, T_WO)));
     {
-      AttnParams p = attn_params(lm, a.qkv);
+      AttnParams p = attn_params(lm, a.qkv, l);
+      p.ws_ready = lm->attn_prepared[l];
       Mark mk(lm, P_ATTN_BWD, attn_flop(lm, 4), 0);
       const int64_t w = 3 * d;
-      attention_backward(p, AttnTensor{a.ao, lm->T * d, lm->Dh, d}, a.aolo,
-                         AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d}, a.am, a.al, lm->delta,
-                         AttnOut{lm->dqkv, lm->T * w, lm->Dh, w},
-                         AttnOut{lm->dqkv + d, lm->T * w, lm->Dh, w},
-                         AttnOut{lm->dqkv + 2 * d, lm->T * w, lm->Dh, w}, s);
+      float* lo = lm->dqkvlo;  // null unless 3xTF32
+      dqkv_split = attention_backward(
+          p, AttnTensor{a.ao, lm->T * d, lm->Dh, d}, a.aolo,
+          AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d}, a.am, a.al, lm->delta,
+          AttnOut{lm->dqkv, lm->T * w, lm->Dh, w, lo}, AttnOut{lm->dqkv + d, lm->T * w, lm->Dh, w, lo ? lo + d : nullptr},
+          AttnOut{lm->dqkv + 2 * d, lm->T * w, lm->Dh, w, lo ? lo + 2 * d : nullptr}, s) && three;
     }
-    bias_grad(lm, lm->dqkv, R, 3 * d, lm->G(lm->lt(l, T_BQKV)));
-    if (three) split(lm, lm->dqkv, lm->dqkvlo, R * 3 * d);
+    if (three && !dqkv_split) split(lm, lm->dqkv, lm->dqkvlo, R * 3 * d);
+    bias_grad(lm, lm->dqkv, R, 3 * d, lm->G(lm->lt(l, T_BQKV)), three ? lm->dqkvlo : nullptr);
     linear_backward_dx(lm, lm->dqkv, lm->dqkvlo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->dtmp);
     linear_backward_dw(lm, lm->dqkv, lm->dqkvlo, a.h1, a.h1lo, R, d, 3 * d,
                        lm->G(lm->lt(l, T_WQKV)));
     {
       Mark mk(lm, P_NORM, 0, 20.0 * R * d);
+      // layer 0's dx only feeds the embedding gradient: no operand pair
       layer_norm_backward(a.x, lm->Pp(lm->lt(l, T_LN1G)), a.mu1, a.rs1, lm->dtmp, lm->dx, 1,
-                          lm->G(lm->lt(l, T_LN1G)), lm->G(lm->lt(l, T_LN1B)), lm->ln_ws, R, d, s);
+                          lm->G(lm->lt(l, T_LN1G)), lm->G(lm->lt(l, T_LN1B)), lm->ln_ws, R, d, s,
+                          l > 0 ? lm->dxhi : nullptr, l > 0 ? lm->dxlo : nullptr);
     }
     allreduce_range(lm, lm->lt(l, 0), lm->lt(l, 0) + kPerLayer, lm->layer_done[l]);
   }
@@ -603,11 +606,18 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->ln_ws = dalloc<float>(lm, ln_workspace_floats(R, d), &err);
   lm->col_ws = dalloc<float>(lm, colsum_workspace_floats(R, widest), &err);
   lm->emb_scratch = dalloc<uint8_t>(lm, embedding_scratch_bytes(R, V), &err);
+  // split-K partials for the weight-gradient GEMMs of the layers (K = rows)
+  lm->splitk_floats = gemm_splitk_floats((int)std::max<int64_t>(3 * d, F), (int)std::max<int64_t>(d, F));
+  lm->splitk_ws = dalloc<float>(lm, lm->splitk_floats, &err);
   {
     AttnParams shape{};
     shape.B = (int)lm->B; shape.Hq = (int)lm->H; shape.Hkv = (int)lm->H;
     shape.Tq = (int)lm->T; shape.Tk = (int)lm->T; shape.Dh = (int)lm->Dh;
-    lm->attn_ws = dalloc<float>(lm, attention_workspace_floats(shape), &err);
+    lm->attn_qkv_ws.resize(L);
+    lm->attn_prepared.assign(L, 0);
+    for (int64_t l = 0; l < L; l++)
+      lm->attn_qkv_ws[l] = dalloc<float>(lm, attention_qkv_workspace_floats(shape), &err);
+    lm->attn_grad_ws = dalloc<float>(lm, attention_grad_workspace_floats(shape), &err);
   }
   lm->ids = dalloc<int64_t>(lm, R, &err);
   lm->targets = dalloc<int64_t>(lm, R, &err);

@@ -163,3 +163,25 @@ def test_launch_counter_and_device_step(lib, cuda):
     assert etb.launch_count() - before > 20
     assert np.isfinite(loss.item())
     model.close()
+
+
+def test_long_sequence_lm_gradients_vs_oracle(lib, cuda):
+    """One layer at T = 1024 and 4 sequences (4,096 rows): the weight-gradient
+    GEMMs then have K = 4,096 over one or two output tiles, which takes the
+    split-K path (partial sums reduced in a fixed order), and attention runs
+    several query tiles per head with RoPE.  Same per-tensor normwise bound as
+    the tiny model."""
+    s = etb.ModelShape(1, 64, 2, 256, 512, 1024, 4)
+    om = orc.LanguageModel(s.layers, s.d_model, s.heads, s.ffn, s.vocabulary, s.seq_len, s.batch)
+    params = om.init(2024)
+    ids, targets = orc.synthetic_batch(88, s.batch, s.seq_len, s.vocabulary)
+    loss_ref, grads_ref = om.forward_backward(params, ids, targets)
+    model = etb.LanguageModel(s, precision=etb.PRECISION_TF32X3)
+    model.init(2024)
+    loss = model.forward_backward(ids, targets)
+    grads = model.read(1)
+    assert abs(loss - loss_ref) <= 2e-5 * abs(loss_ref), (loss, loss_ref)
+    for t, (g, r) in enumerate(zip(om.split(grads), om.split(grads_ref))):
+        err = np.abs(g.astype(np.float64) - r).max() / max(np.abs(r).max(), 1e-30)
+        assert err <= GRAD_TOL[etb.PRECISION_TF32X3], (t, err)
+    model.close()
