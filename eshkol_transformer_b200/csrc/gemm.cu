@@ -393,6 +393,297 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   }
 }
 
+// ---- 2-SM (CTA pair) 3xTF32 kernel ---------------------------------------------
+//
+// A cluster of two CTAs on the two SMs of a TPC computes a 256 x BN output
+// tile with tcgen05.mma.cta_group::2 (M = 256): CTA r holds A rows
+// [128 r, 128 r + 128) and B rows [BN/2 r, BN/2 r + BN/2) of every K block in
+// its own shared memory, and its TMEM receives output rows [128 r, 128 r + 128).
+// Each SM's ring stage is then 64 KB instead of 96 KB, so three stages fit
+// and hide the TMA latency that a two-stage 128 x 256 ring exposes.
+//   both CTAs  warp 0: TMA into its own shared memory; the copies complete on
+//              the leader CTA's full barrier (the leader expects both CTAs'
+//              bytes); warp 1 allocates TMEM (cta_group::2, both CTAs);
+//              warps 2-5: epilogue of its own 128 rows, then an arrive on the
+//              leader's accumulator-empty barrier
+//   leader     warp 1 lane 0 issues the MMAs and commits to the empty /
+//              accumulator-full barriers of both CTAs (one commit per CTA)
+// No TMA load uses cluster multicast.  All waits are bounded; after a
+// timeout every thread still reaches the closing cluster barrier.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+// TMA tile load whose completion may be signalled on the peer CTA's barrier.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// Arrives on `bar_cluster` (either CTA of the pair) once all prior MMAs complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
+               : "memory");
+}
+
+template <int BN, int STAGES>
+struct Tc2Layout {
+  static constexpr int BK = 32;
+  static constexpr int A_BYTES = TC_BM * BK * 4;        // this CTA's 128 A rows
+  static constexpr int B_BYTES = (BN / 2) * BK * 4;      // this CTA's BN/2 B rows
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * 2;  // hi and lo
+  static constexpr int RING_BYTES = STAGE_BYTES * STAGES;
+  static constexpr int SMEM_BYTES = RING_BYTES + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+template <int BN, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
+                const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb_lo,
+                TcArgs args) {
+  using L = Tc2Layout<BN, STAGES>;
+  constexpr int BK = L::BK;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::RING_BYTES);
+  // bars: full[STAGES] (leader's used), empty[STAGES], tfull[2], tempty[2] (leader's used)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 8);  // 4 epilogue warps in each CTA
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // the same warp in both CTAs allocates the pair's TMEM
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(L::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int nkb = (args.K + BK - 1) / BK;
+  const int tiles = args.tiles_m * args.tiles_n;  // tiles_m counts 256-row blocks
+  const int units = tiles * args.splits;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  bool failed = false;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer (both CTAs)
+      const uint32_t full_leader = map_to_rank(full0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int unit = cluster; ok && unit < units; unit += nclusters) {
+        const int tile = unit % tiles, split = unit / tiles;
+        int tm, tn;
+        raster(tile, args.tiles_m, args.tiles_n, tm, tn);
+        const int m0 = tm * 2 * TC_BM + (int)rank * TC_BM, n0 = tn * BN + (int)rank * (BN / 2);
+        const int kb_end = min(nkb, (split + 1) * args.kb_per_split);
+        for (int kb = split * args.kb_per_split; kb < kb_end; kb++) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, args.error)) { ok = false; break; }
+          if (leader) mbar_expect_tx(full0 + 8 * stage, 2 * L::STAGE_BYTES);
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+          const uint32_t fb = full_leader + 8 * stage;
+          const int k0 = kb * BK;
+#pragma unroll
+          for (int op = 0; op < 2; op++) {
+            const CUtensorMap* mA = op == 0 ? &ta : &ta_lo;
+            const CUtensorMap* mB = op == 0 ? &tb : &tb_lo;
+            const uint32_t da = sa + op * (L::A_BYTES + L::B_BYTES);
+            const uint32_t db = sb + op * (L::A_BYTES + L::B_BYTES);
+            if (args.a_mn) {
+              for (int c = 0; c < TC_BM / 32; c++)
+                tma_load_2d_pair(da + (uint32_t)BK * 128u * c, mA, fb, m0 + 32 * c, k0);
+            } else {
+              tma_load_2d_pair(da, mA, fb, k0, m0);
+            }
+            if (args.b_mn) {
+              for (int c = 0; c < (BN / 2) / 32; c++)
+                tma_load_2d_pair(db + (uint32_t)BK * 128u * c, mB, fb, n0 + 32 * c, k0);
+            } else {
+              tma_load_2d_pair(db, mB, fb, k0, n0);
+            }
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      failed = !ok;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA)
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)args.a_mn << 15) |
+                             ((uint32_t)args.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)((2 * TC_BM) >> 4) << 24);
+      const uint32_t peer = 1;
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int unit = cluster; ok && unit < units; unit += nclusters) {
+        const int split = unit / tiles;
+        if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, args.error)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const int kb_begin = split * args.kb_per_split;
+        const int kb_end = min(nkb, kb_begin + args.kb_per_split);
+        for (int kb = kb_begin; kb < kb_end; kb++) {
+          if (!mbar_wait(full0 + 8 * stage, phase, args.error)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+          const uint32_t lo = L::A_BYTES + L::B_BYTES;
+#pragma unroll
+          for (int j = 0; j < BK / 8; j++) {
+            const uint64_t a = tile_desc<BK>(sa, args.a_mn, j);
+            const uint64_t b = tile_desc<BK>(sb, args.b_mn, j);
+            const uint64_t alo = tile_desc<BK>(sa + lo, args.a_mn, j);
+            const uint64_t blo = tile_desc<BK>(sb + lo, args.b_mn, j);
+            umma_tf32_pair(d_tmem, a, b, idesc, (kb > kb_begin || j > 0) ? 1u : 0u);
+            umma_tf32_pair(d_tmem, a, blo, idesc, 1u);
+            umma_tf32_pair(d_tmem, alo, b, idesc, 1u);
+          }
+          umma_commit_pair(empty0 + 8 * stage);
+          umma_commit_pair(map_to_rank(empty0 + 8 * stage, peer));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull0 + 8 * acc);
+        umma_commit_pair(map_to_rank(tfull0 + 8 * acc, peer));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      failed = !ok;
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 own TMEM lanes 32*(warp%4).. of this CTA
+    const int lane_base = 32 * (warp & 3);
+    const uint32_t tempty_leader = map_to_rank(tempty0, 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int unit = cluster; unit < units; unit += nclusters) {
+      const int tile = unit % tiles, split = unit / tiles;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(tfull0 + 8 * acc, acc_phase, args.error) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) { failed = true; break; }
+      __syncwarp();
+      tc_fence_after();
+      int tm, tn;
+      raster(tile, args.tiles_m, args.tiles_n, tm, tn);
+      const int m = tm * 2 * TC_BM + (int)rank * TC_BM + lane_base + lane;
+      const int n_tile = tn * BN;
+      const bool part = args.splits > 1;
+      float* cbase = part ? args.partial + (int64_t)split * args.M * args.N : args.C;
+      const int64_t ldc = part ? (int64_t)args.N : args.ldc;
+      const float* bias = part ? nullptr : args.bias;
+      const int accumulate = part ? 0 : args.accumulate;
+      float* crow = cbase + (int64_t)m * ldc;
+      const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c), v);
+        if (m < args.M) {
+          const int n0 = n_tile + c;
+          if (vec && n0 + 32 <= args.N) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 r = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+              if (bias) {
+                r.x += bias[n0 + i];
+                r.y += bias[n0 + i + 1];
+                r.z += bias[n0 + i + 2];
+                r.w += bias[n0 + i + 3];
+              }
+              float4* dst = reinterpret_cast<float4*>(crow + n0 + i);
+              if (accumulate) {
+                const float4 o = *dst;
+                r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
+              }
+              *dst = r;
+            }
+          } else {
+            for (int i = 0; i < 32; i++) {
+              const int n = n0 + i;
+              if (n >= args.N) break;
+              float r = v[i];
+              if (bias) r += bias[n];
+              if (accumulate) r += crow[n];
+              crow[n] = r;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + 8 * acc);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+  // After a timeout, give copies still in flight (whose completion this CTA
+  // cannot observe when it lands on the peer's barrier) time to land.
+  if (__syncthreads_or(failed)) {
+    const long long start = clock64();
+    while (clock64() - start < (1ll << 22)) {
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no CTA of the pair leaves while the other still uses its memory
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // ---- host side ---------------------------------------------------------------
 
 // Operand map: K-major [rows, K] with box {BK k, tile rows} and the 16-byte-
@@ -521,8 +812,58 @@ bool gemm_tc_supported(const GemmArgs& g) {
   return encode_fn() != nullptr;
 }
 
+// 3xTF32 on CTA pairs: 256 x BN tiles, 3-stage ring of 64 KB per SM.
+template <int BN, int STAGES>
+void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
+  using L = Tc2Layout<BN, STAGES>;
+  CUtensorMap ta, tb, ta_lo, tb_lo;
+  const bool ok = operand_map(&ta, g.A, g.a_kmajor, g.M, g.K, g.lda, TC_BM, L::BK) &&
+                  operand_map(&tb, g.B, g.b_kmajor, g.N, g.K, g.ldb, BN / 2, L::BK) &&
+                  operand_map(&ta_lo, g.A_lo, g.a_kmajor, g.M, g.K, g.lda, TC_BM, L::BK) &&
+                  operand_map(&tb_lo, g.B_lo, g.b_kmajor, g.N, g.K, g.ldb, BN / 2, L::BK);
+  if (!ok) {
+    gemm_simt(g, stream);
+    return;
+  }
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       L::SMEM_BYTES);
+  TcArgs a;
+  a.M = g.M; a.N = g.N; a.K = g.K;
+  a.C = g.C; a.ldc = g.ldc; a.bias = g.bias; a.accumulate = g.accumulate ? 1 : 0;
+  a.a_mn = g.a_kmajor ? 0 : 1;
+  a.b_mn = g.b_kmajor ? 0 : 1;
+  a.tiles_m = (g.M + 2 * TC_BM - 1) / (2 * TC_BM);
+  a.tiles_n = (g.N + BN - 1) / BN;
+  a.error = device_error_word();
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int nkb = (g.K + L::BK - 1) / L::BK;
+  const int pairs = sm_count() / 2;
+  a.splits = 1;
+  a.kb_per_split = nkb;
+  a.partial = nullptr;
+  const int s = choose_splits(tiles, nkb, pairs);
+  if (s > 1 && g.workspace != nullptr &&
+      g.workspace_floats >= (size_t)s * (size_t)g.M * (size_t)g.N) {
+    a.kb_per_split = (nkb + s - 1) / s;
+    a.splits = (nkb + a.kb_per_split - 1) / a.kb_per_split;
+    a.partial = g.workspace;
+  }
+  const int units = tiles * a.splits;
+  const int grid = 2 * (units < pairs ? units : pairs);
+  gemm_tc2_kernel<BN, STAGES><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(ta, ta_lo, tb, tb_lo, a);
+  count_launch();
+  if (a.splits > 1) {
+    const int64_t total = (int64_t)g.M * g.N;
+    const int64_t want = (total + 255) / 256;
+    const int blocks = (int)(want < (int64_t)sm_count() * 16 ? want : (int64_t)sm_count() * 16);
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(a.partial, a.splits, g.M, g.N, g.C, g.ldc,
+                                                      g.bias, g.accumulate ? 1 : 0);
+    count_launch();
+  }
+}
+
 void gemm_tc(const GemmArgs& g, bool three_pass, cudaStream_t stream) {
-  if (three_pass) launch_tc<256, 2, true, 32>(g, stream);
+  if (three_pass) launch_tc2<256, 3>(g, stream);
   else launch_tc<256, 4, false, 32>(g, stream);
 }
 
