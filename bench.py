@@ -102,6 +102,44 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
+# DRAM bytes per algorithmic GFLOP of the 3xTF32 pair GEMM, measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum) on the profiling case's
+# FFN-up and FFN-down launches: 109.7 MB and 171.7 MB for 34.36 GFLOP each.
+GEMM_DRAM_MB_PER_GFLOP = (109.7 + 171.7) / (2 * 34.36)
+
+
+def roofline_entry(gemm: dict, gemm_tflops: float, peak_t: float, peaks: dict,
+                   clocks: dict) -> dict:
+    """The dominant kernel class (every linear GEMM of the timed steps).
+
+    achieved = algorithmic 2*M*N*K FLOP / CUDA-event time; peak = the measured
+    bf16 sustained rate.  3xTF32 issues three TF32 MMAs per algorithmic FMA and
+    TF32 runs at half the bf16 rate, so the tensor work is 3x `achieved` and
+    its own ceiling is 4,096 FLOP/clk/SM at the clock the SMs ran.
+    """
+    per_launch_flop = gemm["flop"] / max(gemm["launches"], 1)
+    sm_mhz = clocks.get("sm_mhz")
+    ceiling = 4096 * 148 * sm_mhz * 1e6 / 1e12 if sm_mhz else None
+    return {
+        "bound": "tensor", "kernel": "linear GEMM (tcgen05.mma.cta_group::2 kind::tf32, 3 passes)",
+        "achieved": round(gemm_tflops, 2), "peak": peak_t, "unit": "TFLOP/s",
+        "frac": round(gemm_tflops / peak_t, 4) if peak_t else None,
+        "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
+        if not peaks.get("fallback") else "fallback",
+        "tensor_mma_per_algorithmic_flop": 3,
+        "tensor_issue_tflops": round(3 * gemm_tflops, 1),
+        "frac_tensor_issue_of_measured_bf16": round(3 * gemm_tflops / peak_t, 4) if peak_t else None,
+        "tf32_ceiling_at_median_clock_tflops": round(ceiling, 1) if ceiling else None,
+        "frac_of_tf32_ceiling_at_clock": round(3 * gemm_tflops / ceiling, 4) if ceiling else None,
+        "flop_per_launch": per_launch_flop,
+        "avg_launch_ms": gemm["ms"] / max(gemm["launches"], 1),
+        "traffic": round(per_launch_flop / 1e9 * GEMM_DRAM_MB_PER_GFLOP * 1e6),
+        "traffic_unit": "bytes per launch",
+        "traffic_source": "ncu DRAM bytes of the profiling-case GEMM launches per algorithmic "
+                          "FLOP, scaled to the average launch",
+    }
+
+
 # ----------------------------------------------------------------- B200 arm
 
 def run_b200(args) -> None:
@@ -193,7 +231,6 @@ def run_b200(args) -> None:
     gemm = prof["gemm"]
     gemm_tflops = gemm["flop"] / (gemm["ms"] / 1e3) / 1e12 if gemm["ms"] else 0.0
     peak_t = peaks.get("bf16_tflops_sustained", 1400.0)
-    per_launch_flop = gemm["flop"] / max(gemm["launches"], 1)
     attn_b = prof["attention_backward"]
     attn_tflops = attn_b["flop"] / (attn_b["ms"] / 1e3) / 1e12 if attn_b["ms"] else 0.0
     total_prof_ms = sum(v["ms"] for v in prof.values())
@@ -207,17 +244,7 @@ def run_b200(args) -> None:
                    "contractions": "3xTF32 tcgen05", "parallelism": f"dp{world}",
                    "l2": "activations (GBs per step) exceed the 126 MB L2; no flush needed"},
         "gpu_launches": launches,
-        "roofline": {"bound": "tensor", "kernel": "linear GEMM (tcgen05 kind::tf32, 3 passes)",
-                     "achieved": round(gemm_tflops, 2), "peak": peak_t, "unit": "TFLOP/s",
-                     "frac": round(gemm_tflops / peak_t, 4) if peak_t else None,
-                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
-                     if not peaks.get("fallback") else "fallback",
-                     "tf32_dense_peak": peak_t / 2,
-                     "frac_of_tf32_peak_algorithmic": round(gemm_tflops / (peak_t / 2), 4),
-                     "tensor_mma_per_algorithmic_flop": 3,
-                     "flop_per_launch": per_launch_flop,
-                     "avg_launch_ms": gemm["ms"] / max(gemm["launches"], 1),
-                     "traffic": None},
+        "roofline": roofline_entry(gemm, gemm_tflops, peak_t, peaks, clocks.summary()),
         "attention_backward": {"achieved_tflops": round(attn_tflops, 2),
                                "ms_per_step": round(attn_b["ms"] / args.steps, 3)},
         "profile_ms_per_step": {k: round(v["ms"] / args.steps, 3) for k, v in prof.items()},
