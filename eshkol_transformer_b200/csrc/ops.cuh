@@ -54,17 +54,25 @@ void layer_norm_forward(const float* x, const float* gamma, const float* beta,
 // dx = (accumulate ? dx : 0) + LN'(dy); dgamma/dbeta over all rows via a
 // fixed-order two-stage column reduction in `workspace` (>= ln_workspace()).
 size_t ln_workspace_floats(size_t rows, size_t d);
-// With dx_hi/dx_lo, the final dx is also written as a 3xTF32 operand pair.
+// With dx_hi/dx_lo, the final dx is also written as a 3xTF32 operand pair;
+// with dsum, the column sums of the final dx (the next bias gradient) too.
 void layer_norm_backward(const float* x, const float* gamma, const float* mean,
                          const float* rstd, const float* dy, float* dx,
                          int accumulate, float* dgamma, float* dbeta,
                          float* workspace, size_t rows, size_t d,
-                         cudaStream_t stream, float* dx_hi = nullptr, float* dx_lo = nullptr);
+                         cudaStream_t stream, float* dx_hi = nullptr, float* dx_lo = nullptr,
+                         float* dsum = nullptr);
 // With a lo output, the result is written as TF32 hi (y / dx) plus residual.
 void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream,
                   float* y_lo = nullptr);
 void gelu_backward(const float* x, const float* dy, float* dx, size_t count,
                    cudaStream_t stream, float* dx_lo = nullptr);
+// GELU backward over a [rows, n] matrix that also sums the columns of dx
+// (the bias gradient of the layer that produced x) into dsum; `workspace`
+// holds gelu_colsum_workspace_floats(rows, n) floats.
+size_t gelu_colsum_workspace_floats(size_t rows, size_t n);
+void gelu_backward_colsum(const float* x, const float* dy, float* dx, float* dx_lo, float* dsum,
+                          float* workspace, size_t rows, size_t n, cudaStream_t stream);
 void relu_forward(const float* x, float* y, size_t count, cudaStream_t stream);
 void relu_backward(const float* x, const float* dy, float* dx, size_t count,
                    cudaStream_t stream);

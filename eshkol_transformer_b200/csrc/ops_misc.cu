@@ -119,6 +119,146 @@ ln_backward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
   }
 }
 
+// Register-resident variant for d = 128 NV (d <= 1024): each warp owns whole
+// rows; lane l holds columns 4 l + 128 i (float4), so x and dy are read once
+// and the column partials (dgamma, dbeta and, with dsum, the column sum of
+// the final dx) accumulate in registers over the warp's rows.  Each warp
+// writes one partial row per quantity; reduce_partials adds them in order.
+constexpr int kLnbWarps = 8;
+
+template <int NV>
+__global__ void __launch_bounds__(kLnbWarps * 32)
+ln_backward_rows_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                        const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                        const float* __restrict__ dy, float* __restrict__ dx, int accumulate,
+                        float* __restrict__ dx_hi, float* __restrict__ dx_lo,
+                        float* __restrict__ partial, int with_sum, int64_t rows) {
+  constexpr int D = 128 * NV;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4 g[NV], ag[NV], ab[NV], as[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    g[i] = reinterpret_cast<const float4*>(gamma)[lane + 32 * i];
+    ag[i] = ab[i] = as[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float dim = (float)D;
+  const float inv_dim = rn_div(1.0f, dim);
+  for (int64_t row = (int64_t)blockIdx.x * kLnbWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kLnbWarps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * D);
+    const float4* gr = reinterpret_cast<const float4*>(dy + row * D);
+    float4 xv[NV], gv[NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      xv[i] = xr[lane + 32 * i];
+      gv[i] = gr[lane + 32 * i];
+    }
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float sh = 0.0f, shn = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+#define LNB_ACC(c)                                                  \
+  {                                                                 \
+    const float n = rn_mul(rn_sub(xv[i].c, mean), rstd);            \
+    const float h = rn_mul(gv[i].c, g[i].c);                        \
+    sh += h;                                                        \
+    shn += rn_mul(h, n);                                            \
+    ag[i].c += rn_mul(gv[i].c, n);                                  \
+    ab[i].c += gv[i].c;                                             \
+  }
+      LNB_ACC(x) LNB_ACC(y) LNB_ACC(z) LNB_ACC(w)
+#undef LNB_ACC
+    }
+    sh = warp_sum(sh);
+    shn = warp_sum(shn);
+    const float factor = rn_mul(rstd, inv_dim);
+    float4* dr = reinterpret_cast<float4*>(dx + row * D);
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      float4 out;
+#define LNB_OUT(c)                                                                         \
+  {                                                                                        \
+    const float n = rn_mul(rn_sub(xv[i].c, mean), rstd);                                   \
+    const float h = rn_mul(gv[i].c, g[i].c);                                               \
+    out.c = rn_mul(factor, rn_sub(rn_sub(rn_mul(dim, h), sh), rn_mul(n, shn)));            \
+  }
+      LNB_OUT(x) LNB_OUT(y) LNB_OUT(z) LNB_OUT(w)
+#undef LNB_OUT
+      if (accumulate) {
+        const float4 o = dr[lane + 32 * i];
+        out.x = rn_add(o.x, out.x); out.y = rn_add(o.y, out.y);
+        out.z = rn_add(o.z, out.z); out.w = rn_add(o.w, out.w);
+      }
+      dr[lane + 32 * i] = out;
+      as[i].x += out.x; as[i].y += out.y; as[i].z += out.z; as[i].w += out.w;
+      if (dx_lo != nullptr) {
+        float4 h4, l4;
+        tf32_split(out.x, h4.x, l4.x);
+        tf32_split(out.y, h4.y, l4.y);
+        tf32_split(out.z, h4.z, l4.z);
+        tf32_split(out.w, h4.w, l4.w);
+        reinterpret_cast<float4*>(dx_hi + row * D)[lane + 32 * i] = h4;
+        reinterpret_cast<float4*>(dx_lo + row * D)[lane + 32 * i] = l4;
+      }
+    }
+  }
+  const int64_t pw = (int64_t)blockIdx.x * kLnbWarps + warp;  // this warp's partial row
+  const int nq = with_sum ? 3 : 2;
+  float4* out = reinterpret_cast<float4*>(partial + pw * nq * D);
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    out[lane + 32 * i] = ag[i];
+    out[D / 4 + lane + 32 * i] = ab[i];
+    if (with_sum) out[2 * (D / 4) + lane + 32 * i] = as[i];
+  }
+}
+
+int ln_backward_rows_blocks(size_t rows) {
+  const size_t want = (rows + kLnbWarps - 1) / kLnbWarps;
+  const size_t cap = (size_t)sm_count() * 2;
+  return (int)(want < cap ? want : cap);
+}
+
+// ---- GELU backward with column sums ----------------------------------------------
+
+constexpr int kGcRows = 512;  // rows per block
+
+// Block (c, r): columns [128 c, 128 c + 128) (float4 per lane) of rows
+// [kGcRows r, ...), one row per warp at a time; each warp writes its column
+// partial row of dx.
+__global__ void __launch_bounds__(256)
+gelu_backward_colsum_kernel(const float* __restrict__ x, const float* __restrict__ dy,
+                            float* __restrict__ dx, float* __restrict__ dx_lo,
+                            float* __restrict__ partial, int64_t rows, int64_t n) {
+  const float inv_sqrt_2 = 0x1.6a09e6p-1f, inv_sqrt_2pi = 0x1.988454p-2f;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t col = (int64_t)blockIdx.x * 128 + 4 * lane;
+  const int64_t r0 = (int64_t)blockIdx.y * kGcRows, r1 = min(rows, r0 + kGcRows);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (col < n) {
+    for (int64_t r = r0 + warp; r < r1; r += 8) {
+      const int64_t i = r * n + col;
+      const float4 v = *reinterpret_cast<const float4*>(x + i);
+      const float4 g = *reinterpret_cast<const float4*>(dy + i);
+      float4 o, lo;
+#define GC_ONE(c)                                                                       \
+  {                                                                                     \
+    const float cdf = rn_mul(0.5f, rn_add(1.0f, erff(rn_mul(v.c, inv_sqrt_2))));        \
+    const float density = rn_mul(expf(-rn_mul(0.5f, rn_mul(v.c, v.c))), inv_sqrt_2pi); \
+    const float slope = rn_add(cdf, rn_mul(v.c, density));                              \
+    o.c = rn_mul(g.c, slope);                                                           \
+    acc.c += o.c;                                                                       \
+    if (dx_lo != nullptr) tf32_split(o.c, o.c, lo.c);                                   \
+  }
+      GC_ONE(x) GC_ONE(y) GC_ONE(z) GC_ONE(w)
+#undef GC_ONE
+      *reinterpret_cast<float4*>(dx + i) = o;
+      if (dx_lo != nullptr) *reinterpret_cast<float4*>(dx_lo + i) = lo;
+    }
+    *reinterpret_cast<float4*>(partial + ((int64_t)blockIdx.y * 8 + warp) * n + col) = acc;
+  }
+}
+
 // Sums `count` partial rows of width `width` (row stride `stride`) in order.
 __global__ void reduce_partials_kernel(const float* __restrict__ partial, int count,
                                        int64_t width, int64_t stride, float* __restrict__ out) {
@@ -333,14 +473,48 @@ void layer_norm_forward(const float* x, const float* gamma, const float* beta, f
 }
 
 size_t ln_workspace_floats(size_t rows, size_t d) {
-  return (size_t)ln_backward_blocks(rows) * 2 * d;
+  const size_t simt = (size_t)ln_backward_blocks(rows) * 2 * d;
+  const size_t regs = (size_t)ln_backward_rows_blocks(rows) * kLnbWarps * 3 * d;
+  const size_t cols = colsum_workspace_floats(rows, d);
+  return std::max(std::max(simt, regs), cols);
 }
 
 void layer_norm_backward(const float* x, const float* gamma, const float* mean, const float* rstd,
                          const float* dy, float* dx, int accumulate, float* dgamma, float* dbeta,
                          float* workspace, size_t rows, size_t d, cudaStream_t stream,
-                         float* dx_hi, float* dx_lo) {
+                         float* dx_hi, float* dx_lo, float* dsum) {
   if (rows == 0) return;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
+                         reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(gamma) |
+                         reinterpret_cast<uintptr_t>(dx_hi) | reinterpret_cast<uintptr_t>(dx_lo)) &
+                        15) == 0;
+  if (aligned && d % 128 == 0 && d <= 1024) {
+    const int blocks = ln_backward_rows_blocks(rows);
+    const int nq = dsum ? 3 : 2;
+    const int with_sum = dsum ? 1 : 0;
+    float* hi = dx_lo ? dx_hi : nullptr;
+    switch (d / 128) {
+#define LNB_CASE(nv)                                                                          \
+  case nv:                                                                                    \
+    ln_backward_rows_kernel<nv><<<blocks, kLnbWarps * 32, 0, stream>>>(                       \
+        x, gamma, mean, rstd, dy, dx, accumulate, hi, dx_lo, workspace, with_sum, (int64_t)rows); \
+    break;
+      LNB_CASE(1) LNB_CASE(2) LNB_CASE(3) LNB_CASE(4) LNB_CASE(5) LNB_CASE(6) LNB_CASE(7)
+      LNB_CASE(8)
+#undef LNB_CASE
+    }
+    const int parts = blocks * kLnbWarps;
+    const int64_t stride = (int64_t)nq * d;
+    reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace, parts, (int64_t)d,
+                                                                 stride, dgamma);
+    reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + d, parts,
+                                                                 (int64_t)d, stride, dbeta);
+    if (dsum)
+      reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + 2 * d, parts,
+                                                                   (int64_t)d, stride, dsum);
+    count_launch(dsum ? 4 : 3);
+    return;
+  }
   const int blocks = ln_backward_blocks(rows);
   const size_t smem = (size_t)kLnWarps * 2 * d * sizeof(float);
   if (smem > 48 * 1024)
@@ -353,6 +527,7 @@ void layer_norm_backward(const float* x, const float* gamma, const float* mean, 
   reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + d, blocks, (int64_t)d,
                                                                (int64_t)(2 * d), dbeta);
   count_launch(3);
+  if (dsum) column_sum(dx, dsum, rows, d, workspace, stream);
 }
 
 void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream, float* y_lo) {
@@ -433,6 +608,33 @@ void embedding_backward(const int64_t* ids, const float* dy, const float* base, 
   embedding_backward_kernel<<<(unsigned)V, 128, 0, stream>>>(keys_out, vals_out, dy, base, dw,
                                                              (int64_t)rows, (int64_t)d);
   count_launch();
+}
+
+size_t gelu_colsum_workspace_floats(size_t rows, size_t n) {
+  return ((rows + kGcRows - 1) / kGcRows) * 8 * n;
+}
+
+void gelu_backward_colsum(const float* x, const float* dy, float* dx, float* dx_lo, float* dsum,
+                          float* workspace, size_t rows, size_t n, cudaStream_t stream) {
+  if (rows == 0) {
+    cudaMemsetAsync(dsum, 0, n * sizeof(float), stream);
+    return;
+  }
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
+                         reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dx_lo)) &
+                        15) == 0;
+  if (!aligned || n % 128 != 0) {
+    gelu_backward(x, dy, dx, rows * n, stream, dx_lo);
+    column_sum(dx, dsum, rows, n, workspace, stream, dx_lo);
+    return;
+  }
+  const unsigned chunks = ceil_div(rows, kGcRows);
+  dim3 grid((unsigned)(n / 128), chunks);
+  gelu_backward_colsum_kernel<<<grid, 256, 0, stream>>>(x, dy, dx, dx_lo, workspace, (int64_t)rows,
+                                                        (int64_t)n);
+  reduce_partials_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(workspace, (int)chunks * 8,
+                                                               (int64_t)n, (int64_t)n, dsum);
+  count_launch(2);
 }
 
 size_t colsum_workspace_floats(size_t rows, size_t n) {

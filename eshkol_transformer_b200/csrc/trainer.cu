@@ -83,7 +83,7 @@ struct et_b200_lm {
   // backward scratch
   float *dx = nullptr, *dxhi = nullptr, *dxlo = nullptr, *dtmp = nullptr, *dqkv = nullptr,
         *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *dg = nullptr, *delta = nullptr;
-  float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr;
+  float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *gelu_ws = nullptr;
   // attention: per-layer prepared Q/K/V (written by the forward, reused by
   // the backward) and one shared backward scratch
   std::vector<float*> attn_qkv_ws;
@@ -342,35 +342,35 @@ void backward(et_b200_lm* lm) {
   linear_backward_dw(lm, dlog, lm->logits_lo, lm->xf, lm->xflo, R, d, V, lm->G(0));
   {
     Mark mk(lm, P_NORM, 0, 16.0 * R * d);
+    // the column sums of this dx are the last layer's b2 gradient
     layer_norm_backward(lm->x_final, lm->Pp(lm->lnf_g()), lm->muf, lm->rsf, lm->dtmp, lm->dx, 0,
                         lm->G(lm->lnf_g()), lm->G(lm->lnf_b()), lm->ln_ws, R, d, s, lm->dxhi,
-                        lm->dxlo);
+                        lm->dxlo, lm->G(lm->lt((int)lm->L - 1, T_B2)));
   }
   for (int l = (int)lm->L - 1; l >= 0; l--) {
     LayerActs& a = lm->layers[l];
     bool dqkv_split = false;
     // FFN down: dY = dx (flows to the skip and the branch)
-    bias_grad(lm, lm->dx, R, d, lm->G(lm->lt(l, T_B2)));
-    // dx arrives with its hi/lo pair from the LayerNorm backward above
+    // dx arrives with its hi/lo pair and its column sums (this layer's b2
+    // gradient) from the LayerNorm backward above
     const float* dyh = three ? lm->dxhi : lm->dx;
     const float* dyl = three ? lm->dxlo : nullptr;
     linear_backward_dx(lm, dyh, dyl, R, F, d, lm->lt(l, T_W2), lm->dg);
     linear_backward_dw(lm, dyh, dyl, a.g, a.glo, R, F, d, lm->G(lm->lt(l, T_W2)));
     {
       Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * F);
-      gelu_backward(a.u, lm->dg, lm->du, R * F, s, lm->dulo);
+      gelu_backward_colsum(a.u, lm->dg, lm->du, lm->dulo, lm->G(lm->lt(l, T_B1)), lm->gelu_ws, R,
+                           F, s);  // + the b1 gradient
     }
-    bias_grad(lm, lm->du, R, F, lm->G(lm->lt(l, T_B1)), lm->dulo);
     linear_backward_dx(lm, lm->du, lm->dulo, R, d, F, lm->lt(l, T_W1), lm->dtmp);
     linear_backward_dw(lm, lm->du, lm->dulo, a.h2, a.h2lo, R, d, F, lm->G(lm->lt(l, T_W1)));
     {
       Mark mk(lm, P_NORM, 0, 20.0 * R * d);
       layer_norm_backward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), a.mu2, a.rs2, lm->dtmp, lm->dx, 1,
                           lm->G(lm->lt(l, T_LN2G)), lm->G(lm->lt(l, T_LN2B)), lm->ln_ws, R, d, s,
-                          lm->dxhi, lm->dxlo);
+                          lm->dxhi, lm->dxlo, lm->G(lm->lt(l, T_BO)));  // + the bo gradient
     }
     // attention output projection: dY = dx
-    bias_grad(lm, lm->dx, R, d, lm->G(lm->lt(l, T_BO)));
     dyh = three ? lm->dxhi : lm->dx;
     dyl = three ? lm->dxlo : nullptr;
     linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp);
@@ -395,9 +395,11 @@ void backward(et_b200_lm* lm) {
     {
       Mark mk(lm, P_NORM, 0, 20.0 * R * d);
       // layer 0's dx only feeds the embedding gradient: no operand pair
+      // + the b2 gradient of the layer below
       layer_norm_backward(a.x, lm->Pp(lm->lt(l, T_LN1G)), a.mu1, a.rs1, lm->dtmp, lm->dx, 1,
                           lm->G(lm->lt(l, T_LN1G)), lm->G(lm->lt(l, T_LN1B)), lm->ln_ws, R, d, s,
-                          l > 0 ? lm->dxhi : nullptr, l > 0 ? lm->dxlo : nullptr);
+                          l > 0 ? lm->dxhi : nullptr, l > 0 ? lm->dxlo : nullptr,
+                          l > 0 ? lm->G(lm->lt(l - 1, T_B2)) : nullptr);
     }
     allreduce_range(lm, lm->lt(l, 0), lm->lt(l, 0) + kPerLayer, lm->layer_done[l]);
   }
@@ -606,6 +608,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->ln_ws = dalloc<float>(lm, ln_workspace_floats(R, d), &err);
   lm->col_ws = dalloc<float>(lm, colsum_workspace_floats(R, widest), &err);
   lm->emb_scratch = dalloc<uint8_t>(lm, embedding_scratch_bytes(R, V), &err);
+  lm->gelu_ws = dalloc<float>(lm, gelu_colsum_workspace_floats(R, F), &err);
   // split-K partials for the weight-gradient GEMMs of the layers (K = rows)
   lm->splitk_floats = gemm_splitk_floats((int)std::max<int64_t>(3 * d, F), (int)std::max<int64_t>(d, F));
   lm->splitk_ws = dalloc<float>(lm, lm->splitk_floats, &err);
