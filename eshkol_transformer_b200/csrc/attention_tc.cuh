@@ -83,19 +83,6 @@ __device__ __forceinline__ uint64_t kslice(uint64_t d0, int j) {
 }
 __device__ __forceinline__ uint64_t mslice(uint64_t d0, int j) { return d0 + (uint64_t)(64 * j); }
 
-__device__ __forceinline__ float4 lds128(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
-  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
-               "f"(v.z), "f"(v.w)
-               : "memory");
-}
-
 // Row `row` of a 128-row K-major tile staged by TMA with the 128-byte swizzle
 // (32-column chunks of 128 rows x 128 B) -> 32 TMEM columns per chunk of this
 // thread's lane, starting at column `col` of `trow`.

@@ -31,6 +31,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "ops.cuh"
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs g) {
 
 constexpr int TC_BM = 128;
 constexpr int TC_THREADS = 192;
+constexpr int TC2_THREADS = 320;  // pair kernel: producer, MMA and 8 epilogue warps
 
 // Operand tiles of one K block of BK f32 (BK = 32: 128-byte rows; BK = 16:
 // 64-byte rows).  Descriptor of K-slice j (8 k) of a staged tile:
@@ -149,8 +151,54 @@ struct TcArgs {
   // writes its raw sum to partial + s * M * N (row stride N)
   int splits, kb_per_split;
   float* partial;
+  // fused epilogue (pair kernel): mode, auxiliary input, extra outputs, and
+  // the per-(tile, warp) column partials of the GELU_BWD mode
+  int epilogue;
+  const float* aux;
+  float* out2;
+  float* out3;
+  float* colpart;
+  // pair kernel: every row pointer and ldc allow float4 access and N % 4 == 0,
+  // so the epilogue goes through the shared-memory transpose (coalesced rows)
+  int staged;
   int* error;
 };
+
+__device__ __forceinline__ float gelu_value(float v) {  // n2_primitives_provider.c:545-583
+  const float inv_sqrt_2 = 0x1.6a09e6p-1f;
+  const float e = erff(rn_mul(v, inv_sqrt_2));
+  return rn_mul(rn_mul(0.5f, v), rn_add(1.0f, e));
+}
+__device__ __forceinline__ float gelu_slope(float v) {
+  const float inv_sqrt_2 = 0x1.6a09e6p-1f, inv_sqrt_2pi = 0x1.988454p-2f;
+  const float cdf = rn_mul(0.5f, rn_add(1.0f, erff(rn_mul(v, inv_sqrt_2))));
+  const float density = rn_mul(expf(-rn_mul(0.5f, rn_mul(v, v))), inv_sqrt_2pi);
+  return rn_add(cdf, rn_mul(v, density));
+}
+
+// One halving stage of warp_column_sums: lanes with bit K set keep the upper
+// K of their first 2K values, the others the lower K, and add the partner's.
+template <int K>
+__device__ __forceinline__ void column_sum_stage(float (&v)[32], int lane) {
+  const bool upper = (lane & K) != 0;
+#pragma unroll
+  for (int i = 0; i < K; i++) {
+    const float send = upper ? v[i] : v[i + K];
+    const float keep = upper ? v[i + K] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, K);
+  }
+}
+// Lane l of the warp receives the sum over the 32 lanes of v[l] (a
+// reduce-scatter: 31 shuffles for 32 columns).
+__device__ __forceinline__ float warp_column_sums(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+  column_sum_stage<16>(v, lane);
+  column_sum_stage<8>(v, lane);
+  column_sum_stage<4>(v, lane);
+  column_sum_stage<2>(v, lane);
+  column_sum_stage<1>(v, lane);
+  return v[0];
+}
 
 // Grouped rasterisation: 16 M-tiles per group so the CTAs in flight share
 // their A row blocks and B column blocks through L2.
@@ -404,7 +452,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
 //   both CTAs  warp 0: TMA into its own shared memory; the copies complete on
 //              the leader CTA's full barrier (the leader expects both CTAs'
 //              bytes); warp 1 allocates TMEM (cta_group::2, both CTAs);
-//              warps 2-5: epilogue of its own 128 rows, then an arrive on the
+//              warps 2-9: epilogue of its own 128 rows (warp w: TMEM lane
+//              quadrant w % 4, column half (w - 2) / 4), then an arrive on the
 //              leader's accumulator-empty barrier
 //   leader     warp 1 lane 0 issues the MMAs and commits to the empty /
 //              accumulator-full barriers of both CTAs (one commit per CTA)
@@ -461,12 +510,14 @@ struct Tc2Layout {
   static constexpr int B_BYTES = (BN / 2) * BK * 4;      // this CTA's BN/2 B rows
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * 2;  // hi and lo
   static constexpr int RING_BYTES = STAGE_BYTES * STAGES;
-  static constexpr int SMEM_BYTES = RING_BYTES + 256 + 1024;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // per epilogue warp a 32 x 32 f32 transpose buffer (16-byte chunks XOR-swizzled by row)
+  static constexpr int STAGE_OUT_BYTES = 8 * 4096;
+  static constexpr int SMEM_BYTES = RING_BYTES + 256 + STAGE_OUT_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  static_assert(SMEM_BYTES <= 232448, "shared memory above the 227 KB per-CTA limit");
 };
 
 template <int BN, int STAGES>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb_lo,
                 TcArgs args) {
@@ -491,7 +542,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, 8);  // 4 epilogue warps in each CTA
+      mbar_init(tempty0 + 8 * a, 16);  // 8 epilogue warps in each CTA
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -602,8 +653,10 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       failed = !ok;
     }
   } else {
-    // ---------------- epilogue: warps 2..5 own TMEM lanes 32*(warp%4).. of this CTA
+    // ---------------- epilogue: warps 2..9 own TMEM lanes 32*(warp%4).. of this CTA
+    // and columns [col_begin, col_begin + BN / 2) of the tile
     const int lane_base = 32 * (warp & 3);
+    const int col_begin = ((warp - 2) >> 2) * (BN / 2);
     const uint32_t tempty_leader = map_to_rank(tempty0, 0);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -624,39 +677,201 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       const int64_t ldc = part ? (int64_t)args.N : args.ldc;
       const float* bias = part ? nullptr : args.bias;
       const int accumulate = part ? 0 : args.accumulate;
-      float* crow = cbase + (int64_t)m * ldc;
+      const int epi = part ? 0 : args.epilogue;
+      const int64_t roff = (int64_t)m * ldc;
       const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0);
+      // the warp's column-partial row of the GELU_BWD mode
+      float* colpart = args.colpart + ((int64_t)(tm * 2 + (int)rank) * 4 + (warp & 3)) * args.N;
+      if (args.staged) {
+        // Each 32-column chunk of the warp's 32 rows goes through shared memory:
+        // lane l writes row l, then lane l handles 4 consecutive columns
+        // (4 (l & 7)) of rows 4 i + (l >> 3), so every global load and store of
+        // the warp covers four whole 128-byte row segments.
+        const uint32_t stage = smem_u32(smem + L::RING_BYTES + 256) + (uint32_t)(warp - 2) * 4096u;
+        const int sub = lane >> 3, q = lane & 7;
+        const int row0 = m - lane;
+        const bool has_aux = epi == GEMM_EPI_RESIDUAL || epi == GEMM_EPI_GELU_BWD;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+        for (int c = col_begin; c < col_begin + BN / 2; c += 32) {
+          const int n = n_tile + c + 4 * q;
+          const bool col_ok = n < args.N;  // N % 4 == 0: the 4 columns are all in or all out
+          // the auxiliary rows of the chunk, loaded before the accumulator wait
+          float4 pre[8];
+#pragma unroll
+          for (int it = 0; it < 8; it++) {
+            const int row = row0 + 4 * it + sub;
+            pre[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (has_aux && row < args.M && col_ok)
+              pre[it] = __ldg(reinterpret_cast<const float4*>(args.aux + (int64_t)row * ldc + n));
+          }
+          float v[32];
+          tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c), v);
+#pragma unroll
+          for (int u = 0; u < 8; u++)
+            sts128(stage + (uint32_t)lane * 128u + (((uint32_t)u ^ (uint32_t)(lane & 7)) << 4),
+                   make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]));
+          __syncwarp();
+          float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (bias != nullptr && col_ok) b4 = *reinterpret_cast<const float4*>(bias + n);
+          float4 cs = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int it = 0; it < 8; it++) {
+            const int r = 4 * it + sub;
+            float4 x = lds128(stage + (uint32_t)r * 128u + (((uint32_t)q ^ (uint32_t)(r & 7)) << 4));
+            const int row = row0 + r;
+            if (row >= args.M || !col_ok) continue;
+            const int64_t off = (int64_t)row * ldc + n;
+            if (epi == GEMM_EPI_GELU_BWD) {
+              // d = y GELU'(u), split into hi (C) and lo (out2); column sums
+              const float4 u4 = pre[it];
+              float4 d;
+              d.x = rn_mul(x.x, gelu_slope(u4.x));
+              d.y = rn_mul(x.y, gelu_slope(u4.y));
+              d.z = rn_mul(x.z, gelu_slope(u4.z));
+              d.w = rn_mul(x.w, gelu_slope(u4.w));
+              cs.x += d.x; cs.y += d.y; cs.z += d.z; cs.w += d.w;
+              if (args.out2 != nullptr) {
+                float4 lo;
+                tf32_split(d.x, d.x, lo.x);
+                tf32_split(d.y, d.y, lo.y);
+                tf32_split(d.z, d.z, lo.z);
+                tf32_split(d.w, d.w, lo.w);
+                *reinterpret_cast<float4*>(args.out2 + off) = lo;
+              }
+              *reinterpret_cast<float4*>(cbase + off) = d;
+              continue;
+            }
+            if (bias != nullptr) {
+              x.x += b4.x; x.y += b4.y; x.z += b4.z; x.w += b4.w;
+            }
+            float4* dst = reinterpret_cast<float4*>(cbase + off);
+            if (epi == GEMM_EPI_RESIDUAL) {
+              const float4 o = pre[it];
+              x.x = rn_add(x.x, o.x); x.y = rn_add(x.y, o.y);
+              x.z = rn_add(x.z, o.z); x.w = rn_add(x.w, o.w);
+            } else if (accumulate) {
+              const float4 o = *dst;
+              x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+            }
+            *dst = x;
+            if (epi == GEMM_EPI_GELU_FWD) {
+              float4 g = make_float4(gelu_value(x.x), gelu_value(x.y), gelu_value(x.z),
+                                     gelu_value(x.w));
+              if (args.out3 != nullptr) {
+                float4 lo;
+                tf32_split(g.x, g.x, lo.x);
+                tf32_split(g.y, g.y, lo.y);
+                tf32_split(g.z, g.z, lo.z);
+                tf32_split(g.w, g.w, lo.w);
+                *reinterpret_cast<float4*>(args.out3 + off) = lo;
+              }
+              *reinterpret_cast<float4*>(args.out2 + off) = g;
+            }
+          }
+          if (epi == GEMM_EPI_GELU_BWD) {
+            // rows sub, sub + 4, ... summed per lane; then over the 4 lanes of a column group
+#pragma unroll
+            for (int o = 8; o <= 16; o <<= 1) {
+              cs.x += __shfl_xor_sync(0xffffffffu, cs.x, o);
+              cs.y += __shfl_xor_sync(0xffffffffu, cs.y, o);
+              cs.z += __shfl_xor_sync(0xffffffffu, cs.z, o);
+              cs.w += __shfl_xor_sync(0xffffffffu, cs.w, o);
+            }
+            if (sub == 0 && col_ok) *reinterpret_cast<float4*>(colpart + n) = cs;
+          }
+          __syncwarp();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader + 8 * acc);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        continue;
+      }
+#pragma unroll 1
+      for (int c = col_begin; c < col_begin + BN / 2; c += 32) {
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c), v);
-        if (m < args.M) {
-          const int n0 = n_tile + c;
-          if (vec && n0 + 32 <= args.N) {
+        const int n0 = n_tile + c;
+        const bool row_ok = m < args.M;
+        const bool full = vec && n0 + 32 <= args.N;
+        if (epi == GEMM_EPI_GELU_BWD) {
+          // d = y GELU'(u); the columns' partial sums include every row of the warp
+          float d[32];
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              float4 r = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-              if (bias) {
-                r.x += bias[n0 + i];
-                r.y += bias[n0 + i + 1];
-                r.z += bias[n0 + i + 2];
-                r.w += bias[n0 + i + 3];
-              }
-              float4* dst = reinterpret_cast<float4*>(crow + n0 + i);
-              if (accumulate) {
-                const float4 o = *dst;
-                r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
-              }
-              *dst = r;
-            }
-          } else {
+          for (int i = 0; i < 32; i++) {
+            const int n = n0 + i;
+            d[i] = (row_ok && n < args.N) ? rn_mul(v[i], gelu_slope(args.aux[roff + n])) : 0.0f;
+          }
+          if (row_ok) {
+#pragma unroll
             for (int i = 0; i < 32; i++) {
               const int n = n0 + i;
-              if (n >= args.N) break;
+              if (n < args.N) {
+                float h = d[i], lo = 0.0f;
+                if (args.out2 != nullptr) tf32_split(d[i], h, lo);
+                cbase[roff + n] = h;
+                if (args.out2 != nullptr) args.out2[roff + n] = lo;
+              }
+            }
+          }
+          float cs[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) cs[i] = d[i];
+          const float colsum = warp_column_sums(cs);
+          if (n0 + lane < args.N) colpart[n0 + lane] = colsum;
+          continue;
+        }
+        if (!row_ok) continue;
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 r = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            if (bias) {
+              r.x += bias[n0 + i];
+              r.y += bias[n0 + i + 1];
+              r.z += bias[n0 + i + 2];
+              r.w += bias[n0 + i + 3];
+            }
+            float4* dst = reinterpret_cast<float4*>(cbase + roff + n0 + i);
+            if (epi == GEMM_EPI_RESIDUAL) {
+              const float4 o = *reinterpret_cast<const float4*>(args.aux + roff + n0 + i);
+              r.x = rn_add(r.x, o.x); r.y = rn_add(r.y, o.y);
+              r.z = rn_add(r.z, o.z); r.w = rn_add(r.w, o.w);
+            } else if (accumulate) {
+              const float4 o = *dst;
+              r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
+            }
+            *dst = r;
+            if (epi == GEMM_EPI_GELU_FWD) {
+              float4 g = make_float4(gelu_value(r.x), gelu_value(r.y), gelu_value(r.z),
+                                     gelu_value(r.w));
+              if (args.out3 != nullptr) {
+                float4 lo;
+                tf32_split(g.x, g.x, lo.x);
+                tf32_split(g.y, g.y, lo.y);
+                tf32_split(g.z, g.z, lo.z);
+                tf32_split(g.w, g.w, lo.w);
+                *reinterpret_cast<float4*>(args.out3 + roff + n0 + i) = lo;
+              }
+              *reinterpret_cast<float4*>(args.out2 + roff + n0 + i) = g;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const int n = n0 + i;
+            if (n < args.N) {
               float r = v[i];
               if (bias) r += bias[n];
-              if (accumulate) r += crow[n];
-              crow[n] = r;
+              if (epi == GEMM_EPI_RESIDUAL) r = rn_add(r, args.aux[roff + n]);
+              else if (accumulate) r += cbase[roff + n];
+              cbase[roff + n] = r;
+              if (epi == GEMM_EPI_GELU_FWD) {
+                float gv = gelu_value(r), lo = 0.0f;
+                if (args.out3 != nullptr) tf32_split(gv, gv, lo);
+                args.out2[roff + n] = gv;
+                if (args.out3 != nullptr) args.out3[roff + n] = lo;
+              }
             }
           }
         }
@@ -754,7 +969,7 @@ void launch_tc(const GemmArgs& g, cudaStream_t stream) {
   }
   cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, THREE, BK>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
-  TcArgs a;
+  TcArgs a{};
   a.M = g.M; a.N = g.N; a.K = g.K;
   a.C = g.C; a.ldc = g.ldc; a.bias = g.bias; a.accumulate = g.accumulate ? 1 : 0;
   a.a_mn = g.a_kmajor ? 0 : 1;
@@ -800,6 +1015,11 @@ void gemm_simt(const GemmArgs& g, cudaStream_t stream) {
 
 size_t gemm_splitk_floats(int M, int N) { return (size_t)16 * (size_t)M * (size_t)N; }
 
+size_t gemm_epilogue_ws_floats(int M, int N) {
+  const size_t pair_parts = (size_t)((M + 2 * TC_BM - 1) / (2 * TC_BM)) * 8 * (size_t)N;
+  return std::max(pair_parts, gelu_colsum_workspace_floats((size_t)M, (size_t)N));
+}
+
 bool gemm_tc_supported(const GemmArgs& g) {
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return false;
@@ -810,6 +1030,16 @@ bool gemm_tc_supported(const GemmArgs& g) {
   // TMA global extents and strides must fit the descriptor limits
   if (g.lda > ((int64_t)1 << 36) || g.ldb > ((int64_t)1 << 36)) return false;
   return encode_fn() != nullptr;
+}
+
+// out[n] = sum over p of part[p * N + n], p ascending.
+__global__ void colpart_reduce_kernel(const float* __restrict__ part, int parts, int N,
+                                      float* __restrict__ out) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float s = 0.0f;
+  for (int p = 0; p < parts; p++) s += part[(int64_t)p * N + n];
+  out[n] = s;
 }
 
 // 3xTF32 on CTA pairs: 256 x BN tiles, 3-stage ring of 64 KB per SM.
@@ -827,7 +1057,7 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   }
   cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        L::SMEM_BYTES);
-  TcArgs a;
+  TcArgs a{};
   a.M = g.M; a.N = g.N; a.K = g.K;
   a.C = g.C; a.ldc = g.ldc; a.bias = g.bias; a.accumulate = g.accumulate ? 1 : 0;
   a.a_mn = g.a_kmajor ? 0 : 1;
@@ -835,13 +1065,23 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   a.tiles_m = (g.M + 2 * TC_BM - 1) / (2 * TC_BM);
   a.tiles_n = (g.N + BN - 1) / BN;
   a.error = device_error_word();
+  a.epilogue = g.epilogue;
+  a.aux = g.aux;
+  a.out2 = g.out2;
+  a.out3 = g.out3;
+  a.colpart = g.epi_ws;
+  {
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    a.staged = (g.ldc % 4 == 0) && (g.N % 4 == 0) && al(g.C) && al(g.aux) && al(g.out2) &&
+               al(g.out3) && al(g.bias) && al(g.epi_ws) && al(g.workspace);
+  }
   const int tiles = a.tiles_m * a.tiles_n;
   const int nkb = (g.K + L::BK - 1) / L::BK;
   const int pairs = sm_count() / 2;
   a.splits = 1;
   a.kb_per_split = nkb;
   a.partial = nullptr;
-  const int s = choose_splits(tiles, nkb, pairs);
+  const int s = g.epilogue == GEMM_EPI_PLAIN ? choose_splits(tiles, nkb, pairs) : 1;
   if (s > 1 && g.workspace != nullptr &&
       g.workspace_floats >= (size_t)s * (size_t)g.M * (size_t)g.N) {
     a.kb_per_split = (nkb + s - 1) / s;
@@ -850,8 +1090,14 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   }
   const int units = tiles * a.splits;
   const int grid = 2 * (units < pairs ? units : pairs);
-  gemm_tc2_kernel<BN, STAGES><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(ta, ta_lo, tb, tb_lo, a);
+  gemm_tc2_kernel<BN, STAGES><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(ta, ta_lo, tb, tb_lo,
+                                                                            a);
   count_launch();
+  if (g.epilogue == GEMM_EPI_GELU_BWD) {
+    colpart_reduce_kernel<<<(g.N + 255) / 256, 256, 0, stream>>>(g.epi_ws, a.tiles_m * 8, g.N,
+                                                                 g.dsum);
+    count_launch();
+  }
   if (a.splits > 1) {
     const int64_t total = (int64_t)g.M * g.N;
     const int64_t want = (total + 255) / 256;
@@ -867,15 +1113,38 @@ void gemm_tc(const GemmArgs& g, bool three_pass, cudaStream_t stream) {
   else launch_tc<256, 4, false, 32>(g, stream);
 }
 
+// The fused epilogues on paths other than the pair kernel: a plain GEMM into
+// C, then the same elementwise operation as a separate pass (C holds an
+// [M, N] matrix with ldc == N, as every caller of those modes has).
+void epilogue_after(const GemmArgs& g, cudaStream_t stream) {
+  const size_t count = (size_t)g.M * (size_t)g.N;
+  switch (g.epilogue) {
+    case GEMM_EPI_RESIDUAL: add_tensors(g.aux, g.C, g.C, count, stream); break;
+    case GEMM_EPI_GELU_FWD: gelu_forward(g.C, g.out2, count, stream, g.out3); break;
+    case GEMM_EPI_GELU_BWD:
+      gelu_backward_colsum(g.aux, g.C, g.C, g.out2, g.dsum, g.epi_ws, (size_t)g.M, (size_t)g.N,
+                           stream);
+      break;
+    default: break;
+  }
+}
+
 void gemm(const GemmArgs& g, int precision, cudaStream_t stream) {
   if (g.M <= 0 || g.N <= 0) return;
   const bool three = precision == ET_B200_PRECISION_TF32X3;
-  if (precision == ET_B200_PRECISION_F32 || !gemm_tc_supported(g) ||
-      (three && (g.A_lo == nullptr || g.B_lo == nullptr))) {
-    gemm_simt(g, stream);
+  const bool pair = three && gemm_tc_supported(g) && g.A_lo != nullptr && g.B_lo != nullptr;
+  if (pair) {
+    gemm_tc(g, true, stream);  // the pair kernel applies every epilogue mode itself
     return;
   }
-  gemm_tc(g, three, stream);
+  GemmArgs plain = g;
+  plain.epilogue = GEMM_EPI_PLAIN;
+  if (g.epilogue != GEMM_EPI_PLAIN) plain.accumulate = false;
+  if (precision == ET_B200_PRECISION_F32 || !gemm_tc_supported(g) || three)
+    gemm_simt(plain, stream);
+  else
+    gemm_tc(plain, false, stream);
+  epilogue_after(g, stream);
 }
 
 }  // namespace etb

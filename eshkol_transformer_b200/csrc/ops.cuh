@@ -199,9 +199,26 @@ struct GemmArgs {
   // [M, N] sums here, then reduced in a fixed order (gemm_splitk_floats).
   float* workspace;
   size_t workspace_floats;
+  // Epilogue applied to y = sum_k A B (all outputs share ldc; `accumulate`
+  // applies to GEMM_EPI_PLAIN only):
+  //   PLAIN     C = y (+ bias) (+ C)
+  //   RESIDUAL  C = y + bias + aux                    (aux: residual stream)
+  //   GELU_FWD  C = u = y + bias; out2 = GELU(u), or its TF32 hi with out3 = lo
+  //   GELU_BWD  d = y * GELU'(aux) (aux = the GELU input); C = d, or its TF32
+  //             hi with out2 = lo; dsum[n] = column sums of d (the bias
+  //             gradient), through `epi_ws` (gemm_epilogue_ws_floats)
+  int epilogue;
+  const float* aux;
+  float* out2;
+  float* out3;
+  float* dsum;
+  float* epi_ws;
 };
+enum { GEMM_EPI_PLAIN = 0, GEMM_EPI_RESIDUAL = 1, GEMM_EPI_GELU_FWD = 2, GEMM_EPI_GELU_BWD = 3 };
 // Scratch floats split-K may use for an M x N output.
 size_t gemm_splitk_floats(int M, int N);
+// Scratch floats the GELU_BWD epilogue needs for an M x N output.
+size_t gemm_epilogue_ws_floats(int M, int N);
 void gemm(const GemmArgs& g, int precision, cudaStream_t stream);
 // True when the tensor-core path accepts this problem (alignment / shape);
 // otherwise gemm() uses the FFMA path.

@@ -122,8 +122,9 @@ ln_backward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
 // Register-resident variant for d = 128 NV (d <= 1024): each warp owns whole
 // rows; lane l holds columns 4 l + 128 i (float4), so x and dy are read once
 // and the column partials (dgamma, dbeta and, with dsum, the column sum of
-// the final dx) accumulate in registers over the warp's rows.  Each warp
-// writes one partial row per quantity; reduce_partials adds them in order.
+// the final dx) accumulate in registers over the warp's rows.  Each block
+// adds its warps' sums in warp order and writes one partial row per quantity;
+// reduce_partials adds the blocks' rows.
 constexpr int kLnbWarps = 8;
 
 template <int NV>
@@ -202,14 +203,24 @@ ln_backward_rows_kernel(const float* __restrict__ x, const float* __restrict__ g
       }
     }
   }
-  const int64_t pw = (int64_t)blockIdx.x * kLnbWarps + warp;  // this warp's partial row
+  // the block's partial row per quantity: the warps' sums added in warp order
+  __shared__ float4 red[kLnbWarps][32 * NV];
   const int nq = with_sum ? 3 : 2;
-  float4* out = reinterpret_cast<float4*>(partial + pw * nq * D);
+  float4* out = reinterpret_cast<float4*>(partial + (int64_t)blockIdx.x * nq * D);
+  for (int qi = 0; qi < nq; qi++) {
 #pragma unroll
-  for (int i = 0; i < NV; i++) {
-    out[lane + 32 * i] = ag[i];
-    out[D / 4 + lane + 32 * i] = ab[i];
-    if (with_sum) out[2 * (D / 4) + lane + 32 * i] = as[i];
+    for (int i = 0; i < NV; i++) red[warp][lane + 32 * i] = qi == 0 ? ag[i] : (qi == 1 ? ab[i] : as[i]);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < 32 * NV; idx += kLnbWarps * 32) {
+      float4 t = red[0][idx];
+#pragma unroll
+      for (int w = 1; w < kLnbWarps; w++) {
+        const float4 o = red[w][idx];
+        t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
+      }
+      out[qi * (D / 4) + idx] = t;
+    }
+    __syncthreads();
   }
 }
 
@@ -227,8 +238,8 @@ constexpr int kGcRows = 512;  // rows per block
 // [kGcRows r, ...), one row per warp at a time; each warp writes its column
 // partial row of dx.
 __global__ void __launch_bounds__(256)
-gelu_backward_colsum_kernel(const float* __restrict__ x, const float* __restrict__ dy,
-                            float* __restrict__ dx, float* __restrict__ dx_lo,
+gelu_backward_colsum_kernel(const float* __restrict__ x, const float* dy,
+                            float* dx, float* __restrict__ dx_lo,
                             float* __restrict__ partial, int64_t rows, int64_t n) {
   const float inv_sqrt_2 = 0x1.6a09e6p-1f, inv_sqrt_2pi = 0x1.988454p-2f;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -259,14 +270,46 @@ gelu_backward_colsum_kernel(const float* __restrict__ x, const float* __restrict
   }
 }
 
-// Sums `count` partial rows of width `width` (row stride `stride`) in order.
-__global__ void reduce_partials_kernel(const float* __restrict__ partial, int count,
-                                       int64_t width, int64_t stride, float* __restrict__ out) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= width) return;
+// Column sums of `count` partial rows: quantity q = blockIdx.y reads columns
+// [q width, q width + width) of each row (row stride `stride`) and writes
+// out[q].  A block covers 32 columns; warp w sums rows w, w + 8, ... (each
+// warp load is one 128-byte row segment), then the 8 warp sums are added in
+// warp order, so the result does not depend on timing.
+struct PartialOuts {
+  float* out[3];
+};
+__global__ void __launch_bounds__(256)
+reduce_partials_kernel(const float* __restrict__ partial, int count, int64_t width,
+                       int64_t stride, PartialOuts outs) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int q = blockIdx.y;
+  const int64_t j = (int64_t)blockIdx.x * 32 + tx;
   float s = 0.0f;
-  for (int b = 0; b < count; b++) s += partial[(size_t)b * stride + j];
-  out[j] = s;
+  if (j < width) {
+    const float* col = partial + (int64_t)q * width + j;
+#pragma unroll 4
+    for (int b = ty; b < count; b += 8) s += col[(int64_t)b * stride];
+  }
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && j < width) {
+    float t = red[0][tx];
+#pragma unroll
+    for (int w = 1; w < 8; w++) t += red[w][tx];
+    float* o = q == 0 ? outs.out[0] : (q == 1 ? outs.out[1] : outs.out[2]);
+    o[j] = t;
+  }
+}
+
+// Launches reduce_partials_kernel for 1 to 3 quantities (o1, o2 optional).
+void reduce_partials(const float* partial, int count, int64_t width, int64_t stride, float* o0,
+                     float* o1, float* o2, cudaStream_t stream) {
+  PartialOuts outs{{o0, o1, o2}};
+  const unsigned nq = o2 ? 3u : (o1 ? 2u : 1u);
+  dim3 grid(ceil_div(width, 32), nq);
+  reduce_partials_kernel<<<grid, 256, 0, stream>>>(partial, count, width, stride, outs);
+  count_launch();
 }
 
 // ---- activations -------------------------------------------------------------
@@ -474,7 +517,7 @@ void layer_norm_forward(const float* x, const float* gamma, const float* beta, f
 
 size_t ln_workspace_floats(size_t rows, size_t d) {
   const size_t simt = (size_t)ln_backward_blocks(rows) * 2 * d;
-  const size_t regs = (size_t)ln_backward_rows_blocks(rows) * kLnbWarps * 3 * d;
+  const size_t regs = (size_t)ln_backward_rows_blocks(rows) * 3 * d;
   const size_t cols = colsum_workspace_floats(rows, d);
   return std::max(std::max(simt, regs), cols);
 }
@@ -503,16 +546,8 @@ void layer_norm_backward(const float* x, const float* gamma, const float* mean, 
       LNB_CASE(8)
 #undef LNB_CASE
     }
-    const int parts = blocks * kLnbWarps;
-    const int64_t stride = (int64_t)nq * d;
-    reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace, parts, (int64_t)d,
-                                                                 stride, dgamma);
-    reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + d, parts,
-                                                                 (int64_t)d, stride, dbeta);
-    if (dsum)
-      reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + 2 * d, parts,
-                                                                   (int64_t)d, stride, dsum);
-    count_launch(dsum ? 4 : 3);
+    count_launch();
+    reduce_partials(workspace, blocks, (int64_t)d, (int64_t)nq * d, dgamma, dbeta, dsum, stream);
     return;
   }
   const int blocks = ln_backward_blocks(rows);
@@ -522,11 +557,8 @@ void layer_norm_backward(const float* x, const float* gamma, const float* mean, 
   ln_backward_kernel<<<blocks, kLnWarps * 32, smem, stream>>>(
       x, gamma, mean, rstd, dy, dx, accumulate, workspace, (int64_t)rows, (int64_t)d,
       dx_lo ? dx_hi : nullptr, dx_lo);
-  reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace, blocks, (int64_t)d,
-                                                               (int64_t)(2 * d), dgamma);
-  reduce_partials_kernel<<<ceil_div(d, 256), 256, 0, stream>>>(workspace + d, blocks, (int64_t)d,
-                                                               (int64_t)(2 * d), dbeta);
-  count_launch(3);
+  count_launch();
+  reduce_partials(workspace, blocks, (int64_t)d, (int64_t)(2 * d), dgamma, dbeta, nullptr, stream);
   if (dsum) column_sum(dx, dsum, rows, d, workspace, stream);
 }
 
@@ -632,9 +664,9 @@ void gelu_backward_colsum(const float* x, const float* dy, float* dx, float* dx_
   dim3 grid((unsigned)(n / 128), chunks);
   gelu_backward_colsum_kernel<<<grid, 256, 0, stream>>>(x, dy, dx, dx_lo, workspace, (int64_t)rows,
                                                         (int64_t)n);
-  reduce_partials_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(workspace, (int)chunks * 8,
-                                                               (int64_t)n, (int64_t)n, dsum);
-  count_launch(2);
+  count_launch();
+  reduce_partials(workspace, (int)chunks * 8, (int64_t)n, (int64_t)n, dsum, nullptr, nullptr,
+                  stream);
 }
 
 size_t colsum_workspace_floats(size_t rows, size_t n) {
@@ -650,9 +682,8 @@ void column_sum(const float* dy, float* out, size_t rows, size_t n, float* works
   }
   dim3 grid(ceil_div(n, 32), chunks);
   colsum_partial_kernel<<<grid, 256, 0, stream>>>(dy, dy_lo, workspace, (int64_t)rows, (int64_t)n);
-  reduce_partials_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(workspace, (int)chunks, (int64_t)n,
-                                                               (int64_t)n, out);
-  count_launch(2);
+  count_launch();
+  reduce_partials(workspace, (int)chunks, (int64_t)n, (int64_t)n, out, nullptr, nullptr, stream);
 }
 
 void rope_apply(const float* x, float* y, const float* cos_table, const float* sin_table, size_t N,

@@ -82,8 +82,8 @@ struct et_b200_lm {
   float *logits = nullptr, *logits_lo = nullptr, *loss_rows = nullptr, *loss_mean = nullptr;
   // backward scratch
   float *dx = nullptr, *dxhi = nullptr, *dxlo = nullptr, *dtmp = nullptr, *dqkv = nullptr,
-        *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *dg = nullptr, *delta = nullptr;
-  float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *gelu_ws = nullptr;
+        *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *delta = nullptr;
+  float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *epi_ws = nullptr;
   // attention: per-layer prepared Q/K/V (written by the forward, reused by
   // the backward) and one shared backward scratch
   std::vector<float*> attn_qkv_ws;
@@ -193,24 +193,38 @@ void split(et_b200_lm* lm, float* x, float* lo, size_t n) {
 
 // ---- linear wrappers ---------------------------------------------------------
 
+// y = x W^T + bias, optionally with a fused epilogue (GemmArgs::epilogue):
+// RESIDUAL adds `aux`; GELU_FWD also writes GELU(y) to out2 (hi) / out3 (lo).
 void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t rows, int64_t din,
-                    int64_t dout, int wt, const float* bias, float* y) {
+                    int64_t dout, int wt, const float* bias, float* y,
+                    int epilogue = GEMM_EPI_PLAIN, const float* aux = nullptr,
+                    float* out2 = nullptr, float* out3 = nullptr) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)dout; g.K = (int)din;
   g.A = x; g.A_lo = xlo; g.lda = din; g.a_kmajor = true;
   g.B = lm->W(wt); g.B_lo = lm->Wlo(wt); g.ldb = din; g.b_kmajor = true;
   g.C = y; g.ldc = dout; g.bias = bias; g.accumulate = false;
+  g.epilogue = epilogue; g.aux = aux; g.out2 = out2; g.out3 = out3;
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->precision, lm->stream);
 }
 
+// dX = dY W; with gelu_in the epilogue applies the GELU backward of the layer
+// whose output this is (dX = dY W * GELU'(gelu_in), hi into dxo and lo into
+// dxo_lo) and writes the column sums (that layer's bias gradient) to dsum.
 void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int64_t rows,
-                        int64_t din, int64_t dout, int wt, float* dxo) {
+                        int64_t din, int64_t dout, int wt, float* dxo,
+                        const float* gelu_in = nullptr, float* dxo_lo = nullptr,
+                        float* dsum = nullptr) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)din; g.K = (int)dout;
   g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = true;
   g.B = lm->W(wt); g.B_lo = lm->Wlo(wt); g.ldb = din; g.b_kmajor = false;
   g.C = dxo; g.ldc = din; g.bias = nullptr; g.accumulate = false;
+  if (gelu_in != nullptr) {
+    g.epilogue = GEMM_EPI_GELU_BWD; g.aux = gelu_in; g.out2 = dxo_lo; g.dsum = dsum;
+    g.epi_ws = lm->epi_ws;
+  }
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->precision, lm->stream);
 }
@@ -285,26 +299,19 @@ void forward(et_b200_lm* lm) {
           attention_forward(p, AttnOut{a.ao, lm->T * d, lm->Dh, d, a.aolo}, a.am, a.al, s);
     }
     if (lm->three && !lm->attn_prepared[l]) split(lm, a.ao, a.aolo, R * d);
-    linear_forward(lm, a.ao, a.aolo, R, d, d, lm->lt(l, T_WO), lm->Pp(lm->lt(l, T_BO)), lm->dtmp);
-    {
-      Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * d);
-      add_tensors(a.x, lm->dtmp, a.xmid, R * d, s);
-    }
+    // x' = x + o Wo^T + bo (the residual add in the GEMM epilogue)
+    linear_forward(lm, a.ao, a.aolo, R, d, d, lm->lt(l, T_WO), lm->Pp(lm->lt(l, T_BO)), a.xmid,
+                   GEMM_EPI_RESIDUAL, a.x);
     {
       Mark mk(lm, P_NORM, 0, 8.0 * R * d);
       layer_norm_forward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), lm->Pp(lm->lt(l, T_LN2B)), lm->eps,
                          a.h2, a.mu2, a.rs2, R, d, s, a.h2lo);
     }
-    linear_forward(lm, a.h2, a.h2lo, R, d, F, lm->lt(l, T_W1), lm->Pp(lm->lt(l, T_B1)), a.u);
-    {
-      Mark mk(lm, P_ELEMENTWISE, 0, 8.0 * R * F);
-      gelu_forward(a.u, a.g, R * F, s, a.glo);
-    }
-    linear_forward(lm, a.g, a.glo, R, F, d, lm->lt(l, T_W2), lm->Pp(lm->lt(l, T_B2)), lm->dtmp);
-    {
-      Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * d);
-      add_tensors(a.xmid, lm->dtmp, xnext, R * d, s);
-    }
+    // u = h2 W1^T + b1 and g = GELU(u) (hi/lo) from the same epilogue
+    linear_forward(lm, a.h2, a.h2lo, R, d, F, lm->lt(l, T_W1), lm->Pp(lm->lt(l, T_B1)), a.u,
+                   GEMM_EPI_GELU_FWD, nullptr, a.g, a.glo);
+    linear_forward(lm, a.g, a.glo, R, F, d, lm->lt(l, T_W2), lm->Pp(lm->lt(l, T_B2)), xnext,
+                   GEMM_EPI_RESIDUAL, a.xmid);
   }
   {
     Mark mk(lm, P_NORM, 0, 8.0 * R * d);
@@ -355,13 +362,10 @@ void backward(et_b200_lm* lm) {
     // gradient) from the LayerNorm backward above
     const float* dyh = three ? lm->dxhi : lm->dx;
     const float* dyl = three ? lm->dxlo : nullptr;
-    linear_backward_dx(lm, dyh, dyl, R, F, d, lm->lt(l, T_W2), lm->dg);
+    // du = (dy W2) * GELU'(u) (hi/lo) and the b1 gradient, from the epilogue
+    linear_backward_dx(lm, dyh, dyl, R, F, d, lm->lt(l, T_W2), lm->du, a.u, lm->dulo,
+                       lm->G(lm->lt(l, T_B1)));
     linear_backward_dw(lm, dyh, dyl, a.g, a.glo, R, F, d, lm->G(lm->lt(l, T_W2)));
-    {
-      Mark mk(lm, P_ELEMENTWISE, 0, 12.0 * R * F);
-      gelu_backward_colsum(a.u, lm->dg, lm->du, lm->dulo, lm->G(lm->lt(l, T_B1)), lm->gelu_ws, R,
-                           F, s);  // + the b1 gradient
-    }
     linear_backward_dx(lm, lm->du, lm->dulo, R, d, F, lm->lt(l, T_W1), lm->dtmp);
     linear_backward_dw(lm, lm->du, lm->dulo, a.h2, a.h2lo, R, d, F, lm->G(lm->lt(l, T_W1)));
     {
@@ -594,7 +598,6 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->dtmp = dalloc<float>(lm, R * d, &err);
   lm->dqkv = dalloc<float>(lm, R * 3 * d, &err);
   lm->du = dalloc<float>(lm, R * F, &err);
-  lm->dg = dalloc<float>(lm, R * F, &err);
   lm->delta = dalloc<float>(lm, R * lm->H, &err);
   if (lm->three) {
     lm->xflo = dalloc<float>(lm, R * d, &err);
@@ -608,7 +611,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->ln_ws = dalloc<float>(lm, ln_workspace_floats(R, d), &err);
   lm->col_ws = dalloc<float>(lm, colsum_workspace_floats(R, widest), &err);
   lm->emb_scratch = dalloc<uint8_t>(lm, embedding_scratch_bytes(R, V), &err);
-  lm->gelu_ws = dalloc<float>(lm, gelu_colsum_workspace_floats(R, F), &err);
+  lm->epi_ws = dalloc<float>(lm, gemm_epilogue_ws_floats((int)R, (int)F), &err);
   // split-K partials for the weight-gradient GEMMs of the layers (K = rows)
   lm->splitk_floats = gemm_splitk_floats((int)std::max<int64_t>(3 * d, F), (int)std::max<int64_t>(d, F));
   lm->splitk_ws = dalloc<float>(lm, lm->splitk_floats, &err);
