@@ -464,7 +464,7 @@ bool launch_fwd_tc(const AttnParams& p, AttnOut o, float* m, float* l, cudaStrea
       !make_map(&mkh, w.kh, DH, krows, DH, KN, SW) || !make_map(&mkl, w.kl, DH, krows, DH, KN, SW) ||
       !make_map(&mvh, w.vh, DH, krows, DH, KN, SW32) || !make_map(&mvl, w.vl, DH, krows, DH, KN, SW32))
     return false;
-  attention_prepare_qkv(p, w, stream);
+  if (!p.qkv_ready) attention_prepare_qkv(p, w, stream);
   TcFwdArgs a{device_error_word()};
   cudaFuncSetAttribute(attn_fwd_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        L::SMEM);
@@ -491,6 +491,36 @@ void attention_prepare_qkv(const AttnParams& p, const AttnWs& w, cudaStream_t st
   prep(p.k, p.Hkv, p.Tk, p.k_cos, p.k_sin, p.k_rope_batched, w.kh, w.kl);
   prep(p.v, p.Hkv, p.Tk, nullptr, nullptr, 0, w.vh, w.vl);
   count_launch(3);
+}
+
+bool attention_qkv_prep(const AttnParams& p, QkvPrep* out) {
+  if (p.ws == nullptr || (reinterpret_cast<uintptr_t>(p.ws) & 15)) return false;
+  if (p.Dh != 32 && p.Dh != 64 && p.Dh != 128) return false;
+  if (p.Tq != p.Tk) return false;  // one qkv matrix holds every operand
+  const AttnWs w = attn_ws(p);
+  QkvPrep q{};
+  q.T = p.Tq; q.Hq = p.Hq; q.Hkv = p.Hkv; q.Dh = p.Dh;
+  q.q_cos = p.q_cos; q.q_sin = p.q_sin; q.k_cos = p.k_cos; q.k_sin = p.k_sin;
+  q.q_rope_batched = p.q_rope_batched; q.k_rope_batched = p.k_rope_batched;
+  q.qh = w.qh; q.ql = w.ql; q.kh = w.kh; q.kl = w.kl; q.vh = w.vh; q.vl = w.vl;
+  *out = q;
+  return true;
+}
+
+void attention_prepare_from_qkv(const float* qkv, int64_t ld, int rows, const QkvPrep& q,
+                                cudaStream_t stream) {
+  const int B = rows / q.T;
+  AttnParams p{};
+  p.B = B; p.Hq = q.Hq; p.Hkv = q.Hkv; p.Tq = q.T; p.Tk = q.T; p.Dh = q.Dh;
+  const int64_t sb = (int64_t)q.T * ld;
+  p.q = AttnTensor{qkv, sb, q.Dh, ld};
+  p.k = AttnTensor{qkv + (int64_t)q.Hq * q.Dh, sb, q.Dh, ld};
+  p.v = AttnTensor{qkv + (int64_t)(q.Hq + q.Hkv) * q.Dh, sb, q.Dh, ld};
+  p.q_cos = q.q_cos; p.q_sin = q.q_sin; p.k_cos = q.k_cos; p.k_sin = q.k_sin;
+  p.q_rope_batched = q.q_rope_batched; p.k_rope_batched = q.k_rope_batched;
+  AttnWs w{};
+  w.qh = q.qh; w.ql = q.ql; w.kh = q.kh; w.kl = q.kl; w.vh = q.vh; w.vl = q.vl;
+  attention_prepare_qkv(p, w, stream);
 }
 
 size_t attention_qkv_workspace_floats(const AttnParams& p) {

@@ -161,6 +161,7 @@ struct TcArgs {
   // pair kernel: every row pointer and ldc allow float4 access and N % 4 == 0,
   // so the epilogue goes through the shared-memory transpose (coalesced rows)
   int staged;
+  QkvPrep qkv;  // GEMM_EPI_QKV (staged epilogue only)
   int* error;
 };
 
@@ -441,6 +442,66 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   }
 }
 
+// Section (0 Q, 1 K, 2 V), head and column within the head of qkv column n.
+__device__ __forceinline__ void qkv_column(const QkvPrep& q, int n, int& sec, int& h, int& j) {
+  const int dq = q.Hq * q.Dh, dk = q.Hkv * q.Dh;
+  int hc;
+  if (n < dq) { sec = 0; hc = n; }
+  else if (n < dq + dk) { sec = 1; hc = n - dq; }
+  else { sec = 2; hc = n - dq - dk; }
+  h = hc / q.Dh;
+  j = hc - h * q.Dh;
+}
+// RoPE coefficients (cos, sin of pair n / 2, cos, sin of pair n / 2 + 1) for
+// qkv columns [n, n + 4) of row `row`; unused (zeros) for V or without tables.
+// (Loading these ahead of the accumulator wait, like the aux rows, measured
+// slower.)
+__device__ __forceinline__ float4 qkv_rope_coeffs(const QkvPrep& q, int row, int n) {
+  int sec, h, j;
+  qkv_column(q, n, sec, h, j);
+  const float* ct = sec == 0 ? q.q_cos : (sec == 1 ? q.k_cos : nullptr);
+  if (ct == nullptr) return make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* st = sec == 0 ? q.q_sin : q.k_sin;
+  const int batched = sec == 0 ? q.q_rope_batched : q.k_rope_batched;
+  const int b = row / q.T, t = row - b * q.T;
+  // j % 4 == 0 and Dh / 2 even: the two pairs' entries are one aligned float2
+  const int64_t ti = (int64_t)(batched ? b * q.T + t : t) * (q.Dh >> 1) + (j >> 1);
+  const float2 c = __ldg(reinterpret_cast<const float2*>(ct + ti));
+  const float2 s = __ldg(reinterpret_cast<const float2*>(st + ti));
+  return make_float4(c.x, s.x, c.y, s.y);
+}
+// Attention operands of qkv columns [n, n + 4) of row `row` (values x =
+// y + bias, as stored to C): head-major TF32 hi / lo copies, with the RoPE
+// rotation (coefficients cs from qkv_rope_coeffs) of the pairs (n, n + 1),
+// (n + 2, n + 3) for Q and K (attention_tc.cu attn_prepare_kernel computes
+// the same values).
+__device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int row, int n, float4 x,
+                                               float4 cs) {
+  int sec, h, j;
+  qkv_column(q, n, sec, h, j);
+  const int b = row / q.T, t = row - b * q.T;
+  const float* ct = sec == 0 ? q.q_cos : (sec == 1 ? q.k_cos : nullptr);
+  if (ct != nullptr) {
+    const float c0 = cs.x, s0 = cs.y, c1 = cs.z, s1 = cs.w;
+    const float x0 = rn_sub(rn_mul(x.x, c0), rn_mul(x.y, s0));
+    const float x1 = rn_add(rn_mul(x.x, s0), rn_mul(x.y, c0));
+    const float x2 = rn_sub(rn_mul(x.z, c1), rn_mul(x.w, s1));
+    const float x3 = rn_add(rn_mul(x.z, s1), rn_mul(x.w, c1));
+    x = make_float4(x0, x1, x2, x3);
+  }
+  const int H = sec == 0 ? q.Hq : q.Hkv;
+  const int64_t o = (((int64_t)b * H + h) * q.T + t) * q.Dh + j;
+  float* hi = sec == 0 ? q.qh : (sec == 1 ? q.kh : q.vh);
+  float* lo = sec == 0 ? q.ql : (sec == 1 ? q.kl : q.vl);
+  float4 h4, l4;
+  tf32_split(x.x, h4.x, l4.x);
+  tf32_split(x.y, h4.y, l4.y);
+  tf32_split(x.z, h4.z, l4.z);
+  tf32_split(x.w, h4.w, l4.w);
+  *reinterpret_cast<float4*>(hi + o) = h4;
+  *reinterpret_cast<float4*>(lo + o) = l4;
+}
+
 // ---- 2-SM (CTA pair) 3xTF32 kernel ---------------------------------------------
 //
 // A cluster of two CTAs on the two SMs of a TPC computes a 256 x BN output
@@ -703,6 +764,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             pre[it] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (has_aux && row < args.M && col_ok)
               pre[it] = __ldg(reinterpret_cast<const float4*>(args.aux + (int64_t)row * ldc + n));
+
           }
           float v[32];
           tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c), v);
@@ -766,6 +828,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
                 *reinterpret_cast<float4*>(args.out3 + off) = lo;
               }
               *reinterpret_cast<float4*>(args.out2 + off) = g;
+            } else if (epi == GEMM_EPI_QKV) {
+              qkv_prep_store(args.qkv, row, n, x, qkv_rope_coeffs(args.qkv, row, n));
             }
           }
           if (epi == GEMM_EPI_GELU_BWD) {
@@ -1032,16 +1096,6 @@ bool gemm_tc_supported(const GemmArgs& g) {
   return encode_fn() != nullptr;
 }
 
-// out[n] = sum over p of part[p * N + n], p ascending.
-__global__ void colpart_reduce_kernel(const float* __restrict__ part, int parts, int N,
-                                      float* __restrict__ out) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  float s = 0.0f;
-  for (int p = 0; p < parts; p++) s += part[(int64_t)p * N + n];
-  out[n] = s;
-}
-
 // 3xTF32 on CTA pairs: 256 x BN tiles, 3-stage ring of 64 KB per SM.
 template <int BN, int STAGES>
 void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
@@ -1070,11 +1124,15 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   a.out2 = g.out2;
   a.out3 = g.out3;
   a.colpart = g.epi_ws;
+  if (g.epilogue == GEMM_EPI_QKV) a.qkv = *g.qkv;
   {
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     a.staged = (g.ldc % 4 == 0) && (g.N % 4 == 0) && al(g.C) && al(g.aux) && al(g.out2) &&
                al(g.out3) && al(g.bias) && al(g.epi_ws) && al(g.workspace);
   }
+  // the QKV operands are written by the staged epilogue only
+  const bool prep_after = g.epilogue == GEMM_EPI_QKV && !a.staged;
+  if (prep_after) a.epilogue = GEMM_EPI_PLAIN;
   const int tiles = a.tiles_m * a.tiles_n;
   const int nkb = (g.K + L::BK - 1) / L::BK;
   const int pairs = sm_count() / 2;
@@ -1094,10 +1152,9 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
                                                                             a);
   count_launch();
   if (g.epilogue == GEMM_EPI_GELU_BWD) {
-    colpart_reduce_kernel<<<(g.N + 255) / 256, 256, 0, stream>>>(g.epi_ws, a.tiles_m * 8, g.N,
-                                                                 g.dsum);
-    count_launch();
+    reduce_partials(g.epi_ws, a.tiles_m * 8, g.N, g.N, g.dsum, nullptr, nullptr, stream);
   }
+  if (prep_after) attention_prepare_from_qkv(g.C, g.ldc, g.M, *g.qkv, stream);
   if (a.splits > 1) {
     const int64_t total = (int64_t)g.M * g.N;
     const int64_t want = (total + 255) / 256;
@@ -1125,6 +1182,7 @@ void epilogue_after(const GemmArgs& g, cudaStream_t stream) {
       gelu_backward_colsum(g.aux, g.C, g.C, g.out2, g.dsum, g.epi_ws, (size_t)g.M, (size_t)g.N,
                            stream);
       break;
+    case GEMM_EPI_QKV: attention_prepare_from_qkv(g.C, g.ldc, g.M, *g.qkv, stream); break;
     default: break;
   }
 }

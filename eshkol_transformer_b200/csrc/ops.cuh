@@ -92,6 +92,11 @@ void embedding_backward(const int64_t* ids, const float* dy, const float* base,
                         void* scratch, cudaStream_t stream);
 // out[n] = sum over rows of dy[r, n] (fixed-order two-stage).
 size_t colsum_workspace_floats(size_t rows, size_t n);
+// out_q[j] = sum over p of partial[p * stride + q * width + j] for the
+// quantities q = 0, 1, 2 whose outputs o0, o1, o2 are given (o1, o2 may be
+// null); a fixed summation order (deterministic).
+void reduce_partials(const float* partial, int count, int64_t width, int64_t stride, float* o0,
+                     float* o1, float* o2, cudaStream_t stream);
 // dy_lo (optional) is added to dy element by element first (hi + lo is exact).
 void column_sum(const float* dy, float* out, size_t rows, size_t n,
                 float* workspace, cudaStream_t stream, const float* dy_lo = nullptr);
@@ -147,7 +152,27 @@ struct AttnParams {
   float* ws;
   float* ws_grad;
   int ws_ready;
+  // qkv_ready: ws already holds the prepared Q/K/V (the fused QKV GEMM
+  // epilogue wrote them), so the forward skips that pass as well.
+  int qkv_ready;
 };
+// Where a fused QKV projection writes the attention operands: the RoPE'd Q
+// and K and plain V of a [B*T, (Hq + 2 Hkv) Dh] row-major qkv matrix (the
+// columns Q | K | V, head-major within each), split into TF32 hi / residual
+// lo, each [B, H, T, Dh] (the layout attention_prepare_qkv writes).
+struct QkvPrep {
+  int T, Hq, Hkv, Dh;
+  const float *q_cos, *q_sin, *k_cos, *k_sin;  // null: no RoPE
+  int q_rope_batched, k_rope_batched;
+  float *qh, *ql, *kh, *kl, *vh, *vl;
+};
+// The QkvPrep of p's workspace (p.ws set, p.q / p.k / p.v columns of one qkv
+// matrix); false when the tensor-core attention cannot use it (Dh not
+// 32 / 64 / 128, or no workspace).
+bool attention_qkv_prep(const AttnParams& p, QkvPrep* out);
+// The same operands from a qkv matrix already in memory (row stride ld).
+void attention_prepare_from_qkv(const float* qkv, int64_t ld, int rows, const QkvPrep& q,
+                                cudaStream_t stream);
 size_t attention_workspace_floats(const AttnParams& p);
 size_t attention_qkv_workspace_floats(const AttnParams& p);
 size_t attention_grad_workspace_floats(const AttnParams& p);
@@ -207,14 +232,22 @@ struct GemmArgs {
   //   GELU_BWD  d = y * GELU'(aux) (aux = the GELU input); C = d, or its TF32
   //             hi with out2 = lo; dsum[n] = column sums of d (the bias
   //             gradient), through `epi_ws` (gemm_epilogue_ws_floats)
+  //   QKV       C = y + bias, and the attention operands of C (QkvPrep `qkv`)
   int epilogue;
   const float* aux;
   float* out2;
   float* out3;
   float* dsum;
   float* epi_ws;
+  const QkvPrep* qkv;
 };
-enum { GEMM_EPI_PLAIN = 0, GEMM_EPI_RESIDUAL = 1, GEMM_EPI_GELU_FWD = 2, GEMM_EPI_GELU_BWD = 3 };
+enum {
+  GEMM_EPI_PLAIN = 0,
+  GEMM_EPI_RESIDUAL = 1,
+  GEMM_EPI_GELU_FWD = 2,
+  GEMM_EPI_GELU_BWD = 3,
+  GEMM_EPI_QKV = 4
+};
 // Scratch floats split-K may use for an M x N output.
 size_t gemm_splitk_floats(int M, int N);
 // Scratch floats the GELU_BWD epilogue needs for an M x N output.

@@ -302,15 +302,6 @@ reduce_partials_kernel(const float* __restrict__ partial, int count, int64_t wid
   }
 }
 
-// Launches reduce_partials_kernel for 1 to 3 quantities (o1, o2 optional).
-void reduce_partials(const float* partial, int count, int64_t width, int64_t stride, float* o0,
-                     float* o1, float* o2, cudaStream_t stream) {
-  PartialOuts outs{{o0, o1, o2}};
-  const unsigned nq = o2 ? 3u : (o1 ? 2u : 1u);
-  dim3 grid(ceil_div(width, 32), nq);
-  reduce_partials_kernel<<<grid, 256, 0, stream>>>(partial, count, width, stride, outs);
-  count_launch();
-}
 
 // ---- activations -------------------------------------------------------------
 
@@ -505,6 +496,16 @@ unsigned grid_for(int64_t n, int threads) {
 }
 
 }  // namespace
+
+// Launches reduce_partials_kernel for 1 to 3 quantities (o1, o2 optional).
+void reduce_partials(const float* partial, int count, int64_t width, int64_t stride, float* o0,
+                     float* o1, float* o2, cudaStream_t stream) {
+  PartialOuts outs{{o0, o1, o2}};
+  const unsigned nq = o2 ? 3u : (o1 ? 2u : 1u);
+  dim3 grid(ceil_div(width, 32), nq);
+  reduce_partials_kernel<<<grid, 256, 0, stream>>>(partial, count, width, stride, outs);
+  count_launch();
+}
 
 void layer_norm_forward(const float* x, const float* gamma, const float* beta, float epsilon,
                         float* y, float* mean, float* rstd, size_t rows, size_t d,

@@ -194,17 +194,18 @@ void split(et_b200_lm* lm, float* x, float* lo, size_t n) {
 // ---- linear wrappers ---------------------------------------------------------
 
 // y = x W^T + bias, optionally with a fused epilogue (GemmArgs::epilogue):
-// RESIDUAL adds `aux`; GELU_FWD also writes GELU(y) to out2 (hi) / out3 (lo).
+// RESIDUAL adds `aux`; GELU_FWD also writes GELU(y) to out2 (hi) / out3 (lo);
+// QKV also writes the attention operands described by `qkv`.
 void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t rows, int64_t din,
                     int64_t dout, int wt, const float* bias, float* y,
                     int epilogue = GEMM_EPI_PLAIN, const float* aux = nullptr,
-                    float* out2 = nullptr, float* out3 = nullptr) {
+                    float* out2 = nullptr, float* out3 = nullptr, const QkvPrep* qkv = nullptr) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)dout; g.K = (int)din;
   g.A = x; g.A_lo = xlo; g.lda = din; g.a_kmajor = true;
   g.B = lm->W(wt); g.B_lo = lm->Wlo(wt); g.ldb = din; g.b_kmajor = true;
   g.C = y; g.ldc = dout; g.bias = bias; g.accumulate = false;
-  g.epilogue = epilogue; g.aux = aux; g.out2 = out2; g.out3 = out3;
+  g.epilogue = epilogue; g.aux = aux; g.out2 = out2; g.out3 = out3; g.qkv = qkv;
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->precision, lm->stream);
 }
@@ -290,10 +291,14 @@ void forward(et_b200_lm* lm) {
       layer_norm_forward(a.x, lm->Pp(lm->lt(l, T_LN1G)), lm->Pp(lm->lt(l, T_LN1B)), lm->eps, a.h1,
                          a.mu1, a.rs1, R, d, s, a.h1lo);
     }
-    linear_forward(lm, a.h1, a.h1lo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->Pp(lm->lt(l, T_BQKV)),
-                   a.qkv);
     {
+      // the QKV epilogue also writes the attention operands (RoPE'd, hi/lo, head-major)
       AttnParams p = attn_params(lm, a.qkv, l);
+      QkvPrep prep;
+      p.qkv_ready = attention_qkv_prep(p, &prep) ? 1 : 0;
+      linear_forward(lm, a.h1, a.h1lo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->Pp(lm->lt(l, T_BQKV)),
+                     a.qkv, p.qkv_ready ? GEMM_EPI_QKV : GEMM_EPI_PLAIN, nullptr, nullptr,
+                     nullptr, p.qkv_ready ? &prep : nullptr);
       Mark mk(lm, P_ATTN_FWD, attn_flop(lm, 2), 0);
       lm->attn_prepared[l] =
           attention_forward(p, AttnOut{a.ao, lm->T * d, lm->Dh, d, a.aolo}, a.am, a.al, s);
