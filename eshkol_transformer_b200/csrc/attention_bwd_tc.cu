@@ -81,27 +81,6 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
 }
 
-// Scales n columns [first, first + n) of an accumulator row and applies the
-// RoPE backward rotation to each (even, odd) pair when a table is given
-// (table entry trow + (col0 + i - first) / 2), in place.
-template <int N>
-__device__ __forceinline__ void grad_row(float (&v)[32], int first, float scale, const float* ct,
-                                         const float* st, int64_t trow, int col0) {
-#pragma unroll
-  for (int i = first; i < first + N; i += 2) {
-    float x0 = rn_mul(v[i], scale), x1 = rn_mul(v[i + 1], scale);
-    if (ct != nullptr) {
-      const int64_t ti = trow + (col0 + i - first) / 2;
-      const float c = ct[ti], s = st[ti];
-      const float a = rn_mul(x0, c), bb = rn_mul(x1, s), cc = rn_mul(x0, s), dd = rn_mul(x1, c);
-      x0 = rn_add(a, bb);
-      x1 = rn_add(-cc, dd);
-    }
-    v[i] = x0;
-    v[i + 1] = x1;
-  }
-}
-
 // Number of entries of the ascending array a[0..n) that are below x.
 __device__ __forceinline__ int count_below(const int64_t* a, int n, int64_t x) {
   int lo = 0, hi = n;
@@ -465,43 +444,40 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
       if (ok) ok = role_wait(B_(KB_DONE), last, a.error, abort);
     }
     ok = __all_sync(0xffffffffu, ok);
-    // warps 0-3: dK (scale, RoPE backward), warps 4-7: dV, staged in the
-    // free operand buffers and written out with coalesced stores; with .lo
-    // outputs the TF32 hi parts go first, then the residuals
+    // warps 0-3 stage the raw dK rows, warps 4-7 the dV rows, in the free
+    // operand buffers; the scale, the RoPE backward rotation (dK) and the
+    // hi/lo split are applied while the rows are written out (coalesced)
     const uint32_t stage = base + (uint32_t)(khalf * 128 * (DH + 4) * 4);
-    const int parts = (dk.lo != nullptr && dv.lo != nullptr) ? 2 : 1;
-    for (int part = 0; part < parts; part++) {
-      if (ok) {
-        tc_fence_after();
-        const float* ct = khalf == 0 ? p.k_cos : nullptr;
-        const float* sn = khalf == 0 ? p.k_sin : nullptr;
-        const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + tk : tk) * (DH / 2);
+    if (ok) {
+      tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < DH / 32; c++) {
-          float v[32];
-          if (n_it > 0) {
-            tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
-          } else {
+      for (int c = 0; c < DH / 32; c++) {
+        float v[32];
+        if (n_it > 0) {
+          tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = 0.0f;
-          }
-          grad_row<32>(v, 0, khalf == 0 ? p.scale : 1.0f, ct, sn, trw, 32 * c);
-          if (parts == 2) split_part(v, part);
-          stage_row32(stage, DH, row, 32 * c, v, 0, 32);
+          for (int i = 0; i < 32; i++) v[i] = 0.0f;
         }
+        stage_row32(stage, DH, row, 32 * c, v, 0, 32);
       }
-      named_sync(1, SOFT);
-      if (ok) {
-        const int rows = min(BK, p.Tk - k0);
-        for (int t = 0; t < 2; t++) {
-          const AttnOut& out = t == 0 ? dk : dv;
-          float* dst = part == 0 ? out.ptr : out.lo;
-          store_staged_rows(base + (uint32_t)(t * 128 * (DH + 4) * 4), DH, rows,
-                            dst + b * out.sb + hkv * out.sh + (int64_t)k0 * out.st, out.st, tid,
-                            SOFT);
-        }
-      }
-      named_sync(1, SOFT);
+    }
+    named_sync(1, SOFT);
+    if (ok) {
+      const bool split = dk.lo != nullptr && dv.lo != nullptr;
+      const int rows = min(BK, p.Tk - k0);
+      const int64_t ko = b * dk.sb + hkv * dk.sh + (int64_t)k0 * dk.st;
+      store_rows_split(base, DH, rows, dk.ptr + ko, split ? dk.lo + ko : nullptr, dk.st, tid, SOFT,
+                       [&](int r, int c4, float4& v) {
+                         const int t = k0 + r;
+                         const int64_t trw =
+                             (int64_t)(p.k_rope_batched ? b * p.Tk + t : t) * (DH / 2);
+                         grad_rotate4(v, p.scale, p.k_cos, p.k_sin, trw, c4);
+                       });
+      const int64_t vo = b * dv.sb + hkv * dv.sh + (int64_t)k0 * dv.st;
+      store_rows_split(base + (uint32_t)(128 * (DH + 4) * 4), DH, rows, dv.ptr + vo,
+                       split ? dv.lo + vo : nullptr, dv.st, tid, SOFT,
+                       [](int, int, float4&) {});
     }
   }
   tc_fence_before();
@@ -780,7 +756,6 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
       if (ok) ok = role_wait(B_(QB_DONE), last, a.error, abort);
     }
     ok = __all_sync(0xffffffffu, ok);
-    const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + tq : tq) * (DH / 2);
     auto load_dq = [&](int col, float (&v)[32]) {
       if (nkb > 0) {
         float w[32];
@@ -793,43 +768,37 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
         for (int i = 0; i < 32; i++) v[i] = 0.0f;
       }
     };
-    // dQ rows staged in the free K/V stages, written out with coalesced
-    // stores; with dq.lo the TF32 hi part first, then the residual
-    const int parts = dq.lo != nullptr ? 2 : 1;
-    for (int part = 0; part < parts; part++) {
-      if (ok) {
-        tc_fence_after();
-        if constexpr (DH >= 64) {
+    // raw dQ rows staged in the free K/V stages; the scale, the RoPE
+    // backward rotation and the hi/lo split are applied while the rows are
+    // written out (coalesced)
+    if (ok) {
+      tc_fence_after();
+      if constexpr (DH >= 64) {
 #pragma unroll
-          for (int c = 0; c < DH / 64; c++) {
-            const int col = khalf * (DH / 2) + 32 * c;
-            float v[32];
-            load_dq(col, v);
-            grad_row<32>(v, 0, p.scale, p.q_cos, p.q_sin, trw, col);
-            if (parts == 2) split_part(v, part);
-            stage_row32(base, DH, row, col, v, 0, 32);
-          }
-        } else {
+        for (int c = 0; c < DH / 64; c++) {
+          const int col = khalf * (DH / 2) + 32 * c;
           float v[32];
-          load_dq(0, v);
-          if (khalf == 0) {
-            grad_row<16>(v, 0, p.scale, p.q_cos, p.q_sin, trw, 0);
-            if (parts == 2) split_part(v, part);
-            stage_row32(base, DH, row, 0, v, 0, 16);
-          } else {
-            grad_row<16>(v, 16, p.scale, p.q_cos, p.q_sin, trw, 16);
-            if (parts == 2) split_part(v, part);
-            stage_row32(base, DH, row, 16, v, 16, 16);
-          }
+          load_dq(col, v);
+          stage_row32(base, DH, row, col, v, 0, 32);
         }
+      } else {
+        float v[32];
+        load_dq(0, v);
+        if (khalf == 0) stage_row32(base, DH, row, 0, v, 0, 16);
+        else stage_row32(base, DH, row, 16, v, 16, 16);
       }
-      named_sync(1, SOFT);
-      if (ok) {
-        float* dst = part == 0 ? dq.ptr : dq.lo;
-        store_staged_rows(base, DH, min(QM, p.Tq - q0),
-                          dst + b * dq.sb + hq * dq.sh + (int64_t)q0 * dq.st, dq.st, tid, SOFT);
-      }
-      named_sync(1, SOFT);
+    }
+    named_sync(1, SOFT);
+    if (ok) {
+      const int64_t qo = b * dq.sb + hq * dq.sh + (int64_t)q0 * dq.st;
+      store_rows_split(base, DH, min(QM, p.Tq - q0), dq.ptr + qo,
+                       dq.lo != nullptr ? dq.lo + qo : nullptr, dq.st, tid, SOFT,
+                       [&](int r, int c4, float4& v) {
+                         const int t = q0 + r;
+                         const int64_t trw =
+                             (int64_t)(p.q_rope_batched ? b * p.Tq + t : t) * (DH / 2);
+                         grad_rotate4(v, p.scale, p.q_cos, p.q_sin, trw, c4);
+                       });
     }
   }
   tc_fence_before();

@@ -126,6 +126,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
   uint8_t* smem = align1024(smem_raw);
   __shared__ int64_t kpos_s[2 * KN];     // key positions of the block, ring of 2
   __shared__ float xmax[2 * 2 * QM];     // [block parity][half][row] maxima / exp-sums
+  __shared__ float lrow_s[QM];           // row exp-sums for the output pass
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
   // barrier slots: full[NST] | empty[NST] | s_full[NSL] | pv_done[NSL] | p_ready[2] |
   // kp_full[2] | rows | pair[4] (the two softmax warps of a lane quarter)
@@ -406,41 +407,53 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
       row_max[ri] = empty ? 0.0f : m_used * kLn2;
       row_sum[ri] = empty ? 0.0f : lsum;
     }
-    // O / l staged in the free stages, written out with coalesced stores; with
-    // o.lo the TF32 hi part goes to o and the residual to o.lo (two rounds)
+    // the raw O rows are staged in the free stages with their exp-sums (0 for
+    // a row without admitted keys); o = O / l, split into the TF32 hi part
+    // (o) and the residual (o.lo) when o.lo is set, is formed while the rows
+    // are written out (coalesced)
+    if (khalf == 0) lrow_s[row] = (empty || nkb == 0) ? 0.0f : lsum;
     const uint32_t stage = base;
-    const int parts = o.lo != nullptr ? 2 : 1;
-    for (int part = 0; part < parts; part++) {
-      if (ok) {
-        tc_fence_after();
-        if constexpr (DH >= 64) {
+    if (ok) {
+      tc_fence_after();
+      if constexpr (DH >= 64) {
 #pragma unroll
-          for (int c = 0; c < DH / 64; c++) {
-            const int col = khalf * (DH / 2) + 32 * c;
-            float ov[32];
-            if (nkb > 0) tmem_ld32(trow + L::O + col, ov);
-#pragma unroll
-            for (int i = 0; i < 32; i++) ov[i] = (empty || nkb == 0) ? 0.0f : rn_div(ov[i], lsum);
-            if (parts == 2) split_part(ov, part);
-            stage_row32(stage, DH, row, col, ov, 0, 32);
-          }
-        } else {
+        for (int c = 0; c < DH / 64; c++) {
+          const int col = khalf * (DH / 2) + 32 * c;
           float ov[32];
-          if (nkb > 0) tmem_ld32(trow + L::O, ov);
+          if (nkb > 0) {
+            tmem_ld32(trow + L::O + col, ov);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; i++) ov[i] = (empty || nkb == 0) ? 0.0f : rn_div(ov[i], lsum);
-          if (parts == 2) split_part(ov, part);
-          if (khalf == 0) stage_row32(stage, DH, row, 0, ov, 0, 16);
-          else stage_row32(stage, DH, row, 16, ov, 16, 16);
+            for (int i = 0; i < 32; i++) ov[i] = 0.0f;
+          }
+          stage_row32(stage, DH, row, col, ov, 0, 32);
         }
+      } else {
+        float ov[32];
+        if (nkb > 0) {
+          tmem_ld32(trow + L::O, ov);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i++) ov[i] = 0.0f;
+        }
+        if (khalf == 0) stage_row32(stage, DH, row, 0, ov, 0, 16);
+        else stage_row32(stage, DH, row, 16, ov, 16, 16);
       }
-      named_sync(1, SOFT);
-      if (ok) {
-        float* dst = part == 0 ? o.ptr : o.lo;
-        store_staged_rows(stage, DH, min(QM, p.Tq - q0),
-                          dst + b * o.sb + hq * o.sh + (int64_t)q0 * o.st, o.st, tid, SOFT);
-      }
-      named_sync(1, SOFT);  // the stage is rewritten by the next round
+    }
+    named_sync(1, SOFT);
+    if (ok) {
+      const int64_t oo = b * o.sb + hq * o.sh + (int64_t)q0 * o.st;
+      store_rows_split(stage, DH, min(QM, p.Tq - q0), o.ptr + oo,
+                       o.lo != nullptr ? o.lo + oo : nullptr, o.st, tid, SOFT,
+                       [&](int r, int, float4& v) {
+                         const float l = lrow_s[r];
+                         if (l == 0.0f) {
+                           v = make_float4(0.f, 0.f, 0.f, 0.f);
+                         } else {
+                           v.x = rn_div(v.x, l); v.y = rn_div(v.y, l);
+                           v.z = rn_div(v.z, l); v.w = rn_div(v.w, l);
+                         }
+                       });
     }
   }
   tc_fence_before();

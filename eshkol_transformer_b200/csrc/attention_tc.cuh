@@ -130,6 +130,66 @@ __device__ __forceinline__ void store_staged_rows(uint32_t stage, int cols, int 
   }
 }
 
+// Writes `rows_valid` staged rows ([128][cols + 4] floats at `stage`) with
+// coalesced float4 stores: thread t of `nthreads` takes float4s t, t +
+// nthreads, ... (row r = i / (cols / 4), column 4 (i % (cols / 4))), applies
+// f(r, c4, v) in place, then stores v to hi_base (lo_base null) or its TF32
+// hi part to hi_base and the residual to lo_base.  Row r goes to
+// base + r * row_stride.
+template <typename F>
+__device__ __forceinline__ void store_rows_split(uint32_t stage, int cols, int rows_valid,
+                                                 float* hi_base, float* lo_base,
+                                                 int64_t row_stride, int t, int nthreads, F f) {
+  const int per_row = cols / 4;
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(hi_base) |
+                         reinterpret_cast<uintptr_t>(lo_base) | (uintptr_t)(row_stride * 4);
+  const bool vec = (bits & 15) == 0;
+#pragma unroll 4
+  for (int idx = t; idx < rows_valid * per_row; idx += nthreads) {
+    const int r = idx / per_row, c4 = idx - r * per_row;
+    float4 v = lds128(stage + ((uint32_t)r * (uint32_t)(cols + 4) + 4u * (uint32_t)c4) * 4u);
+    f(r, c4, v);
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lo_base != nullptr) {
+      tf32_split(v.x, v.x, lo.x);
+      tf32_split(v.y, v.y, lo.y);
+      tf32_split(v.z, v.z, lo.z);
+      tf32_split(v.w, v.w, lo.w);
+    }
+    const int64_t off = (int64_t)r * row_stride + 4 * c4;
+    if (vec) {
+      *reinterpret_cast<float4*>(hi_base + off) = v;
+      if (lo_base != nullptr) *reinterpret_cast<float4*>(lo_base + off) = lo;
+    } else {
+      float* h = hi_base + off;
+      h[0] = v.x; h[1] = v.y; h[2] = v.z; h[3] = v.w;
+      if (lo_base != nullptr) {
+        float* l = lo_base + off;
+        l[0] = lo.x; l[1] = lo.y; l[2] = lo.z; l[3] = lo.w;
+      }
+    }
+  }
+}
+
+// Gradient scaling and RoPE backward rotation of columns 4 c4 .. 4 c4 + 3 of
+// a row (pairs 2 c4, 2 c4 + 1 at table entries trow + 2 c4, + 1): x = v
+// scale, then (x0, x1) -> (x0 c + x1 s, -x0 s + x1 c) when ct is set.
+__device__ __forceinline__ void grad_rotate4(float4& v, float scale, const float* ct,
+                                             const float* st, int64_t trow, int c4) {
+  float x[4] = {rn_mul(v.x, scale), rn_mul(v.y, scale), rn_mul(v.z, scale), rn_mul(v.w, scale)};
+  if (ct != nullptr) {
+#pragma unroll
+    for (int pr = 0; pr < 2; pr++) {
+      const int64_t ti = trow + 2 * c4 + pr;
+      const float c = ct[ti], s = st[ti];
+      const float x0 = x[2 * pr], x1 = x[2 * pr + 1];
+      x[2 * pr] = rn_add(rn_mul(x0, c), rn_mul(x1, s));
+      x[2 * pr + 1] = rn_add(-rn_mul(x0, s), rn_mul(x1, c));
+    }
+  }
+  v = make_float4(x[0], x[1], x[2], x[3]);
+}
+
 // Number of entries of the ascending array a[0..n) that are <= x (le) or < x
 // (!le), found by a 32-ary search of the calling warp (every lane gets the
 // result): each round loads 32 entries at once and narrows the bracket 32-fold,
