@@ -190,7 +190,8 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   auto hq_of = [&](int it) { return hkv * G + it / per_head; };
   if (tid == 0 && n_it > 0) {
     // the key tile: K, V lo stay in shared memory as A operands; K, V hi pass
-    // through the (still unused) Q/dO buffers on their way to TMEM
+    // through the MN-major Q/dO buffers (needed last by the first block) on
+    // their way to TMEM
     mbar_expect_tx(B_(LO_FULL), 4 * L::KT);
     const int r = (int)(((int64_t)b * p.Hkv + hkv) * p.Tk + k0);
 #pragma unroll
@@ -198,8 +199,8 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
       const uint32_t o = (uint32_t)c * BK * 128u;
       tma_load_2d(base + L::KL + o, &kl_map, B_(LO_FULL), 32 * c, r);
       tma_load_2d(base + L::VL + o, &vl_map, B_(LO_FULL), 32 * c, r);
-      tma_load_2d(base + L::QK + o, &kh_map, B_(LO_FULL), 32 * c, r);
-      tma_load_2d(base + L::GK + o, &vh_map, B_(LO_FULL), 32 * c, r);
+      tma_load_2d(base + L::GM + o, &kh_map, B_(LO_FULL), 32 * c, r);
+      tma_load_2d(base + L::QM + o, &vh_map, B_(LO_FULL), 32 * c, r);
     }
   }
 
@@ -207,16 +208,32 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  // K hi (warps 0-3) and V hi (warps 4-7) rows -> TMEM
+  auto load_pair = [&](int full, const CUtensorMap* hm, const CUtensorMap* lm, int off, int r) {
+    mbar_expect_tx(B_(full), 2 * L::QT);
+#pragma unroll
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t o = (uint32_t)c * BQ * 128u;
+      tma_load_2d(base + off + o, hm, B_(full), 32 * c, r);
+      tma_load_2d(base + off + L::QT + o, lm, B_(full), 32 * c, r);
+    }
+  };
+  auto pair_row = [&](int j) { return (int)(((int64_t)b * p.Hq + hq_of(j)) * p.Tq + q0_of(j)); };
+  int nqk = 0, ngk = 0, ngm = 0, nqm = 0;  // pairs issued per buffer (loader lane 0)
+  // K hi (warps 0-3) and V hi (warps 4-7) rows -> TMEM, while the loader
+  // issues the first block's K-major Q and dO pairs
   if (warp < 8 && n_it > 0) {
     const bool ok = mbar_wait(B_(LO_FULL), 0u, a.error);
     if (!ok) *abort = 1;
     if (__all_sync(0xffffffffu, ok)) {
       const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-      tile_row_to_tmem<DH>(base + (khalf == 0 ? L::QK : L::GK), row, trow,
+      tile_row_to_tmem<DH>(base + (khalf == 0 ? L::GM : L::QM), row, trow,
                            khalf == 0 ? L::KH : L::VH);
       tmem_wait_st();
     }
+  } else if (warp == LOADER && lane == 0 && n_it > 0) {
+    load_pair(QK_FULL, &qkh_map, &qkl_map, L::QK, pair_row(0));
+    load_pair(GK_FULL, &gkh_map, &gkl_map, L::GK, pair_row(0));
+    nqk = ngk = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -225,24 +242,14 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   if (warp == LOADER) {
     // ---- producer: operand pairs by TMA, per-block statistics by the lanes
     bool ok = true;
-    auto load_pair = [&](int full, const CUtensorMap* hm, const CUtensorMap* lm, int off, int r) {
-      mbar_expect_tx(B_(full), 2 * L::QT);
-#pragma unroll
-      for (int c = 0; c < DH / 32; c++) {
-        const uint32_t o = (uint32_t)c * BQ * 128u;
-        tma_load_2d(base + off + o, hm, B_(full), 32 * c, r);
-        tma_load_2d(base + off + L::QT + o, lm, B_(full), 32 * c, r);
-      }
-    };
-    int nqk = 0, ngk = 0, ngm = 0, nqm = 0;  // pairs issued per buffer (lane 0)
     for (int j = 0; ok && j < n_it; j++) {
       const int q0 = q0_of(j), hq = hq_of(j);
-      const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
+      const int r = pair_row(j);
       const uint32_t prev = (uint32_t)((j - 1) & 1);
-      if (lane == 0) {
-        if (j > 0) ok = role_wait(B_(QK_EMPTY), prev, a.error, abort);
+      if (lane == 0 && j > 0) {  // block 0's pairs went out with the key tile
+        ok = role_wait(B_(QK_EMPTY), prev, a.error, abort);
         if (ok) { load_pair(QK_FULL, &qkh_map, &qkl_map, L::QK, r); nqk++; }
-        if (ok && j > 0) ok = role_wait(B_(GK_EMPTY), prev, a.error, abort);
+        if (ok) ok = role_wait(B_(GK_EMPTY), prev, a.error, abort);
         if (ok) { load_pair(GK_FULL, &gkh_map, &gkl_map, L::GK, r); ngk++; }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -499,6 +506,10 @@ struct QLayout {
   static constexpr int STAGE = 6 * KT;    // K hi/lo, V hi/lo (K-major); K hi/lo (MN-major)
   static constexpr int NS = 2;
   static constexpr int KPOS = NS * STAGE;  // [2][KN] key positions
+  // before the loop: the Q and dO hi/lo row tiles, behind stage 0's K-major tiles
+  static constexpr int RT = QM * DH * 4;
+  static constexpr int ROWS = 4 * KT;
+  static_assert(ROWS + 4 * RT <= NS * STAGE, "row tiles in the stages");
   static constexpr int BARS = KPOS + 2 * KN * 8;
   static constexpr int SMEM = BARS + 256 + 1024;
   // TMEM: Q hi, Q lo, dO hi, dO lo (A operands); S, dP (dS hi over S, dS lo
@@ -553,6 +564,19 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
+    // Q and dO hi/lo rows pass through the K/V stages behind the first
+    // block's K-major tiles (issued meanwhile) on their way to TMEM
+    mbar_expect_tx(B_(ROWS_FULL), 4 * L::RT);
+    const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
+    const uint32_t rs = smem_u32(smem) + L::ROWS;
+#pragma unroll
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t o = (uint32_t)c * QM * 128u;
+      tma_load_2d(rs + o, &qh_map, B_(ROWS_FULL), 32 * c, r);
+      tma_load_2d(rs + L::RT + o, &ql_map, B_(ROWS_FULL), 32 * c, r);
+      tma_load_2d(rs + 2 * L::RT + o, &gh_map, B_(ROWS_FULL), 32 * c, r);
+      tma_load_2d(rs + 3 * L::RT + o, &gl_map, B_(ROWS_FULL), 32 * c, r);
+    }
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), L::COLS);
 
@@ -568,41 +592,45 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
     full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? seen_all / KN : 0;
   }
   const uint32_t base = smem_u32(smem);
-  constexpr uint32_t RT = QM * DH * 4;  // one [128, DH] row tile
-  if (tid == 0) {
-    // Q and dO hi/lo rows pass through the (still unused) K/V stages on their way to TMEM
-    mbar_expect_tx(B_(ROWS_FULL), 4 * RT);
-    const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      const uint32_t o = (uint32_t)c * QM * 128u;
-      tma_load_2d(base + o, &qh_map, B_(ROWS_FULL), 32 * c, r);
-      tma_load_2d(base + RT + o, &ql_map, B_(ROWS_FULL), 32 * c, r);
-      tma_load_2d(base + 2 * RT + o, &gh_map, B_(ROWS_FULL), 32 * c, r);
-      tma_load_2d(base + 3 * RT + o, &gl_map, B_(ROWS_FULL), 32 * c, r);
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  // Q hi/lo and dO hi/lo rows -> TMEM (warps 0-3 hi, 4-7 lo)
+  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
+  // stage tiles: K hi/lo, V hi/lo (K-major), K hi/lo (MN-major)
+  auto load_tiles = [&](int j, int first, int last) {
+    const uint32_t bar = B_(FULL0 + (j & 1)), dst = base + (j & 1) * L::STAGE;
+    const int r = (int)(kv_row0 + (int64_t)j * KN);
+    const CUtensorMap* maps[6] = {&kkh_map, &kkl_map, &vkh_map, &vkl_map, &kmh_map, &kml_map};
+#pragma unroll
+    for (int t = 0; t < 6; t++) {
+      if (t < first || t >= last) continue;
+#pragma unroll
+      for (int c = 0; c < DH / 32; c++)
+        tma_load_2d(dst + t * L::KT + (uint32_t)c * KN * 128u, maps[t], bar, 32 * c, r);
+    }
+  };
+  // Q hi/lo and dO hi/lo rows -> TMEM (warps 0-3 hi, 4-7 lo), while the
+  // loader issues the first block's K-major tiles
   if (warp < 8) {
     const bool ok = mbar_wait(B_(ROWS_FULL), 0u, a.error);
     if (!ok) *abort = 1;
     if (__all_sync(0xffffffffu, ok)) {
       const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-      tile_row_to_tmem<DH>(base + (uint32_t)khalf * RT, row, trow, khalf == 0 ? L::QH : L::QL);
-      tile_row_to_tmem<DH>(base + (uint32_t)(2 + khalf) * RT, row, trow,
+      const uint32_t rs = base + L::ROWS;
+      tile_row_to_tmem<DH>(rs + (uint32_t)khalf * L::RT, row, trow, khalf == 0 ? L::QH : L::QL);
+      tile_row_to_tmem<DH>(rs + (uint32_t)(2 + khalf) * L::RT, row, trow,
                            khalf == 0 ? L::GH : L::GL);
       tmem_wait_st();
     }
+  } else if (warp == LOADER && lane == 0 && nkb > 0) {
+    mbar_expect_tx(B_(FULL0), L::STAGE);
+    load_tiles(0, 0, 4);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
-  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
   if (warp == LOADER) {
     // ---- producer: K/V stages by TMA, key positions by the lanes
     int loads = 0;
@@ -616,18 +644,11 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
           if (ok) ok = role_wait(B_(EMPTYB0 + s), par, a.error, abort);
         }
         if (ok) {
-          const uint32_t bar = B_(FULL0 + s), dst = base + s * L::STAGE;
-          const int r = (int)(kv_row0 + (int64_t)j * KN);
-          mbar_expect_tx(bar, L::STAGE);
-#pragma unroll
-          for (int c = 0; c < DH / 32; c++) {
-            const uint32_t o = (uint32_t)c * KN * 128u;
-            tma_load_2d(dst + o, &kkh_map, bar, 32 * c, r);
-            tma_load_2d(dst + L::KT + o, &kkl_map, bar, 32 * c, r);
-            tma_load_2d(dst + 2 * L::KT + o, &vkh_map, bar, 32 * c, r);
-            tma_load_2d(dst + 3 * L::KT + o, &vkl_map, bar, 32 * c, r);
-            tma_load_2d(dst + 4 * L::KT + o, &kmh_map, bar, 32 * c, r);
-            tma_load_2d(dst + 5 * L::KT + o, &kml_map, bar, 32 * c, r);
+          if (j == 0) {  // the K-major tiles went out with the rows
+            load_tiles(0, 4, 6);
+          } else {
+            mbar_expect_tx(B_(FULL0 + s), L::STAGE);
+            load_tiles(j, 0, 6);
           }
           loads++;
         }

@@ -48,9 +48,13 @@ struct FwdLayout {
   static constexpr int KT = KN * DH * 4;           // one [KN, DH] tile
   static constexpr int STAGE = 4 * KT;             // K hi, K lo (K-major), V hi, V lo (MN-major)
   static constexpr int RT = QM * DH * 4;           // one [128, DH] row tile
-  // the stages also carry the Q row tiles (before the loop) and the staged
-  // output rows (after it)
-  static constexpr int SMEM_BUF = NSTAGE * STAGE >= 2 * RT ? NSTAGE * STAGE : 2 * RT;
+  // the last stage also carries the Q row tiles (before the loop; with one
+  // stage nothing is loaded meanwhile) and stage 0 the output rows (after it)
+  static constexpr int QROWS = NSTAGE >= 2 ? (NSTAGE - 1) * STAGE : 0;
+  static constexpr int PRELOAD = NSTAGE >= 2 ? NSTAGE - 1 : 0;  // blocks loaded meanwhile
+  static_assert(NSTAGE < 2 || 2 * RT <= STAGE, "Q rows in one stage");
+  static constexpr int SMEM_BUF =
+      NSTAGE * STAGE >= QROWS + 2 * RT ? NSTAGE * STAGE : QROWS + 2 * RT;
   static_assert(QM * (DH + 4) * 4 <= SMEM_BUF, "output stage");
   static constexpr int BARS = SMEM_BUF;
   static constexpr int SMEM = BARS + 256 + 1024;
@@ -155,6 +159,17 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
+    // Q hi/lo rows pass through the last K/V stage (the first ones receive
+    // key blocks meanwhile) on their way to TMEM
+    mbar_expect_tx(ROWS, 2 * L::RT);
+    const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
+    const uint32_t qs = smem_u32(smem) + L::QROWS;
+#pragma unroll
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t off = (uint32_t)c * QM * 128u;
+      tma_load_2d(qs + off, &qh_map, ROWS, 32 * c, r);
+      tma_load_2d(qs + L::RT + off, &ql_map, ROWS, 32 * c, r);
+    }
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), L::COLS);
 
@@ -172,27 +187,59 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
     full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? seen_all / KN : 0;
   }
   const uint32_t base = smem_u32(smem);
-  if (tid == 0) {
-    // Q hi/lo rows pass through the (still unused) K/V stages on their way to TMEM
-    mbar_expect_tx(ROWS, 2 * L::RT);
-    const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
-#pragma unroll
-    for (int c = 0; c < DH / 32; c++) {
-      const uint32_t off = (uint32_t)c * QM * 128u;
-      tma_load_2d(base + off, &qh_map, ROWS, 32 * c, r);
-      tma_load_2d(base + L::RT + off, &ql_map, ROWS, 32 * c, r);
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
   const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-  if (warp < 8) {
+  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
+  // ---- loader (warp LOADER): K/V stages by TMA, key positions by the lanes;
+  // the blocks whose stages the Q rows leave free are issued while the
+  // softmax warps move Q into TMEM
+  int loads = 0;
+  bool lok = true;
+  auto load_block = [&](int j) {
+    const int st = j % NST;
+    bool ok = true;
+    if (lane == 0) {
+      if (j >= NST) ok = role_wait(EMPTY + 8 * st, (uint32_t)((j / NST - 1) & 1), a.error, abort);
+      if (ok) {
+        const uint32_t bar = FULL + 8 * st, dst = base + st * L::STAGE;
+        const int r = (int)(kv_row0 + (int64_t)j * KN);
+        mbar_expect_tx(bar, L::STAGE);
+#pragma unroll
+        for (int c = 0; c < DH / 32; c++) {
+          const uint32_t off = (uint32_t)c * KN * 128u;
+          tma_load_2d(dst + off, &kh_map, bar, 32 * c, r);
+          tma_load_2d(dst + L::KT + off, &kl_map, bar, 32 * c, r);
+          tma_load_2d(dst + 2 * L::KT + off, &vh_map, bar, 32 * c, r);
+          tma_load_2d(dst + 3 * L::KT + off, &vl_map, bar, 32 * c, r);
+        }
+        loads++;
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok && j >= 2) ok = role_wait(PREADY + 8 * (j & 1), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+#pragma unroll
+      for (int h = 0; h < KN / 32; h++) {
+        const int t = j * KN + 32 * h + lane;
+        kpos_s[(j & 1) * KN + 32 * h + lane] = t < p.Tk ? p.kpos[(int64_t)b * p.Tk + t] : INT64_MAX;
+      }
+      mbar_arrive(KPFULL + 8 * (j & 1));
+    }
+    lok = ok;
+  };
+  const int pre = min(L::PRELOAD, nkb);
+  if (warp == LOADER) {
+    for (int j = 0; lok && j < pre; j++) load_block(j);
+  } else if (warp < 8) {
     const bool ok = mbar_wait(ROWS, 0u, a.error);
     if (!ok) *abort = 1;
     if (__all_sync(0xffffffffu, ok)) {
-      tile_row_to_tmem<DH>(base + (uint32_t)khalf * L::RT, row, trow, khalf == 0 ? L::QH : L::QL);
+      tile_row_to_tmem<DH>(base + L::QROWS + (uint32_t)khalf * L::RT, row, trow,
+                           khalf == 0 ? L::QH : L::QL);
       tmem_wait_st();
     }
   }
@@ -200,42 +247,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
   __syncthreads();
   tc_fence_after();
 
-  const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
   if (warp == LOADER) {
-    // ---- K/V stages by TMA, key positions by the lanes
-    int loads = 0;
-    bool ok = true;
-    for (int j = 0; ok && j < nkb; j++) {
-      const int st = j % NST;
-      if (lane == 0) {
-        if (j >= NST) ok = role_wait(EMPTY + 8 * st, (uint32_t)((j / NST - 1) & 1), a.error, abort);
-        if (ok) {
-          const uint32_t bar = FULL + 8 * st, dst = base + st * L::STAGE;
-          const int r = (int)(kv_row0 + (int64_t)j * KN);
-          mbar_expect_tx(bar, L::STAGE);
-#pragma unroll
-          for (int c = 0; c < DH / 32; c++) {
-            const uint32_t off = (uint32_t)c * KN * 128u;
-            tma_load_2d(dst + off, &kh_map, bar, 32 * c, r);
-            tma_load_2d(dst + L::KT + off, &kl_map, bar, 32 * c, r);
-            tma_load_2d(dst + 2 * L::KT + off, &vh_map, bar, 32 * c, r);
-            tma_load_2d(dst + 3 * L::KT + off, &vl_map, bar, 32 * c, r);
-          }
-          loads++;
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok && j >= 2) ok = role_wait(PREADY + 8 * (j & 1), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-#pragma unroll
-        for (int h = 0; h < KN / 32; h++) {
-          const int t = j * KN + 32 * h + lane;
-          kpos_s[(j & 1) * KN + 32 * h + lane] = t < p.Tk ? p.kpos[(int64_t)b * p.Tk + t] : INT64_MAX;
-        }
-        mbar_arrive(KPFULL + 8 * (j & 1));
-      }
-    }
+    for (int j = pre; lok && j < nkb; j++) load_block(j);
     if (lane == 0) {  // every copy has landed before the CTA releases its memory
       for (int j = loads - NST < 0 ? 0 : loads - NST; j < loads; j++)
         mbar_wait(FULL + 8 * (j % NST), (uint32_t)((j / NST) & 1), a.error);
