@@ -503,21 +503,24 @@ constexpr int KN = 64;   // keys per block
 template <int DH>
 struct QLayout {
   static constexpr int KT = KN * DH * 4;  // [KN, DH] tile: DH/32 chunks of KN rows x 128 B
-  static constexpr int STAGE = 6 * KT;    // K hi/lo, V hi/lo (K-major); K hi/lo (MN-major)
-  static constexpr int NS = 2;
-  static constexpr int KPOS = NS * STAGE;  // [2][KN] key positions
-  // before the loop: the Q and dO hi/lo row tiles, behind stage 0's K-major tiles
-  static constexpr int RT = QM * DH * 4;
-  static constexpr int ROWS = 4 * KT;
-  static_assert(ROWS + 4 * RT <= NS * STAGE, "row tiles in the stages");
+  static constexpr int RT = QM * DH * 4;  // [QM, DH] row tile
+  // Q lo and dO lo rows stay in shared memory (A operands of the lo passes);
+  // two stages of K-major K hi/lo, V hi/lo; one buffer of MN-major K hi/lo
+  // (B of dQ, refilled once both dQ chains of the previous block are done)
+  static constexpr int QL = 0, GL = RT, STAGE0 = 2 * RT;
+  static constexpr int STAGE = 4 * KT;
+  static constexpr int MN = STAGE0 + 2 * STAGE;
+  static constexpr int KPOS = MN + 2 * KT;  // [2][KN] key positions
   static constexpr int BARS = KPOS + 2 * KN * 8;
   static constexpr int SMEM = BARS + 256 + 1024;
-  // TMEM: Q hi, Q lo, dO hi, dO lo (A operands); S, dP (dS hi over S, dS lo
-  // over dP); dQ in two accumulators (hi and lo chains), summed at the end
-  static constexpr uint32_t QH = 0, QL = DH, GH = 2 * DH, GL = 3 * DH, S = 4 * DH, DP = S + KN,
-                            DQA = DP + KN, DQB = DQA + DH;
-  static constexpr uint32_t COLS = DQB + DH <= 256 ? 256 : 512;
-  static_assert(DQB + DH <= 512, "TMEM columns");
+  // before the loop the Q hi and dO hi row tiles pass through stage 1
+  static_assert(2 * RT <= STAGE, "row tiles in one stage");
+  // TMEM: Q hi, dO hi (A operands); two slots of S, dP (dS hi over S, dS lo
+  // over dP); dQ in two accumulators (one per chain), summed at the end
+  static constexpr uint32_t QH = 0, GH = DH, SL0 = 2 * DH, SLOT = 2 * KN, DQA = SL0 + 2 * SLOT,
+                            DQB = DQA + DH;
+  static constexpr uint32_t COLS = 512;
+  static_assert(DQB + DH <= COLS, "TMEM columns");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -539,9 +542,11 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
   uint8_t* smem = align1024(smem_raw);
   int64_t* kpos_s = reinterpret_cast<int64_t*>(smem + L::KPOS);  // [2][KN]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
+  // per-slot barriers come in pairs (slot 0, slot 1); a slot serves every
+  // other block, so block j waits phase (j >> 1) & 1 of slot j & 1
   enum {
-    FULL0, FULL1, EMPTYA0, EMPTYA1, EMPTYB0, EMPTYB1, SA_DONE, SB_DONE, DS_READY0, DS_READY1,
-    QA_DONE, QB_DONE, KP_FULL0, KP_FULL1, ROWS_FULL, NBARS
+    FULL0, FULL1, EMPTY0, EMPTY1, SA0, SA1, SB0, SB1, DS0, DS1, QA0, QA1, QB0, QB1, KP0, KP1,
+    MN_FULL, MN_EMPTY, ROWS_HI, ROWS_LO, NBARS
   };
   const uint32_t bar0 = smem_u32(bars);
   auto B_ = [&](int i) { return bar0 + 8u * (uint32_t)i; };
@@ -554,28 +559,31 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
   const int hkv = hq / (p.Hq / p.Hkv);
   const int tq = q0 + row;
   const bool valid_q = tq < p.Tq;
+  const uint32_t base = smem_u32(smem);
   if (tid == 0) {
     for (int i = 0; i < NBARS; i++) {
-      const uint32_t n = (i == DS_READY0 || i == DS_READY1) ? SOFT
-                         : (i == KP_FULL0 || i == KP_FULL1) ? 32
-                                                            : 1;
+      const uint32_t n = (i == DS0 || i == DS1)                      ? SOFT
+                         : (i == KP0 || i == KP1)                    ? 32
+                         : (i == EMPTY0 || i == EMPTY1 || i == MN_EMPTY) ? 2
+                                                                     : 1;
       mbar_init(B_(i), n);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
-    // Q and dO hi/lo rows pass through the K/V stages behind the first
-    // block's K-major tiles (issued meanwhile) on their way to TMEM
-    mbar_expect_tx(B_(ROWS_FULL), 4 * L::RT);
+    // Q lo / dO lo rows to their resident buffers; Q hi / dO hi rows through
+    // stage 1 on their way to TMEM (stage 0 receives the first block meanwhile)
     const int r = (int)(((int64_t)b * p.Hq + hq) * p.Tq + q0);
-    const uint32_t rs = smem_u32(smem) + L::ROWS;
+    mbar_expect_tx(B_(ROWS_LO), 2 * L::RT);
+    mbar_expect_tx(B_(ROWS_HI), 2 * L::RT);
+    const uint32_t hs = base + L::STAGE0 + L::STAGE;
 #pragma unroll
     for (int c = 0; c < DH / 32; c++) {
       const uint32_t o = (uint32_t)c * QM * 128u;
-      tma_load_2d(rs + o, &qh_map, B_(ROWS_FULL), 32 * c, r);
-      tma_load_2d(rs + L::RT + o, &ql_map, B_(ROWS_FULL), 32 * c, r);
-      tma_load_2d(rs + 2 * L::RT + o, &gh_map, B_(ROWS_FULL), 32 * c, r);
-      tma_load_2d(rs + 3 * L::RT + o, &gl_map, B_(ROWS_FULL), 32 * c, r);
+      tma_load_2d(base + L::QL + o, &ql_map, B_(ROWS_LO), 32 * c, r);
+      tma_load_2d(base + L::GL + o, &gl_map, B_(ROWS_LO), 32 * c, r);
+      tma_load_2d(hs + o, &qh_map, B_(ROWS_HI), 32 * c, r);
+      tma_load_2d(hs + L::RT + o, &gh_map, B_(ROWS_HI), 32 * c, r);
     }
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), L::COLS);
@@ -591,135 +599,162 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
     nkb = (seen + KN - 1) / KN;
     full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? seen_all / KN : 0;
   }
-  const uint32_t base = smem_u32(smem);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
   const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
-  // stage tiles: K hi/lo, V hi/lo (K-major), K hi/lo (MN-major)
-  auto load_tiles = [&](int j, int first, int last) {
-    const uint32_t bar = B_(FULL0 + (j & 1)), dst = base + (j & 1) * L::STAGE;
+  auto load_kmajor = [&](int j) {  // K hi/lo, V hi/lo of block j into stage j & 1
+    const uint32_t bar = B_(FULL0 + (j & 1)), dst = base + L::STAGE0 + (j & 1) * L::STAGE;
     const int r = (int)(kv_row0 + (int64_t)j * KN);
-    const CUtensorMap* maps[6] = {&kkh_map, &kkl_map, &vkh_map, &vkl_map, &kmh_map, &kml_map};
+    mbar_expect_tx(bar, L::STAGE);
 #pragma unroll
-    for (int t = 0; t < 6; t++) {
-      if (t < first || t >= last) continue;
-#pragma unroll
-      for (int c = 0; c < DH / 32; c++)
-        tma_load_2d(dst + t * L::KT + (uint32_t)c * KN * 128u, maps[t], bar, 32 * c, r);
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t o = (uint32_t)c * KN * 128u;
+      tma_load_2d(dst + o, &kkh_map, bar, 32 * c, r);
+      tma_load_2d(dst + L::KT + o, &kkl_map, bar, 32 * c, r);
+      tma_load_2d(dst + 2 * L::KT + o, &vkh_map, bar, 32 * c, r);
+      tma_load_2d(dst + 3 * L::KT + o, &vkl_map, bar, 32 * c, r);
     }
   };
-  // Q hi/lo and dO hi/lo rows -> TMEM (warps 0-3 hi, 4-7 lo), while the
-  // loader issues the first block's K-major tiles
+  auto load_mn = [&](int j) {  // MN-major K hi/lo of block j
+    const uint32_t bar = B_(MN_FULL), dst = base + L::MN;
+    const int r = (int)(kv_row0 + (int64_t)j * KN);
+    mbar_expect_tx(bar, 2 * L::KT);
+#pragma unroll
+    for (int c = 0; c < DH / 32; c++) {
+      const uint32_t o = (uint32_t)c * KN * 128u;
+      tma_load_2d(dst + o, &kmh_map, bar, 32 * c, r);
+      tma_load_2d(dst + L::KT + o, &kml_map, bar, 32 * c, r);
+    }
+  };
+  // Q hi and dO hi rows -> TMEM (warps 0-3 Q, 4-7 dO), while the loader
+  // issues block 0
   if (warp < 8) {
-    const bool ok = mbar_wait(B_(ROWS_FULL), 0u, a.error);
+    const bool ok = mbar_wait(B_(ROWS_HI), 0u, a.error);
     if (!ok) *abort = 1;
     if (__all_sync(0xffffffffu, ok)) {
       const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-      const uint32_t rs = base + L::ROWS;
-      tile_row_to_tmem<DH>(rs + (uint32_t)khalf * L::RT, row, trow, khalf == 0 ? L::QH : L::QL);
-      tile_row_to_tmem<DH>(rs + (uint32_t)(2 + khalf) * L::RT, row, trow,
-                           khalf == 0 ? L::GH : L::GL);
+      tile_row_to_tmem<DH>(base + L::STAGE0 + L::STAGE + (uint32_t)khalf * L::RT, row, trow,
+                           khalf == 0 ? L::QH : L::GH);
       tmem_wait_st();
     }
   } else if (warp == LOADER && lane == 0 && nkb > 0) {
-    mbar_expect_tx(B_(FULL0), L::STAGE);
-    load_tiles(0, 0, 4);
+    load_kmajor(0);
+    load_mn(0);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
   if (warp == LOADER) {
-    // ---- producer: K/V stages by TMA, key positions by the lanes
-    int loads = 0;
+    // ---- producer: K-major stages one block ahead of the MN-major buffer,
+    // key positions by the lanes
+    int nk = nkb > 0 ? 1 : 0, nm = nkb > 0 ? 1 : 0;  // blocks issued (lane 0)
     bool ok = true;
+    auto fill_kpos = [&](int j) {
+#pragma unroll
+      for (int h = 0; h < KN / 32; h++) {
+        const int t = j * KN + 32 * h + lane;
+        kpos_s[(j & 1) * KN + 32 * h + lane] = t < p.Tk ? p.kpos[(int64_t)b * p.Tk + t] : INT64_MAX;
+      }
+      mbar_arrive(B_(KP0 + (j & 1)));
+    };
+    if (nkb > 0) fill_kpos(0);
     for (int j = 0; ok && j < nkb; j++) {
-      const int s = j & 1;
-      if (lane == 0) {
-        if (j >= 2) {
-          const uint32_t par = (uint32_t)(((j >> 1) - 1) & 1);
-          ok = role_wait(B_(EMPTYA0 + s), par, a.error, abort);
-          if (ok) ok = role_wait(B_(EMPTYB0 + s), par, a.error, abort);
+      const int jn = j + 1;
+      if (jn < nkb) {
+        // stage jn & 1 is free once S and dP of block jn - 2 completed
+        if (lane == 0) {
+          if (jn >= 2) ok = role_wait(B_(EMPTY0 + (jn & 1)), (uint32_t)(((jn >> 1) - 1) & 1), a.error, abort);
+          if (ok) { load_kmajor(jn); nk++; }
         }
-        if (ok) {
-          if (j == 0) {  // the K-major tiles went out with the rows
-            load_tiles(0, 4, 6);
-          } else {
-            mbar_expect_tx(B_(FULL0 + s), L::STAGE);
-            load_tiles(j, 0, 6);
-          }
-          loads++;
-        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        // position slot jn & 1 is free once block jn - 2's gradients are done
+        if (ok && jn >= 2) ok = role_wait(B_(DS0 + (jn & 1)), (uint32_t)(((jn >> 1) - 1) & 1), a.error, abort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) fill_kpos(jn);
+      }
+      // the MN-major buffer takes block j once both dQ chains of j - 1 are done
+      if (ok && j >= 1 && lane == 0) {
+        ok = role_wait(B_(MN_EMPTY), (uint32_t)((j - 1) & 1), a.error, abort);
+        if (ok) { load_mn(j); nm++; }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok && j >= 2) ok = role_wait(B_(DS_READY0 + s), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-#pragma unroll
-        for (int h = 0; h < KN / 32; h++) {
-          const int t = j * KN + 32 * h + lane;
-          kpos_s[s * KN + 32 * h + lane] = t < p.Tk ? p.kpos[(int64_t)b * p.Tk + t] : INT64_MAX;
-        }
-        mbar_arrive(B_(KP_FULL0 + s));
-      }
     }
     if (lane == 0) {  // every copy has landed before the CTA releases its memory
-      for (int j = loads - 2 < 0 ? 0 : loads - 2; j < loads; j++)
+      mbar_wait(B_(ROWS_LO), 0u, a.error);
+      for (int j = nk - 2 < 0 ? 0 : nk - 2; j < nk; j++)
         mbar_wait(B_(FULL0 + (j & 1)), (uint32_t)((j >> 1) & 1), a.error);
+      if (nm > 0) mbar_wait(B_(MN_FULL), (uint32_t)((nm - 1) & 1), a.error);
     }
   } else if (warp == MMA_A || warp == MMA_B) {
     // ---- MMA chains.  A: S = Q K^T, dQa += dS_hi K.  B: dP = dO V^T, dQb += dS_lo K_hi.
+    // Issue order S(0), S(1), dQ(0), S(2), dQ(1), ...: the score MMAs of a
+    // block run while the SM turns the previous block's scores into dS.
     const bool is_a = warp == MMA_A;
     if (lane == 0 && nkb > 0) {
       constexpr uint32_t idesc_s = idesc_tf32_m128(KN, 0);
       constexpr uint32_t idesc_q = idesc_tf32_m128(DH, 1);
-      const uint32_t xh = tmem + (is_a ? L::QH : L::GH), xl = tmem + (is_a ? L::QL : L::GL);
-      const uint32_t sd = tmem + (is_a ? L::S : L::DP);
+      const uint32_t xh = tmem + (is_a ? L::QH : L::GH);
+      const uint64_t xlo = kmajor_desc(base + (is_a ? L::QL : L::GL), QM, 0);
+      const uint32_t col = is_a ? 0u : (uint32_t)KN;  // S or dP columns of a slot
       const uint32_t dqd = tmem + (is_a ? L::DQA : L::DQB);
-      const int sdone = is_a ? SA_DONE : SB_DONE, qdone = is_a ? QA_DONE : QB_DONE;
-      const int empty0 = is_a ? EMPTYA0 : EMPTYB0;
+      const int sdone = is_a ? SA0 : SB0, qdone = is_a ? QA0 : QB0;
       int s_issued = 0, q_issued = 0;
-      bool ok = true;
+      bool ok = role_wait(B_(ROWS_LO), 0u, a.error, abort);
+      auto issue_dq = [&](int i) {
+        const int s = i & 1;
+        const uint32_t par = (uint32_t)((i >> 1) & 1);
+        ok = role_wait(B_(DS0 + s), par, a.error, abort);
+        if (ok) ok = role_wait(B_(MN_FULL), (uint32_t)(i & 1), a.error, abort);
+        if (!ok) return;
+        tc_fence_after();
+        const uint32_t sd = tmem + L::SL0 + (uint32_t)s * L::SLOT + col;
+        const uint64_t kmh = mnmajor_desc(base + L::MN, KN, 0);
+        const uint64_t kml = mnmajor_desc(base + L::MN + L::KT, KN, 0);
+#pragma unroll
+        for (int k = 0; k < KN / 8; k++) {
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          umma_tf32_ts(dqd, sd + 8 * k, mslice(kmh, k), idesc_q, acc);
+          if (is_a) umma_tf32_ts(dqd, sd + 8 * k, mslice(kml, k), idesc_q, 1u);
+        }
+        umma_commit(B_(qdone + s));
+        umma_commit(B_(MN_EMPTY));
+        q_issued++;
+      };
       for (int j = 0; ok && j < nkb; j++) {
         const int s = j & 1;
         ok = role_wait(B_(FULL0 + s), (uint32_t)((j >> 1) & 1), a.error, abort);
-        if (ok && j > 0) ok = role_wait(B_(qdone), (uint32_t)((j - 1) & 1), a.error, abort);
+        // the slot's columns are free once the dQ MMAs of block j - 2 read them
+        if (ok && j >= 2) ok = role_wait(B_(qdone + s), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t stg = base + s * L::STAGE;
+        const uint32_t stg = base + L::STAGE0 + (uint32_t)s * L::STAGE;
         const uint64_t bh = kmajor_desc(stg + (is_a ? 0 : 2 * L::KT), KN, 0);
         const uint64_t bl = kmajor_desc(stg + (is_a ? L::KT : 3 * L::KT), KN, 0);
+        const uint32_t sd = tmem + L::SL0 + (uint32_t)s * L::SLOT + col;
 #pragma unroll
         for (int k = 0; k < DH / 8; k++) {
           const uint32_t acc = k > 0 ? 1u : 0u;
           umma_tf32_ts(sd, xh + 8 * k, kslice<KN>(bh, k), idesc_s, acc);
           umma_tf32_ts(sd, xh + 8 * k, kslice<KN>(bl, k), idesc_s, 1u);
-          umma_tf32_ts(sd, xl + 8 * k, kslice<KN>(bh, k), idesc_s, 1u);
+          umma_tf32(sd, kslice<QM>(xlo, k), kslice<KN>(bh, k), idesc_s, 1u);
         }
-        umma_commit(B_(sdone));
+        umma_commit(B_(sdone + s));
+        umma_commit(B_(EMPTY0 + s));
         s_issued++;
-        ok = role_wait(B_(DS_READY0 + s), (uint32_t)((j >> 1) & 1), a.error, abort);
-        if (!ok) break;
-        tc_fence_after();
-        const uint64_t kmh = mnmajor_desc(stg + 4 * L::KT, KN, 0);
-        const uint64_t kml = mnmajor_desc(stg + 5 * L::KT, KN, 0);
-#pragma unroll
-        for (int k = 0; k < KN / 8; k++) {
-          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
-          umma_tf32_ts(dqd, sd + 8 * k, mslice(kmh, k), idesc_q, acc);
-          if (is_a) umma_tf32_ts(dqd, sd + 8 * k, mslice(kml, k), idesc_q, 1u);
-        }
-        umma_commit(B_(qdone));
-        umma_commit(B_(empty0 + s));
-        q_issued++;
+        if (j >= 1) issue_dq(j - 1);
       }
+      if (ok) issue_dq(nkb - 1);
       // committed MMAs finish before TMEM and shared memory are released
-      if (s_issued > 0) mbar_wait(B_(sdone), (uint32_t)((s_issued - 1) & 1), a.error);
+      if (s_issued > 0) {
+        const int i = s_issued - 1;
+        mbar_wait(B_(sdone + (i & 1)), (uint32_t)((i >> 1) & 1), a.error);
+      }
       if (q_issued > 0) {
-        mbar_wait(B_(qdone), (uint32_t)((q_issued - 1) & 1), a.error);
-        mbar_wait(B_(empty0 + ((q_issued - 1) & 1)), (uint32_t)(((q_issued - 1) >> 1) & 1), a.error);
+        const int i = q_issued - 1;
+        mbar_wait(B_(qdone + (i & 1)), (uint32_t)((i >> 1) & 1), a.error);
       }
     }
   } else {
@@ -734,7 +769,7 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
     bool ok = true;
     for (int j = 0; ok && j < nkb; j++) {
       const int s = j & 1;
-      const uint32_t par = (uint32_t)(j & 1), spar = (uint32_t)((j >> 1) & 1);
+      const uint32_t spar = (uint32_t)((j >> 1) & 1);
       const bool full_block = j < full_kb;
       uint8_t keep[32];
       if (!full_block && p.mask != nullptr) {  // clamped indices stay in bounds
@@ -742,17 +777,18 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
 #pragma unroll
         for (int i = 0; i < 32; i++) keep[i] = p.mask[mrow + min(j * KN + cb + i, p.Tk - 1)];
       }
-      ok = role_wait(B_(KP_FULL0 + s), spar, a.error, abort);
-      if (ok) ok = role_wait(B_(SA_DONE), par, a.error, abort);
-      if (ok) ok = role_wait(B_(SB_DONE), par, a.error, abort);
+      ok = role_wait(B_(KP0 + s), spar, a.error, abort);
+      if (ok) ok = role_wait(B_(SA0 + s), spar, a.error, abort);
+      if (ok) ok = role_wait(B_(SB0 + s), spar, a.error, abort);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       // keys of the block this query sees: those whose position does not exceed its own
       const int seen = full_block ? KN : count_below(kpos_s + s * KN, KN, qpos_row + 1) - cb;
+      const uint32_t slot = trow + L::SL0 + (uint32_t)s * L::SLOT;
       float sv[32], dp[32];
-      tmem_ld32(trow + L::S + cb, sv);
-      tmem_ld32(trow + L::DP + cb, dp);
+      tmem_ld32(slot + cb, sv);
+      tmem_ld32(slot + KN + cb, dp);
 #pragma unroll
       for (int i = 0; i < 32; i++) {
         bool adm = full_block;
@@ -765,16 +801,17 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
         sv[i] = tf32_hi(ds);
         dp[i] = ds - sv[i];
       }
-      tmem_st32(trow + L::S + cb, sv);
-      tmem_st32(trow + L::DP + cb, dp);
+      tmem_st32(slot + cb, sv);
+      tmem_st32(slot + KN + cb, dp);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(B_(DS_READY0 + s));
+      mbar_arrive(B_(DS0 + s));
     }
     if (ok && nkb > 0) {
-      const uint32_t last = (uint32_t)((nkb - 1) & 1);
-      ok = role_wait(B_(QA_DONE), last, a.error, abort);
-      if (ok) ok = role_wait(B_(QB_DONE), last, a.error, abort);
+      const int i = nkb - 1;
+      const uint32_t last = (uint32_t)((i >> 1) & 1);
+      ok = role_wait(B_(QA0 + (i & 1)), last, a.error, abort);
+      if (ok) ok = role_wait(B_(QB0 + (i & 1)), last, a.error, abort);
     }
     ok = __all_sync(0xffffffffu, ok);
     auto load_dq = [&](int col, float (&v)[32]) {
