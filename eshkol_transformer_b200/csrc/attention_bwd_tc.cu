@@ -35,6 +35,12 @@ namespace {
 
 // ---- prepass -----------------------------------------------------------------------
 
+// Base-2 log-sum-exp of a query row from the forward's statistics (+inf for
+// a row with no admitted key, so every P of it is 0).
+__device__ __forceinline__ float lse2_of(float m, float l) {
+  return l > 0.0f ? (m + logf(l)) * kLog2e : INFINITY;
+}
+
 // One warp per query row (b, hq, tq), row = (b*Hq + hq)*Tq + tq: delta in the
 // SIMT kernel's order (lane-strided fma, warp tree), lse2, dO hi/lo.
 __global__ void attn_bwd_prepare_kernel(AttnParams p, AttnTensor o, const float* __restrict__ o_lo,
@@ -64,8 +70,7 @@ __global__ void attn_bwd_prepare_kernel(AttnParams p, AttnTensor o, const float*
   s = warp_sum(s);
   if (lane == 0) {
     delta[row] = s;
-    const float l = row_sum[row];
-    lse2[row] = l > 0.0f ? (row_max[row] + logf(l)) * kLog2e : INFINITY;
+    lse2[row] = lse2_of(row_max[row], row_sum[row]);
   }
 }
 
@@ -891,9 +896,11 @@ bool launch_bwd_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTen
                make_map(&kmh, w.kh, DH, krows, DH, KN, SW32) && make_map(&kml, w.kl, DH, krows, DH, KN, SW32);
   if (!built) return false;
   if (!p.ws_ready) attention_prepare_qkv(p, w, stream);
-  attn_bwd_prepare_kernel<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(
-      p, o, o_lo, dout, row_max, row_sum, delta, w.lse2, w.doh, w.dol);
-  count_launch();
+  if (!p.grad_ready) {
+    attn_bwd_prepare_kernel<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(
+        p, o, o_lo, dout, row_max, row_sum, delta, w.lse2, w.doh, w.dol);
+    count_launch();
+  }
   TcBwdArgs a{w.kh, w.vh, w.qh, w.ql, w.doh, w.dol, w.lse2, delta, device_error_word()};
   cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        KvLayout<DH>::SMEM);
@@ -924,6 +931,38 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
     default:
       return false;
   }
+}
+
+bool attention_grad_prep(const AttnParams& p, AttnTensor o, const float* o_lo,
+                         const float* row_max, const float* row_sum, float* delta,
+                         AttnGradPrep* out) {
+  if (p.ws == nullptr || p.Dh != 32 && p.Dh != 64) return false;
+  if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
+  // o as merged token-major rows [B*Tq, Hq*Dh]
+  const int64_t ld = (int64_t)p.Hq * p.Dh;
+  if (o.st != ld || o.sh != p.Dh || o.sb != (int64_t)p.Tq * ld) return false;
+  const AttnWs w = attn_ws(p);
+  AttnGradPrep g{};
+  g.T = p.Tq; g.H = p.Hq; g.Dh = p.Dh;
+  g.o = o.ptr; g.o_lo = o_lo;
+  g.row_max = row_max; g.row_sum = row_sum;
+  g.doh = w.doh; g.dol = w.dol; g.delta = delta; g.lse2 = w.lse2;
+  *out = g;
+  return true;
+}
+
+void attention_prepare_grad_from(const float* dout, int64_t ld, int rows, const AttnGradPrep& g,
+                                 cudaStream_t stream) {
+  AttnParams p{};
+  p.B = rows / g.T; p.Hq = g.H; p.Hkv = g.H; p.Tq = g.T; p.Tk = g.T; p.Dh = g.Dh;
+  const int64_t ldo = (int64_t)g.H * g.Dh;
+  const int64_t qrows = (int64_t)p.B * p.Hq * p.Tq;
+  if (qrows == 0) return;
+  attn_bwd_prepare_kernel<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(
+      p, AttnTensor{g.o, (int64_t)g.T * ldo, g.Dh, ldo}, g.o_lo,
+      AttnTensor{dout, (int64_t)g.T * ld, g.Dh, ld}, g.row_max, g.row_sum, g.delta, g.lse2, g.doh,
+      g.dol);
+  count_launch();
 }
 
 }  // namespace etb

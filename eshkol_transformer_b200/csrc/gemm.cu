@@ -161,7 +161,8 @@ struct TcArgs {
   // pair kernel: every row pointer and ldc allow float4 access and N % 4 == 0,
   // so the epilogue goes through the shared-memory transpose (coalesced rows)
   int staged;
-  QkvPrep qkv;  // GEMM_EPI_QKV (staged epilogue only)
+  QkvPrep qkv;          // GEMM_EPI_QKV (staged epilogue only)
+  AttnGradPrep dprep;   // GEMM_EPI_ATTN_DO (staged epilogue only)
   int* error;
 };
 
@@ -502,6 +503,22 @@ __device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int row, int n,
   *reinterpret_cast<float4*>(lo + o) = l4;
 }
 
+// dO columns [n, n + 4) of row `row` as the attention backward's head-major
+// TF32 hi / lo operands (attention_bwd_tc.cu attn_bwd_prepare_kernel writes
+// the same values).
+__device__ __forceinline__ void attn_do_store(const AttnGradPrep& g, int row, int n, float4 x) {
+  const int h = n / g.Dh, j = n - h * g.Dh;
+  const int b = row / g.T, t = row - b * g.T;
+  const int64_t o = (((int64_t)b * g.H + h) * g.T + t) * g.Dh + j;
+  float4 h4, l4;
+  tf32_split(x.x, h4.x, l4.x);
+  tf32_split(x.y, h4.y, l4.y);
+  tf32_split(x.z, h4.z, l4.z);
+  tf32_split(x.w, h4.w, l4.w);
+  *reinterpret_cast<float4*>(g.doh + o) = h4;
+  *reinterpret_cast<float4*>(g.dol + o) = l4;
+}
+
 // ---- 2-SM (CTA pair) 3xTF32 kernel ---------------------------------------------
 //
 // A cluster of two CTAs on the two SMs of a TPC computes a 256 x BN output
@@ -577,7 +594,9 @@ struct Tc2Layout {
   static constexpr uint32_t TMEM_COLS = 2 * BN;  static_assert(SMEM_BYTES <= 232448, "shared memory above the 227 KB per-CTA limit");
 };
 
-template <int BN, int STAGES>
+// ATTN: the instance that also carries the attention-operand epilogues
+// (QKV, ATTN_DO); the other modes use the lighter instance (fewer registers).
+template <int BN, int STAGES, bool ATTN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb_lo,
@@ -738,7 +757,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       const int64_t ldc = part ? (int64_t)args.N : args.ldc;
       const float* bias = part ? nullptr : args.bias;
       const int accumulate = part ? 0 : args.accumulate;
-      const int epi = part ? 0 : args.epilogue;
+      int epi = part ? 0 : args.epilogue;
+      if (!ATTN && (epi == GEMM_EPI_QKV || epi == GEMM_EPI_ATTN_DO)) epi = GEMM_EPI_PLAIN;
       const int64_t roff = (int64_t)m * ldc;
       const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0);
       // the warp's column-partial row of the GELU_BWD mode
@@ -752,6 +772,10 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
         const int sub = lane >> 3, q = lane & 7;
         const int row0 = m - lane;
         const bool has_aux = epi == GEMM_EPI_RESIDUAL || epi == GEMM_EPI_GELU_BWD;
+        // ATTN_DO: per row of the warp, the running dO . O sum of the current head
+        float dacc[8];
+#pragma unroll
+        for (int it = 0; it < 8; it++) dacc[it] = 0.0f;
 #pragma unroll 1
         for (int c = col_begin; c < col_begin + BN / 2; c += 32) {
           const int n = n_tile + c + 4 * q;
@@ -764,6 +788,15 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             pre[it] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (has_aux && row < args.M && col_ok)
               pre[it] = __ldg(reinterpret_cast<const float4*>(args.aux + (int64_t)row * ldc + n));
+            if (ATTN && epi == GEMM_EPI_ATTN_DO && row < args.M && col_ok) {
+              // the forward output o = hi + lo (exact), same layout as dO
+              const int64_t oo = (int64_t)row * (args.dprep.H * args.dprep.Dh) + n;
+              const float4 oh = __ldg(reinterpret_cast<const float4*>(args.dprep.o + oo));
+              float4 ol = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (args.dprep.o_lo != nullptr)
+                ol = __ldg(reinterpret_cast<const float4*>(args.dprep.o_lo + oo));
+              pre[it] = make_float4(oh.x + ol.x, oh.y + ol.y, oh.z + ol.z, oh.w + ol.w);
+            }
 
           }
           float v[32];
@@ -781,6 +814,22 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             const int r = 4 * it + sub;
             float4 x = lds128(stage + (uint32_t)r * 128u + (((uint32_t)q ^ (uint32_t)(r & 7)) << 4));
             const int row = row0 + r;
+            if (ATTN && epi == GEMM_EPI_ATTN_DO) {
+              // C = dO, its head-major hi / lo copies, and the row's dO . O over
+              // these 32 columns (summed over the 8 lanes of the row)
+              float dot = 0.0f;
+              if (row < args.M && col_ok) {
+                *reinterpret_cast<float4*>(cbase + (int64_t)row * ldc + n) = x;
+                attn_do_store(args.dprep, row, n, x);
+                const float4 o = pre[it];
+                dot = fmaf(x.w, o.w, fmaf(x.z, o.z, fmaf(x.y, o.y, x.x * o.x)));
+              }
+              dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+              dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+              dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+              dacc[it] += dot;
+              continue;
+            }
             if (row >= args.M || !col_ok) continue;
             const int64_t off = (int64_t)row * ldc + n;
             if (epi == GEMM_EPI_GELU_BWD) {
@@ -828,7 +877,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
                 *reinterpret_cast<float4*>(args.out3 + off) = lo;
               }
               *reinterpret_cast<float4*>(args.out2 + off) = g;
-            } else if (epi == GEMM_EPI_QKV) {
+            } else if (ATTN && epi == GEMM_EPI_QKV) {
               qkv_prep_store(args.qkv, row, n, x, qkv_rope_coeffs(args.qkv, row, n));
             }
           }
@@ -842,6 +891,23 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               cs.w += __shfl_xor_sync(0xffffffffu, cs.w, o);
             }
             if (sub == 0 && col_ok) *reinterpret_cast<float4*>(colpart + n) = cs;
+          }
+          if (ATTN && epi == GEMM_EPI_ATTN_DO && (n_tile + c + 32) % args.dprep.Dh == 0) {
+            // the chunk completes a head: one lane per row writes its delta and
+            // its base-2 log-sum-exp (the attention backward's formula)
+            const int h = (n_tile + c) / args.dprep.Dh;
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+              const int row = row0 + 4 * it + sub;
+              if (q == 0 && row < args.M && n_tile + c < args.N) {
+                const int b = row / args.dprep.T, t = row - b * args.dprep.T;
+                const int64_t ri = ((int64_t)b * args.dprep.H + h) * args.dprep.T + t;
+                args.dprep.delta[ri] = dacc[it];
+                const float l = args.dprep.row_sum[ri];
+                args.dprep.lse2[ri] = l > 0.0f ? (args.dprep.row_max[ri] + logf(l)) * 1.4426950408889634f : INFINITY;
+              }
+              dacc[it] = 0.0f;
+            }
           }
           __syncwarp();
         }
@@ -1109,8 +1175,10 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
     gemm_simt(g, stream);
     return;
   }
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       L::SMEM_BYTES);
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, false>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, true>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
   TcArgs a{};
   a.M = g.M; a.N = g.N; a.K = g.K;
   a.C = g.C; a.ldc = g.ldc; a.bias = g.bias; a.accumulate = g.accumulate ? 1 : 0;
@@ -1125,13 +1193,18 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   a.out3 = g.out3;
   a.colpart = g.epi_ws;
   if (g.epilogue == GEMM_EPI_QKV) a.qkv = *g.qkv;
+  if (g.epilogue == GEMM_EPI_ATTN_DO) a.dprep = *g.dprep;
   {
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     a.staged = (g.ldc % 4 == 0) && (g.N % 4 == 0) && al(g.C) && al(g.aux) && al(g.out2) &&
                al(g.out3) && al(g.bias) && al(g.epi_ws) && al(g.workspace);
+    if (g.epilogue == GEMM_EPI_ATTN_DO)
+      a.staged = a.staged && al(g.dprep->o) && al(g.dprep->o_lo) && al(g.dprep->doh) &&
+                 al(g.dprep->dol) && g.dprep->Dh % 32 == 0 && g.N == g.dprep->H * g.dprep->Dh;
   }
-  // the QKV operands are written by the staged epilogue only
-  const bool prep_after = g.epilogue == GEMM_EPI_QKV && !a.staged;
+  // the attention operands are written by the staged epilogue only
+  const bool prep_after =
+      (g.epilogue == GEMM_EPI_QKV || g.epilogue == GEMM_EPI_ATTN_DO) && !a.staged;
   if (prep_after) a.epilogue = GEMM_EPI_PLAIN;
   const int tiles = a.tiles_m * a.tiles_n;
   const int nkb = (g.K + L::BK - 1) / L::BK;
@@ -1148,13 +1221,20 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   }
   const int units = tiles * a.splits;
   const int grid = 2 * (units < pairs ? units : pairs);
-  gemm_tc2_kernel<BN, STAGES><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(ta, ta_lo, tb, tb_lo,
-                                                                            a);
+  if (a.epilogue == GEMM_EPI_QKV || a.epilogue == GEMM_EPI_ATTN_DO)
+    gemm_tc2_kernel<BN, STAGES, true><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(
+        ta, ta_lo, tb, tb_lo, a);
+  else
+    gemm_tc2_kernel<BN, STAGES, false><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(
+        ta, ta_lo, tb, tb_lo, a);
   count_launch();
   if (g.epilogue == GEMM_EPI_GELU_BWD) {
     reduce_partials(g.epi_ws, a.tiles_m * 8, g.N, g.N, g.dsum, nullptr, nullptr, stream);
   }
-  if (prep_after) attention_prepare_from_qkv(g.C, g.ldc, g.M, *g.qkv, stream);
+  if (prep_after && g.epilogue == GEMM_EPI_QKV)
+    attention_prepare_from_qkv(g.C, g.ldc, g.M, *g.qkv, stream);
+  if (prep_after && g.epilogue == GEMM_EPI_ATTN_DO)
+    attention_prepare_grad_from(g.C, g.ldc, g.M, *g.dprep, stream);
   if (a.splits > 1) {
     const int64_t total = (int64_t)g.M * g.N;
     const int64_t want = (total + 255) / 256;
@@ -1183,6 +1263,7 @@ void epilogue_after(const GemmArgs& g, cudaStream_t stream) {
                            stream);
       break;
     case GEMM_EPI_QKV: attention_prepare_from_qkv(g.C, g.ldc, g.M, *g.qkv, stream); break;
+    case GEMM_EPI_ATTN_DO: attention_prepare_grad_from(g.C, g.ldc, g.M, *g.dprep, stream); break;
     default: break;
   }
 }

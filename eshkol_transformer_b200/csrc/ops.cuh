@@ -155,7 +155,30 @@ struct AttnParams {
   // qkv_ready: ws already holds the prepared Q/K/V (the fused QKV GEMM
   // epilogue wrote them), so the forward skips that pass as well.
   int qkv_ready;
+  // grad_ready: the backward's dO hi/lo (workspace) and delta were written by
+  // the GEMM that produced dO (AttnGradPrep), so the backward skips its prepass.
+  int grad_ready;
 };
+// Where the GEMM producing dO = dY Wo (rows [B*T, H*Dh], token-major) writes
+// the attention backward's inputs: dO split into TF32 hi / lo head-major
+// [B, H, T, Dh] and delta[(b*H + h)*T + t] = sum_j dO_j (o_j + o_lo_j) over
+// the head's Dh columns (o, o_lo: the forward output, same layout as dO), and
+// the row's base-2 log-sum-exp lse2 from the forward's statistics.
+struct AttnGradPrep {
+  int T, H, Dh;
+  const float* o;
+  const float* o_lo;
+  const float *row_max, *row_sum;
+  float *doh, *dol, *delta, *lse2;
+};
+// The AttnGradPrep of p's backward workspace when the tensor-core backward
+// will run with o given as the merged [B*T, Hq*Dh] rows (false otherwise).
+bool attention_grad_prep(const AttnParams& p, AttnTensor o, const float* o_lo,
+                         const float* row_max, const float* row_sum, float* delta,
+                         AttnGradPrep* out);
+// The same from a dO matrix already in memory (row stride ld).
+void attention_prepare_grad_from(const float* dout, int64_t ld, int rows, const AttnGradPrep& g,
+                                 cudaStream_t stream);
 // Where a fused QKV projection writes the attention operands: the RoPE'd Q
 // and K and plain V of a [B*T, (Hq + 2 Hkv) Dh] row-major qkv matrix (the
 // columns Q | K | V, head-major within each), split into TF32 hi / residual
@@ -233,6 +256,8 @@ struct GemmArgs {
   //             hi with out2 = lo; dsum[n] = column sums of d (the bias
   //             gradient), through `epi_ws` (gemm_epilogue_ws_floats)
   //   QKV       C = y + bias, and the attention operands of C (QkvPrep `qkv`)
+  //   ATTN_DO   C = y, and the attention backward's dO hi/lo and delta
+  //             (AttnGradPrep `dprep`)
   int epilogue;
   const float* aux;
   float* out2;
@@ -240,13 +265,15 @@ struct GemmArgs {
   float* dsum;
   float* epi_ws;
   const QkvPrep* qkv;
+  const AttnGradPrep* dprep;
 };
 enum {
   GEMM_EPI_PLAIN = 0,
   GEMM_EPI_RESIDUAL = 1,
   GEMM_EPI_GELU_FWD = 2,
   GEMM_EPI_GELU_BWD = 3,
-  GEMM_EPI_QKV = 4
+  GEMM_EPI_QKV = 4,
+  GEMM_EPI_ATTN_DO = 5
 };
 // Scratch floats split-K may use for an M x N output.
 size_t gemm_splitk_floats(int M, int N);

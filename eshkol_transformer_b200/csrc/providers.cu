@@ -240,9 +240,19 @@ bool device_finite(const float* p, size_t n) {
   return flag == 0;
 }
 
-// Copies device results to host outputs (host views) and waits.
+// Copies device results to host outputs (host views) and waits.  The kernel
+// ABI's invoke returns nothing, so a CUDA error raised by this call's
+// launches is reported on stderr and the outputs are filled with NaN rather
+// than left holding stale memory.
 void finish(Call& cl, const std::vector<void*>& outs) {
   Pool& P = pool();
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) {
+    fprintf(stderr, "et_b200: CUDA error in a kernel call: %s\n", cudaGetErrorString(st));
+    for (size_t i = 0; i < cl.out.size() && i < outs.size(); i++)
+      if (cl.out[i]->byte_length && outs[i] != nullptr)
+        cudaMemsetAsync(outs[i], 0xff, cl.out[i]->byte_length, P.stream);  // all-ones: NaN
+  }
   if (cl.host)
     for (size_t i = 0; i < cl.out.size(); i++)
       if (cl.out[i]->byte_length)

@@ -216,7 +216,7 @@ void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t ro
 void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int64_t rows,
                         int64_t din, int64_t dout, int wt, float* dxo,
                         const float* gelu_in = nullptr, float* dxo_lo = nullptr,
-                        float* dsum = nullptr) {
+                        float* dsum = nullptr, const AttnGradPrep* dprep = nullptr) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)din; g.K = (int)dout;
   g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = true;
@@ -225,6 +225,10 @@ void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int6
   if (gelu_in != nullptr) {
     g.epilogue = GEMM_EPI_GELU_BWD; g.aux = gelu_in; g.out2 = dxo_lo; g.dsum = dsum;
     g.epi_ws = lm->epi_ws;
+  }
+  if (dprep != nullptr) {
+    g.epilogue = GEMM_EPI_ATTN_DO;
+    g.dprep = dprep;
   }
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->precision, lm->stream);
@@ -382,16 +386,22 @@ void backward(et_b200_lm* lm) {
     // attention output projection: dY = dx
     dyh = three ? lm->dxhi : lm->dx;
     dyl = three ? lm->dxlo : nullptr;
-    linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp);
+    // dO = dY Wo; its epilogue also writes the attention backward's dO
+    // operands and delta
+    AttnParams p = attn_params(lm, a.qkv, l);
+    p.ws_ready = lm->attn_prepared[l];
+    const AttnTensor ao{a.ao, lm->T * d, lm->Dh, d};
+    AttnGradPrep dprep;
+    p.grad_ready = attention_grad_prep(p, ao, a.aolo, a.am, a.al, lm->delta, &dprep) ? 1 : 0;
+    linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp, nullptr, nullptr, nullptr,
+                       p.grad_ready ? &dprep : nullptr);
     linear_backward_dw(lm, dyh, dyl, a.ao, a.aolo, R, d, d, lm->G(lm->lt(l, T_WO)));
     {
-      AttnParams p = attn_params(lm, a.qkv, l);
-      p.ws_ready = lm->attn_prepared[l];
       Mark mk(lm, P_ATTN_BWD, attn_flop(lm, 4), 0);
       const int64_t w = 3 * d;
       float* lo = lm->dqkvlo;  // null unless 3xTF32
       dqkv_split = attention_backward(
-          p, AttnTensor{a.ao, lm->T * d, lm->Dh, d}, a.aolo,
+          p, ao, a.aolo,
           AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d}, a.am, a.al, lm->delta,
           AttnOut{lm->dqkv, lm->T * w, lm->Dh, w, lo}, AttnOut{lm->dqkv + d, lm->T * w, lm->Dh, w, lo ? lo + d : nullptr},
           AttnOut{lm->dqkv + 2 * d, lm->T * w, lm->Dh, w, lo ? lo + 2 * d : nullptr}, s) && three;
