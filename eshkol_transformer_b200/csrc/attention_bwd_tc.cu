@@ -475,21 +475,33 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
       }
     }
     named_sync(1, SOFT);
+    // column-sum scratch behind the two staged tiles (one per output)
+    const uint32_t red = base + (uint32_t)(2 * 128 * (DH + 4) * 4);
     if (ok) {
       const bool split = dk.lo != nullptr && dv.lo != nullptr;
       const int rows = min(BK, p.Tk - k0);
       const int64_t ko = b * dk.sb + hkv * dk.sh + (int64_t)k0 * dk.st;
-      store_rows_split(base, DH, rows, dk.ptr + ko, split ? dk.lo + ko : nullptr, dk.st, tid, SOFT,
-                       [&](int r, int c4, float4& v) {
-                         const int t = k0 + r;
-                         const int64_t trw =
-                             (int64_t)(p.k_rope_batched ? b * p.Tk + t : t) * (DH / 2);
-                         grad_rotate4(v, p.scale, p.k_cos, p.k_sin, trw, c4);
-                       });
+      const float4 sk = store_rows_split(
+          base, DH, rows, dk.ptr + ko, split ? dk.lo + ko : nullptr, dk.st, tid, SOFT,
+          [&](int r, int c4, float4& v) {
+            const int t = k0 + r;
+            const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + t : t) * (DH / 2);
+            grad_rotate4(v, p.scale, p.k_cos, p.k_sin, trw, c4);
+          });
       const int64_t vo = b * dv.sb + hkv * dv.sh + (int64_t)k0 * dv.st;
-      store_rows_split(base + (uint32_t)(128 * (DH + 4) * 4), DH, rows, dv.ptr + vo,
-                       split ? dv.lo + vo : nullptr, dv.st, tid, SOFT,
-                       [](int, int, float4&) {});
+      const float4 sv = store_rows_split(base + (uint32_t)(128 * (DH + 4) * 4), DH, rows,
+                                         dv.ptr + vo, split ? dv.lo + vo : nullptr, dv.st, tid,
+                                         SOFT, [](int, int, float4&) {});
+      colsum_put(red, tid, sk);
+      colsum_put(red + SOFT * 16u, tid, sv);
+    }
+    named_sync(1, SOFT);
+    if (ok) {
+      const int64_t prow = (int64_t)b * ((p.Tk + BK - 1) / BK) + blockIdx.x;
+      if (dk.colsum != nullptr)
+        colsum_get(red, tid, SOFT, DH, dk.colsum + prow * dk.colsum_ld + hkv * DH);
+      if (dv.colsum != nullptr)
+        colsum_get(red + SOFT * 16u, tid, SOFT, DH, dv.colsum + prow * dv.colsum_ld + hkv * DH);
     }
   }
   tc_fence_before();
@@ -852,16 +864,23 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
       }
     }
     named_sync(1, SOFT);
+    // column-sum scratch behind the staged tile
+    const uint32_t red = base + (uint32_t)(128 * (DH + 4) * 4);
     if (ok) {
       const int64_t qo = b * dq.sb + hq * dq.sh + (int64_t)q0 * dq.st;
-      store_rows_split(base, DH, min(QM, p.Tq - q0), dq.ptr + qo,
-                       dq.lo != nullptr ? dq.lo + qo : nullptr, dq.st, tid, SOFT,
-                       [&](int r, int c4, float4& v) {
-                         const int t = q0 + r;
-                         const int64_t trw =
-                             (int64_t)(p.q_rope_batched ? b * p.Tq + t : t) * (DH / 2);
-                         grad_rotate4(v, p.scale, p.q_cos, p.q_sin, trw, c4);
-                       });
+      const float4 sq = store_rows_split(
+          base, DH, min(QM, p.Tq - q0), dq.ptr + qo, dq.lo != nullptr ? dq.lo + qo : nullptr,
+          dq.st, tid, SOFT, [&](int r, int c4, float4& v) {
+            const int t = q0 + r;
+            const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + t : t) * (DH / 2);
+            grad_rotate4(v, p.scale, p.q_cos, p.q_sin, trw, c4);
+          });
+      colsum_put(red, tid, sq);
+    }
+    named_sync(1, SOFT);
+    if (ok && dq.colsum != nullptr) {
+      const int64_t prow = (int64_t)b * ((p.Tq + QM - 1) / QM) + blockIdx.x;
+      colsum_get(red, tid, SOFT, DH, dq.colsum + prow * dq.colsum_ld + hq * DH);
     }
   }
   tc_fence_before();

@@ -135,11 +135,13 @@ __device__ __forceinline__ void store_staged_rows(uint32_t stage, int cols, int 
 // nthreads, ... (row r = i / (cols / 4), column 4 (i % (cols / 4))), applies
 // f(r, c4, v) in place, then stores v to hi_base (lo_base null) or its TF32
 // hi part to hi_base and the residual to lo_base.  Row r goes to
-// base + r * row_stride.
+// base + r * row_stride.  Returns the sum of the thread's v (its rows of
+// columns 4 (t % (cols / 4)) .. when nthreads is a multiple of cols / 4).
 template <typename F>
-__device__ __forceinline__ void store_rows_split(uint32_t stage, int cols, int rows_valid,
-                                                 float* hi_base, float* lo_base,
-                                                 int64_t row_stride, int t, int nthreads, F f) {
+__device__ __forceinline__ float4 store_rows_split(uint32_t stage, int cols, int rows_valid,
+                                                   float* hi_base, float* lo_base,
+                                                   int64_t row_stride, int t, int nthreads, F f) {
+  float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
   const int per_row = cols / 4;
   const uintptr_t bits = reinterpret_cast<uintptr_t>(hi_base) |
                          reinterpret_cast<uintptr_t>(lo_base) | (uintptr_t)(row_stride * 4);
@@ -149,6 +151,7 @@ __device__ __forceinline__ void store_rows_split(uint32_t stage, int cols, int r
     const int r = idx / per_row, c4 = idx - r * per_row;
     float4 v = lds128(stage + ((uint32_t)r * (uint32_t)(cols + 4) + 4u * (uint32_t)c4) * 4u);
     f(r, c4, v);
+    sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
     float4 lo = make_float4(0.f, 0.f, 0.f, 0.f);
     if (lo_base != nullptr) {
       tf32_split(v.x, v.x, lo.x);
@@ -169,6 +172,27 @@ __device__ __forceinline__ void store_rows_split(uint32_t stage, int cols, int r
       }
     }
   }
+  return sum;
+}
+
+// Column sums of a written tile from the threads' store_rows_split sums: each
+// thread puts its sum into shared scratch `red` (nthreads float4) before a
+// barrier of the nthreads threads (colsum_put), then the first cols / 4
+// threads add the groups in thread order and store 4 columns each
+// (colsum_get).
+__device__ __forceinline__ void colsum_put(uint32_t red, int t, float4 sum) {
+  sts128(red + (uint32_t)t * 16u, sum);
+}
+__device__ __forceinline__ void colsum_get(uint32_t red, int t, int nthreads, int cols,
+                                           float* out) {
+  const int per_row = cols / 4;
+  if (t >= per_row) return;
+  float4 s = lds128(red + (uint32_t)t * 16u);
+  for (int g = 1; g < nthreads / per_row; g++) {
+    const float4 v = lds128(red + (uint32_t)(g * per_row + t) * 16u);
+    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+  }
+  *reinterpret_cast<float4*>(out + 4 * t) = s;
 }
 
 // Gradient scaling and RoPE backward rotation of columns 4 c4 .. 4 c4 + 3 of

@@ -125,6 +125,12 @@ struct AttnOut {
   // optional: when set (same strides as ptr), ptr receives the TF32 hi part
   // and lo the residual (a 3xTF32 operand pair); tensor-core kernels only
   float* lo;
+  // optional (tensor-core backward): per 128-row tile of each sequence, the
+  // column sums of that tile's rows go to colsum[(b * ceil(T/128) + tile) *
+  // colsum_ld + h * Dh + j]; summed over the B * ceil(T/128) rows they are the
+  // column sums of the whole gradient (a bias gradient)
+  float* colsum;
+  int64_t colsum_ld;
 };
 struct AttnParams {
   int B, Hq, Hkv, Tq, Tk, Dh;

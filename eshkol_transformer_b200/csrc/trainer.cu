@@ -84,6 +84,9 @@ struct et_b200_lm {
   float *dx = nullptr, *dxhi = nullptr, *dxlo = nullptr, *dtmp = nullptr, *dqkv = nullptr,
         *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *delta = nullptr;
   float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *epi_ws = nullptr;
+  // per-128-row-tile column sums of dqkv from the attention backward (bqkv gradient)
+  float* qkv_colpart = nullptr;
+  int64_t qkv_colrows = 0;
   // attention: per-layer prepared Q/K/V (written by the forward, reused by
   // the backward) and one shared backward scratch
   std::vector<float*> attn_qkv_ws;
@@ -365,7 +368,7 @@ void backward(et_b200_lm* lm) {
   }
   for (int l = (int)lm->L - 1; l >= 0; l--) {
     LayerActs& a = lm->layers[l];
-    bool dqkv_split = false;
+    bool dqkv_split = false, bqkv_done = false;
     // FFN down: dY = dx (flows to the skip and the branch)
     // dx arrives with its hi/lo pair and its column sums (this layer's b2
     // gradient) from the LayerNorm backward above
@@ -400,14 +403,25 @@ void backward(et_b200_lm* lm) {
       Mark mk(lm, P_ATTN_BWD, attn_flop(lm, 4), 0);
       const int64_t w = 3 * d;
       float* lo = lm->dqkvlo;  // null unless 3xTF32
-      dqkv_split = attention_backward(
-          p, ao, a.aolo,
-          AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d}, a.am, a.al, lm->delta,
-          AttnOut{lm->dqkv, lm->T * w, lm->Dh, w, lo}, AttnOut{lm->dqkv + d, lm->T * w, lm->Dh, w, lo ? lo + d : nullptr},
-          AttnOut{lm->dqkv + 2 * d, lm->T * w, lm->Dh, w, lo ? lo + 2 * d : nullptr}, s) && three;
+      // the tensor-core backward also writes per-tile column sums of dq, dk, dv
+      float* cp = lm->qkv_colpart;
+      const bool tc = attention_backward(
+          p, ao, a.aolo, AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d}, a.am, a.al, lm->delta,
+          AttnOut{lm->dqkv, lm->T * w, lm->Dh, w, lo, cp, w},
+          AttnOut{lm->dqkv + d, lm->T * w, lm->Dh, w, lo ? lo + d : nullptr, cp + d, w},
+          AttnOut{lm->dqkv + 2 * d, lm->T * w, lm->Dh, w, lo ? lo + 2 * d : nullptr, cp + 2 * d, w},
+          s);
+      dqkv_split = tc && three;
+      bqkv_done = tc;
     }
     if (three && !dqkv_split) split(lm, lm->dqkv, lm->dqkvlo, R * 3 * d);
-    bias_grad(lm, lm->dqkv, R, 3 * d, lm->G(lm->lt(l, T_BQKV)), three ? lm->dqkvlo : nullptr);
+    if (bqkv_done) {
+      Mark mk(lm, P_ELEMENTWISE, 0, 4.0 * lm->qkv_colrows * 3 * d);
+      reduce_partials(lm->qkv_colpart, (int)lm->qkv_colrows, 3 * d, 3 * d,
+                      lm->G(lm->lt(l, T_BQKV)), nullptr, nullptr, s);
+    } else {
+      bias_grad(lm, lm->dqkv, R, 3 * d, lm->G(lm->lt(l, T_BQKV)), three ? lm->dqkvlo : nullptr);
+    }
     linear_backward_dx(lm, lm->dqkv, lm->dqkvlo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->dtmp);
     linear_backward_dw(lm, lm->dqkv, lm->dqkvlo, a.h1, a.h1lo, R, d, 3 * d,
                        lm->G(lm->lt(l, T_WQKV)));
@@ -627,6 +641,8 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->col_ws = dalloc<float>(lm, colsum_workspace_floats(R, widest), &err);
   lm->emb_scratch = dalloc<uint8_t>(lm, embedding_scratch_bytes(R, V), &err);
   lm->epi_ws = dalloc<float>(lm, gemm_epilogue_ws_floats((int)R, (int)F), &err);
+  lm->qkv_colrows = (int64_t)lm->B * ((lm->T + 127) / 128);
+  lm->qkv_colpart = dalloc<float>(lm, (size_t)lm->qkv_colrows * 3 * d, &err);
   // split-K partials for the weight-gradient GEMMs of the layers (K = rows)
   lm->splitk_floats = gemm_splitk_floats((int)std::max<int64_t>(3 * d, F), (int)std::max<int64_t>(d, F));
   lm->splitk_ws = dalloc<float>(lm, lm->splitk_floats, &err);
