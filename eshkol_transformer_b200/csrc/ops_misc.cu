@@ -120,78 +120,93 @@ ln_backward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
 }
 
 // Register-resident variant for d = 128 NV (d <= 1024): each warp owns whole
-// rows; lane l holds columns 4 l + 128 i (float4), so x and dy are read once
-// and the column partials (dgamma, dbeta and, with dsum, the column sum of
-// the final dx) accumulate in registers over the warp's rows.  Each block
-// adds its warps' sums in warp order and writes one partial row per quantity;
-// reduce_partials adds the blocks' rows.
+// rows; lane l holds columns 4 l + 128 i (float4).  x, dy and (when
+// accumulating) the incoming dx of a row are loaded together up front, so one
+// memory latency covers the row; the column partials (dgamma, dbeta and, with
+// dsum, the column sum of the final dx) accumulate in the warp's slice of
+// shared memory, which keeps the registers low enough for two blocks per SM.
+// Each block adds its warps' sums in warp order and writes one partial row
+// per quantity; reduce_partials adds the blocks' rows.
 constexpr int kLnbWarps = 8;
 
 template <int NV>
-__global__ void __launch_bounds__(kLnbWarps * 32)
+__global__ void __launch_bounds__(kLnbWarps * 32, 2)
 ln_backward_rows_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                         const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                         const float* __restrict__ dy, float* __restrict__ dx, int accumulate,
                         float* __restrict__ dx_hi, float* __restrict__ dx_lo,
                         float* __restrict__ partial, int with_sum, int64_t rows) {
   constexpr int D = 128 * NV;
+  extern __shared__ float4 lnb_acc[];  // [kLnbWarps][3][32 NV] partials, then gamma [32 NV]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float4 g[NV], ag[NV], ab[NV], as[NV];
+  float4* acc = lnb_acc + warp * 3 * 32 * NV;
+  float4* g = lnb_acc + kLnbWarps * 3 * 32 * NV;
+  for (int i = threadIdx.x; i < 32 * NV; i += kLnbWarps * 32)
+    g[i] = reinterpret_cast<const float4*>(gamma)[i];
 #pragma unroll
-  for (int i = 0; i < NV; i++) {
-    g[i] = reinterpret_cast<const float4*>(gamma)[lane + 32 * i];
-    ag[i] = ab[i] = as[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  for (int i = 0; i < NV; i++)
+    acc[lane + 32 * i] = acc[32 * NV + lane + 32 * i] = acc[64 * NV + lane + 32 * i] =
+        make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
   const float dim = (float)D;
   const float inv_dim = rn_div(1.0f, dim);
   for (int64_t row = (int64_t)blockIdx.x * kLnbWarps + warp; row < rows;
        row += (int64_t)gridDim.x * kLnbWarps) {
     const float4* xr = reinterpret_cast<const float4*>(x + row * D);
     const float4* gr = reinterpret_cast<const float4*>(dy + row * D);
-    float4 xv[NV], gv[NV];
+    float4* dr = reinterpret_cast<float4*>(dx + row * D);
+    float4 xv[NV], gv[NV], dv[NV];
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       xv[i] = xr[lane + 32 * i];
       gv[i] = gr[lane + 32 * i];
+      dv[i] = accumulate ? dr[lane + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const float mean = mean_in[row], rstd = rstd_in[row];
     float sh = 0.0f, shn = 0.0f;
 #pragma unroll
     for (int i = 0; i < NV; i++) {
+      float4 ag = acc[lane + 32 * i], ab = acc[32 * NV + lane + 32 * i];
+      const float4 gi = g[lane + 32 * i];
 #define LNB_ACC(c)                                                  \
   {                                                                 \
     const float n = rn_mul(rn_sub(xv[i].c, mean), rstd);            \
-    const float h = rn_mul(gv[i].c, g[i].c);                        \
+    const float h = rn_mul(gv[i].c, gi.c);                          \
     sh += h;                                                        \
     shn += rn_mul(h, n);                                            \
-    ag[i].c += rn_mul(gv[i].c, n);                                  \
-    ab[i].c += gv[i].c;                                             \
+    ag.c += rn_mul(gv[i].c, n);                                     \
+    ab.c += gv[i].c;                                                \
   }
       LNB_ACC(x) LNB_ACC(y) LNB_ACC(z) LNB_ACC(w)
 #undef LNB_ACC
+      acc[lane + 32 * i] = ag;
+      acc[32 * NV + lane + 32 * i] = ab;
     }
     sh = warp_sum(sh);
     shn = warp_sum(shn);
     const float factor = rn_mul(rstd, inv_dim);
-    float4* dr = reinterpret_cast<float4*>(dx + row * D);
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       float4 out;
+      const float4 gi = g[lane + 32 * i];
 #define LNB_OUT(c)                                                                         \
   {                                                                                        \
     const float n = rn_mul(rn_sub(xv[i].c, mean), rstd);                                   \
-    const float h = rn_mul(gv[i].c, g[i].c);                                               \
+    const float h = rn_mul(gv[i].c, gi.c);                                                 \
     out.c = rn_mul(factor, rn_sub(rn_sub(rn_mul(dim, h), sh), rn_mul(n, shn)));            \
   }
       LNB_OUT(x) LNB_OUT(y) LNB_OUT(z) LNB_OUT(w)
 #undef LNB_OUT
       if (accumulate) {
-        const float4 o = dr[lane + 32 * i];
-        out.x = rn_add(o.x, out.x); out.y = rn_add(o.y, out.y);
-        out.z = rn_add(o.z, out.z); out.w = rn_add(o.w, out.w);
+        out.x = rn_add(dv[i].x, out.x); out.y = rn_add(dv[i].y, out.y);
+        out.z = rn_add(dv[i].z, out.z); out.w = rn_add(dv[i].w, out.w);
       }
       dr[lane + 32 * i] = out;
-      as[i].x += out.x; as[i].y += out.y; as[i].z += out.z; as[i].w += out.w;
+      if (with_sum) {
+        float4 as = acc[64 * NV + lane + 32 * i];
+        as.x += out.x; as.y += out.y; as.z += out.z; as.w += out.w;
+        acc[64 * NV + lane + 32 * i] = as;
+      }
       if (dx_lo != nullptr) {
         float4 h4, l4;
         tf32_split(out.x, h4.x, l4.x);
@@ -204,29 +219,23 @@ ln_backward_rows_kernel(const float* __restrict__ x, const float* __restrict__ g
     }
   }
   // the block's partial row per quantity: the warps' sums added in warp order
-  __shared__ float4 red[kLnbWarps][32 * NV];
+  __syncthreads();
   const int nq = with_sum ? 3 : 2;
   float4* out = reinterpret_cast<float4*>(partial + (int64_t)blockIdx.x * nq * D);
-  for (int qi = 0; qi < nq; qi++) {
+  for (int idx = threadIdx.x; idx < nq * 32 * NV; idx += kLnbWarps * 32) {
+    float4 t = lnb_acc[idx];
 #pragma unroll
-    for (int i = 0; i < NV; i++) red[warp][lane + 32 * i] = qi == 0 ? ag[i] : (qi == 1 ? ab[i] : as[i]);
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < 32 * NV; idx += kLnbWarps * 32) {
-      float4 t = red[0][idx];
-#pragma unroll
-      for (int w = 1; w < kLnbWarps; w++) {
-        const float4 o = red[w][idx];
-        t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
-      }
-      out[qi * (D / 4) + idx] = t;
+    for (int w = 1; w < kLnbWarps; w++) {
+      const float4 o = lnb_acc[w * 3 * 32 * NV + idx];
+      t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
     }
-    __syncthreads();
+    out[idx] = t;
   }
 }
 
 int ln_backward_rows_blocks(size_t rows) {
   const size_t want = (rows + kLnbWarps - 1) / kLnbWarps;
-  const size_t cap = (size_t)sm_count() * 2;
+  const size_t cap = (size_t)sm_count() * 4;
   return (int)(want < cap ? want : cap);
 }
 
@@ -539,10 +548,15 @@ void layer_norm_backward(const float* x, const float* gamma, const float* mean, 
     float* hi = dx_lo ? dx_hi : nullptr;
     switch (d / 128) {
 #define LNB_CASE(nv)                                                                          \
-  case nv:                                                                                    \
-    ln_backward_rows_kernel<nv><<<blocks, kLnbWarps * 32, 0, stream>>>(                       \
+  case nv: {                                                                                  \
+    const int smem = (kLnbWarps * 3 + 1) * 32 * (nv) * (int)sizeof(float4);                  \
+    if (smem > 48 * 1024)                                                                     \
+      cudaFuncSetAttribute(ln_backward_rows_kernel<nv>,                                       \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                \
+    ln_backward_rows_kernel<nv><<<blocks, kLnbWarps * 32, smem, stream>>>(                    \
         x, gamma, mean, rstd, dy, dx, accumulate, hi, dx_lo, workspace, with_sum, (int64_t)rows); \
-    break;
+    break;                                                                                    \
+  }
       LNB_CASE(1) LNB_CASE(2) LNB_CASE(3) LNB_CASE(4) LNB_CASE(5) LNB_CASE(6) LNB_CASE(7)
       LNB_CASE(8)
 #undef LNB_CASE
