@@ -101,6 +101,16 @@ __global__ void attn_prepare_kernel(AttnTensor src, int B, int H, int T, int Dh,
   }
 }
 
+// a / b from rb = RN(1 / b): the quotient q = RN(a rb) corrected once with
+// the exact remainder a - q b (one FMA) -- Markstein's division refinement
+// (P. Markstein, IA-64 and Elementary Functions, 2000), which rounds correctly
+// except in rare boundary cases (then within one unit in the last place).
+__device__ __forceinline__ float div_by(float a, float b, float rb) {
+  const float q = __fmul_rn(a, rb);
+  const float r = __fmaf_rn(-q, b, a);
+  return __fmaf_rn(r, rb, q);
+}
+
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
 }
@@ -130,7 +140,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
   uint8_t* smem = align1024(smem_raw);
   __shared__ int64_t kpos_s[2 * KN];     // key positions of the block, ring of 2
   __shared__ float xmax[2 * 2 * QM];     // [block parity][half][row] maxima / exp-sums
-  __shared__ float lrow_s[QM];           // row exp-sums for the output pass
+  __shared__ float lrow_s[QM], rrow_s[QM];  // row exp-sums and their reciprocals (output pass)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
   // barrier slots: full[NST] | empty[NST] | s_full[NSL] | pv_done[NSL] | p_ready[2] |
   // kp_full[2] | rows | pair[4] (the two softmax warps of a lane quarter)
@@ -424,7 +434,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
     // a row without admitted keys); o = O / l, split into the TF32 hi part
     // (o) and the residual (o.lo) when o.lo is set, is formed while the rows
     // are written out (coalesced)
-    if (khalf == 0) lrow_s[row] = (empty || nkb == 0) ? 0.0f : lsum;
+    if (khalf == 0) {
+      lrow_s[row] = (empty || nkb == 0) ? 0.0f : lsum;
+      rrow_s[row] = (empty || nkb == 0) ? 0.0f : rn_div(1.0f, lsum);
+    }
     const uint32_t stage = base;
     if (ok) {
       tc_fence_after();
@@ -459,12 +472,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
       store_rows_split(stage, DH, min(QM, p.Tq - q0), o.ptr + oo,
                        o.lo != nullptr ? o.lo + oo : nullptr, o.st, tid, SOFT,
                        [&](int r, int, float4& v) {
-                         const float l = lrow_s[r];
+                         const float l = lrow_s[r], rl = rrow_s[r];
                          if (l == 0.0f) {
                            v = make_float4(0.f, 0.f, 0.f, 0.f);
                          } else {
-                           v.x = rn_div(v.x, l); v.y = rn_div(v.y, l);
-                           v.z = rn_div(v.z, l); v.w = rn_div(v.w, l);
+                           v.x = div_by(v.x, l, rl); v.y = div_by(v.y, l, rl);
+                           v.z = div_by(v.z, l, rl); v.w = div_by(v.w, l, rl);
                          }
                        });
     }
