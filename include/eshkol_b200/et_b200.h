@@ -243,6 +243,79 @@ int32_t et_b200_lm_profile_v1(et_b200_lm *lm, int32_t enable);
 int32_t et_b200_lm_profile_collect_v1(et_b200_lm *lm);
 int32_t et_b200_lm_profile_read_v1(et_b200_lm *lm, double *out, size_t count);
 
+/* ------------------------------------------------------------ A2 KV cache
+ *
+ * The reference's transactional K/V cache with its storage in device memory
+ * (replaces include/eshkol_transformer/a2_kv_cache.h:42-147, semantics of
+ * native/a2_kv_cache.c:394-880).  Same names, arguments, lease rules and error
+ * categories/codes.  Differences a caller sees: K/V storage [layers, batch,
+ * kv_heads, capacity, head_dimension], the lengths [batch] and the key-keep
+ * mask [batch, capacity] handed out by views and read borrows are device
+ * ("cuda") tensor views on the GPU that was current at create; stage_layer
+ * sources may be "cpu" or "cuda" views; append_counts stays a "cpu" view.
+ * Every call has finished its device work when it returns.  The views feed
+ * the A2 provider's attention directly (cached decoding: Tq new tokens over
+ * Tk = capacity keys, the key-keep mask broadcast over the queries).
+ */
+typedef struct et_a2_kv_cache et_a2_kv_cache;
+typedef struct et_a2_kv_cache_transaction et_a2_kv_cache_transaction;
+typedef struct et_a2_kv_cache_transaction_view et_a2_kv_cache_transaction_view;
+typedef struct et_a2_kv_cache_read_borrow et_a2_kv_cache_read_borrow;
+/* replaces a2_kv_cache.h:42-53 */
+int32_t et_a2_kv_cache_abi_major_v1(void);
+int32_t et_a2_kv_cache_abi_minor_v1(void);
+int32_t et_a2_kv_cache_abi_require_v1(uint32_t major, uint32_t minimum_minor,
+                                      et_kernel_error *error);
+/* replaces a2_kv_cache.h:61-68 (storage zero-initialised in device memory) */
+int32_t et_a2_kv_cache_create_v1(uint64_t layers, uint64_t batch,
+                                 uint64_t kv_heads, uint64_t capacity,
+                                 uint64_t head_dimension,
+                                 et_a2_kv_cache **cache,
+                                 et_kernel_error *error);
+int32_t et_a2_kv_cache_destroy_v1(et_a2_kv_cache **cache,
+                                  et_kernel_error *error);
+/* replaces a2_kv_cache.h:70-85 */
+int32_t et_a2_kv_cache_transaction_begin_v1(
+    et_a2_kv_cache *cache, uint64_t append_width,
+    const et_kernel_tensor_view_v1 *append_counts,
+    et_a2_kv_cache_transaction **transaction, et_kernel_error *error);
+/* replaces a2_kv_cache.h:87-96 ("cpu" or "cuda" sources) */
+int32_t et_a2_kv_cache_transaction_stage_layer_v1(
+    et_a2_kv_cache_transaction *transaction, uint64_t layer,
+    const et_kernel_tensor_view_v1 *keys,
+    const et_kernel_tensor_view_v1 *values, et_kernel_error *error);
+/* replaces a2_kv_cache.h:98-120 (device views) */
+int32_t et_a2_kv_cache_transaction_view_begin_v1(
+    et_a2_kv_cache_transaction *transaction, uint64_t layer,
+    et_a2_kv_cache_transaction_view **view, et_kernel_error *error);
+int32_t et_a2_kv_cache_transaction_view_tensors_v1(
+    const et_a2_kv_cache_transaction_view *view,
+    const et_kernel_tensor_view_v1 **keys,
+    const et_kernel_tensor_view_v1 **values,
+    const et_kernel_tensor_view_v1 **effective_lengths,
+    const et_kernel_tensor_view_v1 **key_keep_mask,
+    et_kernel_error *error);
+int32_t et_a2_kv_cache_transaction_view_end_v1(
+    et_a2_kv_cache_transaction_view **view, et_kernel_error *error);
+/* replaces a2_kv_cache.h:122-126 (abort scrubs staged slots to +0) */
+int32_t et_a2_kv_cache_transaction_commit_v1(
+    et_a2_kv_cache_transaction **transaction, et_kernel_error *error);
+int32_t et_a2_kv_cache_transaction_abort_v1(
+    et_a2_kv_cache_transaction **transaction, et_kernel_error *error);
+/* replaces a2_kv_cache.h:128-147 (device views) */
+int32_t et_a2_kv_cache_read_borrow_begin_v1(
+    et_a2_kv_cache *cache, et_a2_kv_cache_read_borrow **borrow,
+    et_kernel_error *error);
+int32_t et_a2_kv_cache_read_borrow_layer_v1(
+    et_a2_kv_cache_read_borrow *borrow, uint64_t layer,
+    const et_kernel_tensor_view_v1 **keys,
+    const et_kernel_tensor_view_v1 **values,
+    const et_kernel_tensor_view_v1 **lengths,
+    const et_kernel_tensor_view_v1 **key_keep_mask,
+    et_kernel_error *error);
+int32_t et_a2_kv_cache_read_borrow_end_v1(
+    et_a2_kv_cache_read_borrow **borrow, et_kernel_error *error);
+
 #ifdef __cplusplus
 }
 #endif
