@@ -242,13 +242,22 @@ bool device_finite(const float* p, size_t n) {
 
 // Copies device results to host outputs (host views) and waits.  The kernel
 // ABI's invoke returns nothing, so a CUDA error raised by this call's
-// launches is reported on stderr and the outputs are filled with NaN rather
-// than left holding stale memory.
+// launches, or a device-side wait that timed out, is reported on stderr and
+// the outputs are filled with NaN rather than left holding stale memory.
 void finish(Call& cl, const std::vector<void*>& outs) {
   Pool& P = pool();
+  // a launch error, or a bounded device-side wait that gave up (the device
+  // error word), fails the call loudly
+  int word = 0;
+  cudaMemcpyAsync(&word, device_error_word(), sizeof(int), cudaMemcpyDeviceToHost, P.stream);
+  cudaStreamSynchronize(P.stream);
   cudaError_t st = cudaGetLastError();
-  if (st != cudaSuccess) {
-    fprintf(stderr, "et_b200: CUDA error in a kernel call: %s\n", cudaGetErrorString(st));
+  if (st != cudaSuccess || word != 0) {
+    if (st != cudaSuccess)
+      fprintf(stderr, "et_b200: CUDA error in a kernel call: %s\n", cudaGetErrorString(st));
+    else
+      fprintf(stderr, "et_b200: a kernel gave up a bounded wait (error word 0x%x)\n", word);
+    cudaMemsetAsync(device_error_word(), 0, sizeof(int), P.stream);
     for (size_t i = 0; i < cl.out.size() && i < outs.size(); i++)
       if (cl.out[i]->byte_length && outs[i] != nullptr)
         cudaMemsetAsync(outs[i], 0xff, cl.out[i]->byte_length, P.stream);  // all-ones: NaN
