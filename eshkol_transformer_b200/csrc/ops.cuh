@@ -31,6 +31,10 @@ struct AdamwTensor {
   // per-tensor scalars computed on the host with the reference's rounding
   float beta1, beta2, one_minus_beta1, one_minus_beta2, bias1, bias2, lr,
       decay, epsilon;
+  // optional: the updated value's TF32 hi / residual lo pair (the weight
+  // operands of the 3xTF32 GEMMs), written in the same pass
+  float* value_hi;
+  float* value_lo;
 };
 // One fused pass over every tensor of the table (device array `tensors`,
 // `prefix[i]` = first global element of tensor i, total = prefix[count]).

@@ -115,6 +115,7 @@ __global__ void mean_loss_kernel(const float* __restrict__ loss, int64_t rows,
 constexpr int kAdamThreads = 256;
 constexpr int kAdamPerThread = 8;
 constexpr int64_t kAdamChunk = (int64_t)kAdamThreads * kAdamPerThread;
+constexpr int kAdamBatch = 4;
 
 __device__ __forceinline__ int find_tensor(const uint64_t* prefix, int count, uint64_t e) {
   int lo = 0, hi = count - 1;
@@ -139,20 +140,42 @@ adamw_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict
     const AdamwTensor T = tensors[t];
     const uint64_t seg_end = min(end, prefix[t] + T.count);
     const uint64_t base = prefix[t];
-    for (uint64_t e = seg + threadIdx.x; e < seg_end; e += blockDim.x) {
-      const uint64_t i = e - base;
-      const float g = rn_mul(rn_div(T.grad[i], weight), clip);
-      const float m = rn_add(rn_mul(T.beta1, T.exp_avg[i]), rn_mul(T.one_minus_beta1, g));
-      const float v = rn_add(rn_mul(T.beta2, T.exp_avg_sq[i]),
-                             rn_mul(T.one_minus_beta2, rn_mul(g, g)));
-      const float mh = rn_div(m, T.bias1);
-      const float vh = rn_div(v, T.bias2);
-      const float den = rn_add(rn_sqrt(vh), T.epsilon);
-      const float p = rn_sub(rn_mul(T.value[i], T.decay), rn_div(rn_mul(T.lr, mh), den));
-      bad |= !(isfinite(g) && isfinite(m) && isfinite(v) && isfinite(p));
-      T.value[i] = p;
-      T.exp_avg[i] = m;
-      T.exp_avg_sq[i] = v;
+    // kAdamBatch elements per thread per round, their loads issued together
+    for (uint64_t e0 = seg + threadIdx.x; e0 < seg_end; e0 += (uint64_t)kAdamBatch * blockDim.x) {
+      float gr[kAdamBatch], m0[kAdamBatch], v0[kAdamBatch], p0[kAdamBatch];
+#pragma unroll
+      for (int u = 0; u < kAdamBatch; u++) {
+        const uint64_t e = e0 + (uint64_t)u * blockDim.x;
+        const uint64_t i = e - base;
+        const bool in = e < seg_end;
+        gr[u] = in ? T.grad[i] : 0.0f;
+        m0[u] = in ? T.exp_avg[i] : 0.0f;
+        v0[u] = in ? T.exp_avg_sq[i] : 0.0f;
+        p0[u] = in ? T.value[i] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kAdamBatch; u++) {
+        const uint64_t e = e0 + (uint64_t)u * blockDim.x;
+        if (e >= seg_end) continue;
+        const uint64_t i = e - base;
+        const float g = rn_mul(rn_div(gr[u], weight), clip);
+        const float m = rn_add(rn_mul(T.beta1, m0[u]), rn_mul(T.one_minus_beta1, g));
+        const float v = rn_add(rn_mul(T.beta2, v0[u]), rn_mul(T.one_minus_beta2, rn_mul(g, g)));
+        const float mh = rn_div(m, T.bias1);
+        const float vh = rn_div(v, T.bias2);
+        const float den = rn_add(rn_sqrt(vh), T.epsilon);
+        const float p = rn_sub(rn_mul(p0[u], T.decay), rn_div(rn_mul(T.lr, mh), den));
+        bad |= !(isfinite(g) && isfinite(m) && isfinite(v) && isfinite(p));
+        T.value[i] = p;
+        T.exp_avg[i] = m;
+        T.exp_avg_sq[i] = v;
+        if (T.value_hi != nullptr) {
+          float h, l;
+          tf32_split(p, h, l);
+          T.value_hi[i] = h;
+          T.value_lo[i] = l;
+        }
+      }
     }
     seg = seg_end;
   }

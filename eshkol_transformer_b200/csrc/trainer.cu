@@ -479,13 +479,15 @@ void optimizer_step(et_b200_lm* lm) {
   h.lr = lr;
   h.decay = one - lrwd;
   h.epsilon = fbits(c.epsilon_bits);
+  // with 3xTF32 the same pass refreshes the weights' (hi, lo) operand pair
+  h.value_hi = lm->three ? lm->whi : nullptr;
+  h.value_lo = lm->three ? lm->wlo : nullptr;
   cudaMemcpyAsync(lm->d_adam, &h, sizeof(h), cudaMemcpyHostToDevice, lm->stream);
   {
-    Mark mk(lm, P_ADAMW, 0, 28.0 * lm->P);
+    Mark mk(lm, P_ADAMW, 0, (lm->three ? 36.0 : 28.0) * lm->P);
     adamw_multi(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, lm->status, lm->stream);
   }
   lm->updates = t;
-  refresh_weight_split(lm);
 }
 
 int32_t check_ready(et_b200_lm* lm, et_kernel_error* e, const char* op) {
