@@ -26,6 +26,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libet_b200.so"
 PRECISION_TF32X3 = 0
 PRECISION_TF32 = 1
 PRECISION_F32 = 2
+PRECISION_F16X3 = 3  # split-f16 operand pairs (f32-grade, 2x the TF32 tensor rate)
 
 _lib = None
 

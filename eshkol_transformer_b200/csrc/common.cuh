@@ -1,6 +1,7 @@
 // Shared host/device helpers for libet_b200 (sm_100a).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -62,6 +63,53 @@ __device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
   }
   hi = __uint_as_float(b);
   lo = v - hi;
+}
+
+// ---- split-f16 operand pairs ---------------------------------------------
+// A GEMM operand x may be stored as two IEEE binary16 arrays (hi, lo) with
+// x 2^e = hi + lo + r, |r| <= 2^-22 |x 2^e| while x 2^e stays within binary16's
+// normal range: hi = x 2^e rounded to binary16 (11 significant bits) and lo =
+// the rounded remainder (another 11).  e is a per-tensor power-of-two scale
+// read from device memory; the GEMM multiplies its accumulator by
+// 2^-(e_A + e_B), which is exact.  Three tcgen05 kind::f16 products
+// (hi hi + hi lo + lo hi, the split-f16 scheme of Ootomo & Yokota, 2022)
+// then carry the same ~2^-22 operand accuracy as the 3xTF32 scheme at twice
+// its tensor-core rate.
+struct OperandScale {
+  const int* exp;   // e of the output tensor (f16 != 0)
+  unsigned* amax;   // optional: max |x| over the tensor (f32 bits, atomicMax)
+  int f16;          // 1: write a binary16 pair, 0: the TF32 (hi, lo) f32 pair
+};
+// 2^e for e in [-126, 127] (exact).
+__device__ __forceinline__ float exp2_int(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+__device__ __forceinline__ void f16_split(float xs, uint16_t& hi, uint16_t& lo) {
+  const __half h = __float2half_rn(xs);
+  hi = __half_as_ushort(h);
+  lo = __half_as_ushort(__float2half_rn(xs - __half2float(h)));
+}
+// Four consecutive values: x 2^e as binary16 hi / lo quads (8-byte stores).
+__device__ __forceinline__ void f16_store4(uint16_t* hi, uint16_t* lo, int64_t off, float4 x,
+                                           float s) {
+  uint16_t h[4], l[4];
+  f16_split(x.x * s, h[0], l[0]);
+  f16_split(x.y * s, h[1], l[1]);
+  f16_split(x.z * s, h[2], l[2]);
+  f16_split(x.w * s, h[3], l[3]);
+  *reinterpret_cast<uint2*>(hi + off) =
+      make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+  *reinterpret_cast<uint2*>(lo + off) =
+      make_uint2((uint32_t)l[0] | ((uint32_t)l[1] << 16), (uint32_t)l[2] | ((uint32_t)l[3] << 16));
+}
+__device__ __forceinline__ float abs_max4(float m, float4 x) {
+  return fmaxf(fmaxf(m, fmaxf(fabsf(x.x), fabsf(x.y))), fmaxf(fabsf(x.z), fabsf(x.w)));
+}
+// Warp-wide max of m (non-negative, NaN propagating as the largest value)
+// into *slot; every lane of the warp must call it.
+__device__ __forceinline__ void amax_record_warp(unsigned* slot, float m) {
+  unsigned b = (m != m) ? 0x7fffffffu : __float_as_uint(m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+  if ((threadIdx.x & 31) == 0 && slot != nullptr && b != 0u) atomicMax(slot, b);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -164,6 +164,14 @@ struct TcArgs {
   QkvPrep qkv;          // GEMM_EPI_QKV (staged epilogue only)
   AttnGradPrep dprep;   // GEMM_EPI_ATTN_DO (staged epilogue only)
   int* error;
+  // split-f16 operands (pair kernel): binary16 (hi, lo) tiles, 64 k per
+  // 128-byte row, and the accumulator scaled by 2^-(*exp_a + *exp_b)
+  int f16;
+  const int* exp_a;
+  const int* exp_b;
+  // GELU_FWD / GELU_BWD operand-pair outputs: binary16 with this scale, and
+  // their max |x| (either format)
+  OperandScale out_sc;
 };
 
 __device__ __forceinline__ float gelu_value(float v) {  // n2_primitives_provider.c:545-583
@@ -574,6 +582,22 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t a, uint
       "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// binary16 tiles of 64 k (128-byte rows).  K-major: as the f32 tiles, slice j
+// (16 k) at +32j bytes.  MN-major: per 64-wide MN chunk 64 k-rows of 128 B
+// with the 128-byte swizzle; chunks 8 KB apart (LBO), 8-row groups 1 KB apart
+// (SBO), slice j (16 k-rows) at +2 KB j.
+__device__ __forceinline__ uint64_t tile_desc_f16(uint32_t base, int mn_major, int j) {
+  if (mn_major) return sdesc(base + 2048u * j, 8192u, 1024u, 2u);
+  return sdesc(base + 32u * j, 16u, 1024u, 2u);
+}
 // Arrives on `bar_cluster` (either CTA of the pair) once all prior MMAs complete.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -638,7 +662,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int nkb = (args.K + BK - 1) / BK;
+  const bool f16 = args.f16 != 0;
+  const int bke = f16 ? 2 * BK : BK;  // k per 128-byte row of a stage
+  const int nkb = (args.K + bke - 1) / bke;
   const int tiles = args.tiles_m * args.tiles_n;  // tiles_m counts 256-row blocks
   const int units = tiles * args.splits;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
@@ -663,7 +689,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
           const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
           const uint32_t sb = sa + L::A_BYTES;
           const uint32_t fb = full_leader + 8 * stage;
-          const int k0 = kb * BK;
+          const int k0 = kb * bke;
+          // MN-major tiles: one load per 128-byte-wide MN chunk of bke k-rows
+          const int cw = f16 ? 64 : 32;
 #pragma unroll
           for (int op = 0; op < 2; op++) {
             const CUtensorMap* mA = op == 0 ? &ta : &ta_lo;
@@ -671,14 +699,14 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             const uint32_t da = sa + op * (L::A_BYTES + L::B_BYTES);
             const uint32_t db = sb + op * (L::A_BYTES + L::B_BYTES);
             if (args.a_mn) {
-              for (int c = 0; c < TC_BM / 32; c++)
-                tma_load_2d_pair(da + (uint32_t)BK * 128u * c, mA, fb, m0 + 32 * c, k0);
+              for (int c = 0; c < TC_BM / cw; c++)
+                tma_load_2d_pair(da + (uint32_t)bke * 128u * c, mA, fb, m0 + cw * c, k0);
             } else {
               tma_load_2d_pair(da, mA, fb, k0, m0);
             }
             if (args.b_mn) {
-              for (int c = 0; c < (BN / 2) / 32; c++)
-                tma_load_2d_pair(db + (uint32_t)BK * 128u * c, mB, fb, n0 + 32 * c, k0);
+              for (int c = 0; c < (BN / 2) / cw; c++)
+                tma_load_2d_pair(db + (uint32_t)bke * 128u * c, mB, fb, n0 + cw * c, k0);
             } else {
               tma_load_2d_pair(db, mB, fb, k0, n0);
             }
@@ -691,7 +719,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (leader CTA)
-      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)args.a_mn << 15) |
+      // operand format 0 = f16, 2 = tf32 (bits 7-9 A, 10-12 B); f32 accumulator
+      const uint32_t fmt = f16 ? 0u : 2u;
+      const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)args.a_mn << 15) |
                              ((uint32_t)args.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
                              ((uint32_t)((2 * TC_BM) >> 4) << 24);
       const uint32_t peer = 1;
@@ -711,15 +741,28 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
           const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
           const uint32_t sb = sa + L::A_BYTES;
           const uint32_t lo = L::A_BYTES + L::B_BYTES;
+          if (f16) {
 #pragma unroll
-          for (int j = 0; j < BK / 8; j++) {
-            const uint64_t a = tile_desc<BK>(sa, args.a_mn, j);
-            const uint64_t b = tile_desc<BK>(sb, args.b_mn, j);
-            const uint64_t alo = tile_desc<BK>(sa + lo, args.a_mn, j);
-            const uint64_t blo = tile_desc<BK>(sb + lo, args.b_mn, j);
-            umma_tf32_pair(d_tmem, a, b, idesc, (kb > kb_begin || j > 0) ? 1u : 0u);
-            umma_tf32_pair(d_tmem, a, blo, idesc, 1u);
-            umma_tf32_pair(d_tmem, alo, b, idesc, 1u);
+            for (int j = 0; j < 4; j++) {  // 16 k per instruction
+              const uint64_t a = tile_desc_f16(sa, args.a_mn, j);
+              const uint64_t b = tile_desc_f16(sb, args.b_mn, j);
+              const uint64_t alo = tile_desc_f16(sa + lo, args.a_mn, j);
+              const uint64_t blo = tile_desc_f16(sb + lo, args.b_mn, j);
+              umma_f16_pair(d_tmem, a, b, idesc, (kb > kb_begin || j > 0) ? 1u : 0u);
+              umma_f16_pair(d_tmem, a, blo, idesc, 1u);
+              umma_f16_pair(d_tmem, alo, b, idesc, 1u);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < BK / 8; j++) {  // 8 k per instruction
+              const uint64_t a = tile_desc<BK>(sa, args.a_mn, j);
+              const uint64_t b = tile_desc<BK>(sb, args.b_mn, j);
+              const uint64_t alo = tile_desc<BK>(sa + lo, args.a_mn, j);
+              const uint64_t blo = tile_desc<BK>(sb + lo, args.b_mn, j);
+              umma_tf32_pair(d_tmem, a, b, idesc, (kb > kb_begin || j > 0) ? 1u : 0u);
+              umma_tf32_pair(d_tmem, a, blo, idesc, 1u);
+              umma_tf32_pair(d_tmem, alo, b, idesc, 1u);
+            }
           }
           umma_commit_pair(empty0 + 8 * stage);
           umma_commit_pair(map_to_rank(empty0 + 8 * stage, peer));
@@ -740,6 +783,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
     const uint32_t tempty_leader = map_to_rank(tempty0, 0);
     int acc = 0;
     uint32_t acc_phase = 0;
+    // split-f16: accumulator scale 2^-(e_A + e_B); operand-pair output scale
+    const float unscale =
+        f16 ? exp2_int(-((args.exp_a ? *args.exp_a : 0) + (args.exp_b ? *args.exp_b : 0))) : 1.0f;
+    const bool out16 = args.out_sc.f16 != 0;
+    const float out_s = out16 ? exp2_int(*args.out_sc.exp) : 1.0f;
+    float amax = 0.0f;  // max |x| of the operand-pair output this warp wrote
     for (int unit = cluster; unit < units; unit += nclusters) {
       const int tile = unit % tiles, split = unit / tiles;
       int ok = 1;
@@ -801,6 +850,10 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
           }
           float v[32];
           tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c), v);
+          if (f16) {
+#pragma unroll
+            for (int u = 0; u < 32; u++) v[u] *= unscale;
+          }
 #pragma unroll
           for (int u = 0; u < 8; u++)
             sts128(stage + (uint32_t)lane * 128u + (((uint32_t)u ^ (uint32_t)(lane & 7)) << 4),
@@ -841,6 +894,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               d.z = rn_mul(x.z, gelu_slope(u4.z));
               d.w = rn_mul(x.w, gelu_slope(u4.w));
               cs.x += d.x; cs.y += d.y; cs.z += d.z; cs.w += d.w;
+              amax = abs_max4(amax, d);
+              if (out16) {
+                f16_store4(reinterpret_cast<uint16_t*>(cbase), reinterpret_cast<uint16_t*>(args.out2),
+                           off, d, out_s);
+                continue;
+              }
               if (args.out2 != nullptr) {
                 float4 lo;
                 tf32_split(d.x, d.x, lo.x);
@@ -868,6 +927,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             if (epi == GEMM_EPI_GELU_FWD) {
               float4 g = make_float4(gelu_value(x.x), gelu_value(x.y), gelu_value(x.z),
                                      gelu_value(x.w));
+              amax = abs_max4(amax, g);
+              if (out16) {
+                f16_store4(reinterpret_cast<uint16_t*>(args.out2),
+                           reinterpret_cast<uint16_t*>(args.out3), off, g, out_s);
+                continue;
+              }
               if (args.out3 != nullptr) {
                 float4 lo;
                 tf32_split(g.x, g.x, lo.x);
@@ -921,6 +986,10 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       for (int c = col_begin; c < col_begin + BN / 2; c += 32) {
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c), v);
+        if (f16) {  // (the host routes operand-pair outputs to the staged path)
+#pragma unroll
+          for (int u = 0; u < 32; u++) v[u] *= unscale;
+        }
         const int n0 = n_tile + c;
         const bool row_ok = m < args.M;
         const bool full = vec && n0 + 32 <= args.N;
@@ -1011,6 +1080,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       if (lane == 0) mbar_arrive_cluster(tempty_leader + 8 * acc);
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
+    if (args.out_sc.amax != nullptr) amax_record_warp(args.out_sc.amax, amax);
   }
   // After a timeout, give copies still in flight (whose completion this CTA
   // cannot observe when it lands on the peer's barrier) time to land.
@@ -1042,6 +1112,25 @@ bool operand_map(CUtensorMap* map, const float* p, bool kmajor, int rows, int K,
                         bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   return make_map_box(map, p, (uint64_t)rows, (uint64_t)K, ld, 32u, (uint32_t)bk,
                       CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+}
+// binary16 operand map: 64 k (128 bytes) per row.  K-major [rows, K] with box
+// {64 k, tile rows}; MN-major [K, rows] with box {64 mn, 64 k} (one load per
+// 64-wide chunk); both with the 128-byte swizzle.
+bool operand_map_f16(CUtensorMap* map, const void* p, bool kmajor, int rows, int K, int64_t ld,
+                     int tile_rows) {
+  if (kmajor)
+    return make_map_box(map, p, (uint64_t)K, (uint64_t)rows, ld, 64u, (uint32_t)tile_rows,
+                        CU_TENSOR_MAP_SWIZZLE_128B, true);
+  return make_map_box(map, p, (uint64_t)rows, (uint64_t)K, ld, 64u, 64u,
+                      CU_TENSOR_MAP_SWIZZLE_128B, true);
+}
+
+// A split-f16 GEMM the pair kernel cannot take has no other path: report it
+// through the device error word (the model's step then fails loudly).
+void gemm_f16_refused(const GemmArgs& g, const char* why) {
+  fprintf(stderr, "et_b200: split-f16 GEMM %d x %d x %d refused (%s)\n", g.M, g.N, g.K, why);
+  static const int one = 1;
+  cudaMemcpy(device_error_word(), &one, sizeof(int), cudaMemcpyHostToDevice);
 }
 
 // C = (accumulate ? C : 0) + bias + sum over s of partial[s] (s ascending).
@@ -1167,10 +1256,21 @@ template <int BN, int STAGES>
 void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   using L = Tc2Layout<BN, STAGES>;
   CUtensorMap ta, tb, ta_lo, tb_lo;
-  const bool ok = operand_map(&ta, g.A, g.a_kmajor, g.M, g.K, g.lda, TC_BM, L::BK) &&
-                  operand_map(&tb, g.B, g.b_kmajor, g.N, g.K, g.ldb, BN / 2, L::BK) &&
-                  operand_map(&ta_lo, g.A_lo, g.a_kmajor, g.M, g.K, g.lda, TC_BM, L::BK) &&
-                  operand_map(&tb_lo, g.B_lo, g.b_kmajor, g.N, g.K, g.ldb, BN / 2, L::BK);
+  bool ok;
+  if (g.f16)
+    ok = operand_map_f16(&ta, g.A, g.a_kmajor, g.M, g.K, g.lda, TC_BM) &&
+         operand_map_f16(&tb, g.B, g.b_kmajor, g.N, g.K, g.ldb, BN / 2) &&
+         operand_map_f16(&ta_lo, g.A_lo, g.a_kmajor, g.M, g.K, g.lda, TC_BM) &&
+         operand_map_f16(&tb_lo, g.B_lo, g.b_kmajor, g.N, g.K, g.ldb, BN / 2);
+  else
+    ok = operand_map(&ta, g.A, g.a_kmajor, g.M, g.K, g.lda, TC_BM, L::BK) &&
+         operand_map(&tb, g.B, g.b_kmajor, g.N, g.K, g.ldb, BN / 2, L::BK) &&
+         operand_map(&ta_lo, g.A_lo, g.a_kmajor, g.M, g.K, g.lda, TC_BM, L::BK) &&
+         operand_map(&tb_lo, g.B_lo, g.b_kmajor, g.N, g.K, g.ldb, BN / 2, L::BK);
+  if (!ok && g.f16) {
+    gemm_f16_refused(g, "tensor map");
+    return;
+  }
   if (!ok) {
     gemm_simt(g, stream);
     return;
@@ -1192,6 +1292,10 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   a.out2 = g.out2;
   a.out3 = g.out3;
   a.colpart = g.epi_ws;
+  a.f16 = g.f16 ? 1 : 0;
+  a.exp_a = g.exp_a;
+  a.exp_b = g.exp_b;
+  a.out_sc = g.out_sc;
   if (g.epilogue == GEMM_EPI_QKV) a.qkv = *g.qkv;
   if (g.epilogue == GEMM_EPI_ATTN_DO) a.dprep = *g.dprep;
   {
@@ -1202,12 +1306,19 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
       a.staged = a.staged && al(g.dprep->o) && al(g.dprep->o_lo) && al(g.dprep->doh) &&
                  al(g.dprep->dol) && g.dprep->Dh % 32 == 0 && g.N == g.dprep->H * g.dprep->Dh;
   }
+  // split-f16 operand-pair outputs and their max |x| come from the staged epilogue only
+  const bool pair_out = g.epilogue == GEMM_EPI_GELU_FWD || g.epilogue == GEMM_EPI_GELU_BWD;
+  if (!a.staged && pair_out && (g.out_sc.f16 || g.out_sc.amax != nullptr)) {
+    gemm_f16_refused(g, "unstaged epilogue");
+    return;
+  }
+  if (!pair_out) a.out_sc = OperandScale{};
   // the attention operands are written by the staged epilogue only
   const bool prep_after =
       (g.epilogue == GEMM_EPI_QKV || g.epilogue == GEMM_EPI_ATTN_DO) && !a.staged;
   if (prep_after) a.epilogue = GEMM_EPI_PLAIN;
   const int tiles = a.tiles_m * a.tiles_n;
-  const int nkb = (g.K + L::BK - 1) / L::BK;
+  const int nkb = (g.K + (g.f16 ? 2 * L::BK : L::BK) - 1) / (g.f16 ? 2 * L::BK : L::BK);
   const int pairs = sm_count() / 2;
   a.splits = 1;
   a.kb_per_split = nkb;
@@ -1270,6 +1381,13 @@ void epilogue_after(const GemmArgs& g, cudaStream_t stream) {
 
 void gemm(const GemmArgs& g, int precision, cudaStream_t stream) {
   if (g.M <= 0 || g.N <= 0) return;
+  if (g.f16) {  // binary16 pairs exist for the pair kernel only
+    const bool ok = gemm_tc_supported(g) && g.A_lo != nullptr && g.B_lo != nullptr &&
+                    (g.lda % 8) == 0 && (g.ldb % 8) == 0;
+    if (ok) launch_tc2<256, 3>(g, stream);
+    else gemm_f16_refused(g, "operand layout");
+    return;
+  }
   const bool three = precision == ET_B200_PRECISION_TF32X3;
   const bool pair = three && gemm_tc_supported(g) && g.A_lo != nullptr && g.B_lo != nullptr;
   if (pair) {

@@ -113,6 +113,18 @@ void split_tf32(const float* x, float* hi, float* lo, size_t count, cudaStream_t
 void rope_apply(const float* x, float* y, const float* cos_table,
                 const float* sin_table, size_t N, size_t H, size_t T,
                 size_t Dh, int backward, cudaStream_t stream);
+// ---- split-f16 operand pairs (OperandScale in common.cuh)
+// *amax = max(*amax, max |x|) as f32 bits (not reset here).
+void abs_max(const float* x, size_t count, unsigned* amax, cudaStream_t stream);
+// Per slot i: exp[i] = target - k for amax[i] = f 2^k, f in [0.5, 1) (amax
+// 2^exp in [2^(target-1), 2^target)); zero amax keeps exp[i]; nonfinite
+// gives 0; amax cleared when reset.
+void scale_from_amax(unsigned* amax, int* exp, int count, int target, int reset,
+                     cudaStream_t stream);
+// hi / lo binary16 arrays of (x + xlo) 2^(*exp) (xlo optional); the max |x +
+// xlo| goes to amax when it is not null.
+void split_f16(const float* x, const float* xlo, size_t count, uint16_t* hi, uint16_t* lo,
+               const int* exp, unsigned* amax, cudaStream_t stream);
 // status flags: sets *flag = 1 if any of count values is nonfinite.
 void check_finite(const float* x, size_t count, int* flag, cudaStream_t stream);
 
@@ -276,6 +288,14 @@ struct GemmArgs {
   float* epi_ws;
   const QkvPrep* qkv;
   const AttnGradPrep* dprep;
+  // split-f16 operands: A/B (and A_lo/B_lo) hold binary16 arrays scaled by
+  // 2^(*exp_a) / 2^(*exp_b); pair kernel only
+  bool f16;
+  const int* exp_a;
+  const int* exp_b;
+  // format, scale and max-|x| slot of the GELU_FWD (out2/out3) or GELU_BWD
+  // (C/out2) operand-pair output
+  OperandScale out_sc;
 };
 enum {
   GEMM_EPI_PLAIN = 0,

@@ -385,6 +385,66 @@ __global__ void split_tf32_kernel(const float* x, float* hi_out, float* __restri
   }
 }
 
+// max |x| over n values, one atomicMax per warp
+__global__ void abs_max_kernel(const float* __restrict__ x, int64_t n, unsigned* amax) {
+  float m = 0.0f;
+  const int64_t n4 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) ? n >> 2 : 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t i = first; i < n4; i += stride)
+    m = abs_max4(m, __ldg(reinterpret_cast<const float4*>(x) + i));
+  for (int64_t i = 4 * n4 + first; i < n; i += stride) m = fmaxf(m, fabsf(x[i]));
+  amax_record_warp(amax, m);
+}
+
+// exp[i] from amax[i] = f 2^k (f in [0.5, 1)): e = target - k, so that
+// amax 2^e lies in [2^(target-1), 2^target); clamped to [-60, 60].  A zero
+// amax keeps exp[i]; a nonfinite one gives 0.  amax[i] is cleared when reset.
+__global__ void scale_from_amax_kernel(unsigned* amax, int* exp, int count, int target,
+                                       int reset) {
+  for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    const float a = __uint_as_float(amax[i]);
+    if (!isfinite(a)) {
+      exp[i] = 0;
+    } else if (a > 0.0f) {
+      int k;
+      frexpf(a, &k);
+      exp[i] = max(-60, min(60, target - k));
+    }
+    if (reset) amax[i] = 0u;
+  }
+}
+
+// binary16 operand pair of v = x (+ xlo) scaled by 2^(*exp); max |v| to amax
+__global__ void split_f16_kernel(const float* __restrict__ x, const float* __restrict__ xlo,
+                                 int64_t n4, uint16_t* __restrict__ hi, uint16_t* __restrict__ lo,
+                                 const int* __restrict__ exp, unsigned* amax) {
+  const float s = exp2_int(*exp);
+  float m = 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+    if (xlo != nullptr) {
+      const float4 l = __ldg(reinterpret_cast<const float4*>(xlo) + i);
+      v.x += l.x; v.y += l.y; v.z += l.z; v.w += l.w;
+    }
+    m = abs_max4(m, v);
+    f16_store4(hi, lo, 4 * i, v, s);
+  }
+  amax_record_warp(amax, m);
+}
+__global__ void split_f16_tail_kernel(const float* x, const float* xlo, int64_t begin, int64_t n,
+                                      uint16_t* hi, uint16_t* lo, const int* exp, unsigned* amax) {
+  const float s = exp2_int(*exp);
+  float m = 0.0f;
+  for (int64_t i = begin + threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i] + (xlo != nullptr ? xlo[i] : 0.0f);
+    m = fmaxf(m, fabsf(v));
+    f16_split(v * s, hi[i], lo[i]);
+  }
+  amax_record_warp(amax, m);
+}
+
 __global__ void finite_kernel(const float* __restrict__ x, int64_t n, int* flag) {
   bool bad = false;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -606,6 +666,35 @@ void split_tf32(const float* x, float* hi, float* lo, size_t count, cudaStream_t
   if (count == 0) return;
   split_tf32_kernel<<<grid_for(count, 256), 256, 0, stream>>>(x, hi, lo, (int64_t)count);
   count_launch();
+}
+void abs_max(const float* x, size_t count, unsigned* amax, cudaStream_t stream) {
+  if (count == 0) return;
+  abs_max_kernel<<<grid_for((count + 3) / 4, 256), 256, 0, stream>>>(x, (int64_t)count, amax);
+  count_launch();
+}
+void scale_from_amax(unsigned* amax, int* exp, int count, int target, int reset,
+                     cudaStream_t stream) {
+  if (count <= 0) return;
+  scale_from_amax_kernel<<<1, 256, 0, stream>>>(amax, exp, count, target, reset);
+  count_launch();
+}
+void split_f16(const float* x, const float* xlo, size_t count, uint16_t* hi, uint16_t* lo,
+               const int* exp, unsigned* amax, cudaStream_t stream) {
+  if (count == 0) return;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = al(x) && (xlo == nullptr || al(xlo)) &&
+                   (reinterpret_cast<uintptr_t>(hi) & 7) == 0 &&
+                   (reinterpret_cast<uintptr_t>(lo) & 7) == 0;
+  const int64_t n4 = vec ? (int64_t)(count / 4) : 0;
+  if (n4 > 0) {
+    split_f16_kernel<<<grid_for((size_t)n4, 256), 256, 0, stream>>>(x, xlo, n4, hi, lo, exp, amax);
+    count_launch();
+  }
+  if ((size_t)(4 * n4) < count) {
+    split_f16_tail_kernel<<<1, 256, 0, stream>>>(x, xlo, 4 * n4, (int64_t)count, hi, lo, exp,
+                                                 amax);
+    count_launch();
+  }
 }
 void check_finite(const float* x, size_t count, int* flag, cudaStream_t stream) {
   if (count == 0) return;

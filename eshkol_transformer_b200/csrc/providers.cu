@@ -670,19 +670,47 @@ int32_t n2_checks(const et_kernel_call_v1* c, bool n3k, Call& cl, NPlan& pl, et_
   return 0;
 }
 
-// hi/lo split of a device operand into scratch (3xTF32 only).
-void make_pair(const float* x, size_t n, const float** hi, const float** lo) {
+// A GEMM operand as the contraction mode wants it: the tensor itself (TF32,
+// FFMA), its TF32 hi/lo pair (3xTF32), or its binary16 hi/lo pair scaled by
+// 2^exp with exp from the tensor's own max |x| (split-f16; amax 2^exp below
+// 2^15, so no binary16 overflow).
+struct Operand {
+  const float* hi;
+  const float* lo;
+  const int* exp;
+};
+Operand make_pair(const float* x, size_t n, bool f16) {
   Pool& P = pool();
-  if (g_precision != ET_B200_PRECISION_TF32X3) {
-    *hi = x;
-    *lo = nullptr;
-    return;
+  if (f16) {
+    uint16_t* h = (uint16_t*)P.alloc(n * 2);
+    uint16_t* l = (uint16_t*)P.alloc(n * 2);
+    unsigned* amax = (unsigned*)P.alloc(sizeof(unsigned));
+    int* ex = (int*)P.alloc(sizeof(int));
+    cudaMemsetAsync(amax, 0, sizeof(unsigned), P.stream);
+    cudaMemsetAsync(ex, 0, sizeof(int), P.stream);
+    abs_max(x, n, amax, P.stream);
+    scale_from_amax(amax, ex, 1, 15, 0, P.stream);
+    split_f16(x, nullptr, n, h, l, ex, nullptr, P.stream);
+    return Operand{(const float*)h, (const float*)l, ex};
   }
+  if (g_precision != ET_B200_PRECISION_TF32X3 && g_precision != ET_B200_PRECISION_F16X3)
+    return Operand{x, nullptr, nullptr};
   float* h = (float*)P.alloc(n * 4);
   float* l = (float*)P.alloc(n * 4);
   split_tf32(x, h, l, n, P.stream);
-  *hi = h;
-  *lo = l;
+  return Operand{h, l, nullptr};
+}
+// Split-f16 takes the linear ops whose leading dimensions keep binary16 rows
+// 16-byte aligned; the others run 3xTF32.
+int linear_precision(bool f16) {
+  return f16 ? (int)ET_B200_PRECISION_F16X3
+             : (g_precision == ET_B200_PRECISION_F16X3 ? (int)ET_B200_PRECISION_TF32X3
+                                                       : (int)g_precision);
+}
+void set_operands(GemmArgs& g, const Operand& a, const Operand& b) {
+  g.A = a.hi; g.A_lo = a.lo; g.exp_a = a.exp;
+  g.B = b.hi; g.B_lo = b.lo; g.exp_b = b.exp;
+  g.f16 = a.exp != nullptr;
 }
 
 void run_n2(Call& cl, const NPlan& pl, bool scratch, std::vector<void*>& outs) {
@@ -705,36 +733,37 @@ void run_n2(Call& cl, const NPlan& pl, bool scratch, std::vector<void*>& outs) {
     case OP_LIN_F: case OP_LIN_FN: {
       const float *x = (const float*)dev_in(cl, 0), *w = (const float*)dev_in(cl, 1);
       const float* b = pl.kind == OP_LIN_F ? (const float*)dev_in(cl, 2) : nullptr;
-      const float *xh, *xl, *wh, *wl;
-      make_pair(x, rows * d[2], &xh, &xl);
-      make_pair(w, d[3] * d[2], &wh, &wl);
+      const bool f16 = g_precision == ET_B200_PRECISION_F16X3 && d[2] % 8 == 0;
+      const Operand xo = make_pair(x, rows * d[2], f16), wo = make_pair(w, d[3] * d[2], f16);
       GemmArgs g{};
       g.M = (int)rows; g.N = (int)d[3]; g.K = (int)d[2];
-      g.A = xh; g.A_lo = xl; g.lda = d[2]; g.a_kmajor = true;
-      g.B = wh; g.B_lo = wl; g.ldb = d[2]; g.b_kmajor = true;
+      set_operands(g, xo, wo);
+      g.lda = d[2]; g.a_kmajor = true;
+      g.ldb = d[2]; g.b_kmajor = true;
       g.C = (float*)outs[0]; g.ldc = d[3]; g.bias = b; g.accumulate = false;
-      gemm(g, (int)g_precision, s);
+      gemm(g, linear_precision(f16), s);
       break;
     }
     case OP_LIN_B: case OP_LIN_BN: {
       const float *x = (const float*)dev_in(cl, 0), *w = (const float*)dev_in(cl, 1),
                   *dy = (const float*)dev_in(cl, 2);
-      const float *xh, *xl, *wh, *wl, *gh, *gl;
-      make_pair(x, rows * d[2], &xh, &xl);
-      make_pair(w, d[3] * d[2], &wh, &wl);
-      make_pair(dy, rows * d[3], &gh, &gl);
+      const bool f16 = g_precision == ET_B200_PRECISION_F16X3 && d[2] % 8 == 0 && d[3] % 8 == 0;
+      const Operand xo = make_pair(x, rows * d[2], f16), wo = make_pair(w, d[3] * d[2], f16),
+                    go = make_pair(dy, rows * d[3], f16);
       GemmArgs g{};
       g.M = (int)rows; g.N = (int)d[2]; g.K = (int)d[3];
-      g.A = gh; g.A_lo = gl; g.lda = d[3]; g.a_kmajor = true;
-      g.B = wh; g.B_lo = wl; g.ldb = d[2]; g.b_kmajor = false;
+      set_operands(g, go, wo);
+      g.lda = d[3]; g.a_kmajor = true;
+      g.ldb = d[2]; g.b_kmajor = false;
       g.C = (float*)outs[0]; g.ldc = d[2];
-      gemm(g, (int)g_precision, s);
+      gemm(g, linear_precision(f16), s);
       GemmArgs w2{};
       w2.M = (int)d[3]; w2.N = (int)d[2]; w2.K = (int)rows;
-      w2.A = gh; w2.A_lo = gl; w2.lda = d[3]; w2.a_kmajor = false;
-      w2.B = xh; w2.B_lo = xl; w2.ldb = d[2]; w2.b_kmajor = false;
+      set_operands(w2, go, xo);
+      w2.lda = d[3]; w2.a_kmajor = false;
+      w2.ldb = d[2]; w2.b_kmajor = false;
       w2.C = (float*)outs[1]; w2.ldc = d[2];
-      gemm(w2, (int)g_precision, s);
+      gemm(w2, linear_precision(f16), s);
       if (pl.kind == OP_LIN_B) {
         float* ws = (float*)P.alloc(colsum_workspace_floats(rows, d[3]) * 4);
         column_sum(dy, (float*)outs[2], rows, d[3], ws, s);
@@ -982,7 +1011,7 @@ int32_t et_l2_indexed_cross_entropy_abi_minor_v1(void) { return 0; }
 
 // Contraction mode of the K1 matmul / n3k.linear providers (process-wide).
 int32_t et_b200_k1_precision_v1(uint32_t precision) {
-  if (precision > ET_B200_PRECISION_F32) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  if (precision > ET_B200_PRECISION_F16X3) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
   g_precision = precision;
   return 0;
 }

@@ -228,17 +228,20 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 2-D f32 tensor map over a row-major [outer, inner] array with row stride
 // `ld` elements; box {box_inner, box_outer}, zero OOB fill.  The swizzle must
 // match the descriptor layout the MMA reads the tile with.
-inline bool make_map_box(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+// 2-D tensor map over f32 elements, or binary16 ones with f16 = true (ld in
+// elements either way).
+inline bool make_map_box(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                          int64_t ld, uint32_t box_inner, uint32_t box_outer,
-                         CUtensorMapSwizzle swizzle) {
+                         CUtensorMapSwizzle swizzle, bool f16 = false) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * (f16 ? 2 : 4)};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 // Box {32, box_outer}: one 128-byte row of f32 per box row.

@@ -164,7 +164,10 @@ uint32_t et_b200_o2_schedule_factor_v1(uint32_t kind, uint64_t warmup,
 enum {
   ET_B200_PRECISION_TF32X3 = 0, /* 3xTF32 tcgen05 contractions (f32-grade) */
   ET_B200_PRECISION_TF32 = 1,   /* single TF32 tcgen05 contractions        */
-  ET_B200_PRECISION_F32 = 2     /* FP32 FFMA contractions (no tensor core)  */
+  ET_B200_PRECISION_F32 = 2,    /* FP32 FFMA contractions (no tensor core)  */
+  ET_B200_PRECISION_F16X3 = 3   /* split-f16 tcgen05 contractions: binary16
+                                   hi/lo pairs with per-tensor power-of-two
+                                   scales, 3 products (f32-grade)           */
 };
 
 typedef struct et_b200_lm_config_v1 {

@@ -146,11 +146,15 @@ def test_attention_vs_oracle(lib, cuda, shape, masked):
 
 # Normwise bounds against the serial-f32 oracle, whose own rounding error is
 # ~sqrt(K) 2^-24 of the row norm: FFMA 2e-6; 3xTF32 (drops lo*lo and the
-# TF32 rounding of lo: ~2^-22 per product) 1e-5; single TF32 (2^-11) 2e-3.
-LINEAR_TOL = {etb.PRECISION_TF32X3: 1e-5, etb.PRECISION_TF32: 2e-3, etb.PRECISION_F32: 2e-6}
+# TF32 rounding of lo: ~2^-22 per product) 1e-5; split-f16 (binary16 hi/lo
+# pairs, 11 + 11 bits, lo*lo dropped: the same ~2^-22) 1e-5; single TF32
+# (2^-11) 2e-3.
+LINEAR_TOL = {etb.PRECISION_TF32X3: 1e-5, etb.PRECISION_F16X3: 1e-5, etb.PRECISION_TF32: 2e-3,
+              etb.PRECISION_F32: 2e-6}
 
 
-@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_TF32, etb.PRECISION_F32])
+@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F16X3,
+                                       etb.PRECISION_TF32, etb.PRECISION_F32])
 @pytest.mark.parametrize("n,t,din,dout", [(2, 64, 128, 384), (1, 300, 256, 96), (3, 50, 100, 70),
                                           (8, 64, 512, 1024)])
 def test_linear_all_layouts_vs_oracle(lib, cuda, precision, n, t, din, dout):
@@ -173,6 +177,31 @@ def test_linear_all_layouts_vs_oracle(lib, cuda, precision, n, t, din, dout):
     assert_close_norm(dx, dx_r, tol, "dx")
     assert_close_norm(dw, dw_r, tol, "dw")
     assert_close_norm(db, db_r, 2e-6, "db")
+
+
+@pytest.mark.parametrize("sx,sw,sg", [(1e4, 1e-3, 1e-7), (1e-5, 30.0, 2e3)])
+def test_linear_split_f16_scaled_operands(lib, cuda, sx, sw, sg):
+    """Split-f16 operands far from binary16's range: each tensor's power-of-two
+    scale brings it into range, and the accumulator is scaled back exactly."""
+    n, t, din, dout = 2, 96, 256, 192
+    x = orc.fill_normal(8, 1, n * t * din).reshape(n, t, din) * np.float32(sx)
+    w = orc.fill_normal(8, 2, dout * din).reshape(dout, din) * np.float32(sw)
+    b = orc.fill_normal(8, 3, dout)
+    dy = orc.fill_normal(8, 4, n * t * dout).reshape(n, t, dout) * np.float32(sg)
+    shape = (n, t, din, dout)
+    lib.et_b200_k1_precision_v1(etb.PRECISION_F16X3)
+    try:
+        (y,) = run_call(lib, "kernel.matmul", "linear.forward", shape, [x, w, b], [(n, t, dout)],
+                        "cuda")
+        dx, dw, _ = run_call(lib, "kernel.matmul", "linear.backward", shape, [x, w, dy],
+                             [(n, t, din), (dout, din), (dout,)], "cuda")
+    finally:
+        lib.et_b200_k1_precision_v1(etb.PRECISION_TF32X3)
+    tol = LINEAR_TOL[etb.PRECISION_F16X3]
+    assert_close_norm(y, orc.linear_forward(x, w, b), tol, "y")
+    dx_r, dw_r, _ = orc.linear_backward(x, w, dy)
+    assert_close_norm(dx, dx_r, tol, "dx")
+    assert_close_norm(dw, dw_r, tol, "dw")
 
 
 def test_n3k_linear_no_bias(lib, cuda):
