@@ -109,19 +109,22 @@ GEMM_DRAM_MB_PER_GFLOP = (109.7 + 171.7) / (2 * 34.36)
 
 
 def roofline_entry(gemm: dict, gemm_tflops: float, peak_t: float, peaks: dict,
-                   clocks: dict) -> dict:
+                   clocks: dict, f16: bool) -> dict:
     """The dominant kernel class (every linear GEMM of the timed steps).
 
     achieved = algorithmic 2*M*N*K FLOP / CUDA-event time; peak = the measured
-    bf16 sustained rate.  3xTF32 issues three TF32 MMAs per algorithmic FMA and
-    TF32 runs at half the bf16 rate, so the tensor work is 3x `achieved` and
-    its own ceiling is 4,096 FLOP/clk/SM at the clock the SMs ran.
+    bf16 sustained rate.  Both f32-grade modes issue three tensor-core MMAs per
+    algorithmic FMA: split-f16 (binary16 hi/lo pairs, kind::f16) at the
+    bf16/f16 rate, whose ceiling is 8,192 FLOP/clk/SM at the clock the SMs ran,
+    and 3xTF32 (kind::tf32) at half of it (4,096).
     """
     per_launch_flop = gemm["flop"] / max(gemm["launches"], 1)
     sm_mhz = clocks.get("sm_mhz")
-    ceiling = 4096 * 148 * sm_mhz * 1e6 / 1e12 if sm_mhz else None
+    per_clk = 8192 if f16 else 4096
+    ceiling = per_clk * 148 * sm_mhz * 1e6 / 1e12 if sm_mhz else None
+    kind = "kind::f16, split-f16 pairs" if f16 else "kind::tf32"
     return {
-        "bound": "tensor", "kernel": "linear GEMM (tcgen05.mma.cta_group::2 kind::tf32, 3 passes)",
+        "bound": "tensor", "kernel": f"linear GEMM (tcgen05.mma.cta_group::2 {kind}, 3 passes)",
         "achieved": round(gemm_tflops, 2), "peak": peak_t, "unit": "TFLOP/s",
         "frac": round(gemm_tflops / peak_t, 4) if peak_t else None,
         "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
@@ -129,8 +132,8 @@ def roofline_entry(gemm: dict, gemm_tflops: float, peak_t: float, peaks: dict,
         "tensor_mma_per_algorithmic_flop": 3,
         "tensor_issue_tflops": round(3 * gemm_tflops, 1),
         "frac_tensor_issue_of_measured_bf16": round(3 * gemm_tflops / peak_t, 4) if peak_t else None,
-        "tf32_ceiling_at_median_clock_tflops": round(ceiling, 1) if ceiling else None,
-        "frac_of_tf32_ceiling_at_clock": round(3 * gemm_tflops / ceiling, 4) if ceiling else None,
+        "mma_ceiling_at_median_clock_tflops": round(ceiling, 1) if ceiling else None,
+        "frac_of_mma_ceiling_at_clock": round(3 * gemm_tflops / ceiling, 4) if ceiling else None,
         "flop_per_launch": per_launch_flop,
         "avg_launch_ms": gemm["ms"] / max(gemm["launches"], 1),
         "traffic": round(per_launch_flop / 1e9 * GEMM_DRAM_MB_PER_GFLOP * 1e6),
@@ -160,7 +163,9 @@ def run_b200(args) -> None:
     shape = etb.ModelShape(batch=batch, **SHAPE)
     tokens_rank = batch * shape.seq_len
     global_tokens = GLOBAL_BATCH * shape.seq_len
-    model = etb.LanguageModel(shape, precision=etb.PRECISION_TF32X3, global_tokens=global_tokens)
+    f16 = args.contractions == "f16x3"
+    precision = etb.PRECISION_F16X3 if f16 else etb.PRECISION_TF32X3
+    model = etb.LanguageModel(shape, precision=precision, global_tokens=global_tokens)
     model.init(20261201)
     if world > 1:
         uid = [etb.nccl_unique_id() if rank == 0 else None]
@@ -241,10 +246,13 @@ def run_b200(args) -> None:
         "data": "synthetic uniform tokens (seeded), N(0,0.02) random-init weights",
         "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH,
                    "seq_len": shape.seq_len, "tokens_per_step": global_tokens,
-                   "contractions": "3xTF32 tcgen05", "parallelism": f"dp{world}",
+                   "contractions": ("split-f16 tcgen05 (binary16 hi/lo pairs with per-tensor "
+                                    "power-of-two scales, 3 products; f32-grade)" if f16
+                                    else "3xTF32 tcgen05 (f32-grade)"),
+                   "parallelism": f"dp{world}",
                    "l2": "activations (GBs per step) exceed the 126 MB L2; no flush needed"},
         "gpu_launches": launches,
-        "roofline": roofline_entry(gemm, gemm_tflops, peak_t, peaks, clocks.summary()),
+        "roofline": roofline_entry(gemm, gemm_tflops, peak_t, peaks, clocks.summary(), f16),
         "attention_backward": {"achieved_tflops": round(attn_tflops, 2),
                                "ms_per_step": round(attn_b["ms"] / args.steps, 3)},
         "profile_ms_per_step": {k: round(v["ms"] / args.steps, 3) for k, v in prof.items()},
@@ -408,6 +416,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--contractions", default="f16x3", choices=["f16x3", "tf32x3"],
+                    help="f32-grade contraction scheme of the linear GEMMs (split-f16 pairs or "
+                         "3xTF32)")
     ap.add_argument("--profile-case", action="store_true",
                     help="small case of the same kernels for ncu captures (2 layers, global "
                          "batch 4 = 4096 tokens; a few GB on the device); not a bench value")

@@ -13,11 +13,13 @@ namespace etb {
 // upstream is null).  dlogits may alias logits.  status[0] is set to 1 when a
 // target is outside [0, V).
 // With dlogits_lo, dlogits receives the TF32 hi part and dlogits_lo the
-// residual (the 3xTF32 operand pair) instead of the f32 gradient.
+// residual (the 3xTF32 operand pair) instead of the f32 gradient; with
+// sc.f16 the binary16 pair of the gradient 2^(*sc.exp) (dlogits must not
+// alias logits then); sc.amax receives max |gradient|.
 void ce_fused(const float* logits, float* dlogits, const int64_t* targets,
               const float* upstream, float upstream_scale, float* loss,
               size_t rows, size_t V, int* status, cudaStream_t stream,
-              float* dlogits_lo = nullptr);
+              float* dlogits_lo = nullptr, OperandScale sc = OperandScale{});
 // Mean of loss[rows] as one f32 (fixed-order tree in f64).
 void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream);
 
@@ -32,17 +34,20 @@ struct AdamwTensor {
   float beta1, beta2, one_minus_beta1, one_minus_beta2, bias1, bias2, lr,
       decay, epsilon;
   // optional: the updated value's TF32 hi / residual lo pair (the weight
-  // operands of the 3xTF32 GEMMs), written in the same pass
+  // operands of the 3xTF32 GEMMs), written in the same pass; with value_sc.f16
+  // the binary16 pair of value 2^(*value_sc.exp) instead (uint16 arrays)
   float* value_hi;
   float* value_lo;
+  OperandScale value_sc;
 };
 // One fused pass over every tensor of the table (device array `tensors`,
 // `prefix[i]` = first global element of tensor i, total = prefix[count]).
 // weight/clip divide and scale gradients as o2_optimizer.c:1738 does.
-// status[1] is set when any staged value is nonfinite.
+// status[1] is set when any staged value is nonfinite.  With `skip` and
+// *skip != 0 nothing is updated and status[2] counts the skipped step.
 void adamw_multi(const AdamwTensor* tensors, const uint64_t* prefix,
                  int tensor_count, uint64_t total, float weight, float clip,
-                 int* status, cudaStream_t stream);
+                 int* status, cudaStream_t stream, const float* skip = nullptr);
 // Sum of squares of grad/weight over the table, in f64, plus status[0] = 1 on
 // any nonfinite gradient.  out_sumsq receives one double.
 void grad_sumsq(const AdamwTensor* tensors, const uint64_t* prefix,
@@ -51,21 +56,25 @@ void grad_sumsq(const AdamwTensor* tensors, const uint64_t* prefix,
                 int* status, cudaStream_t stream);
 
 // ---------------------------------------------------------------- N2 family
-// With y_lo, y receives the TF32 hi part of the output and y_lo the residual.
+// With y_lo, y receives the TF32 hi part of the output and y_lo the residual;
+// with sc.f16 the binary16 pair (y as hi, y_lo as lo, both uint16 arrays) of
+// y 2^(*sc.exp); sc.amax (either format) receives max |y|.
 void layer_norm_forward(const float* x, const float* gamma, const float* beta,
                         float epsilon, float* y, float* mean, float* rstd,
-                        size_t rows, size_t d, cudaStream_t stream, float* y_lo = nullptr);
+                        size_t rows, size_t d, cudaStream_t stream, float* y_lo = nullptr,
+                        OperandScale sc = OperandScale{});
 // dx = (accumulate ? dx : 0) + LN'(dy); dgamma/dbeta over all rows via a
 // fixed-order two-stage column reduction in `workspace` (>= ln_workspace()).
 size_t ln_workspace_floats(size_t rows, size_t d);
-// With dx_hi/dx_lo, the final dx is also written as a 3xTF32 operand pair;
-// with dsum, the column sums of the final dx (the next bias gradient) too.
+// With dx_hi/dx_lo, the final dx is also written as a 3xTF32 operand pair (or
+// with sc.f16 as the binary16 pair of dx 2^(*sc.exp); d % 128 == 0, d <= 1024
+// only); with dsum, the column sums of the final dx (the next bias gradient).
 void layer_norm_backward(const float* x, const float* gamma, const float* mean,
                          const float* rstd, const float* dy, float* dx,
                          int accumulate, float* dgamma, float* dbeta,
                          float* workspace, size_t rows, size_t d,
                          cudaStream_t stream, float* dx_hi = nullptr, float* dx_lo = nullptr,
-                         float* dsum = nullptr);
+                         float* dsum = nullptr, OperandScale sc = OperandScale{});
 // With a lo output, the result is written as TF32 hi (y / dx) plus residual.
 void gelu_forward(const float* x, float* y, size_t count, cudaStream_t stream,
                   float* y_lo = nullptr);
@@ -125,6 +134,10 @@ void scale_from_amax(unsigned* amax, int* exp, int count, int target, int reset,
 // xlo| goes to amax when it is not null.
 void split_f16(const float* x, const float* xlo, size_t count, uint16_t* hi, uint16_t* lo,
                const int* exp, unsigned* amax, cudaStream_t stream);
+// flag[0] = 1.0 when some slot's amax 2^exp is not below 65504 (a binary16
+// overflow) or NaN, else 0.0; then clears amax[reset_slot] (if >= 0).
+void operand_range_check(unsigned* amax, const int* exp, int count, int reset_slot, float* flag,
+                         cudaStream_t stream);
 // status flags: sets *flag = 1 if any of count values is nonfinite.
 void check_finite(const float* x, size_t count, int* flag, cudaStream_t stream);
 

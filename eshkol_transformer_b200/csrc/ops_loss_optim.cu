@@ -33,7 +33,8 @@ __global__ void __launch_bounds__(kCeThreads)
 ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
                 const int64_t* __restrict__ targets,
                 const float* __restrict__ upstream, float upstream_scale,
-                float* __restrict__ loss, int64_t V, int* status, float* __restrict__ dlo) {
+                float* __restrict__ loss, int64_t V, int* status, float* __restrict__ dlo,
+                OperandScale sc) {
   __shared__ float red_m[32];
   __shared__ float red_s[32];
   const int64_t row = blockIdx.x;
@@ -69,6 +70,11 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
   if (dlogits == nullptr) return;
   const float u = upstream != nullptr ? upstream[row] : upstream_scale;
   float* g = dlogits + row * V;
+  // split-f16: dlogits / dlo hold binary16 hi / lo of the gradient 2^e
+  const float s16 = sc.f16 ? exp2_int(*sc.exp) : 1.0f;
+  uint16_t* gh = reinterpret_cast<uint16_t*>(dlogits) + row * V;
+  uint16_t* gl = reinterpret_cast<uint16_t*>(dlo) + row * V;
+  float amax = 0.0f;
   if (vec) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     float4* g4 = reinterpret_cast<float4*>(g);
@@ -81,6 +87,11 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
       r.y = u * (rn_div(expf(v.y - row_max), row_sum) - (j + 1 == target ? 1.0f : 0.0f));
       r.z = u * (rn_div(expf(v.z - row_max), row_sum) - (j + 2 == target ? 1.0f : 0.0f));
       r.w = u * (rn_div(expf(v.w - row_max), row_sum) - (j + 3 == target ? 1.0f : 0.0f));
+      amax = abs_max4(amax, r);
+      if (sc.f16) {
+        f16_store4(gh, gl, j, r, s16);
+        continue;
+      }
       if (dlo != nullptr) {
         float4 l;
         tf32_split(r.x, r.x, l.x);
@@ -95,10 +106,16 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
     for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
       const float v = x[j];
       float r = u * (rn_div(expf(v - row_max), row_sum) - (j == target ? 1.0f : 0.0f));
+      amax = fmaxf(amax, fabsf(r));
+      if (sc.f16) {
+        f16_split(r * s16, gh[j], gl[j]);
+        continue;
+      }
       if (dlo != nullptr) tf32_split(r, r, dlo[row * V + j]);
       g[j] = r;
     }
   }
+  if (sc.amax != nullptr) amax_record_warp(sc.amax, amax);
 }
 
 __global__ void mean_loss_kernel(const float* __restrict__ loss, int64_t rows,
@@ -128,9 +145,15 @@ __device__ __forceinline__ int find_tensor(const uint64_t* prefix, int count, ui
 
 __global__ void __launch_bounds__(kAdamThreads)
 adamw_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict__ prefix,
-             int tensor_count, uint64_t total, float weight, float clip, int* status) {
+             int tensor_count, uint64_t total, float weight, float clip, int* status,
+             const float* skip) {
   const uint64_t begin = (uint64_t)blockIdx.x * kAdamChunk;
   if (begin >= total) return;
+  if (skip != nullptr && *skip != 0.0f) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(status + 2, 1);
+    return;
+  }
+  float amax = 0.0f;  // max |value| of the tensors that record it
   const uint64_t end = min(total, begin + (uint64_t)kAdamChunk);
   int t = find_tensor(prefix, tensor_count, begin);
   bool bad = false;
@@ -169,7 +192,11 @@ adamw_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict
         T.value[i] = p;
         T.exp_avg[i] = m;
         T.exp_avg_sq[i] = v;
-        if (T.value_hi != nullptr) {
+        if (T.value_sc.f16) {
+          amax = fmaxf(amax, fabsf(p));
+          f16_split(p * exp2_int(*T.value_sc.exp), reinterpret_cast<uint16_t*>(T.value_hi)[i],
+                    reinterpret_cast<uint16_t*>(T.value_lo)[i]);
+        } else if (T.value_hi != nullptr) {
           float h, l;
           tf32_split(p, h, l);
           T.value_hi[i] = h;
@@ -179,6 +206,8 @@ adamw_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict
     }
     seg = seg_end;
   }
+  // (a single max slot per launch: the first tensor's)
+  if (tensors[0].value_sc.amax != nullptr) amax_record_warp(tensors[0].value_sc.amax, amax);
   if (bad) atomicExch(status + 1, 1);
 }
 
@@ -222,11 +251,13 @@ __global__ void sum_partials_kernel(const double* partials, int count, double* o
 
 void ce_fused(const float* logits, float* dlogits, const int64_t* targets,
               const float* upstream, float upstream_scale, float* loss,
-              size_t rows, size_t V, int* status, cudaStream_t stream, float* dlogits_lo) {
+              size_t rows, size_t V, int* status, cudaStream_t stream, float* dlogits_lo,
+              OperandScale sc) {
   if (rows == 0) return;
+  if (dlogits == nullptr) sc = OperandScale{};
   ce_fused_kernel<<<(unsigned)rows, kCeThreads, 0, stream>>>(
       logits, dlogits, targets, upstream, upstream_scale, loss, (int64_t)V, status,
-      dlogits ? dlogits_lo : nullptr);
+      dlogits ? dlogits_lo : nullptr, sc);
   count_launch();
 }
 
@@ -236,11 +267,12 @@ void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream) 
 }
 
 void adamw_multi(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_count,
-                 uint64_t total, float weight, float clip, int* status, cudaStream_t stream) {
+                 uint64_t total, float weight, float clip, int* status, cudaStream_t stream,
+                 const float* skip) {
   if (total == 0) return;
   const unsigned blocks = (unsigned)((total + kAdamChunk - 1) / kAdamChunk);
   adamw_kernel<<<blocks, kAdamThreads, 0, stream>>>(tensors, prefix, tensor_count, total,
-                                                    weight, clip, status);
+                                                    weight, clip, status, skip);
   count_launch();
 }
 

@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(kLnWarps * 32)
 ln_forward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                   const float* __restrict__ beta, float epsilon, float* __restrict__ y,
                   float* __restrict__ mean_out, float* __restrict__ rstd_out,
-                  int64_t rows, int64_t d, float* __restrict__ y_lo) {
+                  int64_t rows, int64_t d, float* __restrict__ y_lo, OperandScale sc) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -43,12 +43,23 @@ ln_forward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
   const float variance = rn_div(v, dim);
   const float rstd = rn_div(1.0f, rn_sqrt(rn_add(variance, epsilon)));
   float* yr = y + row * d;
+  // split-f16: y and y_lo hold binary16 hi / lo of y 2^e
+  const float s16 = sc.f16 ? exp2_int(*sc.exp) : 1.0f;
+  uint16_t* yh = reinterpret_cast<uint16_t*>(y) + row * d;
+  uint16_t* yl = reinterpret_cast<uint16_t*>(y_lo) + row * d;
+  float amax = 0.0f;
   for (int64_t j = lane; j < d; j += 32) {
     const float normalized = rn_mul(rn_sub(xr[j], mean), rstd);
     float val = rn_add(rn_mul(normalized, gamma[j]), beta[j]);
+    amax = fmaxf(amax, fabsf(val));
+    if (sc.f16) {
+      f16_split(val * s16, yh[j], yl[j]);
+      continue;
+    }
     if (y_lo != nullptr) tf32_split(val, val, y_lo[row * d + j]);
     yr[j] = val;
   }
+  if (sc.amax != nullptr) amax_record_warp(sc.amax, amax);
   if (lane == 0) {
     if (mean_out) mean_out[row] = mean;
     if (rstd_out) rstd_out[row] = rstd;
@@ -135,8 +146,11 @@ ln_backward_rows_kernel(const float* __restrict__ x, const float* __restrict__ g
                         const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                         const float* __restrict__ dy, float* __restrict__ dx, int accumulate,
                         float* __restrict__ dx_hi, float* __restrict__ dx_lo,
-                        float* __restrict__ partial, int with_sum, int64_t rows) {
+                        float* __restrict__ partial, int with_sum, int64_t rows,
+                        OperandScale sc) {
   constexpr int D = 128 * NV;
+  const float s16 = sc.f16 ? exp2_int(*sc.exp) : 1.0f;
+  float amax = 0.0f;
   extern __shared__ float4 lnb_acc[];  // [kLnbWarps][3][32 NV] partials, then gamma [32 NV]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float4* acc = lnb_acc + warp * 3 * 32 * NV;
@@ -207,7 +221,11 @@ ln_backward_rows_kernel(const float* __restrict__ x, const float* __restrict__ g
         as.x += out.x; as.y += out.y; as.z += out.z; as.w += out.w;
         acc[64 * NV + lane + 32 * i] = as;
       }
-      if (dx_lo != nullptr) {
+      amax = abs_max4(amax, out);
+      if (sc.f16) {  // dx_hi / dx_lo hold binary16 hi / lo of dx 2^e
+        f16_store4(reinterpret_cast<uint16_t*>(dx_hi), reinterpret_cast<uint16_t*>(dx_lo),
+                   row * D + 4 * (lane + 32 * i), out, s16);
+      } else if (dx_lo != nullptr) {
         float4 h4, l4;
         tf32_split(out.x, h4.x, l4.x);
         tf32_split(out.y, h4.y, l4.y);
@@ -218,6 +236,7 @@ ln_backward_rows_kernel(const float* __restrict__ x, const float* __restrict__ g
       }
     }
   }
+  if (sc.amax != nullptr) amax_record_warp(sc.amax, amax);
   // the block's partial row per quantity: the warps' sums added in warp order
   __syncthreads();
   const int nq = with_sum ? 3 : 2;
@@ -445,6 +464,22 @@ __global__ void split_f16_tail_kernel(const float* x, const float* xlo, int64_t 
   amax_record_warp(amax, m);
 }
 
+// flag[0] = 1 when any slot's amax 2^exp reached binary16's largest finite
+// value 65504 (or is NaN), else 0; amax[reset_slot] is then cleared.
+__global__ void operand_range_kernel(unsigned* amax, const int* exp, int count, int reset_slot,
+                                     float* flag) {
+  bool bad = false;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    const float v = __uint_as_float(amax[i]) * exp2_int(exp[i]);
+    bad |= !(v < 65504.0f);
+  }
+  bad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    flag[0] = bad ? 1.0f : 0.0f;
+    if (reset_slot >= 0) amax[reset_slot] = 0u;
+  }
+}
+
 __global__ void finite_kernel(const float* __restrict__ x, int64_t n, int* flag) {
   bool bad = false;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -578,10 +613,10 @@ void reduce_partials(const float* partial, int count, int64_t width, int64_t str
 
 void layer_norm_forward(const float* x, const float* gamma, const float* beta, float epsilon,
                         float* y, float* mean, float* rstd, size_t rows, size_t d,
-                        cudaStream_t stream, float* y_lo) {
+                        cudaStream_t stream, float* y_lo, OperandScale sc) {
   if (rows == 0) return;
   ln_forward_kernel<<<ceil_div(rows, kLnWarps), kLnWarps * 32, 0, stream>>>(
-      x, gamma, beta, epsilon, y, mean, rstd, (int64_t)rows, (int64_t)d, y_lo);
+      x, gamma, beta, epsilon, y, mean, rstd, (int64_t)rows, (int64_t)d, y_lo, sc);
   count_launch();
 }
 
@@ -595,7 +630,7 @@ size_t ln_workspace_floats(size_t rows, size_t d) {
 void layer_norm_backward(const float* x, const float* gamma, const float* mean, const float* rstd,
                          const float* dy, float* dx, int accumulate, float* dgamma, float* dbeta,
                          float* workspace, size_t rows, size_t d, cudaStream_t stream,
-                         float* dx_hi, float* dx_lo, float* dsum) {
+                         float* dx_hi, float* dx_lo, float* dsum, OperandScale sc) {
   if (rows == 0) return;
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
                          reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(gamma) |
@@ -614,7 +649,8 @@ void layer_norm_backward(const float* x, const float* gamma, const float* mean, 
       cudaFuncSetAttribute(ln_backward_rows_kernel<nv>,                                       \
                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                \
     ln_backward_rows_kernel<nv><<<blocks, kLnbWarps * 32, smem, stream>>>(                    \
-        x, gamma, mean, rstd, dy, dx, accumulate, hi, dx_lo, workspace, with_sum, (int64_t)rows); \
+        x, gamma, mean, rstd, dy, dx, accumulate, hi, dx_lo, workspace, with_sum, (int64_t)rows, \
+        sc);                                                                                  \
     break;                                                                                    \
   }
       LNB_CASE(1) LNB_CASE(2) LNB_CASE(3) LNB_CASE(4) LNB_CASE(5) LNB_CASE(6) LNB_CASE(7)
@@ -623,6 +659,12 @@ void layer_norm_backward(const float* x, const float* gamma, const float* mean, 
     }
     count_launch();
     reduce_partials(workspace, blocks, (int64_t)d, (int64_t)nq * d, dgamma, dbeta, dsum, stream);
+    return;
+  }
+  if (sc.f16 || sc.amax != nullptr) {  // operand scales exist on the register-row path only
+    fprintf(stderr, "et_b200: LayerNorm backward with d = %zu has no split-f16 output\n", d);
+    static const int one = 1;
+    cudaMemcpy(device_error_word(), &one, sizeof(int), cudaMemcpyHostToDevice);
     return;
   }
   const int blocks = ln_backward_blocks(rows);
@@ -695,6 +737,11 @@ void split_f16(const float* x, const float* xlo, size_t count, uint16_t* hi, uin
                                                  amax);
     count_launch();
   }
+}
+void operand_range_check(unsigned* amax, const int* exp, int count, int reset_slot, float* flag,
+                         cudaStream_t stream) {
+  operand_range_kernel<<<1, 256, 0, stream>>>(amax, exp, count, reset_slot, flag);
+  count_launch();
 }
 void check_finite(const float* x, size_t count, int* flag, cudaStream_t stream) {
   if (count == 0) return;

@@ -18,6 +18,16 @@
 // 3xTF32 mode every GEMM operand is kept as a (hi, lo) pair: producers' outputs
 // are split once, weights after every update.
 //
+// Split-f16 mode (ET_B200_PRECISION_F16X3): the operand pairs are binary16
+// (hi, lo) arrays of x 2^e with one power-of-two exponent e per operand
+// tensor ("slot"), taken from the tensor's max |x| in the previous step so
+// that it sits near 2^10, 64x below binary16's overflow (delayed scaling).
+// Producers write the pairs and record the new max in the same pass.  The
+// first step, and any step in which some operand reached the overflow, runs
+// 3xTF32 instead (recording every slot's max); a step whose check fails is
+// not applied (AdamW skips on a flag that the data-parallel reduction sums
+// across ranks) and the host-synchronised entry points redo it in 3xTF32.
+//
 // Data parallelism: each rank runs its own batch; after a layer's backward its
 // contiguous gradient slice is summed across ranks by ncclAllReduce on a side
 // stream while the next layer's backward runs; AdamW waits for the last bucket.
@@ -35,6 +45,10 @@ using namespace etb;
 namespace {
 
 enum { kPerLayer = 12 };
+// split-f16 operand slots of one layer
+enum { S_H1 = 0, S_AO, S_H2, S_G, S_DXF, S_DU, S_DXA, S_DQKV, kSlotsPerLayer };
+// a slot's max |x| 2^e lands in [2^(target-1), 2^target)
+constexpr int kScaleTarget = 10;
 enum {
   T_LN1G = 0, T_LN1B, T_WQKV, T_BQKV, T_WO, T_BO, T_LN2G, T_LN2B, T_W1, T_B1, T_W2, T_B2
 };
@@ -50,6 +64,7 @@ struct LayerActs {
   float *qkv = nullptr, *ao = nullptr, *aolo = nullptr, *am = nullptr, *al = nullptr;
   float *xmid = nullptr, *h2 = nullptr, *h2lo = nullptr, *mu2 = nullptr, *rs2 = nullptr;
   float *u = nullptr, *g = nullptr, *glo = nullptr;
+  float* ao16 = nullptr;  // split-f16: binary16 hi then lo of the attention output
 };
 
 struct ProfileMark {
@@ -67,7 +82,15 @@ struct et_b200_lm {
   int64_t L = 0, d = 0, H = 0, Dh = 0, F = 0, V = 0, T = 0, B = 0, R = 0;
   float ce_scale = 0, eps = 0, attn_scale = 0;
   int precision = 0;
-  bool three = false;
+  bool three = false;  // (hi, lo) operand pairs (3xTF32 or split-f16)
+  int gprec = 0;       // contraction mode of the GEMMs without binary16 operands
+  // split-f16: model mode, scales measured, this step's operand format, and
+  // whether whi / wlo hold the weights' binary16 pair
+  bool f16 = false, calibrated = false, step16 = false, w16_valid = false;
+  int nslots = 0;
+  int* sexp = nullptr;        // per slot exponent e
+  unsigned* samax = nullptr;  // per slot max |x| (f32 bits)
+  float* dqkv16 = nullptr;    // binary16 hi then lo of dqkv
   // parameters (flat, tensor order as documented in et_b200.h)
   size_t P = 0;
   std::vector<size_t> off, sz;
@@ -110,8 +133,19 @@ struct et_b200_lm {
   size_t mark_used = 0;
   double prof[P_COUNT][4] = {};  // launches, ms, flop, bytes
 
-  float* W(int t) { return (three ? whi : params) + off[t]; }
-  float* Wlo(int t) { return three ? wlo + off[t] : nullptr; }
+  // weight operand t: f32, its TF32 pair, or (split-f16 steps) its binary16 pair
+  const float* W(int t) const {
+    if (step16) return reinterpret_cast<const float*>(reinterpret_cast<const uint16_t*>(whi) + off[t]);
+    return (three ? whi : params) + off[t];
+  }
+  const float* Wlo(int t) const {
+    if (step16) return reinterpret_cast<const float*>(reinterpret_cast<const uint16_t*>(wlo) + off[t]);
+    return three ? wlo + off[t] : nullptr;
+  }
+  int slot(int l, int k) const { return l * kSlotsPerLayer + k; }
+  int slot_xf() const { return (int)L * kSlotsPerLayer; }
+  int slot_dlog() const { return slot_xf() + 1; }
+  int slot_w() const { return slot_xf() + 2; }
   float* Pp(int t) { return params + off[t]; }
   float* G(int t) { return grads + off[t]; }
   int lt(int l, int j) const { return 1 + l * kPerLayer + j; }
@@ -194,23 +228,56 @@ void split(et_b200_lm* lm, float* x, float* lo, size_t n) {
   split_tf32(x, x, lo, n, lm->stream);
 }
 
+// Output format of the producer of slot s: the binary16 pair in split-f16
+// steps, and its max |x| in every step of a split-f16 model.
+OperandScale osc(et_b200_lm* lm, int s) {
+  if (!lm->f16) return OperandScale{};
+  return OperandScale{lm->sexp + s, lm->samax + s, lm->step16 ? 1 : 0};
+}
+// `elems` binary16 values past base, as the float pointer GemmArgs carries
+float* half_at(float* base, size_t elems) {
+  return reinterpret_cast<float*>(reinterpret_cast<uint16_t*>(base) + elems);
+}
+// split-f16 steps: A and B are binary16 pairs scaled by slots sa and sb
+void set16(et_b200_lm* lm, GemmArgs& g, int sa, int sb) {
+  if (!lm->step16) return;
+  g.f16 = true;
+  g.exp_a = lm->sexp + sa;
+  g.exp_b = lm->sexp + sb;
+}
+// A tensor that attention wrote as a TF32 pair, as the binary16 pair of
+// slot s (split-f16 steps), or only its max |x| (3xTF32 steps of the model).
+void operand16(et_b200_lm* lm, const float* hi, const float* lo, size_t n, float* out, int s) {
+  if (!lm->f16) return;
+  Mark mk(lm, P_SPLIT, 0, (lm->step16 ? 12.0 : 4.0) * n);
+  if (lm->step16)
+    split_f16(hi, lo, n, reinterpret_cast<uint16_t*>(out), reinterpret_cast<uint16_t*>(out) + n,
+              lm->sexp + s, lm->samax + s, lm->stream);
+  else
+    abs_max(hi, n, lm->samax + s, lm->stream);
+}
+
 // ---- linear wrappers ---------------------------------------------------------
 
 // y = x W^T + bias, optionally with a fused epilogue (GemmArgs::epilogue):
-// RESIDUAL adds `aux`; GELU_FWD also writes GELU(y) to out2 (hi) / out3 (lo);
-// QKV also writes the attention operands described by `qkv`.
+// RESIDUAL adds `aux`; GELU_FWD also writes GELU(y) to out2 (hi) / out3 (lo)
+// in the format of slot `sout`; QKV also writes the attention operands
+// described by `qkv`.  `sa`: the split-f16 slot of x.
 void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t rows, int64_t din,
                     int64_t dout, int wt, const float* bias, float* y,
                     int epilogue = GEMM_EPI_PLAIN, const float* aux = nullptr,
-                    float* out2 = nullptr, float* out3 = nullptr, const QkvPrep* qkv = nullptr) {
+                    float* out2 = nullptr, float* out3 = nullptr, const QkvPrep* qkv = nullptr,
+                    int sa = -1, int sout = -1) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)dout; g.K = (int)din;
   g.A = x; g.A_lo = xlo; g.lda = din; g.a_kmajor = true;
   g.B = lm->W(wt); g.B_lo = lm->Wlo(wt); g.ldb = din; g.b_kmajor = true;
   g.C = y; g.ldc = dout; g.bias = bias; g.accumulate = false;
   g.epilogue = epilogue; g.aux = aux; g.out2 = out2; g.out3 = out3; g.qkv = qkv;
+  set16(lm, g, sa, lm->slot_w());
+  if (epilogue == GEMM_EPI_GELU_FWD && sout >= 0) g.out_sc = osc(lm, sout);
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
-  gemm(g, lm->precision, lm->stream);
+  gemm(g, lm->gprec, lm->stream);
 }
 
 // dX = dY W; with gelu_in the epilogue applies the GELU backward of the layer
@@ -219,7 +286,8 @@ void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t ro
 void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int64_t rows,
                         int64_t din, int64_t dout, int wt, float* dxo,
                         const float* gelu_in = nullptr, float* dxo_lo = nullptr,
-                        float* dsum = nullptr, const AttnGradPrep* dprep = nullptr) {
+                        float* dsum = nullptr, const AttnGradPrep* dprep = nullptr, int sa = -1,
+                        int sout = -1) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)din; g.K = (int)dout;
   g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = true;
@@ -228,25 +296,29 @@ void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int6
   if (gelu_in != nullptr) {
     g.epilogue = GEMM_EPI_GELU_BWD; g.aux = gelu_in; g.out2 = dxo_lo; g.dsum = dsum;
     g.epi_ws = lm->epi_ws;
+    if (sout >= 0) g.out_sc = osc(lm, sout);
   }
   if (dprep != nullptr) {
     g.epilogue = GEMM_EPI_ATTN_DO;
     g.dprep = dprep;
   }
+  set16(lm, g, sa, lm->slot_w());
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
-  gemm(g, lm->precision, lm->stream);
+  gemm(g, lm->gprec, lm->stream);
 }
 
 void linear_backward_dw(et_b200_lm* lm, const float* dy, const float* dylo, const float* x,
-                        const float* xlo, int64_t rows, int64_t din, int64_t dout, float* dw) {
+                        const float* xlo, int64_t rows, int64_t din, int64_t dout, float* dw,
+                        int sa = -1, int sb = -1) {
   GemmArgs g{};
   g.M = (int)dout; g.N = (int)din; g.K = (int)rows;
   g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = false;
   g.B = x; g.B_lo = xlo; g.ldb = din; g.b_kmajor = false;
   g.C = dw; g.ldc = din; g.bias = nullptr; g.accumulate = false;
   g.workspace = lm->splitk_ws; g.workspace_floats = lm->splitk_floats;
+  set16(lm, g, sa, sb);
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
-  gemm(g, lm->precision, lm->stream);
+  gemm(g, lm->gprec, lm->stream);
 }
 
 // db = column sums of dy (+ dy_lo when dy holds only the TF32 hi part).
@@ -295,8 +367,9 @@ void forward(et_b200_lm* lm) {
     {
       Mark mk(lm, P_NORM, 0, 8.0 * R * d);
       // with 3xTF32 the producers write each GEMM operand as a hi/lo pair
+      // (split-f16 steps: the binary16 pair, in the same buffers)
       layer_norm_forward(a.x, lm->Pp(lm->lt(l, T_LN1G)), lm->Pp(lm->lt(l, T_LN1B)), lm->eps, a.h1,
-                         a.mu1, a.rs1, R, d, s, a.h1lo);
+                         a.mu1, a.rs1, R, d, s, a.h1lo, osc(lm, lm->slot(l, S_H1)));
     }
     {
       // the QKV epilogue also writes the attention operands (RoPE'd, hi/lo, head-major)
@@ -305,36 +378,46 @@ void forward(et_b200_lm* lm) {
       p.qkv_ready = attention_qkv_prep(p, &prep) ? 1 : 0;
       linear_forward(lm, a.h1, a.h1lo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->Pp(lm->lt(l, T_BQKV)),
                      a.qkv, p.qkv_ready ? GEMM_EPI_QKV : GEMM_EPI_PLAIN, nullptr, nullptr,
-                     nullptr, p.qkv_ready ? &prep : nullptr);
+                     nullptr, p.qkv_ready ? &prep : nullptr, lm->slot(l, S_H1));
       Mark mk(lm, P_ATTN_FWD, attn_flop(lm, 2), 0);
       lm->attn_prepared[l] =
           attention_forward(p, AttnOut{a.ao, lm->T * d, lm->Dh, d, a.aolo}, a.am, a.al, s);
     }
     if (lm->three && !lm->attn_prepared[l]) split(lm, a.ao, a.aolo, R * d);
+    // the output projection's operand (split-f16: the binary16 pair of o)
+    operand16(lm, a.ao, a.aolo, R * d, a.ao16, lm->slot(l, S_AO));
+    const float* aoh = lm->step16 ? a.ao16 : a.ao;
+    const float* aol = lm->step16 ? half_at(a.ao16, R * d) : a.aolo;
     // x' = x + o Wo^T + bo (the residual add in the GEMM epilogue)
-    linear_forward(lm, a.ao, a.aolo, R, d, d, lm->lt(l, T_WO), lm->Pp(lm->lt(l, T_BO)), a.xmid,
-                   GEMM_EPI_RESIDUAL, a.x);
+    linear_forward(lm, aoh, aol, R, d, d, lm->lt(l, T_WO), lm->Pp(lm->lt(l, T_BO)), a.xmid,
+                   GEMM_EPI_RESIDUAL, a.x, nullptr, nullptr, nullptr, lm->slot(l, S_AO));
     {
       Mark mk(lm, P_NORM, 0, 8.0 * R * d);
       layer_norm_forward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), lm->Pp(lm->lt(l, T_LN2B)), lm->eps,
-                         a.h2, a.mu2, a.rs2, R, d, s, a.h2lo);
+                         a.h2, a.mu2, a.rs2, R, d, s, a.h2lo, osc(lm, lm->slot(l, S_H2)));
     }
     // u = h2 W1^T + b1 and g = GELU(u) (hi/lo) from the same epilogue
     linear_forward(lm, a.h2, a.h2lo, R, d, F, lm->lt(l, T_W1), lm->Pp(lm->lt(l, T_B1)), a.u,
-                   GEMM_EPI_GELU_FWD, nullptr, a.g, a.glo);
+                   GEMM_EPI_GELU_FWD, nullptr, a.g, a.glo, nullptr, lm->slot(l, S_H2),
+                   lm->slot(l, S_G));
     linear_forward(lm, a.g, a.glo, R, F, d, lm->lt(l, T_W2), lm->Pp(lm->lt(l, T_B2)), xnext,
-                   GEMM_EPI_RESIDUAL, a.xmid);
+                   GEMM_EPI_RESIDUAL, a.xmid, nullptr, nullptr, nullptr, lm->slot(l, S_G));
   }
   {
     Mark mk(lm, P_NORM, 0, 8.0 * R * d);
     layer_norm_forward(lm->x_final, lm->Pp(lm->lnf_g()), lm->Pp(lm->lnf_b()), lm->eps, lm->xf,
-                       lm->muf, lm->rsf, R, d, s, lm->xflo);
+                       lm->muf, lm->rsf, R, d, s, lm->xflo, osc(lm, lm->slot_xf()));
   }
-  linear_forward(lm, lm->xf, lm->xflo, R, d, V, 0, nullptr, lm->logits);
+  linear_forward(lm, lm->xf, lm->xflo, R, d, V, 0, nullptr, lm->logits, GEMM_EPI_PLAIN, nullptr,
+                 nullptr, nullptr, nullptr, lm->slot_xf());
   {
-    Mark mk(lm, P_CE, 0, 8.0 * R * V + 12.0 * R);
-    ce_fused(lm->logits, lm->logits, lm->targets, nullptr, lm->ce_scale, lm->loss_rows, R, V,
-             lm->status, s, lm->logits_lo);
+    Mark mk(lm, P_CE, 0, (lm->step16 ? 8.0 : 12.0) * R * V + 12.0 * R);
+    // dlogits in place of the logits (TF32 hi, lo in logits_lo), or
+    // (split-f16 steps) its binary16 pair in logits_lo: hi, then lo
+    float* dh = lm->step16 ? lm->logits_lo : lm->logits;
+    float* dl = lm->step16 ? half_at(lm->logits_lo, (size_t)R * V) : lm->logits_lo;
+    ce_fused(lm->logits, dh, lm->targets, nullptr, lm->ce_scale, lm->loss_rows, R, V, lm->status,
+             s, dl, osc(lm, lm->slot_dlog()));
     mean_loss(lm->loss_rows, R, lm->loss_mean, s);
   }
 }
@@ -355,16 +438,21 @@ void backward(et_b200_lm* lm) {
   const int64_t R = lm->R, d = lm->d, F = lm->F, V = lm->V;
   cudaStream_t s = lm->stream;
   const bool three = lm->three;
-  // head (tied): dlogits already in place of the logits
-  float* dlog = lm->logits;
-  linear_backward_dx(lm, dlog, lm->logits_lo, R, d, V, 0, lm->dtmp);
-  linear_backward_dw(lm, dlog, lm->logits_lo, lm->xf, lm->xflo, R, d, V, lm->G(0));
+  // head (tied): dlogits already in place of the logits (split-f16 steps:
+  // its binary16 pair in logits_lo)
+  float* dlog = lm->step16 ? lm->logits_lo : lm->logits;
+  float* dlog_lo = lm->step16 ? half_at(lm->logits_lo, (size_t)R * V) : lm->logits_lo;
+  linear_backward_dx(lm, dlog, dlog_lo, R, d, V, 0, lm->dtmp, nullptr, nullptr, nullptr, nullptr,
+                     lm->slot_dlog());
+  linear_backward_dw(lm, dlog, dlog_lo, lm->xf, lm->xflo, R, d, V, lm->G(0), lm->slot_dlog(),
+                     lm->slot_xf());
   {
     Mark mk(lm, P_NORM, 0, 16.0 * R * d);
     // the column sums of this dx are the last layer's b2 gradient
     layer_norm_backward(lm->x_final, lm->Pp(lm->lnf_g()), lm->muf, lm->rsf, lm->dtmp, lm->dx, 0,
                         lm->G(lm->lnf_g()), lm->G(lm->lnf_b()), lm->ln_ws, R, d, s, lm->dxhi,
-                        lm->dxlo, lm->G(lm->lt((int)lm->L - 1, T_B2)));
+                        lm->dxlo, lm->G(lm->lt((int)lm->L - 1, T_B2)),
+                        osc(lm, lm->slot((int)lm->L - 1, S_DXF)));
   }
   for (int l = (int)lm->L - 1; l >= 0; l--) {
     LayerActs& a = lm->layers[l];
@@ -376,15 +464,19 @@ void backward(et_b200_lm* lm) {
     const float* dyl = three ? lm->dxlo : nullptr;
     // du = (dy W2) * GELU'(u) (hi/lo) and the b1 gradient, from the epilogue
     linear_backward_dx(lm, dyh, dyl, R, F, d, lm->lt(l, T_W2), lm->du, a.u, lm->dulo,
-                       lm->G(lm->lt(l, T_B1)));
-    linear_backward_dw(lm, dyh, dyl, a.g, a.glo, R, F, d, lm->G(lm->lt(l, T_W2)));
-    linear_backward_dx(lm, lm->du, lm->dulo, R, d, F, lm->lt(l, T_W1), lm->dtmp);
-    linear_backward_dw(lm, lm->du, lm->dulo, a.h2, a.h2lo, R, d, F, lm->G(lm->lt(l, T_W1)));
+                       lm->G(lm->lt(l, T_B1)), nullptr, lm->slot(l, S_DXF), lm->slot(l, S_DU));
+    linear_backward_dw(lm, dyh, dyl, a.g, a.glo, R, F, d, lm->G(lm->lt(l, T_W2)),
+                       lm->slot(l, S_DXF), lm->slot(l, S_G));
+    linear_backward_dx(lm, lm->du, lm->dulo, R, d, F, lm->lt(l, T_W1), lm->dtmp, nullptr, nullptr,
+                       nullptr, nullptr, lm->slot(l, S_DU));
+    linear_backward_dw(lm, lm->du, lm->dulo, a.h2, a.h2lo, R, d, F, lm->G(lm->lt(l, T_W1)),
+                       lm->slot(l, S_DU), lm->slot(l, S_H2));
     {
       Mark mk(lm, P_NORM, 0, 20.0 * R * d);
       layer_norm_backward(a.xmid, lm->Pp(lm->lt(l, T_LN2G)), a.mu2, a.rs2, lm->dtmp, lm->dx, 1,
                           lm->G(lm->lt(l, T_LN2G)), lm->G(lm->lt(l, T_LN2B)), lm->ln_ws, R, d, s,
-                          lm->dxhi, lm->dxlo, lm->G(lm->lt(l, T_BO)));  // + the bo gradient
+                          lm->dxhi, lm->dxlo, lm->G(lm->lt(l, T_BO)),  // + the bo gradient
+                          osc(lm, lm->slot(l, S_DXA)));
     }
     // attention output projection: dY = dx
     dyh = three ? lm->dxhi : lm->dx;
@@ -397,8 +489,10 @@ void backward(et_b200_lm* lm) {
     AttnGradPrep dprep;
     p.grad_ready = attention_grad_prep(p, ao, a.aolo, a.am, a.al, lm->delta, &dprep) ? 1 : 0;
     linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp, nullptr, nullptr, nullptr,
-                       p.grad_ready ? &dprep : nullptr);
-    linear_backward_dw(lm, dyh, dyl, a.ao, a.aolo, R, d, d, lm->G(lm->lt(l, T_WO)));
+                       p.grad_ready ? &dprep : nullptr, lm->slot(l, S_DXA));
+    linear_backward_dw(lm, dyh, dyl, lm->step16 ? a.ao16 : a.ao,
+                       lm->step16 ? half_at(a.ao16, R * d) : a.aolo, R, d, d,
+                       lm->G(lm->lt(l, T_WO)), lm->slot(l, S_DXA), lm->slot(l, S_AO));
     {
       Mark mk(lm, P_ATTN_BWD, attn_flop(lm, 4), 0);
       const int64_t w = 3 * d;
@@ -415,6 +509,8 @@ void backward(et_b200_lm* lm) {
       bqkv_done = tc;
     }
     if (three && !dqkv_split) split(lm, lm->dqkv, lm->dqkvlo, R * 3 * d);
+    // the QKV projection's operand (split-f16: the binary16 pair of dqkv)
+    operand16(lm, lm->dqkv, lm->dqkvlo, R * 3 * d, lm->dqkv16, lm->slot(l, S_DQKV));
     if (bqkv_done) {
       Mark mk(lm, P_ELEMENTWISE, 0, 4.0 * lm->qkv_colrows * 3 * d);
       reduce_partials(lm->qkv_colpart, (int)lm->qkv_colrows, 3 * d, 3 * d,
@@ -422,9 +518,12 @@ void backward(et_b200_lm* lm) {
     } else {
       bias_grad(lm, lm->dqkv, R, 3 * d, lm->G(lm->lt(l, T_BQKV)), three ? lm->dqkvlo : nullptr);
     }
-    linear_backward_dx(lm, lm->dqkv, lm->dqkvlo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->dtmp);
-    linear_backward_dw(lm, lm->dqkv, lm->dqkvlo, a.h1, a.h1lo, R, d, 3 * d,
-                       lm->G(lm->lt(l, T_WQKV)));
+    const float* gq = lm->step16 ? lm->dqkv16 : lm->dqkv;
+    const float* gql = lm->step16 ? half_at(lm->dqkv16, R * 3 * d) : lm->dqkvlo;
+    linear_backward_dx(lm, gq, gql, R, d, 3 * d, lm->lt(l, T_WQKV), lm->dtmp, nullptr, nullptr,
+                       nullptr, nullptr, lm->slot(l, S_DQKV));
+    linear_backward_dw(lm, gq, gql, a.h1, a.h1lo, R, d, 3 * d, lm->G(lm->lt(l, T_WQKV)),
+                       lm->slot(l, S_DQKV), lm->slot(l, S_H1));
     {
       Mark mk(lm, P_NORM, 0, 20.0 * R * d);
       // layer 0's dx only feeds the embedding gradient: no operand pair
@@ -432,7 +531,8 @@ void backward(et_b200_lm* lm) {
       layer_norm_backward(a.x, lm->Pp(lm->lt(l, T_LN1G)), a.mu1, a.rs1, lm->dtmp, lm->dx, 1,
                           lm->G(lm->lt(l, T_LN1G)), lm->G(lm->lt(l, T_LN1B)), lm->ln_ws, R, d, s,
                           l > 0 ? lm->dxhi : nullptr, l > 0 ? lm->dxlo : nullptr,
-                          l > 0 ? lm->G(lm->lt(l - 1, T_B2)) : nullptr);
+                          l > 0 ? lm->G(lm->lt(l - 1, T_B2)) : nullptr,
+                          l > 0 ? osc(lm, lm->slot(l - 1, S_DXF)) : OperandScale{});
     }
     allreduce_range(lm, lm->lt(l, 0), lm->lt(l, 0) + kPerLayer, lm->layer_done[l]);
   }
@@ -440,10 +540,15 @@ void backward(et_b200_lm* lm) {
     Mark mk(lm, P_EMBED, 0, 12.0 * V * d + 8.0 * R * d);
     embedding_backward(lm->ids, lm->dx, lm->G(0), lm->G(0), R, V, d, lm->emb_scratch, s);
   }
+  // split-f16 steps: did an operand reach binary16's overflow?  (the flag at
+  // grads[P] rides the last gradient reduction, so every rank agrees)
+  if (lm->step16)
+    operand_range_check(lm->samax, lm->sexp, lm->nslots, lm->slot_w(), lm->grads + lm->P, s);
   if (lm->dp) {
     allreduce_range(lm, 0, 1, lm->tail_done);
     const int lg = lm->lnf_g();
-    nccl().AllReduce(lm->G(lg), lm->G(lg), lm->sz[lg] + lm->sz[lg + 1], ncclFloat32, ncclSum,
+    const size_t end = lm->f16 ? lm->P + 1 : lm->off[lg + 1] + lm->sz[lg + 1];
+    nccl().AllReduce(lm->G(lg), lm->G(lg), end - lm->off[lg], ncclFloat32, ncclSum,
                      lm->nccl_comm, lm->comm);
     cudaEventRecord(lm->comm_done, lm->comm);
     Mark mk(lm, P_ALLREDUCE_WAIT, 0, 0);
@@ -455,6 +560,41 @@ void refresh_weight_split(et_b200_lm* lm) {
   if (!lm->three) return;
   Mark mk(lm, P_SPLIT, 0, 12.0 * lm->P);
   split_tf32(lm->params, lm->whi, lm->wlo, lm->P, lm->stream);
+  lm->w16_valid = false;
+}
+
+// The weights' exponent from their current max |w| (kept until the weights
+// are split again: AdamW writes the next pair with it).
+void weight_scale(et_b200_lm* lm) {
+  unsigned* am = lm->samax + lm->slot_w();
+  cudaMemsetAsync(am, 0, sizeof(unsigned), lm->stream);
+  abs_max(lm->params, lm->P, am, lm->stream);
+  scale_from_amax(am, lm->sexp + lm->slot_w(), 1, kScaleTarget, 1, lm->stream);
+}
+
+// Operand formats for the step about to be enqueued (split-f16 models):
+// binary16 pairs once a finished step has measured every slot, else 3xTF32
+// with the TF32 weight pair and every slot's max recorded.
+void begin_step(et_b200_lm* lm) {
+  if (!lm->f16) return;
+  lm->step16 = lm->calibrated;
+  cudaMemsetAsync(lm->grads + lm->P, 0, sizeof(float), lm->stream);  // range flag
+  if (lm->step16) {
+    // exponents of the activation / gradient slots from the last step's maxima
+    scale_from_amax(lm->samax, lm->sexp, lm->slot_w(), kScaleTarget, 1, lm->stream);
+    if (!lm->w16_valid) {
+      Mark mk(lm, P_SPLIT, 0, 8.0 * lm->P);
+      weight_scale(lm);
+      split_f16(lm->params, nullptr, lm->P, reinterpret_cast<uint16_t*>(lm->whi),
+                reinterpret_cast<uint16_t*>(lm->wlo), lm->sexp + lm->slot_w(),
+                lm->samax + lm->slot_w(), lm->stream);
+      lm->w16_valid = true;
+    }
+  } else {
+    cudaMemsetAsync(lm->samax, 0, lm->nslots * sizeof(unsigned), lm->stream);
+    refresh_weight_split(lm);
+    weight_scale(lm);
+  }
 }
 
 void optimizer_step(et_b200_lm* lm) {
@@ -479,14 +619,18 @@ void optimizer_step(et_b200_lm* lm) {
   h.lr = lr;
   h.decay = one - lrwd;
   h.epsilon = fbits(c.epsilon_bits);
-  // with 3xTF32 the same pass refreshes the weights' (hi, lo) operand pair
+  // with 3xTF32 the same pass refreshes the weights' (hi, lo) operand pair;
+  // split-f16 models always write the binary16 pair (the next step's format)
   h.value_hi = lm->three ? lm->whi : nullptr;
   h.value_lo = lm->three ? lm->wlo : nullptr;
+  if (lm->f16) h.value_sc = OperandScale{lm->sexp + lm->slot_w(), lm->samax + lm->slot_w(), 1};
   cudaMemcpyAsync(lm->d_adam, &h, sizeof(h), cudaMemcpyHostToDevice, lm->stream);
   {
-    Mark mk(lm, P_ADAMW, 0, (lm->three ? 36.0 : 28.0) * lm->P);
-    adamw_multi(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, lm->status, lm->stream);
+    Mark mk(lm, P_ADAMW, 0, (lm->f16 ? 32.0 : lm->three ? 36.0 : 28.0) * lm->P);
+    adamw_multi(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, lm->status, lm->stream,
+                lm->f16 ? lm->grads + lm->P : nullptr);
   }
+  if (lm->f16) lm->w16_valid = true;
   lm->updates = t;
 }
 
@@ -496,16 +640,36 @@ int32_t check_ready(et_b200_lm* lm, et_kernel_error* e, const char* op) {
   return 0;
 }
 
-int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, const char* op) {
-  float loss = 0.0f;
-  int flags[2] = {0, 0};
+// Reads the loss and the flags of the step just enqueued.  *redo: a
+// split-f16 step that was not applied (an operand reached binary16's
+// overflow); `update`: the step ran AdamW.
+int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, const char* op,
+                         bool update, bool* redo) {
+  float loss = 0.0f, range = 0.0f;
+  int flags[3] = {0, 0, 0};
   int word = 0;
+  *redo = false;
   cudaMemcpyAsync(&loss, lm->loss_mean, sizeof(float), cudaMemcpyDeviceToHost, lm->stream);
   cudaMemcpyAsync(flags, lm->status, sizeof(flags), cudaMemcpyDeviceToHost, lm->stream);
   cudaMemcpyAsync(&word, device_error_word(), sizeof(int), cudaMemcpyDeviceToHost, lm->stream);
+  if (lm->f16)
+    cudaMemcpyAsync(&range, lm->grads + lm->P, sizeof(float), cudaMemcpyDeviceToHost, lm->stream);
   cudaError_t st = cudaStreamSynchronize(lm->stream);
   if (st != cudaSuccess) return cuda_error(e, st, op);
   if (host_loss) *host_loss = loss;
+  const bool skipped = lm->step16 && range != 0.0f;
+  // status[2] counts the steps AdamW skipped: this one, and any enqueued by
+  // et_b200_lm_step_device_v1 since the last host-synchronised call
+  const int earlier = flags[2] - (skipped && update ? 1 : 0);
+  if (flags[2] != 0) {
+    cudaMemsetAsync(lm->status + 2, 0, sizeof(int), lm->stream);
+    cudaStreamSynchronize(lm->stream);
+  }
+  if (earlier > 0) {
+    lm->calibrated = false;
+    return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "a device-enqueued step had an operand beyond its binary16 range and was not applied");
+  }
   if (word != 0) {
     cudaMemset(device_error_word(), 0, sizeof(int));
     return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
@@ -518,8 +682,36 @@ int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, c
                      flags[0] ? "token id or target outside the vocabulary"
                               : "AdamW produced a nonfinite value");
   }
+  *redo = skipped;
   if (e) memset(e, 0, sizeof(*e));
   return 0;
+}
+
+void collect_profile(et_b200_lm* lm);
+
+// One host-synchronised step (forward, backward and, with `update`, AdamW).
+// A split-f16 step whose operand check fails was not applied; it is redone
+// with 3xTF32 contractions, which also re-measure every operand's scale.
+int32_t run_host_step(et_b200_lm* lm, bool update, float* host_loss, et_kernel_error* e,
+                      const char* op) {
+  for (int attempt = 0; attempt < 2; attempt++) {
+    begin_step(lm);
+    forward(lm);
+    backward(lm);
+    if (update) optimizer_step(lm);
+    bool redo = false;
+    const int32_t rc = finish_host_step(lm, host_loss, e, op, update, &redo);
+    collect_profile(lm);
+    if (rc != 0) return rc;
+    if (!redo) {
+      if (lm->f16) lm->calibrated = true;
+      return 0;
+    }
+    lm->calibrated = false;
+    if (update) lm->updates -= 1;
+  }
+  return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                   "the step's operands stayed outside their binary16 range");
 }
 
 void collect_profile(et_b200_lm* lm) {
@@ -552,7 +744,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
     return set_error(e, ET_KERNEL_ERROR_VERSION_MISMATCH, ET_KERNEL_CODE_INVALID_STRUCT_SIZE, op, "config is truncated");
   if (c->layers < 1 || c->d_model < 2 || c->heads < 1 || c->d_model % c->heads != 0 ||
       (c->d_model / c->heads) % 2 != 0 || c->d_model / c->heads > 128 || c->ffn < 1 ||
-      c->vocabulary < 1 || c->seq_len < 1 || c->batch < 1 || c->precision > 2)
+      c->vocabulary < 1 || c->seq_len < 1 || c->batch < 1 || c->precision > 3)
     return set_error(e, ET_KERNEL_ERROR_SHAPE_MISMATCH, ET_KERNEL_CODE_INVALID_SHAPE, op,
                      "unsupported model shape (head dim must be even and <= 128)");
   int32_t rc = et_b200_device_check_v1(e);
@@ -571,13 +763,18 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
     lm->attn_scale = 1.0f / root;
   }
   lm->precision = (int)c->precision;
-  lm->three = c->precision == ET_B200_PRECISION_TF32X3;
+  lm->three = c->precision == ET_B200_PRECISION_TF32X3 || c->precision == ET_B200_PRECISION_F16X3;
+  lm->gprec = lm->three ? (int)ET_B200_PRECISION_TF32X3 : lm->precision;
+  // split-f16 needs binary16 rows of 16-byte multiples and the register-row
+  // LayerNorm backward; other shapes run the whole step 3xTF32
+  lm->f16 = c->precision == ET_B200_PRECISION_F16X3 && c->d_model % 128 == 0 &&
+            c->d_model <= 1024 && c->ffn % 8 == 0 && c->vocabulary % 8 == 0;
   tensor_sizes(*c, lm->sz);
   lm->off.resize(lm->sz.size());
   size_t total = 0;
   for (size_t i = 0; i < lm->sz.size(); i++) {
     lm->off[i] = total;
-    total += (lm->sz[i] + 3) & ~(size_t)3;  // keep every tensor 16-byte aligned
+    total += (lm->sz[i] + 7) & ~(size_t)7;  // every tensor 16-byte aligned, also as binary16
   }
   lm->P = total;
   cudaError_t err = cudaSuccess;
@@ -585,7 +782,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   cudaStreamCreateWithFlags(&lm->stream, cudaStreamNonBlocking);
   cudaStreamCreateWithFlags(&lm->comm, cudaStreamNonBlocking);
   lm->params = dalloc<float>(lm, lm->P, &err);
-  lm->grads = dalloc<float>(lm, lm->P, &err);
+  lm->grads = dalloc<float>(lm, lm->P + 8, &err);  // + the split-f16 range flag at [P]
   lm->m1 = dalloc<float>(lm, lm->P, &err);
   lm->m2 = dalloc<float>(lm, lm->P, &err);
   if (lm->three) {
@@ -617,6 +814,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
       a.h2lo = dalloc<float>(lm, R * d, &err);
       a.glo = dalloc<float>(lm, R * F, &err);
     }
+    if (lm->f16) a.ao16 = dalloc<float>(lm, R * d, &err);
   }
   lm->x_final = dalloc<float>(lm, R * d, &err);
   lm->xf = dalloc<float>(lm, R * d, &err);
@@ -637,6 +835,12 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
     lm->dxlo = dalloc<float>(lm, R * d, &err);
     lm->dqkvlo = dalloc<float>(lm, R * 3 * d, &err);
     lm->dulo = dalloc<float>(lm, R * F, &err);
+  }
+  if (lm->f16) {
+    lm->dqkv16 = dalloc<float>(lm, R * 3 * d, &err);
+    lm->nslots = (int)L * kSlotsPerLayer + 3;
+    lm->sexp = dalloc<int>(lm, lm->nslots, &err);
+    lm->samax = dalloc<unsigned>(lm, lm->nslots, &err);
   }
   const size_t widest = (size_t)std::max<int64_t>(3 * d, F);
   lm->ln_ws = dalloc<float>(lm, ln_workspace_floats(R, d), &err);
@@ -689,7 +893,11 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   cudaMemcpy(lm->rope_sin, st.data(), st.size() * sizeof(float), cudaMemcpyHostToDevice);
   cudaMemcpy(lm->d_prefix, prefix, sizeof(prefix), cudaMemcpyHostToDevice);
   cudaMemset(lm->params, 0, lm->P * sizeof(float));
-  cudaMemset(lm->grads, 0, lm->P * sizeof(float));
+  cudaMemset(lm->grads, 0, (lm->P + 8) * sizeof(float));
+  if (lm->f16) {
+    cudaMemset(lm->sexp, 0, lm->nslots * sizeof(int));
+    cudaMemset(lm->samax, 0, lm->nslots * sizeof(unsigned));
+  }
   cudaMemset(lm->m1, 0, lm->P * sizeof(float));
   cudaMemset(lm->m2, 0, lm->P * sizeof(float));
   cudaMemset(lm->status, 0, 4 * sizeof(int));
@@ -763,7 +971,10 @@ static int32_t transfer(et_b200_lm* lm, int32_t which, float* host, const float*
     if (st != cudaSuccess) return cuda_error(e, st, op);
     packed += lm->sz[t];
   }
-  if (to_device && which == 0) refresh_weight_split(lm);
+  if (to_device && which == 0) {
+    refresh_weight_split(lm);
+    lm->calibrated = false;  // new weights: the next split-f16 step re-measures the scales
+  }
   cudaError_t st = cudaStreamSynchronize(lm->stream);
   if (st != cudaSuccess) return cuda_error(e, st, op);
   if (e) memset(e, 0, sizeof(*e));
@@ -820,9 +1031,11 @@ int32_t et_b200_lm_step_device_v1(et_b200_lm* lm, const int64_t* device_ids,
   if (device_ids == nullptr || device_targets == nullptr)
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, "lm-step", "ids and targets are required");
   if (device_ids != lm->ids) stage_tokens(lm, device_ids, device_targets, cudaMemcpyDeviceToDevice);
+  begin_step(lm);
   forward(lm);
   backward(lm);
   optimizer_step(lm);
+  if (lm->f16) lm->calibrated = true;  // (a failed operand check is reported by the next host call)
   if (device_loss)
     cudaMemcpyAsync(device_loss, lm->loss_mean, sizeof(float), cudaMemcpyDeviceToDevice, lm->stream);
   cudaError_t st = cudaGetLastError();
@@ -837,12 +1050,7 @@ int32_t et_b200_lm_step_v1(et_b200_lm* lm, const int64_t* host_ids, const int64_
   if (host_ids == nullptr || host_targets == nullptr)
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, "lm-step", "ids and targets are required");
   stage_tokens(lm, host_ids, host_targets, cudaMemcpyHostToDevice);
-  forward(lm);
-  backward(lm);
-  optimizer_step(lm);
-  const int32_t rc = finish_host_step(lm, host_loss, e, "lm-step");
-  collect_profile(lm);
-  return rc;
+  return run_host_step(lm, true, host_loss, e, "lm-step");
 }
 
 int32_t et_b200_lm_forward_backward_v1(et_b200_lm* lm, const int64_t* host_ids,
@@ -852,11 +1060,7 @@ int32_t et_b200_lm_forward_backward_v1(et_b200_lm* lm, const int64_t* host_ids,
   if (host_ids == nullptr || host_targets == nullptr)
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, "lm-forward-backward", "ids and targets are required");
   stage_tokens(lm, host_ids, host_targets, cudaMemcpyHostToDevice);
-  forward(lm);
-  backward(lm);
-  const int32_t rc = finish_host_step(lm, host_loss, e, "lm-forward-backward");
-  collect_profile(lm);
-  return rc;
+  return run_host_step(lm, false, host_loss, e, "lm-forward-backward");
 }
 
 void* et_b200_lm_stream_v1(et_b200_lm* lm) { return lm ? (void*)lm->stream : nullptr; }

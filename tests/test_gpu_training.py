@@ -83,11 +83,16 @@ def _oracle_model():
 # Per-tensor gradient tolerance (max |err| <= tol * max |ref|) of one step of
 # the tiny LM against the serial-f32 oracle: the GEMMs, attention, LN and CE
 # reductions all sum in a different order from the reference.
-GRAD_TOL = {etb.PRECISION_TF32X3: 5e-5, etb.PRECISION_F32: 5e-5, etb.PRECISION_TF32: 5e-3}
+GRAD_TOL = {etb.PRECISION_TF32X3: 5e-5, etb.PRECISION_F16X3: 5e-5, etb.PRECISION_F32: 5e-5,
+            etb.PRECISION_TF32: 5e-3}
 
 
-@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F32, etb.PRECISION_TF32])
+@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F16X3,
+                                       etb.PRECISION_F32, etb.PRECISION_TF32])
 def test_tiny_lm_gradients_vs_oracle(lib, cuda, precision):
+    """One forward/backward against the oracle.  Split-f16 measures its
+    operand scales in a first (3xTF32) pass; the second pass, on the same
+    weights, is the split-f16 one compared here."""
     s = TINY
     om = _oracle_model()
     params = om.init(1234)
@@ -97,6 +102,10 @@ def test_tiny_lm_gradients_vs_oracle(lib, cuda, precision):
     model.init(1234)
     assert bits_equal(model.read(0), params)  # seeded init is bit-identical
     loss = model.forward_backward(ids, targets)
+    if precision == etb.PRECISION_F16X3:
+        first = model.read(1)
+        loss = model.forward_backward(ids, targets)
+        assert not bits_equal(model.read(1), first)  # the binary16 path did run
     grads = model.read(1)
     assert abs(loss - loss_ref) <= 2e-5 * abs(loss_ref), (loss, loss_ref)
     worst = []
@@ -108,7 +117,8 @@ def test_tiny_lm_gradients_vs_oracle(lib, cuda, precision):
     model.close()
 
 
-def test_tiny_lm_training_trajectory_vs_oracle(lib, cuda):
+@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F16X3])
+def test_tiny_lm_training_trajectory_vs_oracle(lib, cuda, precision):
     """Five AdamW steps: the loss trajectory within 2e-5 relative (the
     reference's TR3 loss tolerance) and the final weights.  AdamW's update
     lr m/(sqrt(v) + eps) is close to lr sign(g) and so amplifies any gradient
@@ -121,7 +131,7 @@ def test_tiny_lm_training_trajectory_vs_oracle(lib, cuda):
     m = np.zeros_like(params)
     v = np.zeros_like(params)
     opts = orc.adamw_options(1e-3, 0.9, 0.999, 1e-8, 0.01)
-    model = etb.LanguageModel(s, precision=etb.PRECISION_TF32X3)
+    model = etb.LanguageModel(s, precision=precision)
     model.init(99)
     for step in range(1, 6):
         ids, targets = orc.synthetic_batch(1000 + step, s.batch, s.seq_len, s.vocabulary)
