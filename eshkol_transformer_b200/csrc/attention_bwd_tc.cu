@@ -477,24 +477,27 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
     named_sync(1, SOFT);
     // column-sum scratch behind the two staged tiles (one per output)
     const uint32_t red = base + (uint32_t)(2 * 128 * (DH + 4) * 4);
+    float amax_k = 0.0f, amax_v = 0.0f;
     if (ok) {
       const bool split = dk.lo != nullptr && dv.lo != nullptr;
       const int rows = min(BK, p.Tk - k0);
       const int64_t ko = b * dk.sb + hkv * dk.sh + (int64_t)k0 * dk.st;
       const float4 sk = store_rows_split(
-          base, DH, rows, dk.ptr + ko, split ? dk.lo + ko : nullptr, dk.st, tid, SOFT,
+          base, DH, rows, dk.ptr, split ? dk.lo : nullptr, ko, dk.st, tid, SOFT,
           [&](int r, int c4, float4& v) {
             const int t = k0 + r;
             const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + t : t) * (DH / 2);
             grad_rotate4(v, p.scale, p.k_cos, p.k_sin, trw, c4);
-          });
+          }, dk.sc, amax_k);
       const int64_t vo = b * dv.sb + hkv * dv.sh + (int64_t)k0 * dv.st;
       const float4 sv = store_rows_split(base + (uint32_t)(128 * (DH + 4) * 4), DH, rows,
-                                         dv.ptr + vo, split ? dv.lo + vo : nullptr, dv.st, tid,
-                                         SOFT, [](int, int, float4&) {});
+                                         dv.ptr, split ? dv.lo : nullptr, vo, dv.st, tid,
+                                         SOFT, [](int, int, float4&) {}, dv.sc, amax_v);
       colsum_put(red, tid, sk);
       colsum_put(red + SOFT * 16u, tid, sv);
     }
+    if (dk.sc.amax != nullptr) amax_record_warp(dk.sc.amax, amax_k);
+    if (dv.sc.amax != nullptr) amax_record_warp(dv.sc.amax, amax_v);
     named_sync(1, SOFT);
     if (ok) {
       const int64_t prow = (int64_t)b * ((p.Tk + BK - 1) / BK) + blockIdx.x;
@@ -866,17 +869,19 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
     named_sync(1, SOFT);
     // column-sum scratch behind the staged tile
     const uint32_t red = base + (uint32_t)(128 * (DH + 4) * 4);
+    float amax = 0.0f;
     if (ok) {
       const int64_t qo = b * dq.sb + hq * dq.sh + (int64_t)q0 * dq.st;
       const float4 sq = store_rows_split(
-          base, DH, min(QM, p.Tq - q0), dq.ptr + qo, dq.lo != nullptr ? dq.lo + qo : nullptr,
-          dq.st, tid, SOFT, [&](int r, int c4, float4& v) {
+          base, DH, min(QM, p.Tq - q0), dq.ptr, dq.lo, qo, dq.st, tid, SOFT,
+          [&](int r, int c4, float4& v) {
             const int t = q0 + r;
             const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + t : t) * (DH / 2);
             grad_rotate4(v, p.scale, p.q_cos, p.q_sin, trw, c4);
-          });
+          }, dq.sc, amax);
       colsum_put(red, tid, sq);
     }
+    if (dq.sc.amax != nullptr) amax_record_warp(dq.sc.amax, amax);
     named_sync(1, SOFT);
     if (ok && dq.colsum != nullptr) {
       const int64_t prow = (int64_t)b * ((p.Tq + QM - 1) / QM) + blockIdx.x;

@@ -467,10 +467,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
       }
     }
     named_sync(1, SOFT);
+    float amax = 0.0f;
     if (ok) {
       const int64_t oo = b * o.sb + hq * o.sh + (int64_t)q0 * o.st;
-      store_rows_split(stage, DH, min(QM, p.Tq - q0), o.ptr + oo,
-                       o.lo != nullptr ? o.lo + oo : nullptr, o.st, tid, SOFT,
+      store_rows_split(stage, DH, min(QM, p.Tq - q0), o.ptr, o.lo, oo, o.st, tid, SOFT,
                        [&](int r, int, float4& v) {
                          const float l = lrow_s[r], rl = rrow_s[r];
                          if (l == 0.0f) {
@@ -479,8 +479,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
                            v.x = div_by(v.x, l, rl); v.y = div_by(v.y, l, rl);
                            v.z = div_by(v.z, l, rl); v.w = div_by(v.w, l, rl);
                          }
-                       });
+                       }, o.sc, amax);
     }
+    if (o.sc.amax != nullptr) amax_record_warp(o.sc.amax, amax);
   }
   tc_fence_before();
   __syncthreads();

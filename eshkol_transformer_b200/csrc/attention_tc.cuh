@@ -131,18 +131,38 @@ __device__ __forceinline__ void store_staged_rows(uint32_t stage, int cols, int 
 }
 
 // Writes `rows_valid` staged rows ([128][cols + 4] floats at `stage`) with
-// coalesced float4 stores: thread t of `nthreads` takes float4s t, t +
-// nthreads, ... (row r = i / (cols / 4), column 4 (i % (cols / 4))), applies
-// f(r, c4, v) in place, then stores v to hi_base (lo_base null) or its TF32
-// hi part to hi_base and the residual to lo_base.  Row r goes to
-// base + r * row_stride.  Returns the sum of the thread's v (its rows of
-// columns 4 (t % (cols / 4)) .. when nthreads is a multiple of cols / 4).
+// coalesced stores: thread t of `nthreads` takes float4s t, t + nthreads, ...
+// (row r = i / (cols / 4), column 4 (i % (cols / 4))), applies f(r, c4, v) in
+// place, then stores v to hi (lo null), its TF32 hi part to hi and the
+// residual to lo, or (sc.f16) the binary16 pair of v 2^(*sc.exp) to hi / lo
+// as uint16 arrays.  Row r goes to element off + r * row_stride of hi / lo.
+// Returns the sum of the thread's v (its rows of columns 4 (t % (cols / 4))
+// .. when nthreads is a multiple of cols / 4); amax takes max |v|.
 template <typename F>
 __device__ __forceinline__ float4 store_rows_split(uint32_t stage, int cols, int rows_valid,
-                                                   float* hi_base, float* lo_base,
-                                                   int64_t row_stride, int t, int nthreads, F f) {
+                                                   float* hi, float* lo, int64_t off0,
+                                                   int64_t row_stride, int t, int nthreads, F f,
+                                                   const OperandScale& sc, float& amax) {
   float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
   const int per_row = cols / 4;
+  if (sc.f16) {
+    // 8-byte stores: hi / lo 8-byte aligned and row_stride % 4 == 0 (host-checked)
+    uint16_t* hb = reinterpret_cast<uint16_t*>(hi) + off0;
+    uint16_t* lb = reinterpret_cast<uint16_t*>(lo) + off0;
+    const float s = exp2_int(*sc.exp);
+#pragma unroll 4
+    for (int idx = t; idx < rows_valid * per_row; idx += nthreads) {
+      const int r = idx / per_row, c4 = idx - r * per_row;
+      float4 v = lds128(stage + ((uint32_t)r * (uint32_t)(cols + 4) + 4u * (uint32_t)c4) * 4u);
+      f(r, c4, v);
+      sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+      amax = abs_max4(amax, v);
+      f16_store4(hb, lb, (int64_t)r * row_stride + 4 * c4, v, s);
+    }
+    return sum;
+  }
+  float* hi_base = hi + off0;
+  float* lo_base = lo != nullptr ? lo + off0 : nullptr;
   const uintptr_t bits = reinterpret_cast<uintptr_t>(hi_base) |
                          reinterpret_cast<uintptr_t>(lo_base) | (uintptr_t)(row_stride * 4);
   const bool vec = (bits & 15) == 0;
@@ -152,23 +172,24 @@ __device__ __forceinline__ float4 store_rows_split(uint32_t stage, int cols, int
     float4 v = lds128(stage + ((uint32_t)r * (uint32_t)(cols + 4) + 4u * (uint32_t)c4) * 4u);
     f(r, c4, v);
     sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (sc.amax != nullptr) amax = abs_max4(amax, v);
+    float4 lo4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (lo_base != nullptr) {
-      tf32_split(v.x, v.x, lo.x);
-      tf32_split(v.y, v.y, lo.y);
-      tf32_split(v.z, v.z, lo.z);
-      tf32_split(v.w, v.w, lo.w);
+      tf32_split(v.x, v.x, lo4.x);
+      tf32_split(v.y, v.y, lo4.y);
+      tf32_split(v.z, v.z, lo4.z);
+      tf32_split(v.w, v.w, lo4.w);
     }
     const int64_t off = (int64_t)r * row_stride + 4 * c4;
     if (vec) {
       *reinterpret_cast<float4*>(hi_base + off) = v;
-      if (lo_base != nullptr) *reinterpret_cast<float4*>(lo_base + off) = lo;
+      if (lo_base != nullptr) *reinterpret_cast<float4*>(lo_base + off) = lo4;
     } else {
       float* h = hi_base + off;
       h[0] = v.x; h[1] = v.y; h[2] = v.z; h[3] = v.w;
       if (lo_base != nullptr) {
         float* l = lo_base + off;
-        l[0] = lo.x; l[1] = lo.y; l[2] = lo.z; l[3] = lo.w;
+        l[0] = lo4.x; l[1] = lo4.y; l[2] = lo4.z; l[3] = lo4.w;
       }
     }
   }

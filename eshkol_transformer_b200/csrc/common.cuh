@@ -100,6 +100,13 @@ __device__ __forceinline__ void f16_store4(uint16_t* hi, uint16_t* lo, int64_t o
   *reinterpret_cast<uint2*>(lo + off) =
       make_uint2((uint32_t)l[0] | ((uint32_t)l[1] << 16), (uint32_t)l[2] | ((uint32_t)l[3] << 16));
 }
+// binary16 values in the low / high half of a 32-bit word
+__device__ __forceinline__ float half_lo(uint32_t w) {
+  return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+__device__ __forceinline__ float half_hi(uint32_t w) {
+  return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
 __device__ __forceinline__ float abs_max4(float m, float4 x) {
   return fmaxf(fmaxf(m, fmaxf(fabsf(x.x), fabsf(x.y))), fmaxf(fabsf(x.z), fabsf(x.w)));
 }

@@ -172,6 +172,9 @@ struct TcArgs {
   // GELU_FWD / GELU_BWD operand-pair outputs: binary16 with this scale, and
   // their max |x| (either format)
   OperandScale out_sc;
+  // QKV / ATTN_DO: C itself is not stored (the attention operands are its
+  // only consumers)
+  int skip_c;
 };
 
 __device__ __forceinline__ float gelu_value(float v) {  // n2_primitives_provider.c:545-583
@@ -788,6 +791,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
         f16 ? exp2_int(-((args.exp_a ? *args.exp_a : 0) + (args.exp_b ? *args.exp_b : 0))) : 1.0f;
     const bool out16 = args.out_sc.f16 != 0;
     const float out_s = out16 ? exp2_int(*args.out_sc.exp) : 1.0f;
+    // ATTN_DO with o as a binary16 pair: its scale 2^-e
+    const float o_inv =
+        (ATTN && args.dprep.o_exp != nullptr) ? exp2_int(-*args.dprep.o_exp) : 1.0f;
     float amax = 0.0f;  // max |x| of the operand-pair output this warp wrote
     for (int unit = cluster; unit < units; unit += nclusters) {
       const int tile = unit % tiles, split = unit / tiles;
@@ -840,11 +846,22 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             if (ATTN && epi == GEMM_EPI_ATTN_DO && row < args.M && col_ok) {
               // the forward output o = hi + lo (exact), same layout as dO
               const int64_t oo = (int64_t)row * (args.dprep.H * args.dprep.Dh) + n;
-              const float4 oh = __ldg(reinterpret_cast<const float4*>(args.dprep.o + oo));
-              float4 ol = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (args.dprep.o_lo != nullptr)
-                ol = __ldg(reinterpret_cast<const float4*>(args.dprep.o_lo + oo));
-              pre[it] = make_float4(oh.x + ol.x, oh.y + ol.y, oh.z + ol.z, oh.w + ol.w);
+              if (args.dprep.o_exp != nullptr) {  // binary16 pair of o 2^e
+                const uint2 h = __ldg(reinterpret_cast<const uint2*>(
+                    reinterpret_cast<const uint16_t*>(args.dprep.o) + oo));
+                const uint2 l = __ldg(reinterpret_cast<const uint2*>(
+                    reinterpret_cast<const uint16_t*>(args.dprep.o_lo) + oo));
+                pre[it] = make_float4((half_lo(h.x) + half_lo(l.x)) * o_inv,
+                                      (half_hi(h.x) + half_hi(l.x)) * o_inv,
+                                      (half_lo(h.y) + half_lo(l.y)) * o_inv,
+                                      (half_hi(h.y) + half_hi(l.y)) * o_inv);
+              } else {
+                const float4 oh = __ldg(reinterpret_cast<const float4*>(args.dprep.o + oo));
+                float4 ol = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (args.dprep.o_lo != nullptr)
+                  ol = __ldg(reinterpret_cast<const float4*>(args.dprep.o_lo + oo));
+                pre[it] = make_float4(oh.x + ol.x, oh.y + ol.y, oh.z + ol.z, oh.w + ol.w);
+              }
             }
 
           }
@@ -872,7 +889,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               // these 32 columns (summed over the 8 lanes of the row)
               float dot = 0.0f;
               if (row < args.M && col_ok) {
-                *reinterpret_cast<float4*>(cbase + (int64_t)row * ldc + n) = x;
+                if (!args.skip_c) *reinterpret_cast<float4*>(cbase + (int64_t)row * ldc + n) = x;
                 attn_do_store(args.dprep, row, n, x);
                 const float4 o = pre[it];
                 dot = fmaf(x.w, o.w, fmaf(x.z, o.z, fmaf(x.y, o.y, x.x * o.x)));
@@ -923,7 +940,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               const float4 o = *dst;
               x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
             }
-            *dst = x;
+            if (!(ATTN && args.skip_c)) *dst = x;
             if (epi == GEMM_EPI_GELU_FWD) {
               float4 g = make_float4(gelu_value(x.x), gelu_value(x.y), gelu_value(x.z),
                                      gelu_value(x.w));
@@ -1296,6 +1313,7 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   a.exp_a = g.exp_a;
   a.exp_b = g.exp_b;
   a.out_sc = g.out_sc;
+  a.skip_c = g.skip_c && (g.epilogue == GEMM_EPI_QKV || g.epilogue == GEMM_EPI_ATTN_DO) ? 1 : 0;
   if (g.epilogue == GEMM_EPI_QKV) a.qkv = *g.qkv;
   if (g.epilogue == GEMM_EPI_ATTN_DO) a.dprep = *g.dprep;
   {
@@ -1316,7 +1334,14 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   // the attention operands are written by the staged epilogue only
   const bool prep_after =
       (g.epilogue == GEMM_EPI_QKV || g.epilogue == GEMM_EPI_ATTN_DO) && !a.staged;
-  if (prep_after) a.epilogue = GEMM_EPI_PLAIN;
+  if (prep_after && g.epilogue == GEMM_EPI_ATTN_DO && g.dprep->o_exp != nullptr) {
+    gemm_f16_refused(g, "binary16 attention output needs the staged epilogue");
+    return;
+  }
+  if (prep_after) {
+    a.epilogue = GEMM_EPI_PLAIN;
+    a.skip_c = 0;
+  }
   const int tiles = a.tiles_m * a.tiles_n;
   const int nkb = (g.K + (g.f16 ? 2 * L::BK : L::BK) - 1) / (g.f16 ? 2 * L::BK : L::BK);
   const int pairs = sm_count() / 2;

@@ -160,6 +160,10 @@ struct AttnOut {
   // column sums of the whole gradient (a bias gradient)
   float* colsum;
   int64_t colsum_ld;
+  // optional (tensor-core kernels): sc.f16 makes ptr / lo the binary16 pair
+  // of the output 2^(*sc.exp) (uint16 arrays, same element strides; 8-byte
+  // aligned rows); sc.amax receives max |output| in either format
+  OperandScale sc;
 };
 struct AttnParams {
   int B, Hq, Hkv, Tq, Tk, Dh;
@@ -203,6 +207,8 @@ struct AttnGradPrep {
   int T, H, Dh;
   const float* o;
   const float* o_lo;
+  // non-null: o / o_lo are the binary16 pair of o 2^(*o_exp) (uint16 arrays)
+  const int* o_exp;
   const float *row_max, *row_sum;
   float *doh, *dol, *delta, *lse2;
 };
@@ -309,6 +315,9 @@ struct GemmArgs {
   // format, scale and max-|x| slot of the GELU_FWD (out2/out3) or GELU_BWD
   // (C/out2) operand-pair output
   OperandScale out_sc;
+  // QKV / ATTN_DO on the pair kernel's staged epilogue: leave C unwritten
+  // (when the attention operands it writes are C's only consumers)
+  bool skip_c;
 };
 enum {
   GEMM_EPI_PLAIN = 0,

@@ -228,6 +228,16 @@ void split(et_b200_lm* lm, float* x, float* lo, size_t n) {
   split_tf32(x, x, lo, n, lm->stream);
 }
 
+// Head widths whose attention runs on the tensor-core kernels both ways.
+bool tc_attention(const et_b200_lm* lm) { return lm->Dh == 32 || lm->Dh == 64; }
+// A step that cannot be computed as enqueued fails through the device error
+// word (the host-synchronised entry points report it).
+void fail_step(const char* why) {
+  fprintf(stderr, "et_b200: %s\n", why);
+  static const int one = 1;
+  cudaMemcpy(device_error_word(), &one, sizeof(int), cudaMemcpyHostToDevice);
+}
+
 // Output format of the producer of slot s: the binary16 pair in split-f16
 // steps, and its max |x| in every step of a split-f16 model.
 OperandScale osc(et_b200_lm* lm, int s) {
@@ -267,13 +277,14 @@ void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t ro
                     int64_t dout, int wt, const float* bias, float* y,
                     int epilogue = GEMM_EPI_PLAIN, const float* aux = nullptr,
                     float* out2 = nullptr, float* out3 = nullptr, const QkvPrep* qkv = nullptr,
-                    int sa = -1, int sout = -1) {
+                    int sa = -1, int sout = -1, bool skip_c = false) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)dout; g.K = (int)din;
   g.A = x; g.A_lo = xlo; g.lda = din; g.a_kmajor = true;
   g.B = lm->W(wt); g.B_lo = lm->Wlo(wt); g.ldb = din; g.b_kmajor = true;
   g.C = y; g.ldc = dout; g.bias = bias; g.accumulate = false;
   g.epilogue = epilogue; g.aux = aux; g.out2 = out2; g.out3 = out3; g.qkv = qkv;
+  g.skip_c = skip_c;
   set16(lm, g, sa, lm->slot_w());
   if (epilogue == GEMM_EPI_GELU_FWD && sout >= 0) g.out_sc = osc(lm, sout);
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
@@ -287,7 +298,7 @@ void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int6
                         int64_t din, int64_t dout, int wt, float* dxo,
                         const float* gelu_in = nullptr, float* dxo_lo = nullptr,
                         float* dsum = nullptr, const AttnGradPrep* dprep = nullptr, int sa = -1,
-                        int sout = -1) {
+                        int sout = -1, bool skip_c = false) {
   GemmArgs g{};
   g.M = (int)rows; g.N = (int)din; g.K = (int)dout;
   g.A = dy; g.A_lo = dylo; g.lda = dout; g.a_kmajor = true;
@@ -301,6 +312,7 @@ void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int6
   if (dprep != nullptr) {
     g.epilogue = GEMM_EPI_ATTN_DO;
     g.dprep = dprep;
+    g.skip_c = skip_c;
   }
   set16(lm, g, sa, lm->slot_w());
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
@@ -364,6 +376,7 @@ void forward(et_b200_lm* lm) {
   for (int l = 0; l < lm->L; l++) {
     LayerActs& a = lm->layers[l];
     float* xnext = (l + 1 < lm->L) ? lm->layers[l + 1].x : lm->x_final;
+    bool fused_o = false;
     {
       Mark mk(lm, P_NORM, 0, 8.0 * R * d);
       // with 3xTF32 the producers write each GEMM operand as a hi/lo pair
@@ -376,16 +389,27 @@ void forward(et_b200_lm* lm) {
       AttnParams p = attn_params(lm, a.qkv, l);
       QkvPrep prep;
       p.qkv_ready = attention_qkv_prep(p, &prep) ? 1 : 0;
+      // the tensor-core attention (forward and backward) reads only the
+      // operands the epilogue writes, so the f32 qkv itself is not stored
+      const bool skip = p.qkv_ready && tc_attention(lm);
       linear_forward(lm, a.h1, a.h1lo, R, d, 3 * d, lm->lt(l, T_WQKV), lm->Pp(lm->lt(l, T_BQKV)),
                      a.qkv, p.qkv_ready ? GEMM_EPI_QKV : GEMM_EPI_PLAIN, nullptr, nullptr,
-                     nullptr, p.qkv_ready ? &prep : nullptr, lm->slot(l, S_H1));
+                     nullptr, p.qkv_ready ? &prep : nullptr, lm->slot(l, S_H1), -1, skip);
       Mark mk(lm, P_ATTN_FWD, attn_flop(lm, 2), 0);
-      lm->attn_prepared[l] =
-          attention_forward(p, AttnOut{a.ao, lm->T * d, lm->Dh, d, a.aolo}, a.am, a.al, s);
+      // split-f16 steps: the tensor-core forward writes o's binary16 pair
+      // itself; in every step of such a model it records o's max
+      const bool o16 = lm->step16 && skip;
+      AttnOut out = o16 ? AttnOut{a.ao16, lm->T * d, lm->Dh, d, half_at(a.ao16, R * d)}
+                        : AttnOut{a.ao, lm->T * d, lm->Dh, d, a.aolo};
+      if (lm->f16 && p.qkv_ready && (o16 || !lm->step16)) out.sc = osc(lm, lm->slot(l, S_AO));
+      lm->attn_prepared[l] = attention_forward(p, out, a.am, a.al, s);
+      if (skip && !lm->attn_prepared[l]) fail_step("attention forward left the tensor-core path");
+      fused_o = lm->attn_prepared[l] && out.sc.amax != nullptr;
     }
     if (lm->three && !lm->attn_prepared[l]) split(lm, a.ao, a.aolo, R * d);
-    // the output projection's operand (split-f16: the binary16 pair of o)
-    operand16(lm, a.ao, a.aolo, R * d, a.ao16, lm->slot(l, S_AO));
+    // the output projection's operand (split-f16: the binary16 pair of o),
+    // unless the attention epilogue produced it
+    if (!fused_o) operand16(lm, a.ao, a.aolo, R * d, a.ao16, lm->slot(l, S_AO));
     const float* aoh = lm->step16 ? a.ao16 : a.ao;
     const float* aol = lm->step16 ? half_at(a.ao16, R * d) : a.aolo;
     // x' = x + o Wo^T + bo (the residual add in the GEMM epilogue)
@@ -485,32 +509,51 @@ void backward(et_b200_lm* lm) {
     // operands and delta
     AttnParams p = attn_params(lm, a.qkv, l);
     p.ws_ready = lm->attn_prepared[l];
-    const AttnTensor ao{a.ao, lm->T * d, lm->Dh, d};
+    // o as the forward left it: its binary16 pair (split-f16 steps on the
+    // tensor-core path) or its TF32 pair
+    const bool o16 = lm->step16 && p.ws_ready && tc_attention(lm);
+    const AttnTensor ao{o16 ? a.ao16 : a.ao, lm->T * d, lm->Dh, d};
+    const float* ao_lo = o16 ? half_at(a.ao16, R * d) : a.aolo;
     AttnGradPrep dprep;
-    p.grad_ready = attention_grad_prep(p, ao, a.aolo, a.am, a.al, lm->delta, &dprep) ? 1 : 0;
+    p.grad_ready = attention_grad_prep(p, ao, ao_lo, a.am, a.al, lm->delta, &dprep) ? 1 : 0;
+    if (o16) dprep.o_exp = lm->sexp + lm->slot(l, S_AO);
+    if (o16 && !p.grad_ready) fail_step("attention backward cannot read a binary16 output");
+    // dO itself (dtmp) is not stored when the tensor-core backward reads only
+    // the epilogue's operands
+    const bool skip_do = p.grad_ready && p.ws_ready && tc_attention(lm);
     linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp, nullptr, nullptr, nullptr,
-                       p.grad_ready ? &dprep : nullptr, lm->slot(l, S_DXA));
+                       p.grad_ready ? &dprep : nullptr, lm->slot(l, S_DXA), -1, skip_do);
     linear_backward_dw(lm, dyh, dyl, lm->step16 ? a.ao16 : a.ao,
                        lm->step16 ? half_at(a.ao16, R * d) : a.aolo, R, d, d,
                        lm->G(lm->lt(l, T_WO)), lm->slot(l, S_DXA), lm->slot(l, S_AO));
+    bool fused_g = false;
     {
       Mark mk(lm, P_ATTN_BWD, attn_flop(lm, 4), 0);
       const int64_t w = 3 * d;
-      float* lo = lm->dqkvlo;  // null unless 3xTF32
-      // the tensor-core backward also writes per-tile column sums of dq, dk, dv
+      // the tensor-core backward also writes per-tile column sums of dq, dk,
+      // dv; in split-f16 steps it writes dqkv's binary16 pair itself, and in
+      // every step of such a model it records dqkv's max
+      const bool g16 = lm->step16 && skip_do;
+      float* base = g16 ? lm->dqkv16 : lm->dqkv;
+      float* lo = g16 ? half_at(lm->dqkv16, R * w) : lm->dqkvlo;  // null unless pairs
+      auto at = [&](float* x, int64_t e) { return x == nullptr ? nullptr : g16 ? half_at(x, e) : x + e; };
       float* cp = lm->qkv_colpart;
-      const bool tc = attention_backward(
-          p, ao, a.aolo, AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d}, a.am, a.al, lm->delta,
-          AttnOut{lm->dqkv, lm->T * w, lm->Dh, w, lo, cp, w},
-          AttnOut{lm->dqkv + d, lm->T * w, lm->Dh, w, lo ? lo + d : nullptr, cp + d, w},
-          AttnOut{lm->dqkv + 2 * d, lm->T * w, lm->Dh, w, lo ? lo + 2 * d : nullptr, cp + 2 * d, w},
-          s);
+      AttnOut dq{base, lm->T * w, lm->Dh, w, lo, cp, w};
+      AttnOut dk{at(base, d), lm->T * w, lm->Dh, w, at(lo, d), cp + d, w};
+      AttnOut dv{at(base, 2 * d), lm->T * w, lm->Dh, w, at(lo, 2 * d), cp + 2 * d, w};
+      if (lm->f16 && (g16 || !lm->step16))
+        dq.sc = dk.sc = dv.sc = osc(lm, lm->slot(l, S_DQKV));
+      const bool tc = attention_backward(p, ao, ao_lo, AttnTensor{lm->dtmp, lm->T * d, lm->Dh, d},
+                                         a.am, a.al, lm->delta, dq, dk, dv, s);
       dqkv_split = tc && three;
       bqkv_done = tc;
+      fused_g = tc && dq.sc.amax != nullptr;
+      if (skip_do && !tc) fail_step("attention backward left the tensor-core path");
     }
     if (three && !dqkv_split) split(lm, lm->dqkv, lm->dqkvlo, R * 3 * d);
-    // the QKV projection's operand (split-f16: the binary16 pair of dqkv)
-    operand16(lm, lm->dqkv, lm->dqkvlo, R * 3 * d, lm->dqkv16, lm->slot(l, S_DQKV));
+    // the QKV projection's operand (split-f16: the binary16 pair of dqkv),
+    // unless the attention epilogues produced it
+    if (!fused_g) operand16(lm, lm->dqkv, lm->dqkvlo, R * 3 * d, lm->dqkv16, lm->slot(l, S_DQKV));
     if (bqkv_done) {
       Mark mk(lm, P_ELEMENTWISE, 0, 4.0 * lm->qkv_colrows * 3 * d);
       reduce_partials(lm->qkv_colpart, (int)lm->qkv_colrows, 3 * d, 3 * d,
