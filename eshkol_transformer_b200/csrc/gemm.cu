@@ -175,12 +175,24 @@ struct TcArgs {
   // QKV / ATTN_DO: C itself is not stored (the attention operands are its
   // only consumers)
   int skip_c;
+  // GELU_FWD: C = GELU'(u) instead of u; GELU_BWD: aux holds GELU'(u)
+  int gelu_slope_c;
 };
 
 __device__ __forceinline__ float gelu_value(float v) {  // n2_primitives_provider.c:545-583
   const float inv_sqrt_2 = 0x1.6a09e6p-1f;
   const float e = erff(rn_mul(v, inv_sqrt_2));
   return rn_mul(rn_mul(0.5f, v), rn_add(1.0f, e));
+}
+// GELU(v) and GELU'(v) with one erf: the same operations as gelu_value and
+// gelu_slope, so the results are identical to theirs.
+__device__ __forceinline__ void gelu_both(float v, float& g, float& slope) {
+  const float inv_sqrt_2 = 0x1.6a09e6p-1f, inv_sqrt_2pi = 0x1.988454p-2f;
+  const float e = erff(rn_mul(v, inv_sqrt_2));
+  g = rn_mul(rn_mul(0.5f, v), rn_add(1.0f, e));
+  const float cdf = rn_mul(0.5f, rn_add(1.0f, e));
+  const float density = rn_mul(expf(-rn_mul(0.5f, rn_mul(v, v))), inv_sqrt_2pi);
+  slope = rn_add(cdf, rn_mul(v, density));
 }
 __device__ __forceinline__ float gelu_slope(float v) {
   const float inv_sqrt_2 = 0x1.6a09e6p-1f, inv_sqrt_2pi = 0x1.988454p-2f;
@@ -464,41 +476,25 @@ __device__ __forceinline__ void qkv_column(const QkvPrep& q, int n, int& sec, in
   h = hc / q.Dh;
   j = hc - h * q.Dh;
 }
-// RoPE coefficients (cos, sin of pair n / 2, cos, sin of pair n / 2 + 1) for
-// qkv columns [n, n + 4) of row `row`; unused (zeros) for V or without tables.
-// (Loading these ahead of the accumulator wait, like the aux rows, measured
-// slower.)
-__device__ __forceinline__ float4 qkv_rope_coeffs(const QkvPrep& q, int row, int n) {
-  int sec, h, j;
-  qkv_column(q, n, sec, h, j);
-  const float* ct = sec == 0 ? q.q_cos : (sec == 1 ? q.k_cos : nullptr);
-  if (ct == nullptr) return make_float4(0.f, 0.f, 0.f, 0.f);
-  const float* st = sec == 0 ? q.q_sin : q.k_sin;
-  const int batched = sec == 0 ? q.q_rope_batched : q.k_rope_batched;
-  const int b = row / q.T, t = row - b * q.T;
-  // j % 4 == 0 and Dh / 2 even: the two pairs' entries are one aligned float2
-  const int64_t ti = (int64_t)(batched ? b * q.T + t : t) * (q.Dh >> 1) + (j >> 1);
-  const float2 c = __ldg(reinterpret_cast<const float2*>(ct + ti));
-  const float2 s = __ldg(reinterpret_cast<const float2*>(st + ti));
-  return make_float4(c.x, s.x, c.y, s.y);
-}
-// Attention operands of qkv columns [n, n + 4) of row `row` (values x =
-// y + bias, as stored to C): head-major TF32 hi / lo copies, with the RoPE
-// rotation (coefficients cs from qkv_rope_coeffs) of the pairs (n, n + 1),
-// (n + 2, n + 3) for Q and K (attention_tc.cu attn_prepare_kernel computes
-// the same values).
-__device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int row, int n, float4 x,
-                                               float4 cs) {
-  int sec, h, j;
-  qkv_column(q, n, sec, h, j);
-  const int b = row / q.T, t = row - b * q.T;
+// Attention operands of qkv columns [n, n + 4) (section sec, head h, column
+// j of the head; j % 4 == 0) of token t of sequence b, from the values x = y +
+// bias as stored to C: head-major TF32 hi / lo copies, with the RoPE rotation
+// of the pairs (j, j + 1), (j + 2, j + 3) for Q and K (attention_tc.cu
+// attn_prepare_kernel computes the same values).  The host tables' two
+// entries are one aligned float2 (Dh / 2 even).
+__device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int sec, int h, int j, int b,
+                                               int t, float4 x) {
   const float* ct = sec == 0 ? q.q_cos : (sec == 1 ? q.k_cos : nullptr);
   if (ct != nullptr) {
-    const float c0 = cs.x, s0 = cs.y, c1 = cs.z, s1 = cs.w;
-    const float x0 = rn_sub(rn_mul(x.x, c0), rn_mul(x.y, s0));
-    const float x1 = rn_add(rn_mul(x.x, s0), rn_mul(x.y, c0));
-    const float x2 = rn_sub(rn_mul(x.z, c1), rn_mul(x.w, s1));
-    const float x3 = rn_add(rn_mul(x.z, s1), rn_mul(x.w, c1));
+    const float* st = sec == 0 ? q.q_sin : q.k_sin;
+    const int batched = sec == 0 ? q.q_rope_batched : q.k_rope_batched;
+    const int64_t ti = (int64_t)(batched ? b * q.T + t : t) * (q.Dh >> 1) + (j >> 1);
+    const float2 c = __ldg(reinterpret_cast<const float2*>(ct + ti));
+    const float2 s = __ldg(reinterpret_cast<const float2*>(st + ti));
+    const float x0 = rn_sub(rn_mul(x.x, c.x), rn_mul(x.y, s.x));
+    const float x1 = rn_add(rn_mul(x.x, s.x), rn_mul(x.y, c.x));
+    const float x2 = rn_sub(rn_mul(x.z, c.y), rn_mul(x.w, s.y));
+    const float x3 = rn_add(rn_mul(x.z, s.y), rn_mul(x.w, c.y));
     x = make_float4(x0, x1, x2, x3);
   }
   const int H = sec == 0 ? q.Hq : q.Hkv;
@@ -514,12 +510,11 @@ __device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int row, int n,
   *reinterpret_cast<float4*>(lo + o) = l4;
 }
 
-// dO columns [n, n + 4) of row `row` as the attention backward's head-major
-// TF32 hi / lo operands (attention_bwd_tc.cu attn_bwd_prepare_kernel writes
-// the same values).
-__device__ __forceinline__ void attn_do_store(const AttnGradPrep& g, int row, int n, float4 x) {
-  const int h = n / g.Dh, j = n - h * g.Dh;
-  const int b = row / g.T, t = row - b * g.T;
+// dO columns [j, j + 4) of head h, token t of sequence b, as the attention
+// backward's head-major TF32 hi / lo operands (attention_bwd_tc.cu
+// attn_bwd_prepare_kernel writes the same values).
+__device__ __forceinline__ void attn_do_store(const AttnGradPrep& g, int h, int j, int b, int t,
+                                              float4 x) {
   const int64_t o = (((int64_t)b * g.H + h) * g.T + t) * g.Dh + j;
   float4 h4, l4;
   tf32_split(x.x, h4.x, l4.x);
@@ -826,6 +821,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
         const uint32_t stage = smem_u32(smem + L::RING_BYTES + 256) + (uint32_t)(warp - 2) * 4096u;
         const int sub = lane >> 3, q = lane & 7;
         const int row0 = m - lane;
+        // attention-operand modes: sequence and token of row0 + sub
+        int seq0 = 0, tok0 = 0, seqT = 1;
+        if (ATTN && (epi == GEMM_EPI_QKV || epi == GEMM_EPI_ATTN_DO)) {
+          seqT = epi == GEMM_EPI_QKV ? args.qkv.T : args.dprep.T;
+          seq0 = (row0 + sub) / seqT;
+          tok0 = row0 + sub - seq0 * seqT;
+        }
         const bool has_aux = epi == GEMM_EPI_RESIDUAL || epi == GEMM_EPI_GELU_BWD;
         // ATTN_DO: per row of the warp, the running dO . O sum of the current head
         float dacc[8];
@@ -835,6 +837,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
         for (int c = col_begin; c < col_begin + BN / 2; c += 32) {
           const int n = n_tile + c + 4 * q;
           const bool col_ok = n < args.N;  // N % 4 == 0: the 4 columns are all in or all out
+          // attention-operand modes: the lane's section / head / column
+          int a_sec = 0, a_h = 0, a_j = 0;
+          if (ATTN && epi == GEMM_EPI_QKV && col_ok) qkv_column(args.qkv, n, a_sec, a_h, a_j);
+          if (ATTN && epi == GEMM_EPI_ATTN_DO) {
+            a_h = n / args.dprep.Dh;
+            a_j = n - a_h * args.dprep.Dh;
+          }
           // the auxiliary rows of the chunk, loaded before the accumulator wait
           float4 pre[8];
 #pragma unroll
@@ -890,7 +899,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               float dot = 0.0f;
               if (row < args.M && col_ok) {
                 if (!args.skip_c) *reinterpret_cast<float4*>(cbase + (int64_t)row * ldc + n) = x;
-                attn_do_store(args.dprep, row, n, x);
+                int tk = tok0 + 4 * it, sq = seq0;
+                while (tk >= seqT) { tk -= seqT; ++sq; }
+                attn_do_store(args.dprep, a_h, a_j, sq, tk, x);
                 const float4 o = pre[it];
                 dot = fmaf(x.w, o.w, fmaf(x.z, o.z, fmaf(x.y, o.y, x.x * o.x)));
               }
@@ -904,12 +915,20 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             const int64_t off = (int64_t)row * ldc + n;
             if (epi == GEMM_EPI_GELU_BWD) {
               // d = y GELU'(u), split into hi (C) and lo (out2); column sums
+              // (aux holds u, or GELU'(u) itself with gelu_slope_c)
               const float4 u4 = pre[it];
               float4 d;
-              d.x = rn_mul(x.x, gelu_slope(u4.x));
-              d.y = rn_mul(x.y, gelu_slope(u4.y));
-              d.z = rn_mul(x.z, gelu_slope(u4.z));
-              d.w = rn_mul(x.w, gelu_slope(u4.w));
+              if (args.gelu_slope_c) {
+                d.x = rn_mul(x.x, u4.x);
+                d.y = rn_mul(x.y, u4.y);
+                d.z = rn_mul(x.z, u4.z);
+                d.w = rn_mul(x.w, u4.w);
+              } else {
+                d.x = rn_mul(x.x, gelu_slope(u4.x));
+                d.y = rn_mul(x.y, gelu_slope(u4.y));
+                d.z = rn_mul(x.z, gelu_slope(u4.z));
+                d.w = rn_mul(x.w, gelu_slope(u4.w));
+              }
               cs.x += d.x; cs.y += d.y; cs.z += d.z; cs.w += d.w;
               amax = abs_max4(amax, d);
               if (out16) {
@@ -940,6 +959,31 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               const float4 o = *dst;
               x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
             }
+            if (!ATTN && epi == GEMM_EPI_GELU_FWD && args.gelu_slope_c) {
+              // C = GELU'(u) for the backward (one erf shared with GELU(u))
+              float4 g, sl;
+              gelu_both(x.x, g.x, sl.x);
+              gelu_both(x.y, g.y, sl.y);
+              gelu_both(x.z, g.z, sl.z);
+              gelu_both(x.w, g.w, sl.w);
+              *dst = sl;
+              amax = abs_max4(amax, g);
+              if (out16) {
+                f16_store4(reinterpret_cast<uint16_t*>(args.out2),
+                           reinterpret_cast<uint16_t*>(args.out3), off, g, out_s);
+              } else {
+                float4 lo = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (args.out3 != nullptr) {
+                  tf32_split(g.x, g.x, lo.x);
+                  tf32_split(g.y, g.y, lo.y);
+                  tf32_split(g.z, g.z, lo.z);
+                  tf32_split(g.w, g.w, lo.w);
+                  *reinterpret_cast<float4*>(args.out3 + off) = lo;
+                }
+                *reinterpret_cast<float4*>(args.out2 + off) = g;
+              }
+              continue;
+            }
             if (!(ATTN && args.skip_c)) *dst = x;
             if (epi == GEMM_EPI_GELU_FWD) {
               float4 g = make_float4(gelu_value(x.x), gelu_value(x.y), gelu_value(x.z),
@@ -960,7 +1004,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               }
               *reinterpret_cast<float4*>(args.out2 + off) = g;
             } else if (ATTN && epi == GEMM_EPI_QKV) {
-              qkv_prep_store(args.qkv, row, n, x, qkv_rope_coeffs(args.qkv, row, n));
+              int tk = tok0 + 4 * it, sq = seq0;
+              while (tk >= seqT) { tk -= seqT; ++sq; }
+              qkv_prep_store(args.qkv, a_sec, a_h, a_j, sq, tk, x);
             }
           }
           if (epi == GEMM_EPI_GELU_BWD) {
@@ -1314,6 +1360,7 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   a.exp_b = g.exp_b;
   a.out_sc = g.out_sc;
   a.skip_c = g.skip_c && (g.epilogue == GEMM_EPI_QKV || g.epilogue == GEMM_EPI_ATTN_DO) ? 1 : 0;
+  a.gelu_slope_c = g.gelu_slope_c ? 1 : 0;
   if (g.epilogue == GEMM_EPI_QKV) a.qkv = *g.qkv;
   if (g.epilogue == GEMM_EPI_ATTN_DO) a.dprep = *g.dprep;
   {
@@ -1326,7 +1373,7 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   }
   // split-f16 operand-pair outputs and their max |x| come from the staged epilogue only
   const bool pair_out = g.epilogue == GEMM_EPI_GELU_FWD || g.epilogue == GEMM_EPI_GELU_BWD;
-  if (!a.staged && pair_out && (g.out_sc.f16 || g.out_sc.amax != nullptr)) {
+  if (!a.staged && pair_out && (g.out_sc.f16 || g.out_sc.amax != nullptr || g.gelu_slope_c)) {
     gemm_f16_refused(g, "unstaged epilogue");
     return;
   }
@@ -1417,6 +1464,10 @@ void gemm(const GemmArgs& g, int precision, cudaStream_t stream) {
   const bool pair = three && gemm_tc_supported(g) && g.A_lo != nullptr && g.B_lo != nullptr;
   if (pair) {
     gemm_tc(g, true, stream);  // the pair kernel applies every epilogue mode itself
+    return;
+  }
+  if (g.gelu_slope_c) {  // GELU'(u) in C exists on the pair kernel only
+    gemm_f16_refused(g, "GELU slope output");
     return;
   }
   GemmArgs plain = g;

@@ -318,6 +318,9 @@ struct GemmArgs {
   // QKV / ATTN_DO on the pair kernel's staged epilogue: leave C unwritten
   // (when the attention operands it writes are C's only consumers)
   bool skip_c;
+  // GELU_FWD: C receives GELU'(u) instead of u; GELU_BWD: aux is GELU'(u)
+  // (pair kernel's staged epilogue only)
+  bool gelu_slope_c;
 };
 enum {
   GEMM_EPI_PLAIN = 0,

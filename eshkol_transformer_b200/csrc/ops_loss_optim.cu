@@ -3,11 +3,12 @@
 //
 // Cross-entropy follows native/indexed_cross_entropy.c:109-280: per row the
 // maximum m, s = sum exp(x - m), loss = log(s) + (m - x[target]) and the
-// gradient u (exp(x - m) / s - [j == target]).  One CTA owns one row: the
-// first sweep forms per-thread online (max, sum) pairs from 128-bit loads, a
-// block reduction combines them, and the second sweep re-reads the row (an L2
-// hit: the rows in flight occupy far less than the 126 MB L2) and writes the
-// gradient, so HBM sees one read and one write per logit.
+// gradient u (exp(x - m) / s - [j == target]), here exp(x - m) (1 / s).  One
+// CTA owns one row: the first sweep forms per-thread online (max, sum) pairs
+// from 128-bit loads (one maximum update per 4 values), a block reduction
+// combines them, and the second sweep re-reads the row (an L2 hit: the rows in
+// flight occupy far less than the 126 MB L2) and writes the gradient, so HBM
+// sees one read and one write per logit.
 //
 // AdamW follows native/o2_optimizer.c:1738-1756 with every operation rounded
 // separately (no contraction), which makes each updated parameter and moment
@@ -52,11 +53,14 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
     const float4* x4 = reinterpret_cast<const float4*>(x);
     const int64_t n4 = V >> 2;
     for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
+      // one running-maximum update per 4 values, then their 4 exponentials
       const float4 v = __ldg(x4 + i);
-      online_push(v.x, m, s);
-      online_push(v.y, m, s);
-      online_push(v.z, m, s);
-      online_push(v.w, m, s);
+      const float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      if (mx > m) {
+        s = s * expf(m - mx);
+        m = mx;
+      }
+      s += (expf(v.x - m) + expf(v.y - m)) + (expf(v.z - m) + expf(v.w - m));
     }
   } else {
     for (int64_t i = threadIdx.x; i < V; i += blockDim.x) online_push(__ldg(x + i), m, s);
@@ -69,6 +73,7 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
   if (threadIdx.x == 0 && loss != nullptr) loss[row] = logf(row_sum) + (row_max - x_target);
   if (dlogits == nullptr) return;
   const float u = upstream != nullptr ? upstream[row] : upstream_scale;
+  const float inv_sum = rn_div(1.0f, row_sum);  // softmax = exp(x - max) * (1 / sum)
   float* g = dlogits + row * V;
   // split-f16: dlogits / dlo hold binary16 hi / lo of the gradient 2^e
   const float s16 = sc.f16 ? exp2_int(*sc.exp) : 1.0f;
@@ -83,10 +88,10 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
       const float4 v = x4[i];  // plain load: dlogits may alias logits
       float4 r;
       const int64_t j = i << 2;
-      r.x = u * (rn_div(expf(v.x - row_max), row_sum) - (j + 0 == target ? 1.0f : 0.0f));
-      r.y = u * (rn_div(expf(v.y - row_max), row_sum) - (j + 1 == target ? 1.0f : 0.0f));
-      r.z = u * (rn_div(expf(v.z - row_max), row_sum) - (j + 2 == target ? 1.0f : 0.0f));
-      r.w = u * (rn_div(expf(v.w - row_max), row_sum) - (j + 3 == target ? 1.0f : 0.0f));
+      r.x = u * (rn_mul(expf(v.x - row_max), inv_sum) - (j + 0 == target ? 1.0f : 0.0f));
+      r.y = u * (rn_mul(expf(v.y - row_max), inv_sum) - (j + 1 == target ? 1.0f : 0.0f));
+      r.z = u * (rn_mul(expf(v.z - row_max), inv_sum) - (j + 2 == target ? 1.0f : 0.0f));
+      r.w = u * (rn_mul(expf(v.w - row_max), inv_sum) - (j + 3 == target ? 1.0f : 0.0f));
       amax = abs_max4(amax, r);
       if (sc.f16) {
         f16_store4(gh, gl, j, r, s16);
@@ -105,7 +110,7 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
   } else {
     for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
       const float v = x[j];
-      float r = u * (rn_div(expf(v - row_max), row_sum) - (j == target ? 1.0f : 0.0f));
+      float r = u * (rn_mul(expf(v - row_max), inv_sum) - (j == target ? 1.0f : 0.0f));
       amax = fmaxf(amax, fabsf(r));
       if (sc.f16) {
         f16_split(r * s16, gh[j], gl[j]);

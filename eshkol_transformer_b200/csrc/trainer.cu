@@ -287,6 +287,8 @@ void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t ro
   g.skip_c = skip_c;
   set16(lm, g, sa, lm->slot_w());
   if (epilogue == GEMM_EPI_GELU_FWD && sout >= 0) g.out_sc = osc(lm, sout);
+  // split-f16 models keep GELU'(u) (not u) for the backward's epilogue
+  if (epilogue == GEMM_EPI_GELU_FWD) g.gelu_slope_c = lm->f16;
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->gprec, lm->stream);
 }
@@ -308,6 +310,7 @@ void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int6
     g.epilogue = GEMM_EPI_GELU_BWD; g.aux = gelu_in; g.out2 = dxo_lo; g.dsum = dsum;
     g.epi_ws = lm->epi_ws;
     if (sout >= 0) g.out_sc = osc(lm, sout);
+    g.gelu_slope_c = lm->f16;  // gelu_in holds GELU'(u)
   }
   if (dprep != nullptr) {
     g.epilogue = GEMM_EPI_ATTN_DO;
