@@ -2,7 +2,9 @@
 
 Workload: the medium decoder LM (12 layers, d_model 1024, 16 heads, FFN 4096,
 vocab 32768, seq 1024) at a fixed global batch of 64 sequences (65,536
-tokens per step), 3xTF32 contractions with f32 master weights and AdamW;
+tokens per step), f32-grade contractions (split-f16 binary16 hi/lo operand
+pairs by default, 3xTF32 with --contractions tf32x3), f32 master weights and
+AdamW;
 synthetic uniform tokens from a seed, N(0, 0.02) weights.  One step is
 forward + backward (+ NCCL gradient allreduce across ranks) + AdamW.
 
