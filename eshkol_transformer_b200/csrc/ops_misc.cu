@@ -66,6 +66,81 @@ ln_forward_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
   }
 }
 
+// Register-row variant for d = 128 NV (d <= 1024): one warp per row, lane l
+// holding columns 4 l + 128 i (float4), so the row is read from HBM once with
+// 128-bit loads and the mean / variance / output sweeps run from registers;
+// outputs leave as float4 (f32, TF32 pair) or 8-byte binary16 quads.  Same
+// per-element arithmetic as ln_forward_kernel; the row sums add in the lane
+// order of this layout.
+template <int NV>
+__global__ void __launch_bounds__(kLnWarps * 32)
+ln_forward_rows_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                       const float* __restrict__ beta, float epsilon, float* __restrict__ y,
+                       float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t rows,
+                       float* __restrict__ y_lo, OperandScale sc) {
+  constexpr int D = 128 * NV;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * D);
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) v[i] = __ldg(xr + lane + 32 * i);
+  const float dim = (float)D;
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    s += v[i].x; s += v[i].y; s += v[i].z; s += v[i].w;
+  }
+  s = warp_sum(s);
+  const float mean = rn_div(s, dim);
+  float var = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    float dlt;
+    dlt = rn_sub(v[i].x, mean); var += rn_mul(dlt, dlt);
+    dlt = rn_sub(v[i].y, mean); var += rn_mul(dlt, dlt);
+    dlt = rn_sub(v[i].z, mean); var += rn_mul(dlt, dlt);
+    dlt = rn_sub(v[i].w, mean); var += rn_mul(dlt, dlt);
+  }
+  var = warp_sum(var);
+  const float variance = rn_div(var, dim);
+  const float rstd = rn_div(1.0f, rn_sqrt(rn_add(variance, epsilon)));
+  const float s16 = sc.f16 ? exp2_int(*sc.exp) : 1.0f;
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const int c = lane + 32 * i;
+    const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + c);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(beta) + c);
+    float4 o;
+    o.x = rn_add(rn_mul(rn_mul(rn_sub(v[i].x, mean), rstd), g.x), b.x);
+    o.y = rn_add(rn_mul(rn_mul(rn_sub(v[i].y, mean), rstd), g.y), b.y);
+    o.z = rn_add(rn_mul(rn_mul(rn_sub(v[i].z, mean), rstd), g.z), b.z);
+    o.w = rn_add(rn_mul(rn_mul(rn_sub(v[i].w, mean), rstd), g.w), b.w);
+    amax = abs_max4(amax, o);
+    const int64_t off = row * D + 4 * c;
+    if (sc.f16) {
+      f16_store4(reinterpret_cast<uint16_t*>(y), reinterpret_cast<uint16_t*>(y_lo), off, o, s16);
+    } else if (y_lo != nullptr) {
+      float4 l;
+      tf32_split(o.x, o.x, l.x);
+      tf32_split(o.y, o.y, l.y);
+      tf32_split(o.z, o.z, l.z);
+      tf32_split(o.w, o.w, l.w);
+      *reinterpret_cast<float4*>(y + off) = o;
+      *reinterpret_cast<float4*>(y_lo + off) = l;
+    } else {
+      *reinterpret_cast<float4*>(y + off) = o;
+    }
+  }
+  if (sc.amax != nullptr) amax_record_warp(sc.amax, amax);
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = rstd;
+  }
+}
+
 int ln_backward_blocks(size_t rows) {
   const size_t want = (rows + kLnWarps - 1) / kLnWarps;
   const size_t cap = (size_t)sm_count() * 4;
@@ -615,6 +690,23 @@ void layer_norm_forward(const float* x, const float* gamma, const float* beta, f
                         float* y, float* mean, float* rstd, size_t rows, size_t d,
                         cudaStream_t stream, float* y_lo, OperandScale sc) {
   if (rows == 0) return;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(y_lo) | reinterpret_cast<uintptr_t>(gamma) |
+                         reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
+  if (aligned && d % 128 == 0 && d <= 1024) {
+    switch (d / 128) {
+#define LNF_CASE(nv)                                                                        \
+  case nv:                                                                                  \
+    ln_forward_rows_kernel<nv><<<ceil_div(rows, kLnWarps), kLnWarps * 32, 0, stream>>>(      \
+        x, gamma, beta, epsilon, y, mean, rstd, (int64_t)rows, y_lo, sc);                   \
+    break;
+      LNF_CASE(1) LNF_CASE(2) LNF_CASE(3) LNF_CASE(4) LNF_CASE(5) LNF_CASE(6) LNF_CASE(7)
+      LNF_CASE(8)
+#undef LNF_CASE
+    }
+    count_launch();
+    return;
+  }
   ln_forward_kernel<<<ceil_div(rows, kLnWarps), kLnWarps * 32, 0, stream>>>(
       x, gamma, beta, epsilon, y, mean, rstd, (int64_t)rows, (int64_t)d, y_lo, sc);
   count_launch();

@@ -4,7 +4,10 @@ library (one process per GPU).
 Each rank runs half of the tiny LM's batch with the CE weight of the global
 token count; after the bucketed allreduce every rank must hold the full-batch
 gradients (oracle, per-tensor normwise 5e-5), and after the AdamW step both
-ranks' weights must be bit-identical.  Skips on hosts with fewer than 2 GPUs.
+ranks' weights must be bit-identical.  Split-f16 runs a first (3xTF32,
+scale-measuring) pass, then the split-f16 pass that is compared; its
+operand-range flag rides the last gradient reduction, so both ranks take
+the same decision.  Skips on hosts with fewer than 2 GPUs.
 """
 import os
 import socket
@@ -23,7 +26,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, out_dir):
+def _rank(rank, world, port, out_dir, precision):
     import sys
     from pathlib import Path
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
@@ -38,7 +41,7 @@ def _rank(rank, world, port, out_dir):
     s = etb.TINY
     per = s.batch // world
     shape = etb.ModelShape(s.layers, s.d_model, s.heads, s.ffn, s.vocabulary, s.seq_len, per)
-    model = etb.LanguageModel(shape, global_tokens=s.batch * s.seq_len)
+    model = etb.LanguageModel(shape, precision=precision, global_tokens=s.batch * s.seq_len)
     model.init(4321)
     uid = [etb.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
@@ -46,7 +49,10 @@ def _rank(rank, world, port, out_dir):
     ids, targets = orc.synthetic_batch(31, s.batch, s.seq_len, s.vocabulary)
     mine = slice(rank * per, (rank + 1) * per)
     model.forward_backward(ids[mine], targets[mine])
+    if precision == etb.PRECISION_F16X3:
+        model.forward_backward(ids[mine], targets[mine])
     np.save(os.path.join(out_dir, f"grads{rank}.npy"), model.read(1))
+    model.step(ids[mine], targets[mine])
     model.step(ids[mine], targets[mine])
     np.save(os.path.join(out_dir, f"params{rank}.npy"), model.read(0))
     model.close()
@@ -54,12 +60,13 @@ def _rank(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_two_gpu_allreduce_matches_full_batch(tmp_path):
+@pytest.mark.parametrize("precision", [0, 3])  # PRECISION_TF32X3, PRECISION_F16X3
+def test_two_gpu_allreduce_matches_full_batch(tmp_path, precision):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import eshkol_transformer_b200 as etb
     from oracle import oracle as orc
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), precision), nprocs=2,
                        start_method="spawn")
     s = etb.TINY
     om = orc.LanguageModel(s.layers, s.d_model, s.heads, s.ffn, s.vocabulary, s.seq_len, s.batch)
