@@ -74,6 +74,7 @@ def load() -> C.CDLL:
         "et_b200_lm_profile_v1": (C.c_int32, [C.c_void_p, C.c_int32]),
         "et_b200_lm_profile_collect_v1": (C.c_int32, [C.c_void_p]),
         "et_b200_lm_profile_read_v1": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_size_t]),
+        "et_b200_lm_f16_redone_steps_v1": (C.c_int32, [C.c_void_p]),
         "et_b200_o2_optimizer_create_v1": (C.c_int32, [C.c_size_t, C.c_void_p, C.c_uint32,
                                                        C.c_uint32, C.c_uint32, C.c_uint64,
                                                        C.c_uint64, C.c_uint32,
@@ -220,6 +221,10 @@ class LanguageModel:
         err = k1.KernelError()
         _check(self.lib.et_b200_lm_enable_data_parallel_v1(self.handle, buf, rank, world,
                                                            C.byref(err)), err)
+
+    def f16_redone_steps(self) -> int:
+        """Split-f16 steps redone in 3xTF32 after an operand overflow."""
+        return self.lib.et_b200_lm_f16_redone_steps_v1(self.handle)
 
     def profile(self, enable: bool) -> None:
         self.lib.et_b200_lm_profile_v1(self.handle, 1 if enable else 0)

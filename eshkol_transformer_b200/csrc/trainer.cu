@@ -47,7 +47,10 @@ namespace {
 enum { kPerLayer = 12 };
 // split-f16 operand slots of one layer
 enum { S_H1 = 0, S_AO, S_H2, S_G, S_DXF, S_DU, S_DXA, S_DQKV, kSlotsPerLayer };
-// a slot's max |x| 2^e lands in [2^(target-1), 2^target)
+// a slot's max |x| 2^e lands in [2^(target-1), 2^target): 64x below
+// binary16's overflow.  ET_B200_F16_SCALE_TARGET (2 .. 17) overrides it; 17
+// puts every slot's max above 65,504, which exercises the overflow check and
+// the 3xTF32 redo.
 constexpr int kScaleTarget = 10;
 enum {
   T_LN1G = 0, T_LN1B, T_WQKV, T_BQKV, T_WO, T_BO, T_LN2G, T_LN2B, T_W1, T_B1, T_W2, T_B2
@@ -88,6 +91,8 @@ struct et_b200_lm {
   // whether whi / wlo hold the weights' binary16 pair
   bool f16 = false, calibrated = false, step16 = false, w16_valid = false;
   int nslots = 0;
+  int scale_target = kScaleTarget;
+  int redone_steps = 0;       // split-f16 steps redone in 3xTF32 (host-synchronised calls)
   int* sexp = nullptr;        // per slot exponent e
   unsigned* samax = nullptr;  // per slot max |x| (f32 bits)
   float* dqkv16 = nullptr;    // binary16 hi then lo of dqkv
@@ -615,7 +620,7 @@ void weight_scale(et_b200_lm* lm) {
   unsigned* am = lm->samax + lm->slot_w();
   cudaMemsetAsync(am, 0, sizeof(unsigned), lm->stream);
   abs_max(lm->params, lm->P, am, lm->stream);
-  scale_from_amax(am, lm->sexp + lm->slot_w(), 1, kScaleTarget, 1, lm->stream);
+  scale_from_amax(am, lm->sexp + lm->slot_w(), 1, lm->scale_target, 1, lm->stream);
 }
 
 // Operand formats for the step about to be enqueued (split-f16 models):
@@ -627,7 +632,7 @@ void begin_step(et_b200_lm* lm) {
   cudaMemsetAsync(lm->grads + lm->P, 0, sizeof(float), lm->stream);  // range flag
   if (lm->step16) {
     // exponents of the activation / gradient slots from the last step's maxima
-    scale_from_amax(lm->samax, lm->sexp, lm->slot_w(), kScaleTarget, 1, lm->stream);
+    scale_from_amax(lm->samax, lm->sexp, lm->slot_w(), lm->scale_target, 1, lm->stream);
     if (!lm->w16_valid) {
       Mark mk(lm, P_SPLIT, 0, 8.0 * lm->P);
       weight_scale(lm);
@@ -754,6 +759,7 @@ int32_t run_host_step(et_b200_lm* lm, bool update, float* host_loss, et_kernel_e
       return 0;
     }
     lm->calibrated = false;
+    lm->redone_steps++;
     if (update) lm->updates -= 1;
   }
   return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
@@ -815,6 +821,10 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   // LayerNorm backward; other shapes run the whole step 3xTF32
   lm->f16 = c->precision == ET_B200_PRECISION_F16X3 && c->d_model % 128 == 0 &&
             c->d_model <= 1024 && c->ffn % 8 == 0 && c->vocabulary % 8 == 0;
+  if (const char* t = getenv("ET_B200_F16_SCALE_TARGET")) {
+    const int v = atoi(t);
+    if (v >= 2 && v <= 17) lm->scale_target = v;
+  }
   tensor_sizes(*c, lm->sz);
   lm->off.resize(lm->sz.size());
   size_t total = 0;
@@ -1166,6 +1176,10 @@ int32_t et_b200_lm_profile_collect_v1(et_b200_lm* lm) {
   if (!lm) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
   collect_profile(lm);
   return 0;
+}
+
+int32_t et_b200_lm_f16_redone_steps_v1(const et_b200_lm* lm) {
+  return lm ? lm->redone_steps : 0;
 }
 
 int32_t et_b200_lm_profile_read_v1(et_b200_lm* lm, double* out, size_t count) {

@@ -245,6 +245,11 @@ int32_t et_b200_lm_enable_data_parallel_v1(et_b200_lm *lm,
 int32_t et_b200_lm_profile_v1(et_b200_lm *lm, int32_t enable);
 int32_t et_b200_lm_profile_collect_v1(et_b200_lm *lm);
 int32_t et_b200_lm_profile_read_v1(et_b200_lm *lm, double *out, size_t count);
+/* Split-f16 models (ET_B200_PRECISION_F16X3): how many steps of the
+ * host-synchronised calls had an operand reach binary16's overflow and were
+ * redone with 3xTF32 contractions since the model was created (0 for other
+ * modes).  No reference counterpart: the reference has one contraction mode. */
+int32_t et_b200_lm_f16_redone_steps_v1(const et_b200_lm *lm);
 
 /* ------------------------------------------------------------ A2 KV cache
  *

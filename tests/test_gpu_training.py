@@ -146,6 +146,32 @@ def test_tiny_lm_training_trajectory_vs_oracle(lib, cuda, precision):
     model.close()
 
 
+def test_split_f16_overflow_is_redone_in_3xtf32(lib, cuda, monkeypatch):
+    """The operand-overflow path of split-f16, without any GPU fault: with
+    the scale target at 17 every operand's max lands above binary16's largest
+    finite value, so each split-f16 step overflows.  The check after the
+    backward must catch it, AdamW must skip the update, and the host call must
+    redo the step in 3xTF32: the loss trajectory then still follows the
+    oracle (2e-5 relative) and every step after the first is counted."""
+    monkeypatch.setenv("ET_B200_F16_SCALE_TARGET", "17")
+    s = TINY
+    om = _oracle_model()
+    params = om.init(99)
+    m = np.zeros_like(params)
+    v = np.zeros_like(params)
+    opts = orc.adamw_options(1e-3, 0.9, 0.999, 1e-8, 0.01)
+    model = etb.LanguageModel(s, precision=etb.PRECISION_F16X3)
+    model.init(99)
+    for step in range(1, 4):
+        ids, targets = orc.synthetic_batch(1000 + step, s.batch, s.seq_len, s.vocabulary)
+        loss_ref, grads_ref = om.forward_backward(params, ids, targets)
+        assert om.adamw(params, grads_ref, m, v, opts, step) == 0
+        loss = model.step(ids, targets)
+        assert abs(loss - loss_ref) <= 2e-5 * abs(loss_ref), (step, loss, loss_ref)
+    assert model.f16_redone_steps() == 2  # step 1 measures the scales in 3xTF32
+    model.close()
+
+
 def test_step_rejects_out_of_range_ids(lib, cuda):
     s = TINY
     model = etb.LanguageModel(s)
