@@ -118,5 +118,35 @@ def test_reference_k1_runtime_discovers_b200_providers(lib):
 
 def test_k1_precision_setter(lib):
     assert lib.et_b200_k1_precision_v1(etb.PRECISION_F32) == 0
+    assert lib.et_b200_k1_precision_v1(etb.PRECISION_F16X3) == 0
+    assert lib.et_b200_k1_precision_v1(4) != 0
     assert lib.et_b200_k1_precision_v1(9) != 0
     assert lib.et_b200_k1_precision_v1(etb.PRECISION_TF32X3) == 0
+
+
+@pytest.mark.parametrize("precision,rejected", [(4, True), (99, True), (etb.PRECISION_F16X3, False)])
+def test_lm_create_validates_contraction_mode_before_the_device(lib, precision, rejected):
+    """The model's configuration is checked on the host before any device
+    work: an unknown contraction mode is a shape/config error, while the
+    split-f16 mode passes validation (and here, without a GPU, then fails on
+    the device check instead)."""
+    s = etb.TINY
+    cfg = etb.LMConfig(C.sizeof(etb.LMConfig), s.layers, s.d_model, s.heads, s.ffn, s.vocabulary,
+                       s.seq_len, s.batch, 0, etb.f32_bits(1e-5), precision, 10000.0,
+                       etb.f32_bits(1e-3), etb.f32_bits(0.9), etb.f32_bits(0.999),
+                       etb.f32_bits(1e-8), etb.f32_bits(0.01), 0)
+    handle = C.c_void_p()
+    err = k1.KernelError()
+    rc = lib.et_b200_lm_create_v1(C.byref(cfg), C.byref(handle), C.byref(err))
+    shape_error = rc == k1.ERROR_SHAPE_MISMATCH and err.code == 12  # INVALID_SHAPE (kernel_abi.h)
+    if rejected:
+        assert shape_error, (rc, err.category, err.code)
+        assert handle.value is None
+    else:
+        assert not shape_error
+        if rc == 0:  # a GPU is present after all
+            lib.et_b200_lm_destroy_v1(C.byref(handle))
+
+
+def test_f16_redone_steps_of_no_model_is_zero(lib):
+    assert lib.et_b200_lm_f16_redone_steps_v1(None) == 0
