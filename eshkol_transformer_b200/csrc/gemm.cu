@@ -616,13 +616,19 @@ struct Tc2Layout {
   static constexpr uint32_t TMEM_COLS = 2 * BN;  static_assert(SMEM_BYTES <= 232448, "shared memory above the 227 KB per-CTA limit");
 };
 
-// ATTN: the instance that also carries the attention-operand epilogues
-// (QKV, ATTN_DO); the other modes use the lighter instance (fewer registers).
-template <int BN, int STAGES, bool ATTN>
+// EPI: the fused epilogue mode this instance carries besides plain and
+// residual (GEMM_EPI_PLAIN: none).  One instance per mode keeps each kernel's
+// code (and registers) to what its epilogue needs: the epilogue warps' loop
+// is unrolled, and a kernel holding every mode overflowed the instruction
+// cache (ncu: "no_instruction" stalls).
+template <int BN, int STAGES, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb_lo,
                 TcArgs args) {
+  constexpr bool ATTN = EPI == GEMM_EPI_QKV || EPI == GEMM_EPI_ATTN_DO;
+  constexpr bool K_QKV = EPI == GEMM_EPI_QKV, K_DO = EPI == GEMM_EPI_ATTN_DO;
+  constexpr bool K_GF = EPI == GEMM_EPI_GELU_FWD, K_GB = EPI == GEMM_EPI_GELU_BWD;
   using L = Tc2Layout<BN, STAGES>;
   constexpr int BK = L::BK;
   extern __shared__ uint8_t smem_raw[];
@@ -788,7 +794,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
     const float out_s = out16 ? exp2_int(*args.out_sc.exp) : 1.0f;
     // ATTN_DO with o as a binary16 pair: its scale 2^-e
     const float o_inv =
-        (ATTN && args.dprep.o_exp != nullptr) ? exp2_int(-*args.dprep.o_exp) : 1.0f;
+        (K_DO && args.dprep.o_exp != nullptr) ? exp2_int(-*args.dprep.o_exp) : 1.0f;
     float amax = 0.0f;  // max |x| of the operand-pair output this warp wrote
     for (int unit = cluster; unit < units; unit += nclusters) {
       const int tile = unit % tiles, split = unit / tiles;
@@ -808,7 +814,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       const float* bias = part ? nullptr : args.bias;
       const int accumulate = part ? 0 : args.accumulate;
       int epi = part ? 0 : args.epilogue;
-      if (!ATTN && (epi == GEMM_EPI_QKV || epi == GEMM_EPI_ATTN_DO)) epi = GEMM_EPI_PLAIN;
+      if (epi != GEMM_EPI_PLAIN && epi != GEMM_EPI_RESIDUAL && epi != EPI) epi = GEMM_EPI_PLAIN;
       const int64_t roff = (int64_t)m * ldc;
       const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0);
       // the warp's column-partial row of the GELU_BWD mode
@@ -828,7 +834,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
           seq0 = (row0 + sub) / seqT;
           tok0 = row0 + sub - seq0 * seqT;
         }
-        const bool has_aux = epi == GEMM_EPI_RESIDUAL || epi == GEMM_EPI_GELU_BWD;
+        const bool has_aux = epi == GEMM_EPI_RESIDUAL || (K_GB && epi == GEMM_EPI_GELU_BWD);
         // ATTN_DO: per row of the warp, the running dO . O sum of the current head
         float dacc[8];
 #pragma unroll
@@ -839,8 +845,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
           const bool col_ok = n < args.N;  // N % 4 == 0: the 4 columns are all in or all out
           // attention-operand modes: the lane's section / head / column
           int a_sec = 0, a_h = 0, a_j = 0;
-          if (ATTN && epi == GEMM_EPI_QKV && col_ok) qkv_column(args.qkv, n, a_sec, a_h, a_j);
-          if (ATTN && epi == GEMM_EPI_ATTN_DO) {
+          if (K_QKV && epi == GEMM_EPI_QKV && col_ok) qkv_column(args.qkv, n, a_sec, a_h, a_j);
+          if (K_DO && epi == GEMM_EPI_ATTN_DO) {
             a_h = n / args.dprep.Dh;
             a_j = n - a_h * args.dprep.Dh;
           }
@@ -852,7 +858,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             pre[it] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (has_aux && row < args.M && col_ok)
               pre[it] = __ldg(reinterpret_cast<const float4*>(args.aux + (int64_t)row * ldc + n));
-            if (ATTN && epi == GEMM_EPI_ATTN_DO && row < args.M && col_ok) {
+            if (K_DO && epi == GEMM_EPI_ATTN_DO && row < args.M && col_ok) {
               // the forward output o = hi + lo (exact), same layout as dO
               const int64_t oo = (int64_t)row * (args.dprep.H * args.dprep.Dh) + n;
               if (args.dprep.o_exp != nullptr) {  // binary16 pair of o 2^e
@@ -893,7 +899,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             const int r = 4 * it + sub;
             float4 x = lds128(stage + (uint32_t)r * 128u + (((uint32_t)q ^ (uint32_t)(r & 7)) << 4));
             const int row = row0 + r;
-            if (ATTN && epi == GEMM_EPI_ATTN_DO) {
+            if (K_DO && epi == GEMM_EPI_ATTN_DO) {
               // C = dO, its head-major hi / lo copies, and the row's dO . O over
               // these 32 columns (summed over the 8 lanes of the row)
               float dot = 0.0f;
@@ -913,7 +919,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             }
             if (row >= args.M || !col_ok) continue;
             const int64_t off = (int64_t)row * ldc + n;
-            if (epi == GEMM_EPI_GELU_BWD) {
+            if (K_GB && epi == GEMM_EPI_GELU_BWD) {
               // d = y GELU'(u), split into hi (C) and lo (out2); column sums
               // (aux holds u, or GELU'(u) itself with gelu_slope_c)
               const float4 u4 = pre[it];
@@ -959,7 +965,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               const float4 o = *dst;
               x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
             }
-            if (!ATTN && epi == GEMM_EPI_GELU_FWD && args.gelu_slope_c) {
+            if (K_GF && epi == GEMM_EPI_GELU_FWD && args.gelu_slope_c) {
               // C = GELU'(u) for the backward (one erf shared with GELU(u))
               float4 g, sl;
               gelu_both(x.x, g.x, sl.x);
@@ -985,7 +991,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               continue;
             }
             if (!(ATTN && args.skip_c)) *dst = x;
-            if (epi == GEMM_EPI_GELU_FWD) {
+            if (K_GF && epi == GEMM_EPI_GELU_FWD) {
               float4 g = make_float4(gelu_value(x.x), gelu_value(x.y), gelu_value(x.z),
                                      gelu_value(x.w));
               amax = abs_max4(amax, g);
@@ -1003,13 +1009,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
                 *reinterpret_cast<float4*>(args.out3 + off) = lo;
               }
               *reinterpret_cast<float4*>(args.out2 + off) = g;
-            } else if (ATTN && epi == GEMM_EPI_QKV) {
+            } else if (K_QKV && epi == GEMM_EPI_QKV) {
               int tk = tok0 + 4 * it, sq = seq0;
               while (tk >= seqT) { tk -= seqT; ++sq; }
               qkv_prep_store(args.qkv, a_sec, a_h, a_j, sq, tk, x);
             }
           }
-          if (epi == GEMM_EPI_GELU_BWD) {
+          if (K_GB && epi == GEMM_EPI_GELU_BWD) {
             // rows sub, sub + 4, ... summed per lane; then over the 4 lanes of a column group
 #pragma unroll
             for (int o = 8; o <= 16; o <<= 1) {
@@ -1020,7 +1026,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             }
             if (sub == 0 && col_ok) *reinterpret_cast<float4*>(colpart + n) = cs;
           }
-          if (ATTN && epi == GEMM_EPI_ATTN_DO && (n_tile + c + 32) % args.dprep.Dh == 0) {
+          if (K_DO && epi == GEMM_EPI_ATTN_DO && (n_tile + c + 32) % args.dprep.Dh == 0) {
             // the chunk completes a head: one lane per row writes its delta and
             // its base-2 log-sum-exp (the attention backward's formula)
             const int h = (n_tile + c) / args.dprep.Dh;
@@ -1056,7 +1062,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
         const int n0 = n_tile + c;
         const bool row_ok = m < args.M;
         const bool full = vec && n0 + 32 <= args.N;
-        if (epi == GEMM_EPI_GELU_BWD) {
+        if (K_GB && epi == GEMM_EPI_GELU_BWD) {
           // d = y GELU'(u); the columns' partial sums include every row of the warp
           float d[32];
 #pragma unroll
@@ -1104,7 +1110,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               r.x += o.x; r.y += o.y; r.z += o.z; r.w += o.w;
             }
             *dst = r;
-            if (epi == GEMM_EPI_GELU_FWD) {
+            if (K_GF && epi == GEMM_EPI_GELU_FWD) {
               float4 g = make_float4(gelu_value(r.x), gelu_value(r.y), gelu_value(r.z),
                                      gelu_value(r.w));
               if (args.out3 != nullptr) {
@@ -1128,7 +1134,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               if (epi == GEMM_EPI_RESIDUAL) r = rn_add(r, args.aux[roff + n]);
               else if (accumulate) r += cbase[roff + n];
               cbase[roff + n] = r;
-              if (epi == GEMM_EPI_GELU_FWD) {
+              if (K_GF && epi == GEMM_EPI_GELU_FWD) {
                 float gv = gelu_value(r), lo = 0.0f;
                 if (args.out3 != nullptr) tf32_split(gv, gv, lo);
                 args.out2[roff + n] = gv;
@@ -1338,9 +1344,15 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
     gemm_simt(g, stream);
     return;
   }
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, false>,
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_PLAIN>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, true>,
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_GELU_FWD>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_GELU_BWD>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_QKV>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_ATTN_DO>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
   TcArgs a{};
   a.M = g.M; a.N = g.N; a.K = g.K;
@@ -1404,12 +1416,21 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   }
   const int units = tiles * a.splits;
   const int grid = 2 * (units < pairs ? units : pairs);
-  if (a.epilogue == GEMM_EPI_QKV || a.epilogue == GEMM_EPI_ATTN_DO)
-    gemm_tc2_kernel<BN, STAGES, true><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(
-        ta, ta_lo, tb, tb_lo, a);
-  else
-    gemm_tc2_kernel<BN, STAGES, false><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(
-        ta, ta_lo, tb, tb_lo, a);
+  switch (a.epilogue) {
+#define TC2_LAUNCH(mode)                                                                   \
+  case mode:                                                                               \
+    gemm_tc2_kernel<BN, STAGES, mode><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(        \
+        ta, ta_lo, tb, tb_lo, a);                                                          \
+    break;
+    TC2_LAUNCH(GEMM_EPI_GELU_FWD)
+    TC2_LAUNCH(GEMM_EPI_GELU_BWD)
+    TC2_LAUNCH(GEMM_EPI_QKV)
+    TC2_LAUNCH(GEMM_EPI_ATTN_DO)
+#undef TC2_LAUNCH
+    default:  // plain and residual
+      gemm_tc2_kernel<BN, STAGES, GEMM_EPI_PLAIN><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(
+          ta, ta_lo, tb, tb_lo, a);
+  }
   count_launch();
   if (g.epilogue == GEMM_EPI_GELU_BWD) {
     reduce_partials(g.epi_ws, a.tiles_m * 8, g.N, g.N, g.dsum, nullptr, nullptr, stream);
