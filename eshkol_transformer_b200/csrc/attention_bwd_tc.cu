@@ -133,7 +133,9 @@ struct KvLayout {
   static_assert(SMEM <= 232448, "shared memory");
 };
 
-template <int DH>
+// MASKED: the instance for calls with a boolean mask; the other one drops the
+// mask code (smaller unrolled loops).
+template <int DH, bool MASKED>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
                       const __grid_constant__ CUtensorMap vh_map,
@@ -148,6 +150,7 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
                       const __grid_constant__ CUtensorMap gmh_map,
                       const __grid_constant__ CUtensorMap gml_map, AttnParams p, AttnOut dk,
                       AttnOut dv, TcBwdArgs a) {
+  if constexpr (!MASKED) p.mask = nullptr;
   using L = KvLayout<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -544,7 +547,9 @@ struct QLayout {
   static_assert(SMEM <= 232448, "shared memory");
 };
 
-template <int DH>
+// MASKED: the instance for calls with a boolean mask; the other one drops the
+// mask code (smaller unrolled loops).
+template <int DH, bool MASKED>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
                      const __grid_constant__ CUtensorMap ql_map,
@@ -557,6 +562,7 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
                      const __grid_constant__ CUtensorMap kmh_map,
                      const __grid_constant__ CUtensorMap kml_map, AttnParams p, AttnOut dq,
                      TcBwdArgs a) {
+  if constexpr (!MASKED) p.mask = nullptr;
   using L = QLayout<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -926,16 +932,27 @@ bool launch_bwd_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTen
     count_launch();
   }
   TcBwdArgs a{w.kh, w.vh, w.qh, w.ql, w.doh, w.dol, w.lse2, delta, device_error_word()};
-  cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       KvLayout<DH>::SMEM);
-  cudaFuncSetAttribute(attn_bwd_q_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       QLayout<DH>::SMEM);
   dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);  // THREADS: 8 probability warps, MMA, loads
-  attn_bwd_kv_tc_kernel<DH><<<g1, THREADS, KvLayout<DH>::SMEM, stream>>>(
-      kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
   dim3 g2((p.Tq + QM - 1) / QM, p.Hq, p.B);
-  attn_bwd_q_tc_kernel<DH><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(
-      qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml, p, dq, a);
+  if (p.mask != nullptr) {
+    cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<DH, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, KvLayout<DH>::SMEM);
+    cudaFuncSetAttribute(attn_bwd_q_tc_kernel<DH, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QLayout<DH>::SMEM);
+    attn_bwd_kv_tc_kernel<DH, true><<<g1, THREADS, KvLayout<DH>::SMEM, stream>>>(
+        kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
+    attn_bwd_q_tc_kernel<DH, true><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(
+        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml, p, dq, a);
+  } else {
+    cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<DH, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, KvLayout<DH>::SMEM);
+    cudaFuncSetAttribute(attn_bwd_q_tc_kernel<DH, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QLayout<DH>::SMEM);
+    attn_bwd_kv_tc_kernel<DH, false><<<g1, THREADS, KvLayout<DH>::SMEM, stream>>>(
+        kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
+    attn_bwd_q_tc_kernel<DH, false><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(
+        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml, p, dq, a);
+  }
   count_launch(2);
   return true;
 }

@@ -127,13 +127,16 @@ __device__ __forceinline__ int count_below(const int64_t* a, int n, int64_t x) {
 
 // ---- forward kernel --------------------------------------------------------------
 
-template <int DH>
+// MASKED: the instance for calls with a boolean mask; the other one drops the
+// mask code (smaller unrolled loops).
+template <int DH, bool MASKED>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_constant__ CUtensorMap ql_map,
                    const __grid_constant__ CUtensorMap kh_map, const __grid_constant__ CUtensorMap kl_map,
                    const __grid_constant__ CUtensorMap vh_map, const __grid_constant__ CUtensorMap vl_map,
                    AttnParams p, AttnOut o, float* __restrict__ row_max,
                    float* __restrict__ row_sum, TcFwdArgs a) {
+  if constexpr (!MASKED) p.mask = nullptr;
   using L = FwdLayout<DH>;
   constexpr int NSL = L::NSLOT, NST = L::NSTAGE;
   extern __shared__ uint8_t smem_raw[];
@@ -506,11 +509,17 @@ bool launch_fwd_tc(const AttnParams& p, AttnOut o, float* m, float* l, cudaStrea
     return false;
   if (!p.qkv_ready) attention_prepare_qkv(p, w, stream);
   TcFwdArgs a{device_error_word()};
-  cudaFuncSetAttribute(attn_fwd_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(attn_fwd_tc_kernel<DH, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       L::SMEM);
+  cudaFuncSetAttribute(attn_fwd_tc_kernel<DH, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        L::SMEM);
   dim3 grid((p.Tq + QM - 1) / QM, p.Hq, p.B);
-  attn_fwd_tc_kernel<DH><<<grid, THREADS, L::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, p, o,
-                                                              m, l, a);
+  if (p.mask != nullptr)
+    attn_fwd_tc_kernel<DH, true><<<grid, THREADS, L::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl,
+                                                                    p, o, m, l, a);
+  else
+    attn_fwd_tc_kernel<DH, false><<<grid, THREADS, L::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl,
+                                                                     p, o, m, l, a);
   count_launch();
   return true;
 }
