@@ -620,8 +620,11 @@ struct Tc2Layout {
 // residual (GEMM_EPI_PLAIN: none).  One instance per mode keeps each kernel's
 // code (and registers) to what its epilogue needs: the epilogue warps' loop
 // is unrolled, and a kernel holding every mode overflowed the instruction
-// cache (ncu: "no_instruction" stalls).
-template <int BN, int STAGES, int EPI>
+// cache (ncu: "no_instruction" stalls).  VAR fixes the GELU modes' options
+// at compile time for the same reason: bit 0 gelu_slope_c, bit 1 a binary16
+// operand-pair output; kVarRuntime reads both from the arguments.
+constexpr int kVarRuntime = 4;
+template <int BN, int STAGES, int EPI, int VAR>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb_lo,
@@ -790,7 +793,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
     // split-f16: accumulator scale 2^-(e_A + e_B); operand-pair output scale
     const float unscale =
         f16 ? exp2_int(-((args.exp_a ? *args.exp_a : 0) + (args.exp_b ? *args.exp_b : 0))) : 1.0f;
-    const bool out16 = args.out_sc.f16 != 0;
+    const bool out16 = VAR == kVarRuntime ? args.out_sc.f16 != 0 : (VAR & 2) != 0;
+    const bool slope_c = VAR == kVarRuntime ? args.gelu_slope_c != 0 : (VAR & 1) != 0;
     const float out_s = out16 ? exp2_int(*args.out_sc.exp) : 1.0f;
     // ATTN_DO with o as a binary16 pair: its scale 2^-e
     const float o_inv =
@@ -924,7 +928,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               // (aux holds u, or GELU'(u) itself with gelu_slope_c)
               const float4 u4 = pre[it];
               float4 d;
-              if (args.gelu_slope_c) {
+              if (slope_c) {
                 d.x = rn_mul(x.x, u4.x);
                 d.y = rn_mul(x.y, u4.y);
                 d.z = rn_mul(x.z, u4.z);
@@ -965,7 +969,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               const float4 o = *dst;
               x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
             }
-            if (K_GF && epi == GEMM_EPI_GELU_FWD && args.gelu_slope_c) {
+            if (K_GF && epi == GEMM_EPI_GELU_FWD && slope_c) {
               // C = GELU'(u) for the backward (one erf shared with GELU(u))
               float4 g, sl;
               gelu_both(x.x, g.x, sl.x);
@@ -1344,16 +1348,7 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
     gemm_simt(g, stream);
     return;
   }
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_PLAIN>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_GELU_FWD>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_GELU_BWD>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_QKV>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_ATTN_DO>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+
   TcArgs a{};
   a.M = g.M; a.N = g.N; a.K = g.K;
   a.C = g.C; a.ldc = g.ldc; a.bias = g.bias; a.accumulate = g.accumulate ? 1 : 0;
@@ -1416,20 +1411,28 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
   }
   const int units = tiles * a.splits;
   const int grid = 2 * (units < pairs ? units : pairs);
+  // GELU options as a compile-time variant: (slope, binary16 out) of the
+  // split-f16 models' steps (1, 1) / (1, 0) and of the others (0, 0)
+  const int gvar = (a.gelu_slope_c ? 1 : 0) | (a.out_sc.f16 ? 2 : 0);
+  auto launch = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+    kernel<<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(ta, ta_lo, tb, tb_lo, a);
+  };
   switch (a.epilogue) {
-#define TC2_LAUNCH(mode)                                                                   \
+#define TC2_GELU(mode)                                                                     \
   case mode:                                                                               \
-    gemm_tc2_kernel<BN, STAGES, mode><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(        \
-        ta, ta_lo, tb, tb_lo, a);                                                          \
+    if (gvar == 3) launch(gemm_tc2_kernel<BN, STAGES, mode, 3>);                           \
+    else if (gvar == 1) launch(gemm_tc2_kernel<BN, STAGES, mode, 1>);                      \
+    else if (gvar == 0) launch(gemm_tc2_kernel<BN, STAGES, mode, 0>);                      \
+    else launch(gemm_tc2_kernel<BN, STAGES, mode, kVarRuntime>);                           \
     break;
-    TC2_LAUNCH(GEMM_EPI_GELU_FWD)
-    TC2_LAUNCH(GEMM_EPI_GELU_BWD)
-    TC2_LAUNCH(GEMM_EPI_QKV)
-    TC2_LAUNCH(GEMM_EPI_ATTN_DO)
-#undef TC2_LAUNCH
+    TC2_GELU(GEMM_EPI_GELU_FWD)
+    TC2_GELU(GEMM_EPI_GELU_BWD)
+#undef TC2_GELU
+    case GEMM_EPI_QKV: launch(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_QKV, kVarRuntime>); break;
+    case GEMM_EPI_ATTN_DO: launch(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_ATTN_DO, kVarRuntime>); break;
     default:  // plain and residual
-      gemm_tc2_kernel<BN, STAGES, GEMM_EPI_PLAIN><<<grid, TC2_THREADS, L::SMEM_BYTES, stream>>>(
-          ta, ta_lo, tb, tb_lo, a);
+      launch(gemm_tc2_kernel<BN, STAGES, GEMM_EPI_PLAIN, kVarRuntime>);
   }
   count_launch();
   if (g.epilogue == GEMM_EPI_GELU_BWD) {
