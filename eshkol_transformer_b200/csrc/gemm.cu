@@ -6,25 +6,25 @@
 //   backward dX = dY W  : A = dY (K-major), B = W  (N-major)
 //   backward dW = dY^T x: A = dY (M-major), B = x  (N-major)
 //
-// Tensor-core path (sm_100a): a persistent, warp-specialised kernel.
-//   warp 0   one lane issues TMA tile loads (128-byte swizzle, no multicast)
-//            into a STAGES-deep shared-memory ring;
-//   warp 1   allocates the TMEM accumulators and one lane issues
-//            tcgen05.mma.kind::tf32 (M=128, N=BN, K=8 per instruction);
-//            3xTF32 uses 128 x 256 tiles: every MMA reads its A and B from
-//            shared memory, and the wide tile keeps those reads plus the TMA
-//            writes (A, B, A_lo, B_lo) within the shared-memory bandwidth
-//            better than 128 x 128 tiles (measured: 1.11x faster per step);
-//            tcgen05.commit releases ring slots and hands finished
-//            accumulators to the epilogue;
-//   warps 2-5 read the accumulator with tcgen05.ld (one TMEM lane per row),
-//            add the bias and store f32 results.
+// Tensor-core paths (sm_100a), persistent and warp-specialised:
+// * gemm_tc2_kernel (the f32-grade modes): clusters of two CTAs on the two
+//   SMs of a TPC compute 256 x 256 tiles with tcgen05.mma.cta_group::2; warp
+//   0 issues TMA loads (128-byte swizzle, no multicast) into a 3-deep ring of
+//   64 KB per SM, warp 1 allocates the pair's TMEM and the leader's lane 0
+//   issues the MMAs, warps 2-9 drain the double-buffered accumulator through
+//   a shared-memory transpose and apply the fused epilogue (plain, residual,
+//   GELU forward / backward, QKV attention operands, dO operands).  Operands
+//   are (hi, lo) pairs and every algorithmic product is three MMAs (A B +
+//   A B_lo + A_lo B): TF32 pairs with kind::tf32 (K 8 per instruction, 32 k
+//   per 128-byte row) or binary16 pairs scaled by a per-tensor power of two
+//   with kind::f16 (K 16, 64 k per row; twice the rate, the same accuracy;
+//   the epilogue multiplies by 2^-(e_A + e_B)).  One instance per epilogue
+//   mode keeps each kernel's unrolled epilogue small.
+// * gemm_tc_kernel: the single-CTA 128 x 256 kernel of the single-TF32 mode.
 // Two TMEM accumulators (2 x BN columns) let the epilogue of one tile overlap
-// the main loop of the next.  The 3xTF32 mode feeds tf32-exact operands
-// (hi = x rounded to TF32, low 13 mantissa bits zero) plus residuals lo and
-// accumulates A B + A B_lo + A_lo B, which keeps f32-grade accuracy.
-// Every mbarrier wait is bounded (about two seconds of clock) and reports
-// through the device error word instead of hanging.
+// the main loop of the next.  Every mbarrier wait is bounded (about two
+// seconds of clock) and reports through the device error word instead of
+// hanging.
 //
 // FFMA path: a plain 128x128 register-tiled kernel, used for the f32 mode and
 // for shapes the tensor-core path does not take (unaligned strides, K = 0).
