@@ -126,8 +126,8 @@ void rope_apply(const float* x, float* y, const float* cos_table,
 // *amax = max(*amax, max |x|) as f32 bits (not reset here).
 void abs_max(const float* x, size_t count, unsigned* amax, cudaStream_t stream);
 // Per slot i: exp[i] = target - k for amax[i] = f 2^k, f in [0.5, 1) (amax
-// 2^exp in [2^(target-1), 2^target)); zero amax keeps exp[i]; nonfinite
-// gives 0; amax cleared when reset.
+// 2^exp in [2^(target-1), 2^target)); a zero or nonfinite amax keeps
+// exp[i]; amax cleared when reset.
 void scale_from_amax(unsigned* amax, int* exp, int count, int target, int reset,
                      cudaStream_t stream);
 // hi / lo binary16 arrays of (x + xlo) 2^(*exp) (xlo optional); the max |x +

@@ -492,15 +492,16 @@ __global__ void abs_max_kernel(const float* __restrict__ x, int64_t n, unsigned*
 }
 
 // exp[i] from amax[i] = f 2^k (f in [0.5, 1)): e = target - k, so that
-// amax 2^e lies in [2^(target-1), 2^target); clamped to [-60, 60].  A zero
-// amax keeps exp[i]; a nonfinite one gives 0.  amax[i] is cleared when reset.
+// amax 2^e lies in [2^(target-1), 2^target); clamped to [-60, 60].  A zero or
+// nonfinite amax keeps exp[i]: after a step whose operands overflowed, the
+// overflowing tensors' maxima (taken before scaling) are finite and rescale
+// them, while tensors computed from the overflowed values keep the scale of
+// the last good step.  amax[i] is cleared when reset.
 __global__ void scale_from_amax_kernel(unsigned* amax, int* exp, int count, int target,
                                        int reset) {
   for (int i = threadIdx.x; i < count; i += blockDim.x) {
     const float a = __uint_as_float(amax[i]);
-    if (!isfinite(a)) {
-      exp[i] = 0;
-    } else if (a > 0.0f) {
+    if (isfinite(a) && a > 0.0f) {
       int k;
       frexpf(a, &k);
       exp[i] = max(-60, min(60, target - k));
