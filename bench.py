@@ -104,10 +104,13 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
-# DRAM bytes per algorithmic GFLOP of the 3xTF32 pair GEMM, measured by ncu
+# DRAM bytes per algorithmic GFLOP of the pair GEMM, measured by ncu
 # (dram__bytes_read.sum + dram__bytes_write.sum) on the profiling case's
-# FFN-up and FFN-down launches: 109.7 MB and 171.7 MB for 34.36 GFLOP each.
-GEMM_DRAM_MB_PER_GFLOP = (109.7 + 171.7) / (2 * 34.36)
+# FFN-up backward launches: split-f16 dX 84.0 + 5.2 MB and dW 84.0 + 3.5 MB
+# for 34.36 GFLOP each; 3xTF32 (FFN-up and FFN-down forward) 109.7 MB and
+# 171.7 MB.
+GEMM_DRAM_MB_PER_GFLOP = {"f16x3": (84.0 + 5.2 + 84.0 + 3.5) / (2 * 34.36),
+                          "tf32x3": (109.7 + 171.7) / (2 * 34.36)}
 
 
 def roofline_entry(gemm: dict, gemm_tflops: float, peak_t: float, peaks: dict,
@@ -138,7 +141,8 @@ def roofline_entry(gemm: dict, gemm_tflops: float, peak_t: float, peaks: dict,
         "frac_of_mma_ceiling_at_clock": round(3 * gemm_tflops / ceiling, 4) if ceiling else None,
         "flop_per_launch": per_launch_flop,
         "avg_launch_ms": gemm["ms"] / max(gemm["launches"], 1),
-        "traffic": round(per_launch_flop / 1e9 * GEMM_DRAM_MB_PER_GFLOP * 1e6),
+        "traffic": round(per_launch_flop / 1e9 *
+                         GEMM_DRAM_MB_PER_GFLOP["f16x3" if f16 else "tf32x3"] * 1e6),
         "traffic_unit": "bytes per launch",
         "traffic_source": "ncu DRAM bytes of the profiling-case GEMM launches per algorithmic "
                           "FLOP, scaled to the average launch",
