@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -59,11 +60,10 @@ class ClockSampler:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{gpu}_{os.getpid()}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"et_b200_clocks_{gpu}_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -150,6 +150,41 @@ def roofline_entry(gemm: dict, gemm_tflops: float, peak_t: float, peaks: dict,
 
 
 # ----------------------------------------------------------------- B200 arm
+
+def time_steps(etb, shape, precision, global_tokens, dev, stream_of, steps, warmup, rank, world,
+               barrier) -> float:
+    """ms per step (max over ranks) of a fresh model in `precision` over the
+    device-resident batches `dev`."""
+    import torch
+    import torch.distributed as dist
+
+    model = etb.LanguageModel(shape, precision=precision, global_tokens=global_tokens)
+    model.init(20261201)
+    if world > 1:
+        uid = [etb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        model.enable_data_parallel(uid[0], rank, world)
+    stream = torch.cuda.ExternalStream(model.stream())
+    loss = torch.zeros(1, device="cuda")
+    for i in range(warmup):
+        model.step_device(dev[i % len(dev)][0].data_ptr(), dev[i % len(dev)][1].data_ptr(),
+                          loss.data_ptr())
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        ids, tg = dev[i % len(dev)]
+        model.step_device(ids.data_ptr(), tg.data_ptr(), loss.data_ptr())
+    stop.record(stream)
+    barrier()
+    ms = start.elapsed_time(stop) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    model.close()
+    return ms
+
 
 def run_b200(args) -> None:
     import torch
@@ -238,6 +273,15 @@ def run_b200(args) -> None:
         e2e_ms = t.item()
     e2e_value = global_tokens * e2e_steps / (e2e_ms / 1e3)
 
+    model.close()
+    # the config's named contraction mode (3xTF32) on the same box and ranks,
+    # fewer steps: reported beside the headline, not as it
+    tf32x3 = None
+    if f16 and not args.no_tf32x3:
+        tf32x3 = time_steps(etb, shape, etb.PRECISION_TF32X3, global_tokens, dev, stream_of=None,
+                            steps=max(2, min(args.steps, 3)), warmup=2, rank=rank, world=world,
+                            barrier=barrier)
+
     peaks = measured_peaks()
     gemm = prof["gemm"]
     gemm_tflops = gemm["flop"] / (gemm["ms"] / 1e3) / 1e12 if gemm["ms"] else 0.0
@@ -245,6 +289,16 @@ def run_b200(args) -> None:
     attn_b = prof["attention_backward"]
     attn_tflops = attn_b["flop"] / (attn_b["ms"] / 1e3) / 1e12 if attn_b["ms"] else 0.0
     total_prof_ms = sum(v["ms"] for v in prof.values())
+    hbm = peaks.get("hbm_gbs", 6650.0)
+
+    def hbm_entry(name):
+        c = prof[name]
+        if not c["ms"]:
+            return None
+        gbs = c["bytes"] / (c["ms"] / 1e3) / 1e9
+        return {"achieved_gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                "bytes_per_step": c["bytes"] / args.steps,
+                "ms_per_step": round(c["ms"] / args.steps, 3)}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
@@ -261,6 +315,10 @@ def run_b200(args) -> None:
         "roofline": roofline_entry(gemm, gemm_tflops, peak_t, peaks, clocks.summary(), f16),
         "attention_backward": {"achieved_tflops": round(attn_tflops, 2),
                                "ms_per_step": round(attn_b["ms"] / args.steps, 3)},
+        "hbm_frac": {"peak_gbs": hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
+                     if not peaks.get("fallback") else "fallback",
+                     "cross_entropy": hbm_entry("cross_entropy"),
+                     "adamw": hbm_entry("adamw"), "adamw_check": hbm_entry("adamw_check")},
         "profile_ms_per_step": {k: round(v["ms"] / args.steps, 3) for k, v in prof.items()},
         "profile_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in prof.items()}
         if total_prof_ms else {},
@@ -269,11 +327,13 @@ def run_b200(args) -> None:
                 "steps": e2e_steps, "final_loss": losses[-1]},
         "clocks": clocks.summary(),
     }
+    if tf32x3 is not None:
+        line["config"]["tf32x3_ms_per_step"] = round(tf32x3, 3)
+        line["config"]["tf32x3_tokens_per_s"] = round(global_tokens / (tf32x3 / 1e3), 1)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(kind="port", budget_s=args.cpu_budget)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -422,6 +482,8 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tf32x3", action="store_true",
+                    help="skip the 3xTF32 step time reported beside a split-f16 run")
     ap.add_argument("--contractions", default="f16x3", choices=["f16x3", "tf32x3"],
                     help="f32-grade contraction scheme of the linear GEMMs (split-f16 pairs or "
                          "3xTF32)")

@@ -75,6 +75,8 @@ def load() -> C.CDLL:
         "et_b200_lm_profile_collect_v1": (C.c_int32, [C.c_void_p]),
         "et_b200_lm_profile_read_v1": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_size_t]),
         "et_b200_lm_f16_redone_steps_v1": (C.c_int32, [C.c_void_p]),
+        "et_b200_lm_update_counts_v1": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64),
+                                                    C.POINTER(C.c_uint64), E]),
         "et_b200_o2_optimizer_create_v1": (C.c_int32, [C.c_size_t, C.c_void_p, C.c_uint32,
                                                        C.c_uint32, C.c_uint32, C.c_uint64,
                                                        C.c_uint64, C.c_uint32,
@@ -222,6 +224,14 @@ class LanguageModel:
         _check(self.lib.et_b200_lm_enable_data_parallel_v1(self.handle, buf, rank, world,
                                                            C.byref(err)), err)
 
+    def update_counts(self) -> tuple[int, int]:
+        """(applied AdamW updates, device-enqueued steps whose update was skipped)."""
+        done, skipped = C.c_uint64(), C.c_uint64()
+        err = k1.KernelError()
+        _check(self.lib.et_b200_lm_update_counts_v1(self.handle, C.byref(done), C.byref(skipped),
+                                                    C.byref(err)), err)
+        return done.value, skipped.value
+
     def f16_redone_steps(self) -> int:
         """Split-f16 steps redone in 3xTF32 after an operand overflow."""
         return self.lib.et_b200_lm_f16_redone_steps_v1(self.handle)
@@ -231,12 +241,13 @@ class LanguageModel:
 
     PROFILE_CLASSES = ("gemm", "attention_forward", "attention_backward", "cross_entropy",
                        "adamw", "layer_norm", "elementwise", "embedding", "tf32_split",
-                       "allreduce_wait")
+                       "allreduce_wait", "adamw_check")
 
     def profile_read(self) -> dict:
         self.lib.et_b200_lm_profile_collect_v1(self.handle)
-        out = (C.c_double * 40)()
-        self.lib.et_b200_lm_profile_read_v1(self.handle, out, 40)
+        n = 4 * len(self.PROFILE_CLASSES)
+        out = (C.c_double * n)()
+        self.lib.et_b200_lm_profile_read_v1(self.handle, out, n)
         return {name: {"launches": out[4 * i], "ms": out[4 * i + 1], "flop": out[4 * i + 2],
                        "bytes": out[4 * i + 3]} for i, name in enumerate(self.PROFILE_CLASSES)}
 

@@ -640,8 +640,13 @@ int32_t et_a2_kv_cache_transaction_stage_layer_v1(et_a2_kv_cache_transaction* ha
                     "key and value sources must be finite f32");
   cudaError_t st = cudaSuccess;
   if (kdev || vdev) {
-    // device sources: a device finite check (one flag word in the staging area)
-    if (t->staging == nullptr) st = cudaMalloc(&t->staging, 2 * bytes + 16);
+    // Device sources are read like a CPU call reads host memory: once every
+    // kernel and copy already enqueued on this device, on any stream, has
+    // finished (the caller may have produced them on its own stream just
+    // before this call; the cache's stream is not ordered after it).
+    st = cudaDeviceSynchronize();
+    // then a device finite check (one flag word in the staging area)
+    if (st == cudaSuccess && t->staging == nullptr) st = cudaMalloc(&t->staging, 2 * bytes + 16);
     int* flag = t->staging ? reinterpret_cast<int*>(t->staging + 2 * n) : nullptr;
     int bad = 0;
     if (st == cudaSuccess) st = cudaMemsetAsync(flag, 0, sizeof(int), c->stream);

@@ -8,8 +8,12 @@
 // optimizer object (et_b200_o2_optimizer_*) allocates its moments and its norm
 // scratch when it is created; this entry point instead takes every tensor
 // from the caller and keeps its only scratch -- the partial sums of the
-// global gradient norm and two status words -- in the file-scope static
-// device array below, sized for a stated maximum tensor length.
+// global gradient norm and three status words -- in the file-scope static
+// device array below, sized for a stated maximum tensor length.  Like the
+// reference's staged commit, the update is all or nothing: a check pass
+// computes every element's update without writing, and the writing pass
+// runs only when neither the gradient pass nor the check found a nonfinite
+// value.
 //
 // Per element it applies the same separately rounded O2 arithmetic
 // (native/o2_optimizer.c:1738-1756) as the multi-tensor kernel, so with the
@@ -32,7 +36,9 @@ struct NoallocScratch {
   double sumsq;
   float clip;
   uint32_t norm_bits;
-  int status[2];  // [0] a gradient is nonfinite, [1] an update is nonfinite
+  // [0] a gradient is nonfinite, [1] kAdamw* bits of the check pass, [2] the
+  // norm of finite gradients is not representable in f32
+  int status[3];
 };
 
 // The scratch every call shares (64 KiB + a few words per GPU, resident for
@@ -44,6 +50,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[sizeof(NoallocS
 __global__ void noalloc_clear(NoallocScratch* s) {
   s->status[0] = 0;
   s->status[1] = 0;
+  s->status[2] = 0;
 }
 
 // Block b owns elements [b * 65536, (b + 1) * 65536): a fixed partition, so
@@ -76,7 +83,7 @@ __global__ void noalloc_finalize(NoallocScratch* s, int partials, float clip_max
     const float norm = (float)sqrt(sumsq);
     s->norm_bits = __float_as_uint(norm);
     s->clip = (clip_max > 0.0f && norm > clip_max) ? __fdiv_rn(clip_max, norm) : 1.0f;
-    if (!isfinite(norm)) s->status[0] = 1;
+    if (!isfinite(norm) && s->status[0] == 0) s->status[2] = 1;
   }
 }
 
@@ -84,25 +91,50 @@ struct Scalars {
   float beta1, beta2, one_minus_beta1, one_minus_beta2, bias1, bias2, lr, decay, epsilon, weight;
 };
 
+// One element of native/o2_optimizer.c:1738-1756 (each operation separately
+// rounded, as the multi-tensor kernel does); with CHECK, *bad collects the
+// kAdamw* bits for nonfinite inputs, intermediates and results.
+template <bool CHECK>
+__device__ __forceinline__ void noalloc_element(const Scalars& c, float clip, float p0, float g0,
+                                                float m0, float v0, float& p, float& m, float& v,
+                                                int& bad) {
+  const float g = rn_mul(rn_div(g0, c.weight), clip);
+  m = rn_add(rn_mul(c.beta1, m0), rn_mul(c.one_minus_beta1, g));
+  v = rn_add(rn_mul(c.beta2, v0), rn_mul(c.one_minus_beta2, rn_mul(g, g)));
+  const float mh = rn_div(m, c.bias1);
+  const float vh = rn_div(v, c.bias2);
+  const float den = rn_add(rn_sqrt(vh), c.epsilon);
+  p = rn_sub(rn_mul(p0, c.decay), rn_div(rn_mul(c.lr, mh), den));
+  if (CHECK) {
+    if (!(isfinite(p0) && isfinite(g0) && isfinite(m0) && isfinite(v0)))
+      bad |= kAdamwInputNonfinite;
+    else if (!(isfinite(g) && isfinite(m) && isfinite(v) && isfinite(mh) && isfinite(vh) &&
+               vh >= 0.0f && isfinite(den) && den > 0.0f && isfinite(p)))
+      bad |= kAdamwProducedNonfinite;
+  }
+}
+
+// APPLY = false: compute every update and record problems, write nothing.
+// APPLY = true: write, unless the gradient pass or the check pass recorded a
+// problem (then no block writes: the update is all or nothing).
+template <bool APPLY>
 __global__ void __launch_bounds__(256)
 noalloc_adamw(float* __restrict__ value, const float* __restrict__ grad, float* __restrict__ m1,
               float* __restrict__ m2, uint64_t count, Scalars c, NoallocScratch* s) {
-  if (s->status[0]) return;  // nonfinite gradient or norm: leave every tensor untouched
+  if (s->status[0] || s->status[2] || (APPLY && s->status[1])) return;
   const float clip = s->clip;
-  bool bad = false;
+  int bad = 0;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    const float g = rn_mul(rn_div(grad[i], c.weight), clip);
-    const float m = rn_add(rn_mul(c.beta1, m1[i]), rn_mul(c.one_minus_beta1, g));
-    const float v = rn_add(rn_mul(c.beta2, m2[i]), rn_mul(c.one_minus_beta2, rn_mul(g, g)));
-    const float den = rn_add(rn_sqrt(rn_div(v, c.bias2)), c.epsilon);
-    const float p = rn_sub(rn_mul(value[i], c.decay), rn_div(rn_mul(c.lr, rn_div(m, c.bias1)), den));
-    bad |= !(isfinite(m) && isfinite(v) && isfinite(p));
-    value[i] = p;
-    m1[i] = m;
-    m2[i] = v;
+    float p, m, v;
+    noalloc_element<!APPLY>(c, clip, value[i], grad[i], m1[i], m2[i], p, m, v, bad);
+    if (APPLY) {
+      value[i] = p;
+      m1[i] = m;
+      m2[i] = v;
+    }
   }
-  if (bad) atomicExch(&s->status[1], 1);
+  if (!APPLY && bad) atomicOr(&s->status[1], bad);
 }
 
 float f_of(uint32_t b) {
@@ -195,23 +227,33 @@ extern "C" int32_t et_b200_adamw_step_noalloc_v1(
   noalloc_finalize<<<1, 1024, 0, st>>>(s, partials, clip_max_bits ? clip_max : 0.0f);
   const uint64_t want = (count + 255) / 256;
   const unsigned blocks = (unsigned)(want < (uint64_t)sm_count() * 8 ? want : sm_count() * 8);
-  noalloc_adamw<<<blocks, 256, 0, st>>>(value, gradient, exp_avg, exp_avg_sq, count, c, s);
-  count_launch(4);
+  noalloc_adamw<false><<<blocks, 256, 0, st>>>(value, gradient, exp_avg, exp_avg_sq, count, c, s);
+  noalloc_adamw<true><<<blocks, 256, 0, st>>>(value, gradient, exp_avg, exp_avg_sq, count, c, s);
+  count_launch(5);
+  cudaError_t err = cudaGetLastError();  // a launch that failed to start
+  if (err != cudaSuccess) return cuda_error(error, err, op);
   struct {
     uint32_t norm;
-    int status[2];
-  } out = {0, {0, 0}};
-  cudaMemcpyAsync(&out.norm, &s->norm_bits, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
-  cudaMemcpyAsync(out.status, s->status, sizeof(out.status), cudaMemcpyDeviceToHost, st);
-  cudaError_t err = cudaStreamSynchronize(st);
+    int status[3];
+  } out = {0, {0, 0, 0}};
+  err = cudaMemcpyAsync(&out.norm, &s->norm_bits, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(out.status, s->status, sizeof(out.status), cudaMemcpyDeviceToHost, st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
   if (err != cudaSuccess) return cuda_error(error, err, op);
   if (norm_bits) *norm_bits = out.norm;
   if (out.status[0])
     return set_error(error, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
                      "gradient contains a nonfinite value; nothing was updated");
-  if (out.status[1])
+  if (out.status[2])
     return set_error(error, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
-                     "AdamW produced a nonfinite value");
+                     "gradient norm is unrepresentable; nothing was updated");
+  if (out.status[1] & kAdamwInputNonfinite)
+    return set_error(error, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "parameter, gradient, or moment is nonfinite; nothing was updated");
+  if (out.status[1] & kAdamwProducedNonfinite)
+    return set_error(error, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "AdamW produced a nonfinite value; nothing was updated");
   if (error) memset(error, 0, sizeof(*error));
   return 0;
 }

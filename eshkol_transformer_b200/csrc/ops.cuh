@@ -40,14 +40,38 @@ struct AdamwTensor {
   float* value_lo;
   OperandScale value_sc;
 };
-// One fused pass over every tensor of the table (device array `tensors`,
-// `prefix[i]` = first global element of tensor i, total = prefix[count]).
-// weight/clip divide and scale gradients as o2_optimizer.c:1738 does.
-// status[1] is set when any staged value is nonfinite.  With `skip` and
-// *skip != 0 nothing is updated and status[2] counts the skipped step.
-void adamw_multi(const AdamwTensor* tensors, const uint64_t* prefix,
-                 int tensor_count, uint64_t total, float weight, float clip,
-                 int* status, cudaStream_t stream, const float* skip = nullptr);
+// An AdamW update is all or nothing, as the reference's staged commit is
+// (o2_optimizer.c:1813-1926): adamw_check computes every element's update
+// without writing and sets status bits; adamw_apply then writes the table
+// only if no bit is set.  Both are fused passes over every tensor of the
+// table (device array `tensors`, `prefix[i]` = first global element of tensor
+// i, total = prefix[count]); weight/clip divide and scale gradients as
+// o2_optimizer.c:1738 does.
+enum : int {
+  kAdamwInputNonfinite = 1,     // a parameter, gradient or moment is nonfinite
+  kAdamwProducedNonfinite = 2,  // an intermediate or result is nonfinite
+};
+struct AdamwControl {
+  const float* skip;     // optional: nothing is checked or written when *skip != 0
+  int* status;           // [1] |= kAdamw* bits (check); [2] += 1 per skipped apply
+  uint64_t* completed;   // optional: applied updates, +1 by each apply that writes
+};
+// `vec`: every tensor's arrays are 16-byte aligned and its count a multiple
+// of 4 (128-bit loads and stores).
+void adamw_check(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_count,
+                 uint64_t total, float weight, float clip, AdamwControl ctl, bool vec,
+                 cudaStream_t stream);
+void adamw_apply(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_count,
+                 uint64_t total, float weight, float clip, AdamwControl ctl, bool vec,
+                 cudaStream_t stream);
+// tensors[0].bias1 / bias2 of update *completed + 1, computed on the device
+// with the host's rounding sequence (o2_optimizer.c:419-435), so that steps
+// enqueued without a host synchronisation, some of which may be skipped,
+// still use the right update number.
+void adamw_prepare(AdamwTensor* tensors, const uint64_t* completed, cudaStream_t stream);
+// *flag += amount when status[0] is set (a token id or target of the step is
+// out of range).
+void fold_index_flag(const int* status, float* flag, float amount, cudaStream_t stream);
 // Sum of squares of grad/weight over the table, in f64, plus status[0] = 1 on
 // any nonfinite gradient.  out_sumsq receives one double.
 void grad_sumsq(const AdamwTensor* tensors, const uint64_t* prefix,

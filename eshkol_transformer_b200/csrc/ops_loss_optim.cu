@@ -133,11 +133,22 @@ __global__ void mean_loss_kernel(const float* __restrict__ loss, int64_t rows,
 }
 
 // ---- AdamW ----------------------------------------------------------------
+//
+// Two passes per update.  adamw_check reads parameter, gradient and both
+// moments (16 B per element) and computes each element's update exactly as
+// adamw_apply will, writing nothing: any nonfinite input, intermediate or
+// result sets a status bit (the reference checks the same quantities,
+// o2_optimizer.c:1730-1768).  adamw_apply reads the same 16 B, writes value
+// and both moments (12 B) and the weights' next operand pair, unless a
+// status bit or the step's skip flag is set; then no block writes anything.
+// With `vec` each thread moves four consecutive elements per 128-bit access,
+// kAdamGroups groups per stream in flight.
 
 constexpr int kAdamThreads = 256;
-constexpr int kAdamPerThread = 8;
-constexpr int64_t kAdamChunk = (int64_t)kAdamThreads * kAdamPerThread;
-constexpr int kAdamBatch = 4;
+constexpr int kAdamGroups = 2;  // float4 groups per thread (vector path)
+constexpr int kAdamScalarPerThread = 8;
+constexpr int64_t kAdamVecChunk = (int64_t)kAdamThreads * kAdamGroups * 4;
+constexpr int64_t kAdamChunk = (int64_t)kAdamThreads * kAdamScalarPerThread;
 
 __device__ __forceinline__ int find_tensor(const uint64_t* prefix, int count, uint64_t e) {
   int lo = 0, hi = count - 1;
@@ -148,72 +159,160 @@ __device__ __forceinline__ int find_tensor(const uint64_t* prefix, int count, ui
   return lo;
 }
 
-__global__ void __launch_bounds__(kAdamThreads)
-adamw_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict__ prefix,
-             int tensor_count, uint64_t total, float weight, float clip, int* status,
-             const float* skip) {
-  const uint64_t begin = (uint64_t)blockIdx.x * kAdamChunk;
-  if (begin >= total) return;
-  if (skip != nullptr && *skip != 0.0f) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(status + 2, 1);
-    return;
+// One element of native/o2_optimizer.c:1738-1756, each operation separately
+// rounded.  With CHECK, *bad collects the kAdamw* bits.
+template <bool CHECK>
+__device__ __forceinline__ void adamw_element(const AdamwTensor& T, float weight, float clip,
+                                              float p0, float g0, float m0, float v0, float& p,
+                                              float& m, float& v, int& bad) {
+  const float g = rn_mul(rn_div(g0, weight), clip);
+  m = rn_add(rn_mul(T.beta1, m0), rn_mul(T.one_minus_beta1, g));
+  v = rn_add(rn_mul(T.beta2, v0), rn_mul(T.one_minus_beta2, rn_mul(g, g)));
+  const float mh = rn_div(m, T.bias1);
+  const float vh = rn_div(v, T.bias2);
+  const float den = rn_add(rn_sqrt(vh), T.epsilon);
+  p = rn_sub(rn_mul(p0, T.decay), rn_div(rn_mul(T.lr, mh), den));
+  if (CHECK) {
+    if (!(isfinite(p0) && isfinite(g0) && isfinite(m0) && isfinite(v0)))
+      bad |= kAdamwInputNonfinite;
+    else if (!(isfinite(g) && isfinite(m) && isfinite(v) && isfinite(mh) && isfinite(vh) &&
+               vh >= 0.0f && isfinite(den) && den > 0.0f && isfinite(p)))
+      bad |= kAdamwProducedNonfinite;
   }
-  float amax = 0.0f;  // max |value| of the tensors that record it
+}
+
+// True when this launch must not write (APPLY) or need not check: the step
+// is void (skip flag, summed across ranks) or the check found a problem.
+template <bool APPLY>
+__device__ __forceinline__ bool adamw_void(const AdamwControl& ctl) {
+  const bool skip = (ctl.skip != nullptr && *ctl.skip != 0.0f) || (APPLY && ctl.status[1] != 0);
+  if (skip && APPLY && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(ctl.status + 2, 1);
+  return skip;
+}
+
+template <bool APPLY>
+__device__ __forceinline__ void adamw_finish(const AdamwTensor* tensors, const AdamwControl& ctl,
+                                             float amax, int bad) {
+  if (APPLY) {
+    // (a single max slot per launch: the first tensor's)
+    if (tensors[0].value_sc.amax != nullptr) amax_record_warp(tensors[0].value_sc.amax, amax);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && ctl.completed != nullptr) *ctl.completed += 1;
+  } else if (bad) {
+    atomicOr(ctl.status + 1, bad);
+  }
+}
+
+// Vector path: groups of 4 elements never straddle two tensors (every count
+// is a multiple of 4, so every prefix is too).
+template <bool APPLY>
+__global__ void __launch_bounds__(kAdamThreads)
+adamw_vec_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict__ prefix,
+                 int tensor_count, uint64_t total, float weight, float clip, AdamwControl ctl) {
+  if (adamw_void<APPLY>(ctl)) return;
+  const uint64_t begin = (uint64_t)blockIdx.x * kAdamVecChunk;
+  int t = find_tensor(prefix, tensor_count, begin);
+  float4 p0[kAdamGroups], g0[kAdamGroups], m0[kAdamGroups], v0[kAdamGroups];
+  int tg[kAdamGroups];
+#pragma unroll
+  for (int k = 0; k < kAdamGroups; k++) {
+    const uint64_t e = begin + 4 * ((uint64_t)k * kAdamThreads + threadIdx.x);
+    tg[k] = -1;
+    if (e >= total) continue;
+    while (t + 1 < tensor_count && prefix[t + 1] <= e) t++;
+    tg[k] = t;
+    const AdamwTensor& T = tensors[t];
+    const uint64_t i = e - prefix[t];
+    p0[k] = *reinterpret_cast<const float4*>(T.value + i);
+    g0[k] = __ldg(reinterpret_cast<const float4*>(T.grad + i));
+    m0[k] = *reinterpret_cast<const float4*>(T.exp_avg + i);
+    v0[k] = *reinterpret_cast<const float4*>(T.exp_avg_sq + i);
+  }
+  float amax = 0.0f;
+  int bad = 0;
+#pragma unroll
+  for (int k = 0; k < kAdamGroups; k++) {
+    if (tg[k] < 0) continue;
+    const AdamwTensor& T = tensors[tg[k]];
+    float4 p, m, v;
+    adamw_element<!APPLY>(T, weight, clip, p0[k].x, g0[k].x, m0[k].x, v0[k].x, p.x, m.x, v.x, bad);
+    adamw_element<!APPLY>(T, weight, clip, p0[k].y, g0[k].y, m0[k].y, v0[k].y, p.y, m.y, v.y, bad);
+    adamw_element<!APPLY>(T, weight, clip, p0[k].z, g0[k].z, m0[k].z, v0[k].z, p.z, m.z, v.z, bad);
+    adamw_element<!APPLY>(T, weight, clip, p0[k].w, g0[k].w, m0[k].w, v0[k].w, p.w, m.w, v.w, bad);
+    if (!APPLY) continue;
+    const uint64_t i = begin + 4 * ((uint64_t)k * kAdamThreads + threadIdx.x) - prefix[tg[k]];
+    *reinterpret_cast<float4*>(T.value + i) = p;
+    *reinterpret_cast<float4*>(T.exp_avg + i) = m;
+    *reinterpret_cast<float4*>(T.exp_avg_sq + i) = v;
+    if (T.value_sc.f16) {
+      amax = abs_max4(amax, p);
+      f16_store4(reinterpret_cast<uint16_t*>(T.value_hi), reinterpret_cast<uint16_t*>(T.value_lo),
+                 (int64_t)i, p, exp2_int(*T.value_sc.exp));
+    } else if (T.value_hi != nullptr) {
+      float4 h, l;
+      tf32_split(p.x, h.x, l.x);
+      tf32_split(p.y, h.y, l.y);
+      tf32_split(p.z, h.z, l.z);
+      tf32_split(p.w, h.w, l.w);
+      *reinterpret_cast<float4*>(T.value_hi + i) = h;
+      *reinterpret_cast<float4*>(T.value_lo + i) = l;
+    }
+  }
+  adamw_finish<APPLY>(tensors, ctl, amax, bad);
+}
+
+// Scalar path for tensors of any count and alignment.
+template <bool APPLY>
+__global__ void __launch_bounds__(kAdamThreads)
+adamw_scalar_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict__ prefix,
+                    int tensor_count, uint64_t total, float weight, float clip, AdamwControl ctl) {
+  if (adamw_void<APPLY>(ctl)) return;
+  const uint64_t begin = (uint64_t)blockIdx.x * kAdamChunk;
   const uint64_t end = min(total, begin + (uint64_t)kAdamChunk);
   int t = find_tensor(prefix, tensor_count, begin);
-  bool bad = false;
-  uint64_t seg = begin;
-  while (seg < end) {
-    while (t + 1 < tensor_count && prefix[t + 1] <= seg) t++;
-    const AdamwTensor T = tensors[t];
-    const uint64_t seg_end = min(end, prefix[t] + T.count);
-    const uint64_t base = prefix[t];
-    // kAdamBatch elements per thread per round, their loads issued together
-    for (uint64_t e0 = seg + threadIdx.x; e0 < seg_end; e0 += (uint64_t)kAdamBatch * blockDim.x) {
-      float gr[kAdamBatch], m0[kAdamBatch], v0[kAdamBatch], p0[kAdamBatch];
-#pragma unroll
-      for (int u = 0; u < kAdamBatch; u++) {
-        const uint64_t e = e0 + (uint64_t)u * blockDim.x;
-        const uint64_t i = e - base;
-        const bool in = e < seg_end;
-        gr[u] = in ? T.grad[i] : 0.0f;
-        m0[u] = in ? T.exp_avg[i] : 0.0f;
-        v0[u] = in ? T.exp_avg_sq[i] : 0.0f;
-        p0[u] = in ? T.value[i] : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < kAdamBatch; u++) {
-        const uint64_t e = e0 + (uint64_t)u * blockDim.x;
-        if (e >= seg_end) continue;
-        const uint64_t i = e - base;
-        const float g = rn_mul(rn_div(gr[u], weight), clip);
-        const float m = rn_add(rn_mul(T.beta1, m0[u]), rn_mul(T.one_minus_beta1, g));
-        const float v = rn_add(rn_mul(T.beta2, v0[u]), rn_mul(T.one_minus_beta2, rn_mul(g, g)));
-        const float mh = rn_div(m, T.bias1);
-        const float vh = rn_div(v, T.bias2);
-        const float den = rn_add(rn_sqrt(vh), T.epsilon);
-        const float p = rn_sub(rn_mul(p0[u], T.decay), rn_div(rn_mul(T.lr, mh), den));
-        bad |= !(isfinite(g) && isfinite(m) && isfinite(v) && isfinite(p));
-        T.value[i] = p;
-        T.exp_avg[i] = m;
-        T.exp_avg_sq[i] = v;
-        if (T.value_sc.f16) {
-          amax = fmaxf(amax, fabsf(p));
-          f16_split(p * exp2_int(*T.value_sc.exp), reinterpret_cast<uint16_t*>(T.value_hi)[i],
-                    reinterpret_cast<uint16_t*>(T.value_lo)[i]);
-        } else if (T.value_hi != nullptr) {
-          float h, l;
-          tf32_split(p, h, l);
-          T.value_hi[i] = h;
-          T.value_lo[i] = l;
-        }
-      }
+  float amax = 0.0f;
+  int bad = 0;
+  for (uint64_t e = begin + threadIdx.x; e < end; e += blockDim.x) {
+    while (t + 1 < tensor_count && prefix[t + 1] <= e) t++;
+    const AdamwTensor& T = tensors[t];
+    const uint64_t i = e - prefix[t];
+    float p, m, v;
+    adamw_element<!APPLY>(T, weight, clip, T.value[i], T.grad[i], T.exp_avg[i], T.exp_avg_sq[i],
+                          p, m, v, bad);
+    if (!APPLY) continue;
+    T.value[i] = p;
+    T.exp_avg[i] = m;
+    T.exp_avg_sq[i] = v;
+    if (T.value_sc.f16) {
+      amax = fmaxf(amax, fabsf(p));
+      f16_split(p * exp2_int(*T.value_sc.exp), reinterpret_cast<uint16_t*>(T.value_hi)[i],
+                reinterpret_cast<uint16_t*>(T.value_lo)[i]);
+    } else if (T.value_hi != nullptr) {
+      tf32_split(p, T.value_hi[i], T.value_lo[i]);
     }
-    seg = seg_end;
   }
-  // (a single max slot per launch: the first tensor's)
-  if (tensors[0].value_sc.amax != nullptr) amax_record_warp(tensors[0].value_sc.amax, amax);
-  if (bad) atomicExch(status + 1, 1);
+  adamw_finish<APPLY>(tensors, ctl, amax, bad);
+}
+
+// base^e with one f32 rounding per multiply, the host's sequence
+// (o2_optimizer.c:419-435).
+__device__ float pow_steps_device(float base, uint64_t e) {
+  float result = 1.0f, b = base;
+  while (e != 0u) {
+    if (e & 1u) result = __fmul_rn(result, b);
+    e >>= 1u;
+    if (e != 0u) b = __fmul_rn(b, b);
+  }
+  return result;
+}
+
+__global__ void fold_index_flag_kernel(const int* status, float* flag, float amount) {
+  if (status[0] != 0) *flag += amount;
+}
+
+__global__ void adamw_prepare_kernel(AdamwTensor* tensors, const uint64_t* completed) {
+  const uint64_t t = *completed + 1;
+  tensors[0].bias1 = __fsub_rn(1.0f, pow_steps_device(tensors[0].beta1, t));
+  tensors[0].bias2 = __fsub_rn(1.0f, pow_steps_device(tensors[0].beta2, t));
 }
 
 __global__ void __launch_bounds__(kAdamThreads)
@@ -271,13 +370,42 @@ void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream) 
   count_launch();
 }
 
-void adamw_multi(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_count,
-                 uint64_t total, float weight, float clip, int* status, cudaStream_t stream,
-                 const float* skip) {
+namespace {
+template <bool APPLY>
+void adamw_pass(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_count,
+                uint64_t total, float weight, float clip, AdamwControl ctl, bool vec,
+                cudaStream_t stream) {
   if (total == 0) return;
-  const unsigned blocks = (unsigned)((total + kAdamChunk - 1) / kAdamChunk);
-  adamw_kernel<<<blocks, kAdamThreads, 0, stream>>>(tensors, prefix, tensor_count, total,
-                                                    weight, clip, status, skip);
+  if (vec) {
+    adamw_vec_kernel<APPLY><<<ceil_div(total, kAdamVecChunk), kAdamThreads, 0, stream>>>(
+        tensors, prefix, tensor_count, total, weight, clip, ctl);
+  } else {
+    adamw_scalar_kernel<APPLY><<<ceil_div(total, kAdamChunk), kAdamThreads, 0, stream>>>(
+        tensors, prefix, tensor_count, total, weight, clip, ctl);
+  }
+  count_launch();
+}
+}  // namespace
+
+void adamw_check(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_count,
+                 uint64_t total, float weight, float clip, AdamwControl ctl, bool vec,
+                 cudaStream_t stream) {
+  adamw_pass<false>(tensors, prefix, tensor_count, total, weight, clip, ctl, vec, stream);
+}
+
+void adamw_apply(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_count,
+                 uint64_t total, float weight, float clip, AdamwControl ctl, bool vec,
+                 cudaStream_t stream) {
+  adamw_pass<true>(tensors, prefix, tensor_count, total, weight, clip, ctl, vec, stream);
+}
+
+void fold_index_flag(const int* status, float* flag, float amount, cudaStream_t stream) {
+  fold_index_flag_kernel<<<1, 1, 0, stream>>>(status, flag, amount);
+  count_launch();
+}
+
+void adamw_prepare(AdamwTensor* tensors, const uint64_t* completed, cudaStream_t stream) {
+  adamw_prepare_kernel<<<1, 1, 0, stream>>>(tensors, completed);
   count_launch();
 }
 

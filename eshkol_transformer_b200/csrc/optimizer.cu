@@ -136,6 +136,7 @@ struct et_b200_o2_optimizer {
   double* d_partials = nullptr;
   double* d_sumsq = nullptr;
   int* d_status = nullptr;
+  bool vec = false;  // every tensor 16-byte aligned with a count divisible by 4
   std::vector<AdamwTensor> table;
   std::vector<uint64_t> prefix;
 };
@@ -216,14 +217,18 @@ int32_t et_b200_o2_optimizer_create_v1(size_t count, const et_b200_o2_parameter_
   ok = ok && cudaMalloc(&o->d_prefix, (count + 1) * sizeof(uint64_t)) == cudaSuccess;
   ok = ok && cudaMalloc(&o->d_partials, kNormPartials * sizeof(double)) == cudaSuccess;
   ok = ok && cudaMalloc(&o->d_sumsq, sizeof(double)) == cudaSuccess;
-  ok = ok && cudaMalloc(&o->d_status, 2 * sizeof(int)) == cudaSuccess;
+  ok = ok && cudaMalloc(&o->d_status, 3 * sizeof(int)) == cudaSuccess;
   if (!ok) {
     et_b200_o2_optimizer_destroy_v1(&o);
     return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_ALLOCATION_FAILED, op, "cannot allocate optimizer state");
   }
   cudaMemcpy(o->d_prefix, o->prefix.data(), o->prefix.size() * sizeof(uint64_t), cudaMemcpyHostToDevice);
-  cudaMemset(o->d_status, 0, 2 * sizeof(int));
+  cudaMemset(o->d_status, 0, 3 * sizeof(int));
   o->table.resize(count);
+  o->vec = true;
+  for (size_t i = 0; i < count; i++)
+    o->vec = o->vec && params[i].count % 4 == 0 && ((uintptr_t)params[i].value & 15) == 0 &&
+             ((uintptr_t)params[i].gradient & 15) == 0;
   cudaDeviceSynchronize();
   *out = o;
   if (e) memset(e, 0, sizeof(*e));
@@ -263,7 +268,7 @@ int32_t et_b200_o2_optimizer_step_v1(et_b200_o2_optimizer* o, uint32_t weight_bi
   }
   cudaMemcpyAsync(o->d_table, o->table.data(), o->table.size() * sizeof(AdamwTensor),
                   cudaMemcpyHostToDevice, o->stream);
-  cudaMemsetAsync(o->d_status, 0, 2 * sizeof(int), o->stream);
+  cudaMemsetAsync(o->d_status, 0, 3 * sizeof(int), o->stream);
   grad_sumsq(o->d_table, o->d_prefix, (int)o->table.size(), o->elems, weight, o->d_partials,
              kNormPartials, o->d_sumsq, o->d_status, o->stream);
   double sumsq = 0.0;
@@ -283,13 +288,24 @@ int32_t et_b200_o2_optimizer_step_v1(et_b200_o2_optimizer* o, uint32_t weight_bi
     volatile float mx = f_of(o->clip_max_bits);
     clip = mx / norm;
   }
-  adamw_multi(o->d_table, o->d_prefix, (int)o->table.size(), o->elems, weight, clip, o->d_status,
+  // all or nothing: the check pass computes every update without writing;
+  // the apply pass writes only when the check set no status bit
+  const AdamwControl ctl{nullptr, o->d_status, nullptr};
+  adamw_check(o->d_table, o->d_prefix, (int)o->table.size(), o->elems, weight, clip, ctl, o->vec,
               o->stream);
-  cudaMemcpyAsync(status, o->d_status, sizeof(status), cudaMemcpyDeviceToHost, o->stream);
+  adamw_apply(o->d_table, o->d_prefix, (int)o->table.size(), o->elems, weight, clip, ctl, o->vec,
+              o->stream);
+  int after[3] = {0, 0, 0};
+  cudaMemcpyAsync(after, o->d_status, sizeof(after), cudaMemcpyDeviceToHost, o->stream);
   st = cudaStreamSynchronize(o->stream);
+  if (st == cudaSuccess) st = cudaGetLastError();
   if (st != cudaSuccess) return cuda_error(e, st, op);
-  if (status[1])
-    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op, "AdamW produced a nonfinite value");
+  if (after[1] & kAdamwInputNonfinite)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "parameter, gradient, or moment is nonfinite");
+  if (after[1] & kAdamwProducedNonfinite)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "AdamW produced a nonfinite value");
   o->updates = update;
   if (e) memset(e, 0, sizeof(*e));
   return 0;

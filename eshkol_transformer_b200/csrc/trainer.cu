@@ -52,6 +52,10 @@ enum { S_H1 = 0, S_AO, S_H2, S_G, S_DXF, S_DU, S_DXA, S_DQKV, kSlotsPerLayer };
 // puts every slot's max above 65,504, which exercises the overflow check and
 // the 3xTF32 redo.
 constexpr int kScaleTarget = 10;
+// Step-void flag increment for an out-of-range token id or target; below it,
+// the count of ranks whose split-f16 operands overflowed (exact in f32 for
+// any world size below 256).
+constexpr float kVoidIndex = 65536.0f;
 enum {
   T_LN1G = 0, T_LN1B, T_WQKV, T_BQKV, T_WO, T_BO, T_LN2G, T_LN2B, T_W1, T_B1, T_W2, T_B2
 };
@@ -59,7 +63,7 @@ enum {
 // Profile classes reported by et_b200_lm_profile_read_v1.
 enum {
   P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_CE, P_ADAMW, P_NORM, P_ELEMENTWISE, P_EMBED,
-  P_SPLIT, P_ALLREDUCE_WAIT, P_COUNT
+  P_SPLIT, P_ALLREDUCE_WAIT, P_ADAMW_CHECK, P_COUNT
 };
 
 struct LayerActs {
@@ -103,7 +107,9 @@ struct et_b200_lm {
   float *whi = nullptr, *wlo = nullptr;
   AdamwTensor* d_adam = nullptr;
   uint64_t* d_prefix = nullptr;
-  uint64_t updates = 0;
+  uint64_t updates = 0;          // host copy of *d_completed at the last synchronisation
+  uint64_t* d_completed = nullptr;  // applied AdamW updates (device counter)
+  uint64_t skipped = 0;          // device-enqueued steps whose update was not applied
   // activations
   std::vector<LayerActs> layers;
   float *x_final = nullptr, *xf = nullptr, *xflo = nullptr, *muf = nullptr, *rsf = nullptr;
@@ -124,7 +130,9 @@ struct et_b200_lm {
   void* emb_scratch = nullptr;
   int64_t *ids = nullptr, *targets = nullptr, *pos = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
-  int* status = nullptr;  // [0] index range, [1] optimizer nonfinite
+  // [0] a token id or target of this step is out of range; [1] this step's
+  // AdamW check bits (kAdamw*); [2] updates skipped since the last host read
+  int* status = nullptr;
   std::vector<void*> allocations;
   // data parallel
   ncclComm_t nccl_comm = nullptr;
@@ -591,14 +599,17 @@ void backward(et_b200_lm* lm) {
     Mark mk(lm, P_EMBED, 0, 12.0 * V * d + 8.0 * R * d);
     embedding_backward(lm->ids, lm->dx, lm->G(0), lm->G(0), R, V, d, lm->emb_scratch, s);
   }
-  // split-f16 steps: did an operand reach binary16's overflow?  (the flag at
-  // grads[P] rides the last gradient reduction, so every rank agrees)
+  // The step-void flag at grads[P] rides the last gradient reduction, so
+  // every rank agrees on skipping AdamW: + kVoidIndex for a token id or
+  // target out of range, + 1 (split-f16 steps) for an operand that reached
+  // binary16's overflow.
+  fold_index_flag(lm->status, lm->grads + lm->P, kVoidIndex, s);
   if (lm->step16)
     operand_range_check(lm->samax, lm->sexp, lm->nslots, lm->slot_w(), lm->grads + lm->P, s);
   if (lm->dp) {
     allreduce_range(lm, 0, 1, lm->tail_done);
     const int lg = lm->lnf_g();
-    const size_t end = lm->f16 ? lm->P + 1 : lm->off[lg + 1] + lm->sz[lg + 1];
+    const size_t end = lm->P + 1;
     nccl().AllReduce(lm->G(lg), lm->G(lg), end - lm->off[lg], ncclFloat32, ncclSum,
                      lm->nccl_comm, lm->comm);
     cudaEventRecord(lm->comm_done, lm->comm);
@@ -627,9 +638,11 @@ void weight_scale(et_b200_lm* lm) {
 // binary16 pairs once a finished step has measured every slot, else 3xTF32
 // with the TF32 weight pair and every slot's max recorded.
 void begin_step(et_b200_lm* lm) {
+  // the step-void flag behind the gradients and this step's status words
+  cudaMemsetAsync(lm->grads + lm->P, 0, sizeof(float), lm->stream);
+  cudaMemsetAsync(lm->status, 0, 2 * sizeof(int), lm->stream);
   if (!lm->f16) return;
   lm->step16 = lm->calibrated;
-  cudaMemsetAsync(lm->grads + lm->P, 0, sizeof(float), lm->stream);  // range flag
   if (lm->step16) {
     // exponents of the activation / gradient slots from the last step's maxima
     scale_from_amax(lm->samax, lm->sexp, lm->slot_w(), lm->scale_target, 1, lm->stream);
@@ -650,7 +663,6 @@ void begin_step(et_b200_lm* lm) {
 
 void optimizer_step(et_b200_lm* lm) {
   const et_b200_lm_config_v1& c = lm->cfg;
-  const uint64_t t = lm->updates + 1;
   AdamwTensor h{};
   h.value = lm->params;
   h.grad = lm->grads;
@@ -663,8 +675,7 @@ void optimizer_step(et_b200_lm* lm) {
   h.beta2 = b2;
   h.one_minus_beta1 = one - b1;
   h.one_minus_beta2 = one - b2;
-  h.bias1 = one - pow_steps(b1, t);
-  h.bias2 = one - pow_steps(b2, t);
+  // bias1 / bias2 come from the device's update counter (adamw_prepare)
   volatile float lr = fbits(c.learning_rate_bits) * 1.0f;  // constant schedule factor 1
   volatile float lrwd = lr * fbits(c.weight_decay_bits);
   h.lr = lr;
@@ -676,13 +687,19 @@ void optimizer_step(et_b200_lm* lm) {
   h.value_lo = lm->three ? lm->wlo : nullptr;
   if (lm->f16) h.value_sc = OperandScale{lm->sexp + lm->slot_w(), lm->samax + lm->slot_w(), 1};
   cudaMemcpyAsync(lm->d_adam, &h, sizeof(h), cudaMemcpyHostToDevice, lm->stream);
+  adamw_prepare(lm->d_adam, lm->d_completed, lm->stream);
+  // all or nothing: skipped when the step is void (flag summed across ranks)
+  // or when the check pass finds a nonfinite gradient, moment or result
+  const AdamwControl ctl{lm->grads + lm->P, lm->status, lm->d_completed};
+  {
+    Mark mk(lm, P_ADAMW_CHECK, 0, 16.0 * lm->P);
+    adamw_check(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, ctl, true, lm->stream);
+  }
   {
     Mark mk(lm, P_ADAMW, 0, (lm->f16 ? 32.0 : lm->three ? 36.0 : 28.0) * lm->P);
-    adamw_multi(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, lm->status, lm->stream,
-                lm->f16 ? lm->grads + lm->P : nullptr);
+    adamw_apply(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, ctl, true, lm->stream);
   }
   if (lm->f16) lm->w16_valid = true;
-  lm->updates = t;
 }
 
 int32_t check_ready(et_b200_lm* lm, et_kernel_error* e, const char* op) {
@@ -693,47 +710,56 @@ int32_t check_ready(et_b200_lm* lm, et_kernel_error* e, const char* op) {
 
 // Reads the loss and the flags of the step just enqueued.  *redo: a
 // split-f16 step that was not applied (an operand reached binary16's
-// overflow); `update`: the step ran AdamW.
+// overflow on some rank); `update`: the step ran the AdamW passes.  A step
+// that fails here has left parameters, moments and the update counter as
+// they were.  Updates skipped by steps enqueued with
+// et_b200_lm_step_device_v1 since the last synchronised call are added to
+// the skipped-update counter, not reported as this call's error.
 int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, const char* op,
                          bool update, bool* redo) {
-  float loss = 0.0f, range = 0.0f;
+  float loss = 0.0f, flag = 0.0f;
   int flags[3] = {0, 0, 0};
   int word = 0;
+  uint64_t completed = 0;
   *redo = false;
   cudaMemcpyAsync(&loss, lm->loss_mean, sizeof(float), cudaMemcpyDeviceToHost, lm->stream);
   cudaMemcpyAsync(flags, lm->status, sizeof(flags), cudaMemcpyDeviceToHost, lm->stream);
   cudaMemcpyAsync(&word, device_error_word(), sizeof(int), cudaMemcpyDeviceToHost, lm->stream);
-  if (lm->f16)
-    cudaMemcpyAsync(&range, lm->grads + lm->P, sizeof(float), cudaMemcpyDeviceToHost, lm->stream);
+  cudaMemcpyAsync(&flag, lm->grads + lm->P, sizeof(float), cudaMemcpyDeviceToHost, lm->stream);
+  cudaMemcpyAsync(&completed, lm->d_completed, sizeof(completed), cudaMemcpyDeviceToHost,
+                  lm->stream);
   cudaError_t st = cudaStreamSynchronize(lm->stream);
   if (st != cudaSuccess) return cuda_error(e, st, op);
   if (host_loss) *host_loss = loss;
-  const bool skipped = lm->step16 && range != 0.0f;
-  // status[2] counts the steps AdamW skipped: this one, and any enqueued by
-  // et_b200_lm_step_device_v1 since the last host-synchronised call
-  const int earlier = flags[2] - (skipped && update ? 1 : 0);
+  lm->updates = completed;
+  const bool void_step = flag != 0.0f || (update && flags[1] != 0);
   if (flags[2] != 0) {
+    lm->skipped += (uint64_t)(flags[2] - (update && void_step ? 1 : 0));
     cudaMemsetAsync(lm->status + 2, 0, sizeof(int), lm->stream);
     cudaStreamSynchronize(lm->stream);
-  }
-  if (earlier > 0) {
-    lm->calibrated = false;
-    return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
-                     "a device-enqueued step had an operand beyond its binary16 range and was not applied");
+    // a skipped device step may have been a split-f16 overflow: re-measure
+    if (lm->f16) lm->calibrated = false;
   }
   if (word != 0) {
     cudaMemset(device_error_word(), 0, sizeof(int));
     return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
                      "a device pipeline wait timed out");
   }
-  if (flags[0] || flags[1]) {
-    cudaMemsetAsync(lm->status, 0, 2 * sizeof(int), lm->stream);
-    cudaStreamSynchronize(lm->stream);
+  if (flag >= kVoidIndex)
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
-                     flags[0] ? "token id or target outside the vocabulary"
-                              : "AdamW produced a nonfinite value");
+                     flags[0] ? "token id or target outside the vocabulary; nothing was updated"
+                              : "another rank's token id or target is outside the vocabulary; "
+                                "nothing was updated");
+  if (flag != 0.0f && lm->step16) {
+    *redo = true;
+    return 0;
   }
-  *redo = skipped;
+  if (update && (flags[1] & kAdamwInputNonfinite))
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "parameter, gradient, or moment is nonfinite; nothing was updated");
+  if (update && (flags[1] & kAdamwProducedNonfinite))
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     "AdamW produced a nonfinite value; nothing was updated");
   if (e) memset(e, 0, sizeof(*e));
   return 0;
 }
@@ -760,7 +786,6 @@ int32_t run_host_step(et_b200_lm* lm, bool update, float* host_loss, et_kernel_e
     }
     lm->calibrated = false;
     lm->redone_steps++;
-    if (update) lm->updates -= 1;
   }
   return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
                    "the step's operands stayed outside their binary16 range");
@@ -924,6 +949,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->rope_cos = dalloc<float>(lm, lm->T * lm->Dh / 2, &err);
   lm->rope_sin = dalloc<float>(lm, lm->T * lm->Dh / 2, &err);
   lm->status = dalloc<int>(lm, 4, &err);
+  lm->d_completed = dalloc<uint64_t>(lm, 1, &err);
   if (err != cudaSuccess) {
     et_b200_lm_destroy_v1(&lm);
     return set_error(e, ET_KERNEL_ERROR_INTERNAL, ET_KERNEL_CODE_ALLOCATION_FAILED, op,
@@ -957,6 +983,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   cudaMemset(lm->m1, 0, lm->P * sizeof(float));
   cudaMemset(lm->m2, 0, lm->P * sizeof(float));
   cudaMemset(lm->status, 0, 4 * sizeof(int));
+  cudaMemset(lm->d_completed, 0, sizeof(uint64_t));
   lm->layer_done.resize(L);
   for (auto& ev : lm->layer_done) cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
   cudaEventCreateWithFlags(&lm->tail_done, cudaEventDisableTiming);
@@ -1067,7 +1094,9 @@ int32_t et_b200_lm_init_v1(et_b200_lm* lm, uint64_t seed, et_kernel_error* e) {
       for (size_t i = 0; i < lm->sz[t]; i++) host[packed + i] = kind == 1 ? 1.0f : 0.0f;
     packed += lm->sz[t];
   }
+  cudaStreamSynchronize(lm->stream);
   lm->updates = 0;
+  cudaMemset(lm->d_completed, 0, sizeof(uint64_t));
   cudaMemset(lm->m1, 0, lm->P * sizeof(float));
   cudaMemset(lm->m2, 0, lm->P * sizeof(float));
   return et_b200_lm_write_v1(lm, 0, host.data(), n, e);
@@ -1180,6 +1209,26 @@ int32_t et_b200_lm_profile_collect_v1(et_b200_lm* lm) {
 
 int32_t et_b200_lm_f16_redone_steps_v1(const et_b200_lm* lm) {
   return lm ? lm->redone_steps : 0;
+}
+
+int32_t et_b200_lm_update_counts_v1(et_b200_lm* lm, uint64_t* completed, uint64_t* skipped,
+                                    et_kernel_error* e) {
+  const char* op = "lm-update-counts";
+  if (check_ready(lm, e, op)) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  uint64_t done = 0;
+  int pending = 0;
+  cudaMemcpyAsync(&done, lm->d_completed, sizeof(done), cudaMemcpyDeviceToHost, lm->stream);
+  cudaMemcpyAsync(&pending, lm->status + 2, sizeof(int), cudaMemcpyDeviceToHost, lm->stream);
+  cudaMemsetAsync(lm->status + 2, 0, sizeof(int), lm->stream);
+  cudaError_t st = cudaStreamSynchronize(lm->stream);
+  if (st != cudaSuccess) return cuda_error(e, st, op);
+  lm->updates = done;
+  lm->skipped += (uint64_t)pending;
+  if (pending != 0 && lm->f16) lm->calibrated = false;
+  if (completed) *completed = lm->updates;
+  if (skipped) *skipped = lm->skipped;
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
 }
 
 int32_t et_b200_lm_profile_read_v1(et_b200_lm* lm, double* out, size_t count) {

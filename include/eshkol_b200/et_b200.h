@@ -104,7 +104,14 @@ int32_t et_b200_o2_optimizer_create_v1(
     et_kernel_error *error);
 /* replaces et_o2_optimizer_step_v1 (native/o2_optimizer.c:1784-1944).
  * normalization_weight_bits is the f32 bit pattern of the accumulated
- * contribution weight.  norm_bits (optional) receives the global norm. */
+ * contribution weight.  norm_bits (optional) receives the global norm.  All
+ * or nothing like the reference's staged commit: a nonfinite gradient,
+ * parameter or moment, or an update that would be nonfinite, leaves every
+ * tensor and the update counter unchanged and returns INVALID_ARGUMENT.  The
+ * global norm is an f64 sum of squares rounded once to f32; the reference's
+ * is a scaled f32 recurrence in parameter order (o2_optimizer.c:1548-1618),
+ * so the two norms (and with clipping active, the clipped updates) can differ
+ * in the last bits. */
 int32_t et_b200_o2_optimizer_step_v1(et_b200_o2_optimizer *optimizer,
                                      uint32_t normalization_weight_bits,
                                      uint32_t *norm_bits,
@@ -134,8 +141,11 @@ void et_b200_o2_optimizer_destroy_v1(et_b200_o2_optimizer **optimizer);
  * device looks up the array's device address (cudaGetSymbolAddress) and
  * should come before any stream capture.  Enqueued on `stream` (a
  * cudaStream_t, NULL = legacy default stream) and synchronised before
- * returning; norm_bits (optional) receives the norm.  A nonfinite gradient
- * leaves every tensor unchanged and returns INVALID_ARGUMENT. */
+ * returning; norm_bits (optional) receives the norm.  The update is all or
+ * nothing: a nonfinite gradient, a norm beyond f32's range, a nonfinite
+ * parameter or moment, or an update that would produce a nonfinite value
+ * leaves every tensor unchanged and returns INVALID_ARGUMENT (messages as
+ * the reference's optimizer-step!). */
 #define ET_B200_ADAMW_NOALLOC_MAX_ELEMENTS ((uint64_t)8192u * 65536u)
 int32_t et_b200_adamw_step_noalloc_v1(
     float *value, const float *gradient, float *exp_avg, float *exp_avg_sq,
@@ -207,13 +217,22 @@ int32_t et_b200_lm_write_v1(et_b200_lm *lm, int32_t which, const float *host,
                             size_t count, et_kernel_error *error);
 /* One training step from HOST token ids/targets [batch, seq_len]: copies
  * them in, runs forward, backward (with the data-parallel gradient allreduce
- * when enabled), the AdamW update, and copies the mean loss out. */
+ * when enabled), the AdamW update, and copies the mean loss out.  The update
+ * is all or nothing, as O2's staged commit is (o2_optimizer.c:1813-1926): a
+ * token id or target outside the vocabulary (on any rank), a nonfinite
+ * gradient, parameter or moment, or an update that would be nonfinite leaves
+ * parameters, moments and the update counter unchanged and returns
+ * INVALID_ARGUMENT. */
 int32_t et_b200_lm_step_v1(et_b200_lm *lm, const int64_t *host_ids,
                            const int64_t *host_targets, float *host_loss,
                            et_kernel_error *error);
 /* The same step on DEVICE-resident ids/targets; the mean loss stays on the
  * device (device_loss may be NULL).  Enqueued on the model's stream; returns
- * without synchronising. */
+ * without synchronising.  A step the host call above would reject is
+ * skipped on the device with nothing updated; such steps are counted by
+ * et_b200_lm_update_counts_v1 (the update number of later steps is taken
+ * from the device's count of applied updates, so skipped steps do not shift
+ * the bias corrections). */
 int32_t et_b200_lm_step_device_v1(et_b200_lm *lm, const int64_t *device_ids,
                                   const int64_t *device_targets,
                                   float *device_loss, et_kernel_error *error);
@@ -237,8 +256,9 @@ int32_t et_b200_lm_enable_data_parallel_v1(et_b200_lm *lm,
                                            et_kernel_error *error);
 /* Per-kernel-class timing with CUDA events on the model's stream.  Classes,
  * in order: 0 GEMM, 1 attention forward, 2 attention backward, 3 cross-
- * entropy, 4 AdamW, 5 LayerNorm, 6 other elementwise, 7 embedding, 8 TF32
- * split, 9 allreduce wait.  read fills count >= 40 doubles: per class
+ * entropy, 4 AdamW (the writing pass), 5 LayerNorm, 6 other elementwise,
+ * 7 embedding, 8 TF32 split, 9 allreduce wait, 10 AdamW check pass.  read
+ * fills count >= 44 doubles: per class
  * {launch groups, milliseconds, algorithmic FLOP, algorithmic bytes}
  * accumulated since profiling was enabled; collect folds the events of
  * device-side steps into those totals (host steps do it themselves). */
@@ -250,6 +270,13 @@ int32_t et_b200_lm_profile_read_v1(et_b200_lm *lm, double *out, size_t count);
  * redone with 3xTF32 contractions since the model was created (0 for other
  * modes).  No reference counterpart: the reference has one contraction mode. */
 int32_t et_b200_lm_f16_redone_steps_v1(const et_b200_lm *lm);
+/* Applied AdamW updates (the reference's completed_updates,
+ * o2_optimizer.c:1929) and device-enqueued steps whose update was skipped
+ * since the model was created; synchronises the model's stream.  No
+ * reference counterpart for `skipped`: reference steps are host calls that
+ * return their error. */
+int32_t et_b200_lm_update_counts_v1(et_b200_lm *lm, uint64_t *completed,
+                                    uint64_t *skipped, et_kernel_error *error);
 
 /* ------------------------------------------------------------ A2 KV cache
  *
@@ -287,7 +314,10 @@ int32_t et_a2_kv_cache_transaction_begin_v1(
     et_a2_kv_cache *cache, uint64_t append_width,
     const et_kernel_tensor_view_v1 *append_counts,
     et_a2_kv_cache_transaction **transaction, et_kernel_error *error);
-/* replaces a2_kv_cache.h:87-96 ("cpu" or "cuda" sources) */
+/* replaces a2_kv_cache.h:87-96 ("cpu" or "cuda" sources).  "cuda" sources
+ * are read after a device synchronisation, so work that produced them on any
+ * stream of that device (and was enqueued before this call) has finished;
+ * work enqueued later, from another host thread, is not waited for. */
 int32_t et_a2_kv_cache_transaction_stage_layer_v1(
     et_a2_kv_cache_transaction *transaction, uint64_t layer,
     const et_kernel_tensor_view_v1 *keys,

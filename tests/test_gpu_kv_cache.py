@@ -223,3 +223,29 @@ def test_cached_decoding_matches_full_attention_and_reference_fixture(apis, lib)
         assert ours.view_end(view)[0] == 0
         assert ours.commit(txn)[0] == 0
     assert ours.destroy(cache)[0] == 0
+
+
+def test_device_sources_from_another_stream_need_no_sync(apis):
+    """K/V sources written on the caller's own stream just before
+    stage_layer, with no synchronisation in between: the stage must see the
+    finished values (the cache orders its reads after that work)."""
+    ours, ref = apis
+    rng = np.random.default_rng(11)
+    co, cr = ours.create(L, N, H, CAP, D)[2], ref.create(L, N, H, CAP, D)[2]
+    counts = np.array([2, 1, 2], np.int64)
+    to, tr = ours.begin(co, 2, counts)[2], ref.begin(cr, 2, counts)[2]
+    for layer in range(L):
+        k, v, kd_src, vd_src = source(rng, 2, "cuda")
+        torch.cuda.synchronize()
+        producer = torch.cuda.Stream()
+        with torch.cuda.stream(producer):
+            kd = torch.zeros_like(kd_src)
+            vd = torch.zeros_like(vd_src)
+            torch.cuda._sleep(50_000_000)  # the copies below land tens of ms later
+            kd.copy_(kd_src)
+            vd.copy_(vd_src)
+        assert outcome(ours.stage(to, layer, kd, vd)) == (0, 0, 0)
+        assert outcome(ref.stage(tr, layer, k, v)) == (0, 0, 0)
+    assert outcome(ours.commit(to)) == outcome(ref.commit(tr)) == (0, 0, 0)
+    same_state(ours, ref, co, cr)
+    assert outcome(ours.destroy(co)) == outcome(ref.destroy(cr)) == (0, 0, 0)

@@ -119,3 +119,35 @@ def test_noalloc_rejects_oversize_and_nonfinite(lib, cuda):
     rc, err, norm = _step(fn, p, g, m, v, n, 1, 1.0)
     assert rc == 0, str(err)
     assert abs(norm - float(torch.linalg.vector_norm(g.double()))) <= 1e-6 * norm
+
+
+def test_noalloc_leaves_tensors_untouched_on_any_nonfinite(lib, cuda):
+    """All or nothing, as the reference's staged commit: an update that would
+    overflow (finite gradient 1e20: its square is beyond f32), a nonfinite
+    moment, and finite gradients whose norm is beyond f32 each return
+    INVALID_ARGUMENT with the reference's message and leave parameter and
+    moments bit-unchanged."""
+    fn = _entry(lib)
+    n = 70_000  # two norm partials
+    p = torch.from_numpy(etb.fill_normal(31, 0, n)).cuda()
+    m = torch.from_numpy(etb.fill_normal(31, 1, n, 0.0, 1e-3)).cuda()
+    v = torch.from_numpy(np.abs(etb.fill_normal(31, 2, n, 0.0, 1e-3))).cuda()
+    g = torch.from_numpy(etb.fill_normal(31, 3, n)).cuda()
+    cases = []
+    g1 = g.clone()
+    g1[n - 5] = 1e20
+    cases.append((g1, m.clone(), b"AdamW produced a nonfinite value"))
+    m2 = m.clone()
+    m2[3] = float("inf")
+    cases.append((g.clone(), m2, b"parameter, gradient, or moment is nonfinite"))
+    g3 = torch.full((n,), 1e38, device="cuda")
+    cases.append((g3, m.clone(), b"gradient norm is unrepresentable"))
+    for grad, mom, message in cases:
+        pc, vc = p.clone(), v.clone()
+        mc = mom.clone()
+        rc, err, _ = _step(fn, pc, grad, mc, vc, n, 3, 1.0)
+        assert rc == k1.ERROR_INVALID_ARGUMENT, message
+        assert message in err.message, (message, err.message)
+        assert _bits_equal(pc, p) and _bits_equal(mc, mom) and _bits_equal(vc, v), message
+    rc, err, _ = _step(fn, p, g, m, v, n, 3, 1.0)  # and the next finite call applies
+    assert rc == 0, str(err)
