@@ -342,26 +342,23 @@ def run_b200(args) -> None:
 # ----------------------------------------------------------------- CPU arm
 
 def cpu_baseline(kind: str = "port", budget_s: float = 20.0) -> dict:
-    """Sampled per-operation timing of the CPU implementation of one training
-    step of the workload, scaled to tokens/s by the step's operation counts.
+    """The CPU implementation of one training step of the workload, timed per
+    operation on a token sample and scaled to tokens/s by the step's
+    operation counts (a full step takes hours on the CPU).
 
-    kind "port": the oracle restatement (OpenMP over the host cores);
-    kind "reference": the reference's own C providers (oracle/_ref, serial),
-    with AdamW from the port (the O2 optimizer needs the reference's tensor
-    carriers and is 28 B/parameter of streaming work either way).
+    kind "port": the oracle restatement (OpenMP over the host cores).
+    kind "reference": the reference's own C code only (oracle/_ref), serial
+    as the reference is -- see reference_step_sample.
     """
-    import ctypes as C
-
+    if kind == "reference":
+        return reference_step_sample()
     from oracle import oracle as orc
 
-    ref = orc.ref() if kind == "reference" else None
-    if kind == "reference" and ref is None:
-        kind = "port"
-    threads = os.cpu_count() or 1 if kind == "port" else 1
+    threads = os.cpu_count() or 1
     L, d, H, F, V, T = (SHAPE[k] for k in ("layers", "d_model", "heads", "ffn", "vocabulary",
                                          "seq_len"))
     Dh = d // H
-    S = 16 if kind == "reference" else 64  # token sample for the contractions
+    S = 64  # token sample for the contractions
     rows = S
     t = {}
 
@@ -379,18 +376,6 @@ def cpu_baseline(kind: str = "port", budget_s: float = 20.0) -> dict:
         w = orc.fill_normal(1, 3, dout * din, 0, 0.02).reshape(dout, din)
         b = np.zeros(dout, np.float32)
         g = dy[:rows * dout].reshape(1, rows, dout)
-        if ref is not None:
-            y = np.empty((1, rows, dout), np.float32)
-            dx = np.empty_like(xi)
-            dw = np.empty_like(w)
-            db = np.empty(dout, np.float32)
-            p = lambda a: a.ctypes.data_as(C.c_void_p)
-            return lambda: (ref.ref_n2_linear_forward(C.c_size_t(1), C.c_size_t(rows),
-                                                      C.c_size_t(din), C.c_size_t(dout), p(xi),
-                                                      p(w), p(b), p(y)),
-                            ref.ref_n2_linear_backward(C.c_size_t(1), C.c_size_t(rows),
-                                                       C.c_size_t(din), C.c_size_t(dout), p(xi),
-                                                       p(w), p(g), 1, p(dx), p(dw), p(db)))
         return lambda: (orc.linear_forward(xi, w, b), orc.linear_backward(xi, w, g))
 
     timed("qkv", linear_pair(d, 3 * d))
@@ -407,16 +392,14 @@ def cpu_baseline(kind: str = "port", budget_s: float = 20.0) -> dict:
     orc.linear_backward(xh, wh, gh, with_bias=False)
     head = (time.perf_counter() - t0) * S / Sh
     # attention at the full sequence length for one (sequence, head), scaled
-    shp = (1, 1, 1, T, T, Dh) if kind == "port" else (1, 1, 1, 256, 256, Dh)
-    Ta = shp[3]
-    q = orc.fill_normal(2, 1, Ta * Dh).reshape(1, 1, Ta, Dh)
-    pos = np.arange(Ta, dtype=np.int64).reshape(1, Ta)
-    mask = np.ones((1, Ta, Ta), np.uint8)
+    shp = (1, 1, 1, T, T, Dh)
+    q = orc.fill_normal(2, 1, T * Dh).reshape(1, 1, T, Dh)
+    pos = np.arange(T, dtype=np.int64).reshape(1, T)
+    mask = np.ones((1, T, T), np.uint8)
     t0 = time.perf_counter()
     orc.attention_forward(shp, q, q, q, pos, pos, mask)
     orc.attention_backward(shp, q, q, q, pos, pos, mask, q)
-    att_one = (time.perf_counter() - t0) * (T / Ta) ** 2  # O(T^2) per (sequence, head)
-    att_per_token = att_one * H / T
+    att_per_token = (time.perf_counter() - t0) * H / T
     # LN / GELU / CE / AdamW per element, sampled
     xl = orc.fill_normal(3, 1, rows * d).reshape(1, rows, d)
     gam = np.ones(d, np.float32)
@@ -444,10 +427,166 @@ def cpu_baseline(kind: str = "port", budget_s: float = 20.0) -> dict:
     adam = (time.perf_counter() - t0) * n_params / (1 << 20)
     per_token = ((t["qkv"] + t["out"] + t["up"] + t["down"] + 2 * ln + gelu) * L + head + ln
                  + ce) / S + att_per_token * L + adam / (GLOBAL_BATCH * T)
-    return {"value": round(1.0 / per_token, 3), "unit": UNIT, "cores": threads, "kind": kind,
+    return {"value": round(1.0 / per_token, 3), "unit": UNIT, "cores": threads, "kind": "port",
             "sample": (f"per-op timing on {S} tokens of the {WORKLOAD} step (tied head on {Sh} "
-                       f"tokens, attention on one (sequence, head) at T={Ta} scaled by (T/{Ta})^2, "
-                       f"AdamW on 2^20 parameters) scaled by the step's operation counts")}
+                       f"tokens, attention on one (sequence, head) at T={T}, AdamW on 2^20 "
+                       f"parameters) scaled by the step's operation counts")}
+
+
+_REF_O2_READY = False
+
+
+def reference_step_sample(S: int = 16, Ta: int = 256) -> dict:
+    """The reference's own C code (compiled unmodified into oracle/_ref) timed
+    per operation on one host core, then scaled to one step of the workload.
+
+    * the N2 runners: QKV / output / FFN linears and the tied head (forward
+      and backward), LayerNorm forward/backward (3 per layer-step: 2 per
+      layer + the final one), GELU forward/backward, embedding
+      forward/backward -- on S tokens;
+    * A2 through its provider's invoke_call: rope.forward on Q and K,
+      causal-attention.forward, causal-attention.backward, rope.backward on
+      dQ and dK, at [1 sequence, 2 heads, T=Ta] (validate_call, whose cost is
+      O(T^3 Dh^2), is not part of a step and is not timed), scaled by
+      (T/Ta)^2 and heads/2;
+    * L2 through its provider's invoke_call: indexed-cross-entropy forward
+      and backward over S rows of V logits;
+    * O2 through its API: an I2 gradient-plan accumulation, the AdamW step and
+      zero_grad over one 2^20-element parameter, scaled to the model's count.
+    The step time is extrapolated from these samples ("extrapolated": true).
+    """
+    import ctypes as C
+
+    from eshkol_transformer_b200 import k1
+    from oracle import oracle as orc
+
+    global _REF_O2_READY
+    ref = orc.ref()
+    if ref is None:
+        raise SystemExit("oracle/_ref/libref.so is not built (the reference's C sources)")
+    L, d, H, F, V, T = (SHAPE[k] for k in ("layers", "d_model", "heads", "ffn", "vocabulary",
+                                         "seq_len"))
+    Dh = d // H
+    p = lambda a: a.ctypes.data_as(C.c_void_p)
+    sz = C.c_size_t
+    secs = {}
+
+    def timed(name, fn):
+        t0 = time.perf_counter()
+        rc = fn()
+        secs[name] = time.perf_counter() - t0
+        return rc
+
+    x = orc.fill_normal(1, 1, S * F)
+    dy = orc.fill_normal(1, 2, S * F)
+
+    def linear(name, din, dout, bias=True, tokens=S):
+        xi = np.ascontiguousarray(x[:tokens * din])
+        w = orc.fill_normal(1, 3, dout * din, 0, 0.02)
+        b = np.zeros(dout, np.float32)
+        g = np.ascontiguousarray(dy[:tokens * dout]) if tokens * dout <= dy.size else \
+            orc.fill_normal(1, 5, tokens * dout)
+        y = np.empty(tokens * dout, np.float32)
+        dx, dw, db = np.empty_like(xi), np.empty_like(w), np.empty(dout, np.float32)
+        timed(name, lambda: (
+            ref.ref_n2_linear_forward(sz(1), sz(tokens), sz(din), sz(dout), p(xi), p(w),
+                                      p(b) if bias else None, p(y)),
+            ref.ref_n2_linear_backward(sz(1), sz(tokens), sz(din), sz(dout), p(xi), p(w), p(g),
+                                       1 if bias else 0, p(dx), p(dw),
+                                       p(db) if bias else None)))
+
+    linear("qkv", d, 3 * d)
+    linear("out", d, d)
+    linear("up", d, F)
+    linear("down", F, d)
+    Sh = max(2, S // 4)  # the tied head is the largest contraction
+    linear("head", d, V, bias=False, tokens=Sh)
+    secs["head"] *= S / Sh
+    xl = np.ascontiguousarray(x[:S * d])
+    gam, bet = np.ones(d, np.float32), np.zeros(d, np.float32)
+    yl, dxl = np.empty_like(xl), np.empty_like(xl)
+    dgam, dbet = np.empty(d, np.float32), np.empty(d, np.float32)
+    eps = C.c_float(1e-5)
+    timed("layer_norm", lambda: (
+        ref.ref_n2_layer_norm_forward(sz(1), sz(S), sz(d), p(xl), p(gam), p(bet), eps, p(yl)),
+        ref.ref_n2_layer_norm_backward(sz(1), sz(S), sz(d), p(xl), p(gam), eps, p(xl), p(dxl),
+                                       p(dgam), p(dbet))))
+    u = np.ascontiguousarray(x[:S * F])
+    gu, du = np.empty_like(u), np.empty_like(u)
+    timed("gelu", lambda: (ref.ref_n2_gelu(sz(1), sz(S), sz(F), p(u), None, p(gu)),
+                           ref.ref_n2_gelu(sz(1), sz(S), sz(F), p(u), p(u), p(du))))
+    ids = orc.fill_tokens(3, 1, S, V)
+    emb = orc.fill_normal(3, 4, V * d, 0, 0.02)
+    ye, dwe = np.empty(S * d, np.float32), np.empty(V * d, np.float32)
+    timed("embedding", lambda: (
+        ref.ref_n2_embedding_forward(sz(1), sz(S), sz(V), sz(d), p(ids), p(emb), p(ye)),
+        ref.ref_n2_embedding_backward(sz(1), sz(S), sz(V), sz(d), p(ids), p(xl), p(dwe))))
+    # A2: rope + attention forward/backward through invoke_call
+    a2 = k1.provider(ref, "et_a2_kernel_provider_v1")
+    Ha = 2
+    q, kk, vv, go = (orc.fill_normal(2, i, Ha * Ta * Dh).reshape(1, Ha, Ta, Dh)
+                     for i in range(4))
+    pos = np.arange(Ta, dtype=np.int64).reshape(1, Ta)
+    keep = np.ones((1, Ta, Ta), np.uint8)
+    inv = np.array([np.float32(1.0 / 10000.0 ** (2 * i / Dh)) for i in range(Dh // 2)],
+                   np.float32)
+    rshape = (1, Ha, Ta, Dh)
+    qr, kr, o = (np.empty(rshape, np.float32) for _ in range(3))
+    dq, dk, dv, dqr, dkr = (np.empty(rshape, np.float32) for _ in range(5))
+    ashape = (1, Ha, Ha, Ta, Ta, Dh)
+    calls = [
+        k1.KernelCall("kernel.rope", "rope.forward", rshape, [q, pos, inv], [qr]),
+        k1.KernelCall("kernel.rope", "rope.forward", rshape, [kk, pos, inv], [kr]),
+        k1.KernelCall("kernel.causal-attention", "causal-attention.forward", ashape,
+                      [qr, kr, vv, pos, pos, keep], [o]),
+        k1.KernelCall("kernel.causal-attention", "causal-attention.backward", ashape,
+                      [qr, kr, vv, pos, pos, keep, go], [dq, dk, dv]),
+        k1.KernelCall("kernel.rope", "rope.backward", rshape, [dq, pos, inv], [dqr]),
+        k1.KernelCall("kernel.rope", "rope.backward", rshape, [dk, pos, inv], [dkr]),
+    ]
+    timed("attention", lambda: [a2.invoke_call(C.pointer(c.call)) for c in calls])
+    att_per_token = secs["attention"] * (T / Ta) ** 2 * (H / Ha) / T
+    # L2: cross-entropy forward + backward through invoke_call
+    l2 = k1.provider(ref, "et_l2_indexed_cross_entropy_provider_v1")
+    lg = orc.fill_normal(3, 2, S * V).reshape(1, S, V)
+    tg = orc.fill_tokens(3, 3, S, V).reshape(1, S)
+    up = np.full((1, S), 1.0 / (GLOBAL_BATCH * T), np.float32)
+    loss, grad = np.empty((1, S), np.float32), np.empty((1, S, V), np.float32)
+    ce_calls = [k1.KernelCall("kernel.indexed-cross-entropy", "indexed-cross-entropy.forward",
+                              (1, S, V), [lg, tg], [loss]),
+                k1.KernelCall("kernel.indexed-cross-entropy", "indexed-cross-entropy.backward",
+                              (1, S, V), [lg, tg, up], [grad])]
+    timed("cross_entropy", lambda: [l2.invoke_call(C.pointer(c.call)) for c in ce_calls])
+    # O2 through its API (one optimizer per process: the harness keeps it)
+    n_o2 = 1 << 20
+    if not _REF_O2_READY:
+        init = orc.fill_normal(4, 1, n_o2).view(np.uint32)
+        bits = [orc.bits(v) for v in (1e-3, 0.9, 0.999, 1e-8, 0.01)]
+        if ref.ref_o2_create(p(init), sz(n_o2), *[C.c_uint32(b) for b in bits]) != 0:
+            raise SystemExit("the reference's O2 optimizer could not be built")
+        _REF_O2_READY = True
+    grad_bits = orc.fill_normal(4, 2, n_o2, 0.0, 1e-3).view(np.uint32)
+    rc = timed("adamw", lambda: (ref.ref_o2_accumulate(p(grad_bits), C.c_uint32(0x3f800000)),
+                                 ref.ref_o2_step(), ref.ref_o2_zero_grad()))
+    if any(rc):
+        raise SystemExit(f"the reference's O2 step failed: {rc}")
+    n_params = L * (4 * d * d + 2 * d * F) + V * d
+    tokens = GLOBAL_BATCH * T
+    per_token = ((secs["qkv"] + secs["out"] + secs["up"] + secs["down"]
+                  + 2 * secs["layer_norm"] + secs["gelu"]) * L
+                 + secs["head"] + secs["layer_norm"] + secs["cross_entropy"]
+                 + secs["embedding"]) / S + att_per_token * L \
+        + secs["adamw"] * n_params / n_o2 / tokens
+    step_s = per_token * tokens
+    return {"value": round(1.0 / per_token, 4), "unit": UNIT, "cores": 1, "kind": "reference",
+            "extrapolated": True, "step_s": round(step_s, 1),
+            "per_op_sample_s": {k: round(v, 4) for k, v in secs.items()},
+            "sample": (f"the reference's own C code on one core: N2 linears, LayerNorm, GELU and "
+                       f"embedding on {S} tokens (tied head on {Sh}), A2 rope + attention "
+                       f"forward/backward via invoke_call at 1 sequence x {Ha} heads x T={Ta}, "
+                       f"L2 cross-entropy via invoke_call on {S} rows, O2 accumulate + step + "
+                       f"zero_grad on 2^20 parameters; scaled to the {WORKLOAD} step by its "
+                       f"operation counts (attention by (T/{Ta})^2)")}
 
 
 def run_reference(args) -> None:
@@ -455,9 +594,9 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     t0 = time.perf_counter()
-    samples = []
-    for _ in range(max(1, args.steps)):
-        samples.append(cpu_baseline(kind="reference", budget_s=args.cpu_budget))
+    for _ in range(args.warmup if args.warmup < 2 else 1):
+        reference_step_sample()
+    samples = [reference_step_sample() for _ in range(max(1, args.steps))]
     value = statistics.median(s["value"] for s in samples)
     base = samples[0]
     ms_per_step = GLOBAL_BATCH * SHAPE["seq_len"] / value * 1e3
@@ -467,9 +606,11 @@ def run_reference(args) -> None:
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded)",
         "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH,
-                   "seq_len": SHAPE["seq_len"], "parallelism": "host CPU"},
+                   "seq_len": SHAPE["seq_len"], "parallelism": "host CPU, 1 core (serial C)"},
+        "extrapolated": True,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": base["cores"],
-                         "kind": base["kind"], "sample": base["sample"]},
+                         "kind": base["kind"], "sample": base["sample"], "extrapolated": True},
+        "per_op_sample_s": base["per_op_sample_s"],
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": round(time.perf_counter() - t0, 1)}), flush=True)
 

@@ -150,6 +150,11 @@ struct TcArgs {
   // [s * kb_per_split, min(nkb, (s + 1) * kb_per_split)), s = u / tiles, and
   // writes its raw sum to partial + s * M * N (row stride N)
   int splits, kb_per_split;
+  // K blocks per accumulation chunk (>= kb_per_split: one chunk); the
+  // epilogue warps add the chunks of a tile in f32 in chunk_ws (per CTA 8
+  // warps x 32 lanes x BN / 2 floats)
+  int chunk_kb;
+  float* chunk_ws;
   float* partial;
   // fused epilogue (pair kernel): mode, auxiliary input, extra outputs, and
   // the per-(tile, warp) column partials of the GELU_BWD mode
@@ -623,6 +628,108 @@ struct Tc2Layout {
 // cache (ncu: "no_instruction" stalls).  VAR fixes the GELU modes' options
 // at compile time for the same reason: bit 0 gelu_slope_c, bit 1 a binary16
 // operand-pair output; kVarRuntime reads both from the arguments.
+// The K chunks of one tile, for one epilogue warp of the pair kernel (its
+// 32 TMEM lanes, BN / 2 columns from taddr0).  Each chunk's accumulator
+// buffer is added into an f32 running sum and handed back to the MMA warp;
+// the last chunk's buffer receives the total, and `acc` / `phase` are left on
+// it for the epilogue.  The running sum lives in this warp's 16 KB of the
+// global chunk scratch `run`, lane-major (column group q of lane l at
+// run[(q * 32 + l) * 4]) so that each warp access is 512 contiguous bytes:
+// the first chunk is stored, the middle ones are added with fire-and-forget
+// reductions (red.add: round to nearest, applied in this thread's program
+// order, since every element has one owner), and the last chunk reads the
+// sum back once.  Returns false when a bounded wait gave up.
+__device__ __forceinline__ void red_add4(float4* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ float4 ld_relaxed4(const float4* p) {
+  float4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+template <int BN>
+__device__ __forceinline__ bool sum_k_chunks(uint32_t taddr0, int nchunks, uint32_t tfull0,
+                                             uint32_t tempty_leader, int& acc,
+                                             uint32_t& acc_phase, int* error, float* run) {
+  static_assert(BN % 64 == 0, "pairs of 16-column groups");
+  const int lane = threadIdx.x & 31;
+  float4* r4 = reinterpret_cast<float4*>(run) + lane;
+  for (int ch = 0; ch < nchunks; ch++) {
+    const bool last = ch == nchunks - 1;
+    // the last chunk: the running sums of the first two 16-column groups
+    // load while its MMAs finish; later ones are issued one pair ahead
+    float4 pa[4], pb[4];
+    if (last) {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        pa[q] = ld_relaxed4(r4 + q * 32);
+        pb[q] = ld_relaxed4(r4 + (4 + q) * 32);
+      }
+    }
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(tfull0 + 8 * acc, acc_phase, error) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) return false;
+    __syncwarp();
+    tc_fence_after();
+    const uint32_t taddr = taddr0 + (uint32_t)(acc * BN);
+#pragma unroll 1
+    for (int g = 0; g < BN / 32; g += 2) {
+      float va[16], vb[16];
+      tmem_ld16(taddr + 16u * g, va);
+      tmem_ld16(taddr + 16u * (g + 1), vb);
+      if (last) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          va[4 * q] = pa[q].x + va[4 * q];
+          va[4 * q + 1] = pa[q].y + va[4 * q + 1];
+          va[4 * q + 2] = pa[q].z + va[4 * q + 2];
+          va[4 * q + 3] = pa[q].w + va[4 * q + 3];
+          vb[4 * q] = pb[q].x + vb[4 * q];
+          vb[4 * q + 1] = pb[q].y + vb[4 * q + 1];
+          vb[4 * q + 2] = pb[q].z + vb[4 * q + 2];
+          vb[4 * q + 3] = pb[q].w + vb[4 * q + 3];
+        }
+        if (g + 2 < BN / 32) {
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            pa[q] = ld_relaxed4(r4 + (4 * (g + 2) + q) * 32);
+            pb[q] = ld_relaxed4(r4 + (4 * (g + 3) + q) * 32);
+          }
+        }
+        tmem_st16(taddr + 16u * g, va);
+        tmem_st16(taddr + 16u * (g + 1), vb);
+      } else if (ch == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          r4[(4 * g + q) * 32] = make_float4(va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
+          r4[(4 * (g + 1) + q) * 32] =
+              make_float4(vb[4 * q], vb[4 * q + 1], vb[4 * q + 2], vb[4 * q + 3]);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          red_add4(r4 + (4 * g + q) * 32, va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
+          red_add4(r4 + (4 * (g + 1) + q) * 32, vb[4 * q], vb[4 * q + 1], vb[4 * q + 2],
+                   vb[4 * q + 3]);
+        }
+      }
+    }
+    if (last) break;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(tempty_leader + 8 * acc);
+    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+  }
+  tmem_wait_st();
+  return true;
+}
+
 constexpr int kVarRuntime = 4;
 template <int BN, int STAGES, int EPI, int VAR>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
@@ -737,48 +844,54 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       bool ok = true;
       for (int unit = cluster; ok && unit < units; unit += nclusters) {
         const int split = unit / tiles;
-        if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, args.error)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         const int kb_begin = split * args.kb_per_split;
         const int kb_end = min(nkb, kb_begin + args.kb_per_split);
-        for (int kb = kb_begin; kb < kb_end; kb++) {
-          if (!mbar_wait(full0 + 8 * stage, phase, args.error)) { ok = false; break; }
+        // one accumulator buffer per K chunk (the epilogue warps add the
+        // chunks in f32 registers: the tensor-pipe accumulation truncates, so
+        // its error grows with the K it sums)
+        for (int c0 = kb_begin; ok && c0 < kb_end; c0 += args.chunk_kb) {
+          const int c1 = min(kb_end, c0 + args.chunk_kb);
+          if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1u, args.error)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
-          const uint32_t sb = sa + L::A_BYTES;
-          const uint32_t lo = L::A_BYTES + L::B_BYTES;
-          if (f16) {
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+          for (int kb = c0; kb < c1; kb++) {
+            if (!mbar_wait(full0 + 8 * stage, phase, args.error)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+            const uint32_t sb = sa + L::A_BYTES;
+            const uint32_t lo = L::A_BYTES + L::B_BYTES;
+            if (f16) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {  // 16 k per instruction
-              const uint64_t a = tile_desc_f16(sa, args.a_mn, j);
-              const uint64_t b = tile_desc_f16(sb, args.b_mn, j);
-              const uint64_t alo = tile_desc_f16(sa + lo, args.a_mn, j);
-              const uint64_t blo = tile_desc_f16(sb + lo, args.b_mn, j);
-              umma_f16_pair(d_tmem, a, b, idesc, (kb > kb_begin || j > 0) ? 1u : 0u);
-              umma_f16_pair(d_tmem, a, blo, idesc, 1u);
-              umma_f16_pair(d_tmem, alo, b, idesc, 1u);
-            }
-          } else {
+              for (int j = 0; j < 4; j++) {  // 16 k per instruction
+                const uint64_t a = tile_desc_f16(sa, args.a_mn, j);
+                const uint64_t b = tile_desc_f16(sb, args.b_mn, j);
+                const uint64_t alo = tile_desc_f16(sa + lo, args.a_mn, j);
+                const uint64_t blo = tile_desc_f16(sb + lo, args.b_mn, j);
+                umma_f16_pair(d_tmem, a, b, idesc, (kb > c0 || j > 0) ? 1u : 0u);
+                umma_f16_pair(d_tmem, a, blo, idesc, 1u);
+                umma_f16_pair(d_tmem, alo, b, idesc, 1u);
+              }
+            } else {
 #pragma unroll
-            for (int j = 0; j < BK / 8; j++) {  // 8 k per instruction
-              const uint64_t a = tile_desc<BK>(sa, args.a_mn, j);
-              const uint64_t b = tile_desc<BK>(sb, args.b_mn, j);
-              const uint64_t alo = tile_desc<BK>(sa + lo, args.a_mn, j);
-              const uint64_t blo = tile_desc<BK>(sb + lo, args.b_mn, j);
-              umma_tf32_pair(d_tmem, a, b, idesc, (kb > kb_begin || j > 0) ? 1u : 0u);
-              umma_tf32_pair(d_tmem, a, blo, idesc, 1u);
-              umma_tf32_pair(d_tmem, alo, b, idesc, 1u);
+              for (int j = 0; j < BK / 8; j++) {  // 8 k per instruction
+                const uint64_t a = tile_desc<BK>(sa, args.a_mn, j);
+                const uint64_t b = tile_desc<BK>(sb, args.b_mn, j);
+                const uint64_t alo = tile_desc<BK>(sa + lo, args.a_mn, j);
+                const uint64_t blo = tile_desc<BK>(sb + lo, args.b_mn, j);
+                umma_tf32_pair(d_tmem, a, b, idesc, (kb > c0 || j > 0) ? 1u : 0u);
+                umma_tf32_pair(d_tmem, a, blo, idesc, 1u);
+                umma_tf32_pair(d_tmem, alo, b, idesc, 1u);
+              }
             }
+            umma_commit_pair(empty0 + 8 * stage);
+            umma_commit_pair(map_to_rank(empty0 + 8 * stage, peer));
+            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
           }
-          umma_commit_pair(empty0 + 8 * stage);
-          umma_commit_pair(map_to_rank(empty0 + 8 * stage, peer));
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          if (!ok) break;
+          umma_commit_pair(tfull0 + 8 * acc);
+          umma_commit_pair(map_to_rank(tfull0 + 8 * acc, peer));
+          if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
-        if (!ok) break;
-        umma_commit_pair(tfull0 + 8 * acc);
-        umma_commit_pair(map_to_rank(tfull0 + 8 * acc, peer));
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
       failed = !ok;
     }
@@ -803,9 +916,30 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
     for (int unit = cluster; unit < units; unit += nclusters) {
       const int tile = unit % tiles, split = unit / tiles;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(tfull0 + 8 * acc, acc_phase, args.error) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) { failed = true; break; }
+      {
+        // K chunks (the plain / residual instance; the host gives the fused
+        // modes, whose K is d_model, one chunk): every chunk but the last is
+        // added into the f32 running sum in chunk order and its buffer handed
+        // back to the MMA warp; the last chunk's buffer receives the total,
+        // which the epilogue below then reads as a single accumulator.
+        const int kb_begin = split * args.kb_per_split;
+        const int nchunks =
+            EPI != GEMM_EPI_PLAIN ? 1
+            : (min(nkb, kb_begin + args.kb_per_split) - kb_begin + args.chunk_kb - 1) /
+                  args.chunk_kb;
+        if (nchunks > 1) {
+          ok = sum_k_chunks<BN>(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)col_begin,
+                                nchunks, tfull0, tempty_leader, acc, acc_phase, args.error,
+                                args.chunk_ws + ((int64_t)blockIdx.x * 8 + (warp - 2)) *
+                                                    (32 * (BN / 2)));
+          if (!ok) { failed = true; break; }
+        }
+        if (nchunks <= 1) {
+          if (lane == 0) ok = mbar_wait(tfull0 + 8 * acc, acc_phase, args.error) ? 1 : 0;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) { failed = true; break; }
+        }
+      }
       __syncwarp();
       tc_fence_after();
       int tm, tn;
@@ -1206,6 +1340,13 @@ void gemm_f16_refused(const GemmArgs& g, const char* why) {
   cudaMemcpy(device_error_word(), &one, sizeof(int), cudaMemcpyHostToDevice);
 }
 
+// K blocks summed per tensor-pipe accumulator by the pair kernel before the
+// chunk is added into its f32 running sum: 1,024 k of binary16 pairs or 512 k
+// of TF32 pairs, the same MMA time per chunk (about 24k cycles), long enough
+// to hide the epilogue's read-modify-write of the running sum.
+constexpr int kChunkKbF16 = 16;
+constexpr int kChunkKbTf32 = 16;
+
 // C = (accumulate ? C : 0) + bias + sum over s of partial[s] (s ascending).
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
                                      float* __restrict__ C, int64_t ldc,
@@ -1273,6 +1414,7 @@ void launch_tc(const GemmArgs& g, cudaStream_t stream) {
   const int nkb = (g.K + BK - 1) / BK;
   a.splits = 1;
   a.kb_per_split = nkb;
+  a.chunk_kb = nkb;  // (the single-CTA kernel accumulates each split in one buffer)
   a.partial = nullptr;
   const int s = choose_splits(tiles, nkb, sm_count());
   if (s > 1 && g.workspace != nullptr &&
@@ -1306,6 +1448,7 @@ void gemm_simt(const GemmArgs& g, cudaStream_t stream) {
 }
 
 size_t gemm_splitk_floats(int M, int N) { return (size_t)16 * (size_t)M * (size_t)N; }
+size_t gemm_chunk_ws_floats() { return (size_t)sm_count() * 8 * 32 * 128; }
 
 size_t gemm_epilogue_ws_floats(int M, int N) {
   const size_t pair_parts = (size_t)((M + 2 * TC_BM - 1) / (2 * TC_BM)) * 8 * (size_t)N;
@@ -1409,8 +1552,20 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
     a.splits = (nkb + a.kb_per_split - 1) / a.kb_per_split;
     a.partial = g.workspace;
   }
+  // The tensor pipe's f32 accumulation truncates, so its error grows with
+  // the K summed into one accumulator (measured against f64 at K = 65,536:
+  // about 5e-4 relative, against 7e-7 for an FFMA GEMM).  The kernel
+  // therefore accumulates one chunk of K blocks at a time and adds the chunks
+  // in f32 (round to nearest) through the caller's chunk scratch.
   const int units = tiles * a.splits;
   const int grid = 2 * (units < pairs ? units : pairs);
+  a.chunk_kb = a.kb_per_split;
+  a.chunk_ws = nullptr;
+  if ((a.epilogue == GEMM_EPI_PLAIN || a.epilogue == GEMM_EPI_RESIDUAL) && g.chunk_ws != nullptr &&
+      g.chunk_ws_floats >= (size_t)grid * 8 * 32 * (BN / 2)) {
+    a.chunk_kb = g.f16 ? kChunkKbF16 : kChunkKbTf32;
+    a.chunk_ws = g.chunk_ws;
+  }
   // GELU options as a compile-time variant: (slope, binary16 out) of the
   // split-f16 models' steps (1, 1) / (1, 0) and of the others (0, 0)
   const int gvar = (a.gelu_slope_c ? 1 : 0) | (a.out_sc.f16 ? 2 : 0);

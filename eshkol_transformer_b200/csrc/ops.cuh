@@ -158,8 +158,8 @@ void scale_from_amax(unsigned* amax, int* exp, int count, int target, int reset,
 // xlo| goes to amax when it is not null.
 void split_f16(const float* x, const float* xlo, size_t count, uint16_t* hi, uint16_t* lo,
                const int* exp, unsigned* amax, cudaStream_t stream);
-// flag[0] = 1.0 when some slot's amax 2^exp is not below 65504 (a binary16
-// overflow) or NaN, else 0.0; then clears amax[reset_slot] (if >= 0).
+// flag[0] += 1.0 when some slot's amax 2^exp is not below 65504 (a binary16
+// overflow) or NaN; then clears amax[reset_slot] (if >= 0).
 void operand_range_check(unsigned* amax, const int* exp, int count, int reset_slot, float* flag,
                          cudaStream_t stream);
 // status flags: sets *flag = 1 if any of count values is nonfinite.
@@ -288,6 +288,8 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
                            AttnOut dk, AttnOut dv, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMM
+// Floats of GemmArgs::chunk_ws for any GEMM on the current device.
+size_t gemm_chunk_ws_floats();
 // C[m, n] = sum_k A(m, k) B(n, k) (+ bias[n]) (+ C when accumulate).
 // A(m,k) = a_kmajor ? A[m*lda + k] : A[k*lda + m]
 // B(n,k) = b_kmajor ? B[n*ldb + k] : B[k*ldb + n]
@@ -312,6 +314,12 @@ struct GemmArgs {
   // [M, N] sums here, then reduced in a fixed order (gemm_splitk_floats).
   float* workspace;
   size_t workspace_floats;
+  // optional scratch of gemm_chunk_ws_floats() floats: the f32-grade pair
+  // GEMM then sums K in chunks (the tensor pipe's accumulation truncates, so
+  // one accumulator over a long K drifts) and adds them in f32 here.  Calls
+  // that may run at the same time need separate scratch.
+  float* chunk_ws;
+  size_t chunk_ws_floats;
   // Epilogue applied to y = sum_k A B (all outputs share ldc; `accumulate`
   // applies to GEMM_EPI_PLAIN only):
   //   PLAIN     C = y (+ bias) (+ C)

@@ -551,7 +551,7 @@ __global__ void operand_range_kernel(unsigned* amax, const int* exp, int count, 
   }
   bad = __syncthreads_or(bad);
   if (threadIdx.x == 0) {
-    flag[0] = bad ? 1.0f : 0.0f;
+    if (bad) flag[0] += 1.0f;  // (the flag may already hold other step-void marks)
     if (reset_slot >= 0) amax[reset_slot] = 0u;
   }
 }

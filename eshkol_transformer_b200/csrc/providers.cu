@@ -741,6 +741,8 @@ void run_n2(Call& cl, const NPlan& pl, bool scratch, std::vector<void*>& outs) {
       g.lda = d[2]; g.a_kmajor = true;
       g.ldb = d[2]; g.b_kmajor = true;
       g.C = (float*)outs[0]; g.ldc = d[3]; g.bias = b; g.accumulate = false;
+      g.chunk_ws_floats = gemm_chunk_ws_floats();
+      g.chunk_ws = (float*)P.alloc(g.chunk_ws_floats * 4);
       gemm(g, linear_precision(f16), s);
       break;
     }
@@ -756,6 +758,8 @@ void run_n2(Call& cl, const NPlan& pl, bool scratch, std::vector<void*>& outs) {
       g.lda = d[3]; g.a_kmajor = true;
       g.ldb = d[2]; g.b_kmajor = false;
       g.C = (float*)outs[0]; g.ldc = d[2];
+      g.chunk_ws_floats = gemm_chunk_ws_floats();
+      g.chunk_ws = (float*)P.alloc(g.chunk_ws_floats * 4);
       gemm(g, linear_precision(f16), s);
       GemmArgs w2{};
       w2.M = (int)d[3]; w2.N = (int)d[2]; w2.K = (int)rows;
@@ -763,6 +767,8 @@ void run_n2(Call& cl, const NPlan& pl, bool scratch, std::vector<void*>& outs) {
       w2.lda = d[3]; w2.a_kmajor = false;
       w2.ldb = d[2]; w2.b_kmajor = false;
       w2.C = (float*)outs[1]; w2.ldc = d[2];
+      w2.chunk_ws = g.chunk_ws;  // (same stream, after the dX GEMM)
+      w2.chunk_ws_floats = g.chunk_ws_floats;
       gemm(w2, linear_precision(f16), s);
       if (pl.kind == OP_LIN_B) {
         float* ws = (float*)P.alloc(colsum_workspace_floats(rows, d[3]) * 4);

@@ -118,6 +118,8 @@ struct et_b200_lm {
   float *dx = nullptr, *dxhi = nullptr, *dxlo = nullptr, *dtmp = nullptr, *dqkv = nullptr,
         *dqkvlo = nullptr, *du = nullptr, *dulo = nullptr, *delta = nullptr;
   float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *epi_ws = nullptr;
+  float* chunk_ws = nullptr;  // the f32-grade GEMMs' K-chunk running sums
+  size_t chunk_ws_floats = 0;
   // per-128-row-tile column sums of dqkv from the attention backward (bqkv gradient)
   float* qkv_colpart = nullptr;
   int64_t qkv_colrows = 0;
@@ -298,6 +300,7 @@ void linear_forward(et_b200_lm* lm, const float* x, const float* xlo, int64_t ro
   g.C = y; g.ldc = dout; g.bias = bias; g.accumulate = false;
   g.epilogue = epilogue; g.aux = aux; g.out2 = out2; g.out3 = out3; g.qkv = qkv;
   g.skip_c = skip_c;
+  g.chunk_ws = lm->chunk_ws; g.chunk_ws_floats = lm->chunk_ws_floats;
   set16(lm, g, sa, lm->slot_w());
   if (epilogue == GEMM_EPI_GELU_FWD && sout >= 0) g.out_sc = osc(lm, sout);
   // split-f16 models keep GELU'(u) (not u) for the backward's epilogue
@@ -330,6 +333,7 @@ void linear_backward_dx(et_b200_lm* lm, const float* dy, const float* dylo, int6
     g.dprep = dprep;
     g.skip_c = skip_c;
   }
+  g.chunk_ws = lm->chunk_ws; g.chunk_ws_floats = lm->chunk_ws_floats;
   set16(lm, g, sa, lm->slot_w());
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->gprec, lm->stream);
@@ -344,6 +348,7 @@ void linear_backward_dw(et_b200_lm* lm, const float* dy, const float* dylo, cons
   g.B = x; g.B_lo = xlo; g.ldb = din; g.b_kmajor = false;
   g.C = dw; g.ldc = din; g.bias = nullptr; g.accumulate = false;
   g.workspace = lm->splitk_ws; g.workspace_floats = lm->splitk_floats;
+  g.chunk_ws = lm->chunk_ws; g.chunk_ws_floats = lm->chunk_ws_floats;
   set16(lm, g, sa, sb);
   Mark mk(lm, P_GEMM, 2.0 * rows * din * dout, 0);
   gemm(g, lm->gprec, lm->stream);
@@ -933,6 +938,8 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   // split-K partials for the weight-gradient GEMMs of the layers (K = rows)
   lm->splitk_floats = gemm_splitk_floats((int)std::max<int64_t>(3 * d, F), (int)std::max<int64_t>(d, F));
   lm->splitk_ws = dalloc<float>(lm, lm->splitk_floats, &err);
+  lm->chunk_ws_floats = gemm_chunk_ws_floats();
+  lm->chunk_ws = dalloc<float>(lm, lm->chunk_ws_floats, &err);
   {
     AttnParams shape{};
     shape.B = (int)lm->B; shape.Hq = (int)lm->H; shape.Hkv = (int)lm->H;

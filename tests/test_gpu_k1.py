@@ -204,6 +204,74 @@ def test_linear_split_f16_scaled_operands(lib, cuda, sx, sw, sg):
     assert_close_norm(dw, dw_r, tol, "dw")
 
 
+# Long contractions against float64 (torch on the GPU): the tensor pipe's
+# accumulation truncates, so the f32-grade GEMMs sum K in chunks and add the
+# chunks in f32; their error then stays flat in K.  LONG_K_TOL: max |err| <=
+# tol * max |f64| for sign-mixed operands, and the same bound for all-positive
+# operands, where truncation errors cannot cancel.
+LONG_K_TOL = {etb.PRECISION_TF32X3: 1e-5, etb.PRECISION_F16X3: 1.5e-5}
+
+
+@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F16X3])
+@pytest.mark.parametrize("K", [4096, 65536])
+@pytest.mark.parametrize("positive", [False, True])
+def test_linear_long_k_vs_float64(lib, cuda, precision, K, positive):
+    M, N = 256, 512
+    g = torch.Generator(device="cuda").manual_seed(K + positive)
+    x = torch.randn(1, M, K, device="cuda", generator=g)
+    w = torch.randn(N, K, device="cuda", generator=g)
+    if positive:
+        x, w = x.abs(), w.abs()
+    y = torch.full((1, M, N), float("nan"), device="cuda")
+    lib.et_b200_k1_precision_v1(precision)
+    try:
+        call = k1.KernelCall("kernel.matmul", "linear.forward-no-bias", (1, M, K, N), [x, w], [y],
+                             device="cuda")
+        rc, err = k1.dispatch(provider_for(lib, "kernel.matmul"), call)
+        torch.cuda.synchronize()
+    finally:
+        lib.et_b200_k1_precision_v1(etb.PRECISION_TF32X3)
+    assert rc == 0, str(err)
+    ref = x[0].double() @ w.double().T
+    rel = ((y[0].double() - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= LONG_K_TOL[precision], rel
+
+
+@pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F16X3])
+def test_linear_dx_rows_spanning_2e20(lib, cuda, precision):
+    """dY rows scaled from 1 down to 2^-20 inside one tensor: dX row by row
+    against float64, besides the normwise bar.  3xTF32 pairs carry f32's
+    exponent range, so every row keeps the relative bound.  Split-f16 scales
+    each tensor by one power of two, so an element far below the tensor's max
+    keeps an absolute representation error of at most 2^-35 max|dY| (half the
+    binary16 subnormal spacing at that scale); the per-row bound adds what that
+    error contributes to a dX element: 2^-35 max|dY| ||W[:, i]||_1."""
+    n, t, din, dout = 1, 256, 512, 1024
+    x = orc.fill_normal(9, 1, n * t * din).reshape(n, t, din)
+    w = orc.fill_normal(9, 2, dout * din, 0, 0.05).reshape(dout, din)
+    dy = orc.fill_normal(9, 4, n * t * dout).reshape(n, t, dout)
+    row_scale = np.float32(2.0) ** -np.linspace(0, 20, t).astype(np.float32)
+    dy = (dy * row_scale[None, :, None]).astype(np.float32)
+    lib.et_b200_k1_precision_v1(precision)
+    try:
+        dx, _, _ = run_call(lib, "kernel.matmul", "linear.backward", (n, t, din, dout), [x, w, dy],
+                            [(n, t, din), (dout, din), (dout,)], "cuda")
+    finally:
+        lib.et_b200_k1_precision_v1(etb.PRECISION_TF32X3)
+    ref = dy[0].astype(np.float64) @ w.astype(np.float64)
+    err = np.abs(dx[0].astype(np.float64) - ref)
+    assert err.max() <= 1e-5 * np.abs(ref).max(), err.max() / np.abs(ref).max()
+    floor = 0.0
+    if precision == etb.PRECISION_F16X3:
+        floor = 2.0 ** -35 * np.abs(dy).max() * np.abs(w.astype(np.float64)).sum(axis=0)
+    rowmax = np.abs(ref).max(axis=1, keepdims=True)
+    assert np.all(err <= 1e-5 * rowmax + floor), \
+        float(((err - floor) / rowmax).max())
+    per_row = (err / rowmax).max(axis=1)
+    print(f"precision {precision}: normwise {err.max() / np.abs(ref).max():.2e}, worst row "
+          f"{per_row.max():.2e} (row of max 2^-20: {per_row[-1]:.2e})")
+
+
 def test_n3k_linear_no_bias(lib, cuda):
     x = orc.fill_normal(6, 1, 4 * 32 * 64).reshape(4, 32, 64)
     w = orc.fill_normal(6, 2, 48 * 64, 0, 0.1).reshape(48, 64)
