@@ -615,6 +615,137 @@ def run_reference(args) -> None:
         "wall_s": round(time.perf_counter() - t0, 1)}), flush=True)
 
 
+# ----------------------------------------------------------------- attention sweep
+
+SWEEP = dict(batch=4, heads=16, head_dims=(64, 128), seq_lens=(512, 1024, 2048, 4096, 8192, 16384))
+
+
+def attention_sweep(args) -> None:
+    """Causal attention with RoPE, forward and backward, over the sweep's
+    shapes (batch 4, 16 heads, head_dim 64 / 128, T = 512 ... 16384, seeded
+    N(0, 1) Q/K/V/dO) through et_b200_attention_*_v1; one JSON line per
+    shape.  Algorithmic FLOP: forward 2 B H T^2 Dh (the causal half of two
+    GEMMs), backward 4 B H T^2 Dh (four); bytes: each tensor read or written
+    once (forward Q, K, V, O; backward Q, K, V, O, dO, dQ, dK, dV).  The
+    reference's A2 provider (oracle/_ref, one core, invoke_call only) is
+    timed at T <= 2048 on one sequence and two heads and scaled by B H / 2;
+    beyond 2048 its time is extrapolated by (T / 2048)^2 and marked."""
+    import torch
+
+    import eshkol_transformer_b200 as etb
+
+    torch.cuda.set_device(0)
+    peaks = measured_peaks()
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    ref_cache = {}
+    for Dh in SWEEP["head_dims"]:
+        for T in SWEEP["seq_lens"]:
+            B, H = SWEEP["batch"], SWEEP["heads"]
+            g = torch.Generator(device="cuda").manual_seed(T * 1000 + Dh)
+            q, k, v, do = (torch.randn(B, H, T, Dh, device="cuda", generator=g)
+                           for _ in range(4))
+            pos = torch.arange(T, dtype=torch.int64, device="cuda").repeat(B, 1).contiguous()
+            c, s_ = etb.rope_tables(T, Dh)
+            cos, sin = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+            att = etb.Attention(B, H, H, T, T, Dh, pos, pos, None, cos, sin)
+            o = torch.empty_like(q)
+            m = torch.empty(B, H, T, device="cuda")
+            l = torch.empty(B, H, T, device="cuda")
+            dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+            iters = max(2, min(20, int(2e12 / (4.0 * B * H * T * T * Dh))))
+            for _ in range(2):
+                att.forward(q, k, v, o, m, l)
+                att.backward(q, k, v, o, do, m, l, dq, dk, dv)
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            with ClockSampler(0) as clocks:
+                ev[0].record()
+                for _ in range(iters):
+                    att.forward(q, k, v, o, m, l)
+                ev[1].record()
+                for _ in range(iters):
+                    att.backward(q, k, v, o, do, m, l, dq, dk, dv)
+                ev[2].record()
+                torch.cuda.synchronize()
+            fwd_ms = ev[0].elapsed_time(ev[1]) / iters
+            bwd_ms = ev[1].elapsed_time(ev[2]) / iters
+            f_flop = 2.0 * B * H * T * T * Dh
+            b_flop = 4.0 * B * H * T * T * Dh
+            t_bytes = 4.0 * B * H * T * Dh
+            line = {
+                "metric": "attn fwd/bwd % roofline", "workload": "causal attention + RoPE",
+                "batch": B, "heads": H, "seq_len": T, "head_dim": Dh, "dtype": "f32 (3xTF32)",
+                "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
+                "fwd_tflops": round(f_flop / fwd_ms / 1e9, 2),
+                "bwd_tflops": round(b_flop / bwd_ms / 1e9, 2),
+                "fwd_frac_of_measured_bf16": round(f_flop / fwd_ms / 1e9 / bf16, 4),
+                "bwd_frac_of_measured_bf16": round(b_flop / bwd_ms / 1e9 / bf16, 4),
+                "fwd_frac_of_tf32_rate": round(2 * f_flop / fwd_ms / 1e9 / bf16, 4),
+                "bwd_frac_of_tf32_rate": round(2 * b_flop / bwd_ms / 1e9 / bf16, 4),
+                "fwd_gbs": round(4 * t_bytes / fwd_ms / 1e6, 1),
+                "bwd_gbs": round(8 * t_bytes / bwd_ms / 1e6, 1),
+                "hbm_frac_bwd": round(8 * t_bytes / bwd_ms / 1e6 / hbm, 4),
+                "iters": iters, "clocks": clocks.summary(),
+                "tensor_core_backward": Dh in (32, 64),
+            }
+            if not args.no_cpu_baseline:
+                line["reference_cpu"] = reference_attention_seconds(B, H, T, Dh, ref_cache)
+            print(json.dumps(line), flush=True)
+            del q, k, v, do, o, dq, dk, dv, att
+            torch.cuda.empty_cache()
+
+
+def reference_attention_seconds(B, H, T, Dh, cache) -> dict:
+    """The reference's A2 provider (invoke_call; rope fwd on Q, K, attention
+    forward and backward, rope bwd on dQ, dK) on one core for one sequence
+    and two heads at min(T, 2048), scaled by B H / 2 and, above 2048, by
+    (T / 2048)^2 (marked extrapolated)."""
+    import ctypes as C
+
+    from eshkol_transformer_b200 import k1
+    from oracle import oracle as orc
+
+    ref = orc.ref()
+    if ref is None:
+        return {"unavailable": "oracle/_ref/libref.so is not built"}
+    Ta = min(T, 2048)
+    if (Ta, Dh) not in cache:
+        a2 = k1.provider(ref, "et_a2_kernel_provider_v1")
+        Ha = 2
+        q, kk, vv, go = (orc.fill_normal(6, i, Ha * Ta * Dh).reshape(1, Ha, Ta, Dh)
+                         for i in range(4))
+        pos = np.arange(Ta, dtype=np.int64).reshape(1, Ta)
+        keep = np.ones((1, Ta, Ta), np.uint8)
+        inv = np.array([np.float32(1.0 / 10000.0 ** (2 * i / Dh)) for i in range(Dh // 2)],
+                       np.float32)
+        rs = (1, Ha, Ta, Dh)
+        qr, kr, o, dq, dk, dv, dqr, dkr = (np.empty(rs, np.float32) for _ in range(8))
+        asz = (1, Ha, Ha, Ta, Ta, Dh)
+        fwd = [k1.KernelCall("kernel.rope", "rope.forward", rs, [q, pos, inv], [qr]),
+               k1.KernelCall("kernel.rope", "rope.forward", rs, [kk, pos, inv], [kr]),
+               k1.KernelCall("kernel.causal-attention", "causal-attention.forward", asz,
+                             [qr, kr, vv, pos, pos, keep], [o])]
+        bwd = [k1.KernelCall("kernel.causal-attention", "causal-attention.backward", asz,
+                             [qr, kr, vv, pos, pos, keep, go], [dq, dk, dv]),
+               k1.KernelCall("kernel.rope", "rope.backward", rs, [dq, pos, inv], [dqr]),
+               k1.KernelCall("kernel.rope", "rope.backward", rs, [dk, pos, inv], [dkr])]
+        t0 = time.perf_counter()
+        for c in fwd:
+            a2.invoke_call(C.pointer(c.call))
+        t1 = time.perf_counter()
+        for c in bwd:
+            a2.invoke_call(C.pointer(c.call))
+        t2 = time.perf_counter()
+        cache[(Ta, Dh)] = (t1 - t0, t2 - t1, Ha)
+    f, b, Ha = cache[(Ta, Dh)]
+    scale = B * H / Ha * (T / Ta) ** 2
+    return {"fwd_s": round(f * scale, 3), "bwd_s": round(b * scale, 3), "cores": 1,
+            "sample": f"1 sequence x {Ha} heads at T={Ta}, scaled by B*H/{Ha}"
+                      + (f" and (T/{Ta})^2" if T > Ta else ""),
+            "extrapolated": T > Ta}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -631,7 +762,13 @@ def main() -> None:
     ap.add_argument("--profile-case", action="store_true",
                     help="small case of the same kernels for ncu captures (2 layers, global "
                          "batch 4 = 4096 tokens; a few GB on the device); not a bench value")
+    ap.add_argument("--attention-sweep", action="store_true",
+                    help="causal attention + RoPE fwd/bwd over B4 H16 Dh{64,128} T 512..16384 "
+                         "(one JSON line per shape); not the default bench line")
     args = ap.parse_args()
+    if args.attention_sweep:
+        attention_sweep(args)
+        return
     if args.profile_case:
         global GLOBAL_BATCH, WORKLOAD
         SHAPE["layers"] = 2

@@ -77,6 +77,13 @@ def load() -> C.CDLL:
         "et_b200_lm_f16_redone_steps_v1": (C.c_int32, [C.c_void_p]),
         "et_b200_lm_update_counts_v1": (C.c_int32, [C.c_void_p, C.POINTER(C.c_uint64),
                                                     C.POINTER(C.c_uint64), E]),
+        "et_b200_attention_workspace_bytes_v1": (C.c_size_t, [C.c_void_p]),
+        "et_b200_rope_tables_v1": (None, [C.c_int64, C.c_int64, C.c_double, C.c_void_p,
+                                          C.c_void_p]),
+        "et_b200_attention_forward_v1": (C.c_int32, [C.c_void_p] + [C.c_void_p] * 6 +
+                                         [C.c_void_p, C.c_size_t, C.c_void_p, E]),
+        "et_b200_attention_backward_v1": (C.c_int32, [C.c_void_p] + [C.c_void_p] * 10 +
+                                          [C.c_void_p, C.c_size_t, C.c_int32, C.c_void_p, E]),
         "et_b200_o2_optimizer_create_v1": (C.c_int32, [C.c_size_t, C.c_void_p, C.c_uint32,
                                                        C.c_uint32, C.c_uint32, C.c_uint64,
                                                        C.c_uint64, C.c_uint32,
@@ -250,6 +257,63 @@ class LanguageModel:
         self.lib.et_b200_lm_profile_read_v1(self.handle, out, n)
         return {name: {"launches": out[4 * i], "ms": out[4 * i + 1], "flop": out[4 * i + 2],
                        "bytes": out[4 * i + 3]} for i, name in enumerate(self.PROFILE_CLASSES)}
+
+
+class AttentionShape(C.Structure):
+    """et_b200_attention_v1"""
+    _fields_ = [("struct_size", C.c_size_t), ("batch", C.c_int64), ("q_heads", C.c_int64),
+                ("kv_heads", C.c_int64), ("q_len", C.c_int64), ("k_len", C.c_int64),
+                ("head_dim", C.c_int64), ("q_positions", C.c_void_p),
+                ("k_positions", C.c_void_p), ("keep", C.c_void_p), ("rope_cos", C.c_void_p),
+                ("rope_sin", C.c_void_p), ("rope_batched", C.c_int32), ("reserved", C.c_int32)]
+
+
+def rope_tables(length: int, head_dim: int, base: float = 10000.0):
+    """Host RoPE tables [length, head_dim / 2] (cos, sin) built as the reference does."""
+    cos = np.empty((length, head_dim // 2), np.float32)
+    sin = np.empty_like(cos)
+    load().et_b200_rope_tables_v1(length, head_dim, base, cos.ctypes.data, sin.ctypes.data)
+    return cos, sin
+
+
+class Attention:
+    """et_b200_attention_forward_v1 / _backward_v1 over torch CUDA tensors
+    [batch, heads, len, head_dim] (f32), positions [batch, len] (i64) and
+    optional RoPE tables; enqueued on `stream` (a cudaStream_t address, 0 =
+    the legacy default stream)."""
+
+    def __init__(self, batch, q_heads, kv_heads, q_len, k_len, head_dim, q_positions,
+                 k_positions, keep=None, rope_cos=None, rope_sin=None, stream: int = 0):
+        import torch
+        self.lib = load()
+        self.keepalive = [q_positions, k_positions, keep, rope_cos, rope_sin]
+        ptr = lambda t: t.data_ptr() if t is not None else None
+        self.shape = AttentionShape(C.sizeof(AttentionShape), batch, q_heads, kv_heads, q_len,
+                                    k_len, head_dim, ptr(q_positions), ptr(k_positions),
+                                    ptr(keep), ptr(rope_cos), ptr(rope_sin), 0, 0)
+        self.ws_bytes = self.lib.et_b200_attention_workspace_bytes_v1(C.byref(self.shape))
+        if self.ws_bytes == 0:
+            raise ValueError("attention shape rejected")
+        self.ws = torch.empty(self.ws_bytes // 4 + 64, dtype=torch.float32, device="cuda")
+        base = self.ws.data_ptr()
+        self.ws_ptr = (base + 255) & ~255
+        self.stream = stream
+
+    def forward(self, q, k, v, o, row_max, row_sum) -> None:
+        err = k1.KernelError()
+        _check(self.lib.et_b200_attention_forward_v1(
+            C.byref(self.shape), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+            row_max.data_ptr(), row_sum.data_ptr(), self.ws_ptr, self.ws_bytes, self.stream,
+            C.byref(err)), err)
+
+    def backward(self, q, k, v, o, dout, row_max, row_sum, dq, dk, dv,
+                 workspace_from_forward: bool = True) -> None:
+        err = k1.KernelError()
+        _check(self.lib.et_b200_attention_backward_v1(
+            C.byref(self.shape), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+            dout.data_ptr(), row_max.data_ptr(), row_sum.data_ptr(), dq.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), self.ws_ptr, self.ws_bytes,
+            1 if workspace_from_forward else 0, self.stream, C.byref(err)), err)
 
 
 def nccl_unique_id() -> bytes:

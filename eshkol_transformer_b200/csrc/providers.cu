@@ -176,6 +176,14 @@ int32_t check_tables(const et_kernel_call_v1* c, const char* op, size_t nin, siz
         return fail(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_ALIASING_OUTPUT, op,
                     "output storage aliases another output");
   }
+  // "cuda" views are borrowed like host memory: the call reads them once
+  // every kernel and copy already enqueued on the device, on any stream, has
+  // finished (the caller may have produced them on its own stream just
+  // before the call; the provider's stream is not ordered after it).
+  if (!out->host) {
+    const cudaError_t st = cudaDeviceSynchronize();
+    if (st != cudaSuccess) return cuda_error(e, st, op);
+  }
   return 0;
 }
 

@@ -35,8 +35,10 @@ int32_t et_b200_device_check_v1(et_kernel_error *error);
  *
  * Drop-in replacements for the reference's carrier-neutral providers.  They
  * accept dense zero-offset views on device "cuda" (device pointers, results
- * complete when invoke returns) and on device "cpu" (host pointers, staged
- * through the GPU).  Capabilities are verified for every shape the kernels
+ * complete when invoke returns; the call first waits for all work already
+ * enqueued on the device, so inputs produced on any stream are complete) and
+ * on device "cpu" (host pointers, staged through the GPU).  Capabilities are
+ * verified for every shape the kernels
  * support rather than the reference's exact tiny rows.  validate_call keeps
  * the reference's checks (finite inputs, canonical positions and masks, ids
  * in range) and its error categories; invoke_call never fails.
@@ -59,6 +61,54 @@ const et_kernel_provider_v1 *et_l2_indexed_cross_entropy_provider_v1(void);
  * providers use; process-wide, default ET_B200_PRECISION_TF32X3.  No
  * reference counterpart: the reference's only mode is serial FP32. */
 int32_t et_b200_k1_precision_v1(uint32_t precision);
+
+/* ------------------------------------------------------------ attention on device
+ * Causal attention with RoPE on device tensors, for callers that run many
+ * steps without a K1 round trip per call (the A2 provider's arithmetic,
+ * native/a2_attention_provider.c:669-790, with rope.forward on Q and K and
+ * rope.backward on dQ and dK, :792-935).  No reference counterpart for the
+ * split of the statistics: the forward returns per query row the maximum of
+ * the scaled scores and the sum of their exponentials, which the backward
+ * takes instead of recomputing the forward as a K1 backward call does.
+ * Tensors are dense row-major f32 [batch, heads, len, head_dim] on the
+ * current device; the calls enqueue on `stream` (a cudaStream_t, NULL = the
+ * legacy default stream) and return without synchronising.  Inputs are not
+ * validated on the device (finite values, canonical positions): the caller
+ * supplies what the A2 provider's validate_call would accept. */
+typedef struct et_b200_attention_v1 {
+  size_t struct_size;
+  int64_t batch, q_heads, kv_heads, q_len, k_len, head_dim;
+  const int64_t *q_positions; /* device [batch, q_len], strictly increasing */
+  const int64_t *k_positions; /* device [batch, k_len], strictly increasing */
+  const uint8_t *keep;        /* device [batch, q_len, k_len] or NULL (all) */
+  const float *rope_cos;      /* device [len, head_dim/2] (or [batch*len, ..]
+                                 with rope_batched) for Q and K; NULL = no RoPE */
+  const float *rope_sin;
+  int32_t rope_batched;
+  int32_t reserved;
+} et_b200_attention_v1;
+/* Bytes of the workspace both calls take (256-byte aligned). */
+size_t et_b200_attention_workspace_bytes_v1(const et_b200_attention_v1 *shape);
+/* Host-side RoPE tables [len, head_dim/2] the way the reference builds its
+ * rotation: inv_freq = (float)(1 / base^(2i/head_dim)), angle = (float)t *
+ * inv_freq, cosf / sinf (a2_attention_provider.c:792-935 with the base-10000
+ * frequencies the callers pass). */
+void et_b200_rope_tables_v1(int64_t len, int64_t head_dim, double base,
+                            float *cos_out, float *sin_out);
+int32_t et_b200_attention_forward_v1(const et_b200_attention_v1 *shape,
+                                     const float *q, const float *k,
+                                     const float *v, float *o, float *row_max,
+                                     float *row_sum, void *workspace,
+                                     size_t workspace_bytes, void *stream,
+                                     et_kernel_error *error);
+/* workspace_from_forward: the workspace still holds what the forward of the
+ * same Q/K/V wrote into it (the prepared operands are then reused). */
+int32_t et_b200_attention_backward_v1(
+    const et_b200_attention_v1 *shape, const float *q, const float *k,
+    const float *v, const float *o, const float *dout, const float *row_max,
+    const float *row_sum, float *dq, float *dk, float *dv, void *workspace,
+    size_t workspace_bytes, int32_t workspace_from_forward, void *stream,
+    et_kernel_error *error);
 
 /* ------------------------------------------------------------ synthetic data
  * Seeded inputs shared with the tests: value i of (seed, stream) is a pure

@@ -1,0 +1,99 @@
+"""Causal attention with RoPE on device tensors (et_b200_attention_*_v1)
+against the oracle.
+
+The oracle composes the reference's own order: rope.forward on Q and K,
+causal-attention forward and backward (native/a2_attention_provider.c:669-790),
+rope.backward on dQ and dK (:792-935).  Bars: the A2 fixture tolerances,
+2e-5 (output) and 5e-5 (gradients) absolute plus relative.  Shapes cover the
+tensor-core forward and backward (head_dim 32 / 64), head_dim 128 (tensor-core
+forward), grouped query heads, and -- for the attention sweep's shape, batch 4,
+16 heads, T = 2,048, head_dim 64 and 128 -- sampled (sequence, head) slices
+checked against the oracle run on that slice alone.
+"""
+import numpy as np
+import pytest
+import torch
+
+import eshkol_transformer_b200 as etb
+from helpers import assert_close
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _inv_freq(dh: int) -> np.ndarray:
+    return np.array([np.float32(1.0 / 10000.0 ** (2 * i / dh)) for i in range(dh // 2)],
+                    np.float32)
+
+
+def _run(B, Hq, Hkv, T, Dh, seed, rope=True):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(B, Hq, T, Dh, device="cuda", generator=g)
+    k = torch.randn(B, Hkv, T, Dh, device="cuda", generator=g)
+    v = torch.randn(B, Hkv, T, Dh, device="cuda", generator=g)
+    do = torch.randn(B, Hq, T, Dh, device="cuda", generator=g)
+    pos = torch.arange(T, dtype=torch.int64, device="cuda").repeat(B, 1).contiguous()
+    cos = sin = None
+    if rope:
+        c, s = etb.rope_tables(T, Dh)
+        cos, sin = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
+    att = etb.Attention(B, Hq, Hkv, T, T, Dh, pos, pos, None, cos, sin)
+    o = torch.empty_like(q)
+    m = torch.empty(B, Hq, T, device="cuda")
+    l = torch.empty(B, Hq, T, device="cuda")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    att.forward(q, k, v, o, m, l)
+    att.backward(q, k, v, o, do, m, l, dq, dk, dv)
+    torch.cuda.synchronize()
+    host = lambda t: t.cpu().numpy()
+    return [host(t) for t in (q, k, v, do, o, dq, dk, dv)]
+
+
+def _oracle(q, k, v, do, rope=True):
+    B, Hq, T, Dh = q.shape
+    Hkv = k.shape[1]
+    pos = np.tile(np.arange(T, dtype=np.int64), (B, 1))
+    mask = np.ones((B, T, T), np.uint8)
+    inv = _inv_freq(Dh)
+    qr = orc.rope((B, Hq, T, Dh), q, pos, inv) if rope else q
+    kr = orc.rope((B, Hkv, T, Dh), k, pos, inv) if rope else k
+    shape = (B, Hq, Hkv, T, T, Dh)
+    o = orc.attention_forward(shape, qr, kr, v, pos, pos, mask)
+    dqr, dkr, dv = orc.attention_backward(shape, qr, kr, v, pos, pos, mask, do)
+    dq = orc.rope((B, Hq, T, Dh), dqr, pos, inv, backward=True) if rope else dqr
+    dk = orc.rope((B, Hkv, T, Dh), dkr, pos, inv, backward=True) if rope else dkr
+    return o, dq, dk, dv
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,Dh,rope", [(2, 4, 4, 256, 64, True),
+                                                (2, 4, 2, 200, 32, True),
+                                                (1, 2, 2, 384, 128, True),
+                                                (2, 2, 2, 96, 64, False)])
+def test_device_attention_vs_oracle(lib, cuda, B, Hq, Hkv, T, Dh, rope):
+    q, k, v, do, o, dq, dk, dv = _run(B, Hq, Hkv, T, Dh, 7 + T, rope)
+    ro, rdq, rdk, rdv = _oracle(q, k, v, do, rope)
+    assert_close(o, ro, 2e-5, 2e-5, "o")
+    for name, got, want in (("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        assert_close(got, want, 5e-5, 5e-5, name)
+
+
+@pytest.mark.parametrize("Dh", [64, 128])
+def test_sweep_shape_sampled_heads_vs_oracle(lib, cuda, Dh):
+    """B4 H16 T2048: two sampled (sequence, head) slices of the full device
+    computation against the oracle on the slice alone."""
+    B, H, T = 4, 16, 2048
+    q, k, v, do, o, dq, dk, dv = _run(B, H, H, T, Dh, 2048 + Dh)
+    for b, h in ((0, 3), (3, 14)):
+        sl = lambda a: np.ascontiguousarray(a[b:b + 1, h:h + 1])
+        ro, rdq, rdk, rdv = _oracle(sl(q), sl(k), sl(v), sl(do))
+        assert_close(sl(o), ro, 2e-5, 2e-5, f"o[{b},{h}]")
+        for name, got, want in (("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+            assert_close(sl(got), want, 5e-5, 5e-5, f"{name}[{b},{h}]")
+
+
+def test_device_attention_rejects_bad_shapes(lib, cuda):
+    pos = torch.arange(8, dtype=torch.int64, device="cuda").repeat(1, 1)
+    with pytest.raises(ValueError):
+        etb.Attention(1, 3, 2, 8, 8, 64, pos, pos)  # q heads not a multiple of kv heads
+    with pytest.raises(ValueError):
+        etb.Attention(1, 2, 2, 8, 8, 63, pos, pos)  # odd head_dim
