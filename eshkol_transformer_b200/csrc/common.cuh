@@ -88,17 +88,19 @@ __device__ __forceinline__ void f16_split(float xs, uint16_t& hi, uint16_t& lo) 
   lo = __half_as_ushort(__float2half_rn(xs - __half2float(h)));
 }
 // Four consecutive values: x 2^e as binary16 hi / lo quads (8-byte stores).
+// (packed conversions, two values per instruction; each value rounded exactly
+// as f16_split rounds it)
 __device__ __forceinline__ void f16_store4(uint16_t* hi, uint16_t* lo, int64_t off, float4 x,
                                            float s) {
-  uint16_t h[4], l[4];
-  f16_split(x.x * s, h[0], l[0]);
-  f16_split(x.y * s, h[1], l[1]);
-  f16_split(x.z * s, h[2], l[2]);
-  f16_split(x.w * s, h[3], l[3]);
+  const float a = x.x * s, b = x.y * s, c = x.z * s, d = x.w * s;
+  const __half2 h01 = __floats2half2_rn(a, b), h23 = __floats2half2_rn(c, d);
+  const float2 b01 = __half22float2(h01), b23 = __half22float2(h23);
+  const __half2 l01 = __floats2half2_rn(a - b01.x, b - b01.y);
+  const __half2 l23 = __floats2half2_rn(c - b23.x, d - b23.y);
   *reinterpret_cast<uint2*>(hi + off) =
-      make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+      make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
   *reinterpret_cast<uint2*>(lo + off) =
-      make_uint2((uint32_t)l[0] | ((uint32_t)l[1] << 16), (uint32_t)l[2] | ((uint32_t)l[3] << 16));
+      make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
 }
 // binary16 values in the low / high half of a 32-bit word
 __device__ __forceinline__ float half_lo(uint32_t w) {

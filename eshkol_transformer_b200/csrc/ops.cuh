@@ -39,7 +39,14 @@ struct AdamwTensor {
   float* value_hi;
   float* value_lo;
   OperandScale value_sc;
+  // 1 when this tensor's scalars admit adamw_check's finiteness envelope
+  // (adamw_envelope_ok); 0 computes every element's update in the check
+  int envelope;
 };
+// The scalars of T (lr, epsilon, decay, with bias corrections >= 2^-24 as
+// every 1 - beta^t of a beta < 1 is) admit the envelope under which an
+// element's update is finite without computing it.
+bool adamw_envelope_ok(const AdamwTensor& T);
 // An AdamW update is all or nothing, as the reference's staged commit is
 // (o2_optimizer.c:1813-1926): adamw_check computes every element's update
 // without writing and sets status bits; adamw_apply then writes the table

@@ -262,6 +262,7 @@ int32_t et_b200_o2_optimizer_step_v1(et_b200_o2_optimizer* o, uint32_t weight_bi
     t.lr = lr;
     t.decay = one - lrwd;
     t.epsilon = f_of(p.epsilon_bits);
+    t.envelope = adamw_envelope_ok(t) ? 1 : 0;
     if (!(t.bias1 > 0.0f) || !(t.bias2 > 0.0f) || !isfinite((float)lr))
       return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
                        "bias correction or effective learning rate is invalid");

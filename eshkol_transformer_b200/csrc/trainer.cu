@@ -686,6 +686,7 @@ void optimizer_step(et_b200_lm* lm) {
   h.lr = lr;
   h.decay = one - lrwd;
   h.epsilon = fbits(c.epsilon_bits);
+  h.envelope = adamw_envelope_ok(h) ? 1 : 0;
   // with 3xTF32 the same pass refreshes the weights' (hi, lo) operand pair;
   // split-f16 models always write the binary16 pair (the next step's format)
   h.value_hi = lm->three ? lm->whi : nullptr;

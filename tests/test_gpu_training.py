@@ -396,3 +396,30 @@ def test_long_sequence_lm_gradients_vs_oracle(lib, cuda):
         err = np.abs(g.astype(np.float64) - r).max() / max(np.abs(r).max(), 1e-30)
         assert err <= GRAD_TOL[etb.PRECISION_TF32X3], (t, err)
     model.close()
+
+
+def test_o2_device_adamw_outside_check_envelope(lib, cuda):
+    """Finite values outside the check pass's envelope (a gradient of 2^40, a
+    moment of 2^35, a parameter of 2^110) take its exact computation; the
+    update is finite, so it applies, bit-identical to the reference's
+    arithmetic."""
+    n = 4096
+    p = orc.fill_normal(8, 1, n)
+    g = orc.fill_normal(8, 2, n)
+    g[5] = np.float32(2.0 ** 40)
+    p[9] = np.float32(2.0 ** 110)
+    p_dev, g_dev = torch.from_numpy(p.copy()).cuda(), torch.from_numpy(g).cuda()
+    opt = etb.Optimizer([(p_dev.data_ptr(), g_dev.data_ptr(), n, 1e-3, 0.9, 0.999, 1e-8, 0.01)])
+    m_ptr, v_ptr = opt.moments(0)
+    m0 = np.zeros(n, np.float32)
+    m0[17] = np.float32(2.0 ** 35)
+    device_view(m_ptr, n).copy_(torch.from_numpy(m0))
+    ref_p, ref_m, ref_v = p.copy(), m0.copy(), np.zeros(n, np.float32)
+    opt.step(1.0)
+    assert orc.adamw_step(ref_p, g, ref_m, ref_v, orc.adamw_options(1e-3, 0.9, 0.999, 1e-8, 0.01),
+                          1) == 0
+    torch.cuda.synchronize()
+    assert bits_equal(p_dev.cpu().numpy(), ref_p)
+    assert bits_equal(device_view(m_ptr, n).cpu().numpy(), ref_m)
+    assert bits_equal(device_view(v_ptr, n).cpu().numpy(), ref_v)
+    opt.close()
