@@ -9,10 +9,14 @@
 // (o2_optimizer.c:1738-1756), so parameters and moments are bit-identical.
 // The global norm is summed in f64 in a fixed order; the reference's scaled
 // running sum differs from it by rounding only.
+#include <fcntl.h>
 #include <math.h>
+#include <unistd.h>
 
+#include <string>
 #include <vector>
 
+#include "eshkol_b200/o2_bridge.h"
 #include "ops.cuh"
 
 using namespace etb;
@@ -330,6 +334,527 @@ int32_t et_b200_o2_optimizer_moments_v1(et_b200_o2_optimizer* o, size_t index, f
 uint32_t et_b200_o2_schedule_factor_v1(uint32_t kind, uint64_t warmup, uint64_t total,
                                        uint32_t minimum_ratio_bits, uint64_t update) {
   return schedule_factor(kind, warmup, total, minimum_ratio_bits, update);
+}
+
+}  // extern "C"
+
+// ===================================================================== O2 bridge
+//
+// The reference's Eshkol extension binds its optimizer through the
+// et_o2_private_*_v1 externs of native/o2_wave2_extension.esk:4-29
+// (implemented by native/o2_wave2_package_bridge.c:72-200 over the CPU O2
+// optimizer and I2 parameters).  The same names and signatures here drive
+// the device optimizer above, with et_b200_parameter objects (a device value
+// and gradient plus the I2 accumulation metadata, native/f32_parameter_
+// internal.h:55-67) in place of I2 parameters, so the extension binds
+// unchanged.  Return values follow the bridge: O2 status codes
+// (o2_optimizer_internal.h:19-30) for i64 results, NULL for a failed handle,
+// and the last failure's category through et_o2_private_last_error_category_v1.
+
+namespace {
+
+enum : int64_t {
+  kO2Ok = 0, kO2InvalidArgument = 1, kO2ShapeMismatch = 2, kO2InvalidState = 7,
+  kO2Internal = 9
+};
+
+thread_local int64_t g_bridge_category = 0;
+thread_local char g_bridge_message[192] = "";
+
+int64_t bridge_fail(int64_t category, const char* message) {
+  g_bridge_category = category;
+  snprintf(g_bridge_message, sizeof(g_bridge_message), "%s", message);
+  return category;
+}
+int64_t bridge_ok() {
+  g_bridge_category = 0;
+  g_bridge_message[0] = '\0';
+  return kO2Ok;
+}
+// A device optimizer's K1-category failure as the O2 status the reference
+// returns for the same condition.
+int64_t bridge_from(int32_t k1, const et_kernel_error& e) {
+  if (k1 == 0) return bridge_ok();
+  const int64_t cat = k1 == ET_KERNEL_ERROR_INVALID_ARGUMENT ? kO2InvalidState
+                      : k1 == ET_KERNEL_ERROR_SHAPE_MISMATCH ? kO2ShapeMismatch
+                                                             : kO2Internal;
+  return bridge_fail(cat, e.message);
+}
+
+struct BridgeEntry {
+  et_b200_parameter* parameter = nullptr;
+  const void* p1_handle = nullptr;
+  uint32_t lr = 0, beta1 = 0, beta2 = 0, eps = 0, wd = 0;
+  bool set = false;
+};
+
+}  // namespace
+
+struct et_b200_parameter {
+  float* value = nullptr;
+  float* gradient = nullptr;
+  size_t count = 0;
+  bool present = false;       // a gradient has been accumulated
+  uint64_t contributions = 0;
+  uint32_t weight_bits = 0;   // normalisation weight (f32 bits)
+  int device = 0;
+};
+
+struct et_b200_o2_builder {
+  uint32_t clip_kind = 0, clip_bits = 0, schedule_kind = 0, min_ratio_bits = 0;
+  uint64_t warmup = 0, total = 0;
+  std::vector<BridgeEntry> entries;
+};
+
+struct et_b200_o2_bridge {
+  et_b200_o2_optimizer* opt = nullptr;
+  std::vector<BridgeEntry> entries;
+};
+
+struct et_b200_o2_state {
+  uint32_t clip_kind = 0, clip_bits = 0, schedule_kind = 0, min_ratio_bits = 0;
+  uint64_t warmup = 0, total = 0, completed = 0;
+  std::vector<uint64_t> counts;
+  std::vector<uint32_t> options;        // 5 per entry: lr, beta1, beta2, epsilon, weight decay
+  std::vector<std::vector<uint32_t>> m, v;  // moment bits per entry
+};
+
+extern "C" {
+
+int32_t et_b200_parameter_create_v1(float* value, float* gradient, size_t count,
+                                    et_b200_parameter** out, et_kernel_error* e) {
+  const char* op = "parameter-create";
+  if (out == nullptr || value == nullptr || gradient == nullptr)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, op,
+                     "value, gradient and output are required");
+  if (count == 0)
+    return set_error(e, ET_KERNEL_ERROR_SHAPE_MISMATCH, ET_KERNEL_CODE_INVALID_SHAPE, op,
+                     "a parameter needs at least one element");
+  et_b200_parameter* p = new et_b200_parameter();
+  p->value = value;
+  p->gradient = gradient;
+  p->count = count;
+  cudaGetDevice(&p->device);
+  *out = p;
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+int32_t et_b200_parameter_set_gradient_v1(et_b200_parameter* p, uint64_t contributions,
+                                          uint32_t weight_bits, et_kernel_error* e) {
+  const char* op = "parameter-gradient";
+  if (p == nullptr)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, op,
+                     "parameter is null");
+  if (contributions == 0 || contributions > (uint64_t)INT64_MAX || !pos_finite(weight_bits))
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_INVALID_ENUM, op,
+                     "gradient accumulation metadata is inconsistent");
+  p->present = true;
+  p->contributions = contributions;
+  p->weight_bits = weight_bits;
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
+}
+
+int32_t et_b200_parameter_gradient_present_v1(const et_b200_parameter* p) {
+  return p != nullptr && p->present ? 1 : 0;
+}
+
+void et_b200_parameter_destroy_v1(et_b200_parameter** p) {
+  if (p == nullptr || *p == nullptr) return;
+  delete *p;
+  *p = nullptr;
+}
+
+int64_t et_o2_private_last_error_category_v1(void) { return g_bridge_category; }
+
+const char* et_b200_o2_bridge_last_error_message_v1(void) { return g_bridge_message; }
+
+void* et_o2_private_builder_create_v1(int64_t count, int64_t clip_kind, int64_t clip_bits,
+                                      int64_t schedule_kind, int64_t warmup, int64_t total,
+                                      int64_t minimum_ratio_bits) {
+  if (count < 1 || count > 1365 || clip_kind < 0 || clip_bits < 0 || schedule_kind < 0 ||
+      warmup < 0 || total < 0 || minimum_ratio_bits < 0 || clip_kind > UINT32_MAX ||
+      clip_bits > UINT32_MAX || schedule_kind > UINT32_MAX || minimum_ratio_bits > UINT32_MAX) {
+    bridge_fail(kO2InvalidArgument, "optimizer builder arguments are outside their domain");
+    return nullptr;
+  }
+  const uint32_t ck = (uint32_t)clip_kind, cb = (uint32_t)clip_bits,
+                 sk = (uint32_t)schedule_kind, mr = (uint32_t)minimum_ratio_bits;
+  const bool clip_ok = ck == ET_B200_O2_CLIP_NONE ? cb == 0u
+                       : ck == ET_B200_O2_CLIP_GLOBAL_L2 ? pos_finite(cb) : false;
+  bool sched_ok = sk == ET_B200_O2_SCHEDULE_CONSTANT;
+  if (sk == ET_B200_O2_SCHEDULE_LINEAR)
+    sched_ok = total > 0 && warmup < total && nonneg_finite(mr) && f_of(mr) <= 1.0f;
+  if (!clip_ok || !sched_ok) {
+    bridge_fail(kO2InvalidArgument, "clip or schedule configuration is invalid");
+    return nullptr;
+  }
+  et_b200_o2_builder* b = new et_b200_o2_builder();
+  b->clip_kind = ck; b->clip_bits = cb; b->schedule_kind = sk; b->min_ratio_bits = mr;
+  b->warmup = (uint64_t)warmup; b->total = (uint64_t)total;
+  b->entries.resize((size_t)count);
+  bridge_ok();
+  return b;
+}
+
+int64_t et_o2_private_builder_set_v1(void* builder, int64_t index, void* parameter,
+                                     void* p1_handle, int64_t learning_rate_bits,
+                                     int64_t beta1_bits, int64_t beta2_bits,
+                                     int64_t epsilon_bits, int64_t weight_decay_bits) {
+  et_b200_o2_builder* b = static_cast<et_b200_o2_builder*>(builder);
+  if (b == nullptr || parameter == nullptr || p1_handle == nullptr)
+    return bridge_fail(kO2InvalidArgument, "builder, parameter and identity are required");
+  if (index < 0 || (size_t)index >= b->entries.size())
+    return bridge_fail(kO2InvalidArgument, "parameter index is outside the builder");
+  const int64_t bits[5] = {learning_rate_bits, beta1_bits, beta2_bits, epsilon_bits,
+                           weight_decay_bits};
+  for (int64_t x : bits)
+    if (x < 0 || x > UINT32_MAX) return bridge_fail(kO2InvalidArgument, "option bits are invalid");
+  const uint32_t lr = (uint32_t)learning_rate_bits, b1 = (uint32_t)beta1_bits,
+                 b2 = (uint32_t)beta2_bits, eps = (uint32_t)epsilon_bits,
+                 wd = (uint32_t)weight_decay_bits;
+  if (!nonneg_finite(lr) || !nonneg_finite(b1) || f_of(b1) >= 1.0f || !nonneg_finite(b2) ||
+      f_of(b2) >= 1.0f || !pos_finite(eps) || !nonneg_finite(wd))
+    return bridge_fail(kO2InvalidArgument, "AdamW option is outside its domain");
+  for (size_t i = 0; i < b->entries.size(); i++)
+    if (i != (size_t)index && b->entries[i].set && b->entries[i].parameter == parameter)
+      return bridge_fail(kO2InvalidArgument, "parameter is bound twice");
+  BridgeEntry& en = b->entries[(size_t)index];
+  en.parameter = static_cast<et_b200_parameter*>(parameter);
+  en.p1_handle = p1_handle;
+  en.lr = lr; en.beta1 = b1; en.beta2 = b2; en.eps = eps; en.wd = wd;
+  en.set = true;
+  return bridge_ok();
+}
+
+void* et_o2_private_builder_finish_v1(void* builder) {
+  et_b200_o2_builder* b = static_cast<et_b200_o2_builder*>(builder);
+  if (b == nullptr) {
+    bridge_fail(kO2InvalidArgument, "builder is null");
+    return nullptr;
+  }
+  std::vector<et_b200_o2_parameter_v1> ps;
+  for (const BridgeEntry& en : b->entries) {
+    if (!en.set) {
+      bridge_fail(kO2InvalidState, "every parameter slot must be bound before finish");
+      return nullptr;
+    }
+    et_b200_o2_parameter_v1 p{};
+    p.struct_size = sizeof(p);
+    p.value = en.parameter->value;
+    p.gradient = en.parameter->gradient;
+    p.count = en.parameter->count;
+    p.learning_rate_bits = en.lr; p.beta1_bits = en.beta1; p.beta2_bits = en.beta2;
+    p.epsilon_bits = en.eps; p.weight_decay_bits = en.wd;
+    ps.push_back(p);
+  }
+  et_kernel_error e{};
+  et_b200_o2_optimizer* opt = nullptr;
+  const int32_t rc = et_b200_o2_optimizer_create_v1(
+      ps.size(), ps.data(), b->clip_kind, b->clip_bits, b->schedule_kind, b->warmup, b->total,
+      b->min_ratio_bits, &opt, &e);
+  if (rc != 0) {
+    bridge_from(rc, e);
+    return nullptr;
+  }
+  et_b200_o2_bridge* br = new et_b200_o2_bridge();
+  br->opt = opt;
+  br->entries = b->entries;
+  delete b;  // the builder is consumed
+  bridge_ok();
+  return br;
+}
+
+int64_t et_o2_private_builder_abort_v1(void* builder) {
+  if (builder == nullptr) return bridge_fail(kO2InvalidArgument, "builder is null");
+  delete static_cast<et_b200_o2_builder*>(builder);
+  return bridge_ok();
+}
+
+int64_t et_o2_private_optimizer_step_v1(void* optimizer) {
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(optimizer);
+  if (br == nullptr) return bridge_fail(kO2InvalidArgument, "optimizer is null");
+  // o2_optimizer.c:1813-1856: every gradient present, one contribution count
+  // and one normalisation weight across parameters
+  uint64_t count = 0;
+  uint32_t weight = 0;
+  for (size_t i = 0; i < br->entries.size(); i++) {
+    const et_b200_parameter* p = br->entries[i].parameter;
+    if (!p->present)
+      return bridge_fail(kO2InvalidState, "every bound parameter requires a present gradient");
+    if (i > 0 && (p->contributions != count || p->weight_bits != weight))
+      return bridge_fail(kO2InvalidState, "gradient accumulation metadata is inconsistent");
+    count = p->contributions;
+    weight = p->weight_bits;
+  }
+  et_kernel_error e{};
+  return bridge_from(et_b200_o2_optimizer_step_v1(br->opt, weight, nullptr, &e), e);
+}
+
+int64_t et_o2_private_optimizer_zero_grad_v1(void* optimizer) {
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(optimizer);
+  if (br == nullptr) return bridge_fail(kO2InvalidArgument, "optimizer is null");
+  cudaSetDevice(br->opt->device);
+  for (BridgeEntry& en : br->entries) {
+    const cudaError_t st =
+        cudaMemsetAsync(en.parameter->gradient, 0, en.parameter->count * 4, br->opt->stream);
+    if (st != cudaSuccess) return bridge_fail(kO2Internal, cudaGetErrorString(st));
+  }
+  const cudaError_t st = cudaStreamSynchronize(br->opt->stream);
+  if (st != cudaSuccess) return bridge_fail(kO2Internal, cudaGetErrorString(st));
+  for (BridgeEntry& en : br->entries) {
+    en.parameter->present = false;
+    en.parameter->contributions = 0;
+    en.parameter->weight_bits = 0;
+  }
+  return bridge_ok();
+}
+
+int64_t et_o2_private_optimizer_require_absent_gradients_v1(void* optimizer) {
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(optimizer);
+  if (br == nullptr) return bridge_fail(kO2InvalidArgument, "optimizer is null");
+  for (const BridgeEntry& en : br->entries)
+    if (en.parameter->present)
+      return bridge_fail(kO2InvalidState, "optimizer parameters still hold gradients");
+  return bridge_ok();
+}
+
+int64_t et_o2_private_optimizer_completed_updates_v1(void* optimizer) {
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(optimizer);
+  if (br == nullptr) {
+    bridge_fail(kO2InvalidArgument, "optimizer is null");
+    return -1;
+  }
+  bridge_ok();
+  return (int64_t)br->opt->updates;
+}
+
+int64_t et_o2_private_optimizer_schedule_factor_bits_v1(void* optimizer) {
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(optimizer);
+  if (br == nullptr) {
+    bridge_fail(kO2InvalidArgument, "optimizer is null");
+    return -1;
+  }
+  const et_b200_o2_optimizer* o = br->opt;
+  bridge_ok();
+  return (int64_t)schedule_factor(o->schedule_kind, o->warmup, o->total, o->min_ratio_bits,
+                                  o->updates + 1);
+}
+
+// Snapshot: configuration, completed updates, per-parameter options and the
+// moments' bits (copied to host memory).  Like the reference's
+// et_o2_optimizer_state_snapshot_v1 (o2_optimizer.c:2052), it requires every
+// gradient absent.
+void* et_o2_private_optimizer_state_snapshot_v1(void* optimizer) {
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(optimizer);
+  if (br == nullptr) {
+    bridge_fail(kO2InvalidArgument, "optimizer is null");
+    return nullptr;
+  }
+  if (et_o2_private_optimizer_require_absent_gradients_v1(optimizer) != 0) return nullptr;
+  const et_b200_o2_optimizer* o = br->opt;
+  et_b200_o2_state* st = new et_b200_o2_state();
+  st->clip_kind = o->clip_kind; st->clip_bits = o->clip_max_bits;
+  st->schedule_kind = o->schedule_kind; st->min_ratio_bits = o->min_ratio_bits;
+  st->warmup = o->warmup; st->total = o->total; st->completed = o->updates;
+  cudaSetDevice(o->device);
+  for (size_t i = 0; i < o->params.size(); i++) {
+    const et_b200_o2_parameter_v1& p = o->params[i];
+    st->counts.push_back(p.count);
+    for (uint32_t x : {p.learning_rate_bits, p.beta1_bits, p.beta2_bits, p.epsilon_bits,
+                       p.weight_decay_bits})
+      st->options.push_back(x);
+    st->m.emplace_back(p.count);
+    st->v.emplace_back(p.count);
+    cudaError_t err = cudaMemcpy(st->m.back().data(), o->m1[i], p.count * 4, cudaMemcpyDeviceToHost);
+    if (err == cudaSuccess)
+      err = cudaMemcpy(st->v.back().data(), o->m2[i], p.count * 4, cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) {
+      delete st;
+      bridge_fail(kO2Internal, cudaGetErrorString(err));
+      return nullptr;
+    }
+  }
+  bridge_ok();
+  return st;
+}
+
+// Load (o2_optimizer.c:2173): the state must describe this optimizer's
+// configuration and parameters (counts, options); gradients absent.  All or
+// nothing: nothing changes unless every check passes and every copy lands.
+int64_t et_o2_private_optimizer_load_state_v1(void* optimizer, void* state) {
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(optimizer);
+  const et_b200_o2_state* st = static_cast<const et_b200_o2_state*>(state);
+  if (br == nullptr || st == nullptr)
+    return bridge_fail(kO2InvalidArgument, "optimizer and state are required");
+  if (int64_t r = et_o2_private_optimizer_require_absent_gradients_v1(optimizer)) return r;
+  et_b200_o2_optimizer* o = br->opt;
+  if (st->counts.size() != o->params.size())
+    return bridge_fail(kO2ShapeMismatch, "optimizer state parameter count differs");
+  if (st->clip_kind != o->clip_kind || st->clip_bits != o->clip_max_bits ||
+      st->schedule_kind != o->schedule_kind || st->min_ratio_bits != o->min_ratio_bits ||
+      st->warmup != o->warmup || st->total != o->total)
+    return bridge_fail(kO2InvalidState, "optimizer state configuration differs");
+  for (size_t i = 0; i < o->params.size(); i++) {
+    const et_b200_o2_parameter_v1& p = o->params[i];
+    const uint32_t* opt5 = st->options.data() + 5 * i;
+    if (st->counts[i] != p.count)
+      return bridge_fail(kO2ShapeMismatch, "optimizer state parameter shape differs");
+    if (opt5[0] != p.learning_rate_bits || opt5[1] != p.beta1_bits || opt5[2] != p.beta2_bits ||
+        opt5[3] != p.epsilon_bits || opt5[4] != p.weight_decay_bits)
+      return bridge_fail(kO2InvalidState, "optimizer state options differ");
+    for (size_t k = 0; k < p.count; k++)
+      if (!isfinite(f_of(st->m[i][k])) || !nonneg_finite(st->v[i][k]))
+        return bridge_fail(kO2InvalidState, "optimizer state moment is invalid");
+  }
+  cudaSetDevice(o->device);
+  for (size_t i = 0; i < o->params.size(); i++) {
+    cudaError_t err = cudaMemcpy(o->m1[i], st->m[i].data(), st->counts[i] * 4, cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+      err = cudaMemcpy(o->m2[i], st->v[i].data(), st->counts[i] * 4, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) return bridge_fail(kO2Internal, cudaGetErrorString(err));
+  }
+  o->updates = st->completed;
+  return bridge_ok();
+}
+
+int64_t et_o2_private_optimizer_state_release_v1(void* state) {
+  if (state == nullptr) return bridge_fail(kO2InvalidArgument, "state is null");
+  delete static_cast<et_b200_o2_state*>(state);
+  return bridge_ok();
+}
+
+}  // extern "C"
+
+namespace {
+void put_bytes(std::vector<uint8_t>& out, const void* p, size_t n) {
+  const uint8_t* b = static_cast<const uint8_t*>(p);
+  out.insert(out.end(), b, b + n);
+}
+template <typename T> void put(std::vector<uint8_t>& out, T v) { put_bytes(out, &v, sizeof v); }
+uint64_t fnv1a(const uint8_t* p, size_t n) {
+  uint64_t h = 0xcbf29ce484222325ull;
+  for (size_t i = 0; i < n; i++) h = (h ^ p[i]) * 0x100000001b3ull;
+  return h;
+}
+const char kStateMagic[8] = {'E', 'T', 'B', '2', 'O', '2', 'S', 1};
+bool write_all(int fd, const uint8_t* p, size_t n) {
+  while (n > 0) {
+    const ssize_t w = write(fd, p, n);
+    if (w <= 0) return false;
+    p += w;
+    n -= (size_t)w;
+  }
+  return true;
+}
+}  // namespace
+
+extern "C" {
+
+int64_t et_b200_o2_state_write_v1(void* state, const char* path) {
+  const et_b200_o2_state* st = static_cast<const et_b200_o2_state*>(state);
+  if (st == nullptr || path == nullptr || path[0] == '\0')
+    return bridge_fail(kO2InvalidArgument, "state and path are required");
+  std::vector<uint8_t> out;
+  put_bytes(out, kStateMagic, sizeof kStateMagic);
+  put(out, st->clip_kind); put(out, st->clip_bits); put(out, st->schedule_kind);
+  put(out, st->min_ratio_bits); put(out, st->warmup); put(out, st->total);
+  put(out, st->completed); put(out, (uint64_t)st->counts.size());
+  for (size_t i = 0; i < st->counts.size(); i++) {
+    put(out, st->counts[i]);
+    put_bytes(out, st->options.data() + 5 * i, 5 * sizeof(uint32_t));
+    put_bytes(out, st->m[i].data(), st->counts[i] * 4);
+    put_bytes(out, st->v[i].data(), st->counts[i] * 4);
+  }
+  put(out, fnv1a(out.data(), out.size()));
+  // temporary file beside the target, flushed, renamed over it, directory flushed
+  const std::string target(path);
+  const std::string tmp = target + ".tmp." + std::to_string((long)getpid());
+  const int fd = open(tmp.c_str(), O_WRONLY | O_CREAT | O_EXCL | O_CLOEXEC, 0644);
+  if (fd < 0) return bridge_fail(kO2Internal, "cannot create the temporary state file");
+  const bool ok = write_all(fd, out.data(), out.size()) && fsync(fd) == 0;
+  close(fd);
+  if (!ok || rename(tmp.c_str(), target.c_str()) != 0) {
+    unlink(tmp.c_str());
+    return bridge_fail(kO2Internal, "cannot write the state file");
+  }
+  const size_t slash = target.find_last_of('/');
+  const std::string dir = slash == std::string::npos ? "." : (slash == 0 ? "/" : target.substr(0, slash));
+  const int dfd = open(dir.c_str(), O_RDONLY | O_DIRECTORY | O_CLOEXEC);
+  if (dfd >= 0) {
+    fsync(dfd);
+    close(dfd);
+  }
+  return bridge_ok();
+}
+
+void* et_b200_o2_state_read_v1(const char* path) {
+  if (path == nullptr) {
+    bridge_fail(kO2InvalidArgument, "path is required");
+    return nullptr;
+  }
+  const int fd = open(path, O_RDONLY | O_CLOEXEC);
+  if (fd < 0) {
+    bridge_fail(kO2InvalidArgument, "cannot open the state file");
+    return nullptr;
+  }
+  std::vector<uint8_t> in;
+  uint8_t buf[1 << 16];
+  for (;;) {
+    const ssize_t r = read(fd, buf, sizeof buf);
+    if (r < 0) { close(fd); bridge_fail(kO2Internal, "cannot read the state file"); return nullptr; }
+    if (r == 0) break;
+    in.insert(in.end(), buf, buf + r);
+  }
+  close(fd);
+  size_t at = 0;
+  auto take = [&](void* dst, size_t n) {
+    if (in.size() - at < n || at > in.size()) return false;
+    memcpy(dst, in.data() + at, n);
+    at += n;
+    return true;
+  };
+  char magic[8];
+  uint64_t n = 0, hash = 0;
+  et_b200_o2_state* st = new et_b200_o2_state();
+  bool ok = in.size() >= 16 && take(magic, 8) && memcmp(magic, kStateMagic, 8) == 0;
+  if (ok) {
+    memcpy(&hash, in.data() + in.size() - 8, 8);
+    ok = fnv1a(in.data(), in.size() - 8) == hash;
+  }
+  ok = ok && take(&st->clip_kind, 4) && take(&st->clip_bits, 4) && take(&st->schedule_kind, 4) &&
+       take(&st->min_ratio_bits, 4) && take(&st->warmup, 8) && take(&st->total, 8) &&
+       take(&st->completed, 8) && take(&n, 8) && n <= 1365;
+  for (uint64_t i = 0; ok && i < n; i++) {
+    uint64_t c = 0;
+    uint32_t o5[5];
+    ok = take(&c, 8) && take(o5, sizeof o5) && c > 0 && c <= (in.size() - at) / 8;
+    if (!ok) break;
+    st->counts.push_back(c);
+    st->options.insert(st->options.end(), o5, o5 + 5);
+    st->m.emplace_back(c);
+    st->v.emplace_back(c);
+    ok = take(st->m.back().data(), c * 4) && take(st->v.back().data(), c * 4);
+  }
+  ok = ok && at + 8 == in.size();
+  if (!ok) {
+    delete st;
+    bridge_fail(kO2InvalidState, "state file is truncated or corrupted");
+    return nullptr;
+  }
+  bridge_ok();
+  return st;
+}
+
+// Destroys a bridge optimizer (and its device moments); the parameters stay
+// the caller's.  The reference's optimizer has no public destroy.
+void et_b200_o2_bridge_destroy_v1(void** optimizer) {
+  if (optimizer == nullptr || *optimizer == nullptr) return;
+  et_b200_o2_bridge* br = static_cast<et_b200_o2_bridge*>(*optimizer);
+  et_b200_o2_optimizer_destroy_v1(&br->opt);
+  delete br;
+  *optimizer = nullptr;
 }
 
 }  // extern "C"

@@ -1010,7 +1010,53 @@ const et_kernel_provider_v1 n2_provider = PROVIDER(n2_caps, "n2.b200-sm100a", n2
 const et_kernel_provider_v1 n3k_provider =
     PROVIDER(n3k_caps, "n3k.b200-sm100a", n3k_validate, n3k_invoke);
 const et_kernel_provider_v1 l2_provider = PROVIDER(l2_caps, "l2.b200-sm100a", l2_validate, l2_invoke);
+
+// ---- one provider for every capability ---------------------------------------------
+// A K1 runtime takes exactly one provider from its resolver
+// (native/kernel_abi.c:764-840); the composite lists the four providers'
+// capabilities, sorted by name, and hands each call to the provider owning
+// its capability.
+const et_kernel_capability_v1 all_caps[] = {
+    n2_caps[0],   // kernel.activation
+    a2_caps[0],   // kernel.causal-attention
+    n2_caps[1],   // kernel.embedding-backward
+    n2_caps[2],   // kernel.embedding-forward
+    l2_caps[0],   // kernel.indexed-cross-entropy
+    n2_caps[3],   // kernel.matmul
+    n2_caps[4],   // kernel.norm
+    n2_caps[5],   // kernel.residual
+    a2_caps[1],   // kernel.rope
+    n3k_caps[0],  // n3k.linear
+};
+
+const et_kernel_provider_v1* owner_of(const et_kernel_call_v1* c) {
+  if (c == nullptr || c->capability == nullptr) return nullptr;
+  for (const et_kernel_provider_v1* p : {&a2_provider, &n2_provider, &n3k_provider, &l2_provider})
+    for (size_t i = 0; i < p->capability_count; i++)
+      if (strcmp(static_cast<const et_kernel_capability_v1*>(p->capabilities)[i].name,
+                 c->capability) == 0)
+        return p;
+  return nullptr;
+}
+int32_t all_validate(const et_kernel_call_v1* c, et_kernel_error* e) {
+  const et_kernel_provider_v1* p = owner_of(c);
+  if (p == nullptr)
+    return fail(e, ET_KERNEL_ERROR_UNSUPPORTED, ET_KERNEL_CODE_PROVIDER_REJECTED,
+                "b200-dispatch", "capability is not provided");
+  return p->validate_call(c, e);
+}
+void all_invoke(const et_kernel_call_v1* c) {
+  const et_kernel_provider_v1* p = owner_of(c);
+  if (p != nullptr) p->invoke_call(c);
+}
+const et_kernel_provider_v1 all_provider =
+    PROVIDER(all_caps, "b200.sm100a", all_validate, all_invoke);
 #undef PROVIDER
+
+// The fixed resolver's private context (its address is the token).
+const unsigned char k2_resolver_sentinel = 0x62u;
+
+bool same_text(const char* a, const char* b) { return a != nullptr && strcmp(a, b) == 0; }
 
 }  // namespace
 
@@ -1020,6 +1066,45 @@ const et_kernel_provider_v1* et_a2_kernel_provider_v1(void) { return &a2_provide
 const et_kernel_provider_v1* et_n2_kernel_provider_v1(void) { return &n2_provider; }
 const et_kernel_provider_v1* et_n3k_kernel_provider_v1(void) { return &n3k_provider; }
 const et_kernel_provider_v1* et_l2_indexed_cross_entropy_provider_v1(void) { return &l2_provider; }
+const et_kernel_provider_v1* et_b200_kernel_provider_v1(void) { return &all_provider; }
+
+const void* et_b200_k2_resolver_context_v1(void) { return &k2_resolver_sentinel; }
+
+const et_kernel_provider_v1* et_b200_k2_resolver_v1(void* context, const char* symbol) {
+  if (context != &k2_resolver_sentinel || !same_text(symbol, "eshkol_transformer_kernel_provider_v1"))
+    return nullptr;
+  return &all_provider;
+}
+
+int32_t et_b200_k2_audit_provider_v1(const et_kernel_provider_v1* p) {
+  if (p == nullptr) return ET_B200_K2_PROVIDER_ABSENT;
+  if (p->struct_size != sizeof(et_kernel_provider_v1) || p->abi_major != ET_KERNEL_ABI_MAJOR ||
+      p->abi_minor != ET_KERNEL_ABI_MINOR || p->required_features != 0u ||
+      !same_text(p->version, all_provider.version))
+    return ET_B200_K2_PROVIDER_VERSION_MISMATCH;
+  const size_t n = sizeof(all_caps) / sizeof(all_caps[0]);
+  bool exact = same_text(p->name, all_provider.name) &&
+               same_text(p->evidence, all_provider.evidence) && p->capability_count == n &&
+               p->capability_stride == sizeof(et_kernel_capability_v1) &&
+               p->capability_bytes == sizeof(all_caps) && p->capabilities != nullptr &&
+               p->validate_call == all_provider.validate_call &&
+               p->invoke_call == all_provider.invoke_call;
+  for (size_t i = 0; exact && i < n; i++) {
+    const et_kernel_capability_v1& a = static_cast<const et_kernel_capability_v1*>(p->capabilities)[i];
+    const et_kernel_capability_v1& b = all_caps[i];
+    exact = a.struct_size == b.struct_size && same_text(a.name, b.name) && a.status == b.status &&
+            same_text(a.implementation, b.implementation) && same_text(a.version, b.version) &&
+            same_text(a.evidence, b.evidence) && a.deterministic == b.deterministic &&
+            a.operation_count == b.operation_count && a.dtype_count == b.dtype_count &&
+            a.device_count == b.device_count && a.shape_range_count == b.shape_range_count;
+    for (size_t k = 0; exact && k < b.operation_count; k++)
+      exact = same_text(a.operations[k], b.operations[k]);
+    for (size_t k = 0; exact && k < b.device_count; k++)
+      exact = same_text(a.devices[k], b.devices[k]);
+  }
+  return exact ? ET_B200_K2_PROVIDER_EXACT : ET_B200_K2_PROVIDER_METADATA_MISMATCH;
+}
+
 int32_t et_l2_indexed_cross_entropy_abi_major_v1(void) { return 1; }
 int32_t et_l2_indexed_cross_entropy_abi_minor_v1(void) { return 0; }
 

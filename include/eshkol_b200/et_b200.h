@@ -57,6 +57,30 @@ const et_kernel_provider_v1 *et_n3k_kernel_provider_v1(void);
 int32_t et_l2_indexed_cross_entropy_abi_major_v1(void);
 int32_t et_l2_indexed_cross_entropy_abi_minor_v1(void);
 const et_kernel_provider_v1 *et_l2_indexed_cross_entropy_provider_v1(void);
+/* Every capability above in one provider (sorted by name; each call goes to
+ * the provider owning its capability), for K1 runtimes, which take exactly
+ * one provider from their resolver (native/kernel_abi.c:764-840).  No
+ * reference counterpart: the reference composes no providers. */
+const et_kernel_provider_v1 *et_b200_kernel_provider_v1(void);
+/* K2 capability facade support (native/k2_capabilities.c).  K2 discovers
+ * through a fixed private resolver that answers only the K1 provider symbol
+ * with its private context sentinel, and exact-audits the provider it gets,
+ * identity by callback pointers (k2_capabilities.c:493-561).  These are that
+ * resolver and that audit for the B200 provider: a K2 built over libet_b200
+ * calls et_kernel_runtime_discover(et_b200_k2_resolver_v1,
+ * (void *)et_b200_k2_resolver_context_v1(), ...) and admits the provider
+ * when the audit returns ET_B200_K2_PROVIDER_EXACT (the values mirror
+ * enum et_k2_provider_audit, k2_capabilities.c:565-570). */
+enum {
+  ET_B200_K2_PROVIDER_ABSENT = 0,
+  ET_B200_K2_PROVIDER_VERSION_MISMATCH = 1,
+  ET_B200_K2_PROVIDER_METADATA_MISMATCH = 2,
+  ET_B200_K2_PROVIDER_EXACT = 3
+};
+const void *et_b200_k2_resolver_context_v1(void);
+const et_kernel_provider_v1 *et_b200_k2_resolver_v1(void *context,
+                                                    const char *symbol_name);
+int32_t et_b200_k2_audit_provider_v1(const et_kernel_provider_v1 *provider);
 /* Contraction mode (ET_B200_PRECISION_*) the kernel.matmul and n3k.linear
  * providers use; process-wide, default ET_B200_PRECISION_TF32X3.  No
  * reference counterpart: the reference's only mode is serial FP32. */
@@ -407,4 +431,6 @@ int32_t et_a2_kv_cache_read_borrow_end_v1(
 #ifdef __cplusplus
 }
 #endif
+
+#include "eshkol_b200/o2_bridge.h"
 #endif

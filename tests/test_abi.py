@@ -150,3 +150,58 @@ def test_lm_create_validates_contraction_mode_before_the_device(lib, precision, 
 
 def test_f16_redone_steps_of_no_model_is_zero(lib):
     assert lib.et_b200_lm_f16_redone_steps_v1(None) == 0
+
+
+def test_k2_resolver_and_audit_with_reference_runtime(lib):
+    """The fixed resolver and the exact audit K2 needs for the B200 provider
+    (native/k2_capabilities.c:493-561), through the reference's own K1
+    runtime: discovery admits the composite provider and every B200
+    capability is verified; the resolver answers only the K1 symbol with its
+    private context; the audit tells the genuine descriptor from a copy whose
+    callbacks or metadata differ."""
+    ref = orc.ref()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    lib.et_b200_kernel_provider_v1.restype = C.c_void_p
+    lib.et_b200_k2_resolver_context_v1.restype = C.c_void_p
+    lib.et_b200_k2_resolver_v1.restype = C.c_void_p
+    lib.et_b200_k2_resolver_v1.argtypes = [C.c_void_p, C.c_char_p]
+    lib.et_b200_k2_audit_provider_v1.argtypes = [C.c_void_p]
+    genuine = lib.et_b200_kernel_provider_v1()
+    ctx = lib.et_b200_k2_resolver_context_v1()
+    symbol = b"eshkol_transformer_kernel_provider_v1"
+    assert lib.et_b200_k2_resolver_v1(ctx, symbol) == genuine
+    assert lib.et_b200_k2_resolver_v1(None, symbol) is None
+    assert lib.et_b200_k2_resolver_v1(ctx, b"another_symbol") is None
+    # discovery through the reference's K1 runtime with the fixed resolver
+    RESOLVER = C.CFUNCTYPE(C.c_void_p, C.c_void_p, C.c_char_p)
+    resolver = RESOLVER(lambda c, s: lib.et_b200_k2_resolver_v1(c, s))
+    runtime = C.c_void_p()
+    err = k1.KernelError()
+    ref.et_kernel_runtime_discover.argtypes = [RESOLVER, C.c_void_p, C.POINTER(C.c_void_p),
+                                               C.POINTER(k1.KernelError)]
+    assert ref.et_kernel_runtime_discover(resolver, ctx, C.byref(runtime), C.byref(err)) == 0, \
+        str(err)
+    ref.et_kernel_runtime_capability_find.restype = C.POINTER(k1.Capability)
+    ref.et_kernel_runtime_capability_find.argtypes = [C.c_void_p, C.c_char_p]
+    for name in ("kernel.causal-attention", "kernel.matmul", "kernel.indexed-cross-entropy",
+                 "kernel.norm", "kernel.rope", "n3k.linear"):
+        cap = ref.et_kernel_runtime_capability_find(runtime, name.encode())
+        assert cap and cap.contents.status == k1.CAPABILITY_VERIFIED, name
+        assert set(cap.contents.devices[i] for i in range(cap.contents.device_count)) == \
+            {b"cpu", b"cuda"}
+    ref.et_kernel_runtime_destroy.argtypes = [C.c_void_p]
+    ref.et_kernel_runtime_destroy(runtime)
+    # the audit: genuine, absent, a copy with a foreign callback, another version
+    assert lib.et_b200_k2_audit_provider_v1(genuine) == 3
+    assert lib.et_b200_k2_audit_provider_v1(None) == 0
+    copy = k1.Provider.from_buffer_copy(k1.Provider.from_address(genuine))
+    other = k1.provider(lib, "et_a2_kernel_provider_v1")
+    copy.invoke_call = other.invoke_call
+    assert lib.et_b200_k2_audit_provider_v1(C.addressof(copy)) == 2
+    copy = k1.Provider.from_buffer_copy(k1.Provider.from_address(genuine))
+    copy.capability_count = 9
+    assert lib.et_b200_k2_audit_provider_v1(C.addressof(copy)) == 2
+    copy = k1.Provider.from_buffer_copy(k1.Provider.from_address(genuine))
+    copy.abi_minor = 7
+    assert lib.et_b200_k2_audit_provider_v1(C.addressof(copy)) == 1

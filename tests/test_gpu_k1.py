@@ -422,3 +422,47 @@ def test_reference_k1_runtime_dispatches_b200_provider(lib, cuda):
                  5e-5, 5e-5, "o")
     ref.et_kernel_runtime_destroy.argtypes = [C.c_void_p]
     ref.et_kernel_runtime_destroy(runtime)
+
+
+def test_reference_k1_runtime_dispatches_composite_through_k2_resolver(lib, cuda):
+    """The reference's K1 runtime discovering through the fixed K2 resolver
+    (et_b200_k2_resolver_v1 with its private context) gets the composite B200
+    provider and dispatches attention and cross-entropy calls to it."""
+    import ctypes as C
+    ref = orc.ref()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    lib.et_b200_k2_resolver_context_v1.restype = C.c_void_p
+    lib.et_b200_k2_resolver_v1.restype = C.c_void_p
+    lib.et_b200_k2_resolver_v1.argtypes = [C.c_void_p, C.c_char_p]
+    RESOLVER = C.CFUNCTYPE(C.c_void_p, C.c_void_p, C.c_char_p)
+    resolver = RESOLVER(lambda c, s: lib.et_b200_k2_resolver_v1(c, s))
+    runtime = C.c_void_p()
+    err = k1.KernelError()
+    ref.et_kernel_runtime_discover.argtypes = [RESOLVER, C.c_void_p, C.POINTER(C.c_void_p),
+                                               C.POINTER(k1.KernelError)]
+    assert ref.et_kernel_runtime_discover(resolver, lib.et_b200_k2_resolver_context_v1(),
+                                          C.byref(runtime), C.byref(err)) == 0, str(err)
+    ref.et_kernel_runtime_dispatch.argtypes = [C.c_void_p, C.POINTER(k1.Call),
+                                               C.POINTER(k1.KernelError)]
+    shape = (2, 4, 4, 128, 128, 32)
+    q, k, v, qpos, kpos, mask, g = _attention_inputs(shape, 78)
+    out = torch.zeros(q.shape, device="cuda")
+    call = k1.KernelCall("kernel.causal-attention", "causal-attention.forward", shape,
+                         [torch.from_numpy(a).cuda() for a in (q, k, v, qpos, kpos, mask)], [out])
+    assert ref.et_kernel_runtime_dispatch(runtime, C.pointer(call.call), C.byref(err)) == 0
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), orc.attention_forward(shape, q, k, v, qpos, kpos, mask),
+                 5e-5, 5e-5, "o")
+    rows, V = 16, 1024
+    logits = orc.fill_normal(5, 1, rows * V).reshape(1, rows, V)
+    targets = orc.fill_tokens(5, 2, rows, V).reshape(1, rows)
+    loss = torch.zeros(1, rows, device="cuda")
+    call = k1.KernelCall("kernel.indexed-cross-entropy", "indexed-cross-entropy.forward",
+                         (1, rows, V), [torch.from_numpy(logits).cuda(),
+                                        torch.from_numpy(targets).cuda()], [loss])
+    assert ref.et_kernel_runtime_dispatch(runtime, C.pointer(call.call), C.byref(err)) == 0
+    torch.cuda.synchronize()
+    assert_close(loss.cpu().numpy(), orc.ce_forward(logits, targets), 2e-6, 2e-5, "loss")
+    ref.et_kernel_runtime_destroy.argtypes = [C.c_void_p]
+    ref.et_kernel_runtime_destroy(runtime)
