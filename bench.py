@@ -639,8 +639,12 @@ def attention_sweep(args) -> None:
     bf16 = peaks.get("bf16_tflops", 1590.0)
     hbm = peaks.get("hbm_gbs", 6650.0)
     ref_cache = {}
-    for Dh in SWEEP["head_dims"]:
-        for T in SWEEP["seq_lens"]:
+    contraction = {"default": etb.ATTENTION_DEFAULT,
+                   "pairs16": etb.ATTENTION_BWD_PAIRS16}[args.attention_contraction]
+    head_dims = args.sweep_head_dims or SWEEP["head_dims"]
+    seq_lens = args.sweep_seq_lens or SWEEP["seq_lens"]
+    for Dh in head_dims:
+        for T in seq_lens:
             B, H = SWEEP["batch"], SWEEP["heads"]
             g = torch.Generator(device="cuda").manual_seed(T * 1000 + Dh)
             q, k, v, do = (torch.randn(B, H, T, Dh, device="cuda", generator=g)
@@ -648,7 +652,8 @@ def attention_sweep(args) -> None:
             pos = torch.arange(T, dtype=torch.int64, device="cuda").repeat(B, 1).contiguous()
             c, s_ = etb.rope_tables(T, Dh)
             cos, sin = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
-            att = etb.Attention(B, H, H, T, T, Dh, pos, pos, None, cos, sin)
+            att = etb.Attention(B, H, H, T, T, Dh, pos, pos, None, cos, sin,
+                                contraction=contraction)
             o = torch.empty_like(q)
             m = torch.empty(B, H, T, device="cuda")
             l = torch.empty(B, H, T, device="cuda")
@@ -673,9 +678,13 @@ def attention_sweep(args) -> None:
             f_flop = 2.0 * B * H * T * T * Dh
             b_flop = 4.0 * B * H * T * T * Dh
             t_bytes = 4.0 * B * H * T * Dh
+            pairs16 = Dh == 128 or (Dh == 64 and contraction == etb.ATTENTION_BWD_PAIRS16)
             line = {
                 "metric": "attn fwd/bwd % roofline", "workload": "causal attention + RoPE",
-                "batch": B, "heads": H, "seq_len": T, "head_dim": Dh, "dtype": "f32 (3xTF32)",
+                "batch": B, "heads": H, "seq_len": T, "head_dim": Dh, "dtype": "f32",
+                "contractions": {"forward": "3xTF32 pairs (kind::tf32)",
+                                 "backward": "binary16 pairs (kind::f16)" if pairs16
+                                 else "3xTF32 pairs (kind::tf32)"},
                 "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
                 "fwd_tflops": round(f_flop / fwd_ms / 1e9, 2),
                 "bwd_tflops": round(b_flop / bwd_ms / 1e9, 2),
@@ -687,7 +696,7 @@ def attention_sweep(args) -> None:
                 "bwd_gbs": round(8 * t_bytes / bwd_ms / 1e6, 1),
                 "hbm_frac_bwd": round(8 * t_bytes / bwd_ms / 1e6 / hbm, 4),
                 "iters": iters, "clocks": clocks.summary(),
-                "tensor_core_backward": Dh in (32, 64),
+                "tensor_core_backward": Dh in (32, 64, 128),
             }
             if not args.no_cpu_baseline:
                 line["reference_cpu"] = reference_attention_seconds(B, H, T, Dh, ref_cache)
@@ -765,6 +774,14 @@ def main() -> None:
     ap.add_argument("--attention-sweep", action="store_true",
                     help="causal attention + RoPE fwd/bwd over B4 H16 Dh{64,128} T 512..16384 "
                          "(one JSON line per shape); not the default bench line")
+    ap.add_argument("--attention-contraction", choices=("default", "pairs16"), default="default",
+                    help="sweep's contraction mode: default (3xTF32 pairs; binary16 pairs for the "
+                         "head_dim-128 backward) or pairs16 (binary16 pairs in the backward at "
+                         "head_dim 64 too)")
+    ap.add_argument("--sweep-head-dims", type=int, nargs="*", default=None,
+                    help="sweep only these head_dims")
+    ap.add_argument("--sweep-seq-lens", type=int, nargs="*", default=None,
+                    help="sweep only these sequence lengths")
     args = ap.parse_args()
     if args.attention_sweep:
         attention_sweep(args)

@@ -265,7 +265,12 @@ class AttentionShape(C.Structure):
                 ("kv_heads", C.c_int64), ("q_len", C.c_int64), ("k_len", C.c_int64),
                 ("head_dim", C.c_int64), ("q_positions", C.c_void_p),
                 ("k_positions", C.c_void_p), ("keep", C.c_void_p), ("rope_cos", C.c_void_p),
-                ("rope_sin", C.c_void_p), ("rope_batched", C.c_int32), ("reserved", C.c_int32)]
+                ("rope_sin", C.c_void_p), ("rope_batched", C.c_int32),
+                ("contraction", C.c_int32)]
+
+
+ATTENTION_DEFAULT = 0      # 3xTF32 pairs; binary16 pairs for the head_dim-128 backward
+ATTENTION_BWD_PAIRS16 = 1  # binary16 pairs in the backward at head_dim 64 as well
 
 
 def rope_tables(length: int, head_dim: int, base: float = 10000.0):
@@ -283,14 +288,15 @@ class Attention:
     the legacy default stream)."""
 
     def __init__(self, batch, q_heads, kv_heads, q_len, k_len, head_dim, q_positions,
-                 k_positions, keep=None, rope_cos=None, rope_sin=None, stream: int = 0):
+                 k_positions, keep=None, rope_cos=None, rope_sin=None, stream: int = 0,
+                 contraction: int = 0):
         import torch
         self.lib = load()
         self.keepalive = [q_positions, k_positions, keep, rope_cos, rope_sin]
         ptr = lambda t: t.data_ptr() if t is not None else None
         self.shape = AttentionShape(C.sizeof(AttentionShape), batch, q_heads, kv_heads, q_len,
                                     k_len, head_dim, ptr(q_positions), ptr(k_positions),
-                                    ptr(keep), ptr(rope_cos), ptr(rope_sin), 0, 0)
+                                    ptr(keep), ptr(rope_cos), ptr(rope_sin), 0, contraction)
         self.ws_bytes = self.lib.et_b200_attention_workspace_bytes_v1(C.byref(self.shape))
         if self.ws_bytes == 0:
             raise ValueError("attention shape rejected")

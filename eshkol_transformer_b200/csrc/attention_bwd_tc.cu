@@ -964,6 +964,8 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
                            AttnOut dk, AttnOut dv, cudaStream_t stream) {
   if (p.ws == nullptr || encode_fn() == nullptr || p.Tq == 0 || p.Tk == 0) return false;
   if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
+  if ((p.Dh == 128 || (p.Dh == 64 && p.bwd_pairs16)) && !p.grad_ready)
+    return attention_backward_f16(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream);
   switch (p.Dh) {
     case 32:
       return launch_bwd_tc<32>(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream);

@@ -15,12 +15,18 @@ constexpr float kLn2 = 0.6931471805599453f;
 // Head-major [B, H, T, Dh] operand copies in the attention workspace: RoPE'd
 // Q and K and plain V split into TF32 hi and residual lo, dO split the same
 // way (backward), and per-row base-2 log-sum-exp lse2 = (m + ln l) log2(e)
-// (backward; +inf for a row with no admitted key).
+// (backward; +inf for a row with no admitted key).  The binary16-pair
+// backward (attention_bwd_f16.cu) keeps its dO and Q pairs (uint16 hi, lo
+// arrays) where the TF32 dO pair would be, its K and V pairs behind lse2,
+// and the four operand maxima (f32 bits) last.
 struct AttnWs {
   float *qh, *ql, *kh, *kl, *vh, *vl, *doh, *dol, *lse2;
+  uint16_t *g16h, *g16l, *q16h, *q16l, *k16h, *k16l, *v16h, *v16l;
+  unsigned* amax16;
 };
 inline AttnWs attn_ws(const AttnParams& p) {
   const size_t nq = (size_t)p.B * p.Hq * p.Tq * p.Dh, nk = (size_t)p.B * p.Hkv * p.Tk * p.Dh;
+  const size_t rows = (size_t)p.B * p.Hq * p.Tq;
   AttnWs w;
   w.qh = p.ws;
   w.ql = w.qh + nq;
@@ -31,6 +37,15 @@ inline AttnWs attn_ws(const AttnParams& p) {
   w.doh = p.ws_grad != nullptr ? p.ws_grad : w.vl + nk;
   w.dol = w.doh + nq;
   w.lse2 = w.dol + nq;
+  w.g16h = reinterpret_cast<uint16_t*>(w.doh);
+  w.g16l = w.g16h + nq;
+  w.q16h = reinterpret_cast<uint16_t*>(w.dol);
+  w.q16l = w.q16h + nq;
+  w.k16h = reinterpret_cast<uint16_t*>(w.lse2 + ((rows + 63) & ~(size_t)63));
+  w.k16l = w.k16h + nk;
+  w.v16h = w.k16l + nk;
+  w.v16l = w.v16h + nk;
+  w.amax16 = reinterpret_cast<unsigned*>(w.v16l + nk);
   return w;
 }
 

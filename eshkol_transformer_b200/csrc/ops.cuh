@@ -228,6 +228,10 @@ struct AttnParams {
   // grad_ready: the backward's dO hi/lo (workspace) and delta were written by
   // the GEMM that produced dO (AttnGradPrep), so the backward skips its prepass.
   int grad_ready;
+  // bwd_pairs16: the backward carries its operands as binary16 pairs
+  // (attention_bwd_f16.cu) wherever that kernel exists (head_dim 64, 128);
+  // otherwise only head_dim 128 uses it and 32 / 64 take the 3xTF32 kernels.
+  int bwd_pairs16;
 };
 // Where the GEMM producing dO = dY Wo (rows [B*T, H*Dh], token-major) writes
 // the attention backward's inputs: dO split into TF32 hi / lo head-major
@@ -293,6 +297,11 @@ bool attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, At
 bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
                            const float* row_max, const float* row_sum, float* delta, AttnOut dq,
                            AttnOut dk, AttnOut dv, cudaStream_t stream);
+// The binary16-pair tensor-core backward (head_dim 64 and 128, dO from
+// `dout`: not with grad_ready); false when it cannot run this call.
+bool attention_backward_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
+                            const float* row_max, const float* row_sum, float* delta, AttnOut dq,
+                            AttnOut dk, AttnOut dv, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMM
 // Floats of GemmArgs::chunk_ws for any GEMM on the current device.

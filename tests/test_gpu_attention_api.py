@@ -26,18 +26,19 @@ def _inv_freq(dh: int) -> np.ndarray:
                     np.float32)
 
 
-def _run(B, Hq, Hkv, T, Dh, seed, rope=True):
+def _run(B, Hq, Hkv, T, Dh, seed, rope=True, contraction=etb.ATTENTION_DEFAULT,
+         mags=(1.0, 1.0, 1.0, 1.0)):
     g = torch.Generator(device="cuda").manual_seed(seed)
-    q = torch.randn(B, Hq, T, Dh, device="cuda", generator=g)
-    k = torch.randn(B, Hkv, T, Dh, device="cuda", generator=g)
-    v = torch.randn(B, Hkv, T, Dh, device="cuda", generator=g)
-    do = torch.randn(B, Hq, T, Dh, device="cuda", generator=g)
+    q = torch.randn(B, Hq, T, Dh, device="cuda", generator=g) * mags[0]
+    k = torch.randn(B, Hkv, T, Dh, device="cuda", generator=g) * mags[1]
+    v = torch.randn(B, Hkv, T, Dh, device="cuda", generator=g) * mags[2]
+    do = torch.randn(B, Hq, T, Dh, device="cuda", generator=g) * mags[3]
     pos = torch.arange(T, dtype=torch.int64, device="cuda").repeat(B, 1).contiguous()
     cos = sin = None
     if rope:
         c, s = etb.rope_tables(T, Dh)
         cos, sin = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
-    att = etb.Attention(B, Hq, Hkv, T, T, Dh, pos, pos, None, cos, sin)
+    att = etb.Attention(B, Hq, Hkv, T, T, Dh, pos, pos, None, cos, sin, contraction=contraction)
     o = torch.empty_like(q)
     m = torch.empty(B, Hq, T, device="cuda")
     l = torch.empty(B, Hq, T, device="cuda")
@@ -65,24 +66,31 @@ def _oracle(q, k, v, do, rope=True):
     return o, dq, dk, dv
 
 
+MODES = [etb.ATTENTION_DEFAULT, etb.ATTENTION_BWD_PAIRS16]
+
+
+@pytest.mark.parametrize("contraction", MODES)
 @pytest.mark.parametrize("B,Hq,Hkv,T,Dh,rope", [(2, 4, 4, 256, 64, True),
                                                 (2, 4, 2, 200, 32, True),
                                                 (1, 2, 2, 384, 128, True),
+                                                (2, 4, 2, 330, 128, True),
                                                 (2, 2, 2, 96, 64, False)])
-def test_device_attention_vs_oracle(lib, cuda, B, Hq, Hkv, T, Dh, rope):
-    q, k, v, do, o, dq, dk, dv = _run(B, Hq, Hkv, T, Dh, 7 + T, rope)
+def test_device_attention_vs_oracle(lib, cuda, B, Hq, Hkv, T, Dh, rope, contraction):
+    q, k, v, do, o, dq, dk, dv = _run(B, Hq, Hkv, T, Dh, 7 + T, rope, contraction)
     ro, rdq, rdk, rdv = _oracle(q, k, v, do, rope)
     assert_close(o, ro, 2e-5, 2e-5, "o")
     for name, got, want in (("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
         assert_close(got, want, 5e-5, 5e-5, name)
 
 
-@pytest.mark.parametrize("Dh", [64, 128])
-def test_sweep_shape_sampled_heads_vs_oracle(lib, cuda, Dh):
+@pytest.mark.parametrize("Dh,contraction", [(64, etb.ATTENTION_DEFAULT),
+                                            (64, etb.ATTENTION_BWD_PAIRS16),
+                                            (128, etb.ATTENTION_DEFAULT)])
+def test_sweep_shape_sampled_heads_vs_oracle(lib, cuda, Dh, contraction):
     """B4 H16 T2048: two sampled (sequence, head) slices of the full device
     computation against the oracle on the slice alone."""
     B, H, T = 4, 16, 2048
-    q, k, v, do, o, dq, dk, dv = _run(B, H, H, T, Dh, 2048 + Dh)
+    q, k, v, do, o, dq, dk, dv = _run(B, H, H, T, Dh, 2048 + Dh, contraction=contraction)
     for b, h in ((0, 3), (3, 14)):
         sl = lambda a: np.ascontiguousarray(a[b:b + 1, h:h + 1])
         ro, rdq, rdk, rdv = _oracle(sl(q), sl(k), sl(v), sl(do))
@@ -97,3 +105,25 @@ def test_device_attention_rejects_bad_shapes(lib, cuda):
         etb.Attention(1, 3, 2, 8, 8, 64, pos, pos)  # q heads not a multiple of kv heads
     with pytest.raises(ValueError):
         etb.Attention(1, 2, 2, 8, 8, 63, pos, pos)  # odd head_dim
+
+
+@pytest.mark.parametrize("Dh", [64, 128])
+@pytest.mark.parametrize("mags", [(30.0, 0.01, 1000.0, 1e-5), (1e-3, 1e-3, 1e-4, 300.0)])
+def test_binary16_pairs_track_operand_magnitudes(lib, cuda, Dh, mags):
+    """The binary16-pair backward scales each operand tensor by its own power
+    of two: operands far from 1 (dO near 1e-5 as in a mean loss over many
+    tokens, V near 1e3, Q / K near 1e-3) keep the f32-grade bar, normwise per
+    tensor (max error <= tol max |reference|)."""
+    B, H, T = 1, 2, 320
+    q, k, v, do, o, dq, dk, dv = _run(B, H, H, T, Dh, 99 + Dh, True, etb.ATTENTION_BWD_PAIRS16,
+                                      mags)
+    ro, rdq, rdk, rdv = _oracle(q, k, v, do)
+    for name, got, want in (("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        err = np.abs(got.astype(np.float64) - want).max()
+        assert err <= 5e-5 * np.abs(want).max(), (name, err, np.abs(want).max())
+
+
+def test_unknown_contraction_mode_is_rejected(lib, cuda):
+    pos = torch.arange(8, dtype=torch.int64, device="cuda").repeat(1, 1)
+    with pytest.raises(ValueError):
+        etb.Attention(1, 2, 2, 8, 8, 64, pos, pos, contraction=7)

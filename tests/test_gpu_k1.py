@@ -125,6 +125,7 @@ def _attention_inputs(shape, seed, masked=False):
     ((1, 2, 2, 512, 512, 64), False),   # several query tiles, fully visible key blocks
     ((1, 4, 2, 300, 800, 32), False),   # Tq < Tk over several tiles, GQA
     ((1, 2, 2, 256, 256, 128), False),  # Dh 128 over several tiles
+    ((2, 4, 2, 100, 100, 128), True),   # Dh 128 (binary16-pair backward): GQA, mask, empty row
 ])
 def test_attention_vs_oracle(lib, cuda, shape, masked):
     N, Hq, Hkv, Tq, Tk, Dh = shape
