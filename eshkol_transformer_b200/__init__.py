@@ -68,6 +68,10 @@ def load() -> C.CDLL:
         "et_b200_lm_forward_backward_v1": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_void_p,
                                                        C.c_void_p, E]),
         "et_b200_lm_stream_v1": (C.c_void_p, [C.c_void_p]),
+        "et_b200_lm_set_loss_mask_v1": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32, E]),
+        "et_b200_d2_row_count_v1": (C.c_int64, [C.c_uint64, C.c_int64]),
+        "et_b200_d2_rows_v1": (C.c_int32, [C.c_void_p, C.c_uint64, C.c_int64, C.c_int64,
+                                           C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, E]),
         "et_b200_nccl_unique_id_v1": (C.c_int32, [C.c_void_p, E]),
         "et_b200_lm_enable_data_parallel_v1": (C.c_int32, [C.c_void_p, C.c_void_p, C.c_int32,
                                                            C.c_int32, E]),
@@ -222,6 +226,22 @@ class LanguageModel:
         _check(self.lib.et_b200_lm_step_device_v1(self.handle, ids_ptr, targets_ptr, loss_ptr,
                                                   C.byref(err)), err)
 
+    def set_loss_mask(self, mask=None, device_ptr: int | None = None) -> None:
+        """Loss mask [batch, seq_len] (0 / 1 bytes) of the following steps: a
+        host array, or a device pointer; None and no pointer restores the
+        unmasked objective."""
+        err = k1.KernelError()
+        if device_ptr is not None:
+            _check(self.lib.et_b200_lm_set_loss_mask_v1(self.handle, device_ptr, 1, C.byref(err)),
+                   err)
+            return
+        if mask is None:
+            _check(self.lib.et_b200_lm_set_loss_mask_v1(self.handle, None, 0, C.byref(err)), err)
+            return
+        m = np.ascontiguousarray(mask, np.uint8)
+        _check(self.lib.et_b200_lm_set_loss_mask_v1(self.handle, m.ctypes.data, 0, C.byref(err)),
+               err)
+
     def stream(self) -> int:
         return self.lib.et_b200_lm_stream_v1(self.handle)
 
@@ -320,6 +340,25 @@ class Attention:
             dout.data_ptr(), row_max.data_ptr(), row_sum.data_ptr(), dq.data_ptr(),
             dk.data_ptr(), dv.data_ptr(), self.ws_ptr, self.ws_bytes,
             1 if workspace_from_forward else 0, self.stream, C.byref(err)), err)
+
+
+def d2_row_count(tokens: int, seq_len: int) -> int:
+    """Rows of a packed D2 stream of `tokens` tokens (et_b200_d2_row_count_v1)."""
+    return load().et_b200_d2_row_count_v1(tokens, seq_len)
+
+
+def d2_rows(tokens: np.ndarray, seq_len: int, first_row: int, rows: int):
+    """(ids, targets, mask) planes [rows, seq_len] of a packed D2 stream
+    (et_b200_d2_rows_v1)."""
+    toks = np.ascontiguousarray(tokens, np.int64)
+    ids = np.empty((rows, seq_len), np.int64)
+    targets = np.empty((rows, seq_len), np.int64)
+    mask = np.empty((rows, seq_len), np.uint8)
+    err = k1.KernelError()
+    _check(load().et_b200_d2_rows_v1(toks.ctypes.data if toks.size else None, toks.size,
+                                     seq_len, first_row, rows, ids.ctypes.data,
+                                     targets.ctypes.data, mask.ctypes.data, C.byref(err)), err)
+    return ids, targets, mask
 
 
 def nccl_unique_id() -> bytes:

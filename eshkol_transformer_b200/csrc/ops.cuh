@@ -20,8 +20,17 @@ void ce_fused(const float* logits, float* dlogits, const int64_t* targets,
               const float* upstream, float upstream_scale, float* loss,
               size_t rows, size_t V, int* status, cudaStream_t stream,
               float* dlogits_lo = nullptr, OperandScale sc = OperandScale{});
-// Mean of loss[rows] as one f32 (fixed-order tree in f64).
-void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream);
+// Mean of loss[rows] as one f32 (fixed-order tree in f64); with `mask`
+// (u8 [rows], 0 / 1) the masked mean sum(mask loss) / sum(mask), +0 when no
+// row is selected.
+void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream,
+               const uint8_t* mask = nullptr);
+// The L3S numerator seed of a loss mask (native/l3s_masked_objective_provider.c:
+// 125-175): upstream[r] = mask[r] ? scale : 0, and *weight = sum of the mask
+// (the objective's weight, as f32); a byte other than 0 or 1 sets bit 2 of
+// status[0] (the reference rejects it).
+void loss_mask_seed(const uint8_t* mask, size_t rows, float scale, float* upstream, float* weight,
+                    int* status, cudaStream_t stream);
 
 // ---------------------------------------------------------------- O2 AdamW
 struct AdamwTensor {
@@ -62,6 +71,10 @@ struct AdamwControl {
   const float* skip;     // optional: nothing is checked or written when *skip != 0
   int* status;           // [1] |= kAdamw* bits (check); [2] += 1 per skipped apply
   uint64_t* completed;   // optional: applied updates, +1 by each apply that writes
+  // optional: the gradients' normalisation weight read on the device
+  // (*weight_dev * weight_mul replaces the `weight` argument)
+  const float* weight_dev;
+  float weight_mul;
 };
 // `vec`: every tensor's arrays are 16-byte aligned and its count a multiple
 // of 4 (128-bit loads and stores).

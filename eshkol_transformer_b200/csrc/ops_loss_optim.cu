@@ -52,7 +52,7 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
   const float* x = logits + row * V;
   const int64_t target = targets[row];
   const bool target_ok = target >= 0 && target < V;
-  if (!target_ok && threadIdx.x == 0) atomicExch(status, 1);
+  if (!target_ok && threadIdx.x == 0) atomicOr(status, 1);
   // The target logit is read before the block reductions: once they finish,
   // other threads overwrite the row with gradients when dlogits == logits.
   const float x_target = (threadIdx.x == 0 && target_ok) ? x[target] : 0.0f;
@@ -134,12 +134,38 @@ ce_fused_kernel(const float* __restrict__ logits, float* dlogits,
 }
 
 __global__ void mean_loss_kernel(const float* __restrict__ loss, int64_t rows,
-                                 float* out) {
+                                 float* out, const uint8_t* __restrict__ mask) {
   __shared__ double red[32];
-  double acc = 0.0;
-  for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) acc += (double)loss[i];
+  double acc = 0.0, count = 0.0;
+  for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) {
+    if (mask == nullptr) {
+      acc += (double)loss[i];
+    } else if (mask[i] != 0) {
+      acc += (double)loss[i];
+      count += 1.0;
+    }
+  }
   const double total = block_reduce(acc, red, AddOp());
-  if (threadIdx.x == 0) *out = (float)(total / (double)rows);
+  const double n = mask == nullptr ? (double)rows : block_reduce(count, red, AddOp());
+  if (threadIdx.x == 0) *out = n > 0.0 ? (float)(total / n) : 0.0f;
+}
+
+// One block: the numerator seed upstream[r] = mask[r] ? scale : 0 and the
+// mask's sum (exact: an integer count below 2^24 per call).
+__global__ void loss_mask_seed_kernel(const uint8_t* __restrict__ mask, int64_t rows, float scale,
+                                      float* __restrict__ upstream, float* weight, int* status) {
+  __shared__ double red[32];
+  double count = 0.0;
+  bool bad = false;
+  for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) {
+    const uint8_t m = mask[i];
+    bad |= m > 1;
+    upstream[i] = m != 0 ? scale : 0.0f;
+    count += m != 0 ? 1.0 : 0.0;
+  }
+  const double total = block_reduce(count, red, AddOp());
+  if (threadIdx.x == 0) *weight = (float)total;
+  if (bad) atomicOr(status, 2);
 }
 
 // ---- AdamW ----------------------------------------------------------------
@@ -252,6 +278,7 @@ adamw_vec_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __rest
   };
   if (gi < groups) load(gi, t, p0, g0, m0, v0);
   if (adamw_void<APPLY>(ctl)) return;
+  if (ctl.weight_dev != nullptr) weight = *ctl.weight_dev * ctl.weight_mul;
   if (UNIT) weight = clip = 1.0f;
   float amax = 0.0f;
   int bad = 0;
@@ -314,6 +341,7 @@ __global__ void __launch_bounds__(kAdamThreads)
 adamw_scalar_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __restrict__ prefix,
                     int tensor_count, uint64_t total, float weight, float clip, AdamwControl ctl) {
   if (adamw_void<APPLY>(ctl)) return;
+  if (ctl.weight_dev != nullptr) weight = *ctl.weight_dev * ctl.weight_mul;
   const uint64_t begin = (uint64_t)blockIdx.x * kAdamChunk;
   const uint64_t end = min(total, begin + (uint64_t)kAdamChunk);
   int t = find_tensor(prefix, tensor_count, begin);
@@ -388,7 +416,7 @@ grad_sumsq_kernel(const AdamwTensor* __restrict__ tensors, const uint64_t* __res
   }
   const double total_block = block_reduce(acc, red, AddOp());
   if (threadIdx.x == 0) partials[blockIdx.x] = total_block;
-  if (bad) atomicExch(status, 1);
+  if (bad) atomicOr(status, 1);
 }
 
 __global__ void sum_partials_kernel(const double* partials, int count, double* out) {
@@ -413,8 +441,16 @@ void ce_fused(const float* logits, float* dlogits, const int64_t* targets,
   count_launch();
 }
 
-void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream) {
-  mean_loss_kernel<<<1, 1024, 0, stream>>>(loss, (int64_t)rows, out);
+void mean_loss(const float* loss, size_t rows, float* out, cudaStream_t stream,
+               const uint8_t* mask) {
+  mean_loss_kernel<<<1, 1024, 0, stream>>>(loss, (int64_t)rows, out, mask);
+  count_launch();
+}
+
+void loss_mask_seed(const uint8_t* mask, size_t rows, float scale, float* upstream, float* weight,
+                    int* status, cudaStream_t stream) {
+  loss_mask_seed_kernel<<<1, 1024, 0, stream>>>(mask, (int64_t)rows, scale, upstream, weight,
+                                               status);
   count_launch();
 }
 
@@ -427,7 +463,7 @@ void adamw_pass(const AdamwTensor* tensors, const uint64_t* prefix, int tensor_c
   if (vec) {
     const unsigned blocks =
         (unsigned)std::min<uint64_t>(ceil_div(total / 4, kAdamThreads), (uint64_t)sm_count() * 8);
-    if (weight == 1.0f && clip == 1.0f)
+    if (weight == 1.0f && clip == 1.0f && ctl.weight_dev == nullptr)
       adamw_vec_kernel<APPLY, true><<<blocks, kAdamThreads, 0, stream>>>(
           tensors, prefix, tensor_count, total, weight, clip, ctl);
     else

@@ -572,7 +572,7 @@ __global__ void embedding_forward_kernel(const int64_t* __restrict__ ids, const 
   const int64_t row = blockIdx.x;
   const int64_t id = ids[row];
   if (id < 0 || id >= V) {
-    if (threadIdx.x == 0) atomicExch(status, 1);
+    if (threadIdx.x == 0) atomicOr(status, 1);
     return;
   }
   const float* src = w + id * d;

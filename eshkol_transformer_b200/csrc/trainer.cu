@@ -33,6 +33,8 @@
 // stream while the next layer's backward runs; AdamW waits for the last bucket.
 #include <math.h>
 
+#include <cmath>
+
 #include <algorithm>
 #include <string>
 #include <vector>
@@ -131,6 +133,13 @@ struct et_b200_lm {
   size_t splitk_floats = 0;
   void* emb_scratch = nullptr;
   int64_t *ids = nullptr, *targets = nullptr, *pos = nullptr;
+  // the loss mask of the steps (L3S masked objective; `masked` false = every
+  // token counts), its numerator seed, and the power of two 2^-ceil(log2 N)
+  // (N = global tokens) the seed carries
+  uint8_t* loss_mask = nullptr;
+  float* upstream = nullptr;
+  bool masked = false;
+  float mask_scale = 0;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   // [0] a token id or target of this step is out of range; [1] this step's
   // AdamW check bits (kAdamw*); [2] updates skipped since the last host read
@@ -461,9 +470,15 @@ void forward(et_b200_lm* lm) {
     // (split-f16 steps) its binary16 pair in logits_lo: hi, then lo
     float* dh = lm->step16 ? lm->logits_lo : lm->logits;
     float* dl = lm->step16 ? half_at(lm->logits_lo, (size_t)R * V) : lm->logits_lo;
-    ce_fused(lm->logits, dh, lm->targets, nullptr, lm->ce_scale, lm->loss_rows, R, V, lm->status,
-             s, dl, osc(lm, lm->slot_dlog()));
-    mean_loss(lm->loss_rows, R, lm->loss_mean, s);
+    // a loss mask seeds each row with its numerator (mask 2^-k) and puts
+    // the mask's sum, the objective's weight, behind the step-void flag
+    // (grads[P + 1]), which the last gradient all-reduce sums over ranks
+    if (lm->masked)
+      loss_mask_seed(lm->loss_mask, R, lm->mask_scale, lm->upstream, lm->grads + lm->P + 1,
+                     lm->status, s);
+    ce_fused(lm->logits, dh, lm->targets, lm->masked ? lm->upstream : nullptr, lm->ce_scale,
+             lm->loss_rows, R, V, lm->status, s, dl, osc(lm, lm->slot_dlog()));
+    mean_loss(lm->loss_rows, R, lm->loss_mean, s, lm->masked ? lm->loss_mask : nullptr);
   }
 }
 
@@ -606,15 +621,17 @@ void backward(et_b200_lm* lm) {
   }
   // The step-void flag at grads[P] rides the last gradient reduction, so
   // every rank agrees on skipping AdamW: + kVoidIndex for a token id or
-  // target out of range, + 1 (split-f16 steps) for an operand that reached
-  // binary16's overflow.
+  // target out of range (or a loss mask byte other than 0 / 1), + 1
+  // (split-f16 steps) for an operand that reached binary16's overflow.  The
+  // loss mask's weight at grads[P + 1] rides along (summed: the global
+  // weight).
   fold_index_flag(lm->status, lm->grads + lm->P, kVoidIndex, s);
   if (lm->step16)
     operand_range_check(lm->samax, lm->sexp, lm->nslots, lm->slot_w(), lm->grads + lm->P, s);
   if (lm->dp) {
     allreduce_range(lm, 0, 1, lm->tail_done);
     const int lg = lm->lnf_g();
-    const size_t end = lm->P + 1;
+    const size_t end = lm->P + 2;
     nccl().AllReduce(lm->G(lg), lm->G(lg), end - lm->off[lg], ncclFloat32, ncclSum,
                      lm->nccl_comm, lm->comm);
     cudaEventRecord(lm->comm_done, lm->comm);
@@ -643,8 +660,9 @@ void weight_scale(et_b200_lm* lm) {
 // binary16 pairs once a finished step has measured every slot, else 3xTF32
 // with the TF32 weight pair and every slot's max recorded.
 void begin_step(et_b200_lm* lm) {
-  // the step-void flag behind the gradients and this step's status words
-  cudaMemsetAsync(lm->grads + lm->P, 0, sizeof(float), lm->stream);
+  // the step-void flag and the loss mask's weight behind the gradients, and
+  // this step's status words
+  cudaMemsetAsync(lm->grads + lm->P, 0, 2 * sizeof(float), lm->stream);
   cudaMemsetAsync(lm->status, 0, 2 * sizeof(int), lm->stream);
   if (!lm->f16) return;
   lm->step16 = lm->calibrated;
@@ -696,7 +714,11 @@ void optimizer_step(et_b200_lm* lm) {
   adamw_prepare(lm->d_adam, lm->d_completed, lm->stream);
   // all or nothing: skipped when the step is void (flag summed across ranks)
   // or when the check pass finds a nonfinite gradient, moment or result
-  const AdamwControl ctl{lm->grads + lm->P, lm->status, lm->d_completed};
+  // with a loss mask the gradients hold numerators 2^-k: AdamW divides them
+  // by the global weight 2^-k (the reference's O2 division by the
+  // accumulated weight, o2_optimizer.c:1738, exact in the scaling)
+  const AdamwControl ctl{lm->grads + lm->P, lm->status, lm->d_completed,
+                         lm->masked ? lm->grads + lm->P + 1 : nullptr, lm->mask_scale};
   {
     Mark mk(lm, P_ADAMW_CHECK, 0, 16.0 * lm->P);
     adamw_check(lm->d_adam, lm->d_prefix, 1, lm->P, 1.0f, 1.0f, ctl, true, lm->stream);
@@ -723,7 +745,7 @@ int32_t check_ready(et_b200_lm* lm, et_kernel_error* e, const char* op) {
 // the skipped-update counter, not reported as this call's error.
 int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, const char* op,
                          bool update, bool* redo) {
-  float loss = 0.0f, flag = 0.0f;
+  float loss = 0.0f, flag = 0.0f, weight = 1.0f;
   int flags[3] = {0, 0, 0};
   int word = 0;
   uint64_t completed = 0;
@@ -732,6 +754,9 @@ int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, c
   cudaMemcpyAsync(flags, lm->status, sizeof(flags), cudaMemcpyDeviceToHost, lm->stream);
   cudaMemcpyAsync(&word, device_error_word(), sizeof(int), cudaMemcpyDeviceToHost, lm->stream);
   cudaMemcpyAsync(&flag, lm->grads + lm->P, sizeof(float), cudaMemcpyDeviceToHost, lm->stream);
+  if (lm->masked)
+    cudaMemcpyAsync(&weight, lm->grads + lm->P + 1, sizeof(float), cudaMemcpyDeviceToHost,
+                    lm->stream);
   cudaMemcpyAsync(&completed, lm->d_completed, sizeof(completed), cudaMemcpyDeviceToHost,
                   lm->stream);
   cudaError_t st = cudaStreamSynchronize(lm->stream);
@@ -753,13 +778,18 @@ int32_t finish_host_step(et_b200_lm* lm, float* host_loss, et_kernel_error* e, c
   }
   if (flag >= kVoidIndex)
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
-                     flags[0] ? "token id or target outside the vocabulary; nothing was updated"
-                              : "another rank's token id or target is outside the vocabulary; "
-                                "nothing was updated");
+                     (flags[0] & 1) ? "token id or target outside the vocabulary; nothing was updated"
+                     : (flags[0] & 2) ? "loss mask byte other than 0 or 1; nothing was updated"
+                                      : "another rank's token id, target or loss mask byte is "
+                                        "invalid; nothing was updated");
   if (flag != 0.0f && lm->step16) {
     *redo = true;
     return 0;
   }
+  if (lm->masked && weight == 0.0f)
+    return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                     update ? "the loss mask selects no token on any rank; nothing was updated"
+                            : "the loss mask selects no token on any rank");
   if (update && (flags[1] & kAdamwInputNonfinite))
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
                      "parameter, gradient, or moment is nonfinite; nothing was updated");
@@ -840,6 +870,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   lm->R = lm->B * lm->T;
   const double global = c->global_tokens > 0 ? (double)c->global_tokens : (double)lm->R;
   lm->ce_scale = (float)(1.0 / global);
+  lm->mask_scale = std::ldexp(1.0f, -(int)std::ceil(std::log2(global)));
   lm->eps = fbits(c->ln_epsilon_bits);
   {
     volatile float root = sqrtf((float)lm->Dh);
@@ -869,7 +900,7 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   cudaStreamCreateWithFlags(&lm->stream, cudaStreamNonBlocking);
   cudaStreamCreateWithFlags(&lm->comm, cudaStreamNonBlocking);
   lm->params = dalloc<float>(lm, lm->P, &err);
-  lm->grads = dalloc<float>(lm, lm->P + 8, &err);  // + the split-f16 range flag at [P]
+  lm->grads = dalloc<float>(lm, lm->P + 8, &err);  // + the step-void flag [P], mask weight [P + 1]
   lm->m1 = dalloc<float>(lm, lm->P, &err);
   lm->m2 = dalloc<float>(lm, lm->P, &err);
   if (lm->three) {
@@ -953,6 +984,8 @@ int32_t et_b200_lm_create_v1(const et_b200_lm_config_v1* c, et_b200_lm** out,
   }
   lm->ids = dalloc<int64_t>(lm, R, &err);
   lm->targets = dalloc<int64_t>(lm, R, &err);
+  lm->loss_mask = dalloc<uint8_t>(lm, R, &err);
+  lm->upstream = dalloc<float>(lm, R, &err);
   lm->pos = dalloc<int64_t>(lm, R, &err);
   lm->rope_cos = dalloc<float>(lm, lm->T * lm->Dh / 2, &err);
   lm->rope_sin = dalloc<float>(lm, lm->T * lm->Dh / 2, &err);
@@ -1154,6 +1187,37 @@ int32_t et_b200_lm_forward_backward_v1(et_b200_lm* lm, const int64_t* host_ids,
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, "lm-forward-backward", "ids and targets are required");
   stage_tokens(lm, host_ids, host_targets, cudaMemcpyHostToDevice);
   return run_host_step(lm, false, host_loss, e, "lm-forward-backward");
+}
+
+int32_t et_b200_lm_set_loss_mask_v1(et_b200_lm* lm, const uint8_t* mask, int32_t on_device,
+                                    et_kernel_error* e) {
+  const char* op = "lm-loss-mask";
+  if (check_ready(lm, e, op)) return ET_KERNEL_ERROR_INVALID_ARGUMENT;
+  if (mask == nullptr) {
+    lm->masked = false;
+    if (e) memset(e, 0, sizeof(*e));
+    return 0;
+  }
+  if (!on_device) {
+    // the L3S rule (l3s_masked_objective_provider.c:130-134): bytes are 0 or 1
+    for (int64_t i = 0; i < lm->R; i++)
+      if (mask[i] > 1)
+        return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_PROVIDER_REJECTED, op,
+                         "loss mask byte other than 0 or 1");
+  }
+  // ordered on the model's stream after every step enqueued before it
+  cudaMemcpyAsync(lm->loss_mask, mask, (size_t)lm->R, on_device ? cudaMemcpyDeviceToDevice
+                                                                : cudaMemcpyHostToDevice,
+                  lm->stream);
+  if (!on_device) {
+    const cudaError_t st = cudaStreamSynchronize(lm->stream);  // the host buffer is the caller's
+    if (st != cudaSuccess) return cuda_error(e, st, op);
+  }
+  lm->masked = true;
+  const cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return cuda_error(e, st, op);
+  if (e) memset(e, 0, sizeof(*e));
+  return 0;
 }
 
 void* et_b200_lm_stream_v1(et_b200_lm* lm) { return lm ? (void*)lm->stream : nullptr; }

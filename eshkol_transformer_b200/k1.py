@@ -148,9 +148,10 @@ class KernelCall:
         for i, (ptr, nbytes, dt, shape, dev) in enumerate(descs):
             arr = (C.c_uint64 * max(1, len(shape)))(*shape)
             self._keep.append(arr)
+            # a scalar (rank 0) view carries no shape array
             view = TensorView(C.sizeof(TensorView), ptr, nbytes, dt.encode(), dev.encode(),
                               LAYOUT_DENSE_ROW_MAJOR, 0, len(shape),
-                              C.cast(arr, C.POINTER(C.c_uint64)))
+                              C.cast(arr, C.POINTER(C.c_uint64)) if len(shape) else None)
             if i < n_in:
                 self._in[i] = view
             else:

@@ -323,8 +323,43 @@ int32_t et_b200_lm_forward_backward_v1(et_b200_lm *lm,
                                        const int64_t *host_targets,
                                        float *host_loss,
                                        et_kernel_error *error);
+/* Loss mask of the following steps (the L3S masked objective,
+ * native/l3s_masked_objective_provider.c:125-175, with the reference's O2
+ * division by the accumulated weight, o2_optimizer.c:1738): `mask` is
+ * u8 [batch * seq_len] (row-major [batch, seq_len], the D2 loss-mask plane),
+ * each byte 0 or 1, in host memory (on_device 0: checked and copied before
+ * the call returns) or device memory (on_device 1: copied on the model's
+ * stream; a byte other than 0 / 1 voids the next step, which then reports
+ * INVALID_ARGUMENT with nothing updated).  NULL restores the unmasked
+ * objective.  With a mask the loss is sum(mask ce) / sum(mask) over this
+ * rank's tokens, each token's CE gradient is seeded with mask 2^-k
+ * (k = ceil(log2 global tokens), an exact scaling) so the gradients hold the
+ * mask-weighted numerators 2^-k, and AdamW divides them by the global weight
+ * sum(mask) 2^-k (summed over the data-parallel ranks with the last gradient
+ * bucket).  A step whose global weight is 0 updates nothing and reports
+ * INVALID_ARGUMENT.  No reference counterpart for the entry point itself: the
+ * reference feeds the mask through its Eshkol objective bridge. */
+int32_t et_b200_lm_set_loss_mask_v1(et_b200_lm *lm, const uint8_t *mask,
+                                    int32_t on_device, et_kernel_error *error);
 /* The cudaStream_t the model enqueues on. */
 void *et_b200_lm_stream_v1(et_b200_lm *lm);
+
+/* ------------------------------------------------------------ D2 batch planes
+ * The i64 input / target planes and the bool loss-mask plane of a fixed
+ * [rows, seq_len] batch from one flat token stream, by the row rule of the
+ * reference's D2 shard loader in packed mode (docs/D2_SHARD_LOADER.md, "Rows,
+ * shift, mask, and ordering"): the stream holds 0 rows when length < 2, else
+ * 1 + floor((length - 2) / seq_len); row r starts at r seq_len; a position
+ * whose target exists in the stream takes input token[s + t], target
+ * token[s + t + 1] and mask 1; every other position holds 0, 0, 0.  Host
+ * memory; rows first_row .. first_row + rows - 1 of the stream (rows past its
+ * end are all padding); INVALID_ARGUMENT when first_row is past the last row
+ * (a batch needs a true mask bit).  Shuffling and shard boundaries (unpacked
+ * mode) stay with the caller's loader. */
+int64_t et_b200_d2_row_count_v1(uint64_t tokens, int64_t seq_len);
+int32_t et_b200_d2_rows_v1(const int64_t *tokens, uint64_t length, int64_t seq_len,
+                           int64_t first_row, int64_t rows, int64_t *ids,
+                           int64_t *targets, uint8_t *mask, et_kernel_error *error);
 /* Data parallelism: NCCL communicator over `world` ranks.  unique_id is the
  * 128-byte ncclUniqueId rank 0 obtained from et_b200_nccl_unique_id_v1 and
  * shared with every rank.  Gradients are then summed across ranks in buckets

@@ -856,9 +856,45 @@ static void add_into(size_t count, float *dst, const float *src) {
   for (size_t i = 0; i < count; i++) dst[i] = dst[i] + src[i];
 }
 
+/* The L3S reduce (native/l3s_masked_objective_provider.c:139-160) over
+ * `rows` tokens: w = sum of the mask, n = sum of mask * loss, each a
+ * left-to-right f32 sum, mean = n / w (+0 when w is 0). */
+float orc_masked_mean_loss(size_t rows, const float *loss, const uint8_t *mask) {
+  float w = 0.0f, n = 0.0f;
+  for (size_t r = 0; r < rows; r++) {
+    const float m = mask[r] ? 1.0f : 0.0f;
+    w = w + m;
+    const float p = m * loss[r];
+    n = n + p;
+  }
+  return w > 0.0f ? n / w : 0.0f;
+}
+
+static float lm_forward_backward(const orc_lm_config *c, const float *params,
+                                 const int64_t *ids, const int64_t *targets,
+                                 const uint8_t *loss_mask, float scale, float *grads);
+
 float orc_lm_forward_backward(const orc_lm_config *c, const float *params,
                               const int64_t *ids, const int64_t *targets,
                               double token_scale, float *grads) {
+  const double R = (double)c->batch * (double)c->seq_len;
+  return lm_forward_backward(c, params, ids, targets, NULL,
+                             (float)(1.0 / (token_scale > 0 ? token_scale : R)), grads);
+}
+
+/* The masked objective: CE upstream mask[r] * upstream_scale (the L3S
+ * numerator seed, scaled), loss the L3S masked mean; the gradients hold the
+ * mask-weighted numerators times upstream_scale (O2 divides by the weight). */
+float orc_lm_forward_backward_masked(const orc_lm_config *c, const float *params,
+                                     const int64_t *ids, const int64_t *targets,
+                                     const uint8_t *loss_mask, float upstream_scale,
+                                     float *grads) {
+  return lm_forward_backward(c, params, ids, targets, loss_mask, upstream_scale, grads);
+}
+
+static float lm_forward_backward(const orc_lm_config *c, const float *params,
+                                 const int64_t *ids, const int64_t *targets,
+                                 const uint8_t *loss_mask, float scale, float *grads) {
   const size_t L = (size_t)c->layers, d = (size_t)c->d_model,
                H = (size_t)c->heads, F = (size_t)c->ffn,
                V = (size_t)c->vocabulary, T = (size_t)c->seq_len,
@@ -942,13 +978,15 @@ float orc_lm_forward_backward(const orc_lm_config *c, const float *params,
   orc_linear_forward(R, d, V, xf, P(0), NULL, logits);
   float *loss = (float *)malloc(R * sizeof(float));
   orc_ce_forward(R, V, logits, targets, loss);
-  const float mean = orc_mean_loss(R, loss);
+  const float mean = loss_mask ? orc_masked_mean_loss(R, loss, loss_mask)
+                               : orc_mean_loss(R, loss);
 
   /* backward: CE upstream is 1/N (the reference's numerator seed 1 with the
-   * O2 division by the token weight N moved here; exact for N = 2^k). */
+   * O2 division by the token weight N moved here; exact for N = 2^k), or
+   * with a loss mask the seed mask[r] times `scale`. */
   float *upstream = loss; /* reuse */
-  const float scale = (float)(1.0 / (token_scale > 0 ? token_scale : (double)R));
-  for (size_t r = 0; r < R; r++) upstream[r] = scale;
+  for (size_t r = 0; r < R; r++)
+    upstream[r] = loss_mask ? (loss_mask[r] ? scale : 0.0f) : scale;
   float *dlogits = logits; /* in place is fine: each row reads before write */
   {
     float *tmp = (float *)malloc(R * V * sizeof(float));

@@ -116,6 +116,11 @@ void orc_rope_inv_freq(int64_t head_dim, double base, float *inv_freq);
 float orc_lm_forward_backward(const orc_lm_config *c, const float *params,
                               const int64_t *ids, const int64_t *targets,
                               double token_scale, float *grads);
+float orc_lm_forward_backward_masked(const orc_lm_config *c, const float *params,
+                                     const int64_t *ids, const int64_t *targets,
+                                     const uint8_t *loss_mask, float upstream_scale,
+                                     float *grads);
+float orc_masked_mean_loss(size_t rows, const float *loss, const uint8_t *mask);
 /* One AdamW update over all tensors in parameter order. */
 int orc_lm_adamw(const orc_lm_config *c, float *params, const float *grads,
                  float *exp_avg, float *exp_avg_sq,

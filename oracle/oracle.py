@@ -39,6 +39,12 @@ def lib() -> C.CDLL:
                                              C.c_uint64]
         _lib.orc_mean_loss.restype = C.c_float
         _lib.orc_lm_forward_backward.restype = C.c_float
+        _lib.orc_lm_forward_backward_masked.restype = C.c_float
+        _lib.orc_lm_forward_backward_masked.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p,
+                                                        C.c_void_p, C.c_void_p, C.c_float,
+                                                        C.c_void_p]
+        _lib.orc_masked_mean_loss.restype = C.c_float
+        _lib.orc_masked_mean_loss.argtypes = [C.c_size_t, C.c_void_p, C.c_void_p]
         _lib.orc_lm_tensor_count.restype = C.c_size_t
         _lib.orc_lm_tensor_sizes.restype = C.c_size_t
         _lib.orc_fill_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t, C.c_double,
@@ -257,6 +263,33 @@ def mean_loss(loss) -> float:
     return lib().orc_mean_loss(C.c_size_t(loss.size), _p(loss))
 
 
+def masked_mean_loss(loss, mask) -> float:
+    loss = f32(loss)
+    m = np.ascontiguousarray(mask, np.uint8)
+    return lib().orc_masked_mean_loss(C.c_size_t(loss.size), _p(loss), _p(m))
+
+
+def d2_rows(tokens, seq_len: int, first_row: int, rows: int):
+    """The packed D2 row rule (docs/D2_SHARD_LOADER.md, "Rows, shift, mask,
+    and ordering") in plain Python: (ids, targets, mask) planes [rows,
+    seq_len] of rows first_row .. of the stream."""
+    toks = list(int(t) for t in tokens)
+    L = len(toks)
+    count = 0 if L < 2 else 1 + (L - 2) // seq_len
+    ids = np.zeros((rows, seq_len), np.int64)
+    targets = np.zeros((rows, seq_len), np.int64)
+    mask = np.zeros((rows, seq_len), np.uint8)
+    for r in range(rows):
+        if first_row + r >= count:
+            break
+        s = (first_row + r) * seq_len
+        for t in range(seq_len):
+            if s + t + 1 >= L:
+                break
+            ids[r, t], targets[r, t], mask[r, t] = toks[s + t], toks[s + t + 1], 1
+    return ids, targets, mask
+
+
 # ---------------------------------------------------------------- LM
 
 class LMConfig(C.Structure):
@@ -287,6 +320,17 @@ class LanguageModel:
         params, ids, targets = f32(params), i64(ids), i64(targets)
         loss = lib().orc_lm_forward_backward(C.byref(self.cfg), _p(params), _p(ids),
                                              _p(targets), token_scale, _p(grads))
+        return float(loss), grads
+
+    def forward_backward_masked(self, params, ids, targets, loss_mask, upstream_scale: float):
+        """The masked objective: loss = the L3S masked mean, gradients = the
+        mask-weighted numerators times upstream_scale."""
+        grads = np.zeros(self.total, np.float32)
+        params, ids, targets = f32(params), i64(ids), i64(targets)
+        m = np.ascontiguousarray(loss_mask, np.uint8)
+        loss = lib().orc_lm_forward_backward_masked(C.byref(self.cfg), _p(params), _p(ids),
+                                                    _p(targets), _p(m), upstream_scale,
+                                                    _p(grads))
         return float(loss), grads
 
     def adamw(self, params, grads, m, v, options: AdamwOptions, update: int) -> int:
