@@ -26,7 +26,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, out_dir, precision):
+def _loss_mask(R: int) -> np.ndarray:
+    """The masked case's full-batch loss mask: rank 0's half selects no
+    token at all, rank 1's about two thirds."""
+    m = (np.arange(R) % 3 != 1).astype(np.uint8)
+    m[:R // 2] = 0
+    return m
+
+
+def _rank(rank, world, port, out_dir, precision, masked):
     import sys
     from pathlib import Path
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
@@ -48,6 +56,8 @@ def _rank(rank, world, port, out_dir, precision):
     model.enable_data_parallel(uid[0], rank, world)
     ids, targets = orc.synthetic_batch(31, s.batch, s.seq_len, s.vocabulary)
     mine = slice(rank * per, (rank + 1) * per)
+    if masked:
+        model.set_loss_mask(_loss_mask(s.batch * s.seq_len).reshape(s.batch, s.seq_len)[mine])
     model.forward_backward(ids[mine], targets[mine])
     if precision == etb.PRECISION_F16X3:
         model.forward_backward(ids[mine], targets[mine])
@@ -60,19 +70,26 @@ def _rank(rank, world, port, out_dir, precision):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("precision", [0, 3])  # PRECISION_TF32X3, PRECISION_F16X3
-def test_two_gpu_allreduce_matches_full_batch(tmp_path, precision):
+# (precision, masked): PRECISION_TF32X3 = 0, PRECISION_F16X3 = 3; the masked
+# case puts the loss-mask weight on the last bucket's all-reduce (rank 0
+# selects no token, so its AdamW divides by rank 1's weight alone)
+@pytest.mark.parametrize("precision,masked", [(0, False), (3, False), (0, True)])
+def test_two_gpu_allreduce_matches_full_batch(tmp_path, precision, masked):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import eshkol_transformer_b200 as etb
     from oracle import oracle as orc
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), precision), nprocs=2,
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), precision, masked), nprocs=2,
                        start_method="spawn")
     s = etb.TINY
     om = orc.LanguageModel(s.layers, s.d_model, s.heads, s.ffn, s.vocabulary, s.seq_len, s.batch)
     params = om.init(4321)
     ids, targets = orc.synthetic_batch(31, s.batch, s.seq_len, s.vocabulary)
-    _, grads_ref = om.forward_backward(params, ids, targets)
+    if masked:
+        _, grads_ref = om.forward_backward_masked(params, ids, targets,
+                                                  _loss_mask(s.batch * s.seq_len), 2.0 ** -9)
+    else:
+        _, grads_ref = om.forward_backward(params, ids, targets)
     g0, g1 = np.load(tmp_path / "grads0.npy"), np.load(tmp_path / "grads1.npy")
     assert np.array_equal(g0.view(np.uint32), g1.view(np.uint32))
     for t, (a, b) in enumerate(zip(om.split(g0), om.split(grads_ref))):
