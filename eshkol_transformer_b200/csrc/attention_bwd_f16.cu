@@ -261,7 +261,32 @@ struct Bwd16Args {
   const float *lse2, *delta;
   const unsigned* amax;
   int* error;
+  float* chunks;     // dK/dV chunk sums, kBwdChunkFloats per slot
+  int* slot_flags;   // 0 free, 1 taken
+  int chunk_slots;
 };
+
+// dK and dV accumulate over up to G Tq queries; the tensor pipe's f32
+// accumulation truncates, so a CTA whose key tile sees more than
+// kChunkBlocks query blocks (2,048 queries) sums its accumulators in chunks:
+// at every chunk boundary the probability warps add the finished chunk into
+// the CTA's slot in global memory (f32), and the next chunk restarts the
+// TMEM accumulation.  (Measured at T = 16,384: one accumulator per key tile
+// left dK / dV 1e-4 from float64, outside the A2 tolerance.)
+constexpr int kChunkBlocks = 32;
+
+// A free chunk slot for this CTA (thread 0, after its TMEM allocation):
+// bounded scan from a CTA-dependent start; -1 (and the error word) if none
+// is free, which cannot happen with one slot-holding CTA per SM.
+__device__ __forceinline__ int take_chunk_slot(const Bwd16Args& a) {
+  const uint64_t lin = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z);
+  for (int i = 0; i < 4 * a.chunk_slots; i++) {
+    const int s = (int)((lin + (uint64_t)i) % (uint64_t)a.chunk_slots);
+    if (atomicCAS(a.slot_flags + s, 0, 1) == 0) return s;
+  }
+  atomicExch(a.error, 0x6e6d);
+  return -1;
+}
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
@@ -330,7 +355,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
   // EMPTY barrier completes when both chains' MMAs reading the stage are done.
   enum {
     LO_FULL, QF0, QF1, QE0, QE1, GF0, GF1, GE0, GE1, SA_DONE, SB_DONE, P_READY, VA_DONE, KB_DONE,
-    D_READY0, D_READY1, ST_FULL0, ST_FULL1, DRAIN_A, DRAIN_B, NBARS
+    D_READY0, D_READY1, ST_FULL0, ST_FULL1, DRAIN_A, DRAIN_B, CHUNK_DONE, NBARS
   };
   const uint32_t bar0 = smem_u32(bars);
   auto B_ = [&](int i) { return bar0 + 8u * (uint32_t)i; };
@@ -345,7 +370,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
   const bool valid_k = tk < p.Tk;
   if (tid == 0) {
     for (int i = 0; i < NBARS; i++) {
-      const uint32_t n = (i == P_READY || i == D_READY0 || i == D_READY1) ? SOFT
+      const uint32_t n = (i == P_READY || i == D_READY0 || i == D_READY1 || i == CHUNK_DONE) ? SOFT
                          : (i == ST_FULL0 || i == ST_FULL1)               ? 32
                          : (i >= QE0 && i <= QE1) || (i >= GE0 && i <= GE1) ? 2
                                                                           : 1;
@@ -366,6 +391,12 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
   const int n_it = G * per_head;
   auto q0_of = [&](int it) { return (jb + it % per_head) * BQ; };
   auto hq_of = [&](int it) { return hkv * G + it / per_head; };
+  const bool chunked = n_it > kChunkBlocks;
+  volatile int* slot_s = reinterpret_cast<volatile int*>(tslot + 2);
+  if (tid == 0) {
+    *slot_s = chunked ? take_chunk_slot(a) : -1;
+    if (chunked && *slot_s < 0) *abort = 1;
+  }
   const uint32_t kh_stage = base + L::QR + 2 * L::QT, vh_stage = base + L::GR + 2 * L::QT;
   if (tid == 0 && n_it > 0) {
     // the key tile: K, V lo stay in shared memory; K, V hi pass through stage
@@ -497,6 +528,10 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         s_issued++;
         ok = role_wait(B_(is_a ? P_READY : D_READY0 + s), is_a ? par : spar, a.error, abort);
         if (ok) ok = role_wait(B_(mfull + s), spar, a.error, abort);
+        // a new chunk starts once the probability warps have added the last one
+        const bool restart = j % kChunkBlocks == 0;
+        if (ok && restart && j > 0)
+          ok = role_wait(B_(CHUNK_DONE), (uint32_t)((j / kChunkBlocks - 1) & 1), a.error, abort);
         if (!ok) break;
         tc_fence_after();
         const uint32_t mt = base + mring + (uint32_t)s * 2u * L::QT;
@@ -505,7 +540,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
           // queries 16k..16k+15: hi / lo columns of the half that wrote them
           const uint32_t ah = sd + 32u * (uint32_t)(k >> 1) + 8u * (uint32_t)(k & 1);
           const uint64_t bh = mdesc16<BQ>(mt, k), bl = mdesc16<BQ>(mt + L::QT, k);
-          umma_f16_ts(acc_d, ah, bh, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(acc_d, ah, bh, idesc_o, (!restart || k > 0) ? 1u : 0u);
           umma_f16_ts(acc_d, ah, bl, idesc_o, 1u);
           umma_f16_ts(acc_d, ah + 16u, bh, idesc_o, 1u);
         }
@@ -530,6 +565,11 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     const float u_dp = exp2_int(-(ex.v + ex.g));
     const float s_p = exp2_int(kPExp), s_ds = exp2_int(ex.ds);
     const int cb = 32 * khalf;  // this thread's first query column of the block
+    const int slot = *slot_s;
+    // this thread's row of the chunk sums: dK (warps 0-3) or dV (warps 4-7)
+    float* crow = slot >= 0 ? a.chunks + (size_t)slot * kBwdChunkFloats +
+                                  (size_t)(khalf * 128 + row) * DH
+                            : nullptr;
     bool ok = true;
     for (int j = 0; ok && j < n_it; j++) {
       const int s = j & 1;
@@ -584,6 +624,35 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         tc_fence_before();
         mbar_arrive(B_(P_READY));
       }
+      if (j > 0 && j % kChunkBlocks == 0) {
+        // the chunk ending with block j - 1: once this thread's accumulator
+        // (dK for warps 0-3, dV for 4-7) has its last MMA of that chunk, add
+        // it into the slot; the next chunk's first gradient MMAs wait for
+        // every thread (block j's probabilities are already out)
+        ok = role_wait(B_(khalf == 0 ? KB_DONE : VA_DONE), (uint32_t)((j - 1) & 1), a.error,
+                       abort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const bool first = j == kChunkBlocks;
+#pragma unroll
+        for (int c = 0; c < DH / 32; c++) {
+          float v[32];
+          tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+          float4* dst = reinterpret_cast<float4*>(crow + 32 * c);
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            float4 x = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+            if (!first) {
+              const float4 y = dst[u];
+              x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
+            }
+            dst[u] = x;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(B_(CHUNK_DONE));
+      }
       ok = role_wait(B_(SB_DONE), par, a.error, abort);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -627,6 +696,14 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         float v[32];
         if (n_it > 0) {
           tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+          if (crow != nullptr) {  // plus the earlier chunks
+            const float4* src = reinterpret_cast<const float4*>(crow + 32 * c);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+              const float4 y = src[u];
+              v[4 * u] += y.x; v[4 * u + 1] += y.y; v[4 * u + 2] += y.z; v[4 * u + 3] += y.w;
+            }
+          }
 #pragma unroll
           for (int i = 0; i < 32; i++) v[i] *= un;
         } else {
@@ -673,6 +750,10 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, L::COLS);
+  }
+  if (tid == 0 && *slot_s >= 0) {  // the slot's sums were read above
+    __threadfence();
+    atomicExch(a.slot_flags + *slot_s, 0);
   }
 }
 
@@ -1052,7 +1133,9 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
   attn16_split_dout_kernel<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(p, dout, w.g16h,
                                                                           w.g16l, w.amax16);
   count_launch(4);
-  Bwd16Args a{w.lse2, delta, w.amax16, device_error_word()};
+  cudaMemsetAsync(w.slot_flags, 0, (size_t)w.chunk_slots * sizeof(int), stream);
+  Bwd16Args a{w.lse2, delta, w.amax16, device_error_word(), w.chunks, w.slot_flags,
+              w.chunk_slots};
   dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);
   dim3 g2((p.Tq + QM - 1) / QM, p.Hq, p.B);
   if (p.mask != nullptr) {

@@ -80,7 +80,32 @@ struct TcBwdArgs {
   const float *doh, *dol;   // head-major dO hi/lo (dQ kernel)
   const float *lse2, *delta;
   int* error;
+  float* chunks;     // dK/dV chunk sums, kBwdChunkFloats per slot
+  int* slot_flags;   // 0 free, 1 taken
+  int chunk_slots;
 };
+
+// dK and dV accumulate over up to G Tq queries; the tensor pipe's f32
+// accumulation truncates, so a CTA whose key tile sees more than
+// kChunkBlocks query blocks (1,024 queries: 3xTF32 issues twice the MMAs per
+// query of the binary16 kernels) sums its accumulators in chunks: at every
+// chunk boundary the probability warps add the finished chunk into the CTA's
+// slot in global memory (f32), and the next chunk restarts the TMEM
+// accumulation.
+constexpr int kChunkBlocks = 16;
+
+// A free chunk slot for this CTA (thread 0, after its TMEM allocation):
+// bounded scan from a CTA-dependent start; -1 (and the error word) if none
+// is free, which cannot happen with one slot-holding CTA per SM.
+__device__ __forceinline__ int take_chunk_slot(const TcBwdArgs& a) {
+  const uint64_t lin = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z);
+  for (int i = 0; i < 4 * a.chunk_slots; i++) {
+    const int s = (int)((lin + (uint64_t)i) % (uint64_t)a.chunk_slots);
+    if (atomicCAS(a.slot_flags + s, 0, 1) == 0) return s;
+  }
+  atomicExch(a.error, 0x6e6d);
+  return -1;
+}
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
@@ -159,7 +184,8 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BARS);
   enum {
     LO_FULL, QK_FULL, QK_EMPTY, GK_FULL, GK_EMPTY, GM_FULL, GM_EMPTY, QM_FULL, QM_EMPTY,
-    SA_DONE, SB_DONE, P_READY, VA_DONE, KB_DONE, D_READY0, D_READY1, ST_FULL0, ST_FULL1, NBARS
+    SA_DONE, SB_DONE, P_READY, VA_DONE, KB_DONE, D_READY0, D_READY1, ST_FULL0, ST_FULL1,
+    CHUNK_DONE, NBARS
   };
   const uint32_t bar0 = smem_u32(bars);
   auto B_ = [&](int i) { return bar0 + 8u * (uint32_t)i; };
@@ -174,7 +200,7 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   const bool valid_k = tk < p.Tk;
   if (tid == 0) {
     for (int i = 0; i < NBARS; i++) {
-      const uint32_t n = (i == P_READY || i == D_READY0 || i == D_READY1) ? SOFT
+      const uint32_t n = (i == P_READY || i == D_READY0 || i == D_READY1 || i == CHUNK_DONE) ? SOFT
                          : (i == ST_FULL0 || i == ST_FULL1)               ? 32
                                                                           : 1;
       mbar_init(B_(i), n);
@@ -196,6 +222,12 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   const int n_it = G * per_head;
   auto q0_of = [&](int it) { return (jb + it % per_head) * BQ; };
   auto hq_of = [&](int it) { return hkv * G + it / per_head; };
+  const bool chunked = n_it > kChunkBlocks;
+  volatile int* slot_s = reinterpret_cast<volatile int*>(tslot + 2);
+  if (tid == 0) {
+    *slot_s = chunked ? take_chunk_slot(a) : -1;
+    if (chunked && *slot_s < 0) *abort = 1;
+  }
   if (tid == 0 && n_it > 0) {
     // the key tile: K, V lo stay in shared memory as A operands; K, V hi pass
     // through the MN-major Q/dO buffers (needed last by the first block) on
@@ -339,11 +371,15 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
         ok = role_wait(B_(is_a ? P_READY : D_READY0 + (j & 1)), is_a ? par : (uint32_t)((j >> 1) & 1),
                        a.error, abort);
         if (ok) ok = role_wait(B_(mfull), par, a.error, abort);
+        // a new chunk starts once the probability warps have added the last one
+        const bool restart = j % kChunkBlocks == 0;
+        if (ok && restart && j > 0)
+          ok = role_wait(B_(CHUNK_DONE), (uint32_t)((j / kChunkBlocks - 1) & 1), a.error, abort);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < BQ / 8; k++) {
-          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          const uint32_t acc = (!restart || k > 0) ? 1u : 0u;
           umma_tf32_ts(acc_d, sd + 8 * k, mslice(bm_h, k), idesc_o, acc);
           umma_tf32_ts(acc_d, sd + 8 * k, mslice(bm_l, k), idesc_o, 1u);
           umma_tf32_ts(acc_d, lo_op + 8 * k, mslice(bm_h, k), idesc_o, 1u);
@@ -370,6 +406,11 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
     const int64_t kpos_last = kp[min(k0 + BK, p.Tk) - 1];
     const float c2 = p.scale * kLog2e;
     const int cb = 32 * khalf;  // this thread's first column of the block
+    const int slot = *slot_s;
+    // this thread's row of the chunk sums: dK (warps 0-3) or dV (warps 4-7)
+    float* crow = slot >= 0 ? a.chunks + (size_t)slot * kBwdChunkFloats +
+                                  (size_t)(khalf * 128 + row) * DH
+                            : nullptr;
     bool ok = true;
     for (int j = 0; ok && j < n_it; j++) {
       const int s = j & 1;
@@ -427,6 +468,35 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
         tc_fence_before();
         mbar_arrive(B_(P_READY));
       }
+      if (j > 0 && j % kChunkBlocks == 0) {
+        // the chunk ending with block j - 1: once this thread's accumulator
+        // (dK for warps 0-3, dV for 4-7) has its last MMA of that chunk, add
+        // it into the slot; the next chunk's first gradient MMAs wait for
+        // every thread (block j's probabilities are already out)
+        ok = role_wait(B_(khalf == 0 ? KB_DONE : VA_DONE), (uint32_t)((j - 1) & 1), a.error,
+                       abort);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const bool first = j == kChunkBlocks;
+#pragma unroll
+        for (int c = 0; c < DH / 32; c++) {
+          float v[32];
+          tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+          float4* dst = reinterpret_cast<float4*>(crow + 32 * c);
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            float4 x = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+            if (!first) {
+              const float4 y = dst[u];
+              x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
+            }
+            dst[u] = x;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(B_(CHUNK_DONE));
+      }
       ok = role_wait(B_(SB_DONE), par, a.error, abort);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -470,6 +540,14 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
         float v[32];
         if (n_it > 0) {
           tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+          if (crow != nullptr) {  // plus the earlier chunks
+            const float4* src = reinterpret_cast<const float4*>(crow + 32 * c);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+              const float4 y = src[u];
+              v[4 * u] += y.x; v[4 * u + 1] += y.y; v[4 * u + 2] += y.z; v[4 * u + 3] += y.w;
+            }
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < 32; i++) v[i] = 0.0f;
@@ -515,6 +593,10 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, L::COLS);
+  }
+  if (tid == 0 && *slot_s >= 0) {  // the slot's sums were read above
+    __threadfence();
+    atomicExch(a.slot_flags + *slot_s, 0);
   }
 }
 
@@ -931,7 +1013,10 @@ bool launch_bwd_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTen
         p, o, o_lo, dout, row_max, row_sum, delta, w.lse2, w.doh, w.dol);
     count_launch();
   }
-  TcBwdArgs a{w.kh, w.vh, w.qh, w.ql, w.doh, w.dol, w.lse2, delta, device_error_word()};
+  cudaMemsetAsync(w.slot_flags, 0, (size_t)w.chunk_slots * sizeof(int), stream);
+  TcBwdArgs a{w.kh,    w.vh,    w.qh,     w.ql,           w.doh,        w.dol,
+              w.lse2,  delta,   device_error_word(),       w.chunks,     w.slot_flags,
+              w.chunk_slots};
   dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);  // THREADS: 8 probability warps, MMA, loads
   dim3 g2((p.Tq + QM - 1) / QM, p.Hq, p.B);
   if (p.mask != nullptr) {

@@ -579,8 +579,11 @@ size_t attention_qkv_workspace_floats(const AttnParams& p) {
 size_t attention_grad_workspace_floats(const AttnParams& p) {
   const size_t nq = (size_t)p.B * p.Hq * p.Tq * p.Dh, rows = (size_t)p.B * p.Hq * p.Tq;
   const size_t nk = (size_t)p.B * p.Hkv * p.Tk * p.Dh;
-  // dO pair, lse2, then the binary16 K and V pairs and the operand maxima
-  return 2 * nq + ((rows + 63) & ~(size_t)63) + 2 * nk + 64;
+  // dO pair, lse2, then the binary16 K and V pairs, the operand maxima, the
+  // chunk slots' flags and the chunk sums
+  const size_t slots = (size_t)attn_chunk_slots();
+  return 2 * nq + ((rows + 63) & ~(size_t)63) + 2 * nk + 64 + ((slots + 63) & ~(size_t)63) +
+         slots * (size_t)kBwdChunkFloats;
 }
 size_t attention_workspace_floats(const AttnParams& p) {
   return attention_qkv_workspace_floats(p) + attention_grad_workspace_floats(p);

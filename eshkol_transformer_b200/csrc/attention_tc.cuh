@@ -23,7 +23,19 @@ struct AttnWs {
   float *qh, *ql, *kh, *kl, *vh, *vl, *doh, *dol, *lse2;
   uint16_t *g16h, *g16l, *q16h, *q16l, *k16h, *k16l, *v16h, *v16l;
   unsigned* amax16;
+  // dK/dV chunk sums of the backward: `chunk_slots` slots of
+  // kBwdChunkFloats floats (one per CTA holding one), each slot's flag in
+  // slot_flags (0 free, 1 taken; cleared before every backward launch)
+  int* slot_flags;
+  float* chunks;
+  int chunk_slots;
 };
+// dK and dV rows of a 128-key tile at head_dim <= 128, f32.
+constexpr int kBwdChunkFloats = 2 * 128 * 128;
+// Slots: every CTA that sums dK/dV in chunks holds one while it runs, and at
+// most one such CTA is resident per SM (each holds all 512 TMEM columns and
+// takes its slot after allocating them); twice the SM count leaves margin.
+inline int attn_chunk_slots() { return 2 * sm_count(); }
 inline AttnWs attn_ws(const AttnParams& p) {
   const size_t nq = (size_t)p.B * p.Hq * p.Tq * p.Dh, nk = (size_t)p.B * p.Hkv * p.Tk * p.Dh;
   const size_t rows = (size_t)p.B * p.Hq * p.Tq;
@@ -46,6 +58,9 @@ inline AttnWs attn_ws(const AttnParams& p) {
   w.v16h = w.k16l + nk;
   w.v16l = w.v16h + nk;
   w.amax16 = reinterpret_cast<unsigned*>(w.v16l + nk);
+  w.chunk_slots = attn_chunk_slots();
+  w.slot_flags = reinterpret_cast<int*>(w.amax16 + 64);
+  w.chunks = reinterpret_cast<float*>(w.slot_flags + ((w.chunk_slots + 63) & ~63));
   return w;
 }
 

@@ -15,6 +15,7 @@ import pytest
 import torch
 
 import eshkol_transformer_b200 as etb
+from attention_f64 import attention_f64
 from helpers import assert_close
 from oracle import oracle as orc
 
@@ -127,3 +128,32 @@ def test_unknown_contraction_mode_is_rejected(lib, cuda):
     pos = torch.arange(8, dtype=torch.int64, device="cuda").repeat(1, 1)
     with pytest.raises(ValueError):
         etb.Attention(1, 2, 2, 8, 8, 64, pos, pos, contraction=7)
+
+
+@pytest.mark.parametrize("Dh,contraction", [(64, etb.ATTENTION_DEFAULT),
+                                            (64, etb.ATTENTION_BWD_PAIRS16),
+                                            (128, etb.ATTENTION_DEFAULT)])
+def test_long_sequence_slice_vs_float64(lib, cuda, Dh, contraction):
+    """T = 8,192, one (sequence, head): every key tile's dK / dV sums
+    thousands of query rows, across several f32 chunks of the accumulation
+    (without the chunks dK / dV drifted to 1e-4 at T = 16,384).  Against a
+    float64 evaluation, element-wise within the A2 bar (5e-5 abs + rel)."""
+    T = 8192
+    q, k, v, do = (orc.fill_normal(700 + Dh, i, T * Dh).reshape(1, 1, T, Dh) for i in range(4))
+    pos = torch.arange(T, dtype=torch.int64, device="cuda").reshape(1, T)
+    c, s_ = etb.rope_tables(T, Dh)
+    att = etb.Attention(1, 1, 1, T, T, Dh, pos, pos, None, torch.from_numpy(c).cuda(),
+                        torch.from_numpy(s_).cuda(), contraction=contraction)
+    tq, tk, tv, tdo = (torch.from_numpy(x).cuda() for x in (q, k, v, do))
+    o = torch.empty_like(tq)
+    m = torch.empty(1, 1, T, device="cuda")
+    l = torch.empty_like(m)
+    dq, dk, dv = torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv)
+    att.forward(tq, tk, tv, o, m, l)
+    att.backward(tq, tk, tv, o, tdo, m, l, dq, dk, dv)
+    torch.cuda.synchronize()
+    want = attention_f64(q[0, 0], k[0, 0], v[0, 0], do[0, 0], c, s_)
+    for name, got, ref in zip(("o", "dq", "dk", "dv"), (o, dq, dk, dv), want):
+        g = got.cpu().numpy()[0, 0].astype(np.float64)
+        bad = np.abs(g - ref) > 5e-5 + 5e-5 * np.abs(ref)
+        assert not bad.any(), (name, int(bad.sum()), float(np.abs(g - ref).max()))
