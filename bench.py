@@ -639,8 +639,8 @@ def attention_sweep(args) -> None:
     bf16 = peaks.get("bf16_tflops", 1590.0)
     hbm = peaks.get("hbm_gbs", 6650.0)
     ref_cache = {}
-    contraction = {"default": etb.ATTENTION_DEFAULT,
-                   "pairs16": etb.ATTENTION_BWD_PAIRS16}[args.attention_contraction]
+    contraction = {"default": etb.ATTENTION_DEFAULT, "pairs16": etb.ATTENTION_BWD_PAIRS16,
+                   "tf32": etb.ATTENTION_TF32}[args.attention_contraction]
     head_dims = args.sweep_head_dims or SWEEP["head_dims"]
     seq_lens = args.sweep_seq_lens or SWEEP["seq_lens"]
     for Dh in head_dims:
@@ -679,12 +679,17 @@ def attention_sweep(args) -> None:
             b_flop = 4.0 * B * H * T * T * Dh
             t_bytes = 4.0 * B * H * T * Dh
             pairs16 = Dh == 128 or (Dh == 64 and contraction == etb.ATTENTION_BWD_PAIRS16)
+            single = contraction == etb.ATTENTION_TF32
             line = {
                 "metric": "attn fwd/bwd % roofline", "workload": "causal attention + RoPE",
-                "batch": B, "heads": H, "seq_len": T, "head_dim": Dh, "dtype": "f32",
-                "contractions": {"forward": "3xTF32 pairs (kind::tf32)",
-                                 "backward": "binary16 pairs (kind::f16)" if pairs16
-                                 else "3xTF32 pairs (kind::tf32)"},
+                "batch": B, "heads": H, "seq_len": T, "head_dim": Dh,
+                "dtype": "tf32" if single else "f32",
+                "contractions": {
+                    "forward": "TF32 (kind::tf32, 1 product)" if single
+                    else "3xTF32 pairs (kind::tf32)",
+                    "backward": ("binary16 with per-tensor scales (kind::f16, 1 product)"
+                                 if Dh == 128 else "TF32 (kind::tf32, 1 product)") if single
+                    else "binary16 pairs (kind::f16)" if pairs16 else "3xTF32 pairs (kind::tf32)"},
                 "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
                 "fwd_tflops": round(f_flop / fwd_ms / 1e9, 2),
                 "bwd_tflops": round(b_flop / bwd_ms / 1e9, 2),
@@ -774,10 +779,12 @@ def main() -> None:
     ap.add_argument("--attention-sweep", action="store_true",
                     help="causal attention + RoPE fwd/bwd over B4 H16 Dh{64,128} T 512..16384 "
                          "(one JSON line per shape); not the default bench line")
-    ap.add_argument("--attention-contraction", choices=("default", "pairs16"), default="default",
-                    help="sweep's contraction mode: default (3xTF32 pairs; binary16 pairs for the "
-                         "head_dim-128 backward) or pairs16 (binary16 pairs in the backward at "
-                         "head_dim 64 too)")
+    ap.add_argument("--attention-contraction", choices=("default", "pairs16", "tf32"),
+                    default="default",
+                    help="sweep's contraction mode: default (f32-grade: 3xTF32 pairs; binary16 "
+                         "pairs for the head_dim-128 backward), pairs16 (binary16 pairs in the "
+                         "backward at head_dim 64 too) or tf32 (one product of TF32-grade "
+                         "operands, the sweep's TF32 mode)")
     ap.add_argument("--sweep-head-dims", type=int, nargs="*", default=None,
                     help="sweep only these head_dims")
     ap.add_argument("--sweep-seq-lens", type=int, nargs="*", default=None,

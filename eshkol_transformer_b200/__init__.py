@@ -291,6 +291,7 @@ class AttentionShape(C.Structure):
 
 ATTENTION_DEFAULT = 0      # 3xTF32 pairs; binary16 pairs for the head_dim-128 backward
 ATTENTION_BWD_PAIRS16 = 1  # binary16 pairs in the backward at head_dim 64 as well
+ATTENTION_TF32 = 2         # one product of TF32-grade operands (11 significant bits)
 
 
 def rope_tables(length: int, head_dim: int, base: float = 10000.0):

@@ -30,7 +30,8 @@ int32_t check_shape(const et_b200_attention_v1* s, et_kernel_error* e, const cha
   if (s->q_positions == nullptr || s->k_positions == nullptr)
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_NULL_ARGUMENT, op,
                      "query and key positions are required");
-  if (s->contraction != ET_B200_ATTENTION_DEFAULT && s->contraction != ET_B200_ATTENTION_BWD_PAIRS16)
+  if (s->contraction != ET_B200_ATTENTION_DEFAULT && s->contraction != ET_B200_ATTENTION_BWD_PAIRS16 &&
+      s->contraction != ET_B200_ATTENTION_TF32)
     return set_error(e, ET_KERNEL_ERROR_INVALID_ARGUMENT, ET_KERNEL_CODE_INVALID_ENUM, op,
                      "unknown attention contraction mode");
   if ((s->rope_cos == nullptr) != (s->rope_sin == nullptr))
@@ -58,6 +59,7 @@ AttnParams params_of(const et_b200_attention_v1* s, const float* q, const float*
   p.q_rope_batched = s->rope_batched ? 1 : 0;
   p.k_rope_batched = s->rope_batched ? 1 : 0;
   p.bwd_pairs16 = s->contraction == ET_B200_ATTENTION_BWD_PAIRS16 ? 1 : 0;
+  p.single = s->contraction == ET_B200_ATTENTION_TF32 ? 1 : 0;
   return p;
 }
 

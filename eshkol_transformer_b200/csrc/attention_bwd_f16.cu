@@ -43,6 +43,8 @@
 // TMEM is always released.
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "attention_tc.cuh"
 
 namespace etb {
@@ -332,7 +334,7 @@ struct Kv16Layout {
   static_assert(SMEM <= 232448, "shared memory");
 };
 
-template <int DH, bool MASKED>
+template <int DH, bool MASKED, bool THREE>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
                        const __grid_constant__ CUtensorMap kl_map,
@@ -520,8 +522,10 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         for (int k = 0; k < DH / 16; k++) {
           const uint64_t bh = kdesc16<BQ>(kt, k), bl = kdesc16<BQ>(kt + L::QT, k);
           umma_f16_ts(sd, xh + 8 * k, bh, idesc_s, k > 0 ? 1u : 0u);
-          umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
-          umma_f16(sd, kdesc16<BK>(xlo, k), bh, idesc_s, 1u);
+          if (THREE) {
+            umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
+            umma_f16(sd, kdesc16<BK>(xlo, k), bh, idesc_s, 1u);
+          }
         }
         umma_commit(B_(sdone));
         umma_commit(B_(kempty + s));
@@ -541,8 +545,10 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
           const uint32_t ah = sd + 32u * (uint32_t)(k >> 1) + 8u * (uint32_t)(k & 1);
           const uint64_t bh = mdesc16<BQ>(mt, k), bl = mdesc16<BQ>(mt + L::QT, k);
           umma_f16_ts(acc_d, ah, bh, idesc_o, (!restart || k > 0) ? 1u : 0u);
-          umma_f16_ts(acc_d, ah, bl, idesc_o, 1u);
-          umma_f16_ts(acc_d, ah + 16u, bh, idesc_o, 1u);
+          if (THREE) {
+            umma_f16_ts(acc_d, ah, bl, idesc_o, 1u);
+            umma_f16_ts(acc_d, ah + 16u, bh, idesc_o, 1u);
+          }
         }
         umma_commit(B_(gdone));
         umma_commit(B_(mempty + s));
@@ -784,7 +790,7 @@ struct Q16Layout {
   static_assert(SMEM <= 232448, "shared memory");
 };
 
-template <int DH, bool MASKED>
+template <int DH, bool MASKED, bool THREE>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
                       const __grid_constant__ CUtensorMap ql_map,
@@ -949,8 +955,10 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
           const uint32_t ah = sd + 32u * (uint32_t)(k >> 1) + 8u * (uint32_t)(k & 1);
           const uint64_t bh = mdesc16<KN>(kt, k), bl = mdesc16<KN>(kt + L::KT, k);
           umma_f16_ts(tmem + L::DQ, ah, bh, idesc_q, (i > 0 || k > 0) ? 1u : 0u);
-          umma_f16_ts(tmem + L::DQ, ah, bl, idesc_q, 1u);
-          umma_f16_ts(tmem + L::DQ, ah + 16u, bh, idesc_q, 1u);
+          if (THREE) {
+            umma_f16_ts(tmem + L::DQ, ah, bl, idesc_q, 1u);
+            umma_f16_ts(tmem + L::DQ, ah + 16u, bh, idesc_q, 1u);
+          }
         }
         umma_commit(B_(QD0 + s));
         umma_commit(B_(EMPTY0 + s));
@@ -971,8 +979,10 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
         for (int k = 0; k < DH / 16; k++) {
           const uint64_t bh = kdesc16<KN>(stg, k), bl = kdesc16<KN>(stg + L::KT, k);
           umma_f16_ts(sd, xh + 8 * k, bh, idesc_s, k > 0 ? 1u : 0u);
-          umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
-          umma_f16(sd, kdesc16<QM>(xlo, k), bh, idesc_s, 1u);
+          if (THREE) {
+            umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
+            umma_f16(sd, kdesc16<QM>(xlo, k), bh, idesc_s, 1u);
+          }
         }
         umma_commit(B_(sdone + s));
         if (!is_a) umma_commit(B_(EMPTY0 + s));
@@ -1138,24 +1148,24 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
               w.chunk_slots};
   dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);
   dim3 g2((p.Tq + QM - 1) / QM, p.Hq, p.B);
+  // instances: with / without the mask code, three products / one
+  auto go = [&](auto masked, auto three) {
+    constexpr bool M = decltype(masked)::value, T3 = decltype(three)::value;
+    cudaFuncSetAttribute(attn_bwd_kv_f16_kernel<DH, M, T3>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Kv16Layout<DH>::SMEM);
+    cudaFuncSetAttribute(attn_bwd_q_f16_kernel<DH, M, T3>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Q16Layout<DH>::SMEM);
+    attn_bwd_kv_f16_kernel<DH, M, T3><<<g1, THREADS, Kv16Layout<DH>::SMEM, stream>>>(
+        kh, kl, vh, vl, qh, ql, gh, gl, p, dk, dv, a);
+    attn_bwd_q_f16_kernel<DH, M, T3><<<g2, THREADS, Q16Layout<DH>::SMEM, stream>>>(
+        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, p, dq, a);
+  };
+  using Y = std::true_type;
+  using N = std::false_type;
   if (p.mask != nullptr) {
-    cudaFuncSetAttribute(attn_bwd_kv_f16_kernel<DH, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, Kv16Layout<DH>::SMEM);
-    cudaFuncSetAttribute(attn_bwd_q_f16_kernel<DH, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, Q16Layout<DH>::SMEM);
-    attn_bwd_kv_f16_kernel<DH, true><<<g1, THREADS, Kv16Layout<DH>::SMEM, stream>>>(
-        kh, kl, vh, vl, qh, ql, gh, gl, p, dk, dv, a);
-    attn_bwd_q_f16_kernel<DH, true><<<g2, THREADS, Q16Layout<DH>::SMEM, stream>>>(
-        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, p, dq, a);
+    if (p.single) go(Y{}, N{}); else go(Y{}, Y{});
   } else {
-    cudaFuncSetAttribute(attn_bwd_kv_f16_kernel<DH, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, Kv16Layout<DH>::SMEM);
-    cudaFuncSetAttribute(attn_bwd_q_f16_kernel<DH, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, Q16Layout<DH>::SMEM);
-    attn_bwd_kv_f16_kernel<DH, false><<<g1, THREADS, Kv16Layout<DH>::SMEM, stream>>>(
-        kh, kl, vh, vl, qh, ql, gh, gl, p, dk, dv, a);
-    attn_bwd_q_f16_kernel<DH, false><<<g2, THREADS, Q16Layout<DH>::SMEM, stream>>>(
-        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, p, dq, a);
+    if (p.single) go(N{}, N{}); else go(N{}, Y{});
   }
   count_launch(2);
   return true;

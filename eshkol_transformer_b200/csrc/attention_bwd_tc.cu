@@ -27,6 +27,8 @@
 // every query row, so P = 2^(s scale log2(e) - lse2).  All mbarrier waits
 // are bounded; a timeout raises a CTA-wide abort flag, in-flight copies and
 // MMAs are waited for (bounded) and TMEM is always released.
+#include <type_traits>
+
 #include "attention_tc.cuh"
 
 namespace etb {
@@ -160,7 +162,7 @@ struct KvLayout {
 
 // MASKED: the instance for calls with a boolean mask; the other one drops the
 // mask code (smaller unrolled loops).
-template <int DH, bool MASKED>
+template <int DH, bool MASKED, bool THREE>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
                       const __grid_constant__ CUtensorMap vh_map,
@@ -362,8 +364,10 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
         for (int k = 0; k < DH / 8; k++) {
           const uint32_t acc = k > 0 ? 1u : 0u;
           umma_tf32_ts(sd, tmem + xh + 8 * k, kslice<BQ>(bk_h, k), idesc_s, acc);
-          umma_tf32_ts(sd, tmem + xh + 8 * k, kslice<BQ>(bk_l, k), idesc_s, 1u);
-          umma_tf32(sd, kslice<BK>(xlo, k), kslice<BQ>(bk_h, k), idesc_s, 1u);
+          if (THREE) {
+            umma_tf32_ts(sd, tmem + xh + 8 * k, kslice<BQ>(bk_l, k), idesc_s, 1u);
+            umma_tf32(sd, kslice<BK>(xlo, k), kslice<BQ>(bk_h, k), idesc_s, 1u);
+          }
         }
         umma_commit(B_(sdone));
         umma_commit(B_(kempty));
@@ -381,8 +385,10 @@ attn_bwd_kv_tc_kernel(const __grid_constant__ CUtensorMap kh_map,
         for (int k = 0; k < BQ / 8; k++) {
           const uint32_t acc = (!restart || k > 0) ? 1u : 0u;
           umma_tf32_ts(acc_d, sd + 8 * k, mslice(bm_h, k), idesc_o, acc);
-          umma_tf32_ts(acc_d, sd + 8 * k, mslice(bm_l, k), idesc_o, 1u);
-          umma_tf32_ts(acc_d, lo_op + 8 * k, mslice(bm_h, k), idesc_o, 1u);
+          if (THREE) {
+            umma_tf32_ts(acc_d, sd + 8 * k, mslice(bm_l, k), idesc_o, 1u);
+            umma_tf32_ts(acc_d, lo_op + 8 * k, mslice(bm_h, k), idesc_o, 1u);
+          }
         }
         umma_commit(B_(gdone));
         umma_commit(B_(mempty));
@@ -631,7 +637,7 @@ struct QLayout {
 
 // MASKED: the instance for calls with a boolean mask; the other one drops the
 // mask code (smaller unrolled loops).
-template <int DH, bool MASKED>
+template <int DH, bool MASKED, bool THREE>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
                      const __grid_constant__ CUtensorMap ql_map,
@@ -824,8 +830,10 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
 #pragma unroll
         for (int k = 0; k < KN / 8; k++) {
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          umma_tf32_ts(dqd, sd + 8 * k, mslice(kmh, k), idesc_q, acc);
-          if (is_a) umma_tf32_ts(dqd, sd + 8 * k, mslice(kml, k), idesc_q, 1u);
+          // one product (dS hi K hi, chain A) without THREE: chain B's
+          // dQb accumulator stays unused
+          if (THREE || is_a) umma_tf32_ts(dqd, sd + 8 * k, mslice(kmh, k), idesc_q, acc);
+          if (THREE && is_a) umma_tf32_ts(dqd, sd + 8 * k, mslice(kml, k), idesc_q, 1u);
         }
         umma_commit(B_(qdone + s));
         umma_commit(B_(MN_EMPTY));
@@ -846,8 +854,10 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
         for (int k = 0; k < DH / 8; k++) {
           const uint32_t acc = k > 0 ? 1u : 0u;
           umma_tf32_ts(sd, xh + 8 * k, kslice<KN>(bh, k), idesc_s, acc);
-          umma_tf32_ts(sd, xh + 8 * k, kslice<KN>(bl, k), idesc_s, 1u);
-          umma_tf32(sd, kslice<QM>(xlo, k), kslice<KN>(bh, k), idesc_s, 1u);
+          if (THREE) {
+            umma_tf32_ts(sd, xh + 8 * k, kslice<KN>(bl, k), idesc_s, 1u);
+            umma_tf32(sd, kslice<QM>(xlo, k), kslice<KN>(bh, k), idesc_s, 1u);
+          }
         }
         umma_commit(B_(sdone + s));
         umma_commit(B_(EMPTY0 + s));
@@ -924,11 +934,13 @@ attn_bwd_q_tc_kernel(const __grid_constant__ CUtensorMap qh_map,
     ok = __all_sync(0xffffffffu, ok);
     auto load_dq = [&](int col, float (&v)[32]) {
       if (nkb > 0) {
-        float w[32];
         tmem_ld32(trow + L::DQA + col, v);
-        tmem_ld32(trow + L::DQB + col, w);
+        if (THREE) {
+          float w[32];
+          tmem_ld32(trow + L::DQB + col, w);
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = v[i] + w[i];
+          for (int i = 0; i < 32; i++) v[i] = v[i] + w[i];
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 32; i++) v[i] = 0.0f;
@@ -1019,24 +1031,24 @@ bool launch_bwd_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTen
               w.chunk_slots};
   dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);  // THREADS: 8 probability warps, MMA, loads
   dim3 g2((p.Tq + QM - 1) / QM, p.Hq, p.B);
+  // instances: with / without the mask code, three products / one
+  auto go = [&](auto masked, auto three) {
+    constexpr bool M = decltype(masked)::value, T3 = decltype(three)::value;
+    cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<DH, M, T3>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, KvLayout<DH>::SMEM);
+    cudaFuncSetAttribute(attn_bwd_q_tc_kernel<DH, M, T3>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QLayout<DH>::SMEM);
+    attn_bwd_kv_tc_kernel<DH, M, T3><<<g1, THREADS, KvLayout<DH>::SMEM, stream>>>(
+        kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
+    attn_bwd_q_tc_kernel<DH, M, T3><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(
+        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml, p, dq, a);
+  };
+  using Y = std::true_type;
+  using N = std::false_type;
   if (p.mask != nullptr) {
-    cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<DH, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, KvLayout<DH>::SMEM);
-    cudaFuncSetAttribute(attn_bwd_q_tc_kernel<DH, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, QLayout<DH>::SMEM);
-    attn_bwd_kv_tc_kernel<DH, true><<<g1, THREADS, KvLayout<DH>::SMEM, stream>>>(
-        kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
-    attn_bwd_q_tc_kernel<DH, true><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(
-        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml, p, dq, a);
+    if (p.single) go(Y{}, N{}); else go(Y{}, Y{});
   } else {
-    cudaFuncSetAttribute(attn_bwd_kv_tc_kernel<DH, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, KvLayout<DH>::SMEM);
-    cudaFuncSetAttribute(attn_bwd_q_tc_kernel<DH, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, QLayout<DH>::SMEM);
-    attn_bwd_kv_tc_kernel<DH, false><<<g1, THREADS, KvLayout<DH>::SMEM, stream>>>(
-        kh, vh, kl, vl, qkh, qkl, gkh, gkl, qmh, qml, gmh, gml, p, dk, dv, a);
-    attn_bwd_q_tc_kernel<DH, false><<<g2, THREADS, QLayout<DH>::SMEM, stream>>>(
-        qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl, kmh, kml, p, dq, a);
+    if (p.single) go(N{}, N{}); else go(N{}, Y{});
   }
   count_launch(2);
   return true;

@@ -28,6 +28,8 @@
 // P V completes) only on those rare jumps.  All mbarrier waits are bounded;
 // a timeout raises a CTA-wide abort flag, in-flight copies and MMAs are
 // waited for (bounded) and TMEM is always released.
+#include <type_traits>
+
 #include "attention_tc.cuh"
 
 namespace etb {
@@ -129,7 +131,7 @@ __device__ __forceinline__ int count_below(const int64_t* a, int n, int64_t x) {
 
 // MASKED: the instance for calls with a boolean mask; the other one drops the
 // mask code (smaller unrolled loops).
-template <int DH, bool MASKED>
+template <int DH, bool MASKED, bool THREE>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_constant__ CUtensorMap ql_map,
                    const __grid_constant__ CUtensorMap kh_map, const __grid_constant__ CUtensorMap kl_map,
@@ -286,8 +288,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
         for (int k = 0; k < DH / 8; k++) {
           const uint32_t acc = k > 0 ? 1u : 0u;
           umma_tf32_ts(d, tmem + L::QH + 8 * k, kslice<KN>(kh, k), idesc, acc);
-          umma_tf32_ts(d, tmem + L::QH + 8 * k, kslice<KN>(kl, k), idesc, 1u);
-          umma_tf32_ts(d, tmem + L::QL + 8 * k, kslice<KN>(kh, k), idesc, 1u);
+          if (THREE) {
+            umma_tf32_ts(d, tmem + L::QH + 8 * k, kslice<KN>(kl, k), idesc, 1u);
+            umma_tf32_ts(d, tmem + L::QL + 8 * k, kslice<KN>(kh, k), idesc, 1u);
+          }
         }
         umma_commit(SFULL + 8 * sl);
         issued++;
@@ -314,8 +318,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap qh_map, const __grid_cons
         for (int k = 0; k < KN / 8; k++) {
           const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
           umma_tf32_ts(tmem + L::O, ph + 8 * k, mslice(vh, k), idesc, acc);
-          umma_tf32_ts(tmem + L::O, ph + 8 * k, mslice(vl, k), idesc, 1u);
-          umma_tf32_ts(tmem + L::O, pl + 8 * k, mslice(vh, k), idesc, 1u);
+          if (THREE) {
+            umma_tf32_ts(tmem + L::O, ph + 8 * k, mslice(vl, k), idesc, 1u);
+            umma_tf32_ts(tmem + L::O, pl + 8 * k, mslice(vh, k), idesc, 1u);
+          }
         }
         umma_commit(PVD + 8 * sl);
         umma_commit(EMPTY + 8 * st);
@@ -509,17 +515,22 @@ bool launch_fwd_tc(const AttnParams& p, AttnOut o, float* m, float* l, cudaStrea
     return false;
   if (!p.qkv_ready) attention_prepare_qkv(p, w, stream);
   TcFwdArgs a{device_error_word()};
-  cudaFuncSetAttribute(attn_fwd_tc_kernel<DH, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       L::SMEM);
-  cudaFuncSetAttribute(attn_fwd_tc_kernel<DH, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       L::SMEM);
   dim3 grid((p.Tq + QM - 1) / QM, p.Hq, p.B);
-  if (p.mask != nullptr)
-    attn_fwd_tc_kernel<DH, true><<<grid, THREADS, L::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl,
-                                                                    p, o, m, l, a);
-  else
-    attn_fwd_tc_kernel<DH, false><<<grid, THREADS, L::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl,
-                                                                     p, o, m, l, a);
+  // instances: with / without the mask code, three products / one
+  auto go = [&](auto masked, auto three) {
+    constexpr bool M = decltype(masked)::value, T3 = decltype(three)::value;
+    cudaFuncSetAttribute(attn_fwd_tc_kernel<DH, M, T3>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    attn_fwd_tc_kernel<DH, M, T3><<<grid, THREADS, L::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl,
+                                                                      p, o, m, l, a);
+  };
+  using Y = std::true_type;
+  using N = std::false_type;
+  if (p.mask != nullptr) {
+    if (p.single) go(Y{}, N{}); else go(Y{}, Y{});
+  } else {
+    if (p.single) go(N{}, N{}); else go(N{}, Y{});
+  }
   count_launch();
   return true;
 }

@@ -245,6 +245,10 @@ struct AttnParams {
   // (attention_bwd_f16.cu) wherever that kernel exists (head_dim 64, 128);
   // otherwise only head_dim 128 uses it and 32 / 64 take the 3xTF32 kernels.
   int bwd_pairs16;
+  // single: one product of the hi parts per contraction (TF32-grade: 11
+  // significant bits per operand element) instead of the three of the
+  // f32-grade pairs
+  int single;
 };
 // Where the GEMM producing dO = dY Wo (rows [B*T, H*Dh], token-major) writes
 // the attention backward's inputs: dO split into TF32 hi / lo head-major

@@ -111,13 +111,21 @@ typedef struct et_b200_attention_v1 {
   int32_t rope_batched;
   int32_t contraction; /* ET_B200_ATTENTION_* (0 = the default) */
 } et_b200_attention_v1;
-/* Contraction modes, both f32-grade (three products of operand pairs, about
- * 22 significant bits per operand element):
+/* Contraction modes.  f32-grade (three products of operand pairs, about 22
+ * significant bits per operand element):
  * ET_B200_ATTENTION_DEFAULT: 3xTF32 pairs, except the head_dim-128 backward,
  *   which carries binary16 pairs with per-tensor power-of-two scales;
  * ET_B200_ATTENTION_BWD_PAIRS16: binary16 pairs in the backward at head_dim
- *   64 as well. */
-enum { ET_B200_ATTENTION_DEFAULT = 0, ET_B200_ATTENTION_BWD_PAIRS16 = 1 };
+ *   64 as well.
+ * TF32-grade (one product of the hi parts, 11 significant bits per operand
+ * element, the reference sweep's "TF32" mode):
+ * ET_B200_ATTENTION_TF32: TF32 operands (round to nearest), binary16 ones
+ *   with per-tensor scales (the same 11 bits) in the head_dim-128 backward. */
+enum {
+  ET_B200_ATTENTION_DEFAULT = 0,
+  ET_B200_ATTENTION_BWD_PAIRS16 = 1,
+  ET_B200_ATTENTION_TF32 = 2
+};
 /* Bytes of the workspace both calls take (256-byte aligned). */
 size_t et_b200_attention_workspace_bytes_v1(const et_b200_attention_v1 *shape);
 /* Host-side RoPE tables [len, head_dim/2] the way the reference builds its

@@ -157,3 +157,19 @@ def test_long_sequence_slice_vs_float64(lib, cuda, Dh, contraction):
         g = got.cpu().numpy()[0, 0].astype(np.float64)
         bad = np.abs(g - ref) > 5e-5 + 5e-5 * np.abs(ref)
         assert not bad.any(), (name, int(bad.sum()), float(np.abs(g - ref).max()))
+
+
+# TF32-grade mode: one product of operands rounded to 11 significant bits;
+# the bar is the TF32 LM-gradient bar (normwise per tensor).
+TF32_TOL = 5e-3
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,Dh", [(2, 4, 4, 256, 64), (2, 4, 2, 200, 32),
+                                           (1, 2, 2, 384, 128), (1, 4, 2, 300, 128)])
+def test_tf32_mode_vs_oracle(lib, cuda, B, Hq, Hkv, T, Dh):
+    q, k, v, do, o, dq, dk, dv = _run(B, Hq, Hkv, T, Dh, 31 + T, True, etb.ATTENTION_TF32)
+    ro, rdq, rdk, rdv = _oracle(q, k, v, do)
+    for name, got, want in (("o", o, ro), ("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
+        assert err <= TF32_TOL, (name, err)
+        assert err > 1e-5, (name, err)  # one product ran: above the f32-grade ~1e-6
