@@ -678,7 +678,8 @@ def attention_sweep(args) -> None:
             f_flop = 2.0 * B * H * T * T * Dh
             b_flop = 4.0 * B * H * T * T * Dh
             t_bytes = 4.0 * B * H * T * Dh
-            pairs16 = Dh == 128 or (Dh == 64 and contraction == etb.ATTENTION_BWD_PAIRS16)
+            pairs16 = Dh == 128 or (Dh == 64 and (contraction == etb.ATTENTION_BWD_PAIRS16
+                                                  or T * T >= 2048 * 2048))
             single = contraction == etb.ATTENTION_TF32
             line = {
                 "metric": "attn fwd/bwd % roofline", "workload": "causal attention + RoPE",
