@@ -1061,11 +1061,7 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
                            AttnOut dk, AttnOut dv, cudaStream_t stream) {
   if (p.ws == nullptr || encode_fn() == nullptr || p.Tq == 0 || p.Tk == 0) return false;
   if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
-  // binary16 pairs: always at head_dim 128 (the 3xTF32 tiles do not fit);
-  // at head_dim 64 on request, and from Tq Tk = 2,048^2 up, where they
-  // measured faster (their prepasses cost more than they save below)
-  const bool long_seq = (int64_t)p.Tq * p.Tk >= (int64_t)2048 * 2048;
-  if ((p.Dh == 128 || (p.Dh == 64 && (p.bwd_pairs16 || long_seq))) && !p.grad_ready)
+  if (attention_uses_pairs16(p) && !p.grad_ready)
     return attention_backward_f16(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream);
   switch (p.Dh) {
     case 32:

@@ -604,6 +604,10 @@ bool attention_forward_tc(const AttnParams& p, AttnOut o, float* row_max, float*
                           cudaStream_t stream) {
   if (p.ws == nullptr || encode_fn() == nullptr) return false;
   if (reinterpret_cast<uintptr_t>(p.ws) & 15) return false;
+  // binary16 pairs where the backward takes them too (it then reuses the
+  // pairs), unless a producer already wrote the 3xTF32 operands
+  if (!p.qkv_ready && attention_uses_pairs16(p))
+    return attention_forward_f16(p, o, row_max, row_sum, stream);
   switch (p.Dh) {
     case 32: return launch_fwd_tc<32>(p, o, row_max, row_sum, stream);
     case 64: return launch_fwd_tc<64>(p, o, row_max, row_sum, stream);

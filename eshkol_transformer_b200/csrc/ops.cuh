@@ -314,6 +314,16 @@ bool attention_backward(const AttnParams& p, AttnTensor o, const float* o_lo, At
 bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
                            const float* row_max, const float* row_sum, float* delta, AttnOut dq,
                            AttnOut dk, AttnOut dv, cudaStream_t stream);
+// Whether attention carries binary16 operand pairs for p: always at
+// head_dim 128, at head_dim 64 with bwd_pairs16 or from Tq Tk = 2,048^2 up
+// (forward and backward decide alike, so a backward reuses its forward's
+// pairs).
+bool attention_uses_pairs16(const AttnParams& p);
+// Binary16 pairs of RoPE'd Q, K and V and their maxima into the workspace.
+void attention_prepare_pairs16(const AttnParams& p, cudaStream_t stream);
+// The binary16-pair tensor-core forward (head_dim 64 and 128).
+bool attention_forward_f16(const AttnParams& p, AttnOut o, float* row_max, float* row_sum,
+                           cudaStream_t stream);
 // The binary16-pair tensor-core backward (head_dim 64 and 128, dO from
 // `dout`: not with grad_ready); false when it cannot run this call.
 bool attention_backward_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTensor dout,
