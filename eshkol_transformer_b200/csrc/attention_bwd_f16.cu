@@ -61,37 +61,53 @@ __device__ __forceinline__ float lse2_of(float m, float l) {
   return l > 0.0f ? (m + logf(l)) * kLog2e : INFINITY;
 }
 
-// One warp per query row (b, hq, tq), row = (b*Hq + hq)*Tq + tq: delta in the
-// SIMT kernel's order (lane-strided fma, warp tree), lse2, and max |dO| of the
-// row into amax[3].
+// Warps take query rows (b, hq, tq), row = (b*Hq + hq)*Tq + tq, in a
+// grid-stride loop; each lane reads VEC consecutive elements per step:
+// delta = rowsum(dO (o + o_lo)) (lane partial sums, warp tree), lse2, and
+// max |dO| over every row the warp saw into amax[3] (one atomic per warp).
+template <int VEC, bool VLOAD>
 __global__ void attn16_stats_kernel(AttnParams p, AttnTensor o, const float* __restrict__ o_lo,
                                     AttnTensor dout, const float* __restrict__ row_max,
                                     const float* __restrict__ row_sum, float* __restrict__ delta,
                                     float* __restrict__ lse2, unsigned* amax) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int64_t rows = (int64_t)p.B * p.Hq * p.Tq;
-  if (row >= rows) return;
-  const int tq = (int)(row % p.Tq);
-  const int hq = (int)((row / p.Tq) % p.Hq);
-  const int b = (int)(row / ((int64_t)p.Tq * p.Hq));
-  const int64_t ooff = b * o.sb + hq * o.sh + (int64_t)tq * o.st;
-  const float* orow = o.ptr + ooff;
-  const float* lrow = o_lo ? o_lo + ooff : nullptr;
-  const float* grow = dout.ptr + b * dout.sb + hq * dout.sh + (int64_t)tq * dout.st;
-  float s = 0.0f, m = 0.0f;
-  for (int j = lane; j < p.Dh; j += 32) {
-    const float g = grow[j];
-    s = fmaf(g, lrow ? orow[j] + lrow[j] : orow[j], s);
-    m = fmaxf(m, fabsf(g));
-    if (g != g) m = g;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  float m = 0.0f;
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); row < rows;
+       row += warps) {
+    const int tq = (int)(row % p.Tq);
+    const int hq = (int)((row / p.Tq) % p.Hq);
+    const int b = (int)(row / ((int64_t)p.Tq * p.Hq));
+    const int64_t ooff = b * o.sb + hq * o.sh + (int64_t)tq * o.st;
+    const float* orow = o.ptr + ooff;
+    const float* lrow = o_lo ? o_lo + ooff : nullptr;
+    const float* grow = dout.ptr + b * dout.sb + hq * dout.sh + (int64_t)tq * dout.st;
+    float s = 0.0f;
+    for (int j = VEC * lane; j < p.Dh; j += 32 * VEC) {
+      float g[VEC], x[VEC];
+      load_vec<VEC, VLOAD>(grow + j, g);
+      load_vec<VEC, VLOAD>(orow + j, x);
+      if (lrow) {
+        float y[VEC];
+        load_vec<VEC, VLOAD>(lrow + j, y);
+#pragma unroll
+        for (int u = 0; u < VEC; u++) x[u] = x[u] + y[u];
+      }
+#pragma unroll
+      for (int u = 0; u < VEC; u++) {
+        s = fmaf(g[u], x[u], s);
+        m = fmaxf(m, fabsf(g[u]));
+        if (g[u] != g[u]) m = g[u];
+      }
+    }
+    s = warp_sum(s);
+    if (lane == 0) {
+      delta[row] = s;
+      lse2[row] = lse2_of(row_max[row], row_sum[row]);
+    }
   }
-  s = warp_sum(s);
   amax_record_warp(amax + 3, m);
-  if (lane == 0) {
-    delta[row] = s;
-    lse2[row] = lse2_of(row_max[row], row_sum[row]);
-  }
 }
 
 // max |hi + lo| of the workspace's Q, K, V pairs (blockIdx.y = 0, 1, 2) into
@@ -137,24 +153,31 @@ __global__ void attn16_split_qkv_kernel(const float* __restrict__ qh, const floa
 }
 
 // Binary16 pair of dO, head-major [B, Hq, Tq, Dh], from the strided tensor:
-// one warp per row.
+// warps take rows in a grid-stride loop, each lane VEC elements per step.
+template <int VEC, bool VLOAD>
 __global__ void attn16_split_dout_kernel(AttnParams p, AttnTensor dout, uint16_t* g16h,
                                          uint16_t* g16l, const unsigned* amax) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int64_t rows = (int64_t)p.B * p.Hq * p.Tq;
-  if (row >= rows) return;
-  const int tq = (int)(row % p.Tq);
-  const int hq = (int)((row / p.Tq) % p.Hq);
-  const int b = (int)(row / ((int64_t)p.Tq * p.Hq));
-  const float* grow = dout.ptr + b * dout.sb + hq * dout.sh + (int64_t)tq * dout.st;
-  const float s = exp2_int(pair_exponent(__uint_as_float(amax[3])));
-  for (int j = 2 * lane; j < p.Dh; j += 64) {
-    const __half2 h = __floats2half2_rn(grow[j] * s, grow[j + 1] * s);
-    const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(grow[j] * s - hf.x, grow[j + 1] * s - hf.y);
-    *reinterpret_cast<__half2*>(g16h + row * p.Dh + j) = h;
-    *reinterpret_cast<__half2*>(g16l + row * p.Dh + j) = l;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const float sc = exp2_int(pair_exponent(__uint_as_float(amax[3])));
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); row < rows;
+       row += warps) {
+    const int tq = (int)(row % p.Tq);
+    const int hq = (int)((row / p.Tq) % p.Hq);
+    const int b = (int)(row / ((int64_t)p.Tq * p.Hq));
+    const float* grow = dout.ptr + b * dout.sb + hq * dout.sh + (int64_t)tq * dout.st;
+    for (int j = VEC * lane; j < p.Dh; j += 32 * VEC) {
+      float g[VEC];
+      load_vec<VEC, VLOAD>(grow + j, g);
+#pragma unroll
+      for (int u = 0; u < VEC; u += 2) {
+        float hi, lo;
+        pair2(g[u] * sc, g[u + 1] * sc, hi, lo);
+        *reinterpret_cast<uint32_t*>(g16h + row * p.Dh + j + u) = __float_as_uint(hi);
+        *reinterpret_cast<uint32_t*>(g16l + row * p.Dh + j + u) = __float_as_uint(lo);
+      }
+    }
   }
 }
 
@@ -1045,10 +1068,24 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
   }
   // row statistics and max |dO|, then dO's pair
   cudaMemsetAsync(w.amax16 + 3, 0, sizeof(unsigned), stream);
-  attn16_stats_kernel<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(
-      p, o, o_lo, dout, row_max, row_sum, delta, w.lse2, w.amax16);
-  attn16_split_dout_kernel<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(p, dout, w.g16h,
-                                                                          w.g16l, w.amax16);
+  {
+    const int64_t want = (qrows + 7) / 8, cap = (int64_t)sm_count() * 16;
+    const unsigned rg = (unsigned)(want < cap ? want : cap);
+    auto go = [&](auto v, auto vl) {
+      constexpr int V = decltype(v)::value;
+      constexpr bool VL = decltype(vl)::value;
+      attn16_stats_kernel<V, VL><<<rg, 256, 0, stream>>>(p, o, o_lo, dout, row_max, row_sum,
+                                                         delta, w.lse2, w.amax16);
+      attn16_split_dout_kernel<V, VL><<<rg, 256, 0, stream>>>(p, dout, w.g16h, w.g16l, w.amax16);
+    };
+    // read width by alignment
+    if (rows_vec4(o, o_lo) && rows_vec4(dout, nullptr))
+      go(std::integral_constant<int, 4>{}, std::true_type{});
+    else if (rows_vec2(o, o_lo) && rows_vec2(dout, nullptr))
+      go(std::integral_constant<int, 2>{}, std::true_type{});
+    else
+      go(std::integral_constant<int, 2>{}, std::false_type{});
+  }
   count_launch(2);
   cudaMemsetAsync(w.slot_flags, 0, (size_t)w.chunk_slots * sizeof(int), stream);
   Bwd16Args a{w.lse2, delta, w.amax16, device_error_word(), w.chunks, w.slot_flags,

@@ -42,34 +42,43 @@ constexpr float kRescale = 8.0f;  // log2 of the largest P the stale maximum all
 // ---- operand preparation ---------------------------------------------------------
 
 // max |x| of the raw Q, K, V (blockIdx.y = 0, 1, 2; strided [B, H, T, Dh])
-// into amax[blockIdx.y].  RoPE rotates pairs, so a rotated element is at most
-// sqrt(2) max |x|: with 2^e max |x| below 2^15 the pairs stay under 65,504.
+// into amax[blockIdx.y]: warps take rows in a grid-stride loop, each lane
+// VEC elements per step, one atomic per warp.  RoPE rotates pairs, so a
+// rotated element is at most sqrt(2) max |x|: with 2^e max |x| below 2^15
+// the pairs stay under 65,504.
+template <int VEC, bool VLOAD>
 __global__ void attn16_amax_raw_kernel(AttnParams p, unsigned* amax) {
   const int t = blockIdx.y;
   const AttnTensor& x = t == 0 ? p.q : t == 1 ? p.k : p.v;
   const int H = t == 0 ? p.Hq : p.Hkv, T = t == 0 ? p.Tq : p.Tk;
   const int64_t rows = (int64_t)p.B * H * T;
-  const int per_row = p.Dh / 2;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const int lane = threadIdx.x & 31;
   float m = 0.0f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * per_row;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / per_row;
-    const int j = 2 * (int)(i - row * per_row);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); row < rows;
+       row += warps) {
     const int tt = (int)(row % T);
     const int h = (int)((row / T) % H);
     const int b = (int)(row / ((int64_t)T * H));
-    const float* s = x.ptr + b * x.sb + h * x.sh + (int64_t)tt * x.st + j;
-    const float a0 = s[0], a1 = s[1];
-    m = fmaxf(m, fmaxf(fabsf(a0), fabsf(a1)));
-    if (a0 != a0) m = a0;
-    if (a1 != a1) m = a1;
+    const float* s = x.ptr + b * x.sb + h * x.sh + (int64_t)tt * x.st;
+    for (int j = VEC * lane; j < p.Dh; j += 32 * VEC) {
+      float v[VEC];
+      load_vec<VEC, VLOAD>(s + j, v);
+#pragma unroll
+      for (int u = 0; u < VEC; u++) {
+        m = fmaxf(m, fabsf(v[u]));
+        if (v[u] != v[u]) m = v[u];
+      }
+    }
   }
   amax_record_warp(amax + t, m);
 }
 
 // The binary16 pairs of RoPE'd Q, K and plain V (blockIdx.y = 0, 1, 2),
 // head-major [B, H, T, Dh]: the rotation in the reference's rounding order
-// (attention_tc.cu's prepass), then x 2^e split into hi and lo.
+// (attention_tc.cu's prepass), then x 2^e split into hi and lo; warps take
+// rows in a grid-stride loop, each lane VEC elements (VEC / 2 pairs) per step.
+template <int VEC, bool VLOAD>
 __global__ void attn16_split_rope_kernel(AttnParams p, uint16_t* q16h, uint16_t* q16l,
                                          uint16_t* k16h, uint16_t* k16l, uint16_t* v16h,
                                          uint16_t* v16l, const unsigned* amax) {
@@ -83,28 +92,37 @@ __global__ void attn16_split_rope_kernel(AttnParams p, uint16_t* q16h, uint16_t*
   uint16_t* ol = t == 0 ? q16l : t == 1 ? k16l : v16l;
   const float sc = exp2_int(pair_exponent(__uint_as_float(amax[t])));
   const int half = p.Dh / 2;
-  const int64_t total = (int64_t)p.B * H * T * half;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int pr = (int)(i % half);
-    const int64_t row = i / half;  // (b*H + h)*T + t
+  const int64_t rows = (int64_t)p.B * H * T;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); row < rows;
+       row += warps) {
     const int tt = (int)(row % T);
     const int h = (int)((row / T) % H);
     const int b = (int)(row / ((int64_t)T * H));
-    const float* s = x.ptr + b * x.sb + h * x.sh + (int64_t)tt * x.st + 2 * pr;
-    float x0 = s[0], x1 = s[1];
-    if (ct != nullptr) {
-      const int64_t ti = (int64_t)(batched ? b * T + tt : tt) * half + pr;
-      const float c = ct[ti], sn = st[ti];
-      const float aa = rn_mul(x0, c), bb = rn_mul(x1, sn), cc = rn_mul(x0, sn), dd = rn_mul(x1, c);
-      x0 = rn_sub(aa, bb);
-      x1 = rn_add(cc, dd);
+    const float* s = x.ptr + b * x.sb + h * x.sh + (int64_t)tt * x.st;
+    const int64_t trow = (int64_t)(batched ? b * T + tt : tt) * half;
+    for (int j = VEC * lane; j < p.Dh; j += 32 * VEC) {
+      float v[VEC];
+      load_vec<VEC, VLOAD>(s + j, v);
+#pragma unroll
+      for (int u = 0; u < VEC; u += 2) {
+        float x0 = v[u], x1 = v[u + 1];
+        if (ct != nullptr) {
+          const int64_t ti = trow + (j + u) / 2;
+          const float c = ct[ti], sn = st[ti];
+          const float aa = rn_mul(x0, c), bb = rn_mul(x1, sn), cc = rn_mul(x0, sn),
+                      dd = rn_mul(x1, c);
+          x0 = rn_sub(aa, bb);
+          x1 = rn_add(cc, dd);
+        }
+        float hi, lo;
+        pair2(x0 * sc, x1 * sc, hi, lo);
+        const int64_t o = row * p.Dh + j + u;
+        *reinterpret_cast<uint32_t*>(oh + o) = __float_as_uint(hi);
+        *reinterpret_cast<uint32_t*>(ol + o) = __float_as_uint(lo);
+      }
     }
-    float hi, lo;
-    pair2(x0 * sc, x1 * sc, hi, lo);
-    const int64_t o = row * p.Dh + 2 * pr;
-    *reinterpret_cast<uint32_t*>(oh + o) = __float_as_uint(hi);
-    *reinterpret_cast<uint32_t*>(ol + o) = __float_as_uint(lo);
   }
 }
 
@@ -553,13 +571,23 @@ bool attention_uses_pairs16(const AttnParams& p) {
 void attention_prepare_pairs16(const AttnParams& p, cudaStream_t stream) {
   const AttnWs w = attn_ws(p);
   cudaMemsetAsync(w.amax16, 0, 3 * sizeof(unsigned), stream);
-  const int64_t most = (int64_t)p.B * (p.Hq > p.Hkv ? p.Hq : p.Hkv) *
-                       (p.Tq > p.Tk ? p.Tq : p.Tk) * (p.Dh / 2);
-  const int64_t want = (most + 255) / 256, cap = (int64_t)sm_count() * 8;
+  const int64_t most = (int64_t)p.B * (p.Hq > p.Hkv ? p.Hq : p.Hkv) * (p.Tq > p.Tk ? p.Tq : p.Tk);
+  const int64_t want = (most + 7) / 8, cap = (int64_t)sm_count() * 16;
   const dim3 g((unsigned)(want < cap ? want : cap), 3);
-  attn16_amax_raw_kernel<<<g, 256, 0, stream>>>(p, w.amax16);
-  attn16_split_rope_kernel<<<g, 256, 0, stream>>>(p, w.q16h, w.q16l, w.k16h, w.k16l, w.v16h,
-                                                  w.v16l, w.amax16);
+  // read width by alignment (a pair's two floats are always adjacent)
+  const int vec = rows_vec4(p.q, nullptr) && rows_vec4(p.k, nullptr) && rows_vec4(p.v, nullptr) ? 4
+                  : rows_vec2(p.q, nullptr) && rows_vec2(p.k, nullptr) && rows_vec2(p.v, nullptr) ? 2
+                                                                                                  : 0;
+  auto go = [&](auto v, auto vl) {
+    constexpr int V = decltype(v)::value;
+    constexpr bool VL = decltype(vl)::value;
+    attn16_amax_raw_kernel<V, VL><<<g, 256, 0, stream>>>(p, w.amax16);
+    attn16_split_rope_kernel<V, VL><<<g, 256, 0, stream>>>(p, w.q16h, w.q16l, w.k16h, w.k16l,
+                                                           w.v16h, w.v16l, w.amax16);
+  };
+  if (vec == 4) go(std::integral_constant<int, 4>{}, std::true_type{});
+  else if (vec == 2) go(std::integral_constant<int, 2>{}, std::true_type{});
+  else go(std::integral_constant<int, 2>{}, std::false_type{});
   count_launch(2);
 }
 

@@ -113,5 +113,41 @@ __device__ __forceinline__ Exps exps_of(const unsigned* amax, int dh) {
   return x;
 }
 
+// VEC consecutive floats: with VLOAD one 16-byte (VEC 4) or 8-byte (VEC 2)
+// load, the address aligned to it; without, one float at a time.
+template <int VEC, bool VLOAD = true>
+__device__ __forceinline__ void load_vec(const float* src, float (&v)[VEC]) {
+  if constexpr (!VLOAD) {
+#pragma unroll
+    for (int u = 0; u < VEC; u++) v[u] = src[u];
+  } else if constexpr (VEC == 4) {
+    const float4 f = *reinterpret_cast<const float4*>(src);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else if constexpr (VEC == 2) {
+    const float2 f = *reinterpret_cast<const float2*>(src);
+    v[0] = f.x; v[1] = f.y;
+  } else {
+#pragma unroll
+    for (int u = 0; u < VEC; u++) v[u] = src[u];
+  }
+}
+
 }  // namespace f16att
+
+// Whether rows of t (and of `lo`, same strides) can be read as float4: the
+// base and every stride 16-byte aligned (head_dim a multiple of 4 is implied
+// by the binary16 kernels' 64 / 128).
+inline bool rows_vec4(const AttnTensor& t, const float* lo) {
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(t.ptr) | reinterpret_cast<uintptr_t>(lo) |
+                         (uintptr_t)(t.sb * 4) | (uintptr_t)(t.sh * 4) | (uintptr_t)(t.st * 4);
+  return (bits & 15) == 0;
+}
+// The same for 8-byte (float2) reads; otherwise the kernels read one float
+// at a time.
+inline bool rows_vec2(const AttnTensor& t, const float* lo) {
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(t.ptr) | reinterpret_cast<uintptr_t>(lo) |
+                         (uintptr_t)(t.sb * 4) | (uintptr_t)(t.sh * 4) | (uintptr_t)(t.st * 4);
+  return (bits & 7) == 0;
+}
+
 }  // namespace etb
