@@ -679,7 +679,7 @@ def attention_sweep(args) -> None:
             b_flop = 4.0 * B * H * T * T * Dh
             t_bytes = 4.0 * B * H * T * Dh
             pairs16 = Dh == 128 or (Dh == 64 and (contraction == etb.ATTENTION_BWD_PAIRS16
-                                                  or T * T >= 2048 * 2048))
+                                                  or T * T >= 1024 * 1024))
             single = contraction == etb.ATTENTION_TF32
             line = {
                 "metric": "attn fwd/bwd % roofline", "workload": "causal attention + RoPE",

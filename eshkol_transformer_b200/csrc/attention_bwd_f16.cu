@@ -192,12 +192,12 @@ struct Bwd16Args {
 
 // dK and dV accumulate over up to G Tq queries; the tensor pipe's f32
 // accumulation truncates, so a CTA whose key tile sees more than
-// kChunkBlocks query blocks (2,048 queries) sums its accumulators in chunks:
+// kChunkQueries queries sums its accumulators in chunks:
 // at every chunk boundary the probability warps add the finished chunk into
 // the CTA's slot in global memory (f32), and the next chunk restarts the
 // TMEM accumulation.  (Measured at T = 16,384: one accumulator per key tile
 // left dK / dV 1e-4 from float64, outside the A2 tolerance.)
-constexpr int kChunkBlocks = 32;
+constexpr int kChunkQueries = 2048;
 
 // A free chunk slot for this CTA (thread 0, after its TMEM allocation):
 // bounded scan from a CTA-dependent start; -1 (and the error word) if none
@@ -232,10 +232,12 @@ constexpr int MMA_A = 8, MMA_B = 9, LOADER = 10;
 // ---- dK / dV ----------------------------------------------------------------------
 
 constexpr int BK = 128;  // keys per CTA (TMEM lanes)
-constexpr int BQ = 64;   // queries per block
 
 template <int DH>
 struct Kv16Layout {
+  // queries per block: 128 at head_dim 64 (S^T and dP^T at N = 128, the
+  // tensor pipe's full rate; TMEM has the room), 64 at head_dim 128
+  static constexpr int BQ = DH == 64 ? 128 : 64;
   static constexpr int QT = BQ * DH * 2;  // [BQ, DH] binary16 tile
   static constexpr int KT = BK * DH * 2;  // [BK, DH] binary16 tile
   // K lo, V lo (shared-memory A operands); two stages of the Q pair and of the
@@ -269,6 +271,10 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
                        AttnOut dv, Bwd16Args a) {
   if constexpr (!MASKED) p.mask = nullptr;
   using L = Kv16Layout<DH>;
+  constexpr int BQ = L::BQ;
+  constexpr int NQC = BQ / 64;  // 32-query chunks per probability thread
+  // a CTA sums dK / dV in f32 chunks of 2,048 queries
+  constexpr int kChunkBlocks = kChunkQueries / BQ;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   __shared__ __align__(16) float lse_s[2 * BQ], dlt_s[2 * BQ];  // per-block statistics ring
@@ -492,7 +498,9 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     const float c2 = p.scale * kLog2e * exp2_int(-(ex.q + ex.k));
     const float u_dp = exp2_int(-(ex.v + ex.g));
     const float s_p = exp2_int(kPExp), s_ds = exp2_int(ex.ds);
-    const int cb = 32 * khalf;  // this thread's first query column of the block
+    // this thread's queries of each block: NQC chunks of 32 from cb; chunk c's
+    // P and dS pairs go over its own 32 S^T / dP^T columns (hi, then lo)
+    const int cb = 32 * NQC * khalf;
     const int slot = *slot_s;
     // this thread's row of the chunk sums: dK (warps 0-3) or dV (warps 4-7)
     float* crow = slot >= 0 ? a.chunks + (size_t)slot * kBwdChunkFloats +
@@ -503,15 +511,19 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
       const int s = j & 1;
       const uint32_t par = (uint32_t)(j & 1), spar = (uint32_t)((j >> 1) & 1);
       const int q0 = q0_of(j);
-      uint8_t keep[32];
-      if (p.mask != nullptr) {  // issued ahead of the waits; clamped indices stay in bounds
-        const int tkc = min(tk, p.Tk - 1);
+      // mask bytes of this thread's first 32 queries, issued ahead of the
+      // waits (later chunks load theirs in the chunk loop); clamped indices
+      // stay in bounds
+      const int tkc = min(tk, p.Tk - 1);
+      auto mask_chunk = [&](int c, uint8_t (&keep)[32]) {
 #pragma unroll
         for (int i = 0; i < 32; i++) {
-          const int q = min(q0 + cb + i, p.Tq - 1);
+          const int q = min(q0 + cb + 32 * c + i, p.Tq - 1);
           keep[i] = p.mask[((int64_t)b * p.Tq + q) * p.Tk + tkc];
         }
-      }
+      };
+      uint8_t keep[32];
+      if (p.mask != nullptr) mask_chunk(0, keep);
       ok = role_wait(B_(ST_FULL0 + s), spar, a.error, abort);
       if (ok) ok = role_wait(B_(SA_DONE), par, a.error, abort);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld/st are warp-collective
@@ -519,39 +531,45 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
       tc_fence_after();
       const bool full_block =
           p.mask == nullptr && keys_full && q0 + BQ <= p.Tq && qp_s[s * BQ] >= kpos_last;
-      float pv[32];
-      {
+      // queries of the block see this key from the first whose position
+      // reaches it, up to the last query of the sequence
+      const int first = full_block ? 0 : count_below(qp_s + s * BQ, BQ, kpos_row) - cb;
+      const int last = full_block ? 32 * NQC : p.Tq - q0 - cb;
+      float pv[32 * NQC];
+#pragma unroll
+      for (int c = 0; c < NQC; c++) {
         float sv[32], ls[32];
-        tmem_ld32(trow + L::ST + cb, sv);
-        const float4* l4 = reinterpret_cast<const float4*>(lse_s + s * BQ + cb);
+        tmem_ld32(trow + L::ST + cb + 32 * c, sv);
+        const float4* l4 = reinterpret_cast<const float4*>(lse_s + s * BQ + cb + 32 * c);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
           const float4 v = l4[i];
           ls[4 * i] = v.x; ls[4 * i + 1] = v.y; ls[4 * i + 2] = v.z; ls[4 * i + 3] = v.w;
         }
+        float* pc = pv + 32 * c;
         if (full_block) {
 #pragma unroll
-          for (int i = 0; i < 32; i++) pv[i] = ex2(fmaf(sv[i], c2, -ls[i]));
+          for (int i = 0; i < 32; i++) pc[i] = ex2(fmaf(sv[i], c2, -ls[i]));
         } else {
-          // queries of the block see this key from the first whose position
-          // reaches it, up to the last query of the sequence
-          const int first = count_below(qp_s + s * BQ, BQ, kpos_row) - cb;
-          const int last = p.Tq - q0 - cb;
+          if (c > 0 && p.mask != nullptr) mask_chunk(c, keep);
 #pragma unroll
           for (int i = 0; i < 32; i++) {
-            bool adm = i >= first && i < last;
+            const int qi = 32 * c + i;
+            bool adm = qi >= first && qi < last;
             if (p.mask != nullptr) adm = adm && keep[i] != 0;
-            pv[i] = adm ? ex2(fmaf(sv[i], c2, -ls[i])) : 0.0f;
+            pc[i] = adm ? ex2(fmaf(sv[i], c2, -ls[i])) : 0.0f;
           }
         }
-        float hi[16], lo[16];
-        pack_pairs(pv, s_p, hi, lo);
-        tmem_st16(trow + L::ST + cb, hi);
-        tmem_st16(trow + L::ST + cb + 16, lo);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(B_(P_READY));
+        float chunk[32], hi[16], lo[16];
+#pragma unroll
+        for (int i = 0; i < 32; i++) chunk[i] = pc[i];
+        pack_pairs(chunk, s_p, hi, lo);
+        tmem_st16(trow + L::ST + cb + 32 * c, hi);
+        tmem_st16(trow + L::ST + cb + 32 * c + 16, lo);
       }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B_(P_READY));
       if (j > 0 && j % kChunkBlocks == 0) {
         // the chunk ending with block j - 1: once this thread's accumulator
         // (dK for warps 0-3, dV for 4-7) has its last MMA of that chunk, add
@@ -562,7 +580,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        const bool first = j == kChunkBlocks;
+        const bool first_chunk = j == kChunkBlocks;
 #pragma unroll
         for (int c = 0; c < DH / 32; c++) {
           float v[32];
@@ -571,7 +589,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
 #pragma unroll
           for (int u = 0; u < 8; u++) {
             float4 x = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-            if (!first) {
+            if (!first_chunk) {
               const float4 y = dst[u];
               x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
             }
@@ -585,25 +603,26 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      {
+#pragma unroll
+      for (int c = 0; c < NQC; c++) {
         float dp[32], dl[32];
-        tmem_ld32(trow + L::DPT + cb, dp);
-        const float4* d4 = reinterpret_cast<const float4*>(dlt_s + s * BQ + cb);
+        tmem_ld32(trow + L::DPT + cb + 32 * c, dp);
+        const float4* d4 = reinterpret_cast<const float4*>(dlt_s + s * BQ + cb + 32 * c);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
           const float4 v = d4[i];
           dl[4 * i] = v.x; dl[4 * i + 1] = v.y; dl[4 * i + 2] = v.z; dl[4 * i + 3] = v.w;
         }
 #pragma unroll
-        for (int i = 0; i < 32; i++) dp[i] = pv[i] * (dp[i] * u_dp - dl[i]);
+        for (int i = 0; i < 32; i++) dp[i] = pv[32 * c + i] * (dp[i] * u_dp - dl[i]);
         float hi[16], lo[16];
         pack_pairs(dp, s_ds, hi, lo);
-        tmem_st16(trow + L::DPT + cb, hi);
-        tmem_st16(trow + L::DPT + cb + 16, lo);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(B_(D_READY0 + s));
+        tmem_st16(trow + L::DPT + cb + 32 * c, hi);
+        tmem_st16(trow + L::DPT + cb + 32 * c + 16, lo);
       }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(B_(D_READY0 + s));
     }
     if (ok && n_it > 0) {
       const uint32_t last = (uint32_t)((n_it - 1) & 1);
@@ -1041,8 +1060,10 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
   CUtensorMap qh128, ql128, gh128, gl128, kkh, kkl, vkh, vkl;  // dQ kernel
   const bool built = map16(&kh, w.k16h, krows, BK) && map16(&kl, w.k16l, krows, BK) &&
                      map16(&vh, w.v16h, krows, BK) && map16(&vl, w.v16l, krows, BK) &&
-                     map16(&qh, w.q16h, qrows, BQ) && map16(&ql, w.q16l, qrows, BQ) &&
-                     map16(&gh, w.g16h, qrows, BQ) && map16(&gl, w.g16l, qrows, BQ) &&
+                     map16(&qh, w.q16h, qrows, Kv16Layout<DH>::BQ) &&
+                     map16(&ql, w.q16l, qrows, Kv16Layout<DH>::BQ) &&
+                     map16(&gh, w.g16h, qrows, Kv16Layout<DH>::BQ) &&
+                     map16(&gl, w.g16l, qrows, Kv16Layout<DH>::BQ) &&
                      map16(&qh128, w.q16h, qrows, QM) && map16(&ql128, w.q16l, qrows, QM) &&
                      map16(&gh128, w.g16h, qrows, QM) && map16(&gl128, w.g16l, qrows, QM) &&
                      map16(&kkh, w.k16h, krows, KN) && map16(&kkl, w.k16l, krows, KN) &&

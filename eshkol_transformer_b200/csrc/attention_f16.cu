@@ -564,7 +564,10 @@ bool launch_fwd_f16(const AttnParams& p, AttnOut o, float* m, float* l, cudaStre
 }  // namespace
 
 bool attention_uses_pairs16(const AttnParams& p) {
-  const bool long_seq = (int64_t)p.Tq * p.Tk >= (int64_t)2048 * 2048;
+  // head_dim 64: from 1,024^2 the binary16 forward + backward measured
+  // faster than 3xTF32 (the backward's 128-query blocks; the forward alone
+  // wins from 4,096^2), below it the preparation passes weigh more
+  const bool long_seq = (int64_t)p.Tq * p.Tk >= (int64_t)1024 * 1024;
   return p.Dh == 128 || (p.Dh == 64 && (p.bwd_pairs16 || long_seq));
 }
 
