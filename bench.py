@@ -195,6 +195,11 @@ def run_b200(args) -> None:
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
+        # NCCL's communicator-init log (one "comm ... rank r nRanks n" line per
+        # rank and communicator, on stderr) shows how many ranks joined
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", init_method="env://",
                                 timeout=__import__("datetime").timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
