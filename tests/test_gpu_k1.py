@@ -126,6 +126,8 @@ def _attention_inputs(shape, seed, masked=False):
     ((1, 4, 2, 300, 800, 32), False),   # Tq < Tk over several tiles, GQA
     ((1, 2, 2, 256, 256, 128), False),  # Dh 128 over several tiles
     ((2, 4, 2, 100, 100, 128), True),   # Dh 128 (binary16-pair backward): GQA, mask, empty row
+    ((1, 4, 2, 1024, 1024, 64), True),  # Dh 64 at 1024^2 (binary16 pairs, 128-query blocks): GQA, mask
+    ((1, 2, 2, 600, 1800, 64), False),  # Dh 64 binary16 with Tq < Tk over several tiles
 ])
 def test_attention_vs_oracle(lib, cuda, shape, masked):
     N, Hq, Hkv, Tq, Tk, Dh = shape
