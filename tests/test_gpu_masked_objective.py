@@ -62,7 +62,8 @@ def test_masked_gradients_vs_oracle(lib, cuda, precision):
 @pytest.mark.parametrize("precision", MODES)
 def test_masked_training_vs_oracle(lib, cuda, precision):
     """Four AdamW steps, a different mask each: the loss per step and the
-    final weights (each within steps * 2 lr, 99 % within 2e-6)."""
+    final weights (median distance 1e-3 lr, 99th percentile 1e-2 lr, every
+    element within 1 lr of the oracle's)."""
     s = TINY
     om = _oracle_model()
     params = om.init(77)
@@ -83,8 +84,12 @@ def test_masked_training_vs_oracle(lib, cuda, precision):
     assert model.update_counts() == (4, 0)
     w = model.read(0)
     diff = np.abs(w.astype(np.float64) - params)
-    assert diff.max() <= 4 * 2 * 1e-3, diff.max()
-    assert np.mean(diff <= 2e-6) >= 0.99, np.mean(diff <= 2e-6)
+    lr = 1e-3  # bars in units of one update, as the tiny-LM trajectory test states them
+    print(f"weights vs oracle: median {np.median(diff) / lr:.2e} lr, p99 "
+          f"{np.percentile(diff, 99) / lr:.2e} lr, max {diff.max() / lr:.2e} lr")
+    assert np.median(diff) <= 1e-3 * lr
+    assert np.percentile(diff, 99) <= 1e-2 * lr
+    assert diff.max() <= 1.0 * lr
     model.close()
 
 

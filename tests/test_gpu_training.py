@@ -201,11 +201,15 @@ def test_tiny_lm_gradients_vs_oracle(lib, cuda, precision):
 @pytest.mark.parametrize("precision", [etb.PRECISION_TF32X3, etb.PRECISION_F16X3])
 def test_tiny_lm_training_trajectory_vs_oracle(lib, cuda, precision):
     """Five AdamW steps: the loss trajectory within 2e-5 relative (the
-    reference's TR3 loss tolerance) and the final weights.  AdamW's update
-    lr m/(sqrt(v) + eps) is close to lr sign(g) and so amplifies any gradient
-    difference on elements whose gradient is itself near eps; the weight check
-    therefore bounds every element by the update size (steps * lr) and
-    requires 99% of them within 2e-6 of the oracle."""
+    reference's TR3 loss tolerance) and the final weights against the
+    oracle's after the same updates, in units of the learning rate (one update
+    moves a weight by up to about lr): median distance at most 1e-3 lr, 99th
+    percentile at most 1e-2 lr (the bulk follows the oracle to a small part
+    of one update), every element within 1 lr.  AdamW's lr m / (sqrt(v) +
+    eps) is close to lr sign(g), so an element whose gradient lies within the
+    gradient error of zero (a few per million here) can take a step of either
+    sign; the maximum is bounded by the update size, not by the gradient
+    error."""
     s = TINY
     om = _oracle_model()
     params = om.init(99)
@@ -222,8 +226,12 @@ def test_tiny_lm_training_trajectory_vs_oracle(lib, cuda, precision):
         assert abs(loss - loss_ref) <= 2e-5 * abs(loss_ref), (step, loss, loss_ref)
     w = model.read(0)
     diff = np.abs(w.astype(np.float64) - params)
-    assert diff.max() <= 5 * 2 * 1e-3, diff.max()
-    assert np.mean(diff <= 2e-6) >= 0.99, np.mean(diff <= 2e-6)
+    lr = 1e-3
+    print(f"weights vs oracle: median {np.median(diff) / lr:.2e} lr, p99 "
+          f"{np.percentile(diff, 99) / lr:.2e} lr, max {diff.max() / lr:.2e} lr")
+    assert np.median(diff) <= 1e-3 * lr
+    assert np.percentile(diff, 99) <= 1e-2 * lr
+    assert diff.max() <= 1.0 * lr
     model.close()
 
 
