@@ -188,6 +188,7 @@ struct Bwd16Args {
   float* chunks;     // dK/dV chunk sums, kBwdChunkFloats per slot
   int* slot_flags;   // 0 free, 1 taken
   int chunk_slots;
+  const int* exps;   // non-null: the producers' exponents of Q, K, V, dO
 };
 
 // dK and dV accumulate over up to G Tq queries; the tensor pipe's f32
@@ -490,7 +491,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     }
   } else {
     // ---- P^T = 2^(S^T scale log2(e) - lse2), then dS^T = P^T (dP^T - delta)
-    const Exps ex = exps_of(a.amax, DH);
+    const Exps ex = exps_of(a.amax, DH, a.exps);
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int64_t kpos_row = valid_k ? kp[tk] : INT64_MAX;
     const bool keys_full = k0 + BK <= p.Tk;
@@ -939,7 +940,7 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     }
   } else {
     // ---- dS = P (dP - delta), P = 2^(S scale log2(e) - lse2)
-    const Exps ex = exps_of(a.amax, DH);
+    const Exps ex = exps_of(a.amax, DH, a.exps);
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     const int64_t ri = ((int64_t)b * p.Hq + hq) * p.Tq + tq;
     const float lse_row = valid_q ? a.lse2[ri] : INFINITY;
@@ -1072,7 +1073,9 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
   // Q, K, V pairs: from the 3xTF32 pairs a producer left in the workspace
   // (maxima, then the split), kept from this call's binary16 forward, or
   // prepared from q, k, v here
-  if (p.qkv_ready) {
+  if (p.pairs16) {
+    // written by the QKV GEMM epilogue
+  } else if (p.qkv_ready) {
     const int64_t nq4 = qrows * DH / 4, nk4 = krows * DH / 4;
     const int64_t most = nq4 > nk4 ? nq4 : nk4;
     const int64_t want = (most + 255) / 256, cap = (int64_t)sm_count() * 8;
@@ -1087,9 +1090,10 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
   } else if (!p.ws_ready) {
     attention_prepare_pairs16(p, stream);
   }
-  // row statistics and max |dO|, then dO's pair
-  cudaMemsetAsync(w.amax16 + 3, 0, sizeof(unsigned), stream);
-  {
+  // row statistics and max |dO|, then dO's pair (with pairs16 the dO GEMM
+  // epilogue wrote them)
+  if (!p.pairs16) {
+    cudaMemsetAsync(w.amax16 + 3, 0, sizeof(unsigned), stream);
     const int64_t want = (qrows + 7) / 8, cap = (int64_t)sm_count() * 16;
     const unsigned rg = (unsigned)(want < cap ? want : cap);
     auto go = [&](auto v, auto vl) {
@@ -1106,11 +1110,11 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
       go(std::integral_constant<int, 2>{}, std::true_type{});
     else
       go(std::integral_constant<int, 2>{}, std::false_type{});
+    count_launch(2);
   }
-  count_launch(2);
   cudaMemsetAsync(w.slot_flags, 0, (size_t)w.chunk_slots * sizeof(int), stream);
-  Bwd16Args a{w.lse2, delta, w.amax16, device_error_word(), w.chunks, w.slot_flags,
-              w.chunk_slots};
+  Bwd16Args a{w.lse2, delta, p.pairs16 ? p.pair_amax : w.amax16, device_error_word(), w.chunks,
+              w.slot_flags, w.chunk_slots, p.pairs16 ? p.pair_exps : nullptr};
   dim3 g1((p.Tk + BK - 1) / BK, p.Hkv, p.B);
   dim3 g2((p.Tq + QM - 1) / QM, p.Hq, p.B);
   // instances: with / without the mask code, three products / one
@@ -1142,7 +1146,11 @@ bool attention_backward_f16(const AttnParams& p, AttnTensor o, const float* o_lo
                             const float* row_max, const float* row_sum, float* delta, AttnOut dq,
                             AttnOut dk, AttnOut dv, cudaStream_t stream) {
   if (p.ws == nullptr || encode_fn() == nullptr || p.Tq == 0 || p.Tk == 0) return false;
-  if (p.grad_ready) return false;  // the dO pair must come from dout
+  // the dO pair comes from dout, or with pairs16 from the dO GEMM epilogue
+  if (p.pairs16 ? !p.grad_ready || !(p.ws_ready || p.qkv_ready) || p.pair_exps == nullptr ||
+                      p.pair_amax == nullptr
+                : p.grad_ready)
+    return false;
   if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
   switch (p.Dh) {
     case 64:

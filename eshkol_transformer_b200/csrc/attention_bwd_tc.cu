@@ -1061,7 +1061,7 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
                            AttnOut dk, AttnOut dv, cudaStream_t stream) {
   if (p.ws == nullptr || encode_fn() == nullptr || p.Tq == 0 || p.Tk == 0) return false;
   if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
-  if (attention_uses_pairs16(p) && !p.grad_ready)
+  if (p.pairs16 || (attention_uses_pairs16(p) && !p.grad_ready))
     return attention_backward_f16(p, o, o_lo, dout, row_max, row_sum, delta, dq, dk, dv, stream);
   switch (p.Dh) {
     case 32:
@@ -1076,7 +1076,9 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
 bool attention_grad_prep(const AttnParams& p, AttnTensor o, const float* o_lo,
                          const float* row_max, const float* row_sum, float* delta,
                          AttnGradPrep* out) {
-  if (p.ws == nullptr || p.Dh != 32 && p.Dh != 64) return false;
+  if (p.ws == nullptr) return false;
+  if (p.pairs16 ? p.Dh != 64 && p.Dh != 128 : p.Dh != 32 && p.Dh != 64) return false;
+  if (p.pairs16 && p.pair_exps == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
   // o as merged token-major rows [B*Tq, Hq*Dh]
   const int64_t ld = (int64_t)p.Hq * p.Dh;
@@ -1087,6 +1089,11 @@ bool attention_grad_prep(const AttnParams& p, AttnTensor o, const float* o_lo,
   g.o = o.ptr; g.o_lo = o_lo;
   g.row_max = row_max; g.row_sum = row_sum;
   g.doh = w.doh; g.dol = w.dol; g.delta = delta; g.lse2 = w.lse2;
+  if (p.pairs16) {
+    g.g16h = w.g16h; g.g16l = w.g16l;
+    g.g_exp = p.pair_exps + 3;
+  }
+  g.g_amax = p.pair_amax != nullptr ? p.pair_amax + 3 : nullptr;
   *out = g;
   return true;
 }

@@ -174,6 +174,7 @@ struct Fwd16Layout {
 struct Fwd16Args {
   const unsigned* amax;  // [0..2] max |x| of Q, K, V
   int* error;
+  const int* exps;       // non-null: the producers' exponents of Q, K, V
 };
 
 template <int DH, bool MASKED, bool THREE>
@@ -372,7 +373,7 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     }
   } else {
     // ---- probabilities: this thread's NKH keys of each block, row shared with warp w ^ 4
-    const Exps ex = exps_of(a.amax, DH);
+    const Exps ex = exps_of(a.amax, DH, a.exps);
     const float c2 = p.scale * kLog2e * exp2_int(-(ex.q + ex.k));  // base-2 score scale
     const float s_p = exp2_int(kPExpFwd);
     const int cb = NKH * khalf;
@@ -540,8 +541,10 @@ bool launch_fwd_f16(const AttnParams& p, AttnOut o, float* m, float* l, cudaStre
       !map16(&kh, w.k16h, krows, L::KN) || !map16(&kl, w.k16l, krows, L::KN) ||
       !map16(&vh, w.v16h, krows, L::KN) || !map16(&vl, w.v16l, krows, L::KN))
     return false;
-  attention_prepare_pairs16(p, stream);
-  Fwd16Args a{w.amax16, device_error_word()};
+  // the pairs: from a producer (pairs16), else prepared here from q, k, v
+  if (!p.pairs16) attention_prepare_pairs16(p, stream);
+  Fwd16Args a{p.pairs16 ? p.pair_amax : w.amax16, device_error_word(),
+              p.pairs16 ? p.pair_exps : nullptr};
   dim3 grid((p.Tq + QM - 1) / QM, p.Hq, p.B);
   auto go = [&](auto masked, auto three) {
     constexpr bool M = decltype(masked)::value, T3 = decltype(three)::value;
@@ -598,6 +601,7 @@ bool attention_forward_f16(const AttnParams& p, AttnOut o, float* row_max, float
                            cudaStream_t stream) {
   if (p.ws == nullptr || encode_fn() == nullptr || p.Tq == 0 || p.Tk == 0) return false;
   if ((reinterpret_cast<uintptr_t>(p.ws) | reinterpret_cast<uintptr_t>(p.ws_grad)) & 15) return false;
+  if (p.pairs16 && (!p.qkv_ready || p.pair_exps == nullptr || p.pair_amax == nullptr)) return false;
   switch (p.Dh) {
     case 64: return launch_fwd_f16<64>(p, o, row_max, row_sum, stream);
     case 128: return launch_fwd_f16<128>(p, o, row_max, row_sum, stream);

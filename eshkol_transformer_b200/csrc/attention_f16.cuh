@@ -99,15 +99,25 @@ __device__ __forceinline__ int pair_exponent(float amax) {
 struct Exps {
   int q, k, v, g, ds;
 };
-// amax[0..3]: max |x| of Q, K, V, dO (f32 bits).
-__device__ __forceinline__ Exps exps_of(const unsigned* amax, int dh) {
+// amax[0..3]: max |x| of Q, K, V, dO (f32 bits).  fixed (non-null): the
+// producers chose the exponents of Q, K, V, dO (fixed[0..3]); dS's still
+// comes from this call's maxima of V and dO, which bound it.
+__device__ __forceinline__ Exps exps_of(const unsigned* amax, int dh,
+                                       const int* fixed = nullptr) {
   const float aq = __uint_as_float(amax[0]), ak = __uint_as_float(amax[1]);
   const float av = __uint_as_float(amax[2]), ag = __uint_as_float(amax[3]);
   Exps x;
-  x.q = pair_exponent(aq);
-  x.k = pair_exponent(ak);
-  x.v = pair_exponent(av);
-  x.g = pair_exponent(ag);
+  if (fixed != nullptr) {
+    x.q = fixed[0];
+    x.k = fixed[1];
+    x.v = fixed[2];
+    x.g = fixed[3];
+  } else {
+    x.q = pair_exponent(aq);
+    x.k = pair_exponent(ak);
+    x.v = pair_exponent(av);
+    x.g = pair_exponent(ag);
+  }
   // bound 2^e in [2^13, 2^14)
   x.ds = pair_exponent(2.0f * (float)dh * ag * av) - 1;
   return x;

@@ -557,12 +557,19 @@ bool attention_qkv_prep(const AttnParams& p, QkvPrep* out) {
   if (p.ws == nullptr || (reinterpret_cast<uintptr_t>(p.ws) & 15)) return false;
   if (p.Dh != 32 && p.Dh != 64 && p.Dh != 128) return false;
   if (p.Tq != p.Tk) return false;  // one qkv matrix holds every operand
+  if (p.pairs16 && (p.Dh == 32 || p.pair_exps == nullptr)) return false;
   const AttnWs w = attn_ws(p);
   QkvPrep q{};
   q.T = p.Tq; q.Hq = p.Hq; q.Hkv = p.Hkv; q.Dh = p.Dh;
   q.q_cos = p.q_cos; q.q_sin = p.q_sin; q.k_cos = p.k_cos; q.k_sin = p.k_sin;
   q.q_rope_batched = p.q_rope_batched; q.k_rope_batched = p.k_rope_batched;
   q.qh = w.qh; q.ql = w.ql; q.kh = w.kh; q.kl = w.kl; q.vh = w.vh; q.vl = w.vl;
+  if (p.pairs16) {
+    q.q16h = w.q16h; q.q16l = w.q16l; q.k16h = w.k16h; q.k16l = w.k16l;
+    q.v16h = w.v16h; q.v16l = w.v16l;
+    q.exps = p.pair_exps;
+  }
+  q.amax = p.pair_amax;
   *out = q;
   return true;
 }
@@ -605,8 +612,9 @@ bool attention_forward_tc(const AttnParams& p, AttnOut o, float* row_max, float*
   if (p.ws == nullptr || encode_fn() == nullptr) return false;
   if (reinterpret_cast<uintptr_t>(p.ws) & 15) return false;
   // binary16 pairs where the backward takes them too (it then reuses the
-  // pairs), unless a producer already wrote the 3xTF32 operands
-  if (!p.qkv_ready && attention_uses_pairs16(p))
+  // pairs), unless a producer already wrote the 3xTF32 operands; a
+  // producer's binary16 pairs always go to the binary16 kernel
+  if (p.pairs16 || (!p.qkv_ready && attention_uses_pairs16(p)))
     return attention_forward_f16(p, o, row_max, row_sum, stream);
   switch (p.Dh) {
     case 32: return launch_fwd_tc<32>(p, o, row_max, row_sum, stream);

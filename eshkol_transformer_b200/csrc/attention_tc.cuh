@@ -58,6 +58,16 @@ inline AttnWs attn_ws(const AttnParams& p) {
   w.v16h = w.k16l + nk;
   w.v16l = w.v16h + nk;
   w.amax16 = reinterpret_cast<unsigned*>(w.v16l + nk);
+  if (p.pairs16) {
+    // the producers' binary16 Q / K / V pairs live in the Q / K / V part (in
+    // place of the TF32 pairs), so the backward finds them after the forward
+    w.q16h = reinterpret_cast<uint16_t*>(p.ws);
+    w.q16l = w.q16h + nq;
+    w.k16h = w.q16l + nq;
+    w.k16l = w.k16h + nk;
+    w.v16h = w.k16l + nk;
+    w.v16l = w.v16h + nk;
+  }
   w.chunk_slots = attn_chunk_slots();
   w.slot_flags = reinterpret_cast<int*>(w.amax16 + 64);
   w.chunks = reinterpret_cast<float*>(w.slot_flags + ((w.chunk_slots + 63) & ~63));

@@ -485,10 +485,12 @@ __device__ __forceinline__ void qkv_column(const QkvPrep& q, int n, int& sec, in
 // j of the head; j % 4 == 0) of token t of sequence b, from the values x = y +
 // bias as stored to C: head-major TF32 hi / lo copies, with the RoPE rotation
 // of the pairs (j, j + 1), (j + 2, j + 3) for Q and K (attention_tc.cu
-// attn_prepare_kernel computes the same values).  The host tables' two
-// entries are one aligned float2 (Dh / 2 even).
-__device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int sec, int h, int j, int b,
-                                               int t, float4 x) {
+// attn_prepare_kernel computes the same values), or with q.q16h the binary16
+// pair of the rotated values times s (2^exps[sec]).  The host tables' two
+// entries are one aligned float2 (Dh / 2 even).  Returns max |x| of the four
+// stored values.
+__device__ __forceinline__ float qkv_prep_store(const QkvPrep& q, int sec, int h, int j, int b,
+                                                int t, float4 x, float s16) {
   const float* ct = sec == 0 ? q.q_cos : (sec == 1 ? q.k_cos : nullptr);
   if (ct != nullptr) {
     const float* st = sec == 0 ? q.q_sin : q.k_sin;
@@ -504,6 +506,12 @@ __device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int sec, int h,
   }
   const int H = sec == 0 ? q.Hq : q.Hkv;
   const int64_t o = (((int64_t)b * H + h) * q.T + t) * q.Dh + j;
+  if (q.q16h != nullptr) {
+    uint16_t* hi = sec == 0 ? q.q16h : (sec == 1 ? q.k16h : q.v16h);
+    uint16_t* lo = sec == 0 ? q.q16l : (sec == 1 ? q.k16l : q.v16l);
+    f16_store4(hi, lo, o, x, s16);
+    return abs_max4(0.0f, x);
+  }
   float* hi = sec == 0 ? q.qh : (sec == 1 ? q.kh : q.vh);
   float* lo = sec == 0 ? q.ql : (sec == 1 ? q.kl : q.vl);
   float4 h4, l4;
@@ -513,14 +521,20 @@ __device__ __forceinline__ void qkv_prep_store(const QkvPrep& q, int sec, int h,
   tf32_split(x.w, h4.w, l4.w);
   *reinterpret_cast<float4*>(hi + o) = h4;
   *reinterpret_cast<float4*>(lo + o) = l4;
+  return abs_max4(0.0f, x);
 }
 
 // dO columns [j, j + 4) of head h, token t of sequence b, as the attention
 // backward's head-major TF32 hi / lo operands (attention_bwd_tc.cu
-// attn_bwd_prepare_kernel writes the same values).
+// attn_bwd_prepare_kernel writes the same values), or with g.g16h the
+// binary16 pair of dO s16 (s16 = 2^(*g_exp)).
 __device__ __forceinline__ void attn_do_store(const AttnGradPrep& g, int h, int j, int b, int t,
-                                              float4 x) {
+                                              float4 x, float s16) {
   const int64_t o = (((int64_t)b * g.H + h) * g.T + t) * g.Dh + j;
+  if (g.g16h != nullptr) {
+    f16_store4(g.g16h, g.g16l, o, x, s16);
+    return;
+  }
   float4 h4, l4;
   tf32_split(x.x, h4.x, l4.x);
   tf32_split(x.y, h4.y, l4.y);
@@ -913,6 +927,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
     const float o_inv =
         (K_DO && args.dprep.o_exp != nullptr) ? exp2_int(-*args.dprep.o_exp) : 1.0f;
     float amax = 0.0f;  // max |x| of the operand-pair output this warp wrote
+    // attention operands as binary16 pairs: the scales of Q, K, V (QKV) or dO
+    // (ATTN_DO), and max |x| of each operand this lane wrote
+    const float s16_q = (K_QKV && args.qkv.q16h != nullptr) ? exp2_int(args.qkv.exps[0]) : 1.0f;
+    const float s16_k = (K_QKV && args.qkv.q16h != nullptr) ? exp2_int(args.qkv.exps[1]) : 1.0f;
+    const float s16_v = (K_QKV && args.qkv.q16h != nullptr) ? exp2_int(args.qkv.exps[2]) : 1.0f;
+    const float s16_g = (K_DO && args.dprep.g16h != nullptr) ? exp2_int(*args.dprep.g_exp) : 1.0f;
+    float am_q = 0.0f, am_k = 0.0f, am_v = 0.0f, am_g = 0.0f;
     for (int unit = cluster; unit < units; unit += nclusters) {
       const int tile = unit % tiles, split = unit / tiles;
       int ok = 1;
@@ -1045,7 +1066,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
                 if (!args.skip_c) *reinterpret_cast<float4*>(cbase + (int64_t)row * ldc + n) = x;
                 int tk = tok0 + 4 * it, sq = seq0;
                 while (tk >= seqT) { tk -= seqT; ++sq; }
-                attn_do_store(args.dprep, a_h, a_j, sq, tk, x);
+                attn_do_store(args.dprep, a_h, a_j, sq, tk, x, s16_g);
+                am_g = abs_max4(am_g, x);
                 const float4 o = pre[it];
                 dot = fmaf(x.w, o.w, fmaf(x.z, o.z, fmaf(x.y, o.y, x.x * o.x)));
               }
@@ -1150,7 +1172,11 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             } else if (K_QKV && epi == GEMM_EPI_QKV) {
               int tk = tok0 + 4 * it, sq = seq0;
               while (tk >= seqT) { tk -= seqT; ++sq; }
-              qkv_prep_store(args.qkv, a_sec, a_h, a_j, sq, tk, x);
+              const float m4 = qkv_prep_store(args.qkv, a_sec, a_h, a_j, sq, tk, x,
+                                              a_sec == 0 ? s16_q : (a_sec == 1 ? s16_k : s16_v));
+              if (a_sec == 0) am_q = fmaxf(am_q, m4);
+              else if (a_sec == 1) am_k = fmaxf(am_k, m4);
+              else am_v = fmaxf(am_v, m4);
             }
           }
           if (K_GB && epi == GEMM_EPI_GELU_BWD) {
@@ -1288,6 +1314,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
     if (args.out_sc.amax != nullptr) amax_record_warp(args.out_sc.amax, amax);
+    if (K_QKV && args.qkv.amax != nullptr) {
+      amax_record_warp(args.qkv.amax, am_q);
+      amax_record_warp(args.qkv.amax + 1, am_k);
+      amax_record_warp(args.qkv.amax + 2, am_v);
+    }
+    if (K_DO && args.dprep.g_amax != nullptr) amax_record_warp(args.dprep.g_amax, am_g);
   }
   // After a timeout, give copies still in flight (whose completion this CTA
   // cannot observe when it lands on the peer's barrier) time to land.
@@ -1533,6 +1565,11 @@ void launch_tc2(const GemmArgs& g, cudaStream_t stream) {
       (g.epilogue == GEMM_EPI_QKV || g.epilogue == GEMM_EPI_ATTN_DO) && !a.staged;
   if (prep_after && g.epilogue == GEMM_EPI_ATTN_DO && g.dprep->o_exp != nullptr) {
     gemm_f16_refused(g, "binary16 attention output needs the staged epilogue");
+    return;
+  }
+  if (prep_after && ((g.epilogue == GEMM_EPI_QKV && g.qkv->q16h != nullptr) ||
+                     (g.epilogue == GEMM_EPI_ATTN_DO && g.dprep->g16h != nullptr))) {
+    gemm_f16_refused(g, "binary16 attention operands need the staged epilogue");
     return;
   }
   if (prep_after) {

@@ -249,6 +249,19 @@ struct AttnParams {
   // significant bits per operand element) instead of the three of the
   // f32-grade pairs
   int single;
+  // pairs16 (head_dim 64 / 128): the producers write the binary16 operand
+  // pairs themselves, each operand x as x 2^pair_exps[i] (i = 0 Q, 1 K, 2 V,
+  // 3 dO): the QKV GEMM epilogue writes the Q / K / V pairs at the start of
+  // ws (qkv_ready), the dO GEMM epilogue the dO pair, delta and lse2 in
+  // ws_grad (grad_ready; the backward needs it).  The forward and the
+  // backward of one call both set it.
+  int pairs16;
+  const int* pair_exps;
+  // optional: pair_amax[0..3] receives max |x| of Q, K, V (the QKV epilogue,
+  // after RoPE) and dO (the dO epilogue) in either operand format; with
+  // pairs16 the backward takes dS's exponent from this call's V and dO
+  // maxima there (they bound |dS|), so they must be recorded before it runs
+  unsigned* pair_amax;
 };
 // Where the GEMM producing dO = dY Wo (rows [B*T, H*Dh], token-major) writes
 // the attention backward's inputs: dO split into TF32 hi / lo head-major
@@ -263,6 +276,12 @@ struct AttnGradPrep {
   const int* o_exp;
   const float *row_max, *row_sum;
   float *doh, *dol, *delta, *lse2;
+  // non-null (AttnParams.pairs16): dO goes to g16h / g16l as the binary16
+  // pair of dO 2^(*g_exp) instead of doh / dol
+  uint16_t *g16h, *g16l;
+  const int* g_exp;
+  // optional: receives max |dO| (either format)
+  unsigned* g_amax;
 };
 // The AttnGradPrep of p's backward workspace when the tensor-core backward
 // will run with o given as the merged [B*T, Hq*Dh] rows (false otherwise).
@@ -281,10 +300,17 @@ struct QkvPrep {
   const float *q_cos, *q_sin, *k_cos, *k_sin;  // null: no RoPE
   int q_rope_batched, k_rope_batched;
   float *qh, *ql, *kh, *kl, *vh, *vl;
+  // non-null q16h (AttnParams.pairs16): the operands go to the binary16 pairs
+  // q16h / q16l, k16h / k16l, v16h / v16l (same element layout) as x
+  // 2^exps[i] (i = 0 Q, 1 K, 2 V) instead of the TF32 pairs
+  uint16_t *q16h, *q16l, *k16h, *k16l, *v16h, *v16l;
+  const int* exps;
+  // optional: amax[i] receives max |x| of section i (either format)
+  unsigned* amax;
 };
 // The QkvPrep of p's workspace (p.ws set, p.q / p.k / p.v columns of one qkv
 // matrix); false when the tensor-core attention cannot use it (Dh not
-// 32 / 64 / 128, or no workspace).
+// 32 / 64 / 128, or 32 with pairs16, or no workspace).
 bool attention_qkv_prep(const AttnParams& p, QkvPrep* out);
 // The same operands from a qkv matrix already in memory (row stride ld).
 void attention_prepare_from_qkv(const float* qkv, int64_t ld, int rows, const QkvPrep& q,

@@ -48,7 +48,10 @@ namespace {
 
 enum { kPerLayer = 12 };
 // split-f16 operand slots of one layer
-enum { S_H1 = 0, S_AO, S_H2, S_G, S_DXF, S_DU, S_DXA, S_DQKV, kSlotsPerLayer };
+// (S_Q, S_K, S_V, S_DO: the attention's binary16 operand pairs, consecutive
+// as AttnParams.pair_exps / pair_amax take them)
+enum { S_H1 = 0, S_AO, S_H2, S_G, S_DXF, S_DU, S_DXA, S_DQKV, S_Q, S_K, S_V, S_DO,
+       kSlotsPerLayer };
 // a slot's max |x| 2^e lands in [2^(target-1), 2^target): 64x below
 // binary16's overflow.  ET_B200_F16_SCALE_TARGET (2 .. 17) overrides it; 17
 // puts every slot's max above 65,504, which exercises the overflow check and
@@ -253,7 +256,11 @@ void split(et_b200_lm* lm, float* x, float* lo, size_t n) {
 }
 
 // Head widths whose attention runs on the tensor-core kernels both ways.
-bool tc_attention(const et_b200_lm* lm) { return lm->Dh == 32 || lm->Dh == 64; }
+// split-f16 steps at head_dim 64 / 128: the binary16 attention, whose
+// operand pairs the QKV and dO GEMM epilogues write with slot exponents
+bool attn16(const et_b200_lm* lm) { return lm->step16 && (lm->Dh == 64 || lm->Dh == 128); }
+// the tensor-core attention reads only the operands the GEMM epilogues write
+bool tc_attention(const et_b200_lm* lm) { return lm->Dh == 32 || lm->Dh == 64 || attn16(lm); }
 // A step that cannot be computed as enqueued fails through the device error
 // word (the host-synchronised entry points report it).
 void fail_step(const char* why) {
@@ -386,6 +393,13 @@ AttnParams attn_params(et_b200_lm* lm, const float* qkv, int layer) {
   p.ws = lm->attn_qkv_ws[layer];
   p.ws_grad = lm->attn_grad_ws;
   p.ws_ready = 0;
+  // every step of a split-f16 model records the operands' maxima (the next
+  // step's exponents); its split-f16 steps write binary16 operand pairs
+  if (lm->f16) p.pair_amax = lm->samax + lm->slot(layer, S_Q);
+  if (attn16(lm)) {
+    p.pairs16 = 1;
+    p.pair_exps = lm->sexp + lm->slot(layer, S_Q);
+  }
   return p;
 }
 
@@ -559,6 +573,8 @@ void backward(et_b200_lm* lm) {
     const bool skip_do = p.grad_ready && p.ws_ready && tc_attention(lm);
     linear_backward_dx(lm, dyh, dyl, R, d, d, lm->lt(l, T_WO), lm->dtmp, nullptr, nullptr, nullptr,
                        p.grad_ready ? &dprep : nullptr, lm->slot(l, S_DXA), -1, skip_do);
+    // dO's max where no epilogue recorded it (the next split-f16 step's exponent)
+    if (p.pair_amax != nullptr && !p.grad_ready) abs_max(lm->dtmp, R * d, p.pair_amax + 3, s);
     linear_backward_dw(lm, dyh, dyl, lm->step16 ? a.ao16 : a.ao,
                        lm->step16 ? half_at(a.ao16, R * d) : a.aolo, R, d, d,
                        lm->G(lm->lt(l, T_WO)), lm->slot(l, S_DXA), lm->slot(l, S_AO));

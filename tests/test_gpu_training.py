@@ -406,6 +406,37 @@ def test_long_sequence_lm_gradients_vs_oracle(lib, cuda):
     model.close()
 
 
+@pytest.mark.parametrize("heads, d_model, seq_len", [(4, 256, 384), (2, 256, 256)])
+def test_split_f16_lm_binary16_attention_vs_oracle(lib, cuda, heads, d_model, seq_len):
+    """Split-f16 steps at head_dim 64 and 128 run the binary16 attention with
+    its operand pairs written by the GEMM epilogues: the QKV projection's
+    (RoPE'd Q, K and V) and dO's (with delta and the log-sum-exp), each pair
+    scaled by the exponent its slot took from the previous step's maximum,
+    dS's exponent from this step's maxima of V and dO.  The second pass (the
+    first one measures the maxima in 3xTF32) against the oracle, with the LM
+    gradient bar."""
+    s = etb.ModelShape(1, d_model, heads, 4 * d_model, 1024, seq_len, 3)
+    om = orc.LanguageModel(s.layers, s.d_model, s.heads, s.ffn, s.vocabulary, s.seq_len, s.batch)
+    params = om.init(4321)
+    ids, targets = orc.synthetic_batch(55, s.batch, s.seq_len, s.vocabulary)
+    loss_ref, grads_ref = om.forward_backward(params, ids, targets)
+    model = etb.LanguageModel(s, precision=etb.PRECISION_F16X3)
+    model.init(4321)
+    model.forward_backward(ids, targets)
+    first = model.read(1)
+    loss = model.forward_backward(ids, targets)
+    grads = model.read(1)
+    model.close()
+    assert not bits_equal(grads, first)  # the binary16 pass did run
+    assert abs(loss - loss_ref) <= 2e-5 * abs(loss_ref), (loss, loss_ref)
+    worst = 0.0
+    for t, (g, r) in enumerate(zip(om.split(grads), om.split(grads_ref))):
+        err = np.abs(g.astype(np.float64) - r).max() / max(np.abs(r).max(), 1e-30)
+        worst = max(worst, err)
+        assert err <= GRAD_TOL[etb.PRECISION_F16X3], (t, err)
+    print(f"head_dim {d_model // heads}: worst per-tensor normwise gradient error {worst:.2e}")
+
+
 def test_o2_device_adamw_outside_check_envelope(lib, cuda):
     """Finite values outside the check pass's envelope (a gradient of 2^40, a
     moment of 2^35, a parameter of 2^110) take its exact computation; the
