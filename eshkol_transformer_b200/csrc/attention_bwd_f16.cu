@@ -299,7 +299,13 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
   const int G = p.Hq / p.Hkv;
   const int tk = k0 + row;
   const bool valid_k = tk < p.Tk;
-  if (tid == 0) {
+  const uint32_t base = smem_u32(smem);
+  const uint32_t kh_stage = base + L::QR + 2 * L::QT, vh_stage = base + L::GR + 2 * L::QT;
+  if (warp == LOADER && lane == 0) {
+    // the loader initialises the barriers and issues the key tile at once
+    // (its copies overlap the TMEM allocation and the position scan below):
+    // K, V lo stay in shared memory; K, V hi pass through stage 1 of the rings
+    // on their way to TMEM
     for (int i = 0; i < NBARS; i++) {
       const uint32_t n = (i == P_READY || i == D_READY0 || i == D_READY1 || i == CHUNK_DONE) ? SOFT
                          : (i == ST_FULL0 || i == ST_FULL1)               ? 32
@@ -307,15 +313,24 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
                                                                           : 1;
       mbar_init(B_(i), n);
     }
-    *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_async_smem();
+    mbar_expect_tx(B_(LO_FULL), 4 * L::KT);
+    const int r = (int)(((int64_t)b * p.Hkv + hkv) * p.Tk + k0);
+#pragma unroll
+    for (int c = 0; c < DH / 64; c++) {
+      const uint32_t o = (uint32_t)c * BK * 128u;
+      tma_load_2d(base + L::KL + o, &kl_map, B_(LO_FULL), 64 * c, r);
+      tma_load_2d(base + L::VL + o, &vl_map, B_(LO_FULL), 64 * c, r);
+      tma_load_2d(kh_stage + o, &kh_map, B_(LO_FULL), 64 * c, r);
+      tma_load_2d(vh_stage + o, &vh_map, B_(LO_FULL), 64 * c, r);
+    }
   }
+  if (tid == 0) *abort = 0;
   if (warp == 0) tmem_alloc(smem_u32(tslot), L::COLS);
 
   const int64_t* kp = p.kpos + (int64_t)b * p.Tk;
   const int64_t* qp = p.qpos + (int64_t)b * p.Tq;
-  const uint32_t base = smem_u32(smem);
   const int q_begin = warp_count(qp, p.Tq, kp[k0], false);  // first query that can see a key
   const int jb = q_begin / BQ, nqb = (p.Tq + BQ - 1) / BQ;
   const int per_head = q_begin < p.Tq ? nqb - jb : 0;
@@ -328,26 +343,6 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     *slot_s = chunked ? take_chunk_slot(a) : -1;
     if (chunked && *slot_s < 0) *abort = 1;
   }
-  const uint32_t kh_stage = base + L::QR + 2 * L::QT, vh_stage = base + L::GR + 2 * L::QT;
-  if (tid == 0 && n_it > 0) {
-    // the key tile: K, V lo stay in shared memory; K, V hi pass through stage
-    // 1 of the rings on their way to TMEM
-    mbar_expect_tx(B_(LO_FULL), 4 * L::KT);
-    const int r = (int)(((int64_t)b * p.Hkv + hkv) * p.Tk + k0);
-#pragma unroll
-    for (int c = 0; c < DH / 64; c++) {
-      const uint32_t o = (uint32_t)c * BK * 128u;
-      tma_load_2d(base + L::KL + o, &kl_map, B_(LO_FULL), 64 * c, r);
-      tma_load_2d(base + L::VL + o, &vl_map, B_(LO_FULL), 64 * c, r);
-      tma_load_2d(kh_stage + o, &kh_map, B_(LO_FULL), 64 * c, r);
-      tma_load_2d(vh_stage + o, &vh_map, B_(LO_FULL), 64 * c, r);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
   // the hi, lo tiles of block j's pair into stage j & 1 of a ring
   auto load_pair = [&](int ring, int full, const CUtensorMap* hm, const CUtensorMap* lm, int j) {
     const int s = j & 1;
@@ -362,8 +357,17 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     }
   };
   int nq = 0, ng = 0;  // blocks issued per ring (loader lane 0)
-  // K hi (warps 0-3) and V hi (warps 4-7) rows -> TMEM, while the loader
-  // issues block 0's pairs into stage 0
+  if (warp == LOADER && lane == 0 && n_it > 0) {  // block 0's pairs into stage 0
+    load_pair(L::QR, QF0, &qh_map, &ql_map, 0);
+    load_pair(L::GR, GF0, &gh_map, &gl_map, 0);
+    nq = ng = 1;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  // K hi (warps 0-3) and V hi (warps 4-7) rows -> TMEM
   if (warp < 8 && n_it > 0) {
     const bool ok = mbar_wait(B_(LO_FULL), 0u, a.error);
     if (!ok) *abort = 1;
@@ -373,10 +377,6 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
                              khalf == 0 ? L::KH : L::VH);
       tmem_wait_st();
     }
-  } else if (warp == LOADER && lane == 0 && n_it > 0) {
-    load_pair(L::QR, QF0, &qh_map, &ql_map, 0);
-    load_pair(L::GR, GF0, &gh_map, &gl_map, 0);
-    nq = ng = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -411,8 +411,9 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         mbar_arrive(B_(ST_FULL0 + (j & 1)));
       }
     }
-    if (lane == 0 && n_it > 0) {
-      // every copy has landed before the CTA releases its memory
+    if (lane == 0) {
+      // every copy (the key tile's too) has landed before the CTA releases
+      // its memory
       mbar_wait(B_(LO_FULL), 0u, a.error);
       for (int j = nq - 2 < 0 ? 0 : nq - 2; j < nq; j++)
         mbar_wait(B_(QF0 + (j & 1)), (uint32_t)((j >> 1) & 1), a.error);
@@ -636,6 +637,9 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     // gradient scale, the RoPE backward rotation (dK) and the output split are
     // applied while the rows are written out (coalesced)
     const uint32_t stage = base + (uint32_t)(khalf * 128 * (DH + 4) * 4);
+    // a tile no query sees stages its zero rows over the key tile's buffers:
+    // its copies land first
+    if (n_it == 0 && !mbar_wait(B_(LO_FULL), 0u, a.error)) ok = false;
     if (ok) {
       tc_fence_after();
       const float un = khalf == 0 ? exp2_int(-(ex.ds + ex.q)) : exp2_int(-(kPExp + ex.g));
@@ -805,10 +809,6 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     nkb = (seen + KN - 1) / KN;
     full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? seen_all / KN : 0;
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
   const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
   auto load_stage = [&](int j) {  // K hi/lo, V hi/lo of block j into stage j & 1
     const uint32_t bar = B_(FULL0 + (j & 1)), dst = base + L::STAGE0 + (j & 1) * L::STAGE;
@@ -823,8 +823,14 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
       tma_load_2d(dst + 3 * L::KT + o, &vl_map, bar, 64 * c, r);
     }
   };
-  // Q hi and dO hi rows -> TMEM (warps 0-3 Q, 4-7 dO), while the loader
-  // issues block 0
+  // block 0 goes out before the set-up barrier (the thread that initialised
+  // the barriers issues it)
+  if (tid == 0 && nkb > 0) load_stage(0);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  // Q hi and dO hi rows -> TMEM (warps 0-3 Q, 4-7 dO)
   if (warp < 8) {
     const bool ok = mbar_wait(B_(ROWS_HI), 0u, a.error);
     if (!ok) *abort = 1;
@@ -834,8 +840,6 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
                              khalf == 0 ? L::QH : L::GH);
       tmem_wait_st();
     }
-  } else if (warp == LOADER && lane == 0 && nkb > 0) {
-    load_stage(0);
   }
   tc_fence_before();
   __syncthreads();

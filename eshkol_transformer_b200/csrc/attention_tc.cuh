@@ -258,15 +258,27 @@ __device__ __forceinline__ void colsum_get(uint32_t red, int t, int nthreads, in
 
 // Gradient scaling and RoPE backward rotation of columns 4 c4 .. 4 c4 + 3 of
 // a row (pairs 2 c4, 2 c4 + 1 at table entries trow + 2 c4, + 1): x = v
-// scale, then (x0, x1) -> (x0 c + x1 s, -x0 s + x1 c) when ct is set.
+// scale, then (x0, x1) -> (x0 c + x1 s, -x0 s + x1 c) when ct is set.  The
+// tables are read-only for the kernel (non-coherent loads, which the
+// compiler may issue ahead of the output stores), as one float2 per table
+// when both are 8-byte aligned (trow and 2 c4 are even).
 __device__ __forceinline__ void grad_rotate4(float4& v, float scale, const float* ct,
                                              const float* st, int64_t trow, int c4) {
   float x[4] = {rn_mul(v.x, scale), rn_mul(v.y, scale), rn_mul(v.z, scale), rn_mul(v.w, scale)};
   if (ct != nullptr) {
+    float cv[2], sv[2];
+    const int64_t t0 = trow + 2 * c4;
+    if (((reinterpret_cast<uintptr_t>(ct) | reinterpret_cast<uintptr_t>(st)) & 7) == 0) {
+      const float2 c2 = __ldg(reinterpret_cast<const float2*>(ct + t0));
+      const float2 s2 = __ldg(reinterpret_cast<const float2*>(st + t0));
+      cv[0] = c2.x; cv[1] = c2.y; sv[0] = s2.x; sv[1] = s2.y;
+    } else {
+      cv[0] = __ldg(ct + t0); cv[1] = __ldg(ct + t0 + 1);
+      sv[0] = __ldg(st + t0); sv[1] = __ldg(st + t0 + 1);
+    }
 #pragma unroll
     for (int pr = 0; pr < 2; pr++) {
-      const int64_t ti = trow + 2 * c4 + pr;
-      const float c = ct[ti], s = st[ti];
+      const float c = cv[pr], s = sv[pr];
       const float x0 = x[2 * pr], x1 = x[2 * pr + 1];
       x[2 * pr] = rn_add(rn_mul(x0, c), rn_mul(x1, s));
       x[2 * pr + 1] = rn_add(-rn_mul(x0, s), rn_mul(x1, c));
