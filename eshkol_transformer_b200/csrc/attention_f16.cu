@@ -248,11 +248,6 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     nkb = (seen + KN - 1) / KN;
     full_kb = (p.mask == nullptr && q0 + QM <= p.Tq) ? seen_all / KN : 0;
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
-  const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
   const int64_t kv_row0 = ((int64_t)b * p.Hkv + hkv) * p.Tk;
   auto load_stage = [&](int j) {  // K hi/lo, V hi/lo of block j into stage j & 1
     const uint32_t bar = B_(FULL0 + (j & 1)), dst = base + (uint32_t)(j & 1) * L::STAGE;
@@ -267,7 +262,15 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
       tma_load_2d(dst + 3 * L::KT + off, &vl_map, bar, 64 * c, r);
     }
   };
-  // Q hi rows -> TMEM (warps 0-3; DH/2 columns), while the loader issues block 0
+  // block 0 goes out before the set-up barrier (the thread that initialised
+  // the barriers issues it)
+  if (tid == 0 && nkb > 0) load_stage(0);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+  // Q hi rows -> TMEM (warps 0-3; DH/2 columns)
   if (warp < 4) {
     const bool ok = mbar_wait(B_(ROWS_HI), 0u, a.error);
     if (!ok) *abort = 1;
@@ -275,8 +278,6 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
       tile_row16_to_tmem<DH>(rows_hi, row, trow, L::QH);
       tmem_wait_st();
     }
-  } else if (warp == LOADER && lane == 0 && nkb > 0) {
-    load_stage(0);
   }
   tc_fence_before();
   __syncthreads();

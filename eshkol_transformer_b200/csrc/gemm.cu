@@ -1011,6 +1011,24 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
           }
           // the auxiliary rows of the chunk, loaded before the accumulator wait
           float4 pre[8];
+          // ATTN_DO with o as a binary16 pair: every row's pair is requested
+          // before any is converted (one memory round trip per chunk)
+          uint4 raw[8];
+          if (K_DO && epi == GEMM_EPI_ATTN_DO && args.dprep.o_exp != nullptr) {
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+              const int row = row0 + 4 * it + sub;
+              raw[it] = make_uint4(0u, 0u, 0u, 0u);
+              if (row < args.M && col_ok) {
+                const int64_t oo = (int64_t)row * (args.dprep.H * args.dprep.Dh) + n;
+                const uint2 h = __ldg(reinterpret_cast<const uint2*>(
+                    reinterpret_cast<const uint16_t*>(args.dprep.o) + oo));
+                const uint2 l = __ldg(reinterpret_cast<const uint2*>(
+                    reinterpret_cast<const uint16_t*>(args.dprep.o_lo) + oo));
+                raw[it] = make_uint4(h.x, h.y, l.x, l.y);
+              }
+            }
+          }
 #pragma unroll
           for (int it = 0; it < 8; it++) {
             const int row = row0 + 4 * it + sub;
@@ -1021,14 +1039,11 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
               // the forward output o = hi + lo (exact), same layout as dO
               const int64_t oo = (int64_t)row * (args.dprep.H * args.dprep.Dh) + n;
               if (args.dprep.o_exp != nullptr) {  // binary16 pair of o 2^e
-                const uint2 h = __ldg(reinterpret_cast<const uint2*>(
-                    reinterpret_cast<const uint16_t*>(args.dprep.o) + oo));
-                const uint2 l = __ldg(reinterpret_cast<const uint2*>(
-                    reinterpret_cast<const uint16_t*>(args.dprep.o_lo) + oo));
-                pre[it] = make_float4((half_lo(h.x) + half_lo(l.x)) * o_inv,
-                                      (half_hi(h.x) + half_hi(l.x)) * o_inv,
-                                      (half_lo(h.y) + half_lo(l.y)) * o_inv,
-                                      (half_hi(h.y) + half_hi(l.y)) * o_inv);
+                const uint4 r = raw[it];
+                pre[it] = make_float4((half_lo(r.x) + half_lo(r.z)) * o_inv,
+                                      (half_hi(r.x) + half_hi(r.z)) * o_inv,
+                                      (half_lo(r.y) + half_lo(r.w)) * o_inv,
+                                      (half_hi(r.y) + half_hi(r.w)) * o_inv);
               } else {
                 const float4 oh = __ldg(reinterpret_cast<const float4*>(args.dprep.o + oo));
                 float4 ol = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1194,15 +1209,27 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ 
             // the chunk completes a head: one lane per row writes its delta and
             // its base-2 log-sum-exp (the attention backward's formula)
             const int h = (n_tile + c) / args.dprep.Dh;
+            // the rows' forward statistics first (read-only loads, all eight
+            // in flight together), then the stores
+            int64_t ri[8];
+            float lsum[8], lmax[8];
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+              const int row = row0 + 4 * it + sub;
+              const int b = row / args.dprep.T, t = row - b * args.dprep.T;
+              ri[it] = ((int64_t)b * args.dprep.H + h) * args.dprep.T + t;
+              const bool mine = q == 0 && row < args.M && n_tile + c < args.N;
+              lsum[it] = mine ? __ldg(args.dprep.row_sum + ri[it]) : 0.0f;
+              lmax[it] = mine ? __ldg(args.dprep.row_max + ri[it]) : 0.0f;
+            }
 #pragma unroll
             for (int it = 0; it < 8; it++) {
               const int row = row0 + 4 * it + sub;
               if (q == 0 && row < args.M && n_tile + c < args.N) {
-                const int b = row / args.dprep.T, t = row - b * args.dprep.T;
-                const int64_t ri = ((int64_t)b * args.dprep.H + h) * args.dprep.T + t;
-                args.dprep.delta[ri] = dacc[it];
-                const float l = args.dprep.row_sum[ri];
-                args.dprep.lse2[ri] = l > 0.0f ? (args.dprep.row_max[ri] + logf(l)) * 1.4426950408889634f : INFINITY;
+                args.dprep.delta[ri[it]] = dacc[it];
+                const float l = lsum[it];
+                args.dprep.lse2[ri[it]] =
+                    l > 0.0f ? (lmax[it] + logf(l)) * 1.4426950408889634f : INFINITY;
               }
               dacc[it] = 0.0f;
             }
