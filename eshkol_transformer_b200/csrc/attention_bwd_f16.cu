@@ -640,6 +640,17 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     // a tile no query sees stages its zero rows over the key tile's buffers:
     // its copies land first
     if (n_it == 0 && !mbar_wait(B_(LO_FULL), 0u, a.error)) ok = false;
+    // head_dim 64: the tile's RoPE table rows into the freed ring (past the
+    // staging and column-sum areas), so the dK rotation below reads shared
+    // memory
+    const uint32_t tab = base + (uint32_t)(2 * 128 * (DH + 4) * 4 + 2 * SOFT * 16);
+    static_assert(DH != 64 || 2 * 128 * (DH + 4) * 4 + 2 * SOFT * 16 + 2 * 128 * (DH / 2) * 4 <=
+                                  L::BARS, "table copy");
+    bool tab_s = false;
+    if (DH == 64 && ok)
+      tab_s = rope_rows_to_smem(tab, p.k_cos, p.k_sin,
+                                (int64_t)(p.k_rope_batched ? b * p.Tk + k0 : k0),
+                                min(BK, p.Tk - k0), DH, tid, SOFT);
     if (ok) {
       tc_fence_after();
       const float un = khalf == 0 ? exp2_int(-(ex.ds + ex.q)) : exp2_int(-(kPExp + ex.g));
@@ -675,6 +686,10 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
       const float4 sk = store_rows_split(
           base, DH, rows, dk.ptr, split ? dk.lo : nullptr, ko, dk.st, tid, SOFT,
           [&](int r, int c4, float4& v) {
+            if (tab_s) {
+              grad_rotate4_smem(v, p.scale, tab, r, c4, DH / 2);
+              return;
+            }
             const int t = k0 + r;
             const int64_t trw = (int64_t)(p.k_rope_batched ? b * p.Tk + t : t) * (DH / 2);
             grad_rotate4(v, p.scale, p.k_cos, p.k_sin, trw, c4);
@@ -1000,6 +1015,20 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
       ok = role_wait(B_(QD0 + (i & 1)), (uint32_t)((i >> 1) & 1), a.error, abort);
     }
     ok = __all_sync(0xffffffffu, ok);
+    // a tile that sees no key stages its zero rows over the Q / dO lo rows:
+    // their copies land first
+    if (nkb == 0 && !mbar_wait(B_(ROWS_LO), 0u, a.error)) ok = false;
+    // head_dim 64: the tile's RoPE table rows into the freed stages (past the
+    // staging and column-sum areas), so the dQ rotation below reads shared
+    // memory
+    const uint32_t tab = base + (uint32_t)(128 * (DH + 4) * 4 + SOFT * 16);
+    static_assert(DH != 64 || 128 * (DH + 4) * 4 + SOFT * 16 + 2 * 128 * (DH / 2) * 4 <= L::KPOS,
+                  "table copy");
+    bool tab_s = false;
+    if (DH == 64 && ok)
+      tab_s = rope_rows_to_smem(tab, p.q_cos, p.q_sin,
+                                (int64_t)(p.q_rope_batched ? b * p.Tq + q0 : q0),
+                                min(QM, p.Tq - q0), DH, tid, SOFT);
     // dQ rows (multiplied back to f32 scale) staged in the freed stages; the
     // gradient scale, the RoPE backward rotation and the output split are
     // applied while the rows are written out (coalesced)
@@ -1029,6 +1058,10 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
       const float4 sq = store_rows_split(
           base, DH, min(QM, p.Tq - q0), dq.ptr, dq.lo, qo, dq.st, tid, SOFT,
           [&](int r, int c4, float4& v) {
+            if (tab_s) {
+              grad_rotate4_smem(v, p.scale, tab, r, c4, DH / 2);
+              return;
+            }
             const int t = q0 + r;
             const int64_t trw = (int64_t)(p.q_rope_batched ? b * p.Tq + t : t) * (DH / 2);
             grad_rotate4(v, p.scale, p.q_cos, p.q_sin, trw, c4);

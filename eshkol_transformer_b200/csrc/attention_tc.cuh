@@ -287,6 +287,65 @@ __device__ __forceinline__ void grad_rotate4(float4& v, float scale, const float
   v = make_float4(x[0], x[1], x[2], x[3]);
 }
 
+// The RoPE tables' rows [tab_row0, tab_row0 + rows) (rows x dh / 2 floats
+// each, contiguous in the tables) copied into shared memory: cos at dst, sin
+// at dst + 128 * dh / 2 floats, by `nthreads` threads with 16-byte loads,
+// four of a thread's loads per table in flight before its stores (one memory
+// round trip per four rows of dh = 64 per thread, instead of one dependent
+// load per float4 of the gradient).  False (nothing copied) when the tables
+// are absent or not 16-byte aligned; the caller then reads them from
+// global memory.
+__device__ __forceinline__ bool rope_rows_to_smem(uint32_t dst, const float* ct, const float* st,
+                                                  int64_t tab_row0, int rows, int dh, int t,
+                                                  int nthreads) {
+  if (ct == nullptr || ((reinterpret_cast<uintptr_t>(ct) | reinterpret_cast<uintptr_t>(st)) & 15))
+    return false;
+  const int half = dh / 2, n4 = rows * half / 4;
+  const float4* c4 = reinterpret_cast<const float4*>(ct + tab_row0 * half);
+  const float4* s4 = reinterpret_cast<const float4*>(st + tab_row0 * half);
+  const uint32_t sin_dst = dst + (uint32_t)(128 * half * 4);
+  for (int i0 = t; i0 < n4; i0 += 4 * nthreads) {
+    float4 c[4], sn[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = i0 + u * nthreads;
+      if (i < n4) {
+        c[u] = __ldg(c4 + i);
+        sn[u] = __ldg(s4 + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int i = i0 + u * nthreads;
+      if (i < n4) {
+        sts128(dst + 16u * (uint32_t)i, c[u]);
+        sts128(sin_dst + 16u * (uint32_t)i, sn[u]);
+      }
+    }
+  }
+  return true;
+}
+// grad_rotate4 with the table entries of row r (pairs 2 c4, 2 c4 + 1) read
+// from a rope_rows_to_smem copy; the same arithmetic.
+__device__ __forceinline__ void grad_rotate4_smem(float4& v, float scale, uint32_t tab, int r,
+                                                  int c4, int half) {
+  float x[4] = {rn_mul(v.x, scale), rn_mul(v.y, scale), rn_mul(v.z, scale), rn_mul(v.w, scale)};
+  const uint32_t off = 4u * (uint32_t)(r * half + 2 * c4);
+  float2 c, sn;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(c.x), "=f"(c.y) : "r"(tab + off));
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];"
+               : "=f"(sn.x), "=f"(sn.y)
+               : "r"(tab + (uint32_t)(128 * half * 4) + off));
+  const float cv[2] = {c.x, c.y}, sv[2] = {sn.x, sn.y};
+#pragma unroll
+  for (int pr = 0; pr < 2; pr++) {
+    const float x0 = x[2 * pr], x1 = x[2 * pr + 1];
+    x[2 * pr] = rn_add(rn_mul(x0, cv[pr]), rn_mul(x1, sv[pr]));
+    x[2 * pr + 1] = rn_add(-rn_mul(x0, sv[pr]), rn_mul(x1, cv[pr]));
+  }
+  v = make_float4(x[0], x[1], x[2], x[3]);
+}
+
 // Number of entries of the ascending array a[0..n) that are <= x (le) or < x
 // (!le), found by a 32-ary search of the calling warp (every lane gets the
 // result): each round loads 32 entries at once and narrows the bracket 32-fold,
