@@ -727,10 +727,13 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
 // ---- dQ ---------------------------------------------------------------------------
 
 constexpr int QM = 128;  // queries per CTA (TMEM lanes)
-constexpr int KN = 64;   // keys per block
 
 template <int DH>
 struct Q16Layout {
+  // keys per block: 128 at head_dim 64 (S and dP at N = 128, the tensor
+  // pipe's full rate; TMEM then holds one dP buffer, DP1), 64 at head_dim 128
+  static constexpr int KN = DH == 64 ? 128 : 64;
+  static constexpr bool DP1 = KN == 128;
   static constexpr int KT = KN * DH * 2;  // [KN, DH] binary16 tile
   static constexpr int RT = QM * DH * 2;  // [QM, DH] binary16 row tile
   // Q lo and dO lo rows (shared-memory A operands); two stages of K hi/lo,
@@ -743,9 +746,11 @@ struct Q16Layout {
   // Q hi and dO hi rows pass through stage 1 on their way to TMEM
   static_assert(2 * RT <= STAGE, "row tiles in one stage");
   static_assert(128 * (DH + 4) * 4 + SOFT * 16 <= KPOS, "epilogue staging");
-  // TMEM: Q hi, dO hi (two elements per column); two slots of S, dP (the dS
-  // pair over S); the dQ accumulator
-  static constexpr uint32_t QH = 0, GH = DH / 2, SL0 = DH, SLOT = 2 * KN, DQ = SL0 + 2 * SLOT;
+  // TMEM: Q hi, dO hi (two elements per column); two slots of S (the dS pair
+  // over S), each with its dP behind it, or (DP1) one dP buffer behind both
+  // slots; the dQ accumulator
+  static constexpr uint32_t QH = 0, GH = DH / 2, SL0 = DH, SLOT = DP1 ? KN : 2 * KN;
+  static constexpr uint32_t DPB = SL0 + 2 * SLOT, DQ = DPB + (DP1 ? KN : 0);
   static constexpr uint32_t COLS = 512;
   static_assert(DQ + DH <= COLS, "TMEM columns");
   static_assert(SMEM <= 232448, "shared memory");
@@ -764,6 +769,8 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
                       Bwd16Args a) {
   if constexpr (!MASKED) p.mask = nullptr;
   using L = Q16Layout<DH>;
+  constexpr int KN = L::KN;
+  constexpr int NKC = KN / 64;  // 32-key chunks per probability thread
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   int64_t* kpos_s = reinterpret_cast<int64_t*>(smem + L::KPOS);  // [2][KN]
@@ -771,9 +778,11 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
   // per-slot barriers come in pairs (slot 0, slot 1); a slot serves every
   // other block, so block j waits phase (j >> 1) & 1 of slot j & 1.  EMPTY
   // completes when dP (chain B) and dQ (chain A) of the stage's block are done.
+  // DP_FREE (DP1): the probability threads have block j's dP in registers,
+  // so the one dP buffer can take block j + 1's (phase j & 1).
   enum {
     FULL0, FULL1, EMPTY0, EMPTY1, SA0, SA1, SB0, SB1, DS0, DS1, QD0, QD1, KP0, KP1, ROWS_HI,
-    ROWS_LO, DRAIN_A, DRAIN_B, NBARS
+    ROWS_LO, DRAIN_A, DRAIN_B, DP_FREE, NBARS
   };
   const uint32_t bar0 = smem_u32(bars);
   auto B_ = [&](int i) { return bar0 + 8u * (uint32_t)i; };
@@ -790,7 +799,7 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
   const uint32_t rows_hi = base + L::STAGE0 + L::STAGE;  // stage 1
   if (tid == 0) {
     for (int i = 0; i < NBARS; i++) {
-      const uint32_t n = (i == DS0 || i == DS1)         ? SOFT
+      const uint32_t n = (i == DS0 || i == DS1 || i == DP_FREE) ? SOFT
                          : (i == KP0 || i == KP1)       ? 32
                          : (i == EMPTY0 || i == EMPTY1) ? 2
                                                         : 1;
@@ -900,7 +909,6 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
       constexpr uint32_t idesc_q = idesc_f16_m128(DH, 1);
       const uint32_t xh = tmem + (is_a ? L::QH : L::GH);
       const uint32_t xlo = base + (is_a ? L::QL : L::GL);
-      const uint32_t col = is_a ? 0u : (uint32_t)KN;  // S or dP columns of a slot
       const int sdone = is_a ? SA0 : SB0;
       int s_issued = 0, q_issued = 0;
       bool ok = role_wait(B_(ROWS_LO), 0u, a.error, abort);
@@ -929,13 +937,19 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
         const int s = j & 1;
         ok = role_wait(B_(FULL0 + s), (uint32_t)((j >> 1) & 1), a.error, abort);
         // the slot's columns are free once block j - 2's dS was read (dQ, A)
-        // or written (dP columns, B)
-        if (ok && j >= 2)
-          ok = role_wait(B_(is_a ? QD0 + s : DS0 + s), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
+        // or written (dP columns, B); the one dP buffer (DP1) once block j -
+        // 1's dP is in the probability threads' registers
+        if (ok && is_a && j >= 2)
+          ok = role_wait(B_(QD0 + s), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
+        if (ok && !is_a && L::DP1 && j >= 1)
+          ok = role_wait(B_(DP_FREE), (uint32_t)((j - 1) & 1), a.error, abort);
+        if (ok && !is_a && !L::DP1 && j >= 2)
+          ok = role_wait(B_(DS0 + s), (uint32_t)(((j >> 1) - 1) & 1), a.error, abort);
         if (!ok) break;
         tc_fence_after();
         const uint32_t stg = base + L::STAGE0 + (uint32_t)s * L::STAGE + (is_a ? 0u : 2u * L::KT);
-        const uint32_t sd = tmem + L::SL0 + (uint32_t)s * L::SLOT + col;
+        const uint32_t sd = is_a ? tmem + L::SL0 + (uint32_t)s * L::SLOT
+                            : tmem + (L::DP1 ? L::DPB : L::SL0 + (uint32_t)s * L::SLOT + KN);
 #pragma unroll
         for (int k = 0; k < DH / 16; k++) {
           const uint64_t bh = kdesc16<KN>(stg, k), bl = kdesc16<KN>(stg + L::KT, k);
@@ -968,18 +982,14 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     const float c2 = p.scale * kLog2e * exp2_int(-(ex.q + ex.k));
     const float u_dp = exp2_int(-(ex.v + ex.g));
     const float s_ds = exp2_int(ex.ds);
-    const int cb = 32 * khalf;
+    // this thread's keys of each block: NKC chunks of 32 from cb; chunk c's
+    // dS pair goes over its own 32 S columns (hi, then lo)
+    const int cb = 32 * NKC * khalf;
     bool ok = true;
     for (int j = 0; ok && j < nkb; j++) {
       const int s = j & 1;
       const uint32_t spar = (uint32_t)((j >> 1) & 1);
       const bool full_block = j < full_kb;
-      uint8_t keep[32];
-      if (!full_block && p.mask != nullptr) {  // clamped indices stay in bounds
-        const int64_t mrow = ((int64_t)b * p.Tq + min(tq, p.Tq - 1)) * p.Tk;
-#pragma unroll
-        for (int i = 0; i < 32; i++) keep[i] = p.mask[mrow + min(j * KN + cb + i, p.Tk - 1)];
-      }
       ok = role_wait(B_(KP0 + s), spar, a.error, abort);
       if (ok) ok = role_wait(B_(SA0 + s), spar, a.error, abort);
       if (ok) ok = role_wait(B_(SB0 + s), spar, a.error, abort);
@@ -989,23 +999,38 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
       // keys of the block this query sees: those whose position does not exceed its own
       const int seen = full_block ? KN : count_below(kpos_s + s * KN, KN, qpos_row + 1) - cb;
       const uint32_t slot = trow + L::SL0 + (uint32_t)s * L::SLOT;
-      float sv[32], dp[32];
-      tmem_ld32(slot + cb, sv);
-      tmem_ld32(slot + KN + cb, dp);
+      const uint32_t dpc = L::DP1 ? trow + L::DPB : slot + KN;
 #pragma unroll
-      for (int i = 0; i < 32; i++) {
-        bool adm = full_block;
-        if (!full_block) {
-          adm = i < seen;
-          if (p.mask != nullptr) adm = adm && keep[i] != 0;
+      for (int c = 0; c < NKC; c++) {
+        uint8_t keep[32];
+        if (!full_block && p.mask != nullptr) {  // clamped indices stay in bounds
+          const int64_t mrow = ((int64_t)b * p.Tq + min(tq, p.Tq - 1)) * p.Tk;
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            keep[i] = p.mask[mrow + min(j * KN + cb + 32 * c + i, p.Tk - 1)];
         }
-        const float pv = adm ? ex2(fmaf(sv[i], c2, -lse_row)) : 0.0f;
-        sv[i] = pv * (dp[i] * u_dp - dlt_row);
+        float sv[32], dp[32];
+        tmem_ld32(slot + cb + 32 * c, sv);
+        tmem_ld32(dpc + cb + 32 * c, dp);
+        if (L::DP1 && c == NKC - 1) {  // the dP buffer is free for block j + 1
+          tc_fence_before();
+          mbar_arrive(B_(DP_FREE));
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          bool adm = full_block;
+          if (!full_block) {
+            adm = 32 * c + i < seen;
+            if (p.mask != nullptr) adm = adm && keep[i] != 0;
+          }
+          const float pv = adm ? ex2(fmaf(sv[i], c2, -lse_row)) : 0.0f;
+          sv[i] = pv * (dp[i] * u_dp - dlt_row);
+        }
+        float hi[16], lo[16];
+        pack_pairs(sv, s_ds, hi, lo);
+        tmem_st16(slot + cb + 32 * c, hi);
+        tmem_st16(slot + cb + 32 * c + 16, lo);
       }
-      float hi[16], lo[16];
-      pack_pairs(sv, s_ds, hi, lo);
-      tmem_st16(slot + cb, hi);
-      tmem_st16(slot + cb + 16, lo);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(B_(DS0 + s));
@@ -1104,8 +1129,10 @@ bool launch_bwd_f16(const AttnParams& p, AttnTensor o, const float* o_lo, AttnTe
                      map16(&gl, w.g16l, qrows, Kv16Layout<DH>::BQ) &&
                      map16(&qh128, w.q16h, qrows, QM) && map16(&ql128, w.q16l, qrows, QM) &&
                      map16(&gh128, w.g16h, qrows, QM) && map16(&gl128, w.g16l, qrows, QM) &&
-                     map16(&kkh, w.k16h, krows, KN) && map16(&kkl, w.k16l, krows, KN) &&
-                     map16(&vkh, w.v16h, krows, KN) && map16(&vkl, w.v16l, krows, KN);
+                     map16(&kkh, w.k16h, krows, Q16Layout<DH>::KN) &&
+                     map16(&kkl, w.k16l, krows, Q16Layout<DH>::KN) &&
+                     map16(&vkh, w.v16h, krows, Q16Layout<DH>::KN) &&
+                     map16(&vkl, w.v16l, krows, Q16Layout<DH>::KN);
   if (!built) return false;
   // Q, K, V pairs: from the 3xTF32 pairs a producer left in the workspace
   // (maxima, then the split), kept from this call's binary16 forward, or
