@@ -165,9 +165,11 @@ struct Fwd16Layout {
   static_assert(RT <= STAGE, "Q hi rows pass through stage 1");
   static_assert(QM * (DH + 4) * 4 <= 2 * STAGE, "output staging");
   // TMEM: Q hi (two elements per column), two S slots (the P pair over S), O
+  // (f32-grade: 2 DH columns, P hi V hi + P lo V hi in the first DH and P hi
+  // V lo in the second, added in the epilogue)
   static constexpr uint32_t QH = 0, S0 = DH / 2, O = S0 + 2 * KN;
   static constexpr uint32_t COLS = 512;
-  static_assert(O + DH <= COLS, "TMEM columns");
+  static_assert(O + 2 * DH <= COLS, "TMEM columns");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -346,6 +348,11 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     // ---- O += P V
     if (lane == 0 && nkb > 0) {
       constexpr uint32_t idesc = idesc_f16_m128(DH, 1);
+      // V hi and V lo sit one 64-column chunk stride apart in the stage, so one
+      // MN-major descriptor of N = 2 DH covers [V hi | V lo]: P hi times both
+      // in one instruction (the pipe's full rate at N = 128)
+      constexpr uint32_t idesc2 = idesc_f16_m128(2 * DH, 1);
+      static_assert(L::KT == (DH / 64) * KN * 128, "V lo one chunk stride after V hi");
       bool ok = true;
       for (int j = 0; ok && j < nkb; j++) {
         const int s = j & 1;
@@ -359,11 +366,12 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
           // keys 16k..16k+15: the hi / lo columns of the half that wrote them
           const int h = k / (NKH / 16), kk = k % (NKH / 16);
           const uint32_t ah = sd + (uint32_t)(NKH * h + 8 * kk);
-          const uint64_t bh = mdesc16<KN>(vt, k), bl = mdesc16<KN>(vt + L::KT, k);
-          umma_f16_ts(tmem + L::O, ah, bh, idesc, (j > 0 || k > 0) ? 1u : 0u);
+          const uint64_t bh = mdesc16<KN>(vt, k);
           if (THREE) {
-            umma_f16_ts(tmem + L::O, ah, bl, idesc, 1u);
+            umma_f16_ts(tmem + L::O, ah, bh, idesc2, (j > 0 || k > 0) ? 1u : 0u);
             umma_f16_ts(tmem + L::O, ah + (uint32_t)(NKH / 2), bh, idesc, 1u);
+          } else {
+            umma_f16_ts(tmem + L::O, ah, bh, idesc, (j > 0 || k > 0) ? 1u : 0u);
           }
         }
         umma_commit(B_(PVD0 + s));
@@ -430,9 +438,10 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
         if (j > 0) w = role_wait(B_(PVD0 + ((j - 1) & 1)), (uint32_t)(((j - 1) >> 1) & 1), a.error, abort);
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
         tc_fence_after();
+        constexpr int OC = THREE ? 2 * DH : DH;  // O's columns
 #pragma unroll
-        for (int c = 0; c < DH / 64; c++) {
-          const uint32_t col = L::O + (uint32_t)(khalf * (DH / 2) + 32 * c);
+        for (int c = 0; c < OC / 64; c++) {
+          const uint32_t col = L::O + (uint32_t)(khalf * (OC / 2) + 32 * c);
           float ov[32];
           tmem_ld32(trow + col, ov);
 #pragma unroll
@@ -493,6 +502,12 @@ attn_fwd_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
         float ov[32];
         if (nkb > 0) {
           tmem_ld32(trow + L::O + col, ov);
+          if (THREE) {  // plus the P hi V lo half
+            float o2[32];
+            tmem_ld32(trow + L::O + DH + col, o2);
+#pragma unroll
+            for (int i = 0; i < 32; i++) ov[i] += o2[i];
+          }
 #pragma unroll
           for (int i = 0; i < 32; i++) ov[i] *= un;
         } else {
