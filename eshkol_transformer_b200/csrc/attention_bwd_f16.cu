@@ -234,6 +234,15 @@ constexpr int MMA_A = 8, MMA_B = 9, LOADER = 10;
 
 constexpr int BK = 128;  // keys per CTA (TMEM lanes)
 
+// v += the 32 columns of this thread's lane at taddr (the second half of a
+// concatenated accumulator).
+__device__ __forceinline__ void add_acc_half(uint32_t taddr, float (&v)[32]) {
+  float w[32];
+  tmem_ld32(taddr, w);
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] += w[i];
+}
+
 template <int DH>
 struct Kv16Layout {
   // queries per block: 128 at head_dim 64 (S^T and dP^T at N = 128, the
@@ -241,19 +250,31 @@ struct Kv16Layout {
   static constexpr int BQ = DH == 64 ? 128 : 64;
   static constexpr int QT = BQ * DH * 2;  // [BQ, DH] binary16 tile
   static constexpr int KT = BK * DH * 2;  // [BK, DH] binary16 tile
+  // CAT (head_dim 64): dV and dK take P^T / dS^T hi times [dO | Q hi, lo] as
+  // one MMA of N = 2 DH (the lo tile sits one 64-column chunk stride after
+  // the hi tile), into accumulators of 2 DH columns whose halves the
+  // epilogue adds; K hi and V hi then stay in shared memory to leave TMEM
+  // the room
+  static constexpr bool CAT = DH == 64;
   // K lo, V lo (shared-memory A operands); two stages of the Q pair and of the
-  // dO pair (hi, lo), each tile read K-major and MN-major
+  // dO pair (hi, lo), each tile read K-major and MN-major; (CAT) K hi, V hi
   static constexpr int KL = 0, VL = KT, QR = 2 * KT, GR = QR + 4 * QT;
-  static constexpr int BARS = GR + 4 * QT;
+  static constexpr int KHS = GR + 4 * QT, VHS = KHS + KT;
+  static constexpr int BARS = CAT ? VHS + KT : GR + 4 * QT;
   static constexpr int SMEM = BARS + 256 + 1024;
-  // K hi / V hi pass through stage 1 of the Q / dO rings on their way to TMEM
-  static_assert(KT <= 2 * QT, "key tile in one ring stage");
+  static_assert(QT == (DH / 64) * BQ * 128, "lo tile one chunk stride after the hi tile");
+  // otherwise K hi / V hi pass through stage 1 of the Q / dO rings on their
+  // way to TMEM
+  static_assert(CAT || KT <= 2 * QT, "key tile in one ring stage");
   // the epilogue stages dK, dV rows ([128][DH + 4] f32 each) and two column-sum
   // scratch areas in the freed operand buffers
   static_assert(2 * 128 * (DH + 4) * 4 + 2 * SOFT * 16 <= BARS, "epilogue staging");
-  // TMEM: K hi, V hi (two elements per column), dK, dV accumulators, S^T
-  // (then the P^T pair), dP^T (then the dS^T pair)
-  static constexpr uint32_t KH = 0, VH = DH / 2, DK = DH, DV = 2 * DH, ST = 3 * DH, DPT = ST + BQ;
+  // TMEM: K hi, V hi (two elements per column; not with CAT), dK, dV
+  // accumulators (CAT: 2 DH columns each), S^T (then the P^T pair), dP^T
+  // (then the dS^T pair)
+  static constexpr uint32_t ACC = CAT ? 2 * DH : DH;
+  static constexpr uint32_t KH = 0, VH = DH / 2, DK = CAT ? 0 : DH, DV = DK + ACC, ST = DV + ACC;
+  static constexpr uint32_t DPT = ST + BQ;
   static constexpr uint32_t COLS = 512;
   static_assert(DPT + BQ <= COLS, "TMEM columns");
   static_assert(SMEM <= 232448, "shared memory");
@@ -300,7 +321,8 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
   const int tk = k0 + row;
   const bool valid_k = tk < p.Tk;
   const uint32_t base = smem_u32(smem);
-  const uint32_t kh_stage = base + L::QR + 2 * L::QT, vh_stage = base + L::GR + 2 * L::QT;
+  const uint32_t kh_stage = base + (L::CAT ? L::KHS : L::QR + 2 * L::QT);
+  const uint32_t vh_stage = base + (L::CAT ? L::VHS : L::GR + 2 * L::QT);
   if (warp == LOADER && lane == 0) {
     // the loader initialises the barriers and issues the key tile at once
     // (its copies overlap the TMEM allocation and the position scan below):
@@ -367,8 +389,9 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  // K hi (warps 0-3) and V hi (warps 4-7) rows -> TMEM
-  if (warp < 8 && n_it > 0) {
+  // K hi (warps 0-3) and V hi (warps 4-7) rows -> TMEM (CAT: they stay in
+  // shared memory)
+  if (!L::CAT && warp < 8 && n_it > 0) {
     const bool ok = mbar_wait(B_(LO_FULL), 0u, a.error);
     if (!ok) *abort = 1;
     if (__all_sync(0xffffffffu, ok)) {
@@ -426,7 +449,9 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
     if (lane == 0 && n_it > 0) {
       constexpr uint32_t idesc_s = idesc_f16_m128(BQ, 0);
       constexpr uint32_t idesc_o = idesc_f16_m128(DH, 1);
+      constexpr uint32_t idesc_o2 = idesc_f16_m128(2 * DH, 1);   // (CAT) [hi | lo]
       const uint32_t xh = tmem + (is_a ? L::KH : L::VH);          // TMEM A operand (hi)
+      const uint32_t xhs = is_a ? kh_stage : vh_stage;            // (CAT) shared-memory hi
       const uint32_t xlo = base + (is_a ? L::KL : L::VL);         // shared-memory A (lo)
       const int kring = is_a ? L::QR : L::GR, mring = is_a ? L::GR : L::QR;
       const uint32_t sd = tmem + (is_a ? L::ST : L::DPT);         // scores, then the pair
@@ -451,10 +476,18 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
 #pragma unroll
         for (int k = 0; k < DH / 16; k++) {
           const uint64_t bh = kdesc16<BQ>(kt, k), bl = kdesc16<BQ>(kt + L::QT, k);
-          umma_f16_ts(sd, xh + 8 * k, bh, idesc_s, k > 0 ? 1u : 0u);
-          if (THREE) {
-            umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
-            umma_f16(sd, kdesc16<BK>(xlo, k), bh, idesc_s, 1u);
+          if constexpr (L::CAT) {
+            umma_f16(sd, kdesc16<BK>(xhs, k), bh, idesc_s, k > 0 ? 1u : 0u);
+            if (THREE) {
+              umma_f16(sd, kdesc16<BK>(xhs, k), bl, idesc_s, 1u);
+              umma_f16(sd, kdesc16<BK>(xlo, k), bh, idesc_s, 1u);
+            }
+          } else {
+            umma_f16_ts(sd, xh + 8 * k, bh, idesc_s, k > 0 ? 1u : 0u);
+            if (THREE) {
+              umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
+              umma_f16(sd, kdesc16<BK>(xlo, k), bh, idesc_s, 1u);
+            }
           }
         }
         umma_commit(B_(sdone));
@@ -474,10 +507,15 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
           // queries 16k..16k+15: hi / lo columns of the half that wrote them
           const uint32_t ah = sd + 32u * (uint32_t)(k >> 1) + 8u * (uint32_t)(k & 1);
           const uint64_t bh = mdesc16<BQ>(mt, k), bl = mdesc16<BQ>(mt + L::QT, k);
-          umma_f16_ts(acc_d, ah, bh, idesc_o, (!restart || k > 0) ? 1u : 0u);
-          if (THREE) {
-            umma_f16_ts(acc_d, ah, bl, idesc_o, 1u);
+          if (L::CAT && THREE) {  // hi times [hi | lo], then lo times hi
+            umma_f16_ts(acc_d, ah, bh, idesc_o2, (!restart || k > 0) ? 1u : 0u);
             umma_f16_ts(acc_d, ah + 16u, bh, idesc_o, 1u);
+          } else {
+            umma_f16_ts(acc_d, ah, bh, idesc_o, (!restart || k > 0) ? 1u : 0u);
+            if (THREE) {
+              umma_f16_ts(acc_d, ah, bl, idesc_o, 1u);
+              umma_f16_ts(acc_d, ah + 16u, bh, idesc_o, 1u);
+            }
           }
         }
         umma_commit(B_(gdone));
@@ -587,6 +625,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         for (int c = 0; c < DH / 32; c++) {
           float v[32];
           tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+          if (L::CAT && THREE) add_acc_half(trow + (khalf == 0 ? L::DK : L::DV) + DH + 32 * c, v);
           float4* dst = reinterpret_cast<float4*>(crow + 32 * c);
 #pragma unroll
           for (int u = 0; u < 8; u++) {
@@ -659,6 +698,7 @@ attn_bwd_kv_f16_kernel(const __grid_constant__ CUtensorMap kh_map,
         float v[32];
         if (n_it > 0) {
           tmem_ld32(trow + (khalf == 0 ? L::DK : L::DV) + 32 * c, v);
+          if (L::CAT && THREE) add_acc_half(trow + (khalf == 0 ? L::DK : L::DV) + DH + 32 * c, v);
           if (crow != nullptr) {  // plus the earlier chunks
             const float4* src = reinterpret_cast<const float4*>(crow + 32 * c);
 #pragma unroll
