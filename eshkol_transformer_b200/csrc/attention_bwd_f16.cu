@@ -781,18 +781,26 @@ struct Q16Layout {
   static constexpr int QL = 0, GL = RT, STAGE0 = 2 * RT;
   static constexpr int STAGE = 4 * KT;
   static constexpr int KPOS = STAGE0 + 2 * STAGE;  // [2][KN] key positions
-  static constexpr int BARS = KPOS + 2 * KN * 8;
+  // CATQ (head_dim 64): dQ takes dS hi times [K hi | K lo] as one MMA of
+  // N = 2 DH (the lo tile sits one 64-column chunk stride after the hi tile)
+  // into an accumulator of 2 DH columns whose halves the epilogue adds; Q hi
+  // and dO hi then stay in shared memory to leave TMEM the room
+  static constexpr bool CATQ = DH == 64;
+  static constexpr int QHS = KPOS + 2 * KN * 8, GHS = QHS + RT;
+  static constexpr int BARS = CATQ ? GHS + RT : KPOS + 2 * KN * 8;
   static constexpr int SMEM = BARS + 256 + 1024;
-  // Q hi and dO hi rows pass through stage 1 on their way to TMEM
+  static_assert(KT == (DH / 64) * KN * 128, "K lo one chunk stride after K hi");
+  // otherwise Q hi and dO hi rows pass through stage 1 on their way to TMEM
   static_assert(2 * RT <= STAGE, "row tiles in one stage");
   static_assert(128 * (DH + 4) * 4 + SOFT * 16 <= KPOS, "epilogue staging");
   // TMEM: Q hi, dO hi (two elements per column); two slots of S (the dS pair
   // over S), each with its dP behind it, or (DP1) one dP buffer behind both
   // slots; the dQ accumulator
-  static constexpr uint32_t QH = 0, GH = DH / 2, SL0 = DH, SLOT = DP1 ? KN : 2 * KN;
+  static constexpr uint32_t ACC = CATQ ? 2 * DH : DH;  // dQ accumulator columns
+  static constexpr uint32_t QH = 0, GH = DH / 2, SL0 = CATQ ? 0 : DH, SLOT = DP1 ? KN : 2 * KN;
   static constexpr uint32_t DPB = SL0 + 2 * SLOT, DQ = DPB + (DP1 ? KN : 0);
   static constexpr uint32_t COLS = 512;
-  static_assert(DQ + DH <= COLS, "TMEM columns");
+  static_assert(DQ + ACC <= COLS, "TMEM columns");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -836,7 +844,8 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
   const int tq = q0 + row;
   const bool valid_q = tq < p.Tq;
   const uint32_t base = smem_u32(smem);
-  const uint32_t rows_hi = base + L::STAGE0 + L::STAGE;  // stage 1
+  // Q hi, dO hi rows: stage 1 (on their way to TMEM) or (CATQ) their own area
+  const uint32_t rows_hi = base + (L::CATQ ? L::QHS : L::STAGE0 + L::STAGE);
   if (tid == 0) {
     for (int i = 0; i < NBARS; i++) {
       const uint32_t n = (i == DS0 || i == DS1 || i == DP_FREE) ? SOFT
@@ -894,8 +903,9 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  // Q hi and dO hi rows -> TMEM (warps 0-3 Q, 4-7 dO)
-  if (warp < 8) {
+  // Q hi and dO hi rows -> TMEM (warps 0-3 Q, 4-7 dO; CATQ: they stay in
+  // shared memory)
+  if (!L::CATQ && warp < 8) {
     const bool ok = mbar_wait(B_(ROWS_HI), 0u, a.error);
     if (!ok) *abort = 1;
     if (__all_sync(0xffffffffu, ok)) {
@@ -937,6 +947,7 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     }
     if (lane == 0) {  // every copy has landed before the CTA releases its memory
       mbar_wait(B_(ROWS_LO), 0u, a.error);
+      if (L::CATQ) mbar_wait(B_(ROWS_HI), 0u, a.error);
       for (int j = nk - 2 < 0 ? 0 : nk - 2; j < nk; j++)
         mbar_wait(B_(FULL0 + (j & 1)), (uint32_t)((j >> 1) & 1), a.error);
     }
@@ -947,11 +958,14 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
     if (lane == 0 && nkb > 0) {
       constexpr uint32_t idesc_s = idesc_f16_m128(KN, 0);
       constexpr uint32_t idesc_q = idesc_f16_m128(DH, 1);
+      constexpr uint32_t idesc_q2 = idesc_f16_m128(2 * DH, 1);  // (CATQ) [K hi | K lo]
       const uint32_t xh = tmem + (is_a ? L::QH : L::GH);
+      const uint32_t xhs = rows_hi + (is_a ? 0u : (uint32_t)L::RT);  // (CATQ) shared-memory hi
       const uint32_t xlo = base + (is_a ? L::QL : L::GL);
       const int sdone = is_a ? SA0 : SB0;
       int s_issued = 0, q_issued = 0;
       bool ok = role_wait(B_(ROWS_LO), 0u, a.error, abort);
+      if (ok && L::CATQ) ok = role_wait(B_(ROWS_HI), 0u, a.error, abort);
       auto issue_dq = [&](int i) {
         const int s = i & 1;
         ok = role_wait(B_(DS0 + s), (uint32_t)((i >> 1) & 1), a.error, abort);
@@ -963,10 +977,15 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
         for (int k = 0; k < KN / 16; k++) {
           const uint32_t ah = sd + 32u * (uint32_t)(k >> 1) + 8u * (uint32_t)(k & 1);
           const uint64_t bh = mdesc16<KN>(kt, k), bl = mdesc16<KN>(kt + L::KT, k);
-          umma_f16_ts(tmem + L::DQ, ah, bh, idesc_q, (i > 0 || k > 0) ? 1u : 0u);
-          if (THREE) {
-            umma_f16_ts(tmem + L::DQ, ah, bl, idesc_q, 1u);
+          if (L::CATQ && THREE) {  // hi times [hi | lo], then lo times hi
+            umma_f16_ts(tmem + L::DQ, ah, bh, idesc_q2, (i > 0 || k > 0) ? 1u : 0u);
             umma_f16_ts(tmem + L::DQ, ah + 16u, bh, idesc_q, 1u);
+          } else {
+            umma_f16_ts(tmem + L::DQ, ah, bh, idesc_q, (i > 0 || k > 0) ? 1u : 0u);
+            if (THREE) {
+              umma_f16_ts(tmem + L::DQ, ah, bl, idesc_q, 1u);
+              umma_f16_ts(tmem + L::DQ, ah + 16u, bh, idesc_q, 1u);
+            }
           }
         }
         umma_commit(B_(QD0 + s));
@@ -993,10 +1012,18 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
 #pragma unroll
         for (int k = 0; k < DH / 16; k++) {
           const uint64_t bh = kdesc16<KN>(stg, k), bl = kdesc16<KN>(stg + L::KT, k);
-          umma_f16_ts(sd, xh + 8 * k, bh, idesc_s, k > 0 ? 1u : 0u);
-          if (THREE) {
-            umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
-            umma_f16(sd, kdesc16<QM>(xlo, k), bh, idesc_s, 1u);
+          if constexpr (L::CATQ) {
+            umma_f16(sd, kdesc16<QM>(xhs, k), bh, idesc_s, k > 0 ? 1u : 0u);
+            if (THREE) {
+              umma_f16(sd, kdesc16<QM>(xhs, k), bl, idesc_s, 1u);
+              umma_f16(sd, kdesc16<QM>(xlo, k), bh, idesc_s, 1u);
+            }
+          } else {
+            umma_f16_ts(sd, xh + 8 * k, bh, idesc_s, k > 0 ? 1u : 0u);
+            if (THREE) {
+              umma_f16_ts(sd, xh + 8 * k, bl, idesc_s, 1u);
+              umma_f16(sd, kdesc16<QM>(xlo, k), bh, idesc_s, 1u);
+            }
           }
         }
         umma_commit(B_(sdone + s));
@@ -1106,6 +1133,7 @@ attn_bwd_q_f16_kernel(const __grid_constant__ CUtensorMap qh_map,
         float v[32];
         if (nkb > 0) {
           tmem_ld32(trow + L::DQ + col, v);
+          if (L::CATQ && THREE) add_acc_half(trow + L::DQ + DH + col, v);
 #pragma unroll
           for (int i = 0; i < 32; i++) v[i] *= un;
         } else {
