@@ -625,6 +625,16 @@ def run_reference(args) -> None:
 SWEEP = dict(batch=4, heads=16, head_dims=(64, 128), seq_lens=(512, 1024, 2048, 4096, 8192, 16384))
 
 
+def contraction_label(pairs16: bool, single: bool) -> str:
+    """The attention contraction scheme of a sweep shape: binary16 operands
+    (head_dim 128, head_dim 64 from 1,024^2 or on request) or TF32, three
+    products of operand pairs (f32-grade) or one (TF32 mode)."""
+    if single:
+        return ("binary16 with per-tensor scales (kind::f16, 1 product)" if pairs16
+                else "TF32 (kind::tf32, 1 product)")
+    return "binary16 pairs (kind::f16)" if pairs16 else "3xTF32 pairs (kind::tf32)"
+
+
 def attention_sweep(args) -> None:
     """Causal attention with RoPE, forward and backward, over the sweep's
     shapes (batch 4, 16 heads, head_dim 64 / 128, T = 512 ... 16384, seeded
@@ -690,12 +700,10 @@ def attention_sweep(args) -> None:
                 "metric": "attn fwd/bwd % roofline", "workload": "causal attention + RoPE",
                 "batch": B, "heads": H, "seq_len": T, "head_dim": Dh,
                 "dtype": "tf32" if single else "f32",
+                # the forward takes binary16 operands wherever the backward does
                 "contractions": {
-                    "forward": "TF32 (kind::tf32, 1 product)" if single
-                    else "3xTF32 pairs (kind::tf32)",
-                    "backward": ("binary16 with per-tensor scales (kind::f16, 1 product)"
-                                 if Dh == 128 else "TF32 (kind::tf32, 1 product)") if single
-                    else "binary16 pairs (kind::f16)" if pairs16 else "3xTF32 pairs (kind::tf32)"},
+                    "forward": contraction_label(pairs16, single),
+                    "backward": contraction_label(pairs16, single)},
                 "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
                 "fwd_tflops": round(f_flop / fwd_ms / 1e9, 2),
                 "bwd_tflops": round(b_flop / bwd_ms / 1e9, 2),
