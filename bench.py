@@ -627,7 +627,7 @@ SWEEP = dict(batch=4, heads=16, head_dims=(64, 128), seq_lens=(512, 1024, 2048, 
 
 def contraction_label(pairs16: bool, single: bool) -> str:
     """The attention contraction scheme of a sweep shape: binary16 operands
-    (head_dim 128, head_dim 64 from 1,024^2 or on request) or TF32, three
+    (head_dim 128, head_dim 64 from 768^2 or on request) or TF32, three
     products of operand pairs (f32-grade) or one (TF32 mode)."""
     if single:
         return ("binary16 with per-tensor scales (kind::f16, 1 product)" if pairs16
@@ -694,7 +694,7 @@ def attention_sweep(args) -> None:
             b_flop = 4.0 * B * H * T * T * Dh
             t_bytes = 4.0 * B * H * T * Dh
             pairs16 = Dh == 128 or (Dh == 64 and (contraction == etb.ATTENTION_BWD_PAIRS16
-                                                  or T * T >= 1024 * 1024))
+                                                  or T * T >= 768 * 768))
             single = contraction == etb.ATTENTION_TF32
             line = {
                 "metric": "attn fwd/bwd % roofline", "workload": "causal attention + RoPE",

@@ -290,7 +290,7 @@ class AttentionShape(C.Structure):
 
 
 ATTENTION_DEFAULT = 0      # binary16 pairs at head_dim 128 and at head_dim 64 from
-                           # q_len k_len = 1024^2 up; 3xTF32 pairs otherwise
+                           # q_len k_len = 768^2 up; 3xTF32 pairs otherwise
 ATTENTION_BWD_PAIRS16 = 1  # binary16 pairs in the backward at head_dim 64 as well
 ATTENTION_TF32 = 2         # one product of TF32-grade operands (11 significant bits)
 

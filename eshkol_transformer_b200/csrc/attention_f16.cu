@@ -583,10 +583,11 @@ bool launch_fwd_f16(const AttnParams& p, AttnOut o, float* m, float* l, cudaStre
 }  // namespace
 
 bool attention_uses_pairs16(const AttnParams& p) {
-  // head_dim 64: from 1,024^2 the binary16 forward + backward measured
-  // faster than 3xTF32 (the backward's 128-query blocks; the forward alone
-  // wins from 4,096^2), below it the preparation passes weigh more
-  const bool long_seq = (int64_t)p.Tq * p.Tk >= (int64_t)1024 * 1024;
+  // head_dim 64: from 768^2 the binary16 forward + backward measured faster
+  // than 3xTF32 (9 % at 768^2, 2 % at 512^2: the backward's 128-query and
+  // 128-key blocks; the forward alone wins only from 4,096^2), below it the
+  // preparation passes weigh more
+  const bool long_seq = (int64_t)p.Tq * p.Tk >= (int64_t)768 * 768;
   return p.Dh == 128 || (p.Dh == 64 && (p.bwd_pairs16 || long_seq));
 }
 

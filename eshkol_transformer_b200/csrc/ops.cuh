@@ -341,7 +341,7 @@ bool attention_backward_tc(const AttnParams& p, AttnTensor o, const float* o_lo,
                            const float* row_max, const float* row_sum, float* delta, AttnOut dq,
                            AttnOut dk, AttnOut dv, cudaStream_t stream);
 // Whether attention carries binary16 operand pairs for p: always at
-// head_dim 128, at head_dim 64 with bwd_pairs16 or from Tq Tk = 1,024^2 up
+// head_dim 128, at head_dim 64 with bwd_pairs16 or from Tq Tk = 768^2 up
 // (forward and backward decide alike, so a backward reuses its forward's
 // pairs).
 bool attention_uses_pairs16(const AttnParams& p);

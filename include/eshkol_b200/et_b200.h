@@ -114,7 +114,7 @@ typedef struct et_b200_attention_v1 {
 /* Contraction modes.  f32-grade (three products of operand pairs, about 22
  * significant bits per operand element):
  * ET_B200_ATTENTION_DEFAULT: binary16 pairs with per-tensor power-of-two
- *   scales at head_dim 128 and at head_dim 64 from q_len k_len = 1024^2 up,
+ *   scales at head_dim 128 and at head_dim 64 from q_len k_len = 768^2 up,
  *   3xTF32 pairs otherwise;
  * ET_B200_ATTENTION_BWD_PAIRS16: binary16 pairs in the backward at head_dim
  *   64 as well.

@@ -75,7 +75,10 @@ MODES = [etb.ATTENTION_DEFAULT, etb.ATTENTION_BWD_PAIRS16]
                                                 (2, 4, 2, 200, 32, True),
                                                 (1, 2, 2, 384, 128, True),
                                                 (2, 4, 2, 330, 128, True),
-                                                (2, 2, 2, 96, 64, False)])
+                                                (2, 2, 2, 96, 64, False),
+                                                # head_dim 64 just above the default's
+                                                # binary16 threshold (768^2), ragged tiles
+                                                (1, 2, 2, 800, 64, True)])
 def test_device_attention_vs_oracle(lib, cuda, B, Hq, Hkv, T, Dh, rope, contraction):
     q, k, v, do, o, dq, dk, dv = _run(B, Hq, Hkv, T, Dh, 7 + T, rope, contraction)
     ro, rdq, rdk, rdv = _oracle(q, k, v, do, rope)
