@@ -1,5 +1,6 @@
 // A2 causal attention backward on tcgen05 tensor cores with binary16 operand
-// pairs (sm_100a): the head_dim-128 path, and head_dim 64 on request.
+// pairs (sm_100a): head_dim 128, head_dim 64 from Tq Tk = 768^2 or on
+// request, and the training step's split-f16 steps.
 //
 // Semantics are those of the SIMT backward in attention.cu
 // (native/a2_attention_provider.c:416-666) and of the 3xTF32 kernels in
@@ -14,7 +15,9 @@
 // scheme the linear GEMMs use): about 22 significant bits of every element,
 // down to an absolute floor near 2^-39 of the tensor's largest magnitude.
 // The exponent e is one power of two per tensor: for Q, K, V and dO it puts
-// the tensor's max |x| into [2^14, 2^15) (a prepass measures the maxima); for
+// the tensor's max |x| into [2^14, 2^15) (a prepass measures the maxima; in
+// the training step the producing GEMM epilogues write the pairs with their
+// slot's exponent instead); for
 // P (in [0, 1]) it is 14; for dS it comes from the bound
 // |dS| <= |dP| + |delta| <= 2 Dh max|dO| max|V| (|dP_qk| = |dO_q . V_k| and
 // delta_q = dO_q . O_q with O_q a convex combination of V rows).  Scaling by a
@@ -28,14 +31,20 @@
 // element 2c in the low half of column c.
 //
 //   dK/dV kernel: one CTA per 128 keys of one (batch, kv head); TMEM lane r is
-//     key r.  K hi, V hi in TMEM, K lo, V lo in shared memory.  For each
-//     64-query block of every query head of the group:
+//     key r.  K hi, V hi in TMEM (head_dim 128) or shared memory (64), K lo,
+//     V lo in shared memory.  For each query block (128 queries at head_dim
+//     64, 64 at 128) of every query head of the group:
 //       S^T  = K Q^T,  dP^T = V dO^T              (B: Q, dO tiles, K-major)
 //       P^T pair over S^T, dS^T pair over dP^T    (registers -> TMEM)
 //       dV  += P^T dO, dK += dS^T Q               (B: the same tiles, MN-major)
 //   dQ kernel: one CTA per 128 queries of one (batch, head), TMEM lane r is
-//     query r; Q hi, dO hi in TMEM, Q lo, dO lo in shared memory.  For each
-//     64-key block: S = Q K^T, dP = dO V^T; dS pair over S; dQ += dS K.
+//     query r; Q hi, dO hi in TMEM (head_dim 128) or shared memory (64), Q
+//     lo, dO lo in shared memory.  For each key block (128 keys at head_dim
+//     64, 64 at 128): S = Q K^T, dP = dO V^T; dS pair over S; dQ += dS K.
+//   At head_dim 64 the gradient MMAs take hi times [hi | lo] of their B tiles
+//   as one instruction of N = 128 (the lo tile sits one 64-column chunk
+//   stride after the hi tile) into accumulators of 128 columns whose halves
+//   the epilogue adds.
 //
 // Warp roles, barriers, the abort protocol and the output epilogue follow
 // attention_bwd_tc.cu.  All mbarrier waits are bounded; a timeout raises a

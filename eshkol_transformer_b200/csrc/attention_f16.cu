@@ -21,7 +21,10 @@
 // TMEM (A operand), Q lo in shared memory; two TMEM slots of S (P's pair is
 // written over S, each thread over its own columns); O in TMEM with the lazy
 // rescale of attention_tc.cu (the stale row maximum stands until a block
-// exceeds it by 2^8).  All mbarrier waits are bounded; a timeout raises a
+// exceeds it by 2^8).  P hi times [V hi | V lo] is one MMA of N = 2 head_dim
+// (V lo sits one 64-column chunk stride after V hi), into O's 2 head_dim
+// columns, plus P lo times V hi into the first half; the epilogue adds the
+// halves.  All mbarrier waits are bounded; a timeout raises a
 // CTA-wide abort flag, in-flight copies and MMAs are waited for (bounded) and
 // TMEM is always released.
 #include <cuda_fp16.h>
